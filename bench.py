@@ -1,0 +1,580 @@
+"""Throughput of tropnn's routed-layer hot path on B200 (backend="b200").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl b200|reference]
+
+Metric: rows/s of TropLinear / PairwiseLinear forward + backward. The
+default workload is BASELINE config 2: PairwiseLinear(256->512, tables=16,
+comparisons=6, fast_sigmoid_odd, min-margin STE), fp32, forward + STE backward with an
+upstream gradient ~ N(0,1), 4096 rows per GPU (weak scaling; at N>1 each step ends
+with the NCCL all-reduce of the parameter gradients). Other workloads are selectable
+with --workload. Data are seeded synthetic tensors of the configured shapes.
+
+One step = (untimed L2 flush) -> [timed: zero grads, forward, backward, grad
+all-reduce]. W warm-up steps, then exactly K timed steps bracketed by barrier +
+synchronize, each timed with CUDA events on the launching stream; the max over ranks
+is reported. ``e2e`` repeats the step through the same public API with the inputs
+copied from pinned host memory and the output + input gradient copied back inside the
+timed region. ``roofline`` is the dominant kernel's algorithmic bytes per launch over
+its mean CUDA-event duration in the timed region. ``cpu_baseline`` times the numpy
+oracle of the reference's torch path on the host cores (rank 0, N=1 only).
+
+``--impl reference`` runs the CPU arm: the oracle port of the reference's torch CPU
+path, on all host threads, on a bounded row sample per step; under torchrun only rank 0
+runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import contextlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from dataclasses import dataclass, field
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+PEAKS_PATH = REPO / "MEASURED_PEAKS.json"
+TRAFFIC_PATH = REPO / "profiles" / "traffic.json"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+L2_FLUSH_BYTES = 256 * 1024 * 1024
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+
+
+@dataclass
+class Workload:
+    name: str
+    kind: str  # "pairwise" | "trop"
+    in_features: int
+    out_features: int
+    rows_per_gpu: int
+    train: bool
+    dtype: str = "float32"
+    layer_kwargs: dict = field(default_factory=dict)
+    description: str = ""
+    cpu_sample_rows: int = 0  # rows per CPU-baseline step (0 = the full per-GPU batch)
+
+    @property
+    def cpu_rows(self) -> int:
+        return self.cpu_sample_rows or self.rows_per_gpu
+
+    def build(self):
+        import tropnn_b200
+
+        cls = tropnn_b200.PairwiseLinear if self.kind == "pairwise" else tropnn_b200.TropLinear
+        layer = cls(self.in_features, self.out_features, seed=0, **self.layer_kwargs)
+        if self.dtype == "float16":
+            layer = layer.half()
+        return layer
+
+
+WORKLOADS = {
+    "pairwise_cfg2": Workload(
+        "pairwise_cfg2", "pairwise", 256, 512, 4096, True,
+        layer_kwargs=dict(tables=16, comparisons=6, surrogate="fast_sigmoid_odd", use_min_margin_ste=True),
+        description="BASELINE config 2: PairwiseLinear(256->512, tables=16, comparisons=6), fp32, fwd + STE bwd, batch 4096",
+    ),
+    "trop_cfg1": Workload(
+        "trop_cfg1", "trop", 256, 512, 8, False,
+        layer_kwargs=dict(heads=32, cells=4, code_dim=32),
+        description="BASELINE config 1: TropLinear(256->512, H32, K4, D32), fp32, eval forward, batch 8",
+    ),
+    "trop_cfg3_layer1": Workload(
+        "trop_cfg3_layer1", "trop", 784, 128, 512, True,
+        layer_kwargs=dict(heads=256, cells=16, code_dim=64),
+        description="config 3 layer 1: TropLinear(784->128, H256, K16, D64), fp32, fwd + min-face bwd, batch 512",
+    ),
+    "pairwise_cfg5_train": Workload(
+        "pairwise_cfg5_train", "pairwise", 4096, 4096, 16384, True, dtype="float16",
+        layer_kwargs=dict(tables=1024, comparisons=8),
+        description="config 5: PairwiseLinear(4096->4096, T1024, C8), f16 params, train step, batch 16384",
+        cpu_sample_rows=64,
+    ),
+    "trop_cfg5_eval": Workload(
+        "trop_cfg5_eval", "trop", 4096, 4096, 65536, False, dtype="float16",
+        layer_kwargs=dict(heads=1024, cells=16, code_dim=256),
+        description="config 5: TropLinear(4096->4096, H1024, K16, D256), f16 params, eval forward, batch 65536",
+        cpu_sample_rows=256,
+    ),
+}
+
+
+def algorithmic_bytes(w: Workload, kernel: str, rows: int) -> float | None:
+    """Algorithmic bytes one launch of ``kernel`` moves for ``rows`` rows (per-row formulas of
+    the hot-path measurement plan; parameter bytes counted once per gathered row)."""
+    kw = w.layer_kwargs
+    elt = 2 if w.dtype == "float16" else 4
+    if w.kind == "pairwise":
+        T, C, out, inn = kw["tables"], kw["comparisons"], w.out_features, w.in_features
+        per_row = {
+            "pairwise_forward": T * out * elt + inn * 4 + out * 4 + T * 8 + T * C * 4,
+            "pairwise_ste_backward": out * 4 + 2 * T * out * elt + inn * 4 + T * 8 + T * C * 4 + T * 4 + T,
+            "pairwise_lut_grad": T * out * 4 + T * 4,
+            "bucket_sort": T * 8 + T * 4,
+            "pairwise_threshold_grad": T * 4 + T,
+        }.get(kernel)
+        if per_row is None:
+            return None
+        fixed = T * (1 << C) * out * elt if kernel == "pairwise_lut_grad" else 0
+        return float(per_row * rows + fixed)
+    H, K, D = kw["heads"], kw["cells"], kw["code_dim"]
+    per_row = {
+        "trop_route": D * 4 + H * (8 + 1 + 1 + 4),
+        "trop_hidden": H * D * elt * (2 if w.train else 1) + 2 * D * 4 + H * (2 + 4),
+        "trop_backward_rows": 4 * H * D * elt + 2 * D * 4 + H * (2 + 4 + 12),
+        "trop_code_grad": 2 * D * 4 + 2 * 8,
+        "trop_router_grad": 2 * D * 4 + 2 * 8,
+        "bucket_sort": H * (1 + 4),
+    }.get(kernel)
+    if per_row is None:
+        return None
+    fixed = H * K * D * elt if kernel in ("trop_code_grad", "trop_router_grad") else 0
+    return float(per_row * rows + fixed)
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+
+def _peaks() -> tuple[dict, str]:
+    if PEAKS_PATH.exists():
+        return json.loads(PEAKS_PATH.read_text()), "measured"
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    QUERY = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, device: torch.device) -> None:
+        # nvidia-smi numbers GPUs independently of CUDA_VISIBLE_DEVICES; select by UUID.
+        self.device_index = f"GPU-{torch.cuda.get_device_properties(device).uuid}"
+        self.proc: subprocess.Popen | None = None
+        self.lines: list[str] = []
+        self._thread: threading.Thread | None = None
+
+    def __enter__(self) -> "ClockSampler":
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL,
+                text=True,
+            )
+            self._thread = threading.Thread(target=self._read, daemon=True)
+            self._thread.start()
+            time.sleep(0.3)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self) -> None:
+        assert self.proc is not None and self.proc.stdout is not None
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc) -> None:
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            with contextlib.suppress(Exception):
+                self.proc.wait(timeout=5)
+            if self._thread is not None:
+                self._thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        mhz: list[float] = []
+        max_mhz: list[float] = []
+        reasons: set[str] = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                max_mhz.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, value in zip(names, parts[5:9]):
+                if value.lower() == "active":
+                    reasons.add(name)
+        if not mhz:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {
+            "sm_mhz": statistics.median(mhz),
+            "sm_max_mhz": max(max_mhz),
+            "reasons": sorted(reasons),
+            "samples": len(mhz),
+        }
+
+
+def _dist_env() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def _max_over_ranks(value: float, world: int, device: torch.device) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier_sync(world: int, device: torch.device) -> None:
+    torch.cuda.synchronize(device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[device.index])
+    torch.cuda.synchronize(device)
+
+
+# ---------------------------------------------------------------------------
+# b200 arm
+# ---------------------------------------------------------------------------
+
+
+def _make_inputs(w: Workload, rank: int, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    gen = torch.Generator().manual_seed(1 + rank)
+    x = torch.randn(w.rows_per_gpu, w.in_features, generator=gen)
+    g = torch.randn(w.rows_per_gpu, 1, w.out_features, generator=gen)
+    return x, g
+
+
+def _step(layer, x: torch.Tensor, g: torch.Tensor, w: Workload, world: int) -> torch.Tensor:
+    from tropnn_b200.distributed import allreduce_gradients
+
+    if w.train:
+        for p in layer.parameters():
+            p.grad = None
+        y = layer(x)
+        y.backward(g)
+        if world > 1:
+            allreduce_gradients(layer)
+        return y
+    with torch.no_grad():
+        return layer(x)
+
+
+def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
+    import tropnn_b200
+    from tropnn_b200 import trace
+
+    rank, world, local_rank = _dist_env()
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    tropnn_b200._native.load()
+
+    layer = w.build().to(device).train(w.train)
+    x_host, g_host = _make_inputs(w, rank, device)
+    x = x_host.to(device).requires_grad_(w.train)
+    g = g_host.to(device)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+
+    for _ in range(args.warmup):
+        _step(layer, x, g, w, world)
+    _barrier_sync(world, device)
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(device)
+    with sampler, trace.launch_trace() as tr:
+        _barrier_sync(world, device)
+        for i in range(args.steps):
+            flush.fill_(float(i))  # untimed: evicts L2 between timed steps
+            starts[i].record()
+            _step(layer, x, g, w, world)
+            ends[i].record()
+        _barrier_sync(world, device)
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = _max_over_ranks(sum(step_ms), world, device)
+    kernels = tr.summary()
+    launches = tr.launches
+
+    # End to end: inputs from pinned host memory, output + input gradient back to host.
+    x_pin = x_host.pin_memory()
+    g_pin = g_host.pin_memory()
+    y_pin = torch.empty((w.rows_per_gpu, 1, w.out_features), dtype=torch.float32).pin_memory()
+    gx_pin = torch.empty_like(x_host).pin_memory()
+    h2d = x_pin.numel() * 4 + (g_pin.numel() * 4 if w.train else 0)
+    d2h = y_pin.numel() * 4 + (gx_pin.numel() * 4 if w.train else 0)
+    e2e_steps = max(3, args.steps)
+
+    def e2e_step() -> None:
+        xd = x_pin.to(device, non_blocking=True).requires_grad_(w.train)
+        gd = g_pin.to(device, non_blocking=True) if w.train else None
+        y = _step(layer, xd, gd, w, world)
+        y_pin.copy_(y.detach().float(), non_blocking=True)
+        if w.train:
+            gx_pin.copy_(xd.grad, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    _barrier_sync(world, device)
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e_end.record()
+    _barrier_sync(world, device)
+    e2e_ms = _max_over_ranks(e_start.elapsed_time(e_end), world, device)
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+
+    rows_total = w.rows_per_gpu * world
+    value = rows_total * args.steps / (total_ms / 1e3)
+    e2e_value = rows_total * e2e_steps / (e2e_ms / 1e3)
+
+    peaks, peaks_kind = _peaks()
+    roofline = None
+    candidates = {k: v for k, v in kernels.items() if algorithmic_bytes(w, k, w.rows_per_gpu) is not None}
+    if candidates:
+        top = max(candidates, key=lambda k: candidates[k]["total_ms"])
+        per_launch = algorithmic_bytes(w, top, w.rows_per_gpu)
+        mean_s = candidates[top]["mean_ms"] / 1e3
+        achieved = per_launch / mean_s / 1e9
+        traffic = None
+        if TRAFFIC_PATH.exists():
+            traffic = json.loads(TRAFFIC_PATH.read_text()).get(w.name, {}).get(top)
+        roofline = {
+            "kernel": top,
+            "bound": "hbm",
+            "achieved": round(achieved, 1),
+            "peak": peaks["hbm_gbs"],
+            "peak_source": f"{peaks_kind} hbm_gbs",
+            "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 3),
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": per_launch,
+            "mean_launch_us": round(mean_s * 1e6, 2),
+        }
+
+    return {
+        "metric": "TropLinear/PairwiseLinear rows/s fwd+bwd, 1-8 B200; % of HBM/TC roofline",
+        "value": round(value, 1),
+        "unit": "rows/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32" if w.dtype == "float32" else "f16 params / f32 accumulate",
+        "data": "synthetic (seeded N(0,1) inputs and upstream grads; seeded default init)",
+        "config": {
+            "workload": w.description,
+            "rows_per_gpu": w.rows_per_gpu,
+            "global_batch": rows_total,
+            "parallelism": f"dp{world} (batch-row shards, NCCL grad all-reduce)" if world > 1 else "single GPU",
+            "l2": f"flushed between timed steps ({L2_FLUSH_BYTES >> 20} MiB write, untimed)",
+        },
+        "e2e": {
+            "value": round(e2e_value, 1),
+            "unit": "rows/s",
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "ms_per_step": round(e2e_ms / e2e_steps, 4),
+        },
+        "gpu_launches": launches,
+        "kernels": {k: {"launches": v["launches"], "mean_us": round(v["mean_ms"] * 1e3, 2)} for k, v in kernels.items()},
+        "roofline": roofline,
+        "clocks": sampler.summary(),
+    }
+
+
+# ---------------------------------------------------------------------------
+# CPU arm (oracle port of the reference's torch path)
+# ---------------------------------------------------------------------------
+
+
+def _oracle_params(w: Workload) -> tuple[dict[str, np.ndarray], object]:
+    """Seeded parameters as numpy; half tensors are upcast once (exactly, as the reference's
+    ``.to(compute_dtype)`` does on every call) so the timed steps do not repeat it."""
+    layer = w.build()
+    params = {}
+    for k, v in layer.state_dict().items():
+        a = v.detach().numpy()
+        params[k] = a.astype(np.float32) if a.dtype == np.float16 else a
+    return params, layer
+
+
+def _oracle_step(w: Workload, params: dict, layer, x: np.ndarray, g: np.ndarray) -> None:
+    import oracle
+
+    if w.kind == "pairwise":
+        fwd = oracle.pairwise_forward(x, params["anchors"], params["thresholds"], params["lut"], output_scale=layer.output_scale)
+        if w.train:
+            oracle.pairwise_backward(
+                g, fwd["indices"], fwd["margins"], params["anchors"], params["lut"], in_features=w.in_features,
+                output_scale=layer.output_scale, use_min_margin_ste=layer.use_min_margin_ste, surrogate=layer.surrogate,
+            )
+        return
+    fwd = oracle.trop_linear_forward(x, params, code_scale=layer.code_scale, training=w.train, param_dtype=w.dtype)
+    if w.train:
+        oracle.trop_linear_backward(g, x, params, fwd, code_scale=layer.code_scale, training=True, param_dtype=w.dtype)
+
+
+_POOL_STATE: dict = {}
+
+
+def _pool_init(workload: str, sample_rows: int, workers: int) -> None:
+    """Spawned CPU worker: one BLAS thread, its own seeded parameters and row chunk."""
+    from threadpoolctl import threadpool_limits
+
+    torch.set_num_threads(1)
+    _POOL_STATE["limits"] = threadpool_limits(limits=1)
+    w = WORKLOADS[workload]
+    params, layer = _oracle_params(w)
+    gen = np.random.default_rng(7)
+    x = gen.standard_normal((sample_rows, w.in_features), dtype=np.float32)
+    g = gen.standard_normal((sample_rows, w.out_features), dtype=np.float32)
+    _POOL_STATE.update(w=w, params=params, layer=layer, x=x, g=g,
+                       chunks=[c for c in np.array_split(np.arange(sample_rows), workers) if c.size])
+
+
+def _pool_task(i: int) -> int:
+    s = _POOL_STATE
+    chunks = s["chunks"]
+    if i < len(chunks):
+        c = chunks[i]
+        _oracle_step(s["w"], s["params"], s["layer"], s["x"][c], s["g"][c])
+    return i
+
+
+def time_cpu(w: Workload, sample_rows: int, workers: int, *, reps: int | None = None, budget_s: float = 10.0,
+             warmup: int = 1) -> dict:
+    """rows/s of the oracle on ``sample_rows`` rows per step, the rows split over ``workers``
+    spawn-started processes (one core each). Wall time of ``reps`` steps (or of as many
+    steps as fit in ``budget_s``) after ``warmup`` steps."""
+    import multiprocessing
+
+    ctx = multiprocessing.get_context("spawn")
+    with ctx.Pool(workers, initializer=_pool_init, initargs=(w.name, sample_rows, workers)) as pool:
+        for _ in range(max(1, warmup)):
+            pool.map(_pool_task, range(workers), chunksize=1)
+        done = 0
+        t0 = time.perf_counter()
+        while (reps is not None and done < reps) or (reps is None and (done == 0 or time.perf_counter() - t0 < budget_s)):
+            pool.map(_pool_task, range(workers), chunksize=1)
+            done += 1
+        dt = time.perf_counter() - t0
+    return {"rows_per_s": sample_rows * done / dt, "seconds": dt, "steps": done}
+
+
+def cpu_baseline(w: Workload, budget_s: float) -> dict:
+    workers = os.cpu_count() or 1
+    sample = w.cpu_rows
+    res = time_cpu(w, sample, workers, budget_s=budget_s, warmup=2)
+    return {
+        "value": round(res["rows_per_s"], 1),
+        "unit": "rows/s",
+        "cores": workers,
+        "kind": "port",
+        "sample": f"{res['steps']} steps x {sample} rows of {w.name} (numpy oracle of the reference torch CPU path), "
+        f"{res['seconds']:.1f} s over {workers} single-threaded processes",
+    }
+
+
+def run_reference(args: argparse.Namespace, w: Workload) -> dict | None:
+    rank, world, _ = _dist_env()
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    sample = w.cpu_rows
+    res = time_cpu(w, sample, threads, reps=args.steps, warmup=args.warmup)
+    value = res["rows_per_s"]
+    return {
+        "metric": "TropLinear/PairwiseLinear rows/s fwd+bwd, 1-8 B200; % of HBM/TC roofline",
+        "impl": "reference",
+        "value": round(value, 1),
+        "unit": "rows/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(res["seconds"] / args.steps * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32" if w.dtype == "float32" else "f16 params / f32 accumulate",
+        "data": "synthetic (seeded N(0,1) inputs and upstream grads; seeded default init)",
+        "config": {"workload": w.description, "rows_per_step_sample": sample},
+        "cpu_baseline": {
+            "value": round(value, 1),
+            "unit": "rows/s",
+            "cores": threads,
+            "kind": "port",
+            "sample": f"{args.steps} steps x {sample} rows (numpy oracle of the reference torch CPU path, "
+            f"{threads} single-threaded processes)",
+        },
+        "e2e": {"value": round(value, 1), "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main(argv: list[str] | None = None) -> int:
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=50)
+    parser.add_argument("--warmup", type=int, default=10)
+    parser.add_argument("--workload", choices=sorted(WORKLOADS), default="pairwise_cfg2")
+    parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    parser.add_argument("--cpu-budget-s", type=float, default=10.0, help="seconds of CPU-baseline timing (rank 0, N=1)")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args(argv)
+    if args.warmup < 3 and args.impl == "b200":
+        parser.error("--warmup must be >= 3")
+    w = WORKLOADS[args.workload]
+    _, world, _ = _dist_env()
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}; reporting WORLD_SIZE", file=sys.stderr)
+
+    if args.impl == "reference":
+        line = run_reference(args, w)
+    else:
+        line = run_b200(args, w)
+        if line is not None and world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(w, args.cpu_budget_s)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

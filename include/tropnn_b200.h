@@ -1,0 +1,245 @@
+/*
+ * tropnn_b200 — C ABI of the sm_100a kernels behind backend="b200".
+ *
+ * Every entry point takes plain device pointers, int64 sizes, dtype enums and a
+ * cudaStream_t passed as `void *` (NULL = legacy default stream). Nothing here
+ * allocates or frees device memory: outputs, saved route state and the scratch
+ * "workspace" are owned by the caller (the Python host side uses PyTorch's
+ * caching allocator). Work is stream-ordered; no entry point synchronises the
+ * host. Each returns 0 on success or a negative tropnn_b200_status; the message
+ * of the last failure on the calling thread is tropnn_b200_last_error().
+ *
+ * Reference interfaces replaced (paths inside the tropnn package):
+ *   TropLinear route + hidden:   backends/tilelang_route.py:496-585 (_run_trop_forward),
+ *                                layers/tropical.py:148-221 (_route_output, torch path)
+ *   TropLinear min-face backward: backends/tilelang_route.py:619-677,
+ *                                backends/triton_backward.py:357-515,
+ *                                layers/tropical_exact.py:164-237
+ *   PairwiseLinear forward:      backends/pairwise_tilelang.py:413-457 (_run_forward),
+ *                                layers/pairwise.py:99-135
+ *   PairwiseLinear STE backward: backends/pairwise_tilelang.py:482-534,
+ *                                layers/pairwise.py:137-200
+ */
+#ifndef TROPNN_B200_H
+#define TROPNN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TROPNN_B200_API __attribute__((visibility("default")))
+#else
+#define TROPNN_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum tropnn_b200_status {
+  TROPNN_B200_OK = 0,
+  TROPNN_B200_ERR_INVALID = -1,   /* bad shape, size, pointer or flag (host raises ValueError) */
+  TROPNN_B200_ERR_DTYPE = -2,     /* unsupported dtype (host raises TypeError) */
+  TROPNN_B200_ERR_DEVICE = -3,    /* current device is not sm_100 (RuntimeError) */
+  TROPNN_B200_ERR_LAUNCH = -4,    /* CUDA launch or runtime error (RuntimeError) */
+  TROPNN_B200_ERR_WORKSPACE = -5, /* workspace too small (RuntimeError) */
+  TROPNN_B200_ERR_TIMEOUT = -6    /* a bounded device-side wait gave up (RuntimeError) */
+} tropnn_b200_status;
+
+/* Element types of parameters and of outputs written in parameter precision. */
+typedef enum tropnn_b200_dtype {
+  TROPNN_B200_F32 = 0,
+  TROPNN_B200_F16 = 1,
+  TROPNN_B200_BF16 = 2,
+  TROPNN_B200_U8 = 3,  /* packed route indices (cells <= 256) */
+  TROPNN_B200_I16 = 4, /* packed route indices (cells <= 32767) */
+  TROPNN_B200_I64 = 5  /* route indices otherwise */
+} tropnn_b200_dtype;
+
+/* STE surrogates of layers/surrogate.py:9-17. */
+typedef enum tropnn_b200_surrogate {
+  TROPNN_B200_SURROGATE_FAST_SIGMOID_ODD = 0,
+  TROPNN_B200_SURROGATE_IZHIKEVICH = 1
+} tropnn_b200_surrogate;
+
+/* ------------------------------------------------------------------ misc */
+
+/* Message of the last failing call on this host thread ("" if none). */
+TROPNN_B200_API const char *tropnn_b200_last_error(void);
+/* ABI revision; bumped whenever a signature below changes. */
+TROPNN_B200_API int tropnn_b200_abi_version(void);
+/* TROPNN_B200_OK when `device` is an sm_100 GPU, else TROPNN_B200_ERR_DEVICE. */
+TROPNN_B200_API int tropnn_b200_check_device(int device);
+
+/* ------------------------------------------------------- shared machinery */
+
+/*
+ * Stable counting sort of rows by route bucket, one group (head or table) at a time.
+ * keys[n * key_row_stride + g] (dtype U8/I16/I64) is the bucket of row n in group g.
+ * Writes perm[g * rows + j] (row ids, grouped by bucket, ascending row order inside a
+ * bucket) and seg[g * (buckets + 1) + b] (start of bucket b; seg[.. + buckets] = rows).
+ * buckets <= 4096. This is the gather-side replacement of the scatter-add atomics in
+ * backends/pairwise_tilelang.py:118-156 and backends/triton_backward.py:224-305.
+ */
+TROPNN_B200_API int tropnn_b200_bucket_sort(const void *keys, int key_dtype, int64_t rows, int64_t groups,
+                            int64_t key_row_stride, int64_t buckets, int32_t *perm, int32_t *seg,
+                            void *stream);
+
+/*
+ * Segmented weighted row sum: for every group g, bucket b and column j < width
+ *   out[(g*buckets + b)*width + j] = scale * ( sum_{n in list0(g,b)} c0(n,g) * values[n*ld + j]
+ *                                            + sum_{n in list1(g,b)} c1(n,g) * values[n*ld + j] )
+ * where list_i(g,b) = perm_i[g*rows + seg_i[g*(buckets+1)+b] ..< seg_i[..+b+1]] and
+ * c_i(n,g) = coef_sign_i * coef_i[n*groups + g] (or coef_sign_i when coef_i is NULL).
+ * perm1/seg1 may be NULL (one list). Every element of `out` is written exactly once
+ * (buckets without rows get 0), in out_dtype (F32/F16/BF16). If bucket_sum is not
+ * NULL it receives scale * sum of the coefficients per (g, b) in out_dtype.
+ * Deterministic: the summation order is fixed by (perm, seg).
+ */
+TROPNN_B200_API int tropnn_b200_segment_rowsum(const float *values, int64_t rows, int64_t width, int64_t ld,
+                               int64_t groups, int64_t buckets,
+                               const int32_t *perm0, const int32_t *seg0, const float *coef0, float coef_sign0,
+                               const int32_t *perm1, const int32_t *seg1, const float *coef1, float coef_sign1,
+                               float scale, void *out, int out_dtype, void *bucket_sum, void *stream);
+
+/* --------------------------------------------------------- PairwiseLinear */
+
+/*
+ * Fused comparator routing + LUT gather-sum (layers/pairwise.py:99-135, base.py:76-77).
+ *   u[n,t,r]   = (latent[n,a] - latent[n,b]) - thresholds[t,r],  (a,b) = anchors[t,r,:]
+ *   idx[n,t]   = sum_r [u[n,t,r] > 0] << r
+ *   out[n,o]   = output_scale * sum_t lut[t, idx[n,t], o]
+ * latent f32 [items, in_features]; anchors int64 [tables, comparisons, 2];
+ * thresholds [tables, comparisons] and lut [tables, 2^comparisons, out_features] in
+ * their own dtypes (F32/F16/BF16). Outputs: out f32 [items, out_features],
+ * indices int64 [items, tables], margins f32 [items, tables, comparisons].
+ * comparisons <= 12.
+ */
+TROPNN_B200_API int tropnn_b200_pairwise_forward(const float *latent, int64_t items, int64_t in_features,
+                                 const int64_t *anchors, const void *thresholds, int thresholds_dtype,
+                                 int64_t tables, int64_t comparisons,
+                                 const void *lut, int lut_dtype, int64_t out_features, float output_scale,
+                                 float *out, int64_t *indices, float *margins, void *stream);
+
+/*
+ * Inverse anchor map used by the STE backward to gather grad_latent without atomics:
+ * entries of anchors (flattened, e = (t*comparisons + r)*2 + side) grouped by input
+ * feature. feat_start [in_features + 1] int32, feat_entries [tables*comparisons*2] int32.
+ * Depends only on the anchors buffer; callers cache it.
+ */
+TROPNN_B200_API int tropnn_b200_pairwise_anchor_index(const int64_t *anchors, int64_t tables, int64_t comparisons,
+                                      int64_t in_features, int32_t *feat_start, int32_t *feat_entries,
+                                      void *stream);
+
+/*
+ * STE backward rows (layers/pairwise.py:137-200 and their autograd; the surrogate of
+ * layers/surrogate.py:9-17): with g = output_scale * grad_out,
+ *   min mode:  r* = argmin_r |u[n,t,r]| (first on ties), nb = idx ^ (1<<r*),
+ *              gu[n,t] = (sum_o g[n,o] (lut[t,nb,o] - lut[t,idx,o])) * S(u[n,t,r*])
+ *   full mode: the same for every r, gu[n,t,r].
+ *   grad_latent[n,i] = sum over anchor entries of feature i of +gu (side 0) / -gu (side 1).
+ * Writes grad_latent f32 [items, in_features], gu f32 ([items, tables] or
+ * [items, tables, comparisons]) and rstar u8 [items, tables] (min mode only).
+ */
+TROPNN_B200_API int tropnn_b200_pairwise_ste_backward(const float *grad_out, int64_t items, int64_t out_features,
+                                      float output_scale, const int64_t *indices, const float *margins,
+                                      const int64_t *anchors, int64_t tables, int64_t comparisons,
+                                      int64_t in_features, const void *lut, int lut_dtype,
+                                      int use_min_margin_ste, int surrogate,
+                                      const int32_t *feat_start, const int32_t *feat_entries,
+                                      float *grad_latent, float *gu, uint8_t *rstar, void *stream);
+
+/*
+ * grad_thresholds[t,r] = -sum_n gu (min mode: rows whose r* == r), fixed-order
+ * reduction, written in grad_dtype.
+ */
+TROPNN_B200_API int tropnn_b200_pairwise_threshold_grad(const float *gu, const uint8_t *rstar, int64_t items,
+                                        int64_t tables, int64_t comparisons, int use_min_margin_ste,
+                                        void *grad_thresholds, int grad_dtype, void *stream);
+
+/* Bytes of scratch tropnn_b200_pairwise_backward needs. */
+TROPNN_B200_API size_t tropnn_b200_pairwise_backward_workspace_size(int64_t items, int64_t tables, int64_t comparisons,
+                                                    int64_t in_features, int use_min_margin_ste);
+
+/*
+ * Whole PairwiseLinear backward (the autograd backward of pairwise.py:202-248):
+ * grad_lut (lut dtype, may be NULL), grad_latent (f32, NULL to skip the STE part) and
+ * grad_thresholds (grad_thresholds_dtype, may be NULL). Runs bucket_sort +
+ * segment_rowsum for the LUT and anchor_index + ste_backward + threshold_grad for
+ * the STE terms, all inside `workspace`.
+ */
+TROPNN_B200_API int tropnn_b200_pairwise_backward(const float *grad_out, int64_t items, int64_t out_features,
+                                  float output_scale, const int64_t *indices, const float *margins,
+                                  const int64_t *anchors, int64_t tables, int64_t comparisons,
+                                  int64_t in_features, const void *lut, int lut_dtype,
+                                  int use_min_margin_ste, int surrogate,
+                                  float *grad_latent, void *grad_thresholds, int grad_thresholds_dtype,
+                                  void *grad_lut, void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------ TropLinear */
+
+/*
+ * Route scores, top-2 and margins (backend.py:45-46, routing.py:7-10):
+ *   s[n,h,k] = <latent[n,:], router_weight[h,k,:]> + router_bias[h,k]
+ *   winner/runner = top-2 cells (lowest index on exact ties), margin = s_w - s_r.
+ * latent f32 [items, code_dim]; router_weight [heads, cells, code_dim] and router_bias
+ * [heads, cells] in param_dtype. winner_i64 (int64 [items, heads], may be NULL),
+ * winner/runner in index_dtype (U8/I16/I64, the packing of routing.py:18-31),
+ * margins f32 [items, heads].
+ */
+TROPNN_B200_API int tropnn_b200_trop_route(const float *latent, int64_t items, int64_t code_dim,
+                           const void *router_weight, const void *router_bias, int param_dtype,
+                           int64_t heads, int64_t cells,
+                           int64_t *winner_i64, void *winner, void *runner, int index_dtype,
+                           float *margins, void *stream);
+
+/*
+ * hidden[n,:] = latent[n,:] + code_scale * sum_h chat[n,h,:] with chat = code[h,w] (eval)
+ * or code[h,w] + U(m) (code[h,r] - code[h,w]), U(m) = 0.5/(1+|m|) (training)
+ * (layers/tropical.py:131-138, routing.py:13-15). code in param_dtype.
+ */
+TROPNN_B200_API int tropnn_b200_trop_hidden(const float *latent, int64_t items, int64_t code_dim,
+                            const void *code, int param_dtype, int64_t heads, int64_t cells,
+                            const void *winner, const void *runner, int index_dtype,
+                            const float *margins, float code_scale, int training,
+                            float *hidden, void *stream);
+
+/*
+ * Per-row part of the min-face backward (layers/tropical_exact.py:204-237):
+ *   training: gm[n,h] = code_scale * U'(m) * sum_d g[n,d] (code[h,r,d] - code[h,w,d]),
+ *             U'(m) = -0.5 sign(m) / (1+|m|)^2
+ *             grad_latent[n,:] = g[n,:] + sum_h gm[n,h] (W[h,w,:] - W[h,r,:])
+ *             coef_w = code_scale (1 - U(m)), coef_r = code_scale U(m)
+ *   eval:     grad_latent = g, coef_w = code_scale (gm, coef_r untouched).
+ * All per-row outputs f32: grad_latent [items, code_dim], coef_w/coef_r/gm [items, heads].
+ */
+TROPNN_B200_API int tropnn_b200_trop_backward_rows(const float *grad_hidden, int64_t items, int64_t code_dim,
+                                   const void *router_weight, const void *code, int param_dtype,
+                                   int64_t heads, int64_t cells,
+                                   const void *winner, const void *runner, int index_dtype,
+                                   const float *margins, float code_scale, int training,
+                                   float *grad_latent, float *coef_w, float *coef_r, float *gm,
+                                   void *stream);
+
+/* Bytes of scratch tropnn_b200_trop_backward needs. */
+TROPNN_B200_API size_t tropnn_b200_trop_backward_workspace_size(int64_t items, int64_t heads, int64_t cells, int training);
+
+/*
+ * Whole TropLinear route backward (the autograd backward of tropical.py:207-221):
+ * grad_latent f32 [items, code_dim]; grad_code [heads, cells, code_dim] and, in
+ * training, grad_router_weight / grad_router_bias, all in param_dtype (NULL skips).
+ * Runs backward_rows, two bucket sorts and two segment_rowsum passes in `workspace`.
+ */
+TROPNN_B200_API int tropnn_b200_trop_backward(const float *grad_hidden, const float *latent, int64_t items, int64_t code_dim,
+                              const void *router_weight, const void *code, int param_dtype,
+                              int64_t heads, int64_t cells,
+                              const void *winner, const void *runner, int index_dtype,
+                              const float *margins, float code_scale, int training,
+                              float *grad_latent, void *grad_router_weight, void *grad_router_bias,
+                              void *grad_code, void *workspace, size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TROPNN_B200_H */

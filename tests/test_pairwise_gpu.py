@@ -1,0 +1,226 @@
+"""PairwiseLinear backend="b200" on the GPU against the reference's golden vectors and the
+numpy oracle (parity rule: indices bit-exact, values within 1e-5 relative in fp32 and
+2e-2 relative with f16/bf16 parameters)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import tropnn_b200
+from tests.golden_cases import build_layer, case_names, load_case, rel_err, state_arrays, tolerance
+from tests.gpu_runner import run_b200
+
+pytestmark = pytest.mark.gpu
+FP32_TOL = 1e-5
+
+
+@pytest.mark.parametrize("name", case_names("pairwise"))
+def test_pairwise_matches_reference_golden(name: str) -> None:
+    arrays, meta = load_case(name)
+    layer = build_layer(arrays, meta)
+    got = run_b200(layer, arrays, meta)
+    tol = tolerance(meta)
+    assert rel_err(got["y"], arrays["y"]) <= tol
+    assert np.array_equal(got["last_indices"], arrays["last_indices"])
+    assert np.array_equal(got["last_margins"], arrays["last_margins"])
+    if meta["train"]:
+        assert rel_err(got["grad.x"], arrays["grad.x"]) <= tol
+        for key in ("lut", "thresholds"):
+            assert bool(got[f"has_grad.{key}"]) == bool(arrays[f"has_grad.{key}"])
+            assert rel_err(got[f"grad.{key}"], arrays[f"grad.{key}"].astype(np.float32)) <= tol, key
+
+
+def _oracle_case(layer: tropnn_b200.PairwiseLinear, x: np.ndarray, g: np.ndarray, *, ste: bool = True) -> dict:
+    st = state_arrays(layer)
+    fwd = oracle.pairwise_forward(x, st["anchors"], st["thresholds"], st["lut"], output_scale=layer.output_scale)
+    bwd = oracle.pairwise_backward(
+        g,
+        fwd["indices"],
+        fwd["margins"],
+        st["anchors"],
+        st["lut"],
+        in_features=layer.in_features,
+        output_scale=layer.output_scale,
+        use_min_margin_ste=layer.use_min_margin_ste,
+        surrogate=layer.surrogate,
+        ste=ste,
+    )
+    return {**fwd, **{f"grad.{k}": v for k, v in bwd.items()}}
+
+
+def _run(layer: tropnn_b200.PairwiseLinear, x: np.ndarray, g: np.ndarray, *, train: bool = True) -> dict:
+    layer = layer.cuda().train(train)
+    xt = torch.from_numpy(x).cuda().requires_grad_(True)
+    y = layer(xt)
+    y.backward(torch.from_numpy(g).cuda().view_as(y))
+    torch.cuda.synchronize()
+    return {
+        "out": y.detach().cpu().numpy().reshape(x.shape[0], -1),
+        "indices": layer._last_indices.cpu().numpy().reshape(x.shape[0], -1),
+        "margins": layer._last_margins.cpu().numpy().reshape(x.shape[0], layer.tables, layer.comparisons),
+        "grad.x": None if xt.grad is None else xt.grad.cpu().numpy(),
+        "grad.lut": None if layer.lut.grad is None else layer.lut.grad.float().cpu().numpy(),
+        "grad.thresholds": None if layer.thresholds.grad is None else layer.thresholds.grad.float().cpu().numpy(),
+    }
+
+
+def _inputs(n: int, in_f: int, out_f: int, seed: int = 1) -> tuple[np.ndarray, np.ndarray]:
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randn(n, in_f, generator=gen).numpy(), torch.randn(n, out_f, generator=gen).numpy()
+
+
+def _compare(got: dict, ref: dict, tol: float = FP32_TOL) -> None:
+    assert np.array_equal(got["indices"], ref["indices"])
+    assert np.array_equal(got["margins"], ref["margins"])
+    assert rel_err(got["out"], ref["out"]) <= tol
+    for key in ("grad.x", "grad.lut", "grad.thresholds"):
+        if ref[key] is None:
+            assert got[key] is None, key
+        else:
+            assert rel_err(got[key], ref[key]) <= tol, key
+
+
+def test_config2_batch4096_matches_oracle() -> None:
+    """Config 2 at its full batch: PairwiseLinear(256->512, T16, C6) fwd + min-margin STE bwd."""
+    layer = tropnn_b200.PairwiseLinear(256, 512, tables=16, comparisons=6, seed=0)
+    x, g = _inputs(4096, 256, 512)
+    ref = _oracle_case(layer, x, g)
+    _compare(_run(layer, x, g), ref)
+
+
+@pytest.mark.parametrize("surrogate", ["fast_sigmoid_odd", "izhikevich"])
+@pytest.mark.parametrize("use_min", [True, False])
+def test_ste_modes_and_surrogates(surrogate: str, use_min: bool) -> None:
+    layer = tropnn_b200.PairwiseLinear(64, 96, tables=24, comparisons=5, seed=3, surrogate=surrogate, use_min_margin_ste=use_min)
+    with torch.no_grad():
+        layer.thresholds.normal_(0.0, 0.3)
+    x, g = _inputs(300, 64, 96, seed=4)
+    _compare(_run(layer, x, g), _oracle_case(layer, x, g))
+
+
+@pytest.mark.parametrize(
+    ("in_f", "out_f", "tables", "comparisons", "n"),
+    [
+        (2, 1, 1, 1, 5),  # minimum sizes
+        (784, 10, 136, 6, 512),  # config 4 layer 2: ragged width (scalar path)
+        (128, 130, 7, 12, 33),  # maximum comparisons, ragged rows
+        (300, 1000, 3, 2, 17),  # wide output, several column tiles
+    ],
+)
+def test_shapes_and_edges(in_f: int, out_f: int, tables: int, comparisons: int, n: int) -> None:
+    layer = tropnn_b200.PairwiseLinear(in_f, out_f, tables=tables, comparisons=comparisons, seed=5)
+    x, g = _inputs(n, in_f, out_f, seed=6)
+    _compare(_run(layer, x, g), _oracle_case(layer, x, g))
+
+
+def test_empty_batch() -> None:
+    layer = tropnn_b200.PairwiseLinear(16, 8, tables=4, comparisons=3).cuda()
+    x = torch.empty(0, 16, device="cuda", requires_grad=True)
+    y = layer(x)
+    assert y.shape == (0, 1, 8)
+    y.sum().backward()
+    assert x.grad.shape == (0, 16)
+    assert float(layer.lut.grad.abs().sum()) == 0.0
+
+
+def test_three_d_input_and_f16_input_dtype() -> None:
+    layer = tropnn_b200.PairwiseLinear(32, 24, tables=8, comparisons=4, seed=2).cuda()
+    x = torch.randn(3, 5, 32, device="cuda").half()
+    y = layer(x)
+    assert y.shape == (3, 5, 24) and y.dtype == torch.float16
+    assert layer._last_indices.shape == (3, 5, 8) and layer._last_indices.dtype == torch.int64
+    assert layer._last_margins.shape == (3, 5, 8, 4)
+    ref = oracle.pairwise_forward(
+        x.float().reshape(15, 32).cpu().numpy(), *(t.cpu().numpy() for t in (layer.anchors, layer.thresholds, layer.lut)),
+        output_scale=layer.output_scale,
+    )
+    assert rel_err(y.float().reshape(15, 24).cpu().numpy(), ref["out"]) <= 1e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_half_precision_parameters(dtype: torch.dtype) -> None:
+    layer = tropnn_b200.PairwiseLinear(128, 256, tables=32, comparisons=8, seed=0).to(dtype)
+    x, g = _inputs(257, 128, 256, seed=8)
+    got = _run(layer, x, g)
+    ref = _oracle_case(layer, x, g)
+    assert np.array_equal(got["indices"], ref["indices"])
+    for key in ("out", "grad.x", "grad.lut", "grad.thresholds"):
+        assert rel_err(got[key], ref[key]) <= 2e-2, key
+    assert layer.lut.grad.dtype == dtype and layer.thresholds.grad.dtype == dtype
+
+
+def test_eval_mode_with_grad_gives_lut_grad_only() -> None:
+    """The STE term is live only in training (layers/pairwise.py:245); eval backward gives LUT grads only."""
+    layer = tropnn_b200.PairwiseLinear(64, 32, tables=8, comparisons=4, seed=1)
+    x, g = _inputs(40, 64, 32)
+    got = _run(layer, x, g, train=False)
+    ref = _oracle_case(layer, x, g, ste=False)
+    assert got["grad.x"] is None and got["grad.thresholds"] is None
+    assert rel_err(got["grad.lut"], ref["grad.lut"]) <= FP32_TOL
+
+
+def test_backward_is_deterministic() -> None:
+    layer = tropnn_b200.PairwiseLinear(256, 512, tables=16, comparisons=6, seed=0)
+    x, g = _inputs(4096, 256, 512)
+    a = _run(layer, x, g)
+    layer.zero_grad(set_to_none=True)
+    b = _run(layer, x, g)
+    for key in ("out", "grad.x", "grad.lut", "grad.thresholds"):
+        assert np.array_equal(a[key], b[key]), key
+
+
+def test_combined_c_abi_backward_matches_layer() -> None:
+    """tropnn_b200_pairwise_backward (one C call, caller-provided workspace) equals the layer path."""
+    from tropnn_b200 import _native as nat
+
+    layer = tropnn_b200.PairwiseLinear(96, 80, tables=12, comparisons=5, seed=9)
+    x, g = _inputs(200, 96, 80)
+    ref = _run(layer, x, g)
+    lib = nat.load()
+    dev = torch.device("cuda")
+    n, T, C, out_f = 200, 12, 5, 80
+    idx = torch.from_numpy(ref["indices"]).to(dev).contiguous()
+    u = torch.from_numpy(ref["margins"]).to(dev).contiguous()
+    gt = torch.from_numpy(g).to(dev).contiguous()
+    ws_bytes = lib.tropnn_b200_pairwise_backward_workspace_size(n, T, C, 96, 1)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    gx = torch.empty(n, 96, device=dev)
+    gthr = torch.empty(T, C, device=dev)
+    glut = torch.empty_like(layer.lut)
+    status = lib.tropnn_b200_pairwise_backward(
+        gt.data_ptr(), n, out_f, layer.output_scale, idx.data_ptr(), u.data_ptr(), layer.anchors.data_ptr(), T, C, 96,
+        layer.lut.data_ptr(), nat.F32, 1, 0, gx.data_ptr(), gthr.data_ptr(), nat.F32, glut.data_ptr(), ws.data_ptr(),
+        ws_bytes, torch.cuda.current_stream().cuda_stream,
+    )
+    nat.check(status, "pairwise_backward")
+    torch.cuda.synchronize()
+    assert np.array_equal(gx.cpu().numpy(), ref["grad.x"])
+    assert np.array_equal(gthr.cpu().numpy(), ref["grad.thresholds"])
+    assert np.array_equal(glut.cpu().numpy(), ref["grad.lut"])
+    with pytest.raises(RuntimeError, match="workspace"):
+        nat.check(
+            lib.tropnn_b200_pairwise_backward(
+                gt.data_ptr(), n, out_f, 1.0, idx.data_ptr(), u.data_ptr(), layer.anchors.data_ptr(), T, C, 96,
+                layer.lut.data_ptr(), nat.F32, 1, 0, gx.data_ptr(), gthr.data_ptr(), nat.F32, glut.data_ptr(),
+                ws.data_ptr(), ws_bytes - 256, torch.cuda.current_stream().cuda_stream,
+            ),
+            "pairwise_backward",
+        )
+
+
+def test_invalid_arguments_raise_value_and_type_errors() -> None:
+    layer = tropnn_b200.PairwiseLinear(16, 8, tables=4, comparisons=3).cuda()
+    x = torch.randn(2, 1, 16, device="cuda")
+    with pytest.raises(TypeError):
+        tropnn_b200.pairwise_b200(x.double(), layer.anchors, layer.thresholds, layer.lut, use_min_margin_ste=True)
+    with pytest.raises(ValueError):
+        tropnn_b200.pairwise_b200(x, layer.anchors[:2], layer.thresholds, layer.lut, use_min_margin_ste=True)
+    with pytest.raises(ValueError, match="surrogate"):
+        tropnn_b200.pairwise_b200(x, layer.anchors, layer.thresholds, layer.lut, use_min_margin_ste=True, surrogate="x")
+    with torch.no_grad():
+        layer.anchors[0, 0, 0] = 99
+    with pytest.raises(IndexError):
+        layer(x)

@@ -1,0 +1,216 @@
+"""TropLinear backend="b200" on the GPU against the reference's golden vectors and the numpy
+oracle. Route indices are compared where the top-2 margin exceeds 1e-4 relative (the
+parity gate); values within 1e-5 relative in fp32, 2e-2 with f16/bf16 parameters."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import tropnn_b200
+from tests.golden_cases import build_layer, case_names, load_case, rel_err, route_gate, state_arrays, tolerance
+from tests.gpu_runner import run_b200
+
+pytestmark = pytest.mark.gpu
+FP32_TOL = 1e-5
+
+
+def _gate_from_state(x: np.ndarray, st: dict) -> tuple[np.ndarray, np.ndarray]:
+    ref = oracle.trop_linear_forward(x, st, code_scale=1.0, training=False)
+    return route_gate(ref["scores"])
+
+
+@pytest.mark.parametrize("name", case_names("trop"))
+def test_trop_matches_reference_golden(name: str) -> None:
+    arrays, meta = load_case(name)
+    layer = build_layer(arrays, meta)
+    st = state_arrays(layer)
+    got = run_b200(layer, arrays, meta)
+    tol = tolerance(meta)
+    assert rel_err(got["y"], arrays["y"]) <= tol
+    x = arrays["x"].reshape(-1, arrays["x"].shape[-1]).astype(np.float32)
+    win, _ = _gate_from_state(x, st)
+    if "last_indices" in arrays:
+        assert np.array_equal(got["last_indices"].reshape(win.shape)[win], arrays["last_indices"].reshape(win.shape)[win])
+        assert rel_err(got["last_margins"], arrays["last_margins"]) <= max(tol, 1e-5)
+    else:
+        assert "last_indices" not in got  # cache_route_debug=False
+    if meta["train"]:
+        assert rel_err(got["grad.x"], arrays["grad.x"]) <= tol
+        for key in ("proj.weight", "router_weight", "router_bias", "code", "output_proj.weight", "output_proj.bias"):
+            assert bool(got[f"has_grad.{key}"]) == bool(arrays[f"has_grad.{key}"]), key
+            assert rel_err(got[f"grad.{key}"], arrays[f"grad.{key}"].astype(np.float32)) <= tol, key
+
+
+def _inputs(n: int, in_f: int, out_f: int, seed: int = 1, uniform: bool = False) -> tuple[np.ndarray, np.ndarray]:
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.rand(n, in_f, generator=gen) if uniform else torch.randn(n, in_f, generator=gen)
+    return x.numpy(), torch.randn(n, out_f, generator=gen).numpy()
+
+
+def _run(layer: tropnn_b200.TropLinear, x: np.ndarray, g: np.ndarray, *, train: bool) -> dict:
+    layer = layer.cuda().train(train)
+    xt = torch.from_numpy(x).cuda().requires_grad_(True)
+    y = layer(xt)
+    y.backward(torch.from_numpy(g).cuda().view_as(y))
+    torch.cuda.synchronize()
+    out = {"y": y.detach().float().cpu().numpy().reshape(x.shape[0], -1), "grad.x": xt.grad.cpu().numpy()}
+    out["winner"] = layer._last_indices.cpu().numpy().reshape(x.shape[0], -1)
+    out["margins"] = layer._last_margins.cpu().numpy().reshape(x.shape[0], -1)
+    for name, p in layer.named_parameters():
+        out[f"grad.{name}"] = None if p.grad is None else p.grad.float().cpu().numpy()
+    return out
+
+
+def _check_against_oracle(layer: tropnn_b200.TropLinear, x: np.ndarray, g: np.ndarray, *, train: bool, tol: float) -> None:
+    st = state_arrays(layer)
+    pdt = str(layer.proj.weight.dtype).replace("torch.", "")
+    fwd = oracle.trop_linear_forward(x, st, code_scale=layer.code_scale, training=train, param_dtype=pdt)
+    got = _run(layer, x, g, train=train)
+    win, _ = route_gate(fwd["scores"])
+    assert np.array_equal(got["winner"][win], fwd["winner"][win])
+    assert rel_err(got["margins"], fwd["margins"]) <= max(tol, 1e-5)
+    if not np.array_equal(got["winner"], fwd["winner"]):
+        pytest.skip("a near-tie route flipped; value comparison needs identical routes")
+    assert rel_err(got["y"], fwd["y"]) <= tol
+    ref = oracle.trop_linear_backward(g, x, st, fwd, code_scale=layer.code_scale, training=train, param_dtype=pdt)
+    assert rel_err(got["grad.x"], ref["x"]) <= tol
+    for key in ("proj.weight", "code", "output_proj.weight", "output_proj.bias"):
+        assert rel_err(got[f"grad.{key}"], ref[key]) <= tol, key
+    if train:
+        for key in ("router_weight", "router_bias"):
+            assert rel_err(got[f"grad.{key}"], ref[key]) <= tol, key
+    else:
+        assert got["grad.router_weight"] is None and got["grad.router_bias"] is None
+
+
+@pytest.mark.parametrize("train", [True, False])
+def test_config3_layer1_batch512(train: bool) -> None:
+    """Config 3 layer 1: TropLinear(784->128, H256, K16, D64), U[0,1] inputs, batch 512."""
+    layer = tropnn_b200.TropLinear(784, 128, heads=256, cells=16, code_dim=64, seed=0)
+    x, g = _inputs(512, 784, 128, uniform=True)
+    _check_against_oracle(layer, x, g, train=train, tol=FP32_TOL)
+
+
+@pytest.mark.parametrize(
+    ("in_f", "out_f", "heads", "cells", "code_dim", "n"),
+    [
+        (256, 512, 32, 4, 32, 8),  # config 1
+        (5, 3, 1, 2, 1, 7),  # minimum heads/cells/code_dim
+        (40, 20, 6, 300, 12, 64),  # int16 route packing (cells > 256)
+        (33, 17, 9, 256, 7, 130),  # u8 packing at its maximum, ragged code_dim
+        (64, 48, 16, 9, 256, 300),  # code_dim 256 (largest on the SIMT path)
+    ],
+)
+def test_shapes_and_edges(in_f: int, out_f: int, heads: int, cells: int, code_dim: int, n: int) -> None:
+    layer = tropnn_b200.TropLinear(in_f, out_f, heads=heads, cells=cells, code_dim=code_dim, seed=4)
+    x, g = _inputs(n, in_f, out_f, seed=2)
+    _check_against_oracle(layer, x, g, train=True, tol=FP32_TOL)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_half_precision_parameters(dtype: torch.dtype) -> None:
+    """Config-5 style: half parameters, f32 input, f32 accumulation."""
+    layer = tropnn_b200.TropLinear(256, 256, heads=64, cells=16, code_dim=64, seed=0)
+    with torch.no_grad():
+        layer.router_bias.copy_(torch.linspace(-2.0, 2.0, 16).expand_as(layer.router_bias))
+    layer = layer.to(dtype)
+    x, g = _inputs(256, 256, 256, seed=3)
+    _check_against_oracle(layer, x, g, train=True, tol=2e-2)
+    assert layer.code.grad.dtype == dtype and layer.router_weight.grad.dtype == dtype
+
+
+def test_eval_and_train_kats_on_gpu() -> None:
+    """tests/test_tropical_core.py:19-49 on the b200 kernels."""
+    layer = tropnn_b200.TropLinear(1, 1, heads=1, cells=3, code_dim=1, seed=0, use_output_scaling=False)
+    with torch.no_grad():
+        layer.proj.weight.fill_(1.0)
+        layer.router_weight[0, :, 0] = torch.tensor([1.0, 0.0, -1.0])
+        layer.router_bias.zero_()
+        layer.code[0, :, 0] = torch.tensor([10.0, 20.0, 30.0])
+        layer.output_proj.weight.fill_(1.0)
+        layer.output_proj.bias.zero_()
+    layer = layer.cuda().eval()
+    assert float(layer(torch.tensor([[2.0]], device="cuda")).squeeze()) == pytest.approx(12.0)
+    assert float(layer(torch.tensor([[-2.0]], device="cuda")).squeeze()) == pytest.approx(28.0)
+    with torch.no_grad():
+        layer.router_weight[0, :, 0] = torch.tensor([1.0, 0.9, -1.0], device="cuda")
+    layer.train()
+    y = float(layer(torch.tensor([[1.0]], device="cuda")).squeeze())
+    assert y == pytest.approx(1.0 + 10.0 + (0.5 / 1.1) * 10.0, abs=1e-6)
+
+
+def test_output_shapes_and_debug_cache() -> None:
+    layer = tropnn_b200.TropLinear(5, 3, heads=4, cells=3, code_dim=4, seed=0).cuda()
+    y2 = layer(torch.randn(7, 5, device="cuda"))
+    assert y2.shape == (7, 1, 3)
+    assert layer._last_indices.shape == (7, 1, 4) and layer._last_indices.dtype == torch.int64
+    y3 = layer(torch.randn(7, 2, 5, device="cuda"))
+    assert y3.shape == (7, 2, 3)
+    quiet = tropnn_b200.TropLinear(5, 3, heads=4, cells=3, code_dim=4, seed=0, cache_route_debug=False).cuda()
+    quiet(torch.randn(2, 5, device="cuda"))
+    assert quiet._last_indices is None and quiet._last_margins is None
+
+
+def test_index_forcing_backward_through_c_abi() -> None:
+    """Feeds the oracle's routes to tropnn_b200_trop_backward (one C call) to isolate the
+    backward arithmetic from the forward's routing."""
+    from tropnn_b200 import _native as nat
+
+    layer = tropnn_b200.TropLinear(48, 32, heads=16, cells=8, code_dim=24, seed=6)
+    n, D, H, K = 200, 24, 16, 8
+    x, _ = _inputs(n, 48, 32, seed=9)
+    st = state_arrays(layer)
+    fwd = oracle.trop_linear_forward(x, st, code_scale=layer.code_scale, training=True)
+    gen = torch.Generator().manual_seed(5)
+    gh = torch.randn(n, D, generator=gen).numpy()
+    ref = oracle.trop_route_backward(
+        gh, fwd["z"], st["router_weight"], st["code"], fwd["winner"], fwd["runner"], fwd["margins"],
+        code_scale=layer.code_scale, training=True,
+    )
+    dev = torch.device("cuda")
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in
+         dict(g=gh, z=fwd["z"], W=st["router_weight"], c=st["code"], m=fwd["margins"]).items()}
+    win = torch.from_numpy(fwd["winner"]).to(dev, torch.uint8).contiguous()
+    run = torch.from_numpy(fwd["runner"]).to(dev, torch.uint8).contiguous()
+    lib = nat.load()
+    ws_bytes = lib.tropnn_b200_trop_backward_workspace_size(n, H, K, 1)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    gz = torch.empty(n, D, device=dev)
+    gW = torch.empty(H, K, D, device=dev)
+    gb = torch.empty(H, K, device=dev)
+    gc = torch.empty(H, K, D, device=dev)
+    status = lib.tropnn_b200_trop_backward(
+        t["g"].data_ptr(), t["z"].data_ptr(), n, D, t["W"].data_ptr(), t["c"].data_ptr(), nat.F32, H, K,
+        win.data_ptr(), run.data_ptr(), nat.U8, t["m"].data_ptr(), layer.code_scale, 1, gz.data_ptr(),
+        gW.data_ptr(), gb.data_ptr(), gc.data_ptr(), ws.data_ptr(), ws_bytes, torch.cuda.current_stream().cuda_stream,
+    )
+    nat.check(status, "trop_backward")
+    torch.cuda.synchronize()
+    assert rel_err(gz.cpu().numpy(), ref["grad_latent"]) <= FP32_TOL
+    assert rel_err(gW.cpu().numpy(), ref["grad_router_weight"]) <= FP32_TOL
+    assert rel_err(gb.cpu().numpy(), ref["grad_router_bias"]) <= FP32_TOL
+    assert rel_err(gc.cpu().numpy(), ref["grad_code"]) <= FP32_TOL
+
+
+def test_backward_is_deterministic() -> None:
+    layer = tropnn_b200.TropLinear(784, 128, heads=256, cells=16, code_dim=64, seed=0)
+    x, g = _inputs(512, 784, 128, uniform=True)
+    a = _run(layer, x, g, train=True)
+    layer.zero_grad(set_to_none=True)
+    b = _run(layer, x, g, train=True)
+    for key in ("grad.router_weight", "grad.router_bias", "grad.code", "grad.x"):
+        assert np.array_equal(a[key], b[key]), key
+
+
+def test_invalid_arguments_raise() -> None:
+    layer = tropnn_b200.TropLinear(6, 4, heads=3, cells=4, code_dim=5).cuda()
+    with pytest.raises(TypeError):
+        layer(torch.randn(2, 6, device="cuda", dtype=torch.float64))
+    z = torch.randn(1, 2, 5, device="cuda")
+    with pytest.raises(ValueError):
+        tropnn_b200.trop_route_hidden_b200(z, layer.router_weight, layer.router_bias[:2], layer.code, code_scale=1.0)
+    with pytest.raises(ValueError):
+        tropnn_b200.trop_route_hidden_b200(z[..., :4], layer.router_weight, layer.router_bias, layer.code, code_scale=1.0)

@@ -1,0 +1,646 @@
+// PairwiseLinear on sm_100a: comparator routing fused with the LUT gather-sum, and the
+// straight-through-estimator backward.
+//
+// Reference behaviour (paths inside the tropnn package):
+//   forward   layers/pairwise.py:127-135 (_compute_indices), :99-122 (_lookup_chunked),
+//             layers/base.py:76-77 (output_scale); TileLang kernels
+//             backends/pairwise_tilelang.py:17-115.
+//   backward  autograd of layers/pairwise.py:137-200 (_min_margin_ste / _full_ste) with
+//             the surrogates of layers/surrogate.py:9-38; TileLang kernels
+//             backends/pairwise_tilelang.py:159-410.
+//
+// Layout: latent f32 [N, in] row-major; anchors int64 [T, C, 2]; thresholds [T, C];
+// lut [T, 2^C, out] (f32/f16/bf16) row-major so a selected LUT row is one contiguous
+// `out`-wide vector; indices int64 [N, T]; margins f32 [N, T, C].
+#include "common.cuh"
+
+namespace tropnn_b200 {
+
+int bucket_sort_impl(const void *keys, int key_dtype, int64_t rows, int64_t groups, int64_t stride,
+                     int64_t buckets, int32_t *perm, int32_t *seg, cudaStream_t stream);
+int segment_rowsum_impl(const float *values, int64_t rows, int64_t width, int64_t ld, int64_t groups,
+                        int64_t buckets, const int32_t *perm0, const int32_t *seg0, const float *coef0,
+                        float coef_sign0, const int32_t *perm1, const int32_t *seg1, const float *coef1,
+                        float coef_sign1, float scale, void *out, int out_dtype, void *bucket_sum,
+                        cudaStream_t stream);
+
+namespace {
+
+constexpr int kMaxComparisons = 12;
+constexpr int kFwdWarps = 4;
+constexpr int kFwdRows = 8;  // rows per CTA in the forward
+
+__device__ __forceinline__ int64_t clamp_feature(int64_t a, int64_t in) { return a < 0 ? 0 : (a >= in ? in - 1 : a); }
+
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+// CTA = 4 warps, kFwdRows rows, one column tile of 32*VEC*NV outputs.
+// Phase 1: all threads compute the T route indices of the CTA's rows (and, in the
+//          first column tile, write indices + margins).
+// Phase 2: each warp sums the selected LUT rows of its rows over the column tile,
+//          lanes holding VEC consecutive columns (16-byte loads when aligned).
+template <typename LutT, typename ThrT, int VEC, int NV>
+__global__ void __launch_bounds__(kFwdWarps * 32) pairwise_forward_kernel(
+    const float *__restrict__ x, int64_t rows, int64_t in, const int64_t *__restrict__ anchors,
+    const ThrT *__restrict__ thr, int T, int C, const LutT *__restrict__ lut, int64_t out, float out_scale,
+    float *__restrict__ y, int64_t *__restrict__ idx_out, float *__restrict__ u_out) {
+  extern __shared__ int idx_s[];  // [kFwdRows][T]
+  const int64_t row0 = int64_t(blockIdx.x) * kFwdRows;
+  const int rows_here = static_cast<int>(min64(kFwdRows, rows - row0));
+  const bool write_routes = blockIdx.y == 0;
+  const int64_t table_size = int64_t(1) << C;
+
+  for (int task = threadIdx.x; task < rows_here * T; task += kFwdWarps * 32) {
+    const int r = task / T;
+    const int t = task - r * T;
+    const int64_t n = row0 + r;
+    const float *xrow = x + n * in;
+    int bits = 0;
+    for (int c = 0; c < C; ++c) {
+      const int64_t e = (int64_t(t) * C + c) * 2;
+      const int64_t a = clamp_feature(__ldg(anchors + e), in);
+      const int64_t b = clamp_feature(__ldg(anchors + e + 1), in);
+      const float u = __fsub_rn(__fsub_rn(__ldg(xrow + a), __ldg(xrow + b)), ldg_f32(thr + int64_t(t) * C + c));
+      if (write_routes) u_out[(n * T + t) * C + c] = u;
+      bits |= (u > 0.f ? 1 : 0) << c;
+    }
+    idx_s[r * T + t] = bits;
+    if (write_routes) idx_out[n * T + t] = bits;
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t col0 = int64_t(blockIdx.y) * (32 * VEC * NV);
+  for (int r = warp; r < rows_here; r += kFwdWarps) {
+    float acc[NV][VEC];
+#pragma unroll
+    for (int s = 0; s < NV; ++s)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[s][e] = 0.f;
+    const int *my_idx = idx_s + r * T;
+#pragma unroll 4
+    for (int t = 0; t < T; ++t) {
+      const LutT *lrow = lut + (int64_t(t) * table_size + my_idx[t]) * out;
+#pragma unroll
+      for (int s = 0; s < NV; ++s) {
+        const int64_t col = col0 + int64_t(s) * 32 * VEC + int64_t(lane) * VEC;
+        if (col < out) {
+          float v[VEC];
+          VecLoad<LutT, VEC>::load(lrow + col, v);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) acc[s][e] = __fadd_rn(acc[s][e], v[e]);
+        }
+      }
+    }
+    float *yrow = y + (row0 + r) * out;
+#pragma unroll
+    for (int s = 0; s < NV; ++s) {
+      const int64_t col = col0 + int64_t(s) * 32 * VEC + int64_t(lane) * VEC;
+      if (col < out) {
+        if constexpr (VEC % 4 == 0) {
+#pragma unroll
+          for (int e = 0; e < VEC; e += 4) {
+            *reinterpret_cast<float4 *>(yrow + col + e) =
+                make_float4(__fmul_rn(acc[s][e], out_scale), __fmul_rn(acc[s][e + 1], out_scale),
+                            __fmul_rn(acc[s][e + 2], out_scale), __fmul_rn(acc[s][e + 3], out_scale));
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) yrow[col + e] = __fmul_rn(acc[s][e], out_scale);
+        }
+      }
+    }
+  }
+}
+
+template <typename LutT, typename ThrT, int VEC, int NV>
+int launch_forward(const float *x, int64_t rows, int64_t in, const int64_t *anchors, const void *thr, int T, int C,
+                   const void *lut, int64_t out, float out_scale, float *y, int64_t *idx, float *u,
+                   cudaStream_t stream) {
+  const int64_t col_tiles = ceil_div(out, 32 * VEC * NV);
+  const int64_t row_blocks = ceil_div(rows, kFwdRows);
+  TB_REQUIRE(row_blocks < (int64_t(1) << 31) && col_tiles < 65536, TROPNN_B200_ERR_INVALID,
+             "pairwise_forward: grid too large (items=%lld out=%lld)", (long long)rows, (long long)out);
+  const size_t smem = sizeof(int) * kFwdRows * T;
+  auto kernel = pairwise_forward_kernel<LutT, ThrT, VEC, NV>;
+  if (smem > 48 * 1024) {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (err != cudaSuccess)
+      return set_error(TROPNN_B200_ERR_LAUNCH, "pairwise_forward: cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+  }
+  dim3 grid(static_cast<unsigned>(row_blocks), static_cast<unsigned>(col_tiles));
+  kernel<<<grid, kFwdWarps * 32, smem, stream>>>(x, rows, in, anchors, static_cast<const ThrT *>(thr), T, C,
+                                                 static_cast<const LutT *>(lut), out, out_scale, y, idx, u);
+  return check_launch("pairwise_forward");
+}
+
+template <typename LutT, typename ThrT>
+int forward_by_width(const float *x, int64_t rows, int64_t in, const int64_t *anchors, const void *thr, int T, int C,
+                     const void *lut, int64_t out, float out_scale, float *y, int64_t *idx, float *u,
+                     cudaStream_t stream) {
+  constexpr int kVec = 16 / sizeof(LutT);
+  const bool vec_ok = (out % kVec == 0) && (reinterpret_cast<uintptr_t>(lut) % 16 == 0) &&
+                      (reinterpret_cast<uintptr_t>(y) % 16 == 0);
+  if (vec_ok) {
+    // Column tile of 512 outputs (f32) or 1024 (16-bit) when the rows alone fill the GPU,
+    // narrower tiles otherwise.
+    if (out > 32 * kVec * 2 || ceil_div(rows, kFwdRows) >= 4 * 148)
+      return launch_forward<LutT, ThrT, kVec, 4>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u,
+                                                 stream);
+    return launch_forward<LutT, ThrT, kVec, 1>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u,
+                                               stream);
+  }
+  if (out > 64)
+    return launch_forward<LutT, ThrT, 1, 4>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u, stream);
+  return launch_forward<LutT, ThrT, 1, 1>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u, stream);
+}
+
+template <typename LutT>
+int forward_by_thr(int thr_dtype, const float *x, int64_t rows, int64_t in, const int64_t *anchors, const void *thr,
+                   int T, int C, const void *lut, int64_t out, float out_scale, float *y, int64_t *idx, float *u,
+                   cudaStream_t stream) {
+  switch (thr_dtype) {
+    case TROPNN_B200_F32:
+      return forward_by_width<LutT, float>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u, stream);
+    case TROPNN_B200_F16:
+      return forward_by_width<LutT, __half>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u, stream);
+    default:
+      return forward_by_width<LutT, __nv_bfloat16>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u,
+                                                   stream);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// STE backward
+// ---------------------------------------------------------------------------
+// One warp per row. For every table the warp reduces sum_o g[o] (lut[nb,o] - lut[cur,o])
+// across its lanes, applies the surrogate, and keeps gu (and r*) in shared memory.
+// grad_latent is then gathered per input feature through the inverse anchor map, so
+// each element is written once in a fixed order (no atomics, no zero fill).
+constexpr int kSteMaxWarps = 4;
+
+template <typename LutT, int VEC, bool MIN>
+__global__ void __launch_bounds__(kSteMaxWarps * 32) pairwise_ste_kernel(
+    const float *__restrict__ g, int64_t rows, int64_t out, float out_scale, const int64_t *__restrict__ idx,
+    const float *__restrict__ u, int T, int C, int64_t in, const LutT *__restrict__ lut, int surrogate,
+    const int32_t *__restrict__ feat_start, const int32_t *__restrict__ feat_entries, float *__restrict__ grad_x,
+    float *__restrict__ gu_out, uint8_t *__restrict__ rstar_out) {
+  extern __shared__ float ste_smem[];
+  const int warps = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t n = int64_t(blockIdx.x) * warps + warp;
+  if (n >= rows) return;
+  const int per_row = MIN ? T : T * C;
+  float *gu_s = ste_smem + warp * per_row;
+  uint8_t *rs_s = reinterpret_cast<uint8_t *>(ste_smem + warps * per_row) + warp * T;
+  const int64_t table_size = int64_t(1) << C;
+  const float *grow = g + n * out;
+
+  for (int t = 0; t < T; ++t) {
+    const float *urow = u + (n * T + t) * C;
+    const int cur = static_cast<int>(__ldg(idx + n * T + t));
+    const LutT *lcur = lut + (int64_t(t) * table_size + cur) * out;
+    if (MIN) {
+      int rmin = 0;
+      float best = fabsf(__ldg(urow));
+      for (int c = 1; c < C; ++c) {
+        const float a = fabsf(__ldg(urow + c));
+        if (a < best) { best = a; rmin = c; }
+      }
+      const LutT *lnb = lut + (int64_t(t) * table_size + (cur ^ (1 << rmin))) * out;
+      float dot = 0.f;
+      for (int64_t col = int64_t(lane) * VEC; col < out; col += 32 * VEC) {
+        float vc[VEC], vn[VEC], gv[VEC];
+        VecLoad<LutT, VEC>::load(lcur + col, vc);
+        VecLoad<LutT, VEC>::load(lnb + col, vn);
+        VecLoad<float, VEC>::load(grow + col, gv);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) dot = fmaf(__fmul_rn(gv[e], out_scale), __fsub_rn(vn[e], vc[e]), dot);
+      }
+      dot = warp_sum(dot);
+      if (lane == 0) {
+        const float gu = __fmul_rn(dot, surrogate_grad(__ldg(urow + rmin), surrogate));
+        gu_s[t] = gu;
+        rs_s[t] = static_cast<uint8_t>(rmin);
+        gu_out[n * T + t] = gu;
+        rstar_out[n * T + t] = static_cast<uint8_t>(rmin);
+      }
+    } else {
+      float dot[kMaxComparisons];
+#pragma unroll
+      for (int c = 0; c < kMaxComparisons; ++c) dot[c] = 0.f;
+      for (int64_t col = int64_t(lane) * VEC; col < out; col += 32 * VEC) {
+        float vc[VEC], gv[VEC];
+        VecLoad<LutT, VEC>::load(lcur + col, vc);
+        VecLoad<float, VEC>::load(grow + col, gv);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) gv[e] = __fmul_rn(gv[e], out_scale);
+#pragma unroll
+        for (int c = 0; c < kMaxComparisons; ++c) {
+          if (c < C) {
+            const LutT *lnb = lut + (int64_t(t) * table_size + (cur ^ (1 << c))) * out;
+            float vn[VEC];
+            VecLoad<LutT, VEC>::load(lnb + col, vn);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) dot[c] = fmaf(gv[e], __fsub_rn(vn[e], vc[e]), dot[c]);
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < kMaxComparisons; ++c) {
+        if (c < C) {
+          const float d = warp_sum(dot[c]);
+          if (lane == 0) {
+            const float gu = __fmul_rn(d, surrogate_grad(__ldg(urow + c), surrogate));
+            gu_s[t * C + c] = gu;
+            gu_out[(n * T + t) * C + c] = gu;
+          }
+        }
+      }
+    }
+  }
+  __syncwarp();
+
+  float *gxrow = grad_x + n * in;
+  for (int64_t i = lane; i < in; i += 32) {
+    const int lo = __ldg(feat_start + i);
+    const int hi = __ldg(feat_start + i + 1);
+    float acc = 0.f;
+    for (int j = lo; j < hi; ++j) {
+      const int e = __ldg(feat_entries + j);
+      const int tc = e >> 1;
+      const int t = tc / C;
+      const int c = tc - t * C;
+      float v;
+      if (MIN) {
+        v = (rs_s[t] == c) ? gu_s[t] : 0.f;
+      } else {
+        v = gu_s[tc];
+      }
+      acc = (e & 1) ? __fsub_rn(acc, v) : __fadd_rn(acc, v);
+    }
+    gxrow[i] = acc;
+  }
+}
+
+template <typename LutT, int VEC>
+int launch_ste(bool use_min, const float *g, int64_t rows, int64_t out, float out_scale, const int64_t *idx,
+               const float *u, int T, int C, int64_t in, const void *lut, int surrogate, const int32_t *fs,
+               const int32_t *fe, float *gx, float *gu, uint8_t *rs, cudaStream_t stream) {
+  const size_t per_warp = sizeof(float) * (use_min ? T : T * C) + T;
+  int warps = kSteMaxWarps;
+  while (warps > 1 && per_warp * warps > 96 * 1024) --warps;
+  const size_t smem = per_warp * warps + 16;
+  TB_REQUIRE(smem <= 200 * 1024, TROPNN_B200_ERR_INVALID,
+             "pairwise_ste_backward: tables*comparisons=%d too large for the per-row shared buffer", T * C);
+  const int64_t blocks = ceil_div(rows, warps);
+  TB_REQUIRE(blocks < (int64_t(1) << 31), TROPNN_B200_ERR_INVALID, "pairwise_ste_backward: too many rows");
+  auto kernel = use_min ? pairwise_ste_kernel<LutT, VEC, true> : pairwise_ste_kernel<LutT, VEC, false>;
+  if (smem > 48 * 1024) {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (err != cudaSuccess)
+      return set_error(TROPNN_B200_ERR_LAUNCH, "pairwise_ste_backward: cudaFuncSetAttribute: %s",
+                       cudaGetErrorString(err));
+  }
+  kernel<<<static_cast<unsigned>(blocks), warps * 32, smem, stream>>>(
+      g, rows, out, out_scale, idx, u, T, C, in, static_cast<const LutT *>(lut), surrogate, fs, fe, gx, gu, rs);
+  return check_launch("pairwise_ste_backward");
+}
+
+template <typename LutT>
+int ste_by_width(bool use_min, const float *g, int64_t rows, int64_t out, float out_scale, const int64_t *idx,
+                 const float *u, int T, int C, int64_t in, const void *lut, int surrogate, const int32_t *fs,
+                 const int32_t *fe, float *gx, float *gu, uint8_t *rs, cudaStream_t stream) {
+  constexpr int kVec = 16 / sizeof(LutT);
+  // 16-byte LUT loads need kVec | out; g is f32 so with kVec = 8 two float4 loads.
+  const bool vec_ok = (out % kVec == 0) && (reinterpret_cast<uintptr_t>(lut) % 16 == 0) &&
+                      (reinterpret_cast<uintptr_t>(g) % 16 == 0);
+  if (vec_ok)
+    return launch_ste<LutT, kVec>(use_min, g, rows, out, out_scale, idx, u, T, C, in, lut, surrogate, fs, fe, gx, gu,
+                                  rs, stream);
+  return launch_ste<LutT, 1>(use_min, g, rows, out, out_scale, idx, u, T, C, in, lut, surrogate, fs, fe, gx, gu, rs,
+                             stream);
+}
+
+// ---------------------------------------------------------------------------
+// threshold gradient: fixed-order reduction over rows
+// ---------------------------------------------------------------------------
+// CTA = 8 warps over a block of 32 tables; lane <-> table (coalesced reads of gu),
+// warps stride over rows, then a fixed-shape combine across warps.
+template <typename OutT, bool MIN>
+__global__ void __launch_bounds__(256) threshold_grad_kernel(const float *__restrict__ gu,
+                                                             const uint8_t *__restrict__ rstar, int64_t rows, int T,
+                                                             int C, OutT *__restrict__ grad) {
+  __shared__ float part[8][32][kMaxComparisons];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 32 + lane;
+  float acc[kMaxComparisons];
+#pragma unroll
+  for (int c = 0; c < kMaxComparisons; ++c) acc[c] = 0.f;
+  if (t < T) {
+    for (int64_t n = warp; n < rows; n += 8) {
+      if (MIN) {
+        const float v = __ldg(gu + n * T + t);
+        const int r = __ldg(rstar + n * T + t);
+#pragma unroll
+        for (int c = 0; c < kMaxComparisons; ++c)
+          if (c == r) acc[c] = __fadd_rn(acc[c], v);
+      } else {
+#pragma unroll
+        for (int c = 0; c < kMaxComparisons; ++c)
+          if (c < C) acc[c] = __fadd_rn(acc[c], __ldg(gu + (n * T + t) * C + c));
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < kMaxComparisons; ++c) part[warp][lane][c] = acc[c];
+  __syncthreads();
+  for (int k = threadIdx.x; k < 32 * C; k += 256) {
+    const int l = k / C;
+    const int c = k - l * C;
+    const int tt = blockIdx.x * 32 + l;
+    if (tt < T) {
+      float s = 0.f;
+      for (int w = 0; w < 8; ++w) s = __fadd_rn(s, part[w][l][c]);
+      grad[int64_t(tt) * C + c] = from_f32<OutT>(-s);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// inverse anchor map (one CTA; built once per anchors buffer)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) anchor_index_kernel(const int64_t *__restrict__ anchors, int E, int64_t in,
+                                                            int32_t *start, int32_t *__restrict__ entries) {
+  __shared__ int tmp[1024];
+  const int tid = threadIdx.x;
+  for (int64_t i = tid; i <= in; i += 1024) start[i] = 0;
+  __syncthreads();
+  for (int e = tid; e < E; e += 1024) atomicAdd(start + clamp_feature(anchors[e], in) + 1, 1);
+  __syncthreads();
+  // In-place exclusive scan of start[1..in]: afterwards start[f+1] = first slot of feature f.
+  const int64_t per = (in + 1023) / 1024;
+  const int64_t lo = min64(in, tid * per);
+  const int64_t hi = min64(in, lo + per);
+  int local = 0;
+  for (int64_t i = lo; i < hi; ++i) local += start[i + 1];
+  tmp[tid] = local;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    int v = tid >= off ? tmp[tid - off] : 0;
+    __syncthreads();
+    tmp[tid] += v;
+    __syncthreads();
+  }
+  int run = tmp[tid] - local;
+  for (int64_t i = lo; i < hi; ++i) {
+    int v = start[i + 1];
+    start[i + 1] = run;
+    run += v;
+  }
+  __syncthreads();
+  // Stable fill in entry order by one warp; start[f+1] is the cursor of feature f and
+  // ends as the first slot of feature f+1.
+  if (tid < 32) {
+    volatile int32_t *cursor = start;
+    const unsigned lt_mask = (1u << tid) - 1u;
+    for (int base = 0; base < E; base += 32) {
+      const int e = base + tid;
+      const bool valid = e < E;
+      const unsigned active = __ballot_sync(0xffffffffu, valid);
+      int64_t f = 0;
+      unsigned peers = 0;
+      if (valid) {
+        f = clamp_feature(anchors[e], in);
+        peers = __match_any_sync(active, static_cast<unsigned long long>(f));
+        entries[cursor[f + 1] + __popc(peers & lt_mask)] = e;
+      }
+      __syncwarp();
+      if (valid && tid == __ffs(peers) - 1) cursor[f + 1] = cursor[f + 1] + __popc(peers);
+      __syncwarp();
+    }
+  }
+}
+
+int validate_pairwise(int64_t items, int64_t in, int64_t tables, int64_t comparisons, int64_t out) {
+  TB_REQUIRE(items >= 0 && in >= 1 && tables >= 1 && out >= 1, TROPNN_B200_ERR_INVALID,
+             "pairwise: bad sizes items=%lld in=%lld tables=%lld out=%lld", (long long)items, (long long)in,
+             (long long)tables, (long long)out);
+  TB_REQUIRE(comparisons >= 1 && comparisons <= kMaxComparisons, TROPNN_B200_ERR_INVALID,
+             "pairwise: comparisons=%lld outside the supported range [1, %d]", (long long)comparisons,
+             kMaxComparisons);
+  TB_REQUIRE(tables * comparisons * 2 < (int64_t(1) << 31) && tables < (int64_t(1) << 24), TROPNN_B200_ERR_INVALID,
+             "pairwise: tables=%lld too large", (long long)tables);
+  TB_REQUIRE(items < (int64_t(1) << 31), TROPNN_B200_ERR_INVALID, "pairwise: items=%lld exceeds int32",
+             (long long)items);
+  return TROPNN_B200_OK;
+}
+
+}  // namespace
+
+int pairwise_forward_impl(const float *latent, int64_t items, int64_t in, const int64_t *anchors, const void *thr,
+                          int thr_dtype, int64_t tables, int64_t comparisons, const void *lut, int lut_dtype,
+                          int64_t out, float out_scale, float *y, int64_t *idx, float *u, cudaStream_t stream) {
+  TB_CHECK(validate_pairwise(items, in, tables, comparisons, out));
+  TB_REQUIRE(is_float_dtype(thr_dtype) && is_float_dtype(lut_dtype), TROPNN_B200_ERR_DTYPE,
+             "pairwise_forward: thresholds dtype %s / lut dtype %s unsupported", dtype_name(thr_dtype),
+             dtype_name(lut_dtype));
+  if (items == 0) return TROPNN_B200_OK;
+  TB_REQUIRE(latent && anchors && thr && lut && y && idx && u, TROPNN_B200_ERR_INVALID,
+             "pairwise_forward: null pointer");
+  const int T = static_cast<int>(tables), C = static_cast<int>(comparisons);
+  switch (lut_dtype) {
+    case TROPNN_B200_F32:
+      return forward_by_thr<float>(thr_dtype, latent, items, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u,
+                                   stream);
+    case TROPNN_B200_F16:
+      return forward_by_thr<__half>(thr_dtype, latent, items, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u,
+                                    stream);
+    default:
+      return forward_by_thr<__nv_bfloat16>(thr_dtype, latent, items, in, anchors, thr, T, C, lut, out, out_scale, y,
+                                           idx, u, stream);
+  }
+}
+
+int pairwise_anchor_index_impl(const int64_t *anchors, int64_t tables, int64_t comparisons, int64_t in,
+                               int32_t *fs, int32_t *fe, cudaStream_t stream) {
+  TB_CHECK(validate_pairwise(0, in, tables, comparisons, 1));
+  TB_REQUIRE(anchors && fs && fe, TROPNN_B200_ERR_INVALID, "pairwise_anchor_index: null pointer");
+  anchor_index_kernel<<<1, 1024, 0, stream>>>(anchors, static_cast<int>(tables * comparisons * 2), in, fs, fe);
+  return check_launch("pairwise_anchor_index");
+}
+
+int pairwise_ste_impl(const float *g, int64_t items, int64_t out, float out_scale, const int64_t *idx, const float *u,
+                      const int64_t *anchors, int64_t tables, int64_t comparisons, int64_t in, const void *lut,
+                      int lut_dtype, int use_min, int surrogate, const int32_t *fs, const int32_t *fe, float *gx,
+                      float *gu, uint8_t *rs, cudaStream_t stream) {
+  (void)anchors;
+  TB_CHECK(validate_pairwise(items, in, tables, comparisons, out));
+  TB_REQUIRE(is_float_dtype(lut_dtype), TROPNN_B200_ERR_DTYPE, "pairwise_ste_backward: lut dtype %s unsupported",
+             dtype_name(lut_dtype));
+  TB_REQUIRE(surrogate == TROPNN_B200_SURROGATE_FAST_SIGMOID_ODD || surrogate == TROPNN_B200_SURROGATE_IZHIKEVICH,
+             TROPNN_B200_ERR_INVALID, "pairwise_ste_backward: unknown surrogate %d", surrogate);
+  if (items == 0) return TROPNN_B200_OK;
+  TB_REQUIRE(g && idx && u && lut && fs && fe && gx && gu && (rs || !use_min), TROPNN_B200_ERR_INVALID,
+             "pairwise_ste_backward: null pointer");
+  const int T = static_cast<int>(tables), C = static_cast<int>(comparisons);
+  const bool m = use_min != 0;
+  switch (lut_dtype) {
+    case TROPNN_B200_F32:
+      return ste_by_width<float>(m, g, items, out, out_scale, idx, u, T, C, in, lut, surrogate, fs, fe, gx, gu, rs,
+                                 stream);
+    case TROPNN_B200_F16:
+      return ste_by_width<__half>(m, g, items, out, out_scale, idx, u, T, C, in, lut, surrogate, fs, fe, gx, gu, rs,
+                                  stream);
+    default:
+      return ste_by_width<__nv_bfloat16>(m, g, items, out, out_scale, idx, u, T, C, in, lut, surrogate, fs, fe, gx,
+                                         gu, rs, stream);
+  }
+}
+
+int pairwise_threshold_grad_impl(const float *gu, const uint8_t *rs, int64_t items, int64_t tables,
+                                 int64_t comparisons, int use_min, void *grad, int grad_dtype, cudaStream_t stream) {
+  TB_CHECK(validate_pairwise(items, 1, tables, comparisons, 1));
+  TB_REQUIRE(is_float_dtype(grad_dtype), TROPNN_B200_ERR_DTYPE, "pairwise_threshold_grad: dtype %s unsupported",
+             dtype_name(grad_dtype));
+  TB_REQUIRE(grad && (items == 0 || (gu && (rs || !use_min))), TROPNN_B200_ERR_INVALID,
+             "pairwise_threshold_grad: null pointer");
+  const unsigned blocks = static_cast<unsigned>(ceil_div(tables, 32));
+  const int T = static_cast<int>(tables), C = static_cast<int>(comparisons);
+#define TB_THR_LAUNCH(OUT_T)                                                                                   \
+  if (use_min)                                                                                                 \
+    threshold_grad_kernel<OUT_T, true><<<blocks, 256, 0, stream>>>(gu, rs, items, T, C, static_cast<OUT_T *>(grad)); \
+  else                                                                                                         \
+    threshold_grad_kernel<OUT_T, false><<<blocks, 256, 0, stream>>>(gu, rs, items, T, C, static_cast<OUT_T *>(grad));
+  switch (grad_dtype) {
+    case TROPNN_B200_F32: TB_THR_LAUNCH(float) break;
+    case TROPNN_B200_F16: TB_THR_LAUNCH(__half) break;
+    default: TB_THR_LAUNCH(__nv_bfloat16) break;
+  }
+#undef TB_THR_LAUNCH
+  return check_launch("pairwise_threshold_grad");
+}
+
+struct PairwiseBackwardLayout {
+  int32_t *perm, *seg, *fs, *fe;
+  float *gu;
+  uint8_t *rs;
+};
+
+static size_t pairwise_backward_layout(void *ws, size_t bytes, int64_t items, int64_t tables, int64_t comparisons,
+                                       int64_t in, int use_min, PairwiseBackwardLayout *L) {
+  WorkspaceCarver c(ws, bytes);
+  const int64_t buckets = int64_t(1) << comparisons;
+  L->perm = c.take<int32_t>(size_t(items) * tables);
+  L->seg = c.take<int32_t>(size_t(tables) * (buckets + 1));
+  L->fs = c.take<int32_t>(size_t(in) + 1);
+  L->fe = c.take<int32_t>(size_t(tables) * comparisons * 2);
+  L->gu = c.take<float>(size_t(items) * tables * (use_min ? 1 : comparisons));
+  L->rs = c.take<uint8_t>(size_t(items) * tables);
+  return WorkspaceCarver::align(c.used);
+}
+
+int pairwise_backward_impl(const float *g, int64_t items, int64_t out, float out_scale, const int64_t *idx,
+                           const float *u, const int64_t *anchors, int64_t tables, int64_t comparisons, int64_t in,
+                           const void *lut, int lut_dtype, int use_min, int surrogate, float *gx, void *gthr,
+                           int gthr_dtype, void *glut, void *ws, size_t ws_bytes, cudaStream_t stream) {
+  TB_CHECK(validate_pairwise(items, in, tables, comparisons, out));
+  TB_REQUIRE(gthr == nullptr || gx != nullptr, TROPNN_B200_ERR_INVALID,
+             "pairwise_backward: grad_thresholds needs grad_latent (both come from the STE pass)");
+  PairwiseBackwardLayout L{};
+  const size_t need = pairwise_backward_layout(ws, ws_bytes, items, tables, comparisons, in, use_min, &L);
+  TB_REQUIRE(ws != nullptr && need <= ws_bytes, TROPNN_B200_ERR_WORKSPACE,
+             "pairwise_backward: workspace of %zu bytes is smaller than the %zu bytes required", ws_bytes, need);
+  if (glut != nullptr) {
+    TB_CHECK(bucket_sort_impl(idx, TROPNN_B200_I64, items, tables, tables, int64_t(1) << comparisons, L.perm, L.seg,
+                              stream));
+    TB_CHECK(segment_rowsum_impl(g, items, out, out, tables, int64_t(1) << comparisons, L.perm, L.seg, nullptr,
+                                 out_scale, nullptr, nullptr, nullptr, 0.f, 1.f, glut, lut_dtype, nullptr, stream));
+  }
+  if (gx != nullptr) {
+    TB_CHECK(pairwise_anchor_index_impl(anchors, tables, comparisons, in, L.fs, L.fe, stream));
+    TB_CHECK(pairwise_ste_impl(g, items, out, out_scale, idx, u, anchors, tables, comparisons, in, lut, lut_dtype,
+                               use_min, surrogate, L.fs, L.fe, gx, L.gu, L.rs, stream));
+    if (gthr != nullptr)
+      TB_CHECK(pairwise_threshold_grad_impl(L.gu, L.rs, items, tables, comparisons, use_min, gthr, gthr_dtype,
+                                            stream));
+  }
+  return TROPNN_B200_OK;
+}
+
+size_t pairwise_backward_workspace(int64_t items, int64_t tables, int64_t comparisons, int64_t in, int use_min) {
+  if (items < 0 || tables < 1 || comparisons < 1 || comparisons > kMaxComparisons || in < 1) return 0;
+  PairwiseBackwardLayout L{};
+  return pairwise_backward_layout(nullptr, 0, items, tables, comparisons, in, use_min, &L);
+}
+
+}  // namespace tropnn_b200
+
+extern "C" {
+
+int tropnn_b200_pairwise_forward(const float *latent, int64_t items, int64_t in_features, const int64_t *anchors,
+                                 const void *thresholds, int thresholds_dtype, int64_t tables, int64_t comparisons,
+                                 const void *lut, int lut_dtype, int64_t out_features, float output_scale,
+                                 float *out, int64_t *indices, float *margins, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::pairwise_forward_impl(latent, items, in_features, anchors, thresholds, thresholds_dtype,
+                                              tables, comparisons, lut, lut_dtype, out_features, output_scale, out,
+                                              indices, margins, tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+int tropnn_b200_pairwise_anchor_index(const int64_t *anchors, int64_t tables, int64_t comparisons,
+                                      int64_t in_features, int32_t *feat_start, int32_t *feat_entries, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::pairwise_anchor_index_impl(anchors, tables, comparisons, in_features, feat_start,
+                                                   feat_entries, tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+int tropnn_b200_pairwise_ste_backward(const float *grad_out, int64_t items, int64_t out_features, float output_scale,
+                                      const int64_t *indices, const float *margins, const int64_t *anchors,
+                                      int64_t tables, int64_t comparisons, int64_t in_features, const void *lut,
+                                      int lut_dtype, int use_min_margin_ste, int surrogate, const int32_t *feat_start,
+                                      const int32_t *feat_entries, float *grad_latent, float *gu, uint8_t *rstar,
+                                      void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::pairwise_ste_impl(grad_out, items, out_features, output_scale, indices, margins, anchors,
+                                          tables, comparisons, in_features, lut, lut_dtype, use_min_margin_ste,
+                                          surrogate, feat_start, feat_entries, grad_latent, gu, rstar,
+                                          tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+int tropnn_b200_pairwise_threshold_grad(const float *gu, const uint8_t *rstar, int64_t items, int64_t tables,
+                                        int64_t comparisons, int use_min_margin_ste, void *grad_thresholds,
+                                        int grad_dtype, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::pairwise_threshold_grad_impl(gu, rstar, items, tables, comparisons, use_min_margin_ste,
+                                                     grad_thresholds, grad_dtype, tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+size_t tropnn_b200_pairwise_backward_workspace_size(int64_t items, int64_t tables, int64_t comparisons,
+                                                    int64_t in_features, int use_min_margin_ste) {
+  return tropnn_b200::pairwise_backward_workspace(items, tables, comparisons, in_features, use_min_margin_ste);
+}
+
+int tropnn_b200_pairwise_backward(const float *grad_out, int64_t items, int64_t out_features, float output_scale,
+                                  const int64_t *indices, const float *margins, const int64_t *anchors,
+                                  int64_t tables, int64_t comparisons, int64_t in_features, const void *lut,
+                                  int lut_dtype, int use_min_margin_ste, int surrogate, float *grad_latent,
+                                  void *grad_thresholds, int grad_thresholds_dtype, void *grad_lut, void *workspace,
+                                  size_t workspace_bytes, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::pairwise_backward_impl(grad_out, items, out_features, output_scale, indices, margins, anchors,
+                                               tables, comparisons, in_features, lut, lut_dtype, use_min_margin_ste,
+                                               surrogate, grad_latent, grad_thresholds, grad_thresholds_dtype,
+                                               grad_lut, workspace, workspace_bytes, tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+}  // extern "C"

@@ -1,0 +1,500 @@
+// TropLinear on sm_100a, fp32-exact SIMT path: route scores + top-2, selected-code
+// gather-sum, and the per-row part of the min-face backward. (The f16/bf16 score GEMM
+// on the tensor cores lives in score_sm100.cu.)
+//
+// Reference behaviour (paths inside the tropnn package):
+//   scores     backend.py:45-46 (einsum + bias), routing.py:7-10 (topk k=2, margin)
+//   hidden     layers/tropical.py:131-138 (gather + sum * code_scale + latent),
+//              routing.py:13-15 (min-face mix U(m) = 0.5 / (1 + |m|))
+//   backward   layers/tropical_exact.py:204-237 (coefficient form of the autograd of the
+//              torch path), backends/triton_backward.py:27-354
+//
+// Layout: latent f32 [N, D]; router_weight / code [H, K, D] and router_bias [H, K] in
+// param dtype; winner/runner [N, H] in the packed index dtype; margins f32 [N, H].
+#include "common.cuh"
+
+namespace tropnn_b200 {
+
+int bucket_sort_impl(const void *keys, int key_dtype, int64_t rows, int64_t groups, int64_t stride,
+                     int64_t buckets, int32_t *perm, int32_t *seg, cudaStream_t stream);
+int segment_rowsum_impl(const float *values, int64_t rows, int64_t width, int64_t ld, int64_t groups,
+                        int64_t buckets, const int32_t *perm0, const int32_t *seg0, const float *coef0,
+                        float coef_sign0, const int32_t *perm1, const int32_t *seg1, const float *coef1,
+                        float coef_sign1, float scale, void *out, int out_dtype, void *bucket_sum,
+                        cudaStream_t stream);
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// route: scores, top-2, margins
+// ---------------------------------------------------------------------------
+// CTA = 8 warps = 8 heads; lane l owns rows {row0 + l + 32 i, i < RM}. The latent tile
+// [32*RM rows, D] sits in shared memory (row pitch D+4 floats keeps the 16-byte lane
+// reads conflict-free); router weights are warp-uniform broadcast loads. Cells are
+// scored KC at a time with a running top-2, so any cell count works.
+constexpr int kRouteWarps = 8;
+constexpr int kCellChunk = 8;
+
+template <typename PT, typename IT, int RM, bool VEC4>
+__global__ void __launch_bounds__(kRouteWarps * 32) trop_route_kernel(
+    const float *__restrict__ z, int64_t rows, int D, const PT *__restrict__ W, const PT *__restrict__ bias, int H,
+    int K, int64_t *__restrict__ winner_i64, IT *__restrict__ winner, IT *__restrict__ runner,
+    float *__restrict__ margins) {
+  extern __shared__ float z_s[];
+  const int pitch = D + 4;
+  const int64_t row0 = int64_t(blockIdx.x) * 32 * RM;
+  const int rows_here = static_cast<int>(min64(32 * RM, rows - row0));
+  for (int i = threadIdx.x; i < rows_here * D; i += kRouteWarps * 32) {
+    const int r = i / D;
+    const int d = i - r * D;
+    z_s[r * pitch + d] = __ldg(z + (row0 + r) * D + d);
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.y * kRouteWarps + warp;
+  if (h >= H) return;
+
+  float best1[RM], best2[RM];
+  int i1[RM], i2[RM];
+#pragma unroll
+  for (int r = 0; r < RM; ++r) {
+    best1[r] = -INFINITY; best2[r] = -INFINITY; i1[r] = 0; i2[r] = 1;
+  }
+  const PT *Wh = W + int64_t(h) * K * D;
+  for (int k0 = 0; k0 < K; k0 += kCellChunk) {
+    float acc[RM][kCellChunk];
+#pragma unroll
+    for (int r = 0; r < RM; ++r)
+#pragma unroll
+      for (int k = 0; k < kCellChunk; ++k) acc[r][k] = 0.f;
+    if (VEC4) {
+      for (int d = 0; d < D; d += 4) {
+        float zv[RM][4];
+#pragma unroll
+        for (int r = 0; r < RM; ++r) {
+          const float4 q = *reinterpret_cast<const float4 *>(z_s + (lane + 32 * r) * pitch + d);
+          zv[r][0] = q.x; zv[r][1] = q.y; zv[r][2] = q.z; zv[r][3] = q.w;
+        }
+#pragma unroll
+        for (int k = 0; k < kCellChunk; ++k) {
+          if (k0 + k < K) {
+            float wv[4];
+            const PT *wp = Wh + int64_t(k0 + k) * D + d;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) wv[e] = ldg_f32(wp + e);
+#pragma unroll
+            for (int r = 0; r < RM; ++r)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) acc[r][k] = fmaf(zv[r][e], wv[e], acc[r][k]);
+          }
+        }
+      }
+    } else {
+      for (int d = 0; d < D; ++d) {
+        float zv[RM];
+#pragma unroll
+        for (int r = 0; r < RM; ++r) zv[r] = z_s[(lane + 32 * r) * pitch + d];
+#pragma unroll
+        for (int k = 0; k < kCellChunk; ++k) {
+          if (k0 + k < K) {
+            const float wv = ldg_f32(Wh + int64_t(k0 + k) * D + d);
+#pragma unroll
+            for (int r = 0; r < RM; ++r) acc[r][k] = fmaf(zv[r], wv, acc[r][k]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kCellChunk; ++k) {
+      if (k0 + k < K) {
+        const float bk = ldg_f32(bias + int64_t(h) * K + k0 + k);
+#pragma unroll
+        for (int r = 0; r < RM; ++r) {
+          const float s = __fadd_rn(acc[r][k], bk);
+          // Strict '>' keeps the lowest cell index on exact ties.
+          if (s > best1[r]) {
+            best2[r] = best1[r]; i2[r] = i1[r]; best1[r] = s; i1[r] = k0 + k;
+          } else if (s > best2[r]) {
+            best2[r] = s; i2[r] = k0 + k;
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RM; ++r) {
+    const int rr = lane + 32 * r;
+    if (rr < rows_here) {
+      const int64_t o = (row0 + rr) * H + h;
+      if (winner_i64) winner_i64[o] = i1[r];
+      winner[o] = static_cast<IT>(i1[r]);
+      runner[o] = static_cast<IT>(i2[r]);
+      margins[o] = __fsub_rn(best1[r], best2[r]);
+    }
+  }
+}
+
+template <typename PT, typename IT, int RM>
+int launch_route(const float *z, int64_t rows, int D, const void *W, const void *b, int H, int K, int64_t *w64,
+                 void *win, void *run, float *m, cudaStream_t stream) {
+  const bool vec4 = (D % 4 == 0);
+  const size_t smem = sizeof(float) * 32 * RM * (D + 4);
+  TB_REQUIRE(smem <= 200 * 1024, TROPNN_B200_ERR_INVALID, "trop_route: code_dim=%d too large for the SIMT path", D);
+  auto kernel = vec4 ? trop_route_kernel<PT, IT, RM, true> : trop_route_kernel<PT, IT, RM, false>;
+  if (smem > 48 * 1024) {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (err != cudaSuccess)
+      return set_error(TROPNN_B200_ERR_LAUNCH, "trop_route: cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+  }
+  const int64_t row_blocks = ceil_div(rows, 32 * RM);
+  TB_REQUIRE(row_blocks < (int64_t(1) << 31) && ceil_div(H, kRouteWarps) < 65536, TROPNN_B200_ERR_INVALID,
+             "trop_route: grid too large");
+  dim3 grid(static_cast<unsigned>(row_blocks), static_cast<unsigned>(ceil_div(H, kRouteWarps)));
+  kernel<<<grid, kRouteWarps * 32, smem, stream>>>(z, rows, D, static_cast<const PT *>(W), static_cast<const PT *>(b),
+                                                   H, K, w64, static_cast<IT *>(win), static_cast<IT *>(run), m);
+  return check_launch("trop_route");
+}
+
+template <typename PT, typename IT>
+int route_by_rows(const float *z, int64_t rows, int D, const void *W, const void *b, int H, int K, int64_t *w64,
+                  void *win, void *run, float *m, cudaStream_t stream) {
+  // Four rows per lane once there are enough rows to fill the GPU with 128-row tiles.
+  if (ceil_div(rows, 128) * ceil_div(H, kRouteWarps) >= 2 * 148 && 128 * (D + 4) * 4 <= 200 * 1024)
+    return launch_route<PT, IT, 4>(z, rows, D, W, b, H, K, w64, win, run, m, stream);
+  return launch_route<PT, IT, 1>(z, rows, D, W, b, H, K, w64, win, run, m, stream);
+}
+
+// ---------------------------------------------------------------------------
+// hidden: selected-code gather-sum
+// ---------------------------------------------------------------------------
+// One warp per row, lanes over code_dim. Sum over heads in head order, then
+// hidden = latent + sum * code_scale (the operation order of tropical.py:137).
+constexpr int kHiddenWarps = 4;
+
+template <typename PT, typename IT, bool TRAIN>
+__global__ void __launch_bounds__(kHiddenWarps * 32) trop_hidden_kernel(
+    const float *__restrict__ z, int64_t rows, int D, const PT *__restrict__ code, int H, int K,
+    const IT *__restrict__ winner, const IT *__restrict__ runner, const float *__restrict__ margins, float code_scale,
+    float *__restrict__ hidden) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t n = int64_t(blockIdx.x) * kHiddenWarps + warp;
+  if (n >= rows) return;
+  const int64_t d0 = int64_t(blockIdx.y) * 32 * 8;
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  const IT *wrow = winner + n * H;
+  const IT *rrow = runner + n * H;
+  const float *mrow = margins + n * H;
+#pragma unroll 2
+  for (int h = 0; h < H; ++h) {
+    const int w = ld_index(wrow + h);
+    const PT *cw = code + (int64_t(h) * K + w) * D;
+    if (TRAIN) {
+      const int r = ld_index(rrow + h);
+      const PT *cr = code + (int64_t(h) * K + r) * D;
+      const float alpha = __fdiv_rn(0.5f, __fadd_rn(1.f, fabsf(__ldg(mrow + h))));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int64_t d = d0 + lane + 32 * j;
+        if (d < D) {
+          const float a = ldg_f32(cw + d);
+          const float b = ldg_f32(cr + d);
+          acc[j] = __fadd_rn(acc[j], __fadd_rn(a, __fmul_rn(alpha, __fsub_rn(b, a))));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int64_t d = d0 + lane + 32 * j;
+        if (d < D) acc[j] = __fadd_rn(acc[j], ldg_f32(cw + d));
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int64_t d = d0 + lane + 32 * j;
+    if (d < D) hidden[n * D + d] = __fadd_rn(__ldg(z + n * D + d), __fmul_rn(acc[j], code_scale));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// backward rows
+// ---------------------------------------------------------------------------
+// One warp per row, lanes over code_dim. Per head: gm from the warp-reduced
+// <g, c_r - c_w>, then the router term of grad_latent; per-row coefficients of the
+// code / router scatters go to coef_w, coef_r, gm for the segmented sums.
+template <typename PT, typename IT, bool TRAIN>
+__global__ void __launch_bounds__(kHiddenWarps * 32) trop_backward_rows_kernel(
+    const float *__restrict__ g, int64_t rows, int D, const PT *__restrict__ W, const PT *__restrict__ code, int H,
+    int K, const IT *__restrict__ winner, const IT *__restrict__ runner, const float *__restrict__ margins,
+    float code_scale, float *__restrict__ grad_z, float *__restrict__ coef_w, float *__restrict__ coef_r,
+    float *__restrict__ gm_out) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t n = int64_t(blockIdx.x) * kHiddenWarps + warp;
+  if (n >= rows) return;
+  const int nd = (D + 31) / 32;  // <= 8 (code_dim <= 256 on this path)
+  float gv[8], acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int d = lane + 32 * j;
+    gv[j] = (j < nd && d < D) ? __ldg(g + n * D + d) : 0.f;
+    acc[j] = 0.f;
+  }
+  for (int h = 0; h < H; ++h) {
+    const int64_t o = n * H + h;
+    if (!TRAIN) {
+      if (lane == 0) coef_w[o] = code_scale;
+      continue;
+    }
+    const int w = ld_index(winner + o);
+    const int r = ld_index(runner + o);
+    const float m = __ldg(margins + o);
+    const PT *cw = code + (int64_t(h) * K + w) * D;
+    const PT *cr = code + (int64_t(h) * K + r) * D;
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = lane + 32 * j;
+      if (j < nd && d < D)
+        dot = fmaf(__fmul_rn(gv[j], code_scale), __fsub_rn(ldg_f32(cr + d), ldg_f32(cw + d)), dot);
+    }
+    dot = warp_sum(dot);
+    const float am = fabsf(m);
+    const float den = __fadd_rn(1.f, am);
+    const float alpha = __fdiv_rn(0.5f, den);
+    const float sgn = (m > 0.f) ? 1.f : ((m < 0.f) ? -1.f : 0.f);
+    // d/dm [0.5 / (1 + |m|)] = -0.5 sign(m) / (1 + |m|)^2
+    const float dalpha = __fdiv_rn(__fmul_rn(-0.5f, sgn), __fmul_rn(den, den));
+    const float gm = __fmul_rn(dot, dalpha);
+    const PT *ww = W + (int64_t(h) * K + w) * D;
+    const PT *wr = W + (int64_t(h) * K + r) * D;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = lane + 32 * j;
+      if (j < nd && d < D) acc[j] = fmaf(gm, __fsub_rn(ldg_f32(ww + d), ldg_f32(wr + d)), acc[j]);
+    }
+    if (lane == 0) {
+      coef_w[o] = __fmul_rn(code_scale, __fsub_rn(1.f, alpha));
+      coef_r[o] = __fmul_rn(code_scale, alpha);
+      gm_out[o] = gm;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int d = lane + 32 * j;
+    if (j < nd && d < D) grad_z[n * D + d] = __fadd_rn(gv[j], acc[j]);
+  }
+}
+
+int validate_trop(int64_t items, int64_t D, int64_t H, int64_t K) {
+  TB_REQUIRE(items >= 0 && D >= 1 && H >= 1 && K >= 2, TROPNN_B200_ERR_INVALID,
+             "trop: bad sizes items=%lld code_dim=%lld heads=%lld cells=%lld", (long long)items, (long long)D,
+             (long long)H, (long long)K);
+  TB_REQUIRE(items < (int64_t(1) << 31) && H < (int64_t(1) << 24) && D < (int64_t(1) << 20) && K <= 32767,
+             TROPNN_B200_ERR_INVALID, "trop: sizes out of range items=%lld code_dim=%lld heads=%lld cells=%lld",
+             (long long)items, (long long)D, (long long)H, (long long)K);
+  return TROPNN_B200_OK;
+}
+
+int check_index_dtype(int64_t K, int index_dtype) {
+  TB_REQUIRE(is_index_dtype(index_dtype), TROPNN_B200_ERR_DTYPE, "trop: index dtype %s unsupported",
+             dtype_name(index_dtype));
+  TB_REQUIRE(!(index_dtype == TROPNN_B200_U8 && K > 256), TROPNN_B200_ERR_DTYPE,
+             "trop: cells=%lld does not fit the u8 index dtype", (long long)K);
+  return TROPNN_B200_OK;
+}
+
+#define TB_DISPATCH_PT(pt, ...)                              \
+  switch (pt) {                                              \
+    case TROPNN_B200_F32: { using PT = float; __VA_ARGS__ } break;          \
+    case TROPNN_B200_F16: { using PT = __half; __VA_ARGS__ } break;         \
+    default: { using PT = __nv_bfloat16; __VA_ARGS__ } break;               \
+  }
+#define TB_DISPATCH_IT(it, ...)                              \
+  switch (it) {                                              \
+    case TROPNN_B200_U8: { using IT = uint8_t; __VA_ARGS__ } break;         \
+    case TROPNN_B200_I16: { using IT = int16_t; __VA_ARGS__ } break;        \
+    default: { using IT = int64_t; __VA_ARGS__ } break;                     \
+  }
+
+}  // namespace
+
+int trop_route_impl(const float *z, int64_t items, int64_t D, const void *W, const void *b, int pt, int64_t H,
+                    int64_t K, int64_t *w64, void *win, void *run, int it, float *m, cudaStream_t stream) {
+  TB_CHECK(validate_trop(items, D, H, K));
+  TB_REQUIRE(is_float_dtype(pt), TROPNN_B200_ERR_DTYPE, "trop_route: param dtype %s unsupported", dtype_name(pt));
+  TB_CHECK(check_index_dtype(K, it));
+  if (items == 0) return TROPNN_B200_OK;
+  TB_REQUIRE(z && W && b && win && run && m, TROPNN_B200_ERR_INVALID, "trop_route: null pointer");
+  int status = TROPNN_B200_OK;
+  TB_DISPATCH_PT(pt, TB_DISPATCH_IT(it, status = route_by_rows<PT, IT>(z, items, static_cast<int>(D), W, b,
+                                                                       static_cast<int>(H), static_cast<int>(K), w64,
+                                                                       win, run, m, stream);))
+  return status;
+}
+
+int trop_hidden_impl(const float *z, int64_t items, int64_t D, const void *code, int pt, int64_t H, int64_t K,
+                     const void *win, const void *run, int it, const float *m, float code_scale, int training,
+                     float *hidden, cudaStream_t stream) {
+  TB_CHECK(validate_trop(items, D, H, K));
+  TB_REQUIRE(is_float_dtype(pt), TROPNN_B200_ERR_DTYPE, "trop_hidden: param dtype %s unsupported", dtype_name(pt));
+  TB_CHECK(check_index_dtype(K, it));
+  if (items == 0) return TROPNN_B200_OK;
+  TB_REQUIRE(z && code && win && hidden && (!training || (run && m)), TROPNN_B200_ERR_INVALID,
+             "trop_hidden: null pointer");
+  dim3 grid(static_cast<unsigned>(ceil_div(items, kHiddenWarps)), static_cast<unsigned>(ceil_div(D, 256)));
+  TB_REQUIRE(ceil_div(items, kHiddenWarps) < (int64_t(1) << 31), TROPNN_B200_ERR_INVALID, "trop_hidden: too many rows");
+  const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
+  TB_DISPATCH_PT(pt, TB_DISPATCH_IT(it, {
+    if (training)
+      trop_hidden_kernel<PT, IT, true><<<grid, kHiddenWarps * 32, 0, stream>>>(
+          z, items, Di, static_cast<const PT *>(code), Hi, Ki, static_cast<const IT *>(win),
+          static_cast<const IT *>(run), m, code_scale, hidden);
+    else
+      trop_hidden_kernel<PT, IT, false><<<grid, kHiddenWarps * 32, 0, stream>>>(
+          z, items, Di, static_cast<const PT *>(code), Hi, Ki, static_cast<const IT *>(win),
+          static_cast<const IT *>(win), m, code_scale, hidden);
+  }))
+  return check_launch("trop_hidden");
+}
+
+int trop_backward_rows_impl(const float *g, int64_t items, int64_t D, const void *W, const void *code, int pt,
+                            int64_t H, int64_t K, const void *win, const void *run, int it, const float *m,
+                            float code_scale, int training, float *gz, float *cw, float *cr, float *gm,
+                            cudaStream_t stream) {
+  TB_CHECK(validate_trop(items, D, H, K));
+  TB_REQUIRE(D <= 256, TROPNN_B200_ERR_INVALID, "trop_backward_rows: code_dim=%lld > 256 unsupported", (long long)D);
+  TB_REQUIRE(is_float_dtype(pt), TROPNN_B200_ERR_DTYPE, "trop_backward_rows: param dtype %s unsupported",
+             dtype_name(pt));
+  TB_CHECK(check_index_dtype(K, it));
+  if (items == 0) return TROPNN_B200_OK;
+  TB_REQUIRE(g && code && win && gz && cw && (!training || (W && run && m && cr && gm)), TROPNN_B200_ERR_INVALID,
+             "trop_backward_rows: null pointer");
+  const unsigned blocks = static_cast<unsigned>(ceil_div(items, kHiddenWarps));
+  const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
+  TB_DISPATCH_PT(pt, TB_DISPATCH_IT(it, {
+    if (training)
+      trop_backward_rows_kernel<PT, IT, true><<<blocks, kHiddenWarps * 32, 0, stream>>>(
+          g, items, Di, static_cast<const PT *>(W), static_cast<const PT *>(code), Hi, Ki,
+          static_cast<const IT *>(win), static_cast<const IT *>(run), m, code_scale, gz, cw, cr, gm);
+    else
+      trop_backward_rows_kernel<PT, IT, false><<<blocks, kHiddenWarps * 32, 0, stream>>>(
+          g, items, Di, static_cast<const PT *>(W), static_cast<const PT *>(code), Hi, Ki,
+          static_cast<const IT *>(win), static_cast<const IT *>(win), m, code_scale, gz, cw, cr, gm);
+  }))
+  return check_launch("trop_backward_rows");
+}
+
+struct TropBackwardLayout {
+  float *coef_w, *coef_r, *gm;
+  int32_t *perm_w, *seg_w, *perm_r, *seg_r;
+};
+
+static size_t trop_backward_layout(void *ws, size_t bytes, int64_t items, int64_t H, int64_t K, int training,
+                                   TropBackwardLayout *L) {
+  WorkspaceCarver c(ws, bytes);
+  L->coef_w = c.take<float>(size_t(items) * H);
+  L->coef_r = training ? c.take<float>(size_t(items) * H) : nullptr;
+  L->gm = training ? c.take<float>(size_t(items) * H) : nullptr;
+  L->perm_w = c.take<int32_t>(size_t(items) * H);
+  L->seg_w = c.take<int32_t>(size_t(H) * (K + 1));
+  L->perm_r = training ? c.take<int32_t>(size_t(items) * H) : nullptr;
+  L->seg_r = training ? c.take<int32_t>(size_t(H) * (K + 1)) : nullptr;
+  return WorkspaceCarver::align(c.used);
+}
+
+size_t trop_backward_workspace(int64_t items, int64_t H, int64_t K, int training) {
+  if (items < 0 || H < 1 || K < 2) return 0;
+  TropBackwardLayout L{};
+  return trop_backward_layout(nullptr, 0, items, H, K, training, &L);
+}
+
+int trop_backward_impl(const float *g, const float *z, int64_t items, int64_t D, const void *W, const void *code,
+                       int pt, int64_t H, int64_t K, const void *win, const void *run, int it, const float *m,
+                       float code_scale, int training, float *gz, void *gW, void *gb, void *gc, void *ws,
+                       size_t ws_bytes, cudaStream_t stream) {
+  TB_CHECK(validate_trop(items, D, H, K));
+  TropBackwardLayout L{};
+  const size_t need = trop_backward_layout(ws, ws_bytes, items, H, K, training, &L);
+  TB_REQUIRE(ws != nullptr && need <= ws_bytes, TROPNN_B200_ERR_WORKSPACE,
+             "trop_backward: workspace of %zu bytes is smaller than the %zu bytes required", ws_bytes, need);
+  TB_REQUIRE(gz != nullptr, TROPNN_B200_ERR_INVALID, "trop_backward: grad_latent is required");
+  TB_CHECK(trop_backward_rows_impl(g, items, D, W, code, pt, H, K, win, run, it, m, code_scale, training, gz,
+                                   L.coef_w, L.coef_r, L.gm, stream));
+  if (items == 0) return TROPNN_B200_OK;
+  TB_CHECK(bucket_sort_impl(win, it, items, H, H, K, L.perm_w, L.seg_w, stream));
+  if (training) TB_CHECK(bucket_sort_impl(run, it, items, H, H, K, L.perm_r, L.seg_r, stream));
+  if (gc != nullptr) {
+    TB_CHECK(segment_rowsum_impl(g, items, D, D, H, K, L.perm_w, L.seg_w, L.coef_w, 1.f, L.perm_r, L.seg_r,
+                                 L.coef_r, 1.f, 1.f, gc, pt, nullptr, stream));
+  }
+  if (training && (gW != nullptr || gb != nullptr)) {
+    TB_REQUIRE(gW != nullptr && gb != nullptr && z != nullptr, TROPNN_B200_ERR_INVALID,
+               "trop_backward: grad_router_weight, grad_router_bias and latent go together");
+    TB_CHECK(segment_rowsum_impl(z, items, D, D, H, K, L.perm_w, L.seg_w, L.gm, 1.f, L.perm_r, L.seg_r, L.gm, -1.f,
+                                 1.f, gW, pt, gb, stream));
+  }
+  return TROPNN_B200_OK;
+}
+
+}  // namespace tropnn_b200
+
+extern "C" {
+
+int tropnn_b200_trop_route(const float *latent, int64_t items, int64_t code_dim, const void *router_weight,
+                           const void *router_bias, int param_dtype, int64_t heads, int64_t cells,
+                           int64_t *winner_i64, void *winner, void *runner, int index_dtype, float *margins,
+                           void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::trop_route_impl(latent, items, code_dim, router_weight, router_bias, param_dtype, heads, cells,
+                                        winner_i64, winner, runner, index_dtype, margins,
+                                        tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+int tropnn_b200_trop_hidden(const float *latent, int64_t items, int64_t code_dim, const void *code, int param_dtype,
+                            int64_t heads, int64_t cells, const void *winner, const void *runner, int index_dtype,
+                            const float *margins, float code_scale, int training, float *hidden, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::trop_hidden_impl(latent, items, code_dim, code, param_dtype, heads, cells, winner, runner,
+                                         index_dtype, margins, code_scale, training, hidden,
+                                         tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+int tropnn_b200_trop_backward_rows(const float *grad_hidden, int64_t items, int64_t code_dim,
+                                   const void *router_weight, const void *code, int param_dtype, int64_t heads,
+                                   int64_t cells, const void *winner, const void *runner, int index_dtype,
+                                   const float *margins, float code_scale, int training, float *grad_latent,
+                                   float *coef_w, float *coef_r, float *gm, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::trop_backward_rows_impl(grad_hidden, items, code_dim, router_weight, code, param_dtype, heads,
+                                                cells, winner, runner, index_dtype, margins, code_scale, training,
+                                                grad_latent, coef_w, coef_r, gm, tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+size_t tropnn_b200_trop_backward_workspace_size(int64_t items, int64_t heads, int64_t cells, int training) {
+  return tropnn_b200::trop_backward_workspace(items, heads, cells, training);
+}
+
+int tropnn_b200_trop_backward(const float *grad_hidden, const float *latent, int64_t items, int64_t code_dim,
+                              const void *router_weight, const void *code, int param_dtype, int64_t heads,
+                              int64_t cells, const void *winner, const void *runner, int index_dtype,
+                              const float *margins, float code_scale, int training, float *grad_latent,
+                              void *grad_router_weight, void *grad_router_bias, void *grad_code, void *workspace,
+                              size_t workspace_bytes, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::trop_backward_impl(grad_hidden, latent, items, code_dim, router_weight, code, param_dtype,
+                                           heads, cells, winner, runner, index_dtype, margins, code_scale, training,
+                                           grad_latent, grad_router_weight, grad_router_bias, grad_code, workspace,
+                                           workspace_bytes, tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+}  // extern "C"

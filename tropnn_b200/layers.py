@@ -1,0 +1,327 @@
+"""Drop-in ``TropLinear`` / ``PairwiseLinear`` for backend="b200".
+
+Constructor arguments, parameter and buffer names, shapes, dtypes, ``state_dict`` keys
+and the seeded initialisation order are those of the reference classes
+(layers/tropical.py:21-79, layers/pairwise.py:18-68, layers/base.py:13-35), so a
+``state_dict`` saved from the reference loads here unchanged and the same ``seed``
+gives bit-identical parameters. The forward follows layers/base.py:64-84: 2-D input
+becomes ``[B, 1, in]`` (the output stays 3-D), compute dtype is f32 for f16/bf16
+input, and the route debug cache ``_last_indices``/``_last_margins`` is kept. The
+routed part runs on the sm_100a kernels; any backend other than "b200" and any CPU
+input raise, there is no fallback.
+
+The forward bodies are module-agnostic functions (``trop_forward_b200``,
+``pairwise_route_output_b200``) so that ``tropnn_b200.register`` can attach them to the
+reference's own classes.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Literal
+
+import torch
+import torch.nn as nn
+from torch import Tensor
+
+from .ops import pairwise_anchor_index, pairwise_b200, trop_route_hidden_b200
+
+__all__ = [
+    "PairwiseLinear",
+    "RoutedLinearBase",
+    "TropLinear",
+    "pairwise_route_output_b200",
+    "trop_forward_b200",
+]
+
+Backend = Literal["b200"]
+_SURROGATES = ("fast_sigmoid_odd", "izhikevich")
+MAX_COMPARISONS = 12
+
+
+def _check_backend(backend: str) -> None:
+    if backend != "b200":
+        raise ValueError(
+            f"tropnn_b200 layers only run backend='b200' (got {backend!r}); use the reference package for "
+            "the torch/tilelang/triton/zig backends"
+        )
+
+
+def _compute_dtype(x: Tensor) -> torch.dtype:
+    """layers/base.py:34-35."""
+    return torch.float32 if x.dtype in {torch.float16, torch.bfloat16} else x.dtype
+
+
+def _store_debug(layer: nn.Module, indices: Tensor, margins: Tensor) -> None:
+    """layers/base.py:78-83: cache the last routes unless cache_route_debug is False."""
+    if getattr(layer, "cache_route_debug", True):
+        layer._last_indices = indices.detach()
+        layer._last_margins = margins.detach()
+    else:
+        layer._last_indices = None
+        layer._last_margins = None
+
+
+def _require_cuda_input(x: Tensor, layer_name: str) -> None:
+    if not x.is_cuda:
+        raise ValueError(f"{layer_name} backend='b200' requires CUDA input tensors; there is no CPU fallback")
+
+
+def _require_f32_compute(compute_dtype: torch.dtype, layer_name: str) -> None:
+    if compute_dtype != torch.float32:
+        raise TypeError(f"{layer_name} backend='b200' requires float32 compute dtype, got {compute_dtype}")
+
+
+# ---------------------------------------------------------------------------
+# module-agnostic forward bodies
+# ---------------------------------------------------------------------------
+
+
+def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
+    """Full TropLinear forward on sm_100a for any module with the TropLinear attributes.
+
+    Projection (tropical.py:96-99) and output map (tropical.py:140-146) are dense cuBLAS
+    GEMMs through torch; the route scores, top-2, code gather-sum and their backward are
+    the b200 kernels (ops.trop_route_hidden_b200).
+    """
+    if x.ndim == 2:
+        x = x.unsqueeze(1)
+    _require_cuda_input(x, "TropLinear")
+    input_dtype = x.dtype
+    compute_dtype = _compute_dtype(x)
+    _require_f32_compute(compute_dtype, "TropLinear")
+    latent = layer.proj(x.to(dtype=layer.proj.weight.dtype)).to(compute_dtype)
+    hidden, winner, margins = trop_route_hidden_b200(
+        latent,
+        layer.router_weight,
+        layer.router_bias,
+        layer.code,
+        code_scale=layer.code_scale,
+        training=layer.training,
+    )
+    weight = layer.output_proj.weight.to(dtype=compute_dtype)
+    output = torch.matmul(hidden, weight.t())
+    bias = layer.output_proj.bias
+    if bias is not None:
+        output = output + bias.to(dtype=compute_dtype)
+    _store_debug(layer, winner, margins)
+    return output.to(dtype=input_dtype)
+
+
+def _anchor_index(layer: nn.Module, anchors: Tensor) -> tuple[Tensor, Tensor]:
+    """Inverse anchor map cached per (device, anchors version), like the reference's
+    version-keyed parameter caches (layers/pairwise.py:82-92)."""
+    key = (anchors.device, anchors.data_ptr(), anchors._version, tuple(anchors.shape))
+    cached = getattr(layer, "_b200_anchor_index", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    lo = int(anchors.min())
+    hi = int(anchors.max())
+    if lo < 0 or hi >= layer.in_features:
+        raise IndexError(f"PairwiseLinear anchors must lie in [0, {layer.in_features}), found [{lo}, {hi}]")
+    index = pairwise_anchor_index(anchors, layer.in_features)
+    layer._b200_anchor_index = (key, index)
+    return index
+
+
+def pairwise_route_output_b200(layer: nn.Module, latent: Tensor, training: bool) -> tuple[Tensor, Tensor, Tensor]:
+    """PairwiseLinear ``_route_output`` on sm_100a, with ``output_scale`` already applied.
+
+    The straight-through correction is live only when training and latent or thresholds
+    need a gradient (layers/pairwise.py:245).
+    """
+    _require_cuda_input(latent, "PairwiseLinear")
+    _require_f32_compute(latent.dtype, "PairwiseLinear")
+    anchors = layer.anchors
+    if anchors.device != latent.device:
+        anchors = anchors.to(device=latent.device)
+    ste = bool(training and (latent.requires_grad or layer.thresholds.requires_grad))
+    return pairwise_b200(
+        latent,
+        anchors,
+        layer.thresholds,
+        layer.lut,
+        use_min_margin_ste=layer.use_min_margin_ste,
+        surrogate=layer.surrogate,
+        output_scale=layer.output_scale,
+        ste=ste,
+        anchor_index=_anchor_index(layer, anchors),
+    )
+
+
+def pairwise_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
+    """layers/base.py:64-84 for PairwiseLinear, with output_scale fused into the kernels."""
+    if x.ndim == 2:
+        x = x.unsqueeze(1)
+    _require_cuda_input(x, "PairwiseLinear")
+    input_dtype = x.dtype
+    compute_dtype = _compute_dtype(x)
+    _require_f32_compute(compute_dtype, "PairwiseLinear")
+    latent = x.to(compute_dtype)
+    output, indices, margins = pairwise_route_output_b200(layer, latent, layer.training)
+    _store_debug(layer, indices, margins)
+    return output.to(dtype=input_dtype)
+
+
+# ---------------------------------------------------------------------------
+# modules
+# ---------------------------------------------------------------------------
+
+
+class RoutedLinearBase(nn.Module):
+    """Shell of the routed layers (layers/base.py:13-35): sizes, backend, output scale
+    and the route debug cache."""
+
+    def __init__(self, in_features: int, out_features: int, *, backend: Backend = "b200", output_scale: float = 1.0) -> None:
+        super().__init__()
+        if in_features < 1:
+            raise ValueError(f"in_features must be >= 1, got {in_features}")
+        if out_features < 1:
+            raise ValueError(f"out_features must be >= 1, got {out_features}")
+        _check_backend(backend)
+        self.in_features = in_features
+        self.out_features = out_features
+        self.backend = backend
+        self.output_scale = output_scale
+        self._last_indices: Tensor | None = None
+        self._last_margins: Tensor | None = None
+
+    def _compute_dtype(self, x: Tensor) -> torch.dtype:
+        return _compute_dtype(x)
+
+
+class TropLinear(RoutedLinearBase):
+    """Tropical code layer with hard head routing and a shared output map, on sm_100a."""
+
+    def __init__(
+        self,
+        in_features: int,
+        out_features: int,
+        *,
+        heads: int = 32,
+        cells: int = 4,
+        code_dim: int = 32,
+        backend: Backend = "b200",
+        seed: int = 0,
+        code_init_std: float = 0.02,
+        use_output_scaling: bool = True,
+        cpu_param_dtype: Literal["f32", "f16"] = "f32",
+        exact_fused: Literal["off", "eval", "train"] = "off",
+        score_route_max_bytes: int | None = None,
+        cache_route_debug: bool = True,
+    ) -> None:
+        if heads < 1:
+            raise ValueError(f"heads must be >= 1, got {heads}")
+        if cells < 2:
+            raise ValueError(f"cells must be >= 2, got {cells}")
+        if code_dim < 1:
+            raise ValueError(f"code_dim must be >= 1, got {code_dim}")
+        if cpu_param_dtype not in {"f32", "f16"}:
+            raise ValueError(f"cpu_param_dtype must be 'f32' or 'f16', got {cpu_param_dtype!r}")
+        if exact_fused not in {"off", "eval", "train"}:
+            raise ValueError(f"exact_fused must be 'off', 'eval', or 'train', got {exact_fused!r}")
+        if score_route_max_bytes is not None and score_route_max_bytes < 0:
+            raise ValueError(f"score_route_max_bytes must be >= 0 when set, got {score_route_max_bytes}")
+        super().__init__(in_features, out_features, backend=backend, output_scale=1.0)
+        self.heads = heads
+        self.cells = cells
+        self.code_dim = code_dim
+        self.code_scale = 1.0 / math.sqrt(heads) if use_output_scaling else 1.0
+        self.cpu_param_dtype = cpu_param_dtype
+        # The fused b200 route serves every exact_fused mode: the scores are never
+        # materialised, so the option only keeps its reference meaning for state.
+        self.exact_fused = exact_fused
+        self.score_route_max_bytes = score_route_max_bytes
+        self.cache_route_debug = cache_route_debug
+
+        # Seeded initialisation in the reference's RNG order (layers/tropical.py:66-79).
+        torch.manual_seed(seed)
+        self.proj = nn.Linear(in_features, code_dim, bias=False)
+        nn.init.normal_(self.proj.weight, mean=0.0, std=1.0 / math.sqrt(max(1, in_features)))
+        router_std = 1.0 / math.sqrt(max(1, code_dim))
+        self.router_weight = nn.Parameter(torch.randn(heads, cells, code_dim) * router_std)
+        self.router_bias = nn.Parameter(torch.zeros(heads, cells))
+        self.code = nn.Parameter(torch.randn(heads, cells, code_dim) * code_init_std)
+        self.output_proj = nn.Linear(code_dim, out_features)
+        nn.init.kaiming_uniform_(self.output_proj.weight, a=math.sqrt(5))
+        if self.output_proj.bias is not None:
+            fan_in = self.output_proj.weight.shape[1]
+            bound = 1 / math.sqrt(fan_in) if fan_in > 0 else 0
+            nn.init.uniform_(self.output_proj.bias, -bound, bound)
+
+    def extra_repr(self) -> str:
+        return (
+            f"in_features={self.in_features}, out_features={self.out_features}, heads={self.heads}, "
+            f"cells={self.cells}, code_dim={self.code_dim}, backend={self.backend!r}, cpu_param_dtype={self.cpu_param_dtype!r}, "
+            f"exact_fused={self.exact_fused!r}, score_route_max_bytes={self.score_route_max_bytes!r}, "
+            f"cache_route_debug={self.cache_route_debug!r}"
+        )
+
+    def forward(self, x: Tensor) -> Tensor:
+        return trop_forward_b200(self, x)
+
+
+class PairwiseLinear(RoutedLinearBase):
+    """Pairwise-comparator LUT layer with min-margin (or full) STE, on sm_100a."""
+
+    def __init__(
+        self,
+        in_features: int,
+        out_features: int,
+        *,
+        tables: int = 16,
+        comparisons: int = 4,
+        backend: Backend = "b200",
+        seed: int = 0,
+        lut_init_std: float = 0.02,
+        use_min_margin_ste: bool = True,
+        use_output_scaling: bool = True,
+        surrogate: str = "fast_sigmoid_odd",
+        cpu_lut_dtype: Literal["f32", "f16"] = "f32",
+    ) -> None:
+        if tables < 1:
+            raise ValueError(f"tables must be >= 1, got {tables}")
+        if comparisons < 1:
+            raise ValueError(f"comparisons must be >= 1, got {comparisons}")
+        if comparisons > MAX_COMPARISONS:
+            raise ValueError(f"backend='b200' supports comparisons <= {MAX_COMPARISONS}, got {comparisons}")
+        _check_backend(backend)
+        if cpu_lut_dtype not in {"f32", "f16"}:
+            raise ValueError(f"cpu_lut_dtype must be 'f32' or 'f16', got {cpu_lut_dtype!r}")
+        if surrogate not in _SURROGATES:
+            raise ValueError(f"unsupported surrogate {surrogate!r}")
+        output_scale = 1.0 / math.sqrt(tables) if use_output_scaling else 1.0
+        super().__init__(in_features, out_features, backend=backend, output_scale=output_scale)
+        self.tables = tables
+        self.comparisons = comparisons
+        self.table_size = 1 << comparisons
+        self.use_min_margin_ste = use_min_margin_ste
+        self.surrogate = surrogate
+        self.cpu_lut_dtype = cpu_lut_dtype
+
+        # Seeded initialisation in the reference's RNG order (layers/pairwise.py:55-68):
+        # one scalar randint per anchor side, redrawing b while it equals a.
+        torch.manual_seed(seed)
+        anchors = torch.zeros(tables, comparisons, 2, dtype=torch.long)
+        for table_idx in range(tables):
+            for comp_idx in range(comparisons):
+                first = torch.randint(0, in_features, (1,)).item()
+                second = torch.randint(0, in_features, (1,)).item()
+                while second == first:
+                    second = torch.randint(0, in_features, (1,)).item()
+                anchors[table_idx, comp_idx, 0] = first
+                anchors[table_idx, comp_idx, 1] = second
+        self.register_buffer("anchors", anchors)
+        self.thresholds = nn.Parameter(torch.zeros(tables, comparisons))
+        self.lut = nn.Parameter(torch.randn(tables, self.table_size, out_features) * lut_init_std)
+        self.register_buffer("powers", 2 ** torch.arange(comparisons, dtype=torch.long))
+
+    def extra_repr(self) -> str:
+        return (
+            f"in_features={self.in_features}, out_features={self.out_features}, tables={self.tables}, "
+            f"comparisons={self.comparisons}, backend={self.backend!r}, use_min_margin_ste={self.use_min_margin_ste}, "
+            f"surrogate={self.surrogate!r}, cpu_lut_dtype={self.cpu_lut_dtype!r}"
+        )
+
+    def forward(self, x: Tensor) -> Tensor:
+        return pairwise_forward_b200(self, x)

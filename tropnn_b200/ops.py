@@ -1,0 +1,573 @@
+"""Autograd operators of backend="b200" over the sm_100a C ABI.
+
+``trop_route_hidden_b200`` mirrors ``trop_route_hidden_tilelang``
+(backends/tilelang_route.py:680-727) and ``pairwise_b200`` mirrors ``pairwise_tilelang``
+(backends/pairwise_tilelang.py:537-549): same positional arguments, same outputs
+(``hidden, winner, margins`` / ``out, indices, margins``), route outputs marked
+non-differentiable, gradients only for the float inputs. Every kernel runs on
+``torch.cuda.current_stream()``; buffers come from PyTorch's caching allocator and are
+handed to the kernels as raw pointers. There is no CPU path: CPU tensors raise.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Any
+
+import torch
+from torch import Tensor
+
+from . import _native as nat
+from . import trace
+
+__all__ = [
+    "packed_route_index_dtype",
+    "pairwise_anchor_index",
+    "pairwise_b200",
+    "trop_route_hidden_b200",
+]
+
+
+def packed_route_index_dtype(cells: int) -> torch.dtype:
+    """Route-index packing of the reference (layers/routing.py:18-23)."""
+    if cells <= 256:
+        return torch.uint8
+    if cells <= 32767:
+        return torch.int16
+    return torch.int64
+
+
+def _launch(name: str, fn: Any, *args: Any) -> None:
+    tr = trace.current()
+    if tr is None:
+        nat.check(fn(*args), name)
+        return
+    rec = tr.begin(name)
+    status = fn(*args)
+    tr.end(rec)
+    nat.check(status, name)
+
+
+def _require_cuda(t: Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"backend='b200' requires CUDA tensors ({what} is on {t.device}); there is no CPU fallback")
+
+
+def _require_f32(t: Tensor, what: str) -> None:
+    if t.dtype != torch.float32:
+        raise TypeError(f"backend='b200' computes in float32; {what} has dtype {t.dtype}")
+
+
+# ---------------------------------------------------------------------------
+# PairwiseLinear
+# ---------------------------------------------------------------------------
+
+
+def pairwise_anchor_index(anchors: Tensor, in_features: int) -> tuple[Tensor, Tensor]:
+    """Inverse anchor map (feature -> anchor entries) used by the STE backward."""
+    _require_cuda(anchors, "anchors")
+    tables, comparisons, _ = anchors.shape
+    lib = nat.load()
+    anchors_c = anchors.to(dtype=torch.int64).contiguous()
+    start = torch.empty(in_features + 1, device=anchors.device, dtype=torch.int32)
+    entries = torch.empty(tables * comparisons * 2, device=anchors.device, dtype=torch.int32)
+    with torch.cuda.device(anchors.device):
+        _launch(
+            "pairwise_anchor_index",
+            lib.tropnn_b200_pairwise_anchor_index,
+            anchors_c.data_ptr(),
+            tables,
+            comparisons,
+            in_features,
+            start.data_ptr(),
+            entries.data_ptr(),
+            nat.stream_handle(anchors.device),
+        )
+    return start, entries
+
+
+class _PairwiseB200Function(torch.autograd.Function):
+    @staticmethod
+    def forward(  # type: ignore[override]
+        ctx: Any,
+        latent: Tensor,
+        thresholds: Tensor,
+        lut: Tensor,
+        anchors: Tensor,
+        anchor_start: Tensor,
+        anchor_entries: Tensor,
+        use_min_margin_ste: bool,
+        surrogate: int,
+        output_scale: float,
+        ste: bool,
+    ) -> tuple[Tensor, Tensor, Tensor]:
+        batch, steps, in_features = latent.shape
+        tables, comparisons, _ = anchors.shape
+        out_features = lut.shape[2]
+        items = batch * steps
+        dev = latent.device
+        latent_flat = latent.reshape(items, in_features).contiguous()
+        thr = thresholds.contiguous()
+        lut_c = lut.contiguous()
+        out = torch.empty((items, out_features), device=dev, dtype=torch.float32)
+        indices = torch.empty((items, tables), device=dev, dtype=torch.int64)
+        margins = torch.empty((items, tables, comparisons), device=dev, dtype=torch.float32)
+        lib = nat.load()
+        _launch(
+            "pairwise_forward",
+            lib.tropnn_b200_pairwise_forward,
+            latent_flat.data_ptr(),
+            items,
+            in_features,
+            anchors.data_ptr(),
+            thr.data_ptr(),
+            nat.float_code(thr.dtype),
+            tables,
+            comparisons,
+            lut_c.data_ptr(),
+            nat.float_code(lut_c.dtype),
+            out_features,
+            float(output_scale),
+            out.data_ptr(),
+            indices.data_ptr(),
+            margins.data_ptr(),
+            nat.stream_handle(dev),
+        )
+        ctx.save_for_backward(indices, margins, anchors, lut_c, anchor_start, anchor_entries)
+        ctx.shape = (batch, steps, in_features, tables, comparisons, out_features)
+        ctx.use_min = bool(use_min_margin_ste)
+        ctx.surrogate = int(surrogate)
+        ctx.output_scale = float(output_scale)
+        ctx.ste = bool(ste)
+        ctx.thr_dtype = thr.dtype
+        idx_out = indices.view(batch, steps, tables)
+        margins_out = margins.view(batch, steps, tables, comparisons)
+        ctx.mark_non_differentiable(idx_out, margins_out)
+        return out.view(batch, steps, out_features), idx_out, margins_out
+
+    @staticmethod
+    def backward(ctx: Any, grad_out: Tensor, grad_idx: Tensor | None, grad_margins: Tensor | None) -> tuple[Any, ...]:
+        del grad_idx, grad_margins
+        indices, margins, anchors, lut, anchor_start, anchor_entries = ctx.saved_tensors
+        batch, steps, in_features, tables, comparisons, out_features = ctx.shape
+        items = batch * steps
+        dev = grad_out.device
+        g = grad_out.reshape(items, out_features).to(torch.float32).contiguous()
+        stream = nat.stream_handle(dev)
+        lib = nat.load()
+        buckets = 1 << comparisons
+
+        grad_lut = None
+        if ctx.needs_input_grad[2]:
+            perm = torch.empty((tables, items), device=dev, dtype=torch.int32)
+            seg = torch.empty((tables, buckets + 1), device=dev, dtype=torch.int32)
+            _launch(
+                "bucket_sort",
+                lib.tropnn_b200_bucket_sort,
+                indices.data_ptr(),
+                nat.I64,
+                items,
+                tables,
+                tables,
+                buckets,
+                perm.data_ptr(),
+                seg.data_ptr(),
+                stream,
+            )
+            grad_lut = torch.empty_like(lut)
+            _launch(
+                "pairwise_lut_grad",
+                lib.tropnn_b200_segment_rowsum,
+                g.data_ptr(),
+                items,
+                out_features,
+                out_features,
+                tables,
+                buckets,
+                perm.data_ptr(),
+                seg.data_ptr(),
+                None,
+                ctx.output_scale,
+                None,
+                None,
+                None,
+                0.0,
+                1.0,
+                grad_lut.data_ptr(),
+                nat.float_code(grad_lut.dtype),
+                None,
+                stream,
+            )
+
+        grad_latent = grad_thr = None
+        want_latent = ctx.needs_input_grad[0]
+        want_thr = ctx.needs_input_grad[1]
+        if ctx.ste and (want_latent or want_thr):
+            gx = torch.empty((items, in_features), device=dev, dtype=torch.float32)
+            gu = torch.empty((items, tables) if ctx.use_min else (items, tables, comparisons), device=dev, dtype=torch.float32)
+            rstar = torch.empty((items, tables), device=dev, dtype=torch.uint8)
+            _launch(
+                "pairwise_ste_backward",
+                lib.tropnn_b200_pairwise_ste_backward,
+                g.data_ptr(),
+                items,
+                out_features,
+                ctx.output_scale,
+                indices.data_ptr(),
+                margins.data_ptr(),
+                anchors.data_ptr(),
+                tables,
+                comparisons,
+                in_features,
+                lut.data_ptr(),
+                nat.float_code(lut.dtype),
+                int(ctx.use_min),
+                ctx.surrogate,
+                anchor_start.data_ptr(),
+                anchor_entries.data_ptr(),
+                gx.data_ptr(),
+                gu.data_ptr(),
+                rstar.data_ptr(),
+                stream,
+            )
+            if want_thr:
+                grad_thr = torch.empty((tables, comparisons), device=dev, dtype=ctx.thr_dtype)
+                _launch(
+                    "pairwise_threshold_grad",
+                    lib.tropnn_b200_pairwise_threshold_grad,
+                    gu.data_ptr(),
+                    rstar.data_ptr(),
+                    items,
+                    tables,
+                    comparisons,
+                    int(ctx.use_min),
+                    grad_thr.data_ptr(),
+                    nat.float_code(ctx.thr_dtype),
+                    stream,
+                )
+            if want_latent:
+                grad_latent = gx.view(batch, steps, in_features)
+        return grad_latent, grad_thr, grad_lut, None, None, None, None, None, None, None
+
+
+def _check_pairwise_args(latent: Tensor, anchors: Tensor, thresholds: Tensor, lut: Tensor) -> None:
+    for name, t in (("latent", latent), ("anchors", anchors), ("thresholds", thresholds), ("lut", lut)):
+        _require_cuda(t, name)
+        if t.device != latent.device:
+            raise ValueError(f"{name} is on {t.device} but latent is on {latent.device}")
+    if latent.ndim != 3:
+        raise ValueError(f"latent must have shape [batch, steps, in_features], got {tuple(latent.shape)}")
+    _require_f32(latent, "latent")
+    if anchors.ndim != 3 or anchors.shape[2] != 2:
+        raise ValueError(f"anchors must have shape [tables, comparisons, 2], got {tuple(anchors.shape)}")
+    if anchors.dtype != torch.int64:
+        raise TypeError(f"anchors must be int64, got {anchors.dtype}")
+    tables, comparisons, _ = anchors.shape
+    if thresholds.shape != (tables, comparisons):
+        raise ValueError(f"thresholds must have shape {(tables, comparisons)}, got {tuple(thresholds.shape)}")
+    if lut.ndim != 3 or lut.shape[0] != tables or lut.shape[1] != (1 << comparisons):
+        raise ValueError(f"lut must have shape [tables, 2**comparisons, out_features], got {tuple(lut.shape)}")
+    nat.float_code(thresholds.dtype)
+    nat.float_code(lut.dtype)
+
+
+def pairwise_b200(
+    latent: Tensor,
+    anchors: Tensor,
+    thresholds: Tensor,
+    lut: Tensor,
+    *,
+    use_min_margin_ste: bool,
+    surrogate: str = "fast_sigmoid_odd",
+    output_scale: float = 1.0,
+    ste: bool = True,
+    anchor_index: tuple[Tensor, Tensor] | None = None,
+) -> tuple[Tensor, Tensor, Tensor]:
+    """PairwiseLinear route + LUT sum with the STE backward, on sm_100a.
+
+    Returns ``(out [B,S,out] f32, indices [B,S,T] int64, margins [B,S,T,C] f32)`` like
+    ``pairwise_tilelang``. ``output_scale`` is folded into the kernels (the
+    ``output * output_scale`` of layers/base.py:76-77); ``ste=False`` drops the
+    straight-through terms so ``latent``/``thresholds`` get no gradient, which is what the
+    torch path does outside training (layers/pairwise.py:245).
+    """
+    if surrogate not in nat.SURROGATES:
+        raise ValueError(f"Pairwise b200 backend does not support surrogate={surrogate!r}")
+    _check_pairwise_args(latent, anchors, thresholds, lut)
+    anchors = anchors.contiguous()
+    if anchor_index is None:
+        anchor_index = pairwise_anchor_index(anchors, latent.shape[-1])
+    start, entries = anchor_index
+    with torch.cuda.device(latent.device):
+        return _PairwiseB200Function.apply(
+            latent,
+            thresholds,
+            lut,
+            anchors,
+            start,
+            entries,
+            bool(use_min_margin_ste),
+            nat.SURROGATES[surrogate],
+            float(output_scale),
+            bool(ste),
+        )
+
+
+# ---------------------------------------------------------------------------
+# TropLinear
+# ---------------------------------------------------------------------------
+
+
+class _TropRouteB200Function(torch.autograd.Function):
+    @staticmethod
+    def forward(  # type: ignore[override]
+        ctx: Any,
+        latent: Tensor,
+        router_weight: Tensor,
+        router_bias: Tensor,
+        code: Tensor,
+        code_scale: float,
+        training: bool,
+    ) -> tuple[Tensor, Tensor, Tensor]:
+        batch, steps, code_dim = latent.shape
+        heads, cells, _ = router_weight.shape
+        items = batch * steps
+        dev = latent.device
+        z = latent.reshape(items, code_dim).contiguous()
+        weight = router_weight.contiguous()
+        bias = router_bias.contiguous()
+        code_c = code.contiguous()
+        pdt = nat.float_code(weight.dtype)
+        if bias.dtype != weight.dtype or code_c.dtype != weight.dtype:
+            raise TypeError("router_weight, router_bias and code must share one dtype on backend='b200'")
+        idx_dtype = packed_route_index_dtype(cells)
+        winner64 = torch.empty((items, heads), device=dev, dtype=torch.int64)
+        winner = winner64 if idx_dtype == torch.int64 else torch.empty((items, heads), device=dev, dtype=idx_dtype)
+        runner = torch.empty((items, heads), device=dev, dtype=idx_dtype)
+        margins = torch.empty((items, heads), device=dev, dtype=torch.float32)
+        hidden = torch.empty((items, code_dim), device=dev, dtype=torch.float32)
+        stream = nat.stream_handle(dev)
+        lib = nat.load()
+        icode = nat.index_code(idx_dtype)
+        _launch(
+            "trop_route",
+            lib.tropnn_b200_trop_route,
+            z.data_ptr(),
+            items,
+            code_dim,
+            weight.data_ptr(),
+            bias.data_ptr(),
+            pdt,
+            heads,
+            cells,
+            None if winner is winner64 else winner64.data_ptr(),
+            winner.data_ptr(),
+            runner.data_ptr(),
+            icode,
+            margins.data_ptr(),
+            stream,
+        )
+        _launch(
+            "trop_hidden",
+            lib.tropnn_b200_trop_hidden,
+            z.data_ptr(),
+            items,
+            code_dim,
+            code_c.data_ptr(),
+            pdt,
+            heads,
+            cells,
+            winner.data_ptr(),
+            runner.data_ptr(),
+            icode,
+            margins.data_ptr(),
+            float(code_scale),
+            int(bool(training)),
+            hidden.data_ptr(),
+            stream,
+        )
+        ctx.save_for_backward(z, weight, code_c, winner, runner, margins)
+        ctx.code_scale = float(code_scale)
+        ctx.training = bool(training)
+        ctx.shape = (batch, steps, code_dim, heads, cells)
+        winner_out = winner64.view(batch, steps, heads)
+        margins_out = margins.view(batch, steps, heads)
+        ctx.mark_non_differentiable(winner_out, margins_out)
+        return hidden.view(batch, steps, code_dim), winner_out, margins_out
+
+    @staticmethod
+    def backward(ctx: Any, grad_hidden: Tensor, grad_winner: Tensor | None, grad_margins: Tensor | None) -> tuple[Any, ...]:
+        del grad_winner, grad_margins
+        z, weight, code, winner, runner, margins = ctx.saved_tensors
+        batch, steps, code_dim, heads, cells = ctx.shape
+        items = batch * steps
+        dev = grad_hidden.device
+        training = ctx.training
+        g = grad_hidden.reshape(items, code_dim).to(torch.float32).contiguous()
+        stream = nat.stream_handle(dev)
+        lib = nat.load()
+        pdt = nat.float_code(weight.dtype)
+        icode = nat.index_code(winner.dtype)
+
+        grad_z = torch.empty((items, code_dim), device=dev, dtype=torch.float32)
+        coef_w = torch.empty((items, heads), device=dev, dtype=torch.float32)
+        coef_r = torch.empty((items, heads), device=dev, dtype=torch.float32) if training else None
+        gm = torch.empty((items, heads), device=dev, dtype=torch.float32) if training else None
+        _launch(
+            "trop_backward_rows",
+            lib.tropnn_b200_trop_backward_rows,
+            g.data_ptr(),
+            items,
+            code_dim,
+            weight.data_ptr(),
+            code.data_ptr(),
+            pdt,
+            heads,
+            cells,
+            winner.data_ptr(),
+            runner.data_ptr(),
+            icode,
+            margins.data_ptr(),
+            ctx.code_scale,
+            int(training),
+            grad_z.data_ptr(),
+            coef_w.data_ptr(),
+            nat.ptr(coef_r),
+            nat.ptr(gm),
+            stream,
+        )
+        want_code = ctx.needs_input_grad[3]
+        want_router = training and (ctx.needs_input_grad[1] or ctx.needs_input_grad[2])
+        grad_w = grad_b = grad_c = None
+        if (want_code or want_router) and items > 0:
+            perm_w = torch.empty((heads, items), device=dev, dtype=torch.int32)
+            seg_w = torch.empty((heads, cells + 1), device=dev, dtype=torch.int32)
+            _launch(
+                "bucket_sort",
+                lib.tropnn_b200_bucket_sort,
+                winner.data_ptr(),
+                icode,
+                items,
+                heads,
+                heads,
+                cells,
+                perm_w.data_ptr(),
+                seg_w.data_ptr(),
+                stream,
+            )
+            perm_r = seg_r = None
+            if training:
+                perm_r = torch.empty((heads, items), device=dev, dtype=torch.int32)
+                seg_r = torch.empty((heads, cells + 1), device=dev, dtype=torch.int32)
+                _launch(
+                    "bucket_sort",
+                    lib.tropnn_b200_bucket_sort,
+                    runner.data_ptr(),
+                    icode,
+                    items,
+                    heads,
+                    heads,
+                    cells,
+                    perm_r.data_ptr(),
+                    seg_r.data_ptr(),
+                    stream,
+                )
+            if want_code:
+                grad_c = torch.empty_like(code)
+                _launch(
+                    "trop_code_grad",
+                    lib.tropnn_b200_segment_rowsum,
+                    g.data_ptr(),
+                    items,
+                    code_dim,
+                    code_dim,
+                    heads,
+                    cells,
+                    perm_w.data_ptr(),
+                    seg_w.data_ptr(),
+                    coef_w.data_ptr(),
+                    1.0,
+                    nat.ptr(perm_r),
+                    nat.ptr(seg_r),
+                    nat.ptr(coef_r),
+                    1.0,
+                    1.0,
+                    grad_c.data_ptr(),
+                    pdt,
+                    None,
+                    stream,
+                )
+            if want_router:
+                grad_w = torch.empty_like(weight)
+                grad_b = torch.empty((heads, cells), device=dev, dtype=weight.dtype)
+                _launch(
+                    "trop_router_grad",
+                    lib.tropnn_b200_segment_rowsum,
+                    z.data_ptr(),
+                    items,
+                    code_dim,
+                    code_dim,
+                    heads,
+                    cells,
+                    perm_w.data_ptr(),
+                    seg_w.data_ptr(),
+                    gm.data_ptr(),
+                    1.0,
+                    perm_r.data_ptr(),
+                    seg_r.data_ptr(),
+                    gm.data_ptr(),
+                    -1.0,
+                    1.0,
+                    grad_w.data_ptr(),
+                    pdt,
+                    grad_b.data_ptr(),
+                    stream,
+                )
+        elif want_code:
+            grad_c = torch.zeros_like(code)
+        if want_router and grad_w is None:
+            grad_w = torch.zeros_like(weight)
+            grad_b = torch.zeros((heads, cells), device=dev, dtype=weight.dtype)
+        if not ctx.needs_input_grad[1]:
+            grad_w = None
+        if not ctx.needs_input_grad[2]:
+            grad_b = None
+        return grad_z.view(batch, steps, code_dim), grad_w, grad_b, grad_c, None, None
+
+
+def trop_route_hidden_b200(
+    latent: Tensor,
+    router_weight: Tensor,
+    router_bias: Tensor,
+    code: Tensor,
+    *,
+    code_scale: float,
+    training: bool = False,
+) -> tuple[Tensor, Tensor, Tensor]:
+    """TropLinear route + selected-code sum with the min-face backward, on sm_100a.
+
+    ``latent`` f32 ``[B, S, D]``; ``router_weight``/``code`` ``[H, K, D]`` and
+    ``router_bias`` ``[H, K]`` in one float dtype (f32/f16/bf16, upcast in-kernel).
+    Returns ``(hidden [B,S,D] f32, winner [B,S,H] int64, margins [B,S,H] f32)`` like
+    ``trop_route_hidden_tilelang``. In eval mode (``training=False``) the output does not
+    depend on the margins, so router gradients are ``None`` as in the torch path.
+    """
+    for name, t in (("latent", latent), ("router_weight", router_weight), ("router_bias", router_bias), ("code", code)):
+        _require_cuda(t, name)
+        if t.device != latent.device:
+            raise ValueError(f"{name} is on {t.device} but latent is on {latent.device}")
+    if latent.ndim != 3:
+        raise ValueError(f"latent must have shape [batch, steps, code_dim], got {tuple(latent.shape)}")
+    if router_weight.ndim != 3:
+        raise ValueError(f"router_weight must have shape [heads, cells, code_dim], got {tuple(router_weight.shape)}")
+    if router_bias.shape != router_weight.shape[:2]:
+        raise ValueError(f"router_bias must have shape [heads, cells], got {tuple(router_bias.shape)}")
+    if code.shape != router_weight.shape:
+        raise ValueError(f"code must match router_weight shape, got {tuple(code.shape)} and {tuple(router_weight.shape)}")
+    if latent.shape[-1] != router_weight.shape[-1]:
+        raise ValueError(f"latent code_dim {latent.shape[-1]} does not match router_weight code_dim {router_weight.shape[-1]}")
+    _require_f32(latent, "latent")
+    if not math.isfinite(float(code_scale)):
+        raise ValueError(f"code_scale must be finite, got {code_scale}")
+    with torch.cuda.device(latent.device):
+        return _TropRouteB200Function.apply(latent, router_weight, router_bias, code, float(code_scale), bool(training))
