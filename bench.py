@@ -266,24 +266,52 @@ def _make_inputs(w: Workload, rank: int, device: torch.device) -> tuple[torch.Te
     return x, g
 
 
-def _step(layer, x: torch.Tensor, g: torch.Tensor, w: Workload, world: int) -> torch.Tensor:
-    from tropnn_b200.distributed import allreduce_gradients
-
+def _step(layer, x: torch.Tensor, g: torch.Tensor | None, w: Workload) -> torch.Tensor:
+    """One forward (+ backward) of the layer through its public module API."""
     if w.train:
         for p in layer.parameters():
             p.grad = None
         y = layer(x)
         y.backward(g)
-        if world > 1:
-            allreduce_gradients(layer)
         return y
     with torch.no_grad():
         return layer(x)
 
 
+def _capture(fn, device: torch.device, during_capture=contextlib.nullcontext) -> torch.cuda.CUDAGraph:
+    """Captures ``fn`` (warmed up on a side stream first) into a CUDA graph."""
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with during_capture(), torch.cuda.graph(graph):
+        fn()
+    torch.cuda.synchronize(device)
+    return graph
+
+
+def _timed(steps: int, body, flush: torch.Tensor, world: int, device: torch.device) -> float:
+    """Sum of per-step CUDA-event durations (ms) of ``steps`` calls of ``body``, with an
+    untimed L2 flush before each step; barrier + synchronize on both sides."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    _barrier_sync(world, device)
+    for i in range(steps):
+        flush.fill_(float(i))
+        starts[i].record()
+        body()
+        ends[i].record()
+    _barrier_sync(world, device)
+    return sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+
+
 def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
     import tropnn_b200
     from tropnn_b200 import trace
+    from tropnn_b200.distributed import allreduce_gradients
 
     rank, world, local_rank = _dist_env()
     device = torch.device("cuda", local_rank)
@@ -302,54 +330,74 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
     g = g_host.to(device)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
 
+    def reduce_grads() -> None:
+        if world > 1 and w.train:
+            allreduce_gradients(layer)
+
+    def eager_step() -> None:
+        _step(layer, x, g, w)
+        reduce_grads()
+
     for _ in range(args.warmup):
-        _step(layer, x, g, w, world)
+        eager_step()
     _barrier_sync(world, device)
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    # Timed region: the step captured once as a CUDA graph (no host launch gaps) and
+    # replayed; at N>1 the NCCL gradient all-reduce follows each replay.
+    graph = _capture(lambda: _step(layer, x, g, w), device)
     sampler = ClockSampler(device)
-    with sampler, trace.launch_trace() as tr:
-        _barrier_sync(world, device)
-        for i in range(args.steps):
-            flush.fill_(float(i))  # untimed: evicts L2 between timed steps
-            starts[i].record()
-            _step(layer, x, g, w, world)
-            ends[i].record()
-        _barrier_sync(world, device)
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = _max_over_ranks(sum(step_ms), world, device)
-    kernels = tr.summary()
-    launches = tr.launches
 
-    # End to end: inputs from pinned host memory, output + input gradient back to host.
+    def graph_step() -> None:
+        graph.replay()
+        reduce_grads()
+
+    with sampler:
+        total_ms = _max_over_ranks(_timed(args.steps, graph_step, flush, world, device), world, device)
+
+    # Per-kernel device time: a second capture with CUDA events around every b200 launch.
+    holder: dict = {}
+
+    @contextlib.contextmanager
+    def tracing():
+        with trace.launch_trace() as t:
+            holder["trace"] = t
+            yield
+
+    traced = _capture(lambda: _step(layer, x, g, w), device, during_capture=tracing)
+    tr = holder["trace"]
+    launches_per_step = len(tr.records)
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        traced.replay()
+        tr.harvest()
+    kernels = tr.summary()
+    del traced
+
+    # The same step run eagerly through the module API (host launch overhead included).
+    eager_ms = _max_over_ranks(_timed(args.steps, eager_step, flush, world, device), world, device)
+
+    # End to end: eager public API, inputs copied from pinned host memory and the output
+    # (+ input gradient) copied back inside the timed region.
     x_pin = x_host.pin_memory()
     g_pin = g_host.pin_memory()
     y_pin = torch.empty((w.rows_per_gpu, 1, w.out_features), dtype=torch.float32).pin_memory()
     gx_pin = torch.empty_like(x_host).pin_memory()
     h2d = x_pin.numel() * 4 + (g_pin.numel() * 4 if w.train else 0)
     d2h = y_pin.numel() * 4 + (gx_pin.numel() * 4 if w.train else 0)
-    e2e_steps = max(3, args.steps)
 
     def e2e_step() -> None:
         xd = x_pin.to(device, non_blocking=True).requires_grad_(w.train)
         gd = g_pin.to(device, non_blocking=True) if w.train else None
-        y = _step(layer, xd, gd, w, world)
+        y = _step(layer, xd, gd, w)
+        reduce_grads()
         y_pin.copy_(y.detach().float(), non_blocking=True)
         if w.train:
             gx_pin.copy_(xd.grad, non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
-    _barrier_sync(world, device)
-    e_start = torch.cuda.Event(enable_timing=True)
-    e_end = torch.cuda.Event(enable_timing=True)
-    e_start.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e_end.record()
-    _barrier_sync(world, device)
-    e2e_ms = _max_over_ranks(e_start.elapsed_time(e_end), world, device)
+    e2e_ms = _max_over_ranks(_timed(args.steps, e2e_step, flush, world, device), world, device)
+    del graph
 
     if world > 1:
         import torch.distributed as dist
@@ -360,7 +408,7 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
 
     rows_total = w.rows_per_gpu * world
     value = rows_total * args.steps / (total_ms / 1e3)
-    e2e_value = rows_total * e2e_steps / (e2e_ms / 1e3)
+    e2e_value = rows_total * args.steps / (e2e_ms / 1e3)
 
     peaks, peaks_kind = _peaks()
     roofline = None
@@ -385,6 +433,7 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
             "algorithmic_bytes_per_launch": per_launch,
             "mean_launch_us": round(mean_s * 1e6, 2),
         }
+    step_kernel_ms = sum(v["total_ms"] for v in kernels.values()) / args.steps
 
     return {
         "metric": "TropLinear/PairwiseLinear rows/s fwd+bwd, 1-8 B200; % of HBM/TC roofline",
@@ -405,16 +454,22 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
             "global_batch": rows_total,
             "parallelism": f"dp{world} (batch-row shards, NCCL grad all-reduce)" if world > 1 else "single GPU",
             "l2": f"flushed between timed steps ({L2_FLUSH_BYTES >> 20} MiB write, untimed)",
+            "timing": "step captured as one CUDA graph and replayed (all-reduce eager after it at N>1)",
         },
+        "eager": {"value": round(rows_total * args.steps / (eager_ms / 1e3), 1), "unit": "rows/s",
+                  "ms_per_step": round(eager_ms / args.steps, 4)},
         "e2e": {
             "value": round(e2e_value, 1),
             "unit": "rows/s",
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "ms_per_step": round(e2e_ms / e2e_steps, 4),
+            "ms_per_step": round(e2e_ms / args.steps, 4),
+            "path": "eager module API, pinned host inputs in, output + input gradient out",
         },
-        "gpu_launches": launches,
-        "kernels": {k: {"launches": v["launches"], "mean_us": round(v["mean_ms"] * 1e3, 2)} for k, v in kernels.items()},
+        "gpu_launches": launches_per_step * args.steps,
+        "kernels": {k: {"launches_per_step": v["launches"] // args.steps, "mean_us": round(v["mean_ms"] * 1e3, 2)}
+                    for k, v in kernels.items()},
+        "kernel_ms_per_step": round(step_kernel_ms, 4),
         "roofline": roofline,
         "clocks": sampler.summary(),
     }

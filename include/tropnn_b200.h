@@ -149,13 +149,19 @@ TROPNN_B200_API int tropnn_b200_pairwise_ste_backward(const float *grad_out, int
                                       const int32_t *feat_start, const int32_t *feat_entries,
                                       float *grad_latent, float *gu, uint8_t *rstar, void *stream);
 
+/* Bytes of scratch tropnn_b200_pairwise_threshold_grad needs (row-block partial sums). */
+TROPNN_B200_API size_t tropnn_b200_pairwise_threshold_grad_workspace_size(int64_t items, int64_t tables,
+                                                                          int64_t comparisons);
+
 /*
- * grad_thresholds[t,r] = -sum_n gu (min mode: rows whose r* == r), fixed-order
- * reduction, written in grad_dtype.
+ * grad_thresholds[t,r] = -sum_n gu (min mode: rows whose r* == r), written in
+ * grad_dtype. Two launches: per-row-block partial sums into `workspace`, then a
+ * fixed-order sum of the partials (deterministic).
  */
 TROPNN_B200_API int tropnn_b200_pairwise_threshold_grad(const float *gu, const uint8_t *rstar, int64_t items,
                                         int64_t tables, int64_t comparisons, int use_min_margin_ste,
-                                        void *grad_thresholds, int grad_dtype, void *stream);
+                                        void *grad_thresholds, int grad_dtype, void *workspace,
+                                        size_t workspace_bytes, void *stream);
 
 /* Bytes of scratch tropnn_b200_pairwise_backward needs. */
 TROPNN_B200_API size_t tropnn_b200_pairwise_backward_workspace_size(int64_t items, int64_t tables, int64_t comparisons,

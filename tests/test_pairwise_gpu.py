@@ -134,10 +134,11 @@ def test_three_d_input_and_f16_input_dtype() -> None:
     assert layer._last_indices.shape == (3, 5, 8) and layer._last_indices.dtype == torch.int64
     assert layer._last_margins.shape == (3, 5, 8, 4)
     ref = oracle.pairwise_forward(
-        x.float().reshape(15, 32).cpu().numpy(), *(t.cpu().numpy() for t in (layer.anchors, layer.thresholds, layer.lut)),
+        x.float().reshape(15, 32).cpu().numpy(),
+        *(t.detach().cpu().numpy() for t in (layer.anchors, layer.thresholds, layer.lut)),
         output_scale=layer.output_scale,
     )
-    assert rel_err(y.float().reshape(15, 24).cpu().numpy(), ref["out"]) <= 1e-3
+    assert rel_err(y.detach().float().reshape(15, 24).cpu().numpy(), ref["out"]) <= 1e-3
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])

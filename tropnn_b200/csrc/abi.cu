@@ -1,4 +1,7 @@
 // Status plumbing and device checks shared by every entry point.
+#include <mutex>
+#include <vector>
+
 #include "common.cuh"
 
 namespace tropnn_b200 {
@@ -63,13 +66,47 @@ int check_launch(const char *what) {
   return TROPNN_B200_OK;
 }
 
+namespace {
+struct SmemEntry {
+  const void *func;
+  int device;
+  size_t bytes;
+};
+std::mutex g_smem_mutex;
+std::vector<SmemEntry> g_smem_table;
+}  // namespace
+
+int ensure_dynamic_smem(const void *func, size_t bytes, const char *what) {
+  if (bytes <= 48 * 1024) return TROPNN_B200_OK;
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return set_error(TROPNN_B200_ERR_DEVICE, "%s: cudaGetDevice: %s", what, cudaGetErrorString(err));
+  std::lock_guard<std::mutex> lock(g_smem_mutex);
+  for (auto &e : g_smem_table) {
+    if (e.func == func && e.device == device) {
+      if (e.bytes >= bytes) return TROPNN_B200_OK;
+      err = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+      if (err != cudaSuccess)
+        return set_error(TROPNN_B200_ERR_LAUNCH, "%s: %zu bytes of shared memory: %s", what, bytes,
+                         cudaGetErrorString(err));
+      e.bytes = bytes;
+      return TROPNN_B200_OK;
+    }
+  }
+  err = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (err != cudaSuccess)
+    return set_error(TROPNN_B200_ERR_LAUNCH, "%s: %zu bytes of shared memory: %s", what, bytes, cudaGetErrorString(err));
+  g_smem_table.push_back({func, device, bytes});
+  return TROPNN_B200_OK;
+}
+
 }  // namespace tropnn_b200
 
 extern "C" {
 
 const char *tropnn_b200_last_error(void) { return tropnn_b200::g_last_error.c_str(); }
 
-int tropnn_b200_abi_version(void) { return 1; }
+int tropnn_b200_abi_version(void) { return 2; }
 
 int tropnn_b200_check_device(int device) {
   int major = 0;

@@ -55,6 +55,25 @@ __device__ int block_exclusive_scan(int *vals, int count, int *tmp) {
   return total;
 }
 
+// Keys of up to kSortTileRows rows are staged in shared memory (uint16) at a time, with
+// every thread issuing independent loads, so the strided key column is read once per
+// pass with full memory-level parallelism.
+constexpr int kSortTileRows = 16384;
+
+template <typename K>
+__device__ __forceinline__ void stage_keys(const K *__restrict__ keys, int64_t tile0, int tile_rows, int64_t stride,
+                                           int64_t g, int buckets, uint16_t *keys_s) {
+#pragma unroll 8
+  for (int i = threadIdx.x; i < tile_rows; i += kSortThreads)
+    keys_s[i] = static_cast<uint16_t>(load_key(keys, tile0 + i, stride, g, buckets));
+}
+
+// Stable counting sort of one group's rows by key (one CTA per group).
+// Pass 1 counts every bucket (shared-memory atomics on integers: order-free), the
+// exclusive scan gives the bucket starts. Pass 2 walks the tiles in row order; inside
+// a tile warp w owns a contiguous run of rows, so
+//   position = bucket start + rows of earlier tiles + rows of earlier warps + rank in warp
+// keeps rows of a bucket in ascending order.
 template <typename K>
 __global__ void __launch_bounds__(kSortThreads) bucket_sort_kernel(const K *__restrict__ keys, int64_t rows,
                                                                    int64_t stride, int buckets,
@@ -62,71 +81,84 @@ __global__ void __launch_bounds__(kSortThreads) bucket_sort_kernel(const K *__re
                                                                    int32_t *__restrict__ seg) {
   extern __shared__ int smem[];
   int *counts = smem;                            // [kSortWarps][buckets]
-  int *totals = counts + kSortWarps * buckets;   // [buckets]
-  int *tmp = totals + buckets;                   // [kSortThreads]
+  int *base = counts + kSortWarps * buckets;     // [buckets] running start per bucket
+  int *tmp = base + buckets;                     // [kSortThreads]
+  uint16_t *keys_s = reinterpret_cast<uint16_t *>(tmp + kSortThreads);  // [kSortTileRows]
   const int64_t g = blockIdx.x;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const unsigned lt_mask = (1u << lane) - 1u;
+  const int tiles = static_cast<int>((rows + kSortTileRows - 1) / kSortTileRows);
 
-  for (int i = threadIdx.x; i < kSortWarps * buckets; i += kSortThreads) counts[i] = 0;
+  for (int b = threadIdx.x; b < buckets; b += kSortThreads) base[b] = 0;
   __syncthreads();
-
-  // Contiguous row range per warp, a multiple of 32 rows long.
-  const int64_t per_warp = ((rows + kSortWarps - 1) / kSortWarps + 31) & ~int64_t(31);
-  const int64_t start = min(rows, int64_t(warp) * per_warp);
-  const int64_t end = min(rows, start + per_warp);
-  int *my_counts = counts + warp * buckets;
-
-  for (int64_t base = start; base < end; base += 32) {
-    const int64_t n = base + lane;
-    const bool valid = n < end;
-    const unsigned active = __ballot_sync(0xffffffffu, valid);
-    if (valid) {
-      const int key = load_key(keys, n, stride, g, buckets);
-      const unsigned peers = __match_any_sync(active, key);
-      if (lane == __ffs(peers) - 1) my_counts[key] += __popc(peers);
+  for (int tile = 0; tile < tiles; ++tile) {
+    const int64_t tile0 = int64_t(tile) * kSortTileRows;
+    const int tile_rows = static_cast<int>(min64(kSortTileRows, rows - tile0));
+    if (tiles > 1 || tile == 0) {
+      stage_keys(keys, tile0, tile_rows, stride, g, buckets, keys_s);
+      __syncthreads();
     }
-    __syncwarp();
+    for (int i = threadIdx.x; i < tile_rows; i += kSortThreads) atomicAdd(base + keys_s[i], 1);
+    __syncthreads();
   }
-  __syncthreads();
-
-  for (int b = threadIdx.x; b < buckets; b += kSortThreads) {
-    int s = 0;
-    for (int w = 0; w < kSortWarps; ++w) s += counts[w * buckets + b];
-    totals[b] = s;
-  }
-  __syncthreads();
-  block_exclusive_scan(totals, buckets, tmp);
+  block_exclusive_scan(base, buckets, tmp);
   int32_t *my_seg = seg + g * (buckets + 1);
-  for (int b = threadIdx.x; b < buckets; b += kSortThreads) {
-    int run = totals[b];
-    my_seg[b] = run;
-    for (int w = 0; w < kSortWarps; ++w) {
-      int c = counts[w * buckets + b];
-      counts[w * buckets + b] = run;
-      run += c;
-    }
-  }
+  for (int b = threadIdx.x; b < buckets; b += kSortThreads) my_seg[b] = base[b];
   if (threadIdx.x == 0) my_seg[buckets] = static_cast<int32_t>(rows);
-  __syncthreads();
 
   int32_t *my_perm = perm + g * rows;
-  for (int64_t base = start; base < end; base += 32) {
-    const int64_t n = base + lane;
-    const bool valid = n < end;
-    const unsigned active = __ballot_sync(0xffffffffu, valid);
-    int key = 0;
-    unsigned peers = 0;
-    if (valid) {
-      key = load_key(keys, n, stride, g, buckets);
-      peers = __match_any_sync(active, key);
-      const int pos = my_counts[key] + __popc(peers & lt_mask);
-      my_perm[pos] = static_cast<int32_t>(n);
+  int *my_counts = counts + warp * buckets;
+  for (int tile = 0; tile < tiles; ++tile) {
+    const int64_t tile0 = int64_t(tile) * kSortTileRows;
+    const int tile_rows = static_cast<int>(min64(kSortTileRows, rows - tile0));
+    if (tiles > 1) {
+      __syncthreads();
+      stage_keys(keys, tile0, tile_rows, stride, g, buckets, keys_s);
     }
-    __syncwarp();
-    if (valid && lane == __ffs(peers) - 1) my_counts[key] += __popc(peers);
-    __syncwarp();
+    for (int i = threadIdx.x; i < kSortWarps * buckets; i += kSortThreads) counts[i] = 0;
+    __syncthreads();
+    // Contiguous run of the tile per warp, a multiple of 32 rows long.
+    const int per_warp = ((tile_rows + kSortWarps - 1) / kSortWarps + 31) & ~31;
+    const int start = min(tile_rows, warp * per_warp);
+    const int end = min(tile_rows, start + per_warp);
+    for (int r0 = start; r0 < end; r0 += 32) {
+      const int r = r0 + lane;
+      const bool valid = r < end;
+      const unsigned active = __ballot_sync(0xffffffffu, valid);
+      if (valid) {
+        const int key = keys_s[r];
+        const unsigned peers = __match_any_sync(active, key);
+        if (lane == __ffs(peers) - 1) my_counts[key] += __popc(peers);
+      }
+      __syncwarp();
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < buckets; b += kSortThreads) {
+      int run = base[b];
+      for (int w = 0; w < kSortWarps; ++w) {
+        const int c = counts[w * buckets + b];
+        counts[w * buckets + b] = run;
+        run += c;
+      }
+      base[b] = run;
+    }
+    __syncthreads();
+    for (int r0 = start; r0 < end; r0 += 32) {
+      const int r = r0 + lane;
+      const bool valid = r < end;
+      const unsigned active = __ballot_sync(0xffffffffu, valid);
+      int key = 0;
+      unsigned peers = 0;
+      if (valid) {
+        key = keys_s[r];
+        peers = __match_any_sync(active, key);
+        my_perm[my_counts[key] + __popc(peers & lt_mask)] = static_cast<int32_t>(tile0 + r);
+      }
+      __syncwarp();
+      if (valid && lane == __ffs(peers) - 1) my_counts[key] += __popc(peers);
+      __syncwarp();
+    }
   }
 }
 
@@ -163,7 +195,34 @@ __device__ __forceinline__ void accumulate_list(const SegList &L, const float *_
   const int lo = __ldg(segp + b);
   const int hi = __ldg(segp + b + 1);
   const int32_t *permp = L.perm + g * rows;
-  for (int j = lo; j < hi; ++j) {
+  int j = lo;
+  // Four rows per pass keep 4*NV vector loads in flight; the accumulation order (ascending
+  // position in the bucket) is the same as the one-row loop below.
+  for (; j + 4 <= hi; j += 4) {
+    int64_t n[4];
+    float c[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) n[u] = __ldg(permp + j + u);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      c[u] = L.coef ? __fmul_rn(L.sign, __ldg(L.coef + n[u] * groups + g)) : L.sign;
+      coef_total += c[u];
+    }
+#pragma unroll
+    for (int s = 0; s < NV; ++s) {
+      const int64_t col = col0 + int64_t(s) * 32 * VEC + int64_t(lane) * VEC;
+      if (col < width) {
+        float v[4][VEC];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) VecLoad<float, VEC>::load(values + n[u] * ld + col, v[u]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) acc[s][e] = fmaf(c[u], v[u][e], acc[s][e]);
+      }
+    }
+  }
+  for (; j < hi; ++j) {
     const int64_t n = __ldg(permp + j);
     const float c = L.coef ? __fmul_rn(L.sign, __ldg(L.coef + n * groups + g)) : L.sign;
     coef_total += c;
@@ -275,35 +334,27 @@ int bucket_sort_impl(const void *keys, int key_dtype, int64_t rows, int64_t grou
   if (groups == 0) return TROPNN_B200_OK;
   TB_REQUIRE(seg != nullptr && ((keys != nullptr && perm != nullptr) || rows == 0), TROPNN_B200_ERR_INVALID,
              "bucket_sort: null pointer");
-  const size_t smem = sizeof(int) * (kSortWarps * buckets + buckets + kSortThreads);
+  const size_t smem = sizeof(int) * (kSortWarps * buckets + buckets + kSortThreads) +
+                      sizeof(uint16_t) * static_cast<size_t>(min64(rows, kSortTileRows));
   const int nb = static_cast<int>(buckets);
-  cudaError_t attr_err = cudaSuccess;
+  const unsigned grid = static_cast<unsigned>(groups);
   switch (key_dtype) {
     case TROPNN_B200_U8:
-      attr_err = cudaFuncSetAttribute(bucket_sort_kernel<uint8_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(smem));
-      if (attr_err == cudaSuccess)
-        bucket_sort_kernel<uint8_t><<<static_cast<unsigned>(groups), kSortThreads, smem, stream>>>(
-            static_cast<const uint8_t *>(keys), rows, stride, nb, perm, seg);
+      TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(bucket_sort_kernel<uint8_t>), smem, "bucket_sort"));
+      bucket_sort_kernel<uint8_t><<<grid, kSortThreads, smem, stream>>>(static_cast<const uint8_t *>(keys), rows,
+                                                                         stride, nb, perm, seg);
       break;
     case TROPNN_B200_I16:
-      attr_err = cudaFuncSetAttribute(bucket_sort_kernel<int16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(smem));
-      if (attr_err == cudaSuccess)
-        bucket_sort_kernel<int16_t><<<static_cast<unsigned>(groups), kSortThreads, smem, stream>>>(
-            static_cast<const int16_t *>(keys), rows, stride, nb, perm, seg);
+      TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(bucket_sort_kernel<int16_t>), smem, "bucket_sort"));
+      bucket_sort_kernel<int16_t><<<grid, kSortThreads, smem, stream>>>(static_cast<const int16_t *>(keys), rows,
+                                                                         stride, nb, perm, seg);
       break;
     default:
-      attr_err = cudaFuncSetAttribute(bucket_sort_kernel<int64_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(smem));
-      if (attr_err == cudaSuccess)
-        bucket_sort_kernel<int64_t><<<static_cast<unsigned>(groups), kSortThreads, smem, stream>>>(
-            static_cast<const int64_t *>(keys), rows, stride, nb, perm, seg);
+      TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(bucket_sort_kernel<int64_t>), smem, "bucket_sort"));
+      bucket_sort_kernel<int64_t><<<grid, kSortThreads, smem, stream>>>(static_cast<const int64_t *>(keys), rows,
+                                                                         stride, nb, perm, seg);
       break;
   }
-  if (attr_err != cudaSuccess)
-    return set_error(TROPNN_B200_ERR_LAUNCH, "bucket_sort: cudaFuncSetAttribute failed: %s",
-                     cudaGetErrorString(attr_err));
   return check_launch("bucket_sort");
 }
 

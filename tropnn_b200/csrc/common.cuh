@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -27,6 +28,9 @@ int clear_error();
 int check_current_device();
 // Maps a pending CUDA launch error to TROPNN_B200_ERR_LAUNCH (with `what` in the message).
 int check_launch(const char *what);
+// Raises `func`'s dynamic shared-memory limit on the current device to at least `bytes`
+// (once per kernel and device; later calls are a table lookup).
+int ensure_dynamic_smem(const void *func, size_t bytes, const char *what);
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 

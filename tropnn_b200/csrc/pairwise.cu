@@ -28,7 +28,7 @@ namespace {
 
 constexpr int kMaxComparisons = 12;
 constexpr int kFwdWarps = 4;
-constexpr int kFwdRows = 8;  // rows per CTA in the forward
+constexpr int kFwdRows = 4;  // rows per CTA in the forward (one per warp)
 
 __device__ __forceinline__ int64_t clamp_feature(int64_t a, int64_t in) { return a < 0 ? 0 : (a >= in ? in - 1 : a); }
 
@@ -57,13 +57,18 @@ __global__ void __launch_bounds__(kFwdWarps * 32) pairwise_forward_kernel(
     const int64_t n = row0 + r;
     const float *xrow = x + n * in;
     int bits = 0;
-    for (int c = 0; c < C; ++c) {
-      const int64_t e = (int64_t(t) * C + c) * 2;
-      const int64_t a = clamp_feature(__ldg(anchors + e), in);
-      const int64_t b = clamp_feature(__ldg(anchors + e + 1), in);
-      const float u = __fsub_rn(__fsub_rn(__ldg(xrow + a), __ldg(xrow + b)), ldg_f32(thr + int64_t(t) * C + c));
-      if (write_routes) u_out[(n * T + t) * C + c] = u;
-      bits |= (u > 0.f ? 1 : 0) << c;
+    // Fully unrolled over the comparison slots so the 2C anchor and latent loads of a
+    // table are independent and in flight together.
+#pragma unroll
+    for (int c = 0; c < kMaxComparisons; ++c) {
+      if (c < C) {
+        const int64_t e = (int64_t(t) * C + c) * 2;
+        const int64_t a = clamp_feature(__ldg(anchors + e), in);
+        const int64_t b = clamp_feature(__ldg(anchors + e + 1), in);
+        const float u = __fsub_rn(__fsub_rn(__ldg(xrow + a), __ldg(xrow + b)), ldg_f32(thr + int64_t(t) * C + c));
+        if (write_routes) u_out[(n * T + t) * C + c] = u;
+        bits |= (u > 0.f ? 1 : 0) << c;
+      }
     }
     idx_s[r * T + t] = bits;
     if (write_routes) idx_out[n * T + t] = bits;
@@ -125,11 +130,7 @@ int launch_forward(const float *x, int64_t rows, int64_t in, const int64_t *anch
              "pairwise_forward: grid too large (items=%lld out=%lld)", (long long)rows, (long long)out);
   const size_t smem = sizeof(int) * kFwdRows * T;
   auto kernel = pairwise_forward_kernel<LutT, ThrT, VEC, NV>;
-  if (smem > 48 * 1024) {
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (err != cudaSuccess)
-      return set_error(TROPNN_B200_ERR_LAUNCH, "pairwise_forward: cudaFuncSetAttribute: %s", cudaGetErrorString(err));
-  }
+  TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "pairwise_forward"));
   dim3 grid(static_cast<unsigned>(row_blocks), static_cast<unsigned>(col_tiles));
   kernel<<<grid, kFwdWarps * 32, smem, stream>>>(x, rows, in, anchors, static_cast<const ThrT *>(thr), T, C,
                                                  static_cast<const LutT *>(lut), out, out_scale, y, idx, u);
@@ -196,39 +197,77 @@ __global__ void __launch_bounds__(kSteMaxWarps * 32) pairwise_ste_kernel(
   const int per_row = MIN ? T : T * C;
   float *gu_s = ste_smem + warp * per_row;
   uint8_t *rs_s = reinterpret_cast<uint8_t *>(ste_smem + warps * per_row) + warp * T;
+  uint16_t *cur_s = reinterpret_cast<uint16_t *>(ste_smem + warps * per_row + (warps * T + 3) / 4) + warp * T;
   const int64_t table_size = int64_t(1) << C;
   const float *grow = g + n * out;
 
-  for (int t = 0; t < T; ++t) {
+  if (MIN) {
+    // Prologue, lanes over tables: r* = argmin |u| (first on ties), the current bucket,
+    // and u at r* (parked in gu_s until lane 0 turns it into gu).
+    for (int t = lane; t < T; t += 32) {
+      const float *urow = u + (n * T + t) * C;
+      int rmin = 0;
+      float ustar = __ldg(urow);
+      float best = fabsf(ustar);
+      for (int c = 1; c < C; ++c) {
+        const float v = __ldg(urow + c);
+        if (fabsf(v) < best) { best = fabsf(v); rmin = c; ustar = v; }
+      }
+      rs_s[t] = static_cast<uint8_t>(rmin);
+      cur_s[t] = static_cast<uint16_t>(__ldg(idx + n * T + t));
+      gu_s[t] = ustar;
+    }
+    __syncwarp();
+    // Four tables per pass: one read of g, eight LUT rows in flight, four reductions.
+    constexpr int TB = 4;
+    for (int t0 = 0; t0 < T; t0 += TB) {
+      const LutT *lcur[TB];
+      const LutT *lnb[TB];
+      float dot[TB];
+#pragma unroll
+      for (int k = 0; k < TB; ++k) {
+        const int t = min(t0 + k, T - 1);
+        const int cur = cur_s[t];
+        lcur[k] = lut + (int64_t(t) * table_size + cur) * out;
+        lnb[k] = lut + (int64_t(t) * table_size + (cur ^ (1 << rs_s[t]))) * out;
+        dot[k] = 0.f;
+      }
+      for (int64_t col = int64_t(lane) * VEC; col < out; col += 32 * VEC) {
+        float gv[VEC];
+        VecLoad<float, VEC>::load(grow + col, gv);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) gv[e] = __fmul_rn(gv[e], out_scale);
+#pragma unroll
+        for (int k = 0; k < TB; ++k) {
+          float vc[VEC], vn[VEC];
+          VecLoad<LutT, VEC>::load(lcur[k] + col, vc);
+          VecLoad<LutT, VEC>::load(lnb[k] + col, vn);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) dot[k] = fmaf(gv[e], __fsub_rn(vn[e], vc[e]), dot[k]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < TB; ++k) dot[k] = warp_sum(dot[k]);
+      if (lane == 0) {
+#pragma unroll
+        for (int k = 0; k < TB; ++k) {
+          const int t = t0 + k;
+          if (t < T) {
+            const float gu = __fmul_rn(dot[k], surrogate_grad(gu_s[t], surrogate));
+            gu_s[t] = gu;
+            gu_out[n * T + t] = gu;
+            rstar_out[n * T + t] = rs_s[t];
+          }
+        }
+      }
+    }
+  }
+
+  for (int t = 0; t < (MIN ? 0 : T); ++t) {
     const float *urow = u + (n * T + t) * C;
     const int cur = static_cast<int>(__ldg(idx + n * T + t));
     const LutT *lcur = lut + (int64_t(t) * table_size + cur) * out;
-    if (MIN) {
-      int rmin = 0;
-      float best = fabsf(__ldg(urow));
-      for (int c = 1; c < C; ++c) {
-        const float a = fabsf(__ldg(urow + c));
-        if (a < best) { best = a; rmin = c; }
-      }
-      const LutT *lnb = lut + (int64_t(t) * table_size + (cur ^ (1 << rmin))) * out;
-      float dot = 0.f;
-      for (int64_t col = int64_t(lane) * VEC; col < out; col += 32 * VEC) {
-        float vc[VEC], vn[VEC], gv[VEC];
-        VecLoad<LutT, VEC>::load(lcur + col, vc);
-        VecLoad<LutT, VEC>::load(lnb + col, vn);
-        VecLoad<float, VEC>::load(grow + col, gv);
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) dot = fmaf(__fmul_rn(gv[e], out_scale), __fsub_rn(vn[e], vc[e]), dot);
-      }
-      dot = warp_sum(dot);
-      if (lane == 0) {
-        const float gu = __fmul_rn(dot, surrogate_grad(__ldg(urow + rmin), surrogate));
-        gu_s[t] = gu;
-        rs_s[t] = static_cast<uint8_t>(rmin);
-        gu_out[n * T + t] = gu;
-        rstar_out[n * T + t] = static_cast<uint8_t>(rmin);
-      }
-    } else {
+    {
       float dot[kMaxComparisons];
 #pragma unroll
       for (int c = 0; c < kMaxComparisons; ++c) dot[c] = 0.f;
@@ -290,7 +329,8 @@ template <typename LutT, int VEC>
 int launch_ste(bool use_min, const float *g, int64_t rows, int64_t out, float out_scale, const int64_t *idx,
                const float *u, int T, int C, int64_t in, const void *lut, int surrogate, const int32_t *fs,
                const int32_t *fe, float *gx, float *gu, uint8_t *rs, cudaStream_t stream) {
-  const size_t per_warp = sizeof(float) * (use_min ? T : T * C) + T;
+  // gu (f32, one per table or per comparison) + r* (u8) + current bucket (u16) per row.
+  const size_t per_warp = sizeof(float) * (use_min ? T : T * C) + 3 * size_t(T);
   int warps = kSteMaxWarps;
   while (warps > 1 && per_warp * warps > 96 * 1024) --warps;
   const size_t smem = per_warp * warps + 16;
@@ -299,12 +339,7 @@ int launch_ste(bool use_min, const float *g, int64_t rows, int64_t out, float ou
   const int64_t blocks = ceil_div(rows, warps);
   TB_REQUIRE(blocks < (int64_t(1) << 31), TROPNN_B200_ERR_INVALID, "pairwise_ste_backward: too many rows");
   auto kernel = use_min ? pairwise_ste_kernel<LutT, VEC, true> : pairwise_ste_kernel<LutT, VEC, false>;
-  if (smem > 48 * 1024) {
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (err != cudaSuccess)
-      return set_error(TROPNN_B200_ERR_LAUNCH, "pairwise_ste_backward: cudaFuncSetAttribute: %s",
-                       cudaGetErrorString(err));
-  }
+  TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "pairwise_ste_backward"));
   kernel<<<static_cast<unsigned>(blocks), warps * 32, smem, stream>>>(
       g, rows, out, out_scale, idx, u, T, C, in, static_cast<const LutT *>(lut), surrogate, fs, fe, gx, gu, rs);
   return check_launch("pairwise_ste_backward");
@@ -328,21 +363,35 @@ int ste_by_width(bool use_min, const float *g, int64_t rows, int64_t out, float 
 // ---------------------------------------------------------------------------
 // threshold gradient: fixed-order reduction over rows
 // ---------------------------------------------------------------------------
-// CTA = 8 warps over a block of 32 tables; lane <-> table (coalesced reads of gu),
-// warps stride over rows, then a fixed-shape combine across warps.
-template <typename OutT, bool MIN>
-__global__ void __launch_bounds__(256) threshold_grad_kernel(const float *__restrict__ gu,
-                                                             const uint8_t *__restrict__ rstar, int64_t rows, int T,
-                                                             int C, OutT *__restrict__ grad) {
+// Stage 1: CTA (table block of 32, row block) = 8 warps; lane <-> table (coalesced reads
+// of gu), warps stride over the block's rows, a fixed-shape combine across warps writes
+// partial[row_block][t][c]. Stage 2 sums the partials over row blocks in order. The
+// result is deterministic; rows are spread over many CTAs instead of one.
+constexpr int kThrRowsPerBlock = 64;
+constexpr int kThrMaxRowBlocks = 1024;
+
+inline int64_t threshold_row_blocks(int64_t rows) {
+  return std::max<int64_t>(1, std::min<int64_t>(kThrMaxRowBlocks, ceil_div(rows, kThrRowsPerBlock)));
+}
+
+template <bool MIN>
+__global__ void __launch_bounds__(256) threshold_partial_kernel(const float *__restrict__ gu,
+                                                                const uint8_t *__restrict__ rstar, int64_t rows,
+                                                                int T, int C, float *__restrict__ partial) {
   __shared__ float part[8][32][kMaxComparisons];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 32 + lane;
+  const int64_t blocks = gridDim.y;
+  const int64_t per_block = (rows + blocks - 1) / blocks;
+  const int64_t r0 = int64_t(blockIdx.y) * per_block;
+  const int64_t r1 = min64(rows, r0 + per_block);
   float acc[kMaxComparisons];
 #pragma unroll
   for (int c = 0; c < kMaxComparisons; ++c) acc[c] = 0.f;
   if (t < T) {
-    for (int64_t n = warp; n < rows; n += 8) {
+#pragma unroll 4
+    for (int64_t n = r0 + warp; n < r1; n += 8) {
       if (MIN) {
         const float v = __ldg(gu + n * T + t);
         const int r = __ldg(rstar + n * T + t);
@@ -366,9 +415,19 @@ __global__ void __launch_bounds__(256) threshold_grad_kernel(const float *__rest
     if (tt < T) {
       float s = 0.f;
       for (int w = 0; w < 8; ++w) s = __fadd_rn(s, part[w][l][c]);
-      grad[int64_t(tt) * C + c] = from_f32<OutT>(-s);
+      partial[(int64_t(blockIdx.y) * T + tt) * C + c] = s;
     }
   }
+}
+
+template <typename OutT>
+__global__ void __launch_bounds__(256) threshold_combine_kernel(const float *__restrict__ partial, int blocks,
+                                                                int64_t TC, OutT *__restrict__ grad) {
+  const int64_t k = int64_t(blockIdx.x) * 256 + threadIdx.x;
+  if (k >= TC) return;
+  float s = 0.f;
+  for (int b = 0; b < blocks; ++b) s = __fadd_rn(s, __ldg(partial + int64_t(b) * TC + k));
+  grad[k] = from_f32<OutT>(-s);
 }
 
 // ---------------------------------------------------------------------------
@@ -502,26 +561,46 @@ int pairwise_ste_impl(const float *g, int64_t items, int64_t out, float out_scal
   }
 }
 
+size_t threshold_grad_workspace(int64_t items, int64_t tables, int64_t comparisons) {
+  return WorkspaceCarver::align(sizeof(float) * size_t(threshold_row_blocks(items)) * size_t(tables) *
+                                size_t(comparisons));
+}
+
 int pairwise_threshold_grad_impl(const float *gu, const uint8_t *rs, int64_t items, int64_t tables,
-                                 int64_t comparisons, int use_min, void *grad, int grad_dtype, cudaStream_t stream) {
+                                 int64_t comparisons, int use_min, void *grad, int grad_dtype, void *ws,
+                                 size_t ws_bytes, cudaStream_t stream) {
   TB_CHECK(validate_pairwise(items, 1, tables, comparisons, 1));
   TB_REQUIRE(is_float_dtype(grad_dtype), TROPNN_B200_ERR_DTYPE, "pairwise_threshold_grad: dtype %s unsupported",
              dtype_name(grad_dtype));
   TB_REQUIRE(grad && (items == 0 || (gu && (rs || !use_min))), TROPNN_B200_ERR_INVALID,
              "pairwise_threshold_grad: null pointer");
-  const unsigned blocks = static_cast<unsigned>(ceil_div(tables, 32));
+  const size_t need = threshold_grad_workspace(items, tables, comparisons);
+  TB_REQUIRE(ws != nullptr && ws_bytes >= need, TROPNN_B200_ERR_WORKSPACE,
+             "pairwise_threshold_grad: workspace of %zu bytes is smaller than the %zu bytes required", ws_bytes, need);
   const int T = static_cast<int>(tables), C = static_cast<int>(comparisons);
-#define TB_THR_LAUNCH(OUT_T)                                                                                   \
-  if (use_min)                                                                                                 \
-    threshold_grad_kernel<OUT_T, true><<<blocks, 256, 0, stream>>>(gu, rs, items, T, C, static_cast<OUT_T *>(grad)); \
-  else                                                                                                         \
-    threshold_grad_kernel<OUT_T, false><<<blocks, 256, 0, stream>>>(gu, rs, items, T, C, static_cast<OUT_T *>(grad));
+  const int64_t row_blocks = threshold_row_blocks(items);
+  float *partial = static_cast<float *>(ws);
+  dim3 grid(static_cast<unsigned>(ceil_div(tables, 32)), static_cast<unsigned>(row_blocks));
+  if (use_min)
+    threshold_partial_kernel<true><<<grid, 256, 0, stream>>>(gu, rs, items, T, C, partial);
+  else
+    threshold_partial_kernel<false><<<grid, 256, 0, stream>>>(gu, rs, items, T, C, partial);
+  TB_CHECK(check_launch("pairwise_threshold_grad (partials)"));
+  const int64_t TC = tables * comparisons;
+  const unsigned cblocks = static_cast<unsigned>(ceil_div(TC, 256));
+  const int rb = static_cast<int>(row_blocks);
   switch (grad_dtype) {
-    case TROPNN_B200_F32: TB_THR_LAUNCH(float) break;
-    case TROPNN_B200_F16: TB_THR_LAUNCH(__half) break;
-    default: TB_THR_LAUNCH(__nv_bfloat16) break;
+    case TROPNN_B200_F32:
+      threshold_combine_kernel<float><<<cblocks, 256, 0, stream>>>(partial, rb, TC, static_cast<float *>(grad));
+      break;
+    case TROPNN_B200_F16:
+      threshold_combine_kernel<__half><<<cblocks, 256, 0, stream>>>(partial, rb, TC, static_cast<__half *>(grad));
+      break;
+    default:
+      threshold_combine_kernel<__nv_bfloat16><<<cblocks, 256, 0, stream>>>(partial, rb, TC,
+                                                                           static_cast<__nv_bfloat16 *>(grad));
+      break;
   }
-#undef TB_THR_LAUNCH
   return check_launch("pairwise_threshold_grad");
 }
 
@@ -529,6 +608,8 @@ struct PairwiseBackwardLayout {
   int32_t *perm, *seg, *fs, *fe;
   float *gu;
   uint8_t *rs;
+  void *thr;
+  size_t thr_bytes;
 };
 
 static size_t pairwise_backward_layout(void *ws, size_t bytes, int64_t items, int64_t tables, int64_t comparisons,
@@ -541,6 +622,8 @@ static size_t pairwise_backward_layout(void *ws, size_t bytes, int64_t items, in
   L->fe = c.take<int32_t>(size_t(tables) * comparisons * 2);
   L->gu = c.take<float>(size_t(items) * tables * (use_min ? 1 : comparisons));
   L->rs = c.take<uint8_t>(size_t(items) * tables);
+  L->thr_bytes = threshold_grad_workspace(items, tables, comparisons);
+  L->thr = c.take<char>(L->thr_bytes);
   return WorkspaceCarver::align(c.used);
 }
 
@@ -566,8 +649,8 @@ int pairwise_backward_impl(const float *g, int64_t items, int64_t out, float out
     TB_CHECK(pairwise_ste_impl(g, items, out, out_scale, idx, u, anchors, tables, comparisons, in, lut, lut_dtype,
                                use_min, surrogate, L.fs, L.fe, gx, L.gu, L.rs, stream));
     if (gthr != nullptr)
-      TB_CHECK(pairwise_threshold_grad_impl(L.gu, L.rs, items, tables, comparisons, use_min, gthr, gthr_dtype,
-                                            stream));
+      TB_CHECK(pairwise_threshold_grad_impl(L.gu, L.rs, items, tables, comparisons, use_min, gthr, gthr_dtype, L.thr,
+                                            L.thr_bytes, stream));
   }
   return TROPNN_B200_OK;
 }
@@ -615,12 +698,18 @@ int tropnn_b200_pairwise_ste_backward(const float *grad_out, int64_t items, int6
   return tropnn_b200::clear_error();
 }
 
+size_t tropnn_b200_pairwise_threshold_grad_workspace_size(int64_t items, int64_t tables, int64_t comparisons) {
+  if (items < 0 || tables < 1 || comparisons < 1) return 0;
+  return tropnn_b200::threshold_grad_workspace(items, tables, comparisons);
+}
+
 int tropnn_b200_pairwise_threshold_grad(const float *gu, const uint8_t *rstar, int64_t items, int64_t tables,
                                         int64_t comparisons, int use_min_margin_ste, void *grad_thresholds,
-                                        int grad_dtype, void *stream) {
+                                        int grad_dtype, void *workspace, size_t workspace_bytes, void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
   TB_CHECK(tropnn_b200::pairwise_threshold_grad_impl(gu, rstar, items, tables, comparisons, use_min_margin_ste,
-                                                     grad_thresholds, grad_dtype, tropnn_b200::as_stream(stream)));
+                                                     grad_thresholds, grad_dtype, workspace, workspace_bytes,
+                                                     tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 

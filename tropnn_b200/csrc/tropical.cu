@@ -143,11 +143,7 @@ int launch_route(const float *z, int64_t rows, int D, const void *W, const void 
   const size_t smem = sizeof(float) * 32 * RM * (D + 4);
   TB_REQUIRE(smem <= 200 * 1024, TROPNN_B200_ERR_INVALID, "trop_route: code_dim=%d too large for the SIMT path", D);
   auto kernel = vec4 ? trop_route_kernel<PT, IT, RM, true> : trop_route_kernel<PT, IT, RM, false>;
-  if (smem > 48 * 1024) {
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (err != cudaSuccess)
-      return set_error(TROPNN_B200_ERR_LAUNCH, "trop_route: cudaFuncSetAttribute: %s", cudaGetErrorString(err));
-  }
+  TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_route"));
   const int64_t row_blocks = ceil_div(rows, 32 * RM);
   TB_REQUIRE(row_blocks < (int64_t(1) << 31) && ceil_div(H, kRouteWarps) < 65536, TROPNN_B200_ERR_INVALID,
              "trop_route: grid too large");

@@ -232,6 +232,8 @@ class _PairwiseB200Function(torch.autograd.Function):
             )
             if want_thr:
                 grad_thr = torch.empty((tables, comparisons), device=dev, dtype=ctx.thr_dtype)
+                ws_bytes = lib.tropnn_b200_pairwise_threshold_grad_workspace_size(items, tables, comparisons)
+                ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
                 _launch(
                     "pairwise_threshold_grad",
                     lib.tropnn_b200_pairwise_threshold_grad,
@@ -243,6 +245,8 @@ class _PairwiseB200Function(torch.autograd.Function):
                     int(ctx.use_min),
                     grad_thr.data_ptr(),
                     nat.float_code(ctx.thr_dtype),
+                    ws.data_ptr(),
+                    ws_bytes,
                     stream,
                 )
             if want_latent:
