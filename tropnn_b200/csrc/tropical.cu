@@ -163,128 +163,216 @@ int route_by_rows(const float *z, int64_t rows, int D, const void *W, const void
 }
 
 // ---------------------------------------------------------------------------
-// hidden: selected-code gather-sum
+// per-row code kernels: hidden (selected-code gather-sum) and backward rows
 // ---------------------------------------------------------------------------
-// One warp per row, lanes over code_dim. Sum over heads in head order, then
-// hidden = latent + sum * code_scale (the operation order of tropical.py:137).
-constexpr int kHiddenWarps = 4;
+// One CTA of 8 warps per row (and code_dim slice); warp w owns a contiguous range of
+// heads. The slice is split in vector slots of VEC elements (16-byte loads when VEC > 1);
+// lanes form groups of `lph` lanes, each group takes one head per pass (so a warp covers
+// 32/lph heads at once when code_dim is small) and lane l of a group owns slots
+// l + j*lph, j < NJ. Per-lane partial sums are combined in a fixed order (warp, then
+// lane group), so results are deterministic.
+constexpr int kRowWarps = 8;
 
-template <typename PT, typename IT, bool TRAIN>
-__global__ void __launch_bounds__(kHiddenWarps * 32) trop_hidden_kernel(
-    const float *__restrict__ z, int64_t rows, int D, const PT *__restrict__ code, int H, int K,
-    const IT *__restrict__ winner, const IT *__restrict__ runner, const float *__restrict__ margins, float code_scale,
+__device__ __forceinline__ float group_sum(float v, int lph) {
+  for (int off = lph >> 1; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// hidden = latent + code_scale * sum_h chat_h (the operation order of tropical.py:137).
+template <typename PT, typename IT, bool TRAIN, int VEC, int NJ>
+__global__ void __launch_bounds__(kRowWarps * 32) trop_hidden_kernel(
+    const float *__restrict__ z, int D, const PT *__restrict__ code, int H, int K, const IT *__restrict__ winner,
+    const IT *__restrict__ runner, const float *__restrict__ margins, float code_scale, int lph,
     float *__restrict__ hidden) {
+  __shared__ float part[kRowWarps * 32 * NJ * VEC];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t n = int64_t(blockIdx.x) * kHiddenWarps + warp;
-  if (n >= rows) return;
-  const int64_t d0 = int64_t(blockIdx.y) * 32 * 8;
-  float acc[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  const int64_t n = blockIdx.x;
+  const int d_base = blockIdx.y * (32 * NJ * VEC);
+  const int slots = min(32 * NJ, (D - d_base + VEC - 1) / VEC);
+  const int hpw = 32 / lph;
+  const int sub = lane / lph;
+  const int l = lane - sub * lph;
+  const int hw = (H + kRowWarps - 1) / kRowWarps;
+  const int hs = min(H, warp * hw);
+  const int he = min(H, hs + hw);
   const IT *wrow = winner + n * H;
   const IT *rrow = runner + n * H;
   const float *mrow = margins + n * H;
-#pragma unroll 2
-  for (int h = 0; h < H; ++h) {
-    const int w = ld_index(wrow + h);
-    const PT *cw = code + (int64_t(h) * K + w) * D;
+  float acc[NJ][VEC];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j)
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[j][e] = 0.f;
+#pragma unroll 4
+  for (int h = hs + sub; h < he; h += hpw) {
+    const PT *cw = code + (int64_t(h) * K + ld_index(wrow + h)) * D + d_base;
     if (TRAIN) {
-      const int r = ld_index(rrow + h);
-      const PT *cr = code + (int64_t(h) * K + r) * D;
+      const PT *cr = code + (int64_t(h) * K + ld_index(rrow + h)) * D + d_base;
       const float alpha = __fdiv_rn(0.5f, __fadd_rn(1.f, fabsf(__ldg(mrow + h))));
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int64_t d = d0 + lane + 32 * j;
-        if (d < D) {
-          const float a = ldg_f32(cw + d);
-          const float b = ldg_f32(cr + d);
-          acc[j] = __fadd_rn(acc[j], __fadd_rn(a, __fmul_rn(alpha, __fsub_rn(b, a))));
+      for (int j = 0; j < NJ; ++j) {
+        const int s = l + j * lph;
+        if (s < slots) {
+          float a[VEC], b[VEC];
+          VecLoad<PT, VEC>::load(cw + s * VEC, a);
+          VecLoad<PT, VEC>::load(cr + s * VEC, b);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) acc[j][e] = __fadd_rn(acc[j][e], __fadd_rn(a[e], __fmul_rn(alpha, __fsub_rn(b[e], a[e]))));
         }
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int64_t d = d0 + lane + 32 * j;
-        if (d < D) acc[j] = __fadd_rn(acc[j], ldg_f32(cw + d));
+      for (int j = 0; j < NJ; ++j) {
+        const int s = l + j * lph;
+        if (s < slots) {
+          float a[VEC];
+          VecLoad<PT, VEC>::load(cw + s * VEC, a);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) acc[j][e] = __fadd_rn(acc[j][e], a[e]);
+        }
       }
     }
   }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int64_t d = d0 + lane + 32 * j;
-    if (d < D) hidden[n * D + d] = __fadd_rn(__ldg(z + n * D + d), __fmul_rn(acc[j], code_scale));
+  for (int j = 0; j < NJ; ++j)
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) part[((warp * 32 + lane) * NJ + j) * VEC + e] = acc[j][e];
+  __syncthreads();
+  for (int q = threadIdx.x; q < slots * VEC; q += kRowWarps * 32) {
+    const int s = q / VEC;
+    const int e = q - s * VEC;
+    const int j = s / lph;
+    const int ls = s - j * lph;
+    float sum = 0.f;
+    for (int w = 0; w < kRowWarps; ++w)
+      for (int sb = 0; sb < hpw; ++sb) sum = __fadd_rn(sum, part[((w * 32 + sb * lph + ls) * NJ + j) * VEC + e]);
+    const int64_t o = n * D + d_base + q;
+    hidden[o] = __fadd_rn(__ldg(z + o), __fmul_rn(sum, code_scale));
   }
 }
 
-// ---------------------------------------------------------------------------
-// backward rows
-// ---------------------------------------------------------------------------
-// One warp per row, lanes over code_dim. Per head: gm from the warp-reduced
-// <g, c_r - c_w>, then the router term of grad_latent; per-row coefficients of the
-// code / router scatters go to coef_w, coef_r, gm for the segmented sums.
-template <typename PT, typename IT, bool TRAIN>
-__global__ void __launch_bounds__(kHiddenWarps * 32) trop_backward_rows_kernel(
-    const float *__restrict__ g, int64_t rows, int D, const PT *__restrict__ W, const PT *__restrict__ code, int H,
-    int K, const IT *__restrict__ winner, const IT *__restrict__ runner, const float *__restrict__ margins,
-    float code_scale, float *__restrict__ grad_z, float *__restrict__ coef_w, float *__restrict__ coef_r,
+// Per-row part of the min-face backward: gm from the group-reduced <g, c_r - c_w>, the
+// router term of grad_latent, and the per-row coefficients of the code / router
+// scatters. Needs the whole code_dim in one CTA (slots <= 32 * NJ).
+template <typename PT, typename IT, bool TRAIN, int VEC, int NJ>
+__global__ void __launch_bounds__(kRowWarps * 32) trop_backward_rows_kernel(
+    const float *__restrict__ g, int D, const PT *__restrict__ W, const PT *__restrict__ code, int H, int K,
+    const IT *__restrict__ winner, const IT *__restrict__ runner, const float *__restrict__ margins, float code_scale,
+    int lph, float *__restrict__ grad_z, float *__restrict__ coef_w, float *__restrict__ coef_r,
     float *__restrict__ gm_out) {
+  __shared__ float part[kRowWarps * 32 * NJ * VEC];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t n = int64_t(blockIdx.x) * kHiddenWarps + warp;
-  if (n >= rows) return;
-  const int nd = (D + 31) / 32;  // <= 8 (code_dim <= 256 on this path)
-  float gv[8], acc[8];
+  const int64_t n = blockIdx.x;
+  const int slots = (D + VEC - 1) / VEC;
+  const int hpw = 32 / lph;
+  const int sub = lane / lph;
+  const int l = lane - sub * lph;
+  const int hw = (H + kRowWarps - 1) / kRowWarps;
+  const int hs = min(H, warp * hw);
+  const int he = min(H, hs + hw);
+  const float *grow = g + n * D;
+  float gv[NJ][VEC], acc[NJ][VEC];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int d = lane + 32 * j;
-    gv[j] = (j < nd && d < D) ? __ldg(g + n * D + d) : 0.f;
-    acc[j] = 0.f;
+  for (int j = 0; j < NJ; ++j) {
+    const int s = l + j * lph;
+    if (s < slots) {
+      VecLoad<float, VEC>::load(grow + s * VEC, gv[j]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) gv[j][e] = 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[j][e] = 0.f;
   }
-  for (int h = 0; h < H; ++h) {
+  // Warp-uniform trip count: every lane takes part in the group shuffles.
+  for (int h0 = hs; h0 < he; h0 += hpw) {
+    const int h = h0 + sub;
+    const bool valid = h < he;
     const int64_t o = n * H + h;
     if (!TRAIN) {
-      if (lane == 0) coef_w[o] = code_scale;
+      if (valid && l == 0) coef_w[o] = code_scale;
       continue;
     }
-    const int w = ld_index(winner + o);
-    const int r = ld_index(runner + o);
-    const float m = __ldg(margins + o);
-    const PT *cw = code + (int64_t(h) * K + w) * D;
-    const PT *cr = code + (int64_t(h) * K + r) * D;
+    int w = 0, r = 0;
+    float m = 0.f;
+    if (valid) {
+      w = ld_index(winner + o);
+      r = ld_index(runner + o);
+      m = __ldg(margins + o);
+    }
+    const int64_t hk = int64_t(valid ? h : hs) * K;
+    const PT *cw = code + (hk + w) * D;
+    const PT *cr = code + (hk + r) * D;
     float dot = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int d = lane + 32 * j;
-      if (j < nd && d < D)
-        dot = fmaf(__fmul_rn(gv[j], code_scale), __fsub_rn(ldg_f32(cr + d), ldg_f32(cw + d)), dot);
+    for (int j = 0; j < NJ; ++j) {
+      const int s = l + j * lph;
+      if (valid && s < slots) {
+        float a[VEC], b[VEC];
+        VecLoad<PT, VEC>::load(cw + s * VEC, a);
+        VecLoad<PT, VEC>::load(cr + s * VEC, b);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) dot = fmaf(__fmul_rn(gv[j][e], code_scale), __fsub_rn(b[e], a[e]), dot);
+      }
     }
-    dot = warp_sum(dot);
-    const float am = fabsf(m);
-    const float den = __fadd_rn(1.f, am);
+    dot = group_sum(dot, lph);
+    if (!valid) continue;
+    const float den = __fadd_rn(1.f, fabsf(m));
     const float alpha = __fdiv_rn(0.5f, den);
     const float sgn = (m > 0.f) ? 1.f : ((m < 0.f) ? -1.f : 0.f);
     // d/dm [0.5 / (1 + |m|)] = -0.5 sign(m) / (1 + |m|)^2
-    const float dalpha = __fdiv_rn(__fmul_rn(-0.5f, sgn), __fmul_rn(den, den));
-    const float gm = __fmul_rn(dot, dalpha);
-    const PT *ww = W + (int64_t(h) * K + w) * D;
-    const PT *wr = W + (int64_t(h) * K + r) * D;
+    const float gm = __fmul_rn(dot, __fdiv_rn(__fmul_rn(-0.5f, sgn), __fmul_rn(den, den)));
+    const PT *ww = W + (hk + w) * D;
+    const PT *wr = W + (hk + r) * D;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int d = lane + 32 * j;
-      if (j < nd && d < D) acc[j] = fmaf(gm, __fsub_rn(ldg_f32(ww + d), ldg_f32(wr + d)), acc[j]);
+    for (int j = 0; j < NJ; ++j) {
+      const int s = l + j * lph;
+      if (s < slots) {
+        float a[VEC], b[VEC];
+        VecLoad<PT, VEC>::load(ww + s * VEC, a);
+        VecLoad<PT, VEC>::load(wr + s * VEC, b);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc[j][e] = fmaf(gm, __fsub_rn(a[e], b[e]), acc[j][e]);
+      }
     }
-    if (lane == 0) {
+    if (l == 0) {
       coef_w[o] = __fmul_rn(code_scale, __fsub_rn(1.f, alpha));
       coef_r[o] = __fmul_rn(code_scale, alpha);
       gm_out[o] = gm;
     }
   }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int d = lane + 32 * j;
-    if (j < nd && d < D) grad_z[n * D + d] = __fadd_rn(gv[j], acc[j]);
+  for (int j = 0; j < NJ; ++j)
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) part[((warp * 32 + lane) * NJ + j) * VEC + e] = acc[j][e];
+  __syncthreads();
+  for (int q = threadIdx.x; q < D; q += kRowWarps * 32) {
+    const int s = q / VEC;
+    const int e = q - s * VEC;
+    const int j = s / lph;
+    const int ls = s - j * lph;
+    float sum = 0.f;
+    for (int w = 0; w < kRowWarps; ++w)
+      for (int sb = 0; sb < hpw; ++sb) sum = __fadd_rn(sum, part[((w * 32 + sb * lph + ls) * NJ + j) * VEC + e]);
+    grad_z[n * D + q] = __fadd_rn(__ldg(grow + q), sum);
   }
+}
+
+// Lanes per head: all 32 once a slice has >= 32 slots, else the next power of two.
+inline int lanes_per_head(int slots) {
+  int lph = 1;
+  while (lph < 32 && lph < slots) lph <<= 1;
+  return lph;
+}
+
+// Vector width of the per-row kernels: 16-byte loads when code_dim allows it.
+template <typename PT>
+inline bool row_vec_ok(int D, const void *p0, const void *p1, const void *p2) {
+  constexpr int V = 16 / sizeof(PT);
+  auto al = [](const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  return D % V == 0 && al(p0) && al(p1) && al(p2);
 }
 
 int validate_trop(int64_t items, int64_t D, int64_t H, int64_t K) {
@@ -334,6 +422,25 @@ int trop_route_impl(const float *z, int64_t items, int64_t D, const void *W, con
   return status;
 }
 
+template <typename PT, typename IT, int VEC, int NJ>
+int launch_hidden(const float *z, int64_t items, int D, const void *code, int H, int K, const void *win,
+                  const void *run, const float *m, float code_scale, bool training, float *hidden,
+                  cudaStream_t stream) {
+  const int slice = 32 * NJ * VEC;
+  const int lph = lanes_per_head(std::min(32 * NJ, (D + VEC - 1) / VEC));
+  TB_REQUIRE(ceil_div(D, slice) < 65536, TROPNN_B200_ERR_INVALID, "trop_hidden: code_dim=%d too large", D);
+  dim3 grid(static_cast<unsigned>(items), static_cast<unsigned>(ceil_div(D, slice)));
+  if (training)
+    trop_hidden_kernel<PT, IT, true, VEC, NJ><<<grid, kRowWarps * 32, 0, stream>>>(
+        z, D, static_cast<const PT *>(code), H, K, static_cast<const IT *>(win), static_cast<const IT *>(run), m,
+        code_scale, lph, hidden);
+  else
+    trop_hidden_kernel<PT, IT, false, VEC, NJ><<<grid, kRowWarps * 32, 0, stream>>>(
+        z, D, static_cast<const PT *>(code), H, K, static_cast<const IT *>(win), static_cast<const IT *>(win), m,
+        code_scale, lph, hidden);
+  return check_launch("trop_hidden");
+}
+
 int trop_hidden_impl(const float *z, int64_t items, int64_t D, const void *code, int pt, int64_t H, int64_t K,
                      const void *win, const void *run, int it, const float *m, float code_scale, int training,
                      float *hidden, cudaStream_t stream) {
@@ -343,20 +450,38 @@ int trop_hidden_impl(const float *z, int64_t items, int64_t D, const void *code,
   if (items == 0) return TROPNN_B200_OK;
   TB_REQUIRE(z && code && win && hidden && (!training || (run && m)), TROPNN_B200_ERR_INVALID,
              "trop_hidden: null pointer");
-  dim3 grid(static_cast<unsigned>(ceil_div(items, kHiddenWarps)), static_cast<unsigned>(ceil_div(D, 256)));
-  TB_REQUIRE(ceil_div(items, kHiddenWarps) < (int64_t(1) << 31), TROPNN_B200_ERR_INVALID, "trop_hidden: too many rows");
   const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
+  const bool train = training != 0;
+  int status = TROPNN_B200_OK;
   TB_DISPATCH_PT(pt, TB_DISPATCH_IT(it, {
-    if (training)
-      trop_hidden_kernel<PT, IT, true><<<grid, kHiddenWarps * 32, 0, stream>>>(
-          z, items, Di, static_cast<const PT *>(code), Hi, Ki, static_cast<const IT *>(win),
-          static_cast<const IT *>(run), m, code_scale, hidden);
+    if (row_vec_ok<PT>(Di, code, code, code))
+      status = launch_hidden<PT, IT, 16 / sizeof(PT), 2>(z, items, Di, code, Hi, Ki, win, run, m, code_scale, train,
+                                                          hidden, stream);
     else
-      trop_hidden_kernel<PT, IT, false><<<grid, kHiddenWarps * 32, 0, stream>>>(
-          z, items, Di, static_cast<const PT *>(code), Hi, Ki, static_cast<const IT *>(win),
-          static_cast<const IT *>(win), m, code_scale, hidden);
+      status = launch_hidden<PT, IT, 1, 8>(z, items, Di, code, Hi, Ki, win, run, m, code_scale, train, hidden,
+                                           stream);
   }))
-  return check_launch("trop_hidden");
+  return status;
+}
+
+template <typename PT, typename IT, int VEC, int NJ>
+int launch_backward_rows(const float *g, int64_t items, int D, const void *W, const void *code, int H, int K,
+                         const void *win, const void *run, const float *m, float code_scale, bool training, float *gz,
+                         float *cw, float *cr, float *gm, cudaStream_t stream) {
+  const int slots = (D + VEC - 1) / VEC;
+  TB_REQUIRE(slots <= 32 * NJ, TROPNN_B200_ERR_INVALID,
+             "trop_backward_rows: code_dim=%d exceeds the per-row limit (%d elements)", D, 32 * NJ * VEC);
+  const int lph = lanes_per_head(slots);
+  const unsigned blocks = static_cast<unsigned>(items);
+  if (training)
+    trop_backward_rows_kernel<PT, IT, true, VEC, NJ><<<blocks, kRowWarps * 32, 0, stream>>>(
+        g, D, static_cast<const PT *>(W), static_cast<const PT *>(code), H, K, static_cast<const IT *>(win),
+        static_cast<const IT *>(run), m, code_scale, lph, gz, cw, cr, gm);
+  else
+    trop_backward_rows_kernel<PT, IT, false, VEC, NJ><<<blocks, kRowWarps * 32, 0, stream>>>(
+        g, D, static_cast<const PT *>(W), static_cast<const PT *>(code), H, K, static_cast<const IT *>(win),
+        static_cast<const IT *>(win), m, code_scale, lph, gz, cw, cr, gm);
+  return check_launch("trop_backward_rows");
 }
 
 int trop_backward_rows_impl(const float *g, int64_t items, int64_t D, const void *W, const void *code, int pt,
@@ -364,26 +489,25 @@ int trop_backward_rows_impl(const float *g, int64_t items, int64_t D, const void
                             float code_scale, int training, float *gz, float *cw, float *cr, float *gm,
                             cudaStream_t stream) {
   TB_CHECK(validate_trop(items, D, H, K));
-  TB_REQUIRE(D <= 256, TROPNN_B200_ERR_INVALID, "trop_backward_rows: code_dim=%lld > 256 unsupported", (long long)D);
   TB_REQUIRE(is_float_dtype(pt), TROPNN_B200_ERR_DTYPE, "trop_backward_rows: param dtype %s unsupported",
              dtype_name(pt));
   TB_CHECK(check_index_dtype(K, it));
   if (items == 0) return TROPNN_B200_OK;
   TB_REQUIRE(g && code && win && gz && cw && (!training || (W && run && m && cr && gm)), TROPNN_B200_ERR_INVALID,
              "trop_backward_rows: null pointer");
-  const unsigned blocks = static_cast<unsigned>(ceil_div(items, kHiddenWarps));
   const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
+  const bool train = training != 0;
+  int status = TROPNN_B200_OK;
   TB_DISPATCH_PT(pt, TB_DISPATCH_IT(it, {
-    if (training)
-      trop_backward_rows_kernel<PT, IT, true><<<blocks, kHiddenWarps * 32, 0, stream>>>(
-          g, items, Di, static_cast<const PT *>(W), static_cast<const PT *>(code), Hi, Ki,
-          static_cast<const IT *>(win), static_cast<const IT *>(run), m, code_scale, gz, cw, cr, gm);
+    const bool vec = row_vec_ok<PT>(Di, code, train ? W : code, g) && (reinterpret_cast<uintptr_t>(g) % 16 == 0);
+    if (vec)
+      status = launch_backward_rows<PT, IT, 16 / sizeof(PT), 2>(g, items, Di, W, code, Hi, Ki, win, run, m,
+                                                                 code_scale, train, gz, cw, cr, gm, stream);
     else
-      trop_backward_rows_kernel<PT, IT, false><<<blocks, kHiddenWarps * 32, 0, stream>>>(
-          g, items, Di, static_cast<const PT *>(W), static_cast<const PT *>(code), Hi, Ki,
-          static_cast<const IT *>(win), static_cast<const IT *>(win), m, code_scale, gz, cw, cr, gm);
+      status = launch_backward_rows<PT, IT, 1, 8>(g, items, Di, W, code, Hi, Ki, win, run, m, code_scale, train, gz,
+                                                  cw, cr, gm, stream);
   }))
-  return check_launch("trop_backward_rows");
+  return status;
 }
 
 struct TropBackwardLayout {

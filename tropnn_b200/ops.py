@@ -413,33 +413,39 @@ class _TropRouteB200Function(torch.autograd.Function):
         pdt = nat.float_code(weight.dtype)
         icode = nat.index_code(winner.dtype)
 
-        grad_z = torch.empty((items, code_dim), device=dev, dtype=torch.float32)
-        coef_w = torch.empty((items, heads), device=dev, dtype=torch.float32)
-        coef_r = torch.empty((items, heads), device=dev, dtype=torch.float32) if training else None
-        gm = torch.empty((items, heads), device=dev, dtype=torch.float32) if training else None
-        _launch(
-            "trop_backward_rows",
-            lib.tropnn_b200_trop_backward_rows,
-            g.data_ptr(),
-            items,
-            code_dim,
-            weight.data_ptr(),
-            code.data_ptr(),
-            pdt,
-            heads,
-            cells,
-            winner.data_ptr(),
-            runner.data_ptr(),
-            icode,
-            margins.data_ptr(),
-            ctx.code_scale,
-            int(training),
-            grad_z.data_ptr(),
-            coef_w.data_ptr(),
-            nat.ptr(coef_r),
-            nat.ptr(gm),
-            stream,
-        )
+        coef_w = coef_r = gm = None
+        if training and items > 0:
+            grad_z = torch.empty((items, code_dim), device=dev, dtype=torch.float32)
+            coef_w = torch.empty((items, heads), device=dev, dtype=torch.float32)
+            coef_r = torch.empty((items, heads), device=dev, dtype=torch.float32)
+            gm = torch.empty((items, heads), device=dev, dtype=torch.float32)
+            _launch(
+                "trop_backward_rows",
+                lib.tropnn_b200_trop_backward_rows,
+                g.data_ptr(),
+                items,
+                code_dim,
+                weight.data_ptr(),
+                code.data_ptr(),
+                pdt,
+                heads,
+                cells,
+                winner.data_ptr(),
+                runner.data_ptr(),
+                icode,
+                margins.data_ptr(),
+                ctx.code_scale,
+                1,
+                grad_z.data_ptr(),
+                coef_w.data_ptr(),
+                coef_r.data_ptr(),
+                gm.data_ptr(),
+                stream,
+            )
+        else:
+            # Eval: the output does not depend on the routes' margins, so grad_latent is the
+            # incoming gradient and every winner code gets code_scale * g (coefficient constant).
+            grad_z = g
         want_code = ctx.needs_input_grad[3]
         want_router = training and (ctx.needs_input_grad[1] or ctx.needs_input_grad[2])
         grad_w = grad_b = grad_c = None
@@ -489,8 +495,8 @@ class _TropRouteB200Function(torch.autograd.Function):
                     cells,
                     perm_w.data_ptr(),
                     seg_w.data_ptr(),
-                    coef_w.data_ptr(),
-                    1.0,
+                    nat.ptr(coef_w),
+                    1.0 if training else ctx.code_scale,
                     nat.ptr(perm_r),
                     nat.ptr(seg_r),
                     nat.ptr(coef_r),
