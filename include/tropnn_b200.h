@@ -182,6 +182,33 @@ TROPNN_B200_API int tropnn_b200_pairwise_backward(const float *grad_out, int64_t
                                   float *grad_latent, void *grad_thresholds, int grad_thresholds_dtype,
                                   void *grad_lut, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Size of the fixed scratch buffer behind tropnn_b200_pairwise_backward_noalloc. */
+#define TROPNN_B200_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+
+/*
+ * tropnn_b200_pairwise_backward without a workspace argument, for callers that cannot
+ * allocate device memory (a host with a fixed, fully pre-partitioned memory budget, a
+ * foreign-language caller without a CUDA allocator, a loop that must not pay
+ * cudaMalloc's implicit synchronisation). No counterpart in the reference: its torch and
+ * TileLang paths always allocate their temporaries.
+ *
+ * Scratch comes from one TROPNN_B200_NOALLOC_SCRATCH_BYTES (8 MiB) device buffer compiled
+ * into the library; problems whose tropnn_b200_pairwise_backward_workspace_size() is
+ * larger are rejected with TROPNN_B200_ERR_INVALID. The buffer is shared by every call on
+ * a GPU: calls that can overlap on that GPU (different streams, threads or processes
+ * sharing the context) race on it and must be serialised by the caller. The first call
+ * on each device looks up the buffer's device address (cudaGetSymbolAddress) and caches
+ * it; make that first call before any stream capture. Each GPU on which it has run keeps
+ * the 8 MiB until the process exits. Arguments and results as tropnn_b200_pairwise_backward.
+ */
+TROPNN_B200_API int tropnn_b200_pairwise_backward_noalloc(const float *grad_out, int64_t items, int64_t out_features,
+                                          float output_scale, const int64_t *indices, const float *margins,
+                                          const int64_t *anchors, int64_t tables, int64_t comparisons,
+                                          int64_t in_features, const void *lut, int lut_dtype,
+                                          int use_min_margin_ste, int surrogate,
+                                          float *grad_latent, void *grad_thresholds, int grad_thresholds_dtype,
+                                          void *grad_lut, void *stream);
+
 /* ------------------------------------------------------------ TropLinear */
 
 /*

@@ -68,6 +68,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i32,
         [_p, _i64, _i64, _f32, _p, _p, _p, _i64, _i64, _i64, _p, _i32, _i32, _i32, _p, _p, _i32, _p, _p, _sz, _p],
     ),
+    "tropnn_b200_pairwise_backward_noalloc": (
+        _i32,
+        [_p, _i64, _i64, _f32, _p, _p, _p, _i64, _i64, _i64, _p, _i32, _i32, _i32, _p, _p, _i32, _p, _p],
+    ),
     "tropnn_b200_trop_route": (_i32, [_p, _i64, _i64, _p, _p, _i32, _i64, _i64, _p, _p, _p, _i32, _p, _p]),
     "tropnn_b200_trop_hidden": (_i32, [_p, _i64, _i64, _p, _i32, _i64, _i64, _p, _p, _i32, _p, _f32, _i32, _p, _p]),
     "tropnn_b200_trop_backward_rows": (
