@@ -148,6 +148,29 @@ def algorithmic_bytes(w: Workload, kernel: str, rows: int) -> float | None:
     return float(per_row * rows + fixed)
 
 
+def tensor_core_route(w: Workload, rows: int) -> bool:
+    """Whether trop_route runs on the tcgen05 tensor cores for this workload (the C ABI's rule)."""
+    if w.kind != "trop" or w.dtype == "float32":
+        return False
+    kw = w.layer_kwargs
+    H, K, D = kw["heads"], kw["cells"], kw["code_dim"]
+    return K in (2, 4, 8, 16, 32, 64) and D % 8 == 0 and (D + 63) // 64 <= 6 and rows >= 128 and H * K >= 128
+
+
+def kernel_roofline(w: Workload, kernel: str, rows: int, peaks: dict) -> tuple[str, float, str, float] | None:
+    """(bound, algorithmic work per launch, unit, peak) of one kernel: FLOPs against the
+    measured bf16 tensor peak for the tensor-core score GEMM, bytes against the measured HBM
+    copy bandwidth for everything else."""
+    if kernel == "trop_route" and tensor_core_route(w, rows):
+        kw = w.layer_kwargs
+        flops = 2.0 * kw["heads"] * kw["cells"] * kw["code_dim"] * rows
+        return "tensor", flops, "TFLOP/s", peaks["bf16_tflops"]
+    work = algorithmic_bytes(w, kernel, rows)
+    if work is None:
+        return None
+    return "hbm", work, "GB/s", peaks["hbm_gbs"]
+
+
 # ---------------------------------------------------------------------------
 # helpers
 # ---------------------------------------------------------------------------
@@ -411,28 +434,31 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
     e2e_value = rows_total * args.steps / (e2e_ms / 1e3)
 
     peaks, peaks_kind = _peaks()
-    roofline = None
-    candidates = {k: v for k, v in kernels.items() if algorithmic_bytes(w, k, w.rows_per_gpu) is not None}
-    if candidates:
-        top = max(candidates, key=lambda k: candidates[k]["total_ms"])
-        per_launch = algorithmic_bytes(w, top, w.rows_per_gpu)
-        mean_s = candidates[top]["mean_ms"] / 1e3
-        achieved = per_launch / mean_s / 1e9
-        traffic = None
-        if TRAFFIC_PATH.exists():
-            traffic = json.loads(TRAFFIC_PATH.read_text()).get(w.name, {}).get(top)
-        roofline = {
-            "kernel": top,
-            "bound": "hbm",
+    traffic_table = json.loads(TRAFFIC_PATH.read_text()).get(w.name, {}) if TRAFFIC_PATH.exists() else {}
+    per_kernel_roofline = {}
+    for name, stats in kernels.items():
+        rl = kernel_roofline(w, name, w.rows_per_gpu, peaks)
+        if rl is None:
+            continue
+        bound, work, unit, peak = rl
+        mean_s = stats["mean_ms"] / 1e3
+        achieved = work / mean_s / (1e12 if bound == "tensor" else 1e9)
+        per_kernel_roofline[name] = {
+            "kernel": name,
+            "bound": bound,
             "achieved": round(achieved, 1),
-            "peak": peaks["hbm_gbs"],
-            "peak_source": f"{peaks_kind} hbm_gbs",
-            "unit": "GB/s",
-            "frac": round(achieved / peaks["hbm_gbs"], 3),
-            "traffic": traffic,
-            "algorithmic_bytes_per_launch": per_launch,
+            "peak": peak,
+            "peak_source": f"{peaks_kind} {'bf16_tflops' if bound == 'tensor' else 'hbm_gbs'}",
+            "unit": unit,
+            "frac": round(achieved / peak, 3),
+            "traffic": traffic_table.get(name),
+            ("algorithmic_flops_per_launch" if bound == "tensor" else "algorithmic_bytes_per_launch"): work,
             "mean_launch_us": round(mean_s * 1e6, 2),
         }
+    roofline = None
+    if per_kernel_roofline:
+        top = max(per_kernel_roofline, key=lambda k: kernels[k]["total_ms"])
+        roofline = per_kernel_roofline[top]
     step_kernel_ms = sum(v["total_ms"] for v in kernels.values()) / args.steps
 
     return {
@@ -471,6 +497,7 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
                     for k, v in kernels.items()},
         "kernel_ms_per_step": round(step_kernel_ms, 4),
         "roofline": roofline,
+        "kernel_rooflines": {k: {kk: v[kk] for kk in ("bound", "achieved", "unit", "frac")} for k, v in per_kernel_roofline.items()},
         "clocks": sampler.summary(),
     }
 

@@ -215,12 +215,15 @@ TROPNN_B200_API int tropnn_b200_pairwise_backward_noalloc(const float *grad_out,
  * Route scores, top-2 and margins (backend.py:45-46, routing.py:7-10):
  *   s[n,h,k] = <latent[n,:], router_weight[h,k,:]> + router_bias[h,k]
  *   winner/runner = top-2 cells (lowest index on exact ties), margin = s_w - s_r.
- * latent f32 [items, code_dim]; router_weight [heads, cells, code_dim] and router_bias
- * [heads, cells] in param_dtype. winner_i64 (int64 [items, heads], may be NULL),
- * winner/runner in index_dtype (U8/I16/I64, the packing of routing.py:18-31),
- * margins f32 [items, heads].
+ * latent [items, code_dim] in latent_dtype: F32 (fp32 FMA path, parameters upcast) or
+ * the parameter dtype. With F16/BF16 latent and parameters, cells in {2,4,8,16,32,64},
+ * code_dim % 8 == 0 and <= 384, U8 routes and >= 128 rows and score columns, the scores
+ * run on the tensor cores (tcgen05, TMEM accumulators, TMA) and only the routes leave
+ * the chip. router_weight [heads, cells, code_dim] and router_bias [heads, cells] in
+ * param_dtype. winner_i64 (int64 [items, heads], may be NULL), winner/runner in
+ * index_dtype (U8/I16/I64, the packing of routing.py:18-31), margins f32 [items, heads].
  */
-TROPNN_B200_API int tropnn_b200_trop_route(const float *latent, int64_t items, int64_t code_dim,
+TROPNN_B200_API int tropnn_b200_trop_route(const void *latent, int latent_dtype, int64_t items, int64_t code_dim,
                            const void *router_weight, const void *router_bias, int param_dtype,
                            int64_t heads, int64_t cells,
                            int64_t *winner_i64, void *winner, void *runner, int index_dtype,
@@ -229,13 +232,21 @@ TROPNN_B200_API int tropnn_b200_trop_route(const float *latent, int64_t items, i
 /*
  * hidden[n,:] = latent[n,:] + code_scale * sum_h chat[n,h,:] with chat = code[h,w] (eval)
  * or code[h,w] + U(m) (code[h,r] - code[h,w]), U(m) = 0.5/(1+|m|) (training)
- * (layers/tropical.py:131-138, routing.py:13-15). code in param_dtype.
+ * (layers/tropical.py:131-138, routing.py:13-15). code in param_dtype; latent in
+ * latent_dtype (F32 or the parameter dtype); hidden f32 [items, code_dim].
  */
-TROPNN_B200_API int tropnn_b200_trop_hidden(const float *latent, int64_t items, int64_t code_dim,
+TROPNN_B200_API int tropnn_b200_trop_hidden(const void *latent, int latent_dtype, int64_t items, int64_t code_dim,
                             const void *code, int param_dtype, int64_t heads, int64_t cells,
                             const void *winner, const void *runner, int index_dtype,
                             const float *margins, float code_scale, int training,
                             float *hidden, void *stream);
+
+/*
+ * Reads and clears the library's device error word: 1 after a tensor-core kernel gave up
+ * a bounded wait (its CTA then released its resources and exited). Synchronises with the
+ * device; call it off the hot path.
+ */
+TROPNN_B200_API int tropnn_b200_device_error(int *value);
 
 /*
  * Per-row part of the min-face backward (layers/tropical_exact.py:204-237):

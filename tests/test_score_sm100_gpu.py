@@ -1,0 +1,97 @@
+"""The tensor-core (tcgen05) route scores against the fp32 SIMT route kernel.
+
+With half-precision latent and parameters, tropnn_b200_trop_route runs the scores as a
+tcgen05 GEMM with the top-2 in its epilogue. The same call with the latent upcast to f32
+takes the SIMT fp32-FMA kernel. Both see exactly the same values (the upcast is exact and
+every f16/bf16 product is exact in f32), so routes must agree wherever the top-2 margin
+exceeds 1e-4 relative, and margins within 1e-5 relative (f32 summation order only).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.golden_cases import rel_err, route_gate
+from tropnn_b200 import _native as nat
+
+pytestmark = pytest.mark.gpu
+
+
+def _route(z: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> tuple[np.ndarray, ...]:
+    lib = nat.load()
+    items, code_dim = z.shape
+    heads, cells, _ = weight.shape
+    dev = z.device
+    w64 = torch.empty(items, heads, dtype=torch.int64, device=dev)
+    win = torch.empty(items, heads, dtype=torch.uint8, device=dev)
+    run = torch.empty(items, heads, dtype=torch.uint8, device=dev)
+    m = torch.empty(items, heads, dtype=torch.float32, device=dev)
+    status = lib.tropnn_b200_trop_route(
+        z.data_ptr(), nat.float_code(z.dtype), items, code_dim, weight.data_ptr(), bias.data_ptr(),
+        nat.float_code(weight.dtype), heads, cells, w64.data_ptr(), win.data_ptr(), run.data_ptr(), nat.U8,
+        m.data_ptr(), torch.cuda.current_stream().cuda_stream,
+    )
+    nat.check(status, "trop_route")
+    torch.cuda.synchronize()
+    return w64.cpu().numpy(), win.cpu().numpy(), run.cpu().numpy(), m.cpu().numpy()
+
+
+def _case(items: int, heads: int, cells: int, code_dim: int, dtype: torch.dtype, seed: int = 0):
+    gen = torch.Generator().manual_seed(seed)
+    z = (torch.randn(items, code_dim, generator=gen)).to(dtype)
+    weight = (torch.randn(heads, cells, code_dim, generator=gen) / code_dim**0.5).to(dtype)
+    bias = (0.1 * torch.randn(heads, cells, generator=gen)).to(dtype)
+    return z.cuda(), weight.cuda(), bias.cuda()
+
+
+def _check(items: int, heads: int, cells: int, code_dim: int, dtype: torch.dtype) -> None:
+    z, weight, bias = _case(items, heads, cells, code_dim, dtype)
+    tc = _route(z, weight, bias)  # half latent: tensor-core path
+    simt = _route(z.float(), weight, bias)  # f32 latent: SIMT fp32 path
+    scores = oracle.trop_scores(z.float().cpu().numpy(), weight.float().cpu().numpy(), bias.float().cpu().numpy())
+    win_gate, run_gate = route_gate(scores)
+    assert win_gate.mean() > 0.99
+    assert np.array_equal(tc[0], tc[1].astype(np.int64))
+    assert np.array_equal(tc[1][win_gate], simt[1][win_gate])
+    assert np.array_equal(tc[2][run_gate], simt[2][run_gate])
+    assert rel_err(tc[3], simt[3]) <= 1e-5
+    ref_w, ref_r, ref_m = oracle.top2_indices(scores)
+    assert np.array_equal(tc[1][win_gate].astype(np.int64), ref_w[win_gate])
+    assert np.array_equal(tc[2][run_gate].astype(np.int64), ref_r[run_gate])
+    assert rel_err(tc[3], ref_m) <= 1e-5
+
+
+@pytest.mark.parametrize("cells", [2, 4, 8, 16, 32, 64])
+def test_cells(cells: int) -> None:
+    _check(items=256, heads=max(4, 1024 // cells), cells=cells, code_dim=64, dtype=torch.float16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_config5_layer_shape(dtype: torch.dtype) -> None:
+    """Config 5's router: H1024, K16, D256 (16384 score columns), 640 rows."""
+    _check(items=640, heads=1024, cells=16, code_dim=256, dtype=dtype)
+
+
+@pytest.mark.parametrize(
+    ("items", "heads", "cells", "code_dim"),
+    [
+        (300, 12, 16, 64),  # ragged rows (300 = 2*128 + 44) and a half-filled last score tile
+        (129, 9, 16, 40),  # code_dim not a multiple of 64 (zero-filled k block), 9 heads
+        (1000, 200, 8, 128),  # many tiles, several column splits
+        (128, 8, 16, 384),  # largest code_dim of the kernel (6 k blocks)
+    ],
+)
+def test_ragged_shapes(items: int, heads: int, cells: int, code_dim: int) -> None:
+    _check(items, heads, cells, code_dim, torch.float16)
+
+
+def test_no_device_error_after_tensor_core_runs() -> None:
+    import ctypes
+
+    _check(items=512, heads=64, cells=16, code_dim=64, dtype=torch.float16)
+    flag = ctypes.c_int(-1)
+    nat.check(nat.load().tropnn_b200_device_error(ctypes.byref(flag)), "device_error")
+    assert flag.value == 0

@@ -16,7 +16,13 @@ from __future__ import annotations
 from typing import Any
 
 from .layers import PairwiseLinear, RoutedLinearBase, TropLinear, pairwise_forward_b200, trop_forward_b200
-from .ops import packed_route_index_dtype, pairwise_anchor_index, pairwise_b200, trop_route_hidden_b200
+from .ops import (
+    packed_route_index_dtype,
+    pairwise_anchor_index,
+    pairwise_b200,
+    trop_route_hidden_b200,
+    trop_route_hidden_packed,
+)
 
 __all__ = [
     "PairwiseLinear",
@@ -27,6 +33,7 @@ __all__ = [
     "pairwise_b200",
     "register",
     "trop_route_hidden_b200",
+    "trop_route_hidden_packed",
 ]
 
 

@@ -1,0 +1,561 @@
+// TropLinear route scores on the sm_100a tensor cores: tcgen05.mma (kind::f16, f32
+// accumulation in TMEM) fed by TMA, with the per-head top-2 fused into the epilogue, so
+// the [rows, heads*cells] score matrix never reaches HBM.
+//
+// Reference behaviour (paths inside the tropnn package): scores = einsum(z, W) + b
+// (backend.py:45-46), top-2 and margin (routing.py:7-10), packed route indices
+// (routing.py:18-31). This is the path for half-precision parameters, where z and W are
+// exactly representable in the MMA's f16/bf16 operands (z is rounded to the parameter
+// dtype by the projection, tropical.py:99) and each product is exact in f32.
+//
+// CTA = 10 warps, one 128-row block of z, a contiguous range of 128-column score tiles
+// (128/cells heads each):
+//   warp 0      TMA producer: the z block once (resident, K-major, 128B swizzle), then
+//               the router-weight tile of every (score tile, 64-wide k block) through an
+//               8-stage ring.
+//   warp 1      allocates 256 TMEM columns (two 128-column f32 accumulators); lane 0
+//               issues the MMAs (M=128, N=128, K=16 each) and commits them to mbarriers.
+//   warps 2-9   epilogue: each thread owns one accumulator row (TMEM lane) and one half
+//               of the tile's columns; it reads 64 scores with tcgen05.ld, adds the bias,
+//               takes the top-2 of every head and writes winner/runner (u8), the margin
+//               (f32) and optionally the int64 winner.
+// Every mbarrier wait gives up after ~1 s (clock64-independent %globaltimer), sets the
+// library's device error word, lets the other roles exit, drains the copies and MMAs it
+// issued (bounded again) and frees TMEM, so a protocol error cannot hang the GPU.
+// No TMA multicast and no peer memory: safe in multi-GPU processes.
+#include <cuda.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace tropnn_b200 {
+
+namespace {
+
+constexpr int kBM = 128;              // rows per CTA (MMA M, TMEM lanes)
+constexpr int kBN = 128;              // score columns per tile (MMA N)
+constexpr int kBK = 64;               // k-block width: 64 f16 = one 128-byte swizzle row
+constexpr int kStages = 8;            // router-weight ring depth
+constexpr int kTileBytesA = kBM * 128;  // one k block of the z tile
+constexpr int kTileBytesB = kBN * 128;  // one k block of a weight tile
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr int kTmemCols = 2 * kBN;
+constexpr int kMaxKBlocks = 8;         // code_dim <= 512
+constexpr unsigned long long kWaitLimitNs = 1000ull * 1000ull * 1000ull;
+
+// Library-wide device error word: nonzero after a bounded wait gave up.
+__device__ int g_score_error = 0;
+
+struct Barriers {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t a_full;
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for phase `parity` of `bar`. Returns false (and raises the CTA abort flag
+// and the device error word) after kWaitLimitNs, or false at once if another role aborted.
+__device__ bool mbar_wait(uint64_t *bar, uint32_t parity, Barriers *bs) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  volatile int *abort = &bs->abort;
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spin & 255u) == 0) {
+      if (*abort) return false;
+      if (global_ns() - start > kWaitLimitNs) {
+        *abort = 1;
+        atomicExch(&g_score_error, 1);
+        return false;
+      }
+    }
+  }
+}
+
+// Drain-only wait used on the abort path: bounded, never raises anything.
+__device__ void mbar_drain(uint64_t *bar, uint32_t parity) {
+  const uint64_t start = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - start > kWaitLimitNs) return;
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor, K-major operand in the 128-byte swizzle layout: rows of
+// 128 bytes, 8-row groups 1024 bytes apart (SBO), version 1, swizzle mode 2.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr >> 4) & 0x3FFFu);
+  d |= uint64_t(1) << 16;           // leading byte offset (unused for swizzled K-major)
+  d |= uint64_t(1024 >> 4) << 32;   // stride byte offset
+  d |= uint64_t(1) << 46;           // descriptor version (sm_100)
+  d |= uint64_t(2) << 61;           // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor of kind::f16: f32 accumulator, A/B f16 (0) or bf16 (1), both
+// K-major, N and M in their encoded fields.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int ab_format, int m, int n) {
+  return (1u << 4) | (uint32_t(ab_format) << 7) | (uint32_t(ab_format) << 10) | (uint32_t(n >> 3) << 17) |
+         (uint32_t(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive f32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+constexpr int kWriteRunner = 1;
+constexpr int kWriteMargins = 2;
+
+// N consecutive route bytes / margins of one row, as 4-byte / 16-byte stores when N allows
+// (the caller guarantees the destination is N-element aligned).
+template <int N>
+__device__ __forceinline__ void store_run(uint8_t *dst, const uint8_t (&v)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4)
+      *reinterpret_cast<uint32_t *>(dst + i) =
+          uint32_t(v[i]) | (uint32_t(v[i + 1]) << 8) | (uint32_t(v[i + 2]) << 16) | (uint32_t(v[i + 3]) << 24);
+  } else if constexpr (N == 2) {
+    *reinterpret_cast<uint16_t *>(dst) = static_cast<uint16_t>(uint32_t(v[0]) | (uint32_t(v[1]) << 8));
+  } else {
+    dst[0] = v[0];
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void store_run(float *dst, const float (&v)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) *reinterpret_cast<float4 *>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+  } else if constexpr (N == 2) {
+    *reinterpret_cast<float2 *>(dst) = make_float2(v[0], v[1]);
+  } else {
+    dst[0] = v[0];
+  }
+}
+
+template <typename PT, int K>
+__global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
+    const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_w, const PT *__restrict__ bias,
+    int64_t rows, int H, int kblocks, int tiles_total, int tiles_per_cta, int flags, bool vec_stores,
+    int64_t *__restrict__ winner_i64, uint8_t *__restrict__ winner, uint8_t *__restrict__ runner,
+    float *__restrict__ margins) {
+  static_assert(64 % K == 0 && K >= 2, "cells must divide 64");
+  constexpr int kHeadsPerHalf = 64 / K;
+  constexpr int kHeadsPerTile = kBN / K;
+  constexpr uint32_t kIdesc = umma_idesc_f16(sizeof(PT) == 2 && !std::is_same<PT, __half>::value ? 1 : 0, kBM, kBN);
+
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the 128-byte swizzle atoms.
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *a_smem = smem;                                     // kblocks x [128 rows x 128 B]
+  uint8_t *b_smem = a_smem + kblocks * kTileBytesA;            // kStages x [128 rows x 128 B]
+  Barriers *bs = reinterpret_cast<Barriers *>(b_smem + kStages * kTileBytesB);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t row0 = int64_t(blockIdx.x) * kBM;
+  const int tile_begin = blockIdx.y * tiles_per_cta;
+  const int tile_end = min(tiles_total, tile_begin + tiles_per_cta);
+  const int ntiles = max(0, tile_end - tile_begin);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bs->full[s], 1);
+      mbar_init(&bs->empty[s], 1);
+    }
+    mbar_init(&bs->a_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bs->tmem_full[b], 1);
+      mbar_init(&bs->tmem_empty[b], kEpiWarps * 32);
+    }
+    mbar_init(&bs->mma_done, 1);
+    bs->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&bs->tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem_base = bs->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0 && ntiles > 0) {
+      // ---------------- TMA producer ----------------
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_z)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
+      mbar_expect_tx(&bs->a_full, uint32_t(kblocks) * kTileBytesA);
+      for (int kb = 0; kb < kblocks; ++kb)
+        tma_load_2d(a_smem + kb * kTileBytesA, &map_z, &bs->a_full, kb * kBK, static_cast<int>(row0));
+      uint32_t issued[kStages];
+      for (int s = 0; s < kStages; ++s) issued[s] = 0;
+      bool ok = true;
+      int it = 0;
+      for (int t = 0; t < ntiles && ok; ++t) {
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t phase = (it / kStages) & 1;
+          if (!mbar_wait(&bs->empty[s], phase ^ 1u, bs)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bs->full[s], kTileBytesB);
+          tma_load_2d(b_smem + s * kTileBytesB, &map_w, &bs->full[s], kb * kBK, (tile_begin + t) * kBN);
+          issued[s] = (it / kStages) + 1;
+        }
+      }
+      // Every copy this thread issued must land before the CTA may exit.
+      mbar_drain(&bs->a_full, 0);
+      for (int s = 0; s < kStages; ++s)
+        if (issued[s] > 0) mbar_drain(&bs->full[s], (issued[s] - 1) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && ntiles > 0) {
+      // ---------------- MMA issuer ----------------
+      bool ok = mbar_wait(&bs->a_full, 0, bs);
+      tmem_fence_after();
+      int it = 0;
+      for (int t = 0; t < ntiles && ok; ++t) {
+        const int b = t & 1;
+        const uint32_t use = t >> 1;
+        if (!mbar_wait(&bs->tmem_empty[b], (use & 1u) ^ 1u, bs)) {
+          ok = false;
+          break;
+        }
+        tmem_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(b * kBN);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t phase = (it / kStages) & 1;
+          if (!mbar_wait(&bs->full[s], phase, bs)) {
+            ok = false;
+            break;
+          }
+          tmem_fence_after();
+          const uint32_t a_base = smem_addr(a_smem + kb * kTileBytesA);
+          const uint32_t b_base = smem_addr(b_smem + s * kTileBytesB);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16(d_tmem, umma_desc_sw128(a_base + kk * 32), umma_desc_sw128(b_base + kk * 32), kIdesc,
+                     (kb | kk) != 0 ? 1u : 0u);
+          umma_commit(&bs->empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&bs->tmem_full[b]);
+      }
+      // All MMAs issued by this thread must finish before TMEM is freed.
+      umma_commit(&bs->mma_done);
+      mbar_drain(&bs->mma_done, 0);
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int ew = warp - 2;
+    const int quarter = warp & 3;       // TMEM lane quarter this warp may access
+    const int half = ew >> 2;           // which 64 columns of the tile
+    const int r = quarter * 32 + lane;  // accumulator row
+    const int64_t row = row0 + r;
+    for (int t = 0; t < ntiles; ++t) {
+      const int b = t & 1;
+      const uint32_t use = t >> 1;
+      // Warp-collective wait: lane 0 polls, the whole warp follows its verdict, so the
+      // .sync.aligned TMEM loads below always run converged.
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&bs->tmem_full[b], use & 1u, bs) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      __syncwarp();
+      tmem_fence_after();
+      const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(b * kBN + half * 64);
+      float v[64];
+      {
+        float lo[32], hi[32];
+        tmem_ld32(taddr, lo);
+        tmem_ld32(taddr + 32, hi);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          v[i] = lo[i];
+          v[32 + i] = hi[i];
+        }
+      }
+      tmem_fence_before();
+      mbar_arrive(&bs->tmem_empty[b]);
+
+      const int tile = tile_begin + t;
+      const int h0 = tile * kHeadsPerTile + half * kHeadsPerHalf;
+      uint8_t wv[kHeadsPerHalf], rv[kHeadsPerHalf];
+      float mv[kHeadsPerHalf];
+#pragma unroll
+      for (int hh = 0; hh < kHeadsPerHalf; ++hh) {
+        const int h = min(h0 + hh, H - 1);
+        const PT *bh = bias + int64_t(h) * K;
+        float bv[K];
+        if constexpr (K % 8 == 0) {
+#pragma unroll
+          for (int k0 = 0; k0 < K; k0 += 8) {
+            float q[8];
+            VecLoad<PT, 8>::load(bh + k0, q);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) bv[k0 + j] = q[j];
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < K; ++k) bv[k] = ldg_f32(bh + k);
+        }
+        float best1 = -INFINITY, best2 = -INFINITY;
+        int i1 = 0, i2 = 1;
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          const float s = __fadd_rn(v[hh * K + k], bv[k]);
+          // Strict '>' keeps the lowest cell index on exact ties.
+          if (s > best1) {
+            best2 = best1; i2 = i1; best1 = s; i1 = k;
+          } else if (s > best2) {
+            best2 = s; i2 = k;
+          }
+        }
+        wv[hh] = static_cast<uint8_t>(i1);
+        rv[hh] = static_cast<uint8_t>(i2);
+        mv[hh] = __fsub_rn(best1, best2);
+      }
+      if (row < rows) {
+        const int64_t o = row * H + h0;
+        if (vec_stores && h0 + kHeadsPerHalf <= H) {
+          // One row's kHeadsPerHalf consecutive heads: a few vector stores per tile.
+          store_run<kHeadsPerHalf>(winner + o, wv);
+          if (flags & kWriteRunner) store_run<kHeadsPerHalf>(runner + o, rv);
+          if (flags & kWriteMargins) store_run<kHeadsPerHalf>(margins + o, mv);
+        } else {
+#pragma unroll
+          for (int hh = 0; hh < kHeadsPerHalf; ++hh) {
+            if (h0 + hh < H) {
+              winner[o + hh] = wv[hh];
+              if (flags & kWriteRunner) runner[o + hh] = rv[hh];
+              if (flags & kWriteMargins) margins[o + hh] = mv[hh];
+            }
+          }
+        }
+        if (winner_i64 != nullptr) {
+#pragma unroll
+          for (int hh = 0; hh < kHeadsPerHalf; ++hh)
+            if (h0 + hh < H) winner_i64[o + hh] = wv[hh];
+        }
+      }
+    }
+  }
+
+  tmem_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+  }
+}
+
+// --------------------------------------------------------------------------- host side
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_fn(EncodeTiledFn *out) {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (fn == nullptr)
+    return set_error(TROPNN_B200_ERR_DEVICE, "cuTensorMapEncodeTiled unavailable: %s", cudaGetErrorString(err));
+  *out = fn;
+  return TROPNN_B200_OK;
+}
+
+// 2-D K-major tensor map over a row-major [outer, inner] half-precision matrix, boxes of
+// 64 x box_rows with the 128-byte swizzle; out-of-range elements read as zero.
+int make_map(CUtensorMap *map, const void *ptr, CUtensorMapDataType dt, int64_t inner, int64_t outer, int box_rows) {
+  EncodeTiledFn fn = nullptr;
+  TB_CHECK(encode_fn(&fn));
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(TROPNN_B200_ERR_LAUNCH, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return TROPNN_B200_OK;
+}
+
+size_t score_smem_bytes(int kblocks) {
+  return 1024 + size_t(kblocks) * kTileBytesA + size_t(kStages) * kTileBytesB + sizeof(Barriers);
+}
+
+template <typename PT, int K>
+int launch_score(const void *z, int64_t rows, int D, const void *W, const void *bias, int H, int64_t *w64,
+                 uint8_t *win, uint8_t *run, float *m, cudaStream_t stream) {
+  const CUtensorMapDataType dt =
+      std::is_same<PT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap map_z, map_w;
+  TB_CHECK(make_map(&map_z, z, dt, D, rows, kBM));
+  TB_CHECK(make_map(&map_w, W, dt, D, int64_t(H) * K, kBN));
+  const int kblocks = (D + kBK - 1) / kBK;
+  const int tiles_total = static_cast<int>(ceil_div(int64_t(H) * K, kBN));
+  const int64_t row_blocks = ceil_div(rows, kBM);
+  // Split the score tiles of a row block over several CTAs when there are few row blocks.
+  int splits = static_cast<int>(std::min<int64_t>(tiles_total, std::max<int64_t>(1, ceil_div(2 * 148, row_blocks))));
+  const int tiles_per_cta = (tiles_total + splits - 1) / splits;
+  splits = (tiles_total + tiles_per_cta - 1) / tiles_per_cta;
+  const size_t smem = score_smem_bytes(kblocks);
+  const int flags = (run != nullptr ? kWriteRunner : 0) | (m != nullptr ? kWriteMargins : 0);
+  // Vector stores need every row's run of heads to start on a multiple of its length.
+  constexpr int kRun = 64 / K;
+  auto al16 = [](const void *p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  const bool vec_stores = (H % kRun == 0) && al16(win) && al16(run) && al16(m);
+  auto kernel = trop_score_top2_kernel<PT, K>;
+  TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_score_sm100"));
+  dim3 grid(static_cast<unsigned>(row_blocks), static_cast<unsigned>(splits));
+  kernel<<<grid, kThreads, smem, stream>>>(map_z, map_w, static_cast<const PT *>(bias), rows, H, kblocks, tiles_total,
+                                           tiles_per_cta, flags, vec_stores, w64, win, run, m);
+  return check_launch("trop_score_sm100");
+}
+
+template <typename PT>
+int dispatch_cells(int K, const void *z, int64_t rows, int D, const void *W, const void *bias, int H, int64_t *w64,
+                   uint8_t *win, uint8_t *run, float *m, cudaStream_t stream) {
+  switch (K) {
+    case 2: return launch_score<PT, 2>(z, rows, D, W, bias, H, w64, win, run, m, stream);
+    case 4: return launch_score<PT, 4>(z, rows, D, W, bias, H, w64, win, run, m, stream);
+    case 8: return launch_score<PT, 8>(z, rows, D, W, bias, H, w64, win, run, m, stream);
+    case 16: return launch_score<PT, 16>(z, rows, D, W, bias, H, w64, win, run, m, stream);
+    case 32: return launch_score<PT, 32>(z, rows, D, W, bias, H, w64, win, run, m, stream);
+    default: return launch_score<PT, 64>(z, rows, D, W, bias, H, w64, win, run, m, stream);
+  }
+}
+
+}  // namespace
+
+bool score_sm100_supported(int64_t D, int64_t K, int pt, const void *z, const void *W, const void *bias) {
+  const bool cells_ok = K == 2 || K == 4 || K == 8 || K == 16 || K == 32 || K == 64;
+  const int64_t kblocks = (D + kBK - 1) / kBK;
+  auto al16 = [](const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  return (pt == TROPNN_B200_F16 || pt == TROPNN_B200_BF16) && cells_ok && D % 8 == 0 && kblocks <= kMaxKBlocks &&
+         score_smem_bytes(static_cast<int>(kblocks)) <= 227 * 1024 && al16(z) && al16(W) && al16(bias);
+}
+
+int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W, const void *bias, int pt, int64_t H,
+                          int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, cudaStream_t stream) {
+  TB_REQUIRE(score_sm100_supported(D, K, pt, z, W, bias), TROPNN_B200_ERR_INVALID,
+             "trop_score_sm100: unsupported shape or alignment code_dim=%lld cells=%lld dtype=%s", (long long)D,
+             (long long)K, dtype_name(pt));
+  if (items == 0) return TROPNN_B200_OK;
+  TB_REQUIRE(z && W && bias && win, TROPNN_B200_ERR_INVALID, "trop_score_sm100: null pointer");
+  const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
+  if (pt == TROPNN_B200_F16) return dispatch_cells<__half>(Ki, z, items, Di, W, bias, Hi, w64, win, run, m, stream);
+  return dispatch_cells<__nv_bfloat16>(Ki, z, items, Di, W, bias, Hi, w64, win, run, m, stream);
+}
+
+int read_score_error(int *value) {
+  int v = 0;
+  cudaError_t err = cudaMemcpyFromSymbol(&v, g_score_error, sizeof(int));
+  if (err != cudaSuccess)
+    return set_error(TROPNN_B200_ERR_LAUNCH, "reading the device error word: %s", cudaGetErrorString(err));
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_score_error, &zero, sizeof(int));
+  }
+  *value = v;
+  return TROPNN_B200_OK;
+}
+
+}  // namespace tropnn_b200

@@ -23,6 +23,11 @@ int segment_rowsum_impl(const float *values, int64_t rows, int64_t width, int64_
                         float coef_sign1, float scale, void *out, int out_dtype, void *bucket_sum,
                         cudaStream_t stream);
 
+bool score_sm100_supported(int64_t D, int64_t K, int pt, const void *z, const void *W, const void *bias);
+int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W, const void *bias, int pt, int64_t H,
+                          int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, cudaStream_t stream);
+int read_score_error(int *value);
+
 namespace {
 
 // ---------------------------------------------------------------------------
@@ -35,9 +40,19 @@ namespace {
 constexpr int kRouteWarps = 8;
 constexpr int kCellChunk = 8;
 
-template <typename PT, typename IT, int RM, bool VEC4>
+// Latent element load: f32, or (ZP) the parameter dtype, upcast exactly.
+template <typename PT, bool ZP>
+__device__ __forceinline__ float load_latent(const void *z, int64_t i) {
+  if constexpr (ZP) {
+    return ldg_f32(static_cast<const PT *>(z) + i);
+  } else {
+    return __ldg(static_cast<const float *>(z) + i);
+  }
+}
+
+template <typename PT, typename IT, int RM, bool VEC4, bool ZP>
 __global__ void __launch_bounds__(kRouteWarps * 32) trop_route_kernel(
-    const float *__restrict__ z, int64_t rows, int D, const PT *__restrict__ W, const PT *__restrict__ bias, int H,
+    const void *__restrict__ z, int64_t rows, int D, const PT *__restrict__ W, const PT *__restrict__ bias, int H,
     int K, int64_t *__restrict__ winner_i64, IT *__restrict__ winner, IT *__restrict__ runner,
     float *__restrict__ margins) {
   extern __shared__ float z_s[];
@@ -47,7 +62,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) trop_route_kernel(
   for (int i = threadIdx.x; i < rows_here * D; i += kRouteWarps * 32) {
     const int r = i / D;
     const int d = i - r * D;
-    z_s[r * pitch + d] = __ldg(z + (row0 + r) * D + d);
+    z_s[r * pitch + d] = load_latent<PT, ZP>(z, (row0 + r) * D + d);
   }
   __syncthreads();
 
@@ -130,19 +145,20 @@ __global__ void __launch_bounds__(kRouteWarps * 32) trop_route_kernel(
       const int64_t o = (row0 + rr) * H + h;
       if (winner_i64) winner_i64[o] = i1[r];
       winner[o] = static_cast<IT>(i1[r]);
-      runner[o] = static_cast<IT>(i2[r]);
-      margins[o] = __fsub_rn(best1[r], best2[r]);
+      if (runner != nullptr) runner[o] = static_cast<IT>(i2[r]);
+      if (margins != nullptr) margins[o] = __fsub_rn(best1[r], best2[r]);
     }
   }
 }
 
 template <typename PT, typename IT, int RM>
-int launch_route(const float *z, int64_t rows, int D, const void *W, const void *b, int H, int K, int64_t *w64,
-                 void *win, void *run, float *m, cudaStream_t stream) {
+int launch_route(const void *z, bool zp, int64_t rows, int D, const void *W, const void *b, int H, int K,
+                 int64_t *w64, void *win, void *run, float *m, cudaStream_t stream) {
   const bool vec4 = (D % 4 == 0);
   const size_t smem = sizeof(float) * 32 * RM * (D + 4);
   TB_REQUIRE(smem <= 200 * 1024, TROPNN_B200_ERR_INVALID, "trop_route: code_dim=%d too large for the SIMT path", D);
-  auto kernel = vec4 ? trop_route_kernel<PT, IT, RM, true> : trop_route_kernel<PT, IT, RM, false>;
+  auto kernel = zp ? (vec4 ? trop_route_kernel<PT, IT, RM, true, true> : trop_route_kernel<PT, IT, RM, false, true>)
+                   : (vec4 ? trop_route_kernel<PT, IT, RM, true, false> : trop_route_kernel<PT, IT, RM, false, false>);
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_route"));
   const int64_t row_blocks = ceil_div(rows, 32 * RM);
   TB_REQUIRE(row_blocks < (int64_t(1) << 31) && ceil_div(H, kRouteWarps) < 65536, TROPNN_B200_ERR_INVALID,
@@ -154,12 +170,12 @@ int launch_route(const float *z, int64_t rows, int D, const void *W, const void 
 }
 
 template <typename PT, typename IT>
-int route_by_rows(const float *z, int64_t rows, int D, const void *W, const void *b, int H, int K, int64_t *w64,
-                  void *win, void *run, float *m, cudaStream_t stream) {
+int route_by_rows(const void *z, bool zp, int64_t rows, int D, const void *W, const void *b, int H, int K,
+                  int64_t *w64, void *win, void *run, float *m, cudaStream_t stream) {
   // Four rows per lane once there are enough rows to fill the GPU with 128-row tiles.
   if (ceil_div(rows, 128) * ceil_div(H, kRouteWarps) >= 2 * 148 && 128 * (D + 4) * 4 <= 200 * 1024)
-    return launch_route<PT, IT, 4>(z, rows, D, W, b, H, K, w64, win, run, m, stream);
-  return launch_route<PT, IT, 1>(z, rows, D, W, b, H, K, w64, win, run, m, stream);
+    return launch_route<PT, IT, 4>(z, zp, rows, D, W, b, H, K, w64, win, run, m, stream);
+  return launch_route<PT, IT, 1>(z, zp, rows, D, W, b, H, K, w64, win, run, m, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -179,9 +195,9 @@ __device__ __forceinline__ float group_sum(float v, int lph) {
 }
 
 // hidden = latent + code_scale * sum_h chat_h (the operation order of tropical.py:137).
-template <typename PT, typename IT, bool TRAIN, int VEC, int NJ>
+template <typename PT, typename IT, bool TRAIN, int VEC, int NJ, bool ZP>
 __global__ void __launch_bounds__(kRowWarps * 32) trop_hidden_kernel(
-    const float *__restrict__ z, int D, const PT *__restrict__ code, int H, int K, const IT *__restrict__ winner,
+    const void *__restrict__ z, int D, const PT *__restrict__ code, int H, int K, const IT *__restrict__ winner,
     const IT *__restrict__ runner, const float *__restrict__ margins, float code_scale, int lph,
     float *__restrict__ hidden) {
   __shared__ float part[kRowWarps * 32 * NJ * VEC];
@@ -248,7 +264,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) trop_hidden_kernel(
     for (int w = 0; w < kRowWarps; ++w)
       for (int sb = 0; sb < hpw; ++sb) sum = __fadd_rn(sum, part[((w * 32 + sb * lph + ls) * NJ + j) * VEC + e]);
     const int64_t o = n * D + d_base + q;
-    hidden[o] = __fadd_rn(__ldg(z + o), __fmul_rn(sum, code_scale));
+    hidden[o] = __fadd_rn(load_latent<PT, ZP>(z, o), __fmul_rn(sum, code_scale));
   }
 }
 
@@ -408,22 +424,35 @@ int check_index_dtype(int64_t K, int index_dtype) {
 
 }  // namespace
 
-int trop_route_impl(const float *z, int64_t items, int64_t D, const void *W, const void *b, int pt, int64_t H,
+int check_latent_dtype(int zt, int pt, const char *what) {
+  TB_REQUIRE(zt == TROPNN_B200_F32 || zt == pt, TROPNN_B200_ERR_DTYPE,
+             "%s: latent dtype %s must be f32 or the parameter dtype %s", what, dtype_name(zt), dtype_name(pt));
+  return TROPNN_B200_OK;
+}
+
+int trop_route_impl(const void *z, int zt, int64_t items, int64_t D, const void *W, const void *b, int pt, int64_t H,
                     int64_t K, int64_t *w64, void *win, void *run, int it, float *m, cudaStream_t stream) {
   TB_CHECK(validate_trop(items, D, H, K));
   TB_REQUIRE(is_float_dtype(pt), TROPNN_B200_ERR_DTYPE, "trop_route: param dtype %s unsupported", dtype_name(pt));
   TB_CHECK(check_index_dtype(K, it));
+  TB_CHECK(check_latent_dtype(zt, pt, "trop_route"));
   if (items == 0) return TROPNN_B200_OK;
-  TB_REQUIRE(z && W && b && win && run && m, TROPNN_B200_ERR_INVALID, "trop_route: null pointer");
+  TB_REQUIRE(z && W && b && win, TROPNN_B200_ERR_INVALID, "trop_route: null pointer");
+  // Half-precision latent and parameters: scores on the tensor cores (tcgen05) when the
+  // shape fits the kernel's tiles; the SIMT kernel serves everything else.
+  const bool zp = zt != TROPNN_B200_F32;
+  if (zp && it == TROPNN_B200_U8 && items >= 128 && H * K >= 128 && score_sm100_supported(D, K, pt, z, W, b))
+    return trop_score_sm100_impl(z, items, D, W, b, pt, H, K, w64, static_cast<uint8_t *>(win),
+                                 static_cast<uint8_t *>(run), m, stream);
   int status = TROPNN_B200_OK;
-  TB_DISPATCH_PT(pt, TB_DISPATCH_IT(it, status = route_by_rows<PT, IT>(z, items, static_cast<int>(D), W, b,
+  TB_DISPATCH_PT(pt, TB_DISPATCH_IT(it, status = route_by_rows<PT, IT>(z, zp, items, static_cast<int>(D), W, b,
                                                                        static_cast<int>(H), static_cast<int>(K), w64,
                                                                        win, run, m, stream);))
   return status;
 }
 
-template <typename PT, typename IT, int VEC, int NJ>
-int launch_hidden(const float *z, int64_t items, int D, const void *code, int H, int K, const void *win,
+template <typename PT, typename IT, int VEC, int NJ, bool ZP>
+int launch_hidden(const void *z, int64_t items, int D, const void *code, int H, int K, const void *win,
                   const void *run, const float *m, float code_scale, bool training, float *hidden,
                   cudaStream_t stream) {
   const int slice = 32 * NJ * VEC;
@@ -431,35 +460,50 @@ int launch_hidden(const float *z, int64_t items, int D, const void *code, int H,
   TB_REQUIRE(ceil_div(D, slice) < 65536, TROPNN_B200_ERR_INVALID, "trop_hidden: code_dim=%d too large", D);
   dim3 grid(static_cast<unsigned>(items), static_cast<unsigned>(ceil_div(D, slice)));
   if (training)
-    trop_hidden_kernel<PT, IT, true, VEC, NJ><<<grid, kRowWarps * 32, 0, stream>>>(
+    trop_hidden_kernel<PT, IT, true, VEC, NJ, ZP><<<grid, kRowWarps * 32, 0, stream>>>(
         z, D, static_cast<const PT *>(code), H, K, static_cast<const IT *>(win), static_cast<const IT *>(run), m,
         code_scale, lph, hidden);
   else
-    trop_hidden_kernel<PT, IT, false, VEC, NJ><<<grid, kRowWarps * 32, 0, stream>>>(
+    trop_hidden_kernel<PT, IT, false, VEC, NJ, ZP><<<grid, kRowWarps * 32, 0, stream>>>(
         z, D, static_cast<const PT *>(code), H, K, static_cast<const IT *>(win), static_cast<const IT *>(win), m,
         code_scale, lph, hidden);
   return check_launch("trop_hidden");
 }
 
-int trop_hidden_impl(const float *z, int64_t items, int64_t D, const void *code, int pt, int64_t H, int64_t K,
+template <typename PT, typename IT, bool ZP>
+int hidden_by_width(const void *z, int64_t items, int D, const void *code, int H, int K, const void *win,
+                    const void *run, const float *m, float code_scale, bool training, float *hidden,
+                    cudaStream_t stream) {
+  if (row_vec_ok<PT>(D, code, code, code))
+    return launch_hidden<PT, IT, 16 / sizeof(PT), 2, ZP>(z, items, D, code, H, K, win, run, m, code_scale, training,
+                                                          hidden, stream);
+  return launch_hidden<PT, IT, 1, 8, ZP>(z, items, D, code, H, K, win, run, m, code_scale, training, hidden, stream);
+}
+
+int trop_hidden_impl(const void *z, int zt, int64_t items, int64_t D, const void *code, int pt, int64_t H, int64_t K,
                      const void *win, const void *run, int it, const float *m, float code_scale, int training,
                      float *hidden, cudaStream_t stream) {
   TB_CHECK(validate_trop(items, D, H, K));
   TB_REQUIRE(is_float_dtype(pt), TROPNN_B200_ERR_DTYPE, "trop_hidden: param dtype %s unsupported", dtype_name(pt));
   TB_CHECK(check_index_dtype(K, it));
+  TB_CHECK(check_latent_dtype(zt, pt, "trop_hidden"));
   if (items == 0) return TROPNN_B200_OK;
   TB_REQUIRE(z && code && win && hidden && (!training || (run && m)), TROPNN_B200_ERR_INVALID,
              "trop_hidden: null pointer");
   const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
   const bool train = training != 0;
+  const bool zp = zt != TROPNN_B200_F32;
   int status = TROPNN_B200_OK;
   TB_DISPATCH_PT(pt, TB_DISPATCH_IT(it, {
-    if (row_vec_ok<PT>(Di, code, code, code))
-      status = launch_hidden<PT, IT, 16 / sizeof(PT), 2>(z, items, Di, code, Hi, Ki, win, run, m, code_scale, train,
-                                                          hidden, stream);
-    else
-      status = launch_hidden<PT, IT, 1, 8>(z, items, Di, code, Hi, Ki, win, run, m, code_scale, train, hidden,
-                                           stream);
+    if constexpr (sizeof(PT) == 2) {
+      if (zp) {
+        status = hidden_by_width<PT, IT, true>(z, items, Di, code, Hi, Ki, win, run, m, code_scale, train, hidden,
+                                               stream);
+        break;
+      }
+    }
+    status = hidden_by_width<PT, IT, false>(z, items, Di, code, Hi, Ki, win, run, m, code_scale, train, hidden,
+                                            stream);
   }))
   return status;
 }
@@ -566,24 +610,31 @@ int trop_backward_impl(const float *g, const float *z, int64_t items, int64_t D,
 
 extern "C" {
 
-int tropnn_b200_trop_route(const float *latent, int64_t items, int64_t code_dim, const void *router_weight,
-                           const void *router_bias, int param_dtype, int64_t heads, int64_t cells,
-                           int64_t *winner_i64, void *winner, void *runner, int index_dtype, float *margins,
-                           void *stream) {
+int tropnn_b200_trop_route(const void *latent, int latent_dtype, int64_t items, int64_t code_dim,
+                           const void *router_weight, const void *router_bias, int param_dtype, int64_t heads,
+                           int64_t cells, int64_t *winner_i64, void *winner, void *runner, int index_dtype,
+                           float *margins, void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
-  TB_CHECK(tropnn_b200::trop_route_impl(latent, items, code_dim, router_weight, router_bias, param_dtype, heads, cells,
-                                        winner_i64, winner, runner, index_dtype, margins,
+  TB_CHECK(tropnn_b200::trop_route_impl(latent, latent_dtype, items, code_dim, router_weight, router_bias, param_dtype,
+                                        heads, cells, winner_i64, winner, runner, index_dtype, margins,
                                         tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 
-int tropnn_b200_trop_hidden(const float *latent, int64_t items, int64_t code_dim, const void *code, int param_dtype,
-                            int64_t heads, int64_t cells, const void *winner, const void *runner, int index_dtype,
-                            const float *margins, float code_scale, int training, float *hidden, void *stream) {
+int tropnn_b200_trop_hidden(const void *latent, int latent_dtype, int64_t items, int64_t code_dim, const void *code,
+                            int param_dtype, int64_t heads, int64_t cells, const void *winner, const void *runner,
+                            int index_dtype, const float *margins, float code_scale, int training, float *hidden,
+                            void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
-  TB_CHECK(tropnn_b200::trop_hidden_impl(latent, items, code_dim, code, param_dtype, heads, cells, winner, runner,
-                                         index_dtype, margins, code_scale, training, hidden,
+  TB_CHECK(tropnn_b200::trop_hidden_impl(latent, latent_dtype, items, code_dim, code, param_dtype, heads, cells, winner,
+                                         runner, index_dtype, margins, code_scale, training, hidden,
                                          tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+int tropnn_b200_device_error(int *value) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::read_score_error(value));
   return tropnn_b200::clear_error();
 }
 

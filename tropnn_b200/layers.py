@@ -24,7 +24,7 @@ import torch
 import torch.nn as nn
 from torch import Tensor
 
-from .ops import pairwise_anchor_index, pairwise_b200, trop_route_hidden_b200
+from .ops import pairwise_anchor_index, pairwise_b200, trop_route_hidden_packed
 
 __all__ = [
     "PairwiseLinear",
@@ -53,9 +53,17 @@ def _compute_dtype(x: Tensor) -> torch.dtype:
 
 
 def _store_debug(layer: nn.Module, indices: Tensor, margins: Tensor) -> None:
-    """layers/base.py:78-83: cache the last routes unless cache_route_debug is False."""
+    """layers/base.py:78-83: cache the last routes unless cache_route_debug is False.
+
+    Packed (uint8/int16) route indices are kept as they are on this package's own layers,
+    which widen them to the reference's int64 only when ``_last_indices`` is read; other
+    modules (the reference classes under ``register``) get the int64 tensor at once.
+    """
     if getattr(layer, "cache_route_debug", True):
-        layer._last_indices = indices.detach()
+        if indices.dtype != torch.int64 and isinstance(layer, RoutedLinearBase):
+            layer._set_packed_indices(indices.detach())
+        else:
+            layer._last_indices = indices.detach().to(torch.int64)
         layer._last_margins = margins.detach()
     else:
         layer._last_indices = None
@@ -90,14 +98,19 @@ def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
     input_dtype = x.dtype
     compute_dtype = _compute_dtype(x)
     _require_f32_compute(compute_dtype, "TropLinear")
-    latent = layer.proj(x.to(dtype=layer.proj.weight.dtype)).to(compute_dtype)
-    hidden, winner, margins = trop_route_hidden_b200(
+    z = layer.proj(x.to(dtype=layer.proj.weight.dtype))
+    # The reference upcasts z to the compute dtype (tropical.py:99); with half-precision
+    # parameters the b200 op takes z in that dtype instead (the upcast is exact and happens
+    # in-kernel), which lets the route scores run on the tensor cores.
+    latent = z if z.dtype in (torch.float16, torch.bfloat16) and z.dtype == layer.router_weight.dtype else z.to(compute_dtype)
+    hidden, winner, margins = trop_route_hidden_packed(
         latent,
         layer.router_weight,
         layer.router_bias,
         layer.code,
         code_scale=layer.code_scale,
         training=layer.training,
+        keep_margins=getattr(layer, "cache_route_debug", True),
     )
     weight = layer.output_proj.weight.to(dtype=compute_dtype)
     output = torch.matmul(hidden, weight.t())
@@ -188,6 +201,25 @@ class RoutedLinearBase(nn.Module):
 
     def _compute_dtype(self, x: Tensor) -> torch.dtype:
         return _compute_dtype(x)
+
+    # Route debug cache. `_last_indices` reads as the reference's int64 tensor; when the
+    # kernels hand over packed routes the widening copy is made on first read only.
+    @property
+    def _last_indices(self) -> Tensor | None:
+        packed = self.__dict__.get("_b200_packed_indices")
+        if packed is not None:
+            self.__dict__["_b200_indices"] = packed.to(torch.int64)
+            self.__dict__["_b200_packed_indices"] = None
+        return self.__dict__.get("_b200_indices")
+
+    @_last_indices.setter
+    def _last_indices(self, value: Tensor | None) -> None:
+        self.__dict__["_b200_indices"] = value
+        self.__dict__["_b200_packed_indices"] = None
+
+    def _set_packed_indices(self, packed: Tensor) -> None:
+        self.__dict__["_b200_indices"] = None
+        self.__dict__["_b200_packed_indices"] = packed
 
 
 class TropLinear(RoutedLinearBase):

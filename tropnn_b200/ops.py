@@ -332,6 +332,7 @@ class _TropRouteB200Function(torch.autograd.Function):
         code: Tensor,
         code_scale: float,
         training: bool,
+        keep_margins: bool,
     ) -> tuple[Tensor, Tensor, Tensor]:
         batch, steps, code_dim = latent.shape
         heads, cells, _ = router_weight.shape
@@ -345,18 +346,21 @@ class _TropRouteB200Function(torch.autograd.Function):
         if bias.dtype != weight.dtype or code_c.dtype != weight.dtype:
             raise TypeError("router_weight, router_bias and code must share one dtype on backend='b200'")
         idx_dtype = packed_route_index_dtype(cells)
-        winner64 = torch.empty((items, heads), device=dev, dtype=torch.int64)
-        winner = winner64 if idx_dtype == torch.int64 else torch.empty((items, heads), device=dev, dtype=idx_dtype)
-        runner = torch.empty((items, heads), device=dev, dtype=idx_dtype)
-        margins = torch.empty((items, heads), device=dev, dtype=torch.float32)
+        # Packed routes only; the runner-up and the margins exist only when the min-face
+        # mix (training) or the caller (debug cache) needs them.
+        winner = torch.empty((items, heads), device=dev, dtype=idx_dtype)
+        runner = torch.empty((items, heads), device=dev, dtype=idx_dtype) if training else None
+        margins = torch.empty((items, heads) if (training or keep_margins) else (0,), device=dev, dtype=torch.float32)
         hidden = torch.empty((items, code_dim), device=dev, dtype=torch.float32)
         stream = nat.stream_handle(dev)
         lib = nat.load()
         icode = nat.index_code(idx_dtype)
+        zcode = nat.float_code(z.dtype)
         _launch(
             "trop_route",
             lib.tropnn_b200_trop_route,
             z.data_ptr(),
+            zcode,
             items,
             code_dim,
             weight.data_ptr(),
@@ -364,17 +368,18 @@ class _TropRouteB200Function(torch.autograd.Function):
             pdt,
             heads,
             cells,
-            None if winner is winner64 else winner64.data_ptr(),
+            None,
             winner.data_ptr(),
-            runner.data_ptr(),
+            nat.ptr(runner),
             icode,
-            margins.data_ptr(),
+            margins.data_ptr() if margins.numel() else None,
             stream,
         )
         _launch(
             "trop_hidden",
             lib.tropnn_b200_trop_hidden,
             z.data_ptr(),
+            zcode,
             items,
             code_dim,
             code_c.data_ptr(),
@@ -382,9 +387,9 @@ class _TropRouteB200Function(torch.autograd.Function):
             heads,
             cells,
             winner.data_ptr(),
-            runner.data_ptr(),
+            nat.ptr(runner),
             icode,
-            margins.data_ptr(),
+            margins.data_ptr() if margins.numel() else None,
             float(code_scale),
             int(bool(training)),
             hidden.data_ptr(),
@@ -394,8 +399,8 @@ class _TropRouteB200Function(torch.autograd.Function):
         ctx.code_scale = float(code_scale)
         ctx.training = bool(training)
         ctx.shape = (batch, steps, code_dim, heads, cells)
-        winner_out = winner64.view(batch, steps, heads)
-        margins_out = margins.view(batch, steps, heads)
+        winner_out = winner.view(batch, steps, heads)
+        margins_out = margins.view(batch, steps, heads) if margins.dim() == 2 else margins
         ctx.mark_non_differentiable(winner_out, margins_out)
         return hidden.view(batch, steps, code_dim), winner_out, margins_out
 
@@ -510,10 +515,11 @@ class _TropRouteB200Function(torch.autograd.Function):
             if want_router:
                 grad_w = torch.empty_like(weight)
                 grad_b = torch.empty((heads, cells), device=dev, dtype=weight.dtype)
+                z32 = z if z.dtype == torch.float32 else z.float()
                 _launch(
                     "trop_router_grad",
                     lib.tropnn_b200_segment_rowsum,
-                    z.data_ptr(),
+                    z32.data_ptr(),
                     items,
                     code_dim,
                     code_dim,
@@ -542,7 +548,9 @@ class _TropRouteB200Function(torch.autograd.Function):
             grad_w = None
         if not ctx.needs_input_grad[2]:
             grad_b = None
-        return grad_z.view(batch, steps, code_dim), grad_w, grad_b, grad_c, None, None
+        # A half-precision latent gets its gradient rounded once to its dtype, as the
+        # reference's `.to(compute_dtype)` backward does.
+        return grad_z.view(batch, steps, code_dim).to(z.dtype), grad_w, grad_b, grad_c, None, None, None
 
 
 def trop_route_hidden_b200(
@@ -556,12 +564,34 @@ def trop_route_hidden_b200(
 ) -> tuple[Tensor, Tensor, Tensor]:
     """TropLinear route + selected-code sum with the min-face backward, on sm_100a.
 
-    ``latent`` f32 ``[B, S, D]``; ``router_weight``/``code`` ``[H, K, D]`` and
-    ``router_bias`` ``[H, K]`` in one float dtype (f32/f16/bf16, upcast in-kernel).
-    Returns ``(hidden [B,S,D] f32, winner [B,S,H] int64, margins [B,S,H] f32)`` like
-    ``trop_route_hidden_tilelang``. In eval mode (``training=False``) the output does not
-    depend on the margins, so router gradients are ``None`` as in the torch path.
+    ``router_weight``/``code`` ``[H, K, D]`` and ``router_bias`` ``[H, K]`` share one float
+    dtype (f32/f16/bf16, upcast in-kernel). ``latent`` ``[B, S, D]`` is f32, or the
+    parameters' half dtype: then the route scores run on the tensor cores (tcgen05) when
+    the shape allows, with exact products of the half-precision operands and f32
+    accumulation. Returns ``(hidden [B,S,D] f32, winner [B,S,H] int64, margins [B,S,H]
+    f32)`` like ``trop_route_hidden_tilelang``. In eval mode (``training=False``) the output
+    does not depend on the margins, so router gradients are ``None`` as in the torch path.
     """
+    hidden, winner, margins = trop_route_hidden_packed(
+        latent, router_weight, router_bias, code, code_scale=code_scale, training=training, keep_margins=True
+    )
+    return hidden, winner.to(torch.int64), margins
+
+
+def trop_route_hidden_packed(
+    latent: Tensor,
+    router_weight: Tensor,
+    router_bias: Tensor,
+    code: Tensor,
+    *,
+    code_scale: float,
+    training: bool = False,
+    keep_margins: bool = True,
+) -> tuple[Tensor, Tensor, Tensor]:
+    """``trop_route_hidden_b200`` with the winners in the packed route dtype (uint8 for
+    cells <= 256, layers/routing.py:18-23) instead of int64, and the margins computed in
+    eval only when ``keep_margins`` (otherwise an empty tensor). The layers use it so the
+    int64 debug-cache copy of the routes is made only when someone reads it."""
     for name, t in (("latent", latent), ("router_weight", router_weight), ("router_bias", router_bias), ("code", code)):
         _require_cuda(t, name)
         if t.device != latent.device:
@@ -576,8 +606,13 @@ def trop_route_hidden_b200(
         raise ValueError(f"code must match router_weight shape, got {tuple(code.shape)} and {tuple(router_weight.shape)}")
     if latent.shape[-1] != router_weight.shape[-1]:
         raise ValueError(f"latent code_dim {latent.shape[-1]} does not match router_weight code_dim {router_weight.shape[-1]}")
-    _require_f32(latent, "latent")
+    if latent.dtype not in (torch.float32, router_weight.dtype):
+        raise TypeError(
+            f"backend='b200' latent must be float32 or the parameter dtype {router_weight.dtype}, got {latent.dtype}"
+        )
     if not math.isfinite(float(code_scale)):
         raise ValueError(f"code_scale must be finite, got {code_scale}")
     with torch.cuda.device(latent.device):
-        return _TropRouteB200Function.apply(latent, router_weight, router_bias, code, float(code_scale), bool(training))
+        return _TropRouteB200Function.apply(
+            latent, router_weight, router_bias, code, float(code_scale), bool(training), bool(keep_margins)
+        )
