@@ -639,10 +639,15 @@ def main(argv: list[str] | None = None) -> int:
     parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
     parser.add_argument("--cpu-budget-s", type=float, default=10.0, help="seconds of CPU-baseline timing (rank 0, N=1)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--rows", type=int, default=0, help="override the per-GPU row count (profiling runs)")
     args = parser.parse_args(argv)
     if args.warmup < 3 and args.impl == "b200":
         parser.error("--warmup must be >= 3")
     w = WORKLOADS[args.workload]
+    if args.rows > 0:
+        import dataclasses
+
+        w = dataclasses.replace(w, rows_per_gpu=args.rows, description=f"{w.description} [rows overridden: {args.rows}]")
     _, world, _ = _dist_env()
     if world != args.gpus:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}; reporting WORLD_SIZE", file=sys.stderr)
