@@ -22,7 +22,8 @@
 // Every mbarrier wait gives up after ~1 s (clock64-independent %globaltimer), sets the
 // library's device error word, lets the other roles exit, drains the copies and MMAs it
 // issued (bounded again) and frees TMEM, so a protocol error cannot hang the GPU.
-// No TMA multicast and no peer memory: safe in multi-GPU processes.
+// Every TMA load is a plain per-CTA load of this GPU's own memory (no cluster-wide
+// delivery, no peer memory), so the kernel is safe in multi-GPU processes.
 #include <cuda.h>
 
 #include <mutex>
