@@ -154,7 +154,7 @@ def tensor_core_route(w: Workload, rows: int) -> bool:
         return False
     kw = w.layer_kwargs
     H, K, D = kw["heads"], kw["cells"], kw["code_dim"]
-    return K in (2, 4, 8, 16, 32, 64) and D % 8 == 0 and (D + 63) // 64 <= 6 and rows >= 128 and H * K >= 128
+    return K in (2, 4, 8, 16, 32) and D % 8 == 0 and (D + 63) // 64 <= 6 and rows >= 128 and H * K >= 128
 
 
 def kernel_roofline(w: Workload, kernel: str, rows: int, peaks: dict) -> tuple[str, float, str, float] | None:

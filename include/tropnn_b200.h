@@ -216,15 +216,17 @@ TROPNN_B200_API int tropnn_b200_pairwise_backward_noalloc(const float *grad_out,
  *   s[n,h,k] = <latent[n,:], router_weight[h,k,:]> + router_bias[h,k]
  *   winner/runner = top-2 cells (lowest index on exact ties), margin = s_w - s_r.
  * latent [items, code_dim] in latent_dtype: F32 (fp32 FMA path, parameters upcast) or
- * the parameter dtype. With F16/BF16 latent and parameters, cells in {2,4,8,16,32,64},
+ * the parameter dtype. With F16/BF16 latent and parameters, cells in {2,4,8,16,32},
  * code_dim % 8 == 0 and <= 384, U8 routes and >= 128 rows and score columns, the scores
  * run on the tensor cores (tcgen05, TMEM accumulators, TMA) and only the routes leave
- * the chip. router_weight [heads, cells, code_dim] and router_bias [heads, cells] in
- * param_dtype. winner_i64 (int64 [items, heads], may be NULL), winner/runner in
- * index_dtype (U8/I16/I64, the packing of routing.py:18-31), margins f32 [items, heads].
+ * the chip; that path needs router_bias in F32 (bias_dtype), which spares its epilogue
+ * every conversion. router_weight [heads, cells, code_dim] in param_dtype; router_bias
+ * [heads, cells] in bias_dtype (F32 or param_dtype). winner_i64 (int64 [items, heads])
+ * may be NULL; winner in index_dtype (U8/I16/I64, the packing of routing.py:18-31);
+ * runner (index_dtype) and margins (f32 [items, heads]) may be NULL when not needed.
  */
 TROPNN_B200_API int tropnn_b200_trop_route(const void *latent, int latent_dtype, int64_t items, int64_t code_dim,
-                           const void *router_weight, const void *router_bias, int param_dtype,
+                           const void *router_weight, const void *router_bias, int bias_dtype, int param_dtype,
                            int64_t heads, int64_t cells,
                            int64_t *winner_i64, void *winner, void *runner, int index_dtype,
                            float *margins, void *stream);

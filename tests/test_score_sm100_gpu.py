@@ -31,8 +31,8 @@ def _route(z: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> tuple[n
     m = torch.empty(items, heads, dtype=torch.float32, device=dev)
     status = lib.tropnn_b200_trop_route(
         z.data_ptr(), nat.float_code(z.dtype), items, code_dim, weight.data_ptr(), bias.data_ptr(),
-        nat.float_code(weight.dtype), heads, cells, w64.data_ptr(), win.data_ptr(), run.data_ptr(), nat.U8,
-        m.data_ptr(), torch.cuda.current_stream().cuda_stream,
+        nat.float_code(bias.dtype), nat.float_code(weight.dtype), heads, cells, w64.data_ptr(), win.data_ptr(),
+        run.data_ptr(), nat.U8, m.data_ptr(), torch.cuda.current_stream().cuda_stream,
     )
     nat.check(status, "trop_route")
     torch.cuda.synchronize()
@@ -49,7 +49,7 @@ def _case(items: int, heads: int, cells: int, code_dim: int, dtype: torch.dtype,
 
 def _check(items: int, heads: int, cells: int, code_dim: int, dtype: torch.dtype) -> None:
     z, weight, bias = _case(items, heads, cells, code_dim, dtype)
-    tc = _route(z, weight, bias)  # half latent: tensor-core path
+    tc = _route(z, weight, bias.float())  # half latent, f32 bias: tensor-core path
     simt = _route(z.float(), weight, bias)  # f32 latent: SIMT fp32 path
     scores = oracle.trop_scores(z.float().cpu().numpy(), weight.float().cpu().numpy(), bias.float().cpu().numpy())
     win_gate, run_gate = route_gate(scores)

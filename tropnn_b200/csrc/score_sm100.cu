@@ -15,10 +15,10 @@
 //               8-stage ring.
 //   warp 1      allocates 256 TMEM columns (two 128-column f32 accumulators); lane 0
 //               issues the MMAs (M=128, N=128, K=16 each) and commits them to mbarriers.
-//   warps 2-9   epilogue: each thread owns one accumulator row (TMEM lane) and one half
-//               of the tile's columns; it reads 64 scores with tcgen05.ld, adds the bias,
-//               takes the top-2 of every head and writes winner/runner (u8), the margin
-//               (f32) and optionally the int64 winner.
+//   warps 2-17  epilogue: each thread owns one accumulator row (TMEM lane) and 32 of the
+//               tile's columns; it reads them with one tcgen05.ld, adds the bias, takes
+//               the top-2 of every head and writes winner (u8) and, when asked, runner
+//               (u8), margin (f32) and the int64 winner.
 // Every mbarrier wait gives up after ~1 s (clock64-independent %globaltimer), sets the
 // library's device error word, lets the other roles exit, drains the copies and MMAs it
 // issued (bounded again) and frees TMEM, so a protocol error cannot hang the GPU.
@@ -41,8 +41,12 @@ constexpr int kBK = 64;               // k-block width: 64 f16 = one 128-byte sw
 constexpr int kStages = 8;            // router-weight ring depth
 constexpr int kTileBytesA = kBM * 128;  // one k block of the z tile
 constexpr int kTileBytesB = kBN * 128;  // one k block of a weight tile
-constexpr int kEpiWarps = 8;
+#ifndef TROPNN_B200_SCORE_EPILOGUE_WARPS
+#define TROPNN_B200_SCORE_EPILOGUE_WARPS 16
+#endif
+constexpr int kEpiWarps = TROPNN_B200_SCORE_EPILOGUE_WARPS;  // 8 or 16
 constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr int kEpiCols = kBN * 4 / kEpiWarps;  // accumulator columns per epilogue warp
 constexpr int kTmemCols = 2 * kBN;
 constexpr int kMaxKBlocks = 8;         // code_dim <= 512
 constexpr unsigned long long kWaitLimitNs = 1000ull * 1000ull * 1000ull;
@@ -218,13 +222,16 @@ __device__ __forceinline__ void store_run(float *dst, const float (&v)[N]) {
 
 template <typename PT, int K>
 __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
-    const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_w, const PT *__restrict__ bias,
+    const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_w, const float *__restrict__ bias,
     int64_t rows, int H, int kblocks, int tiles_total, int tiles_per_cta, int flags, bool vec_stores,
     int64_t *__restrict__ winner_i64, uint8_t *__restrict__ winner, uint8_t *__restrict__ runner,
     float *__restrict__ margins) {
-  static_assert(64 % K == 0 && K >= 2, "cells must divide 64");
-  constexpr int kHeadsPerHalf = 64 / K;
+  static_assert(32 % K == 0 && K >= 2, "cells must divide 32");
+  static_assert(kEpiCols % K == 0 && kEpiCols % 32 == 0, "an epilogue warp must own whole heads");
+  constexpr int kHeadsPerGroup = kEpiCols / K;  // heads in one epilogue warp's columns
   constexpr int kHeadsPerTile = kBN / K;
+  constexpr int kIdxBits = K <= 2 ? 1 : K <= 4 ? 2 : K <= 8 ? 3 : K <= 16 ? 4 : 5;
+  constexpr uint32_t kIdxMask = (1u << kIdxBits) - 1u;
   constexpr uint32_t kIdesc = umma_idesc_f16(sizeof(PT) == 2 && !std::is_same<PT, __half>::value ? 1 : 0, kBM, kBN);
 
   extern __shared__ uint8_t smem_raw[];
@@ -337,14 +344,32 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
     }
   } else {
     // ---------------- epilogue ----------------
-    const int ew = warp - 2;
     const int quarter = warp & 3;       // TMEM lane quarter this warp may access
-    const int half = ew >> 2;           // which 64 columns of the tile
+    const int group = (warp - 2) >> 2;  // which kEpiCols columns of the tile
     const int r = quarter * 32 + lane;  // accumulator row
     const int64_t row = row0 + r;
     for (int t = 0; t < ntiles; ++t) {
       const int b = t & 1;
       const uint32_t use = t >> 1;
+      const int tile = tile_begin + t;
+      const int h0 = tile * kHeadsPerTile + group * kHeadsPerGroup;
+      // The group's bias values (f32, so the epilogue converts nothing), loaded before
+      // the wait so that their latency overlaps it.
+      float bv[kEpiCols];
+      {
+        const int64_t c0 = int64_t(tile) * kBN + group * kEpiCols;
+        const float *bp = bias + c0;
+        if (c0 + kEpiCols <= int64_t(H) * K) {
+#pragma unroll
+          for (int c = 0; c < kEpiCols; c += 4) {
+            const float4 q = __ldg(reinterpret_cast<const float4 *>(bp + c));
+            bv[c] = q.x; bv[c + 1] = q.y; bv[c + 2] = q.z; bv[c + 3] = q.w;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < kEpiCols; ++c) bv[c] = (c0 + c < int64_t(H) * K) ? __ldg(bp + c) : 0.f;
+        }
+      }
       // Warp-collective wait: lane 0 polls, the whole warp follows its verdict, so the
       // .sync.aligned TMEM loads below always run converged.
       int ok = 1;
@@ -353,69 +378,55 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
       if (!ok) break;
       __syncwarp();
       tmem_fence_after();
-      const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(b * kBN + half * 64);
-      float v[64];
-      {
-        float lo[32], hi[32];
-        tmem_ld32(taddr, lo);
-        tmem_ld32(taddr + 32, hi);
-        tmem_wait_ld();
+      float v[kEpiCols];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          v[i] = lo[i];
-          v[32 + i] = hi[i];
-        }
+      for (int c = 0; c < kEpiCols; c += 32) {
+        float part[32];
+        tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(b * kBN + group * kEpiCols + c), part);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[c + i] = part[i];
       }
+      tmem_wait_ld();
       tmem_fence_before();
       mbar_arrive(&bs->tmem_empty[b]);
 
-      const int tile = tile_begin + t;
-      const int h0 = tile * kHeadsPerTile + half * kHeadsPerHalf;
-      uint8_t wv[kHeadsPerHalf], rv[kHeadsPerHalf];
-      float mv[kHeadsPerHalf];
+      // Top-2 per head on index-packed keys: the cell index replaces the kIdxBits lowest
+      // mantissa bits of each score (K-1-k above zero, k below, so the larger key is the
+      // larger score and, between scores equal after packing, the lower cell), and two
+      // float max/min per score keep the best two keys. Routes therefore equal the fp32
+      // routes whenever the top-2 scores differ by more than 2^kIdxBits ulp (~2^-19
+      // relative for 16 cells), far inside the 1e-4 relative parity gate; the margin is
+      // the difference of the two packed keys.
+      uint8_t wv[kHeadsPerGroup], rv[kHeadsPerGroup];
+      float mv[kHeadsPerGroup];
 #pragma unroll
-      for (int hh = 0; hh < kHeadsPerHalf; ++hh) {
-        const int h = min(h0 + hh, H - 1);
-        const PT *bh = bias + int64_t(h) * K;
-        float bv[K];
-        if constexpr (K % 8 == 0) {
-#pragma unroll
-          for (int k0 = 0; k0 < K; k0 += 8) {
-            float q[8];
-            VecLoad<PT, 8>::load(bh + k0, q);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) bv[k0 + j] = q[j];
-          }
-        } else {
-#pragma unroll
-          for (int k = 0; k < K; ++k) bv[k] = ldg_f32(bh + k);
-        }
-        float best1 = -INFINITY, best2 = -INFINITY;
-        int i1 = 0, i2 = 1;
+      for (int hh = 0; hh < kHeadsPerGroup; ++hh) {
+        float k1 = -INFINITY, k2 = -INFINITY;
 #pragma unroll
         for (int k = 0; k < K; ++k) {
-          const float s = __fadd_rn(v[hh * K + k], bv[k]);
-          // Strict '>' keeps the lowest cell index on exact ties.
-          if (s > best1) {
-            best2 = best1; i2 = i1; best1 = s; i1 = k;
-          } else if (s > best2) {
-            best2 = s; i2 = k;
-          }
+          const uint32_t bits = __float_as_uint(__fadd_rn(v[hh * K + k], bv[hh * K + k]));
+          const uint32_t flip = static_cast<uint32_t>(static_cast<int32_t>(bits) >> 31) & kIdxMask;
+          const float key = __uint_as_float((bits & ~kIdxMask) | ((uint32_t(K - 1 - k)) ^ flip));
+          k2 = fmaxf(k2, fminf(k1, key));
+          k1 = fmaxf(k1, key);
         }
-        wv[hh] = static_cast<uint8_t>(i1);
-        rv[hh] = static_cast<uint8_t>(i2);
-        mv[hh] = __fsub_rn(best1, best2);
+        const uint32_t b1 = __float_as_uint(k1), b2 = __float_as_uint(k2);
+        const uint32_t l1 = (b1 & kIdxMask) ^ (static_cast<uint32_t>(static_cast<int32_t>(b1) >> 31) & kIdxMask);
+        const uint32_t l2 = (b2 & kIdxMask) ^ (static_cast<uint32_t>(static_cast<int32_t>(b2) >> 31) & kIdxMask);
+        wv[hh] = static_cast<uint8_t>(K - 1 - l1);
+        rv[hh] = static_cast<uint8_t>(K - 1 - l2);
+        mv[hh] = __fsub_rn(k1, k2);
       }
       if (row < rows) {
         const int64_t o = row * H + h0;
-        if (vec_stores && h0 + kHeadsPerHalf <= H) {
-          // One row's kHeadsPerHalf consecutive heads: a few vector stores per tile.
-          store_run<kHeadsPerHalf>(winner + o, wv);
-          if (flags & kWriteRunner) store_run<kHeadsPerHalf>(runner + o, rv);
-          if (flags & kWriteMargins) store_run<kHeadsPerHalf>(margins + o, mv);
+        if (vec_stores && h0 + kHeadsPerGroup <= H) {
+          // One row's consecutive heads: one or two vector stores per output per tile.
+          store_run<kHeadsPerGroup>(winner + o, wv);
+          if (flags & kWriteRunner) store_run<kHeadsPerGroup>(runner + o, rv);
+          if (flags & kWriteMargins) store_run<kHeadsPerGroup>(margins + o, mv);
         } else {
 #pragma unroll
-          for (int hh = 0; hh < kHeadsPerHalf; ++hh) {
+          for (int hh = 0; hh < kHeadsPerGroup; ++hh) {
             if (h0 + hh < H) {
               winner[o + hh] = wv[hh];
               if (flags & kWriteRunner) runner[o + hh] = rv[hh];
@@ -425,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
         }
         if (winner_i64 != nullptr) {
 #pragma unroll
-          for (int hh = 0; hh < kHeadsPerHalf; ++hh)
+          for (int hh = 0; hh < kHeadsPerGroup; ++hh)
             if (h0 + hh < H) winner_i64[o + hh] = wv[hh];
         }
       }
@@ -500,13 +511,13 @@ int launch_score(const void *z, int64_t rows, int D, const void *W, const void *
   const size_t smem = score_smem_bytes(kblocks);
   const int flags = (run != nullptr ? kWriteRunner : 0) | (m != nullptr ? kWriteMargins : 0);
   // Vector stores need every row's run of heads to start on a multiple of its length.
-  constexpr int kRun = 64 / K;
+  constexpr int kRun = kEpiCols / K;
   auto al16 = [](const void *p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   const bool vec_stores = (H % kRun == 0) && al16(win) && al16(run) && al16(m);
   auto kernel = trop_score_top2_kernel<PT, K>;
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_score_sm100"));
   dim3 grid(static_cast<unsigned>(row_blocks), static_cast<unsigned>(splits));
-  kernel<<<grid, kThreads, smem, stream>>>(map_z, map_w, static_cast<const PT *>(bias), rows, H, kblocks, tiles_total,
+  kernel<<<grid, kThreads, smem, stream>>>(map_z, map_w, static_cast<const float *>(bias), rows, H, kblocks, tiles_total,
                                            tiles_per_cta, flags, vec_stores, w64, win, run, m);
   return check_launch("trop_score_sm100");
 }
@@ -519,24 +530,25 @@ int dispatch_cells(int K, const void *z, int64_t rows, int D, const void *W, con
     case 4: return launch_score<PT, 4>(z, rows, D, W, bias, H, w64, win, run, m, stream);
     case 8: return launch_score<PT, 8>(z, rows, D, W, bias, H, w64, win, run, m, stream);
     case 16: return launch_score<PT, 16>(z, rows, D, W, bias, H, w64, win, run, m, stream);
-    case 32: return launch_score<PT, 32>(z, rows, D, W, bias, H, w64, win, run, m, stream);
-    default: return launch_score<PT, 64>(z, rows, D, W, bias, H, w64, win, run, m, stream);
+    default: return launch_score<PT, 32>(z, rows, D, W, bias, H, w64, win, run, m, stream);
   }
 }
 
 }  // namespace
 
-bool score_sm100_supported(int64_t D, int64_t K, int pt, const void *z, const void *W, const void *bias) {
-  const bool cells_ok = K == 2 || K == 4 || K == 8 || K == 16 || K == 32 || K == 64;
+bool score_sm100_supported(int64_t D, int64_t K, int pt, int bias_dtype, const void *z, const void *W,
+                           const void *bias) {
+  const bool cells_ok = K == 2 || K == 4 || K == 8 || K == 16 || K == 32;
   const int64_t kblocks = (D + kBK - 1) / kBK;
   auto al16 = [](const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
-  return (pt == TROPNN_B200_F16 || pt == TROPNN_B200_BF16) && cells_ok && D % 8 == 0 && kblocks <= kMaxKBlocks &&
+  return (pt == TROPNN_B200_F16 || pt == TROPNN_B200_BF16) && bias_dtype == TROPNN_B200_F32 && cells_ok &&
+         D % 8 == 0 && kblocks <= kMaxKBlocks &&
          score_smem_bytes(static_cast<int>(kblocks)) <= 227 * 1024 && al16(z) && al16(W) && al16(bias);
 }
 
 int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W, const void *bias, int pt, int64_t H,
                           int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, cudaStream_t stream) {
-  TB_REQUIRE(score_sm100_supported(D, K, pt, z, W, bias), TROPNN_B200_ERR_INVALID,
+  TB_REQUIRE(score_sm100_supported(D, K, pt, TROPNN_B200_F32, z, W, bias), TROPNN_B200_ERR_INVALID,
              "trop_score_sm100: unsupported shape or alignment code_dim=%lld cells=%lld dtype=%s", (long long)D,
              (long long)K, dtype_name(pt));
   if (items == 0) return TROPNN_B200_OK;

@@ -23,7 +23,8 @@ int segment_rowsum_impl(const float *values, int64_t rows, int64_t width, int64_
                         float coef_sign1, float scale, void *out, int out_dtype, void *bucket_sum,
                         cudaStream_t stream);
 
-bool score_sm100_supported(int64_t D, int64_t K, int pt, const void *z, const void *W, const void *bias);
+bool score_sm100_supported(int64_t D, int64_t K, int pt, int bias_dtype, const void *z, const void *W,
+                           const void *bias);
 int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W, const void *bias, int pt, int64_t H,
                           int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, cudaStream_t stream);
 int read_score_error(int *value);
@@ -52,7 +53,7 @@ __device__ __forceinline__ float load_latent(const void *z, int64_t i) {
 
 template <typename PT, typename IT, int RM, bool VEC4, bool ZP>
 __global__ void __launch_bounds__(kRouteWarps * 32) trop_route_kernel(
-    const void *__restrict__ z, int64_t rows, int D, const PT *__restrict__ W, const PT *__restrict__ bias, int H,
+    const void *__restrict__ z, int64_t rows, int D, const PT *__restrict__ W, const void *__restrict__ bias, bool bias_f32, int H,
     int K, int64_t *__restrict__ winner_i64, IT *__restrict__ winner, IT *__restrict__ runner,
     float *__restrict__ margins) {
   extern __shared__ float z_s[];
@@ -124,7 +125,8 @@ __global__ void __launch_bounds__(kRouteWarps * 32) trop_route_kernel(
 #pragma unroll
     for (int k = 0; k < kCellChunk; ++k) {
       if (k0 + k < K) {
-        const float bk = ldg_f32(bias + int64_t(h) * K + k0 + k);
+        const int64_t bi = int64_t(h) * K + k0 + k;
+        const float bk = bias_f32 ? __ldg(static_cast<const float *>(bias) + bi) : ldg_f32(static_cast<const PT *>(bias) + bi);
 #pragma unroll
         for (int r = 0; r < RM; ++r) {
           const float s = __fadd_rn(acc[r][k], bk);
@@ -152,8 +154,8 @@ __global__ void __launch_bounds__(kRouteWarps * 32) trop_route_kernel(
 }
 
 template <typename PT, typename IT, int RM>
-int launch_route(const void *z, bool zp, int64_t rows, int D, const void *W, const void *b, int H, int K,
-                 int64_t *w64, void *win, void *run, float *m, cudaStream_t stream) {
+int launch_route(const void *z, bool zp, int64_t rows, int D, const void *W, const void *b, bool bias_f32, int H,
+                 int K, int64_t *w64, void *win, void *run, float *m, cudaStream_t stream) {
   const bool vec4 = (D % 4 == 0);
   const size_t smem = sizeof(float) * 32 * RM * (D + 4);
   TB_REQUIRE(smem <= 200 * 1024, TROPNN_B200_ERR_INVALID, "trop_route: code_dim=%d too large for the SIMT path", D);
@@ -164,18 +166,18 @@ int launch_route(const void *z, bool zp, int64_t rows, int D, const void *W, con
   TB_REQUIRE(row_blocks < (int64_t(1) << 31) && ceil_div(H, kRouteWarps) < 65536, TROPNN_B200_ERR_INVALID,
              "trop_route: grid too large");
   dim3 grid(static_cast<unsigned>(row_blocks), static_cast<unsigned>(ceil_div(H, kRouteWarps)));
-  kernel<<<grid, kRouteWarps * 32, smem, stream>>>(z, rows, D, static_cast<const PT *>(W), static_cast<const PT *>(b),
-                                                   H, K, w64, static_cast<IT *>(win), static_cast<IT *>(run), m);
+  kernel<<<grid, kRouteWarps * 32, smem, stream>>>(z, rows, D, static_cast<const PT *>(W), b, bias_f32, H, K, w64,
+                                                   static_cast<IT *>(win), static_cast<IT *>(run), m);
   return check_launch("trop_route");
 }
 
 template <typename PT, typename IT>
-int route_by_rows(const void *z, bool zp, int64_t rows, int D, const void *W, const void *b, int H, int K,
-                  int64_t *w64, void *win, void *run, float *m, cudaStream_t stream) {
+int route_by_rows(const void *z, bool zp, int64_t rows, int D, const void *W, const void *b, bool bias_f32, int H,
+                  int K, int64_t *w64, void *win, void *run, float *m, cudaStream_t stream) {
   // Four rows per lane once there are enough rows to fill the GPU with 128-row tiles.
   if (ceil_div(rows, 128) * ceil_div(H, kRouteWarps) >= 2 * 148 && 128 * (D + 4) * 4 <= 200 * 1024)
-    return launch_route<PT, IT, 4>(z, zp, rows, D, W, b, H, K, w64, win, run, m, stream);
-  return launch_route<PT, IT, 1>(z, zp, rows, D, W, b, H, K, w64, win, run, m, stream);
+    return launch_route<PT, IT, 4>(z, zp, rows, D, W, b, bias_f32, H, K, w64, win, run, m, stream);
+  return launch_route<PT, IT, 1>(z, zp, rows, D, W, b, bias_f32, H, K, w64, win, run, m, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -430,24 +432,28 @@ int check_latent_dtype(int zt, int pt, const char *what) {
   return TROPNN_B200_OK;
 }
 
-int trop_route_impl(const void *z, int zt, int64_t items, int64_t D, const void *W, const void *b, int pt, int64_t H,
-                    int64_t K, int64_t *w64, void *win, void *run, int it, float *m, cudaStream_t stream) {
+int trop_route_impl(const void *z, int zt, int64_t items, int64_t D, const void *W, const void *b, int bt, int pt,
+                    int64_t H, int64_t K, int64_t *w64, void *win, void *run, int it, float *m, cudaStream_t stream) {
   TB_CHECK(validate_trop(items, D, H, K));
   TB_REQUIRE(is_float_dtype(pt), TROPNN_B200_ERR_DTYPE, "trop_route: param dtype %s unsupported", dtype_name(pt));
   TB_CHECK(check_index_dtype(K, it));
   TB_CHECK(check_latent_dtype(zt, pt, "trop_route"));
+  TB_REQUIRE(bt == pt || bt == TROPNN_B200_F32, TROPNN_B200_ERR_DTYPE,
+             "trop_route: bias dtype %s must be f32 or the parameter dtype %s", dtype_name(bt), dtype_name(pt));
   if (items == 0) return TROPNN_B200_OK;
   TB_REQUIRE(z && W && b && win, TROPNN_B200_ERR_INVALID, "trop_route: null pointer");
   // Half-precision latent and parameters: scores on the tensor cores (tcgen05) when the
   // shape fits the kernel's tiles; the SIMT kernel serves everything else.
   const bool zp = zt != TROPNN_B200_F32;
-  if (zp && it == TROPNN_B200_U8 && items >= 128 && H * K >= 128 && score_sm100_supported(D, K, pt, z, W, b))
+  if (zp && it == TROPNN_B200_U8 && items >= 128 && H * K >= 128 && score_sm100_supported(D, K, pt, bt, z, W, b))
     return trop_score_sm100_impl(z, items, D, W, b, pt, H, K, w64, static_cast<uint8_t *>(win),
                                  static_cast<uint8_t *>(run), m, stream);
   int status = TROPNN_B200_OK;
+  const bool bias_f32 = bt == TROPNN_B200_F32;
   TB_DISPATCH_PT(pt, TB_DISPATCH_IT(it, status = route_by_rows<PT, IT>(z, zp, items, static_cast<int>(D), W, b,
-                                                                       static_cast<int>(H), static_cast<int>(K), w64,
-                                                                       win, run, m, stream);))
+                                                                       bias_f32, static_cast<int>(H),
+                                                                       static_cast<int>(K), w64, win, run, m,
+                                                                       stream);))
   return status;
 }
 
@@ -611,11 +617,12 @@ int trop_backward_impl(const float *g, const float *z, int64_t items, int64_t D,
 extern "C" {
 
 int tropnn_b200_trop_route(const void *latent, int latent_dtype, int64_t items, int64_t code_dim,
-                           const void *router_weight, const void *router_bias, int param_dtype, int64_t heads,
-                           int64_t cells, int64_t *winner_i64, void *winner, void *runner, int index_dtype,
-                           float *margins, void *stream) {
+                           const void *router_weight, const void *router_bias, int bias_dtype, int param_dtype,
+                           int64_t heads, int64_t cells, int64_t *winner_i64, void *winner, void *runner,
+                           int index_dtype, float *margins, void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
-  TB_CHECK(tropnn_b200::trop_route_impl(latent, latent_dtype, items, code_dim, router_weight, router_bias, param_dtype,
+  TB_CHECK(tropnn_b200::trop_route_impl(latent, latent_dtype, items, code_dim, router_weight, router_bias, bias_dtype,
+                                        param_dtype,
                                         heads, cells, winner_i64, winner, runner, index_dtype, margins,
                                         tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();

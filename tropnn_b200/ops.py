@@ -356,6 +356,8 @@ class _TropRouteB200Function(torch.autograd.Function):
         lib = nat.load()
         icode = nat.index_code(idx_dtype)
         zcode = nat.float_code(z.dtype)
+        # The tensor-core route reads the bias in f32 (exact upcast of the parameter).
+        bias_in = bias if bias.dtype == torch.float32 else bias.float()
         _launch(
             "trop_route",
             lib.tropnn_b200_trop_route,
@@ -364,7 +366,8 @@ class _TropRouteB200Function(torch.autograd.Function):
             items,
             code_dim,
             weight.data_ptr(),
-            bias.data_ptr(),
+            bias_in.data_ptr(),
+            nat.F32,
             pdt,
             heads,
             cells,
