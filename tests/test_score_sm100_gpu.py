@@ -81,7 +81,11 @@ def test_config5_layer_shape(dtype: torch.dtype) -> None:
         (300, 12, 16, 64),  # ragged rows (300 = 2*128 + 44) and a half-filled last score tile
         (129, 9, 16, 40),  # code_dim not a multiple of 64 (zero-filled k block), 9 heads
         (1000, 200, 8, 128),  # many tiles, several column splits
-        (128, 8, 16, 384),  # largest code_dim of the kernel (6 k blocks)
+        (128, 8, 16, 384),  # 6 k blocks: one 128-row half per row block, 8-stage ring
+        (200, 8, 16, 448),  # 7 k blocks: 7-stage ring
+        (130, 16, 8, 512),  # largest code_dim (8 k blocks, 6-stage ring), 2 rows in the last block
+        (20000, 128, 16, 128),  # ~8.5 units per CTA: z block reloads inside a CTA's range
+        (12345, 96, 4, 256),  # odd row count, 3 tiles per row block, second half empty at the end
     ],
 )
 def test_ragged_shapes(items: int, heads: int, cells: int, code_dim: int) -> None:

@@ -105,7 +105,7 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
     with _lock:
         if _lib is not None and path is None:
             return _lib
-        lib_path = Path(path or os.environ.get("TROPNN_B200_LIB", LIB_PATH))
+        lib_path = Path(path or os.environ.get("TROPNN_B200_LIB") or LIB_PATH)
         if not lib_path.exists():
             raise B200Unavailable(
                 f"backend='b200' kernel library not found at {lib_path}; build it with "

@@ -8,17 +8,22 @@
 // exactly representable in the MMA's f16/bf16 operands (z is rounded to the parameter
 // dtype by the projection, tropical.py:99) and each product is exact in f32.
 //
-// CTA = 10 warps, one 128-row block of z, a contiguous range of 128-column score tiles
-// (128/cells heads each):
-//   warp 0      TMA producer: the z block once (resident, K-major, 128B swizzle), then
-//               the router-weight tile of every (score tile, 64-wide k block) through an
-//               8-stage ring.
-//   warp 1      allocates 256 TMEM columns (two 128-column f32 accumulators); lane 0
-//               issues the MMAs (M=128, N=128, K=16 each) and commits them to mbarriers.
-//   warps 2-17  epilogue: each thread owns one accumulator row (TMEM lane) and 32 of the
-//               tile's columns; it reads them with one tcgen05.ld, adds the bias, takes
-//               the top-2 of every head and writes winner (u8) and, when asked, runner
-//               (u8), margin (f32) and the int64 winner.
+// Work unit = (128-row block of z, 256-column score tile of 256/cells heads). N=256 MMAs
+// keep the tensor pipe at its rate with the weight tiles streaming in by TMA (N=128 MMAs
+// fed the same way ran at ~60% of it). The grid is persistent, one CTA per SM, each CTA
+// running a contiguous range of the row-major unit sequence, so the load is balanced to
+// within one unit and consecutive units share their z block. CTA = 2 + 16 warps:
+//   warp 0      TMA producer: the z block (resident, K-major, 128B swizzle; reloaded
+//               when the unit sequence enters the next row block, once the MMAs on the
+//               old block are done), then the router-weight tile of every (unit,
+//               64-wide k block) through a 3-8 stage ring of 32 KB stages.
+//   warp 1      allocates all 512 TMEM columns (two 256-column f32 accumulators); lane
+//               0 issues the MMAs (M=128, N=256, K=16 each) and commits them to mbarriers.
+//   warps 2-17  epilogue: each thread owns one accumulator row (TMEM lane) and 64 of the
+//               unit's columns; per 32-column chunk it reads them with one tcgen05.ld,
+//               adds the bias, takes the top-2 of every head, and at the end of the unit
+//               writes winner (u8) and, when asked, runner (u8), margin (f32) and the
+//               int64 winner.
 // Every mbarrier wait gives up after ~1 s (clock64-independent %globaltimer), sets the
 // library's device error word, lets the other roles exit, drains the copies and MMAs it
 // issued (bounded again) and frees TMEM, so a protocol error cannot hang the GPU.
@@ -35,34 +40,39 @@ namespace tropnn_b200 {
 
 namespace {
 
-constexpr int kBM = 128;              // rows per CTA (MMA M, TMEM lanes)
-constexpr int kBN = 128;              // score columns per tile (MMA N)
-constexpr int kBK = 64;               // k-block width: 64 f16 = one 128-byte swizzle row
-constexpr int kStages = 8;            // router-weight ring depth
-constexpr int kTileBytesA = kBM * 128;  // one k block of the z tile
+constexpr int kBM = 128;               // rows per unit (MMA M, TMEM lanes)
+constexpr int kBN = 256;               // score columns per unit (MMA N)
+constexpr int kBK = 64;                // k-block width: 64 f16 = one 128-byte swizzle row
+constexpr int kMaxStages = 8;          // router-weight ring depth (as shared memory allows)
+constexpr int kMinStages = 3;
+constexpr int kTileBytesA = kBM * 128;  // one k block of the z block
 constexpr int kTileBytesB = kBN * 128;  // one k block of a weight tile
+constexpr int kBoxRows = 128;           // weight rows per TMA copy (two per stage)
 #ifndef TROPNN_B200_SCORE_EPILOGUE_WARPS
 #define TROPNN_B200_SCORE_EPILOGUE_WARPS 16
 #endif
 constexpr int kEpiWarps = TROPNN_B200_SCORE_EPILOGUE_WARPS;  // 8 or 16
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr int kEpiCols = kBN * 4 / kEpiWarps;  // accumulator columns per epilogue warp
-constexpr int kTmemCols = 2 * kBN;
-constexpr int kMaxKBlocks = 8;         // code_dim <= 512
+constexpr int kTmemCols = 2 * kBN;             // double-buffered accumulator: all 512 columns
+constexpr int kMaxKBlocks = 8;                 // code_dim <= 512
+constexpr size_t kSmemLimit = 227 * 1024;
 constexpr unsigned long long kWaitLimitNs = 1000ull * 1000ull * 1000ull;
 
 // Library-wide device error word: nonzero after a bounded wait gave up.
 __device__ int g_score_error = 0;
 
 struct Barriers {
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
   uint64_t a_full;
+  uint64_t a_empty;
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
+  int epi_go[2];
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -187,7 +197,53 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Named barrier 1 over the epilogue warps (barrier 0 is __syncthreads).
+__device__ __forceinline__ void epilogue_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__host__ __device__ constexpr int score_store_heads(int K) { return kEpiCols / K <= 4 ? kEpiCols / K : 32 / K; }
+
+// Score with its kIdxBits lowest bits replaced by a cell code.
+template <uint32_t kMask>
+__device__ __forceinline__ float packed_key(float score, uint32_t code) {
+  return __uint_as_float((__float_as_uint(score) & ~kMask) | code);
+}
+
+// Three-input max.f32 (PTX ISA 8.8, sm_100): one instruction instead of two.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 32 bias values from `c` on (f32, so the epilogue converts nothing; every lane reads the
+// same addresses), zero past `hk`.
+__device__ __forceinline__ void load_bias32(const float *__restrict__ bias, int64_t c, int64_t hk, float (&bv)[32]) {
+  const float *bp = bias + c;
+  if (c + 32 <= hk) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 q = __ldg(reinterpret_cast<const float4 *>(bp + i));
+      bv[i] = q.x;
+      bv[i + 1] = q.y;
+      bv[i + 2] = q.z;
+      bv[i + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) bv[i] = (c + i < hk) ? __ldg(bp + i) : 0.f;
+  }
+}
+
+// Ties registers written by tcgen05.ld to the preceding tcgen05.wait::ld, so that no use
+// of them is scheduled above the wait.
+__device__ __forceinline__ void reg_fence(float (&v)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) asm volatile("" : "+f"(v[i]));
+}
 
 constexpr int kWriteRunner = 1;
 constexpr int kWriteMargins = 2;
@@ -223,12 +279,16 @@ __device__ __forceinline__ void store_run(float *dst, const float (&v)[N]) {
 template <typename PT, int K>
 __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
     const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_w, const float *__restrict__ bias,
-    int64_t rows, int H, int kblocks, int tiles_total, int tiles_per_cta, int flags, bool vec_stores,
+    int64_t rows, int H, int kblocks, int stages, int tiles_total, int64_t units, int flags, bool vec_stores,
     int64_t *__restrict__ winner_i64, uint8_t *__restrict__ winner, uint8_t *__restrict__ runner,
     float *__restrict__ margins) {
   static_assert(32 % K == 0 && K >= 2, "cells must divide 32");
-  static_assert(kEpiCols % K == 0 && kEpiCols % 32 == 0, "an epilogue warp must own whole heads");
+  static_assert(kEpiCols % 32 == 0, "an epilogue warp reads whole 32-column chunks");
   constexpr int kHeadsPerGroup = kEpiCols / K;  // heads in one epilogue warp's columns
+  constexpr int kHeadsPerChunk = 32 / K;
+  // Heads whose routes are kept in registers before one store: the warp's whole group
+  // for 16 and 32 cells, one chunk's for fewer cells (whose groups hold many heads).
+  constexpr int kStoreHeads = score_store_heads(K);
   constexpr int kHeadsPerTile = kBN / K;
   constexpr int kIdxBits = K <= 2 ? 1 : K <= 4 ? 2 : K <= 8 ? 3 : K <= 16 ? 4 : 5;
   constexpr uint32_t kIdxMask = (1u << kIdxBits) - 1u;
@@ -237,26 +297,26 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms.
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *a_smem = smem;                                     // kblocks x [128 rows x 128 B]
-  uint8_t *b_smem = a_smem + kblocks * kTileBytesA;            // kStages x [128 rows x 128 B]
-  Barriers *bs = reinterpret_cast<Barriers *>(b_smem + kStages * kTileBytesB);
+  uint8_t *a_smem = smem;                                // kblocks x [128 rows x 128 B]
+  uint8_t *b_smem = a_smem + kblocks * kTileBytesA;      // stages x [256 rows x 128 B]
+  Barriers *bs = reinterpret_cast<Barriers *>(b_smem + stages * kTileBytesB);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t row0 = int64_t(blockIdx.x) * kBM;
-  const int tile_begin = blockIdx.y * tiles_per_cta;
-  const int tile_end = min(tiles_total, tile_begin + tiles_per_cta);
-  const int ntiles = max(0, tile_end - tile_begin);
+  // This CTA's contiguous range of the unit sequence u = row_block * tiles_total + tile.
+  const int64_t u_begin = units * blockIdx.x / gridDim.x;
+  const int64_t u_end = units * (blockIdx.x + 1) / gridDim.x;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&bs->full[s], 1);
       mbar_init(&bs->empty[s], 1);
     }
     mbar_init(&bs->a_full, 1);
+    mbar_init(&bs->a_empty, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bs->tmem_full[b], 1);
-      mbar_init(&bs->tmem_empty[b], kEpiWarps * 32);
+      mbar_init(&bs->tmem_empty[b], kEpiWarps);
     }
     mbar_init(&bs->mma_done, 1);
     bs->abort = 0;
@@ -275,42 +335,70 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
   const uint32_t tmem_base = bs->tmem_base;
 
   if (warp == 0) {
-    if (lane == 0 && ntiles > 0) {
+    if (lane == 0 && u_begin < u_end) {
       // ---------------- TMA producer ----------------
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_z)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
-      mbar_expect_tx(&bs->a_full, uint32_t(kblocks) * kTileBytesA);
-      for (int kb = 0; kb < kblocks; ++kb)
-        tma_load_2d(a_smem + kb * kTileBytesA, &map_z, &bs->a_full, kb * kBK, static_cast<int>(row0));
-      uint32_t issued[kStages];
-      for (int s = 0; s < kStages; ++s) issued[s] = 0;
+      uint32_t issued[kMaxStages];
+      for (int s = 0; s < kMaxStages; ++s) issued[s] = 0;
       bool ok = true;
-      int it = 0;
-      for (int t = 0; t < ntiles && ok; ++t) {
+      int it = 0, a_loads = 0;
+      int64_t cur_rb = -1;
+      for (int64_t u = u_begin; u < u_end && ok; ++u) {
+        const int64_t rb = u / tiles_total;
+        const int tile = static_cast<int>(u - rb * tiles_total);
+        if (rb != cur_rb) {
+          // z block of the next row block, once the MMAs have released the previous one.
+          if (a_loads > 0 && !mbar_wait(&bs->a_empty, uint32_t(a_loads - 1) & 1u, bs)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bs->a_full, uint32_t(kblocks) * kTileBytesA);
+          for (int kb = 0; kb < kblocks; ++kb)
+            tma_load_2d(a_smem + kb * kTileBytesA, &map_z, &bs->a_full, kb * kBK, static_cast<int>(rb * kBM));
+          ++a_loads;
+          cur_rb = rb;
+        }
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = it % kStages;
-          const uint32_t phase = (it / kStages) & 1;
+          const int s = it % stages;
+          const uint32_t phase = uint32_t(it / stages) & 1u;
           if (!mbar_wait(&bs->empty[s], phase ^ 1u, bs)) {
             ok = false;
             break;
           }
           mbar_expect_tx(&bs->full[s], kTileBytesB);
-          tma_load_2d(b_smem + s * kTileBytesB, &map_w, &bs->full[s], kb * kBK, (tile_begin + t) * kBN);
-          issued[s] = (it / kStages) + 1;
+          for (int q = 0; q < kBN / kBoxRows; ++q)
+            tma_load_2d(b_smem + s * kTileBytesB + q * kBoxRows * 128, &map_w, &bs->full[s], kb * kBK,
+                        tile * kBN + q * kBoxRows);
+          issued[s] = uint32_t(it / stages) + 1;
         }
       }
-      // Every copy this thread issued must land before the CTA may exit.
-      mbar_drain(&bs->a_full, 0);
-      for (int s = 0; s < kStages; ++s)
+      // Every copy this thread issued must land before the CTA may exit. A z load is only
+      // issued after the MMAs consumed the previous one, so only the last can be pending.
+      if (a_loads > 0) mbar_drain(&bs->a_full, uint32_t(a_loads - 1) & 1u);
+      for (int s = 0; s < stages; ++s)
         if (issued[s] > 0) mbar_drain(&bs->full[s], (issued[s] - 1) & 1u);
     }
   } else if (warp == 1) {
-    if (lane == 0 && ntiles > 0) {
+    if (lane == 0 && u_begin < u_end) {
       // ---------------- MMA issuer ----------------
-      bool ok = mbar_wait(&bs->a_full, 0, bs);
-      tmem_fence_after();
-      int it = 0;
-      for (int t = 0; t < ntiles && ok; ++t) {
+      bool ok = true;
+      int it = 0, a_uses = 0;
+      int64_t cur_rb = -1;
+      uint32_t t = 0;
+      for (int64_t u = u_begin; u < u_end && ok; ++u, ++t) {
+        const int64_t rb = u / tiles_total;
+        if (rb != cur_rb) {
+          // The previous z block is free once every MMA issued so far has completed.
+          if (a_uses > 0) umma_commit(&bs->a_empty);
+          if (!mbar_wait(&bs->a_full, uint32_t(a_uses) & 1u, bs)) {
+            ok = false;
+            break;
+          }
+          tmem_fence_after();
+          ++a_uses;
+          cur_rb = rb;
+        }
         const int b = t & 1;
         const uint32_t use = t >> 1;
         if (!mbar_wait(&bs->tmem_empty[b], (use & 1u) ^ 1u, bs)) {
@@ -320,8 +408,8 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
         tmem_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(b * kBN);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = it % kStages;
-          const uint32_t phase = (it / kStages) & 1;
+          const int s = it % stages;
+          const uint32_t phase = uint32_t(it / stages) & 1u;
           if (!mbar_wait(&bs->full[s], phase, bs)) {
             ok = false;
             break;
@@ -347,97 +435,105 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
     const int quarter = warp & 3;       // TMEM lane quarter this warp may access
     const int group = (warp - 2) >> 2;  // which kEpiCols columns of the tile
     const int r = quarter * 32 + lane;  // accumulator row
-    const int64_t row = row0 + r;
-    for (int t = 0; t < ntiles; ++t) {
+    const int64_t hk = int64_t(H) * K;
+    uint32_t t = 0;
+    for (int64_t u = u_begin; u < u_end; ++u, ++t) {
+      const int64_t rb = u / tiles_total;
+      const int tile = static_cast<int>(u - rb * tiles_total);
       const int b = t & 1;
       const uint32_t use = t >> 1;
-      const int tile = tile_begin + t;
       const int h0 = tile * kHeadsPerTile + group * kHeadsPerGroup;
-      // The group's bias values (f32, so the epilogue converts nothing), loaded before
-      // the wait so that their latency overlaps it.
-      float bv[kEpiCols];
-      {
-        const int64_t c0 = int64_t(tile) * kBN + group * kEpiCols;
-        const float *bp = bias + c0;
-        if (c0 + kEpiCols <= int64_t(H) * K) {
-#pragma unroll
-          for (int c = 0; c < kEpiCols; c += 4) {
-            const float4 q = __ldg(reinterpret_cast<const float4 *>(bp + c));
-            bv[c] = q.x; bv[c + 1] = q.y; bv[c + 2] = q.z; bv[c + 3] = q.w;
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < kEpiCols; ++c) bv[c] = (c0 + c < int64_t(H) * K) ? __ldg(bp + c) : 0.f;
-        }
-      }
-      // Warp-collective wait: lane 0 polls, the whole warp follows its verdict, so the
-      // .sync.aligned TMEM loads below always run converged.
-      int ok = 1;
-      if (lane == 0) ok = mbar_wait(&bs->tmem_full[b], use & 1u, bs) ? 1 : 0;
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
+      const int64_t c0 = int64_t(tile) * kBN + group * kEpiCols;
+      const int64_t row = rb * kBM + r;
+      // One epilogue thread polls the accumulator barrier and the others wait on a
+      // hardware named barrier (all epilogue warps polling slowed the TMA/MMA pipeline).
+      // The verdict passes through a two-slot flag: slot t&1 is rewritten two units later,
+      // after every epilogue warp has passed the next named barrier and so has read it.
+      // All epilogue warps thus take the same branch, and the .sync.aligned TMEM loads
+      // below run converged.
+      if (warp == 2 && lane == 0) bs->epi_go[b] = mbar_wait(&bs->tmem_full[b], use & 1u, bs) ? 1 : 0;
+      epilogue_sync();
+      if (*reinterpret_cast<volatile int *>(&bs->epi_go[b]) == 0) break;
       __syncwarp();
       tmem_fence_after();
-      float v[kEpiCols];
+      uint8_t wv[kStoreHeads], rv[kStoreHeads];
+      float mv[kStoreHeads];
+      const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(b * kBN + group * kEpiCols);
 #pragma unroll
       for (int c = 0; c < kEpiCols; c += 32) {
-        float part[32];
-        tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(b * kBN + group * kEpiCols + c), part);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[c + i] = part[i];
-      }
-      tmem_wait_ld();
-      tmem_fence_before();
-      mbar_arrive(&bs->tmem_empty[b]);
-
-      // Top-2 per head on index-packed keys: the cell index replaces the kIdxBits lowest
-      // mantissa bits of each score (K-1-k above zero, k below, so the larger key is the
-      // larger score and, between scores equal after packing, the lower cell), and two
-      // float max/min per score keep the best two keys. Routes therefore equal the fp32
-      // routes whenever the top-2 scores differ by more than 2^kIdxBits ulp (~2^-19
-      // relative for 16 cells), far inside the 1e-4 relative parity gate; the margin is
-      // the difference of the two packed keys.
-      uint8_t wv[kHeadsPerGroup], rv[kHeadsPerGroup];
-      float mv[kHeadsPerGroup];
-#pragma unroll
-      for (int hh = 0; hh < kHeadsPerGroup; ++hh) {
-        float k1 = -INFINITY, k2 = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < K; ++k) {
-          const uint32_t bits = __float_as_uint(__fadd_rn(v[hh * K + k], bv[hh * K + k]));
-          const uint32_t flip = static_cast<uint32_t>(static_cast<int32_t>(bits) >> 31) & kIdxMask;
-          const float key = __uint_as_float((bits & ~kIdxMask) | ((uint32_t(K - 1 - k)) ^ flip));
-          k2 = fmaxf(k2, fminf(k1, key));
-          k1 = fmaxf(k1, key);
+        float v[32], bv[32];
+        tmem_ld32(taddr + uint32_t(c), v);
+        load_bias32(bias, c0 + c, hk, bv);  // in flight together with the TMEM read
+        tmem_wait_ld();
+        reg_fence(v);
+        if (c + 32 == kEpiCols) {
+          // All of this warp's columns are in registers: the accumulator may be reused.
+          // One arrive per warp (512 per-thread arrives on one mbarrier per unit slowed
+          // the whole pipeline).
+          tmem_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bs->tmem_empty[b]);
         }
-        const uint32_t b1 = __float_as_uint(k1), b2 = __float_as_uint(k2);
-        const uint32_t l1 = (b1 & kIdxMask) ^ (static_cast<uint32_t>(static_cast<int32_t>(b1) >> 31) & kIdxMask);
-        const uint32_t l2 = (b2 & kIdxMask) ^ (static_cast<uint32_t>(static_cast<int32_t>(b2) >> 31) & kIdxMask);
-        wv[hh] = static_cast<uint8_t>(K - 1 - l1);
-        rv[hh] = static_cast<uint8_t>(K - 1 - l2);
-        mv[hh] = __fsub_rn(k1, k2);
-      }
-      if (row < rows) {
-        const int64_t o = row * H + h0;
-        if (vec_stores && h0 + kHeadsPerGroup <= H) {
-          // One row's consecutive heads: one or two vector stores per output per tile.
-          store_run<kHeadsPerGroup>(winner + o, wv);
-          if (flags & kWriteRunner) store_run<kHeadsPerGroup>(runner + o, rv);
-          if (flags & kWriteMargins) store_run<kHeadsPerGroup>(margins + o, mv);
-        } else {
+        // Top-2 per head on index-packed keys: the cell index K-1-k replaces the kIdxBits
+        // lowest mantissa bits of each score, which makes the K keys of a head distinct and
+        // keeps their order wherever the scores differ by more than 2^kIdxBits ulp (~2^-19
+        // relative for 16 cells, far inside the 1e-4 relative parity gate). Scores equal
+        // after packing go to the lower cell when positive, the higher when negative. The
+        // best two are found with K + 3 (K/2 - 1) min/max for K keys, three-input max.f32
+        // (sm_100) included. The margin is the difference of the two packed keys.
 #pragma unroll
-          for (int hh = 0; hh < kHeadsPerGroup; ++hh) {
-            if (h0 + hh < H) {
-              winner[o + hh] = wv[hh];
-              if (flags & kWriteRunner) runner[o + hh] = rv[hh];
-              if (flags & kWriteMargins) margins[o + hh] = mv[hh];
+        for (int hh = 0; hh < kHeadsPerChunk; ++hh) {
+          // (max, min) of every key pair, then a merge tree of best-two pairs: ILP of
+          // K/2 at the leaves, 1 + log2(K/2) dependent levels.
+          float hi[K / 2], lo[K / 2];
+#pragma unroll
+          for (int p = 0; p < K / 2; ++p) {
+            const int k = 2 * p;
+            const float x = packed_key<kIdxMask>(__fadd_rn(v[hh * K + k], bv[hh * K + k]), uint32_t(K - 1 - k));
+            const float y =
+                packed_key<kIdxMask>(__fadd_rn(v[hh * K + k + 1], bv[hh * K + k + 1]), uint32_t(K - 2 - k));
+            hi[p] = fmaxf(x, y);
+            lo[p] = fminf(x, y);
+          }
+#pragma unroll
+          for (int w = 1; w < K / 2; w *= 2) {
+#pragma unroll
+            for (int p = 0; p + w < K / 2; p += 2 * w) {
+              const float a1 = hi[p], b1 = hi[p + w];
+              lo[p] = fmax3(fminf(a1, b1), lo[p], lo[p + w]);
+              hi[p] = fmaxf(a1, b1);
             }
           }
+          const float k1 = hi[0], k2 = lo[0];
+          const uint32_t l1 = __float_as_uint(k1) & kIdxMask, l2 = __float_as_uint(k2) & kIdxMask;
+          const int g = (c / K + hh) % kStoreHeads;
+          wv[g] = static_cast<uint8_t>(K - 1 - l1);
+          rv[g] = static_cast<uint8_t>(K - 1 - l2);
+          mv[g] = __fsub_rn(k1, k2);
         }
-        if (winner_i64 != nullptr) {
+        if ((c / K + kHeadsPerChunk) % kStoreHeads == 0 && row < rows) {
+          // kStoreHeads consecutive heads of one row: vector stores where aligned.
+          const int hs = h0 + c / K + kHeadsPerChunk - kStoreHeads;
+          const int64_t o = row * H + hs;
+          if (vec_stores && hs + kStoreHeads <= H) {
+            store_run<kStoreHeads>(winner + o, wv);
+            if (flags & kWriteRunner) store_run<kStoreHeads>(runner + o, rv);
+            if (flags & kWriteMargins) store_run<kStoreHeads>(margins + o, mv);
+          } else {
 #pragma unroll
-          for (int hh = 0; hh < kHeadsPerGroup; ++hh)
-            if (h0 + hh < H) winner_i64[o + hh] = wv[hh];
+            for (int hh = 0; hh < kStoreHeads; ++hh) {
+              if (hs + hh < H) {
+                winner[o + hh] = wv[hh];
+                if (flags & kWriteRunner) runner[o + hh] = rv[hh];
+                if (flags & kWriteMargins) margins[o + hh] = mv[hh];
+              }
+            }
+          }
+          if (winner_i64 != nullptr) {
+#pragma unroll
+            for (int hh = 0; hh < kStoreHeads; ++hh)
+              if (hs + hh < H) winner_i64[o + hh] = wv[hh];
+          }
         }
       }
     }
@@ -489,8 +585,17 @@ int make_map(CUtensorMap *map, const void *ptr, CUtensorMapDataType dt, int64_t 
   return TROPNN_B200_OK;
 }
 
-size_t score_smem_bytes(int kblocks) {
-  return 1024 + size_t(kblocks) * kTileBytesA + size_t(kStages) * kTileBytesB + sizeof(Barriers);
+size_t score_smem_bytes(int kblocks, int stages) {
+  return 1024 + size_t(kblocks) * kTileBytesA + size_t(stages) * kTileBytesB + sizeof(Barriers);
+}
+
+// Weight-ring depth: the shared memory left after the resident z block, up to kMaxStages;
+// 0 when fewer than kMinStages fit.
+int score_stages(int kblocks) {
+  const size_t fixed = score_smem_bytes(kblocks, 0);
+  if (fixed >= kSmemLimit) return 0;
+  const int stages = static_cast<int>(std::min<size_t>(kMaxStages, (kSmemLimit - fixed) / kTileBytesB));
+  return stages >= kMinStages ? stages : 0;
 }
 
 template <typename PT, int K>
@@ -498,27 +603,31 @@ int launch_score(const void *z, int64_t rows, int D, const void *W, const void *
                  uint8_t *win, uint8_t *run, float *m, cudaStream_t stream) {
   const CUtensorMapDataType dt =
       std::is_same<PT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int kblocks = (D + kBK - 1) / kBK;
+  const int stages = score_stages(kblocks);
+  TB_REQUIRE(stages > 0, TROPNN_B200_ERR_INVALID, "trop_score_sm100: code_dim=%d does not fit shared memory", D);
+  const size_t smem = score_smem_bytes(kblocks, stages);
   CUtensorMap map_z, map_w;
   TB_CHECK(make_map(&map_z, z, dt, D, rows, kBM));
-  TB_CHECK(make_map(&map_w, W, dt, D, int64_t(H) * K, kBN));
-  const int kblocks = (D + kBK - 1) / kBK;
+  TB_CHECK(make_map(&map_w, W, dt, D, int64_t(H) * K, kBoxRows));
   const int tiles_total = static_cast<int>(ceil_div(int64_t(H) * K, kBN));
-  const int64_t row_blocks = ceil_div(rows, kBM);
-  // Split the score tiles of a row block over several CTAs when there are few row blocks.
-  int splits = static_cast<int>(std::min<int64_t>(tiles_total, std::max<int64_t>(1, ceil_div(2 * 148, row_blocks))));
-  const int tiles_per_cta = (tiles_total + splits - 1) / splits;
-  splits = (tiles_total + tiles_per_cta - 1) / tiles_per_cta;
-  const size_t smem = score_smem_bytes(kblocks);
+  const int64_t units = ceil_div(rows, int64_t(kBM)) * tiles_total;
+  int dev = 0, sms = 0;
+  TB_REQUIRE(cudaGetDevice(&dev) == cudaSuccess &&
+                 cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0,
+             TROPNN_B200_ERR_DEVICE, "trop_score_sm100: cannot read the SM count");
   const int flags = (run != nullptr ? kWriteRunner : 0) | (m != nullptr ? kWriteMargins : 0);
   // Vector stores need every row's run of heads to start on a multiple of its length.
-  constexpr int kRun = kEpiCols / K;
+  constexpr int kRun = score_store_heads(K);
   auto al16 = [](const void *p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   const bool vec_stores = (H % kRun == 0) && al16(win) && al16(run) && al16(m);
   auto kernel = trop_score_top2_kernel<PT, K>;
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_score_sm100"));
-  dim3 grid(static_cast<unsigned>(row_blocks), static_cast<unsigned>(splits));
-  kernel<<<grid, kThreads, smem, stream>>>(map_z, map_w, static_cast<const float *>(bias), rows, H, kblocks, tiles_total,
-                                           tiles_per_cta, flags, vec_stores, w64, win, run, m);
+  // Persistent grid: one CTA per SM (shared memory and TMEM admit no second), units
+  // split evenly.
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(units, sms));
+  kernel<<<grid, kThreads, smem, stream>>>(map_z, map_w, static_cast<const float *>(bias), rows, H, kblocks, stages,
+                                           tiles_total, units, flags, vec_stores, w64, win, run, m);
   return check_launch("trop_score_sm100");
 }
 
@@ -542,8 +651,8 @@ bool score_sm100_supported(int64_t D, int64_t K, int pt, int bias_dtype, const v
   const int64_t kblocks = (D + kBK - 1) / kBK;
   auto al16 = [](const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   return (pt == TROPNN_B200_F16 || pt == TROPNN_B200_BF16) && bias_dtype == TROPNN_B200_F32 && cells_ok &&
-         D % 8 == 0 && kblocks <= kMaxKBlocks &&
-         score_smem_bytes(static_cast<int>(kblocks)) <= 227 * 1024 && al16(z) && al16(W) && al16(bias);
+         D % 8 == 0 && kblocks <= kMaxKBlocks && score_stages(static_cast<int>(kblocks)) > 0 && al16(z) &&
+         al16(W) && al16(bias);
 }
 
 int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W, const void *bias, int pt, int64_t H,
@@ -553,6 +662,10 @@ int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W
              (long long)K, dtype_name(pt));
   if (items == 0) return TROPNN_B200_OK;
   TB_REQUIRE(z && W && bias && win, TROPNN_B200_ERR_INVALID, "trop_score_sm100: null pointer");
+  // TMA row coordinates are 32-bit.
+  TB_REQUIRE(items <= (int64_t(1) << 31) - 1024 && H * K <= (int64_t(1) << 31) - 1024, TROPNN_B200_ERR_INVALID,
+             "trop_score_sm100: %lld rows x %lld score columns exceed the 32-bit tile coordinates",
+             (long long)items, (long long)(H * K));
   const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
   if (pt == TROPNN_B200_F16) return dispatch_cells<__half>(Ki, z, items, Di, W, bias, Hi, w64, win, run, m, stream);
   return dispatch_cells<__nv_bfloat16>(Ki, z, items, Di, W, bias, Hi, w64, win, run, m, stream);
