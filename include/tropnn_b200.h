@@ -236,15 +236,27 @@ TROPNN_B200_API int tropnn_b200_trop_route(const void *latent, int latent_dtype,
  * or code[h,w] + U(m) (code[h,r] - code[h,w]), U(m) = 0.5/(1+|m|) (training)
  * (layers/tropical.py:131-138, routing.py:13-15). code in param_dtype; latent in
  * latent_dtype (F32 or the parameter dtype); hidden f32 [items, code_dim].
+ * code_t (may be NULL): code transposed to [code_dim, heads*cells] by
+ * tropnn_b200_trop_code_transpose. With it, F16/BF16 codes, U8 routes, cells in
+ * {2,4,8,16,32}, code_dim in {64,128,192,256}, heads*cells % 8 == 0 and >= 128 items,
+ * the sum runs as a one-hot GEMM on the tensor cores (tcgen05); in training the two
+ * mixing weights are then rounded to the parameter dtype. Otherwise a per-row gather.
  */
 TROPNN_B200_API int tropnn_b200_trop_hidden(const void *latent, int latent_dtype, int64_t items, int64_t code_dim,
-                            const void *code, int param_dtype, int64_t heads, int64_t cells,
+                            const void *code, const void *code_t, int param_dtype, int64_t heads, int64_t cells,
                             const void *winner, const void *runner, int index_dtype,
                             const float *margins, float code_scale, int training,
                             float *hidden, void *stream);
 
 /*
- * Reads and clears the library's device error word: 1 after a tensor-core kernel gave up
+ * code_t[d, h*cells + k] = code[h, k, d]: the K-major right operand of the tensor-core
+ * code sum (F16/BF16 only). No reference counterpart: a layout step of this backend.
+ */
+TROPNN_B200_API int tropnn_b200_trop_code_transpose(const void *code, int param_dtype, int64_t heads, int64_t cells,
+                                    int64_t code_dim, void *code_t, void *stream);
+
+/*
+ * Reads and clears the library's device error words: 1 after a tensor-core kernel gave up
  * a bounded wait (its CTA then released its resources and exited). Synchronises with the
  * device; call it off the hot path.
  */

@@ -1,0 +1,144 @@
+"""The tensor-core (one-hot GEMM) code sum against the per-row gather kernel and the oracle.
+
+tropnn_b200_trop_hidden with code_t runs sum_h code[h, route] as a tcgen05 GEMM whose left
+operand is the one-hot route matrix; without code_t the same call gathers per row. In eval
+both sum exactly the same f16/bf16 code values in f32 (order differs), so they agree to
+1e-5 relative. In training the tensor-core path rounds the two mixing weights to the
+parameter dtype: within 2e-3 (f16) / 1e-2 (bf16) relative, inside the 2e-2 half-precision
+parity tolerance.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.golden_cases import rel_err
+from tropnn_b200 import _native as nat
+
+pytestmark = pytest.mark.gpu
+
+TRAIN_TOL = {torch.float16: 2e-3, torch.bfloat16: 1e-2}
+
+
+def _routes(items: int, heads: int, cells: int, gen: torch.Generator) -> tuple[torch.Tensor, ...]:
+    winner = torch.randint(0, cells, (items, heads), generator=gen)
+    shift = torch.randint(1, cells, (items, heads), generator=gen)
+    runner = (winner + shift) % cells  # distinct from the winner
+    margins = torch.rand(items, heads, generator=gen) * 3.0
+    return winner.to(torch.uint8), runner.to(torch.uint8), margins
+
+
+def _hidden(latent, code, winner, runner, margins, code_scale, training, use_tc):
+    lib = nat.load()
+    items, code_dim = latent.shape
+    heads, cells, _ = code.shape
+    stream = torch.cuda.current_stream().cuda_stream
+    code_t = None
+    if use_tc:
+        code_t = torch.empty((code_dim, heads * cells), device=code.device, dtype=code.dtype)
+        nat.check(
+            lib.tropnn_b200_trop_code_transpose(
+                code.data_ptr(), nat.float_code(code.dtype), heads, cells, code_dim, code_t.data_ptr(), stream
+            ),
+            "trop_code_transpose",
+        )
+    hidden = torch.empty((items, code_dim), device=latent.device, dtype=torch.float32)
+    nat.check(
+        lib.tropnn_b200_trop_hidden(
+            latent.data_ptr(), nat.float_code(latent.dtype), items, code_dim, code.data_ptr(), nat.ptr(code_t),
+            nat.float_code(code.dtype), heads, cells, winner.data_ptr(), runner.data_ptr(), nat.U8,
+            margins.data_ptr(), float(code_scale), int(training), hidden.data_ptr(), stream,
+        ),
+        "trop_hidden",
+    )
+    torch.cuda.synchronize()
+    return hidden.cpu().numpy()
+
+
+def _oracle_hidden(latent, code, winner, runner, margins, code_scale, training):
+    z = latent.float().cpu().numpy()
+    c = code.float().cpu().numpy()
+    w = winner.long().cpu().numpy()
+    r = runner.long().cpu().numpy()
+    m = margins.cpu().numpy()
+    heads = c.shape[0]
+    head_ix = np.arange(heads)[None, :]
+    values = c[head_ix, w]
+    if training:
+        values = oracle.minface_mix(values, c[head_ix, r], m)
+    return (z + values.sum(axis=1, dtype=np.float32) * np.float32(code_scale)).astype(np.float32)
+
+
+def _check(items, heads, cells, code_dim, dtype, training, latent_f32=False, seed=0):
+    gen = torch.Generator().manual_seed(seed)
+    latent = torch.randn(items, code_dim, generator=gen).to(torch.float32 if latent_f32 else dtype).cuda()
+    code = (torch.randn(heads, cells, code_dim, generator=gen) * 0.5).to(dtype).cuda()
+    winner, runner, margins = (t.cuda() for t in _routes(items, heads, cells, gen))
+    scale = heads**-0.5
+    tc = _hidden(latent, code, winner, runner, margins, scale, training, use_tc=True)
+    simt = _hidden(latent, code, winner, runner, margins, scale, training, use_tc=False)
+    ref = _oracle_hidden(latent, code, winner, runner, margins, scale, training)
+    assert np.isfinite(tc).all()
+    tol = TRAIN_TOL[dtype] if training else 1e-5
+    assert rel_err(tc, simt) <= tol
+    assert rel_err(tc, ref) <= tol
+    assert rel_err(simt, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("training", [False, True])
+def test_config5_shape(dtype, training):
+    """Config 5's code table: H1024, K16, D256 (256 k blocks per row block)."""
+    _check(items=640, heads=1024, cells=16, code_dim=256, dtype=dtype, training=training)
+
+
+@pytest.mark.parametrize("cells", [2, 4, 8, 16, 32])
+def test_cells(cells):
+    _check(items=256, heads=max(4, 512 // cells), cells=cells, code_dim=128, dtype=torch.float16, training=False)
+    _check(items=256, heads=max(4, 512 // cells), cells=cells, code_dim=128, dtype=torch.float16, training=True)
+
+
+@pytest.mark.parametrize(
+    ("items", "heads", "cells", "code_dim"),
+    [
+        (300, 12, 16, 64),  # ragged rows, 3 k blocks with a partial last one
+        (1000, 200, 8, 192),  # many row blocks, N=192
+        (129, 20, 2, 64),  # one live row in the last block, 40 entries (one partial k block)
+        (20000, 64, 16, 128),  # ~1 row block per CTA and more: the persistent loop
+    ],
+)
+def test_ragged_shapes(items, heads, cells, code_dim):
+    _check(items, heads, cells, code_dim, torch.float16, training=False)
+    _check(items, heads, cells, code_dim, torch.bfloat16, training=True)
+
+
+def test_f32_latent():
+    """F32 latent with half-precision codes (the reference's upcast z) takes the same path."""
+    _check(items=512, heads=64, cells=16, code_dim=256, dtype=torch.float16, training=False, latent_f32=True)
+
+
+def test_code_transpose():
+    gen = torch.Generator().manual_seed(3)
+    code = torch.randn(37, 8, 96, generator=gen).half().cuda()
+    out = torch.empty(96, 37 * 8, dtype=torch.float16, device="cuda")
+    lib = nat.load()
+    nat.check(
+        lib.tropnn_b200_trop_code_transpose(
+            code.data_ptr(), nat.F16, 37, 8, 96, out.data_ptr(), torch.cuda.current_stream().cuda_stream
+        ),
+        "trop_code_transpose",
+    )
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), code.reshape(37 * 8, 96).t().cpu())
+
+
+def test_no_device_error_after_tensor_core_runs():
+    import ctypes
+
+    _check(items=512, heads=64, cells=16, code_dim=128, dtype=torch.float16, training=True)
+    flag = ctypes.c_int(-1)
+    nat.check(nat.load().tropnn_b200_device_error(ctypes.byref(flag)), "device_error")
+    assert flag.value == 0

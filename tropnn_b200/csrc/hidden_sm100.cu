@@ -1,0 +1,484 @@
+// TropLinear selected-code sum on the sm_100a tensor cores. With half-precision codes the
+// gather-sum of layers/tropical.py:131-138 is a GEMM with a one-hot left operand:
+//   hidden[n,:] = latent[n,:] + code_scale * sum_{h,k} P[n,(h,k)] * code[h,k,:]
+//   P[n,(h,k)] = 1 at the winner cell (eval), or 1-U(m) at the winner and U(m) at the
+//   runner-up (training, the min-face mix of routing.py:13-15, U(m) = 0.5/(1+|m|)).
+// A 128-row block of items then streams the code table once through the tensor cores
+// (tcgen05, f32 accumulation in TMEM) instead of gathering heads x code_dim values per
+// item: the gather's L2 traffic shrinks by a factor of 128 / cells-per-k-block.
+//
+// Eval is exact up to f32 summation order: P is 0/1 and every product is a code value.
+// In training the two mixing weights are rounded to the parameter dtype (relative error
+// 2^-11 for f16, 2^-8 for bf16), far inside the 2e-2 tolerance of half-precision layers.
+//
+// Operands: B = code^T [code_dim, heads*cells] (K-major, built by trop_code_transpose),
+// loaded by TMA in 64-wide k blocks; A = the one-hot block, built in registers from the
+// u8 routes and written straight into TMEM (tcgen05.st), so it never touches shared
+// memory: the MMA reads A from TMEM and B from shared memory.
+//
+// CTA = 10 warps, persistent over row blocks rb = blockIdx.x + i * gridDim.x:
+//   warp 0      TMA producer of the code^T k blocks (3-8 stage ring, D x 128 B each).
+//   warp 1      allocates all 512 TMEM columns (accumulator [0, D), one-hot ring
+//               [256, 512): 8 slots of 32 columns); lane 0 issues the MMAs (M=128,
+//               N=code_dim, K=16, A from TMEM) and commits them to mbarriers.
+//   warps 2-5   build the one-hot k blocks: one thread per row, 32 packed f16/bf16 pairs
+//               per k block, stored with tcgen05.st into the thread's TMEM lane.
+//   warps 6-9   epilogue: hidden = latent + code_scale * acc for the thread's row.
+// All waits are bounded (sm100.cuh); waits by whole warps of builders and epilogue use
+// mbarrier suspend hints instead of spinning, which kept the TMA/MMA pipeline at rate.
+#include <cuda.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace tropnn_b200 {
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kBM = 128;                 // rows per row block (MMA M, TMEM lanes)
+constexpr int kBK = 64;                  // (head, cell) entries per k block
+constexpr int kMaxD = 256;               // MMA N = code_dim
+constexpr int kMaxBStages = 8;
+constexpr int kMinBStages = 3;
+constexpr int kAStages = 8;              // one-hot ring slots in TMEM
+constexpr int kBuildWarps = 4;           // one per TMEM lane quarter
+constexpr int kEpiWarps = 4;             // one per TMEM lane quarter
+constexpr int kThreads = 32 * (2 + kBuildWarps + kEpiWarps);
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAColBase = 256;      // one-hot ring after the (<= 256-column) accumulator
+constexpr size_t kSmemLimit = 227 * 1024;
+constexpr uint32_t kSleepHintNs = 1000000u;
+
+// Library-wide device error word of this kernel: nonzero after a bounded wait gave up.
+__device__ int g_hidden_error = 0;
+
+struct Barriers {
+  uint64_t b_full[kMaxBStages];
+  uint64_t b_empty[kMaxBStages];
+  uint64_t a_full[kAStages];
+  uint64_t a_empty[kAStages];
+  uint64_t acc_full;
+  uint64_t acc_empty;
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, Barriers *bs) {
+  return sm100::mbar_wait(bar, parity, &bs->abort, &g_hidden_error);
+}
+
+// Bounded wait that suspends the thread between polls (mbarrier suspend-time hint).
+__device__ __forceinline__ bool wait_bar_sleep(uint64_t *bar, uint32_t parity, Barriers *bs) {
+  const uint64_t start = global_ns();
+  volatile int *abort = &bs->abort;
+  for (;;) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(kSleepHintNs)
+        : "memory");
+    if (ok) return true;
+    if (*abort) return false;
+    if (global_ns() - start > kWaitLimitNs) {
+      *abort = 1;
+      atomicExch(&g_hidden_error, 1);
+      return false;
+    }
+  }
+}
+
+// Warp-collective form: lane 0 waits, the warp follows its verdict (converged after).
+__device__ __forceinline__ bool warp_wait_sleep(uint64_t *bar, uint32_t parity, Barriers *bs, int lane) {
+  int ok = 1;
+  if (lane == 0) ok = wait_bar_sleep(bar, parity, bs) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
+template <typename PT>
+struct HalfBits;
+template <>
+struct HalfBits<__half> {
+  static constexpr uint32_t kOne = 0x3C00u;
+  static constexpr int kFormat = 0;
+  __device__ static uint32_t bits(float x) { return __half_as_ushort(__float2half_rn(x)); }
+};
+template <>
+struct HalfBits<__nv_bfloat16> {
+  static constexpr uint32_t kOne = 0x3F80u;
+  static constexpr int kFormat = 1;
+  __device__ static uint32_t bits(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+};
+
+// 32 latent values of one row as f32.
+template <typename LT>
+__device__ __forceinline__ void load_row32(const LT *__restrict__ p, float (&out)[32]) {
+  if constexpr (std::is_same<LT, float>::value) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 q = __ldg(reinterpret_cast<const float4 *>(p + i));
+      out[i] = q.x;
+      out[i + 1] = q.y;
+      out[i + 2] = q.z;
+      out[i + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+      float t[8];
+      VecLoad<LT, 8>::load(p + i, t);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) out[i + e] = t[e];
+    }
+  }
+}
+
+template <typename PT, typename LT, int K, bool TRAIN>
+__global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
+    const __grid_constant__ CUtensorMap map_ct, const LT *__restrict__ latent, const uint8_t *__restrict__ winner,
+    const uint8_t *__restrict__ runner, const float *__restrict__ margins, float code_scale, int64_t rows, int H,
+    int D, int kblocks, int bstages, int64_t row_blocks, float *__restrict__ hidden) {
+  static_assert(K >= 2 && K <= kBK && K % 2 == 0, "cells must be even and at most 64");
+  constexpr int kHeadsPerBlock = kBK / K;
+  constexpr uint32_t kOne = HalfBits<PT>::kOne;
+  const uint32_t idesc = umma_idesc_f16(HalfBits<PT>::kFormat, kBM, D);
+  const int b_stage_bytes = D * 128;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *b_smem = smem;  // bstages x [D rows x 128 B], K-major, 128-byte swizzle
+  Barriers *bs = reinterpret_cast<Barriers *>(b_smem + bstages * b_stage_bytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < bstages; ++s) {
+      mbar_init(&bs->b_full[s], 1);
+      mbar_init(&bs->b_empty[s], 1);
+    }
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(&bs->a_full[s], kBuildWarps);
+      mbar_init(&bs->a_empty[s], 1);
+    }
+    mbar_init(&bs->acc_full, 1);
+    mbar_init(&bs->acc_empty, kEpiWarps);
+    mbar_init(&bs->mma_done, 1);
+    bs->abort = 0;
+    mbar_init_fence();
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(&bs->tmem_base, kTmemCols);
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem_base = bs->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer: code^T k blocks ----------------
+      prefetch_map(&map_ct);
+      uint32_t issued[kMaxBStages];
+      for (int s = 0; s < kMaxBStages; ++s) issued[s] = 0;
+      bool ok = true;
+      int it = 0;
+      for (int64_t rb = blockIdx.x; rb < row_blocks && ok; rb += gridDim.x) {
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % bstages;
+          const uint32_t phase = uint32_t(it / bstages) & 1u;
+          if (!wait_bar(&bs->b_empty[s], phase ^ 1u, bs)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bs->b_full[s], uint32_t(b_stage_bytes));
+          tma_load_2d(b_smem + s * b_stage_bytes, &map_ct, &bs->b_full[s], kb * kBK, 0);
+          issued[s] = uint32_t(it / bstages) + 1;
+        }
+      }
+      for (int s = 0; s < bstages; ++s)
+        if (issued[s] > 0) mbar_drain(&bs->b_full[s], (issued[s] - 1) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      bool ok = true;
+      int bit = 0, ait = 0;
+      uint32_t i = 0;
+      for (int64_t rb = blockIdx.x; rb < row_blocks && ok; rb += gridDim.x, ++i) {
+        if (!wait_bar(&bs->acc_empty, (i & 1u) ^ 1u, bs)) {
+          ok = false;
+          break;
+        }
+        tmem_fence_after();
+        for (int kb = 0; kb < kblocks; ++kb, ++bit, ++ait) {
+          const int sa = ait % kAStages, sb = bit % bstages;
+          if (!wait_bar(&bs->a_full[sa], uint32_t(ait / kAStages) & 1u, bs) ||
+              !wait_bar(&bs->b_full[sb], uint32_t(bit / bstages) & 1u, bs)) {
+            ok = false;
+            break;
+          }
+          tmem_fence_after();
+          const uint32_t b_base = smem_addr(b_smem + sb * b_stage_bytes);
+          const uint32_t a_col = tmem_base + kAColBase + uint32_t(sa * 32);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16_tmem_a(tmem_base, a_col + uint32_t(kk * 8), umma_desc_sw128(b_base + kk * 32), idesc,
+                            (kb | kk) != 0 ? 1u : 0u);
+          umma_commit(&bs->a_empty[sa]);
+          umma_commit(&bs->b_empty[sb]);
+        }
+        if (!ok) break;
+        umma_commit(&bs->acc_full);
+      }
+      // All MMAs issued by this thread must finish before TMEM is freed.
+      umma_commit(&bs->mma_done);
+      mbar_drain(&bs->mma_done, 0);
+    }
+  } else if (warp < 2 + kBuildWarps) {
+    // ---------------- one-hot builders ----------------
+    const int quarter = warp & 3;
+    const uint32_t lane_base = tmem_base + (uint32_t(quarter * 32) << 16) + kAColBase;
+    int ait = 0;
+    bool ok = true;
+    for (int64_t rb = blockIdx.x; rb < row_blocks && ok; rb += gridDim.x) {
+      const int64_t row = rb * kBM + quarter * 32 + lane;
+      const bool live = row < rows;
+      const uint8_t *wrow = winner + (live ? row : 0) * H;
+      const uint8_t *rrow = TRAIN ? runner + (live ? row : 0) * H : nullptr;
+      const float *mrow = TRAIN ? margins + (live ? row : 0) * H : nullptr;
+      for (int kb = 0; kb < kblocks; ++kb, ++ait) {
+        const int sa = ait % kAStages;
+        // Route bytes first, so their latency overlaps the wait for the slot.
+        uint32_t wc[kHeadsPerBlock], rc[kHeadsPerBlock], vw[kHeadsPerBlock], vr[kHeadsPerBlock];
+#pragma unroll
+        for (int hh = 0; hh < kHeadsPerBlock; ++hh) {
+          const int h = kb * kHeadsPerBlock + hh;
+          wc[hh] = 0xFFu;
+          rc[hh] = 0xFFu;
+          vw[hh] = kOne;
+          vr[hh] = 0u;
+          if (live && h < H) {
+            wc[hh] = __ldg(wrow + h);
+            if constexpr (TRAIN) {
+              rc[hh] = __ldg(rrow + h);
+              const float alpha = __fdiv_rn(0.5f, __fadd_rn(1.f, fabsf(__ldg(mrow + h))));
+              vw[hh] = HalfBits<PT>::bits(__fsub_rn(1.f, alpha));
+              vr[hh] = HalfBits<PT>::bits(alpha);
+            }
+          }
+        }
+        if (!warp_wait_sleep(&bs->a_empty[sa], (uint32_t(ait / kAStages) & 1u) ^ 1u, bs, lane)) {
+          ok = false;
+          break;
+        }
+        tmem_fence_after();
+        // Column j of the k block holds entries 2j (low half) and 2j+1 (high half); both
+        // belong to head j / (K/2), cells 2 (j % (K/2)) and that + 1.
+        uint32_t reg[32];
+#pragma unroll
+        for (int hh = 0; hh < kHeadsPerBlock; ++hh) {
+#pragma unroll
+          for (int jj = 0; jj < K / 2; ++jj) {
+            const uint32_t c0 = 2u * jj, c1 = c0 + 1u;
+            uint32_t lo = wc[hh] == c0 ? vw[hh] : 0u;
+            uint32_t hi = wc[hh] == c1 ? vw[hh] : 0u;
+            if constexpr (TRAIN) {
+              lo |= rc[hh] == c0 ? vr[hh] : 0u;
+              hi |= rc[hh] == c1 ? vr[hh] : 0u;
+            }
+            reg[hh * (K / 2) + jj] = lo | (hi << 16);
+          }
+        }
+        tmem_st32(lane_base + uint32_t(sa * 32), reg);
+        tmem_wait_st();
+        tmem_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bs->a_full[sa]);
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int quarter = warp & 3;
+    const uint32_t lane_base = tmem_base + (uint32_t(quarter * 32) << 16);
+    uint32_t i = 0;
+    for (int64_t rb = blockIdx.x; rb < row_blocks; rb += gridDim.x, ++i) {
+      const int64_t row = rb * kBM + quarter * 32 + lane;
+      if (!warp_wait_sleep(&bs->acc_full, i & 1u, bs, lane)) break;
+      tmem_fence_after();
+      for (int c = 0; c < D; c += 32) {
+        float acc[32];
+        tmem_ld32(lane_base + uint32_t(c), acc);
+        float lat[32];
+        if (row < rows) load_row32<LT>(latent + row * D + c, lat);
+        tmem_wait_ld();
+        reg_fence(acc);
+        if (c + 32 >= D) {
+          // The accumulator is in registers: the next row block may start.
+          tmem_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bs->acc_empty);
+        }
+        if (row < rows) {
+          float *out = hidden + row * D + c;
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4 *>(out + e) = make_float4(
+                __fadd_rn(lat[e], __fmul_rn(acc[e], code_scale)), __fadd_rn(lat[e + 1], __fmul_rn(acc[e + 1], code_scale)),
+                __fadd_rn(lat[e + 2], __fmul_rn(acc[e + 2], code_scale)),
+                __fadd_rn(lat[e + 3], __fmul_rn(acc[e + 3], code_scale)));
+        }
+      }
+    }
+  }
+
+  tmem_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// code [rows_in, cols_in] -> code_t [cols_in, rows_in] (32 x 32 tiles through shared memory).
+template <typename PT>
+__global__ void __launch_bounds__(256) transpose_kernel(const PT *__restrict__ in, PT *__restrict__ out,
+                                                        int64_t rows_in, int cols_in) {
+  __shared__ PT tile[32][33];
+  const int64_t r0 = int64_t(blockIdx.x) * 32;
+  const int c0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int j = ty; j < 32; j += 8)
+    if (r0 + j < rows_in && c0 + tx < cols_in) tile[j][tx] = in[(r0 + j) * cols_in + c0 + tx];
+  __syncthreads();
+  for (int j = ty; j < 32; j += 8)
+    if (c0 + j < cols_in && r0 + tx < rows_in) out[int64_t(c0 + j) * rows_in + r0 + tx] = tile[tx][j];
+}
+
+int b_stages(int D) {
+  const size_t stage = size_t(D) * 128;
+  const size_t room = kSmemLimit - 1024 - sizeof(Barriers);
+  const int s = static_cast<int>(std::min<size_t>(kMaxBStages, room / stage));
+  return s >= kMinBStages ? s : 0;
+}
+
+template <typename PT, typename LT, int K>
+int launch_onehot(const void *latent, int64_t rows, int D, const void *code_t, int H, const uint8_t *win,
+                  const uint8_t *run, const float *m, float code_scale, bool training, float *hidden,
+                  cudaStream_t stream) {
+  const CUtensorMapDataType dt =
+      std::is_same<PT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int64_t hk = int64_t(H) * K;
+  CUtensorMap map_ct;
+  TB_CHECK(make_map_k64(&map_ct, code_t, dt, hk, D, D));
+  const int kblocks = static_cast<int>(ceil_div(hk, int64_t(kBK)));
+  const int bst = b_stages(D);
+  // At least half of the SM's shared memory, so that no second CTA shares the SM: each
+  // CTA allocates all 512 TMEM columns.
+  const size_t smem = std::max<size_t>(1024 + size_t(bst) * D * 128 + sizeof(Barriers), 120 * 1024);
+  const int64_t row_blocks = ceil_div(rows, int64_t(kBM));
+  int sms = 0;
+  TB_CHECK(sm_count(&sms));
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(row_blocks, sms));
+  auto kernel = training ? trop_hidden_onehot_kernel<PT, LT, K, true> : trop_hidden_onehot_kernel<PT, LT, K, false>;
+  TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_hidden_sm100"));
+  kernel<<<grid, kThreads, smem, stream>>>(map_ct, static_cast<const LT *>(latent), win, run, m, code_scale, rows, H, D,
+                                           kblocks, bst, row_blocks, hidden);
+  return check_launch("trop_hidden_sm100");
+}
+
+template <typename PT, typename LT>
+int dispatch_onehot(int K, const void *latent, int64_t rows, int D, const void *code_t, int H, const uint8_t *win,
+                    const uint8_t *run, const float *m, float code_scale, bool training, float *hidden,
+                    cudaStream_t stream) {
+  switch (K) {
+    case 2: return launch_onehot<PT, LT, 2>(latent, rows, D, code_t, H, win, run, m, code_scale, training, hidden, stream);
+    case 4: return launch_onehot<PT, LT, 4>(latent, rows, D, code_t, H, win, run, m, code_scale, training, hidden, stream);
+    case 8: return launch_onehot<PT, LT, 8>(latent, rows, D, code_t, H, win, run, m, code_scale, training, hidden, stream);
+    case 16:
+      return launch_onehot<PT, LT, 16>(latent, rows, D, code_t, H, win, run, m, code_scale, training, hidden, stream);
+    default:
+      return launch_onehot<PT, LT, 32>(latent, rows, D, code_t, H, win, run, m, code_scale, training, hidden, stream);
+  }
+}
+
+}  // namespace
+
+bool hidden_sm100_supported(int64_t items, int64_t D, int64_t H, int64_t K, int pt, int zt, int it, const void *latent,
+                            const void *code_t, const void *hidden) {
+  const bool cells_ok = K == 2 || K == 4 || K == 8 || K == 16 || K == 32;
+  auto al16 = [](const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  return code_t != nullptr && (pt == TROPNN_B200_F16 || pt == TROPNN_B200_BF16) && (zt == pt || zt == TROPNN_B200_F32) &&
+         it == TROPNN_B200_U8 && cells_ok && D % 64 == 0 && D >= 64 && D <= kMaxD && (H * K) % 8 == 0 &&
+         items >= kBM && b_stages(static_cast<int>(D)) > 0 && al16(latent) && al16(code_t) && al16(hidden);
+}
+
+int trop_hidden_sm100_impl(const void *latent, int zt, int64_t items, int64_t D, const void *code_t, int pt,
+                           int64_t H, int64_t K, const void *win, const void *run, const float *m, float code_scale,
+                           int training, float *hidden, cudaStream_t stream) {
+  TB_REQUIRE(hidden_sm100_supported(items, D, H, K, pt, zt, TROPNN_B200_U8, latent, code_t, hidden),
+             TROPNN_B200_ERR_INVALID, "trop_hidden_sm100: unsupported shape, dtype or alignment");
+  TB_REQUIRE(win && (!training || (run && m)), TROPNN_B200_ERR_INVALID, "trop_hidden_sm100: null pointer");
+  const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
+  const auto *w = static_cast<const uint8_t *>(win);
+  const auto *r = static_cast<const uint8_t *>(run);
+  const bool train = training != 0;
+  if (pt == TROPNN_B200_F16) {
+    if (zt == TROPNN_B200_F32)
+      return dispatch_onehot<__half, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, train, hidden,
+                                            stream);
+    return dispatch_onehot<__half, __half>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, train, hidden,
+                                           stream);
+  }
+  if (zt == TROPNN_B200_F32)
+    return dispatch_onehot<__nv_bfloat16, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, train, hidden,
+                                                 stream);
+  return dispatch_onehot<__nv_bfloat16, __nv_bfloat16>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, train,
+                                                       hidden, stream);
+}
+
+int trop_code_transpose_impl(const void *code, int pt, int64_t H, int64_t K, int64_t D, void *code_t,
+                             cudaStream_t stream) {
+  TB_REQUIRE(pt == TROPNN_B200_F16 || pt == TROPNN_B200_BF16, TROPNN_B200_ERR_DTYPE,
+             "trop_code_transpose: param dtype %s unsupported (f16/bf16 only)", dtype_name(pt));
+  TB_REQUIRE(H > 0 && K > 0 && D > 0 && D <= (1 << 20) && H * K < (int64_t(1) << 36), TROPNN_B200_ERR_INVALID,
+             "trop_code_transpose: bad shape heads=%lld cells=%lld code_dim=%lld", (long long)H, (long long)K,
+             (long long)D);
+  TB_REQUIRE(code && code_t, TROPNN_B200_ERR_INVALID, "trop_code_transpose: null pointer");
+  const int64_t rows_in = H * K;
+  const dim3 grid(static_cast<unsigned>(ceil_div(rows_in, int64_t(32))), static_cast<unsigned>(ceil_div(D, int64_t(32))));
+  if (pt == TROPNN_B200_F16)
+    transpose_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half *>(code), static_cast<__half *>(code_t),
+                                                       rows_in, static_cast<int>(D));
+  else
+    transpose_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16 *>(code),
+                                                              static_cast<__nv_bfloat16 *>(code_t), rows_in,
+                                                              static_cast<int>(D));
+  return check_launch("trop_code_transpose");
+}
+
+int read_hidden_error(int *value) {
+  int v = 0;
+  cudaError_t err = cudaMemcpyFromSymbol(&v, g_hidden_error, sizeof(int));
+  if (err != cudaSuccess)
+    return set_error(TROPNN_B200_ERR_LAUNCH, "reading the device error word: %s", cudaGetErrorString(err));
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_hidden_error, &zero, sizeof(int));
+  }
+  *value = v;
+  return TROPNN_B200_OK;
+}
+
+}  // namespace tropnn_b200

@@ -31,14 +31,16 @@
 // delivery, no peer memory), so the kernel is safe in multi-GPU processes.
 #include <cuda.h>
 
-#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace tropnn_b200 {
 
 namespace {
+
+using namespace sm100;
 
 constexpr int kBM = 128;               // rows per unit (MMA M, TMEM lanes)
 constexpr int kBN = 256;               // score columns per unit (MMA N)
@@ -57,7 +59,6 @@ constexpr int kEpiCols = kBN * 4 / kEpiWarps;  // accumulator columns per epilog
 constexpr int kTmemCols = 2 * kBN;             // double-buffered accumulator: all 512 columns
 constexpr int kMaxKBlocks = 8;                 // code_dim <= 512
 constexpr size_t kSmemLimit = 227 * 1024;
-constexpr unsigned long long kWaitLimitNs = 1000ull * 1000ull * 1000ull;
 
 // Library-wide device error word: nonzero after a bounded wait gave up.
 __device__ int g_score_error = 0;
@@ -75,134 +76,13 @@ struct Barriers {
   int epi_go[2];
 };
 
-__device__ __forceinline__ uint32_t smem_addr(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait for phase `parity` of `bar`. Returns false (and raises the CTA abort flag
-// and the device error word) after kWaitLimitNs, or false at once if another role aborted.
-__device__ bool mbar_wait(uint64_t *bar, uint32_t parity, Barriers *bs) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = global_ns();
-  volatile int *abort = &bs->abort;
-  for (uint32_t spin = 1;; ++spin) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((spin & 255u) == 0) {
-      if (*abort) return false;
-      if (global_ns() - start > kWaitLimitNs) {
-        *abort = 1;
-        atomicExch(&g_score_error, 1);
-        return false;
-      }
-    }
-  }
-}
-
-// Drain-only wait used on the abort path: bounded, never raises anything.
-__device__ void mbar_drain(uint64_t *bar, uint32_t parity) {
-  const uint64_t start = global_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - start > kWaitLimitNs) return;
-  }
-}
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-
-// UMMA shared-memory descriptor, K-major operand in the 128-byte swizzle layout: rows of
-// 128 bytes, 8-row groups 1024 bytes apart (SBO), version 1, swizzle mode 2.
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= uint64_t((saddr >> 4) & 0x3FFFu);
-  d |= uint64_t(1) << 16;           // leading byte offset (unused for swizzled K-major)
-  d |= uint64_t(1024 >> 4) << 32;   // stride byte offset
-  d |= uint64_t(1) << 46;           // descriptor version (sm_100)
-  d |= uint64_t(2) << 61;           // SWIZZLE_128B
-  return d;
-}
-
-// Instruction descriptor of kind::f16: f32 accumulator, A/B f16 (0) or bf16 (1), both
-// K-major, N and M in their encoded fields.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(int ab_format, int m, int n) {
-  return (1u << 4) | (uint32_t(ab_format) << 7) | (uint32_t(ab_format) << 10) | (uint32_t(n >> 3) << 17) |
-         (uint32_t(m >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 32 consecutive f32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+// Bounded mbarrier wait bound to this CTA's abort flag and the kernel's error word.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, Barriers *bs) {
+  return sm100::mbar_wait(bar, parity, &bs->abort, &g_score_error);
 }
 
 // Named barrier 1 over the epilogue warps (barrier 0 is __syncthreads).
-__device__ __forceinline__ void epilogue_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void epilogue_sync() { named_sync(1, kEpiWarps * 32); }
 
 __host__ __device__ constexpr int score_store_heads(int K) { return kEpiCols / K <= 4 ? kEpiCols / K : 32 / K; }
 
@@ -236,13 +116,6 @@ __device__ __forceinline__ void load_bias32(const float *__restrict__ bias, int6
 #pragma unroll
     for (int i = 0; i < 32; ++i) bv[i] = (c + i < hk) ? __ldg(bp + i) : 0.f;
   }
-}
-
-// Ties registers written by tcgen05.ld to the preceding tcgen05.wait::ld, so that no use
-// of them is scheduled above the wait.
-__device__ __forceinline__ void reg_fence(float (&v)[32]) {
-#pragma unroll
-  for (int i = 0; i < 32; ++i) asm volatile("" : "+f"(v[i]));
 }
 
 constexpr int kWriteRunner = 1;
@@ -320,14 +193,11 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
     }
     mbar_init(&bs->mma_done, 1);
     bs->abort = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_init_fence();
   }
   if (warp == 1) {
     __syncwarp();
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&bs->tmem_base)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tmem_alloc(&bs->tmem_base, kTmemCols);
   }
   tmem_fence_before();
   __syncthreads();
@@ -337,8 +207,8 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
   if (warp == 0) {
     if (lane == 0 && u_begin < u_end) {
       // ---------------- TMA producer ----------------
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_z)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
+      prefetch_map(&map_z);
+      prefetch_map(&map_w);
       uint32_t issued[kMaxStages];
       for (int s = 0; s < kMaxStages; ++s) issued[s] = 0;
       bool ok = true;
@@ -544,46 +414,11 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
   if (warp == 1) {
     __syncwarp();
     tmem_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
 // --------------------------------------------------------------------------- host side
-
-using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-int encode_fn(EncodeTiledFn *out) {
-  static std::once_flag once;
-  static EncodeTiledFn fn = nullptr;
-  static cudaError_t err = cudaSuccess;
-  std::call_once(once, [] {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  if (fn == nullptr)
-    return set_error(TROPNN_B200_ERR_DEVICE, "cuTensorMapEncodeTiled unavailable: %s", cudaGetErrorString(err));
-  *out = fn;
-  return TROPNN_B200_OK;
-}
-
-// 2-D K-major tensor map over a row-major [outer, inner] half-precision matrix, boxes of
-// 64 x box_rows with the 128-byte swizzle; out-of-range elements read as zero.
-int make_map(CUtensorMap *map, const void *ptr, CUtensorMapDataType dt, int64_t inner, int64_t outer, int box_rows) {
-  EncodeTiledFn fn = nullptr;
-  TB_CHECK(encode_fn(&fn));
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * 2};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, dt, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(TROPNN_B200_ERR_LAUNCH, "cuTensorMapEncodeTiled failed (%d)", int(r));
-  return TROPNN_B200_OK;
-}
 
 size_t score_smem_bytes(int kblocks, int stages) {
   return 1024 + size_t(kblocks) * kTileBytesA + size_t(stages) * kTileBytesB + sizeof(Barriers);
@@ -608,14 +443,12 @@ int launch_score(const void *z, int64_t rows, int D, const void *W, const void *
   TB_REQUIRE(stages > 0, TROPNN_B200_ERR_INVALID, "trop_score_sm100: code_dim=%d does not fit shared memory", D);
   const size_t smem = score_smem_bytes(kblocks, stages);
   CUtensorMap map_z, map_w;
-  TB_CHECK(make_map(&map_z, z, dt, D, rows, kBM));
-  TB_CHECK(make_map(&map_w, W, dt, D, int64_t(H) * K, kBoxRows));
+  TB_CHECK(make_map_k64(&map_z, z, dt, D, rows, kBM));
+  TB_CHECK(make_map_k64(&map_w, W, dt, D, int64_t(H) * K, kBoxRows));
   const int tiles_total = static_cast<int>(ceil_div(int64_t(H) * K, kBN));
   const int64_t units = ceil_div(rows, int64_t(kBM)) * tiles_total;
-  int dev = 0, sms = 0;
-  TB_REQUIRE(cudaGetDevice(&dev) == cudaSuccess &&
-                 cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0,
-             TROPNN_B200_ERR_DEVICE, "trop_score_sm100: cannot read the SM count");
+  int sms = 0;
+  TB_CHECK(sm_count(&sms));
   const int flags = (run != nullptr ? kWriteRunner : 0) | (m != nullptr ? kWriteMargins : 0);
   // Vector stores need every row's run of heads to start on a multiple of its length.
   constexpr int kRun = score_store_heads(K);

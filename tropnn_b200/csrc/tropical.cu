@@ -28,6 +28,14 @@ bool score_sm100_supported(int64_t D, int64_t K, int pt, int bias_dtype, const v
 int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W, const void *bias, int pt, int64_t H,
                           int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, cudaStream_t stream);
 int read_score_error(int *value);
+bool hidden_sm100_supported(int64_t items, int64_t D, int64_t H, int64_t K, int pt, int zt, int it, const void *latent,
+                            const void *code_t, const void *hidden);
+int trop_hidden_sm100_impl(const void *latent, int zt, int64_t items, int64_t D, const void *code_t, int pt,
+                           int64_t H, int64_t K, const void *win, const void *run, const float *m, float code_scale,
+                           int training, float *hidden, cudaStream_t stream);
+int trop_code_transpose_impl(const void *code, int pt, int64_t H, int64_t K, int64_t D, void *code_t,
+                             cudaStream_t stream);
+int read_hidden_error(int *value);
 
 namespace {
 
@@ -486,9 +494,9 @@ int hidden_by_width(const void *z, int64_t items, int D, const void *code, int H
   return launch_hidden<PT, IT, 1, 8, ZP>(z, items, D, code, H, K, win, run, m, code_scale, training, hidden, stream);
 }
 
-int trop_hidden_impl(const void *z, int zt, int64_t items, int64_t D, const void *code, int pt, int64_t H, int64_t K,
-                     const void *win, const void *run, int it, const float *m, float code_scale, int training,
-                     float *hidden, cudaStream_t stream) {
+int trop_hidden_impl(const void *z, int zt, int64_t items, int64_t D, const void *code, const void *code_t, int pt,
+                     int64_t H, int64_t K, const void *win, const void *run, int it, const float *m, float code_scale,
+                     int training, float *hidden, cudaStream_t stream) {
   TB_CHECK(validate_trop(items, D, H, K));
   TB_REQUIRE(is_float_dtype(pt), TROPNN_B200_ERR_DTYPE, "trop_hidden: param dtype %s unsupported", dtype_name(pt));
   TB_CHECK(check_index_dtype(K, it));
@@ -496,6 +504,9 @@ int trop_hidden_impl(const void *z, int zt, int64_t items, int64_t D, const void
   if (items == 0) return TROPNN_B200_OK;
   TB_REQUIRE(z && code && win && hidden && (!training || (run && m)), TROPNN_B200_ERR_INVALID,
              "trop_hidden: null pointer");
+  // Half-precision codes with their transpose at hand: one-hot GEMM on the tensor cores.
+  if (hidden_sm100_supported(items, D, H, K, pt, zt, it, z, code_t, hidden))
+    return trop_hidden_sm100_impl(z, zt, items, D, code_t, pt, H, K, win, run, m, code_scale, training, hidden, stream);
   const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
   const bool train = training != 0;
   const bool zp = zt != TROPNN_B200_F32;
@@ -629,19 +640,30 @@ int tropnn_b200_trop_route(const void *latent, int latent_dtype, int64_t items, 
 }
 
 int tropnn_b200_trop_hidden(const void *latent, int latent_dtype, int64_t items, int64_t code_dim, const void *code,
-                            int param_dtype, int64_t heads, int64_t cells, const void *winner, const void *runner,
-                            int index_dtype, const float *margins, float code_scale, int training, float *hidden,
-                            void *stream) {
+                            const void *code_t, int param_dtype, int64_t heads, int64_t cells, const void *winner,
+                            const void *runner, int index_dtype, const float *margins, float code_scale, int training,
+                            float *hidden, void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
-  TB_CHECK(tropnn_b200::trop_hidden_impl(latent, latent_dtype, items, code_dim, code, param_dtype, heads, cells, winner,
-                                         runner, index_dtype, margins, code_scale, training, hidden,
+  TB_CHECK(tropnn_b200::trop_hidden_impl(latent, latent_dtype, items, code_dim, code, code_t, param_dtype, heads, cells,
+                                         winner, runner, index_dtype, margins, code_scale, training, hidden,
                                          tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+int tropnn_b200_trop_code_transpose(const void *code, int param_dtype, int64_t heads, int64_t cells, int64_t code_dim,
+                                    void *code_t, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::trop_code_transpose_impl(code, param_dtype, heads, cells, code_dim, code_t,
+                                                 tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 
 int tropnn_b200_device_error(int *value) {
   TB_CHECK(tropnn_b200::check_current_device());
-  TB_CHECK(tropnn_b200::read_score_error(value));
+  int score = 0, hidden = 0;
+  TB_CHECK(tropnn_b200::read_score_error(&score));
+  TB_CHECK(tropnn_b200::read_hidden_error(&hidden));
+  *value = score | hidden;
   return tropnn_b200::clear_error();
 }
 

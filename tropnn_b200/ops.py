@@ -322,6 +322,19 @@ def pairwise_b200(
 # ---------------------------------------------------------------------------
 
 
+def _onehot_hidden_eligible(items: int, code_dim: int, heads: int, cells: int, dtype: torch.dtype, idx: torch.dtype) -> bool:
+    """Shapes the tensor-core code sum takes (tropnn_b200_trop_hidden with code_t)."""
+    return (
+        dtype in (torch.float16, torch.bfloat16)
+        and idx == torch.uint8
+        and cells in (2, 4, 8, 16, 32)
+        and code_dim % 64 == 0
+        and 64 <= code_dim <= 256
+        and (heads * cells) % 8 == 0
+        and items >= 128
+    )
+
+
 class _TropRouteB200Function(torch.autograd.Function):
     @staticmethod
     def forward(  # type: ignore[override]
@@ -378,6 +391,23 @@ class _TropRouteB200Function(torch.autograd.Function):
             margins.data_ptr() if margins.numel() else None,
             stream,
         )
+        # Half-precision codes: the selected-code sum runs as a one-hot tensor-core GEMM
+        # over code^T (rebuilt every call: code may have changed in place, and the
+        # transpose is one pass over the table).
+        code_t = None
+        if _onehot_hidden_eligible(items, code_dim, heads, cells, code_c.dtype, idx_dtype):
+            code_t = torch.empty((code_dim, heads * cells), device=dev, dtype=code_c.dtype)
+            _launch(
+                "trop_code_transpose",
+                lib.tropnn_b200_trop_code_transpose,
+                code_c.data_ptr(),
+                pdt,
+                heads,
+                cells,
+                code_dim,
+                code_t.data_ptr(),
+                stream,
+            )
         _launch(
             "trop_hidden",
             lib.tropnn_b200_trop_hidden,
@@ -386,6 +416,7 @@ class _TropRouteB200Function(torch.autograd.Function):
             items,
             code_dim,
             code_c.data_ptr(),
+            nat.ptr(code_t),
             pdt,
             heads,
             cells,
