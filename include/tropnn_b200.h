@@ -256,6 +256,27 @@ TROPNN_B200_API int tropnn_b200_trop_code_transpose(const void *code, int param_
                                     int64_t code_dim, void *code_t, void *stream);
 
 /*
+ * out[rows, 2*cols] = [hi | lo] per row of the f32 matrix x [rows, cols]: hi = x rounded
+ * to dtype (F16/BF16), lo = (x - hi) rounded to dtype; hi + lo carries x to ~2^-22
+ * relative (f16). cols % 4 == 0. Left operand of tropnn_b200_linear_f32out for an f32
+ * input. No reference counterpart: a precision-splitting step of this backend.
+ */
+TROPNN_B200_API int tropnn_b200_split_half(const float *x, int64_t rows, int64_t cols, int dtype, void *out,
+                           void *stream);
+
+/*
+ * out[n, o] = sum_s sum_k a[n, s*in + k] * weight[o, k] + bias[o] (f32 accumulation on the
+ * tensor cores, f32 out [rows, out_features]); a [rows, slices*in] and weight
+ * [out_features, in] in dtype (F16/BF16), bias f32 [out_features] or NULL. slices = 2
+ * with a from tropnn_b200_split_half is the f32-input linear map of the output projection
+ * (layers/tropical.py:140-146: F.linear on the f32 hidden with the weight upcast).
+ * in % 64 == 0, slices * in <= 512, out_features % 4 == 0, 16-byte aligned operands.
+ */
+TROPNN_B200_API int tropnn_b200_linear_f32out(const void *a, int64_t rows, int64_t slices, const void *weight,
+                              int64_t out_features, int64_t in_features, int dtype, const float *bias,
+                              float *out, void *stream);
+
+/*
  * Reads and clears the library's device error words: 1 after a tensor-core kernel gave up
  * a bounded wait (its CTA then released its resources and exited). Synchronises with the
  * device; call it off the hot path.

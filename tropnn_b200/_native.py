@@ -78,6 +78,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _i32, _i64, _i64, _p, _p, _i32, _i64, _i64, _p, _p, _i32, _p, _f32, _i32, _p, _p],
     ),
     "tropnn_b200_trop_code_transpose": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p]),
+    "tropnn_b200_split_half": (_i32, [_p, _i64, _i64, _i32, _p, _p]),
+    "tropnn_b200_linear_f32out": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _i32, _p, _p, _p]),
     "tropnn_b200_device_error": (_i32, [ctypes.POINTER(ctypes.c_int)]),
     "tropnn_b200_trop_backward_rows": (
         _i32,

@@ -1,0 +1,431 @@
+// Dense f32-output linear map on the sm_100a tensor cores:
+//   out[m, n] = sum_s sum_k a[m, s*K + k] * w[n, k] + bias[n]      (f32 accumulation)
+// with a and w in f16/bf16 and `slices` copies of the K-wide left operand side by side.
+// With slices = 2 and a = [hi | lo], hi = half(x), lo = half(x - hi) (split_half), this
+// is an f32 x half-precision-weight product accurate to ~2^-22 relative for f16: the
+// output map of TropLinear (layers/tropical.py:140-146), whose reference computes an
+// f32 GEMM with the half-precision weight upcast, runs on tcgen05 instead of f32 FMA.
+//
+// Work unit = (128-row block, 256-column output tile); persistent grid, one CTA per SM,
+// each CTA running a contiguous range of the row-major unit sequence (consecutive units
+// share their left block). CTA = 2 + 8 warps:
+//   warp 0      TMA producer: the left block (all slices, resident, K-major, 128B swizzle;
+//               reloaded when the unit sequence enters the next row block, once the MMAs
+//               on the old one are done), then the weight k blocks (256 x 64) through a
+//               ring; each weight k block serves every slice.
+//   warp 1      allocates all 512 TMEM columns (two 256-column f32 accumulators); lane 0
+//               issues the MMAs (M=128, N=256, K=16) and commits them to mbarriers.
+//   warps 2-9   epilogue: each thread owns one accumulator row and 128 columns: adds the
+//               bias; the warp stages 32 x 32 f32 tiles in shared memory and writes each
+//               with one TMA store.
+// Waits are bounded (sm100.cuh); one epilogue thread polls the accumulator barrier and
+// the other epilogue warps wait on a named barrier.
+#include <cuda.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "sm100.cuh"
+#include "tropnn_b200.h"
+
+namespace tropnn_b200 {
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;
+constexpr int kMaxStages = 8;
+constexpr int kMinStages = 2;
+constexpr int kTileBytesA = kBM * 128;
+constexpr int kTileBytesB = kBN * 128;
+constexpr int kBoxRows = 128;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr int kEpiCols = kBN * 4 / kEpiWarps;  // 128
+constexpr int kStageOutBytes = 32 * 128;       // one warp's 32 x 32 f32 store tile
+constexpr int kTmemCols = 2 * kBN;
+constexpr int kMaxABlocks = 8;                 // slices * K <= 512
+constexpr size_t kSmemLimit = 227 * 1024;
+
+__device__ int g_gemm_error = 0;
+
+struct Barriers {
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
+  uint64_t a_full;
+  uint64_t a_empty;
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+  int epi_go[2];
+};
+
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, Barriers *bs) {
+  return sm100::mbar_wait(bar, parity, &bs->abort, &g_gemm_error);
+}
+
+template <typename PT>
+__global__ void __launch_bounds__(kThreads, 1) linear_f32out_kernel(
+    const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+    const __grid_constant__ CUtensorMap map_out, const float *__restrict__ bias, int out_features, int slices,
+    int b_kblocks, int stages, int tiles_total, int64_t units) {
+  constexpr uint32_t kIdesc =
+      umma_idesc_f16(std::is_same<PT, __half>::value ? 0 : 1, kBM, kBN);
+  const int a_blocks = slices * b_kblocks;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *a_smem = smem;                               // a_blocks x [128 rows x 128 B]
+  uint8_t *b_smem = a_smem + a_blocks * kTileBytesA;    // stages x [256 rows x 128 B]
+  uint8_t *o_smem = b_smem + stages * kTileBytesB;      // kEpiWarps x [32 rows x 128 B]
+  Barriers *bs = reinterpret_cast<Barriers *>(o_smem + kEpiWarps * kStageOutBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t u_begin = units * blockIdx.x / gridDim.x;
+  const int64_t u_end = units * (blockIdx.x + 1) / gridDim.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&bs->full[s], 1);
+      mbar_init(&bs->empty[s], 1);
+    }
+    mbar_init(&bs->a_full, 1);
+    mbar_init(&bs->a_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bs->tmem_full[b], 1);
+      mbar_init(&bs->tmem_empty[b], kEpiWarps);
+    }
+    mbar_init(&bs->mma_done, 1);
+    bs->abort = 0;
+    mbar_init_fence();
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(&bs->tmem_base, kTmemCols);
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem_base = bs->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0 && u_begin < u_end) {
+      // ---------------- TMA producer ----------------
+      prefetch_map(&map_a);
+      prefetch_map(&map_w);
+      uint32_t issued[kMaxStages];
+      for (int s = 0; s < kMaxStages; ++s) issued[s] = 0;
+      bool ok = true;
+      int it = 0, a_loads = 0;
+      int64_t cur_rb = -1;
+      for (int64_t u = u_begin; u < u_end && ok; ++u) {
+        const int64_t rb = u / tiles_total;
+        const int tile = static_cast<int>(u - rb * tiles_total);
+        if (rb != cur_rb) {
+          if (a_loads > 0 && !wait_bar(&bs->a_empty, uint32_t(a_loads - 1) & 1u, bs)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bs->a_full, uint32_t(a_blocks) * kTileBytesA);
+          for (int kb = 0; kb < a_blocks; ++kb)
+            tma_load_2d(a_smem + kb * kTileBytesA, &map_a, &bs->a_full, kb * kBK, static_cast<int>(rb * kBM));
+          ++a_loads;
+          cur_rb = rb;
+        }
+        for (int kb = 0; kb < b_kblocks; ++kb, ++it) {
+          const int s = it % stages;
+          const uint32_t phase = uint32_t(it / stages) & 1u;
+          if (!wait_bar(&bs->empty[s], phase ^ 1u, bs)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bs->full[s], kTileBytesB);
+          for (int q = 0; q < kBN / kBoxRows; ++q)
+            tma_load_2d(b_smem + s * kTileBytesB + q * kBoxRows * 128, &map_w, &bs->full[s], kb * kBK,
+                        tile * kBN + q * kBoxRows);
+          issued[s] = uint32_t(it / stages) + 1;
+        }
+      }
+      if (a_loads > 0) mbar_drain(&bs->a_full, uint32_t(a_loads - 1) & 1u);
+      for (int s = 0; s < stages; ++s)
+        if (issued[s] > 0) mbar_drain(&bs->full[s], (issued[s] - 1) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && u_begin < u_end) {
+      // ---------------- MMA issuer ----------------
+      bool ok = true;
+      int it = 0, a_uses = 0;
+      int64_t cur_rb = -1;
+      uint32_t t = 0;
+      for (int64_t u = u_begin; u < u_end && ok; ++u, ++t) {
+        const int64_t rb = u / tiles_total;
+        if (rb != cur_rb) {
+          if (a_uses > 0) umma_commit(&bs->a_empty);
+          if (!wait_bar(&bs->a_full, uint32_t(a_uses) & 1u, bs)) {
+            ok = false;
+            break;
+          }
+          tmem_fence_after();
+          ++a_uses;
+          cur_rb = rb;
+        }
+        const int b = t & 1;
+        const uint32_t use = t >> 1;
+        if (!wait_bar(&bs->tmem_empty[b], (use & 1u) ^ 1u, bs)) {
+          ok = false;
+          break;
+        }
+        tmem_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(b * kBN);
+        for (int kb = 0; kb < b_kblocks; ++kb, ++it) {
+          const int s = it % stages;
+          if (!wait_bar(&bs->full[s], uint32_t(it / stages) & 1u, bs)) {
+            ok = false;
+            break;
+          }
+          tmem_fence_after();
+          const uint32_t b_base = smem_addr(b_smem + s * kTileBytesB);
+          for (int sl = 0; sl < slices; ++sl) {
+            const uint32_t a_base = smem_addr(a_smem + (sl * b_kblocks + kb) * kTileBytesA);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma_f16(d_tmem, umma_desc_sw128(a_base + kk * 32), umma_desc_sw128(b_base + kk * 32), kIdesc,
+                       (kb | sl | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&bs->empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&bs->tmem_full[b]);
+      }
+      umma_commit(&bs->mma_done);
+      mbar_drain(&bs->mma_done, 0);
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    // Each warp owns 32 accumulator rows x 128 columns of a unit and writes them as four
+    // 32 x 32 f32 tiles: registers -> its 4 KB shared tile (128-byte swizzle, so the 32
+    // lanes' row writes hit distinct banks) -> one TMA store, which writes whole lines
+    // (row-per-lane global stores ran at a third of HBM bandwidth).
+    const int quarter = warp & 3;
+    const int group = (warp - 2) >> 2;
+    uint8_t *stage = o_smem + (warp - 2) * kStageOutBytes;
+    uint32_t t = 0;
+    for (int64_t u = u_begin; u < u_end; ++u, ++t) {
+      const int64_t rb = u / tiles_total;
+      const int tile = static_cast<int>(u - rb * tiles_total);
+      const int b = t & 1;
+      const uint32_t use = t >> 1;
+      const int col0 = tile * kBN + group * kEpiCols;
+      // One thread polls; the verdict travels through a two-slot flag (slot t&1 is
+      // rewritten two units later, after every epilogue warp has read it).
+      if (warp == 2 && lane == 0) bs->epi_go[b] = wait_bar(&bs->tmem_full[b], use & 1u, bs) ? 1 : 0;
+      named_sync(1, kEpiWarps * 32);
+      if (*reinterpret_cast<volatile int *>(&bs->epi_go[b]) == 0) break;
+      __syncwarp();
+      tmem_fence_after();
+      const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(b * kBN + group * kEpiCols);
+#pragma unroll 1
+      for (int c = 0; c < kEpiCols; c += 32) {
+        float v[32];
+        tmem_ld32(taddr + uint32_t(c), v);
+        float bv[32];
+        const int cc = col0 + c;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) bv[i] = 0.f;
+        if (bias != nullptr) {
+          if (cc + 32 <= out_features) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const float4 q = __ldg(reinterpret_cast<const float4 *>(bias + cc + i));
+              bv[i] = q.x;
+              bv[i + 1] = q.y;
+              bv[i + 2] = q.z;
+              bv[i + 3] = q.w;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (cc + i < out_features) bv[i] = __ldg(bias + cc + i);
+          }
+        }
+        tmem_wait_ld();
+        reg_fence(v);
+        if (c + 32 == kEpiCols) {
+          tmem_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bs->tmem_empty[b]);
+        }
+        // The previous tile's TMA store must have read the staging buffer.
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        uint8_t *my_row = stage + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 q = make_float4(__fadd_rn(v[4 * j], bv[4 * j]), __fadd_rn(v[4 * j + 1], bv[4 * j + 1]),
+                                       __fadd_rn(v[4 * j + 2], bv[4 * j + 2]), __fadd_rn(v[4 * j + 3], bv[4 * j + 3]));
+          *reinterpret_cast<float4 *>(my_row + ((j ^ (lane & 7)) << 4)) = q;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&map_out, stage, cc, static_cast<int>(rb * kBM + quarter * 32));
+          bulk_commit();
+        }
+      }
+    }
+    // Every store must be complete before the CTA exits.
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tmem_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// [hi | lo] halves of each f32 row: hi = half(x), lo = half(x - hi).
+template <typename PT>
+__global__ void __launch_bounds__(256) split_half_kernel(const float *__restrict__ x, int64_t rows, int cols,
+                                                          PT *__restrict__ out) {
+  const int64_t total = rows * cols / 4;
+  for (int64_t q = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; q < total; q += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t i = q * 4;
+    const int64_t row = i / cols;
+    const int col = static_cast<int>(i - row * cols);
+    const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + q);
+    const float xs[4] = {v.x, v.y, v.z, v.w};
+    PT hi[4], lo[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      hi[e] = from_f32<PT>(xs[e]);
+      lo[e] = from_f32<PT>(__fsub_rn(xs[e], to_f32(hi[e])));
+    }
+    PT *o = out + row * (2 * int64_t(cols)) + col;
+    *reinterpret_cast<uint2 *>(o) = *reinterpret_cast<const uint2 *>(hi);
+    *reinterpret_cast<uint2 *>(o + cols) = *reinterpret_cast<const uint2 *>(lo);
+  }
+}
+
+size_t linear_fixed_smem(int a_blocks) {
+  return 1024 + size_t(a_blocks) * kTileBytesA + size_t(kEpiWarps) * kStageOutBytes + sizeof(Barriers);
+}
+
+int linear_stages(int a_blocks) {
+  const size_t fixed = linear_fixed_smem(a_blocks);
+  if (fixed >= kSmemLimit) return 0;
+  const int s = static_cast<int>(std::min<size_t>(kMaxStages, (kSmemLimit - fixed) / kTileBytesB));
+  return s >= kMinStages ? s : 0;
+}
+
+template <typename PT>
+int launch_linear(const void *a, int64_t rows, int slices, const void *w, int out_features, int in_features,
+                  const float *bias, float *out, cudaStream_t stream) {
+  const CUtensorMapDataType dt =
+      std::is_same<PT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int b_kblocks = in_features / kBK;
+  const int a_blocks = slices * b_kblocks;
+  const int stages = linear_stages(a_blocks);
+  const size_t smem = linear_fixed_smem(a_blocks) + size_t(stages) * kTileBytesB;
+  CUtensorMap map_a, map_w, map_out;
+  TB_CHECK(make_map_k64(&map_a, a, dt, int64_t(slices) * in_features, rows, kBM));
+  TB_CHECK(make_map_k64(&map_w, w, dt, in_features, out_features, kBoxRows));
+  TB_CHECK(make_map_f32_store32(&map_out, out, out_features, rows));
+  const int tiles_total = static_cast<int>(ceil_div(int64_t(out_features), int64_t(kBN)));
+  const int64_t units = ceil_div(rows, int64_t(kBM)) * tiles_total;
+  int sms = 0;
+  TB_CHECK(sm_count(&sms));
+  auto kernel = linear_f32out_kernel<PT>;
+  TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "linear_f32out"));
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(units, sms));
+  kernel<<<grid, kThreads, smem, stream>>>(map_a, map_w, map_out, bias, out_features, slices, b_kblocks, stages,
+                                           tiles_total, units);
+  return check_launch("linear_f32out");
+}
+
+}  // namespace
+
+bool linear_f32out_supported(int64_t rows, int64_t slices, int64_t out_features, int64_t in_features, int dtype) {
+  return (dtype == TROPNN_B200_F16 || dtype == TROPNN_B200_BF16) && (slices == 1 || slices == 2) && rows >= 1 &&
+         rows <= (int64_t(1) << 31) - 1024 && in_features % kBK == 0 && in_features >= kBK &&
+         slices * (in_features / kBK) <= kMaxABlocks && linear_stages(static_cast<int>(slices * in_features / kBK)) > 0 &&
+         out_features >= 1 && out_features % 4 == 0 && out_features <= (int64_t(1) << 30);
+}
+
+int linear_f32out_impl(const void *a, int64_t rows, int64_t slices, const void *w, int64_t out_features,
+                       int64_t in_features, int dtype, const float *bias, float *out, cudaStream_t stream) {
+  TB_REQUIRE(linear_f32out_supported(rows, slices, out_features, in_features, dtype), TROPNN_B200_ERR_INVALID,
+             "linear_f32out: unsupported shape rows=%lld slices=%lld out=%lld in=%lld dtype=%s", (long long)rows,
+             (long long)slices, (long long)out_features, (long long)in_features, dtype_name(dtype));
+  TB_REQUIRE(a && w && out, TROPNN_B200_ERR_INVALID, "linear_f32out: null pointer");
+  auto al16 = [](const void *p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  TB_REQUIRE(al16(a) && al16(w) && al16(bias) && al16(out), TROPNN_B200_ERR_INVALID,
+             "linear_f32out: operands must be 16-byte aligned");
+  const int s = static_cast<int>(slices), n = static_cast<int>(out_features), k = static_cast<int>(in_features);
+  if (dtype == TROPNN_B200_F16) return launch_linear<__half>(a, rows, s, w, n, k, bias, out, stream);
+  return launch_linear<__nv_bfloat16>(a, rows, s, w, n, k, bias, out, stream);
+}
+
+int split_half_impl(const float *x, int64_t rows, int64_t cols, int dtype, void *out, cudaStream_t stream) {
+  TB_REQUIRE(dtype == TROPNN_B200_F16 || dtype == TROPNN_B200_BF16, TROPNN_B200_ERR_DTYPE,
+             "split_half: dtype %s unsupported (f16/bf16 only)", dtype_name(dtype));
+  TB_REQUIRE(rows >= 0 && cols > 0 && cols % 4 == 0 && cols <= (1 << 30), TROPNN_B200_ERR_INVALID,
+             "split_half: cols=%lld must be a positive multiple of 4", (long long)cols);
+  if (rows == 0) return TROPNN_B200_OK;
+  TB_REQUIRE(x && out, TROPNN_B200_ERR_INVALID, "split_half: null pointer");
+  TB_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 8 == 0,
+             TROPNN_B200_ERR_INVALID, "split_half: misaligned operands");
+  int sms = 0;
+  TB_CHECK(sm_count(&sms));
+  const int64_t quads = rows * cols / 4;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(quads, int64_t(256)), int64_t(sms) * 8));
+  if (dtype == TROPNN_B200_F16)
+    split_half_kernel<__half><<<grid, 256, 0, stream>>>(x, rows, static_cast<int>(cols), static_cast<__half *>(out));
+  else
+    split_half_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(x, rows, static_cast<int>(cols),
+                                                               static_cast<__nv_bfloat16 *>(out));
+  return check_launch("split_half");
+}
+
+int read_gemm_error(int *value) {
+  int v = 0;
+  cudaError_t err = cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof(int));
+  if (err != cudaSuccess)
+    return set_error(TROPNN_B200_ERR_LAUNCH, "reading the device error word: %s", cudaGetErrorString(err));
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof(int));
+  }
+  *value = v;
+  return TROPNN_B200_OK;
+}
+
+}  // namespace tropnn_b200
+
+extern "C" {
+
+int tropnn_b200_split_half(const float *x, int64_t rows, int64_t cols, int dtype, void *out, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::split_half_impl(x, rows, cols, dtype, out, tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+int tropnn_b200_linear_f32out(const void *a, int64_t rows, int64_t slices, const void *weight, int64_t out_features,
+                              int64_t in_features, int dtype, const float *bias, float *out, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  if (rows == 0) return tropnn_b200::clear_error();
+  TB_CHECK(tropnn_b200::linear_f32out_impl(a, rows, slices, weight, out_features, in_features, dtype, bias, out,
+                                           tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+}  // extern "C"

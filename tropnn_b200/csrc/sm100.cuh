@@ -91,6 +91,23 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
+// 2-D tiled TMA store from this CTA's shared memory (bulk-group completion); the rows and
+// columns of the box outside the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_addr(src)), "r"(x), "r"(y)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The shared-memory sources of all committed bulk stores have been read.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// All committed bulk stores have completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA) reads.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 __device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -239,6 +256,21 @@ inline int make_map_k64(CUtensorMap *map, const void *ptr, CUtensorMapDataType d
   CUresult r = fn(map, dt, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(TROPNN_B200_ERR_LAUNCH, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return TROPNN_B200_OK;
+}
+
+// 2-D tensor map over a row-major f32 [outer, inner] matrix for 32 x 32 TMA stores
+// staged in shared memory with the 128-byte swizzle (one 128-byte row per box row).
+inline int make_map_f32_store32(CUtensorMap *map, void *ptr, int64_t inner, int64_t outer) {
+  EncodeTiledFn fn = nullptr;
+  TB_CHECK(encode_fn(&fn));
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * 4};
+  const cuuint32_t box[2] = {32u, 32u};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(TROPNN_B200_ERR_LAUNCH, "cuTensorMapEncodeTiled (store) failed (%d)", int(r));
   return TROPNN_B200_OK;
 }
 

@@ -36,6 +36,7 @@ int trop_hidden_sm100_impl(const void *latent, int zt, int64_t items, int64_t D,
 int trop_code_transpose_impl(const void *code, int pt, int64_t H, int64_t K, int64_t D, void *code_t,
                              cudaStream_t stream);
 int read_hidden_error(int *value);
+int read_gemm_error(int *value);
 
 namespace {
 
@@ -660,10 +661,11 @@ int tropnn_b200_trop_code_transpose(const void *code, int param_dtype, int64_t h
 
 int tropnn_b200_device_error(int *value) {
   TB_CHECK(tropnn_b200::check_current_device());
-  int score = 0, hidden = 0;
+  int score = 0, hidden = 0, gemm = 0;
   TB_CHECK(tropnn_b200::read_score_error(&score));
   TB_CHECK(tropnn_b200::read_hidden_error(&hidden));
-  *value = score | hidden;
+  TB_CHECK(tropnn_b200::read_gemm_error(&gemm));
+  *value = score | hidden | gemm;
   return tropnn_b200::clear_error();
 }
 

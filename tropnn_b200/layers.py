@@ -24,7 +24,13 @@ import torch
 import torch.nn as nn
 from torch import Tensor
 
-from .ops import pairwise_anchor_index, pairwise_b200, trop_route_hidden_packed
+from .ops import (
+    linear_f32out_b200,
+    linear_f32out_eligible,
+    pairwise_anchor_index,
+    pairwise_b200,
+    trop_route_hidden_packed,
+)
 
 __all__ = [
     "PairwiseLinear",
@@ -88,9 +94,10 @@ def _require_f32_compute(compute_dtype: torch.dtype, layer_name: str) -> None:
 def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
     """Full TropLinear forward on sm_100a for any module with the TropLinear attributes.
 
-    Projection (tropical.py:96-99) and output map (tropical.py:140-146) are dense cuBLAS
-    GEMMs through torch; the route scores, top-2, code gather-sum and their backward are
-    the b200 kernels (ops.trop_route_hidden_b200).
+    The projection (tropical.py:96-99) is a dense cuBLAS GEMM through torch; the route
+    scores, top-2, code sum and their backward are the b200 kernels
+    (ops.trop_route_hidden_packed); the output map (tropical.py:140-146) is the b200
+    tensor-core linear map for half-precision weights (ops.linear_f32out_b200), else torch.
     """
     if x.ndim == 2:
         x = x.unsqueeze(1)
@@ -112,11 +119,16 @@ def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
         training=layer.training,
         keep_margins=getattr(layer, "cache_route_debug", True),
     )
-    weight = layer.output_proj.weight.to(dtype=compute_dtype)
-    output = torch.matmul(hidden, weight.t())
     bias = layer.output_proj.bias
-    if bias is not None:
-        output = output + bias.to(dtype=compute_dtype)
+    if linear_f32out_eligible(hidden, layer.output_proj.weight):
+        # Half-precision output weight: the f32 product on the tensor cores (split f32
+        # hidden, bias fused), the reference's f32 math in the backward.
+        output = linear_f32out_b200(hidden, layer.output_proj.weight, bias)
+    else:
+        weight = layer.output_proj.weight.to(dtype=compute_dtype)
+        output = torch.matmul(hidden, weight.t())
+        if bias is not None:
+            output = output + bias.to(dtype=compute_dtype)
     _store_debug(layer, winner, margins)
     return output.to(dtype=input_dtype)
 

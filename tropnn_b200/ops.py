@@ -650,3 +650,81 @@ def trop_route_hidden_packed(
         return _TropRouteB200Function.apply(
             latent, router_weight, router_bias, code, float(code_scale), bool(training), bool(keep_margins)
         )
+
+
+def linear_f32out_eligible(hidden: Tensor, weight: Tensor) -> bool:
+    """Shapes the tensor-core f32-input linear map takes (tropnn_b200_linear_f32out)."""
+    out_features, in_features = weight.shape
+    return (
+        hidden.is_cuda
+        and hidden.dtype == torch.float32
+        and weight.dtype in (torch.float16, torch.bfloat16)
+        and in_features % 64 == 0
+        and 64 <= in_features <= 256
+        and out_features % 4 == 0
+        and hidden.shape[-1] == in_features
+    )
+
+
+class _LinearF32OutFunction(torch.autograd.Function):
+    """F.linear(hidden, weight.float(), bias.float()) for f32 ``hidden`` and half-precision
+    parameters (layers/tropical.py:140-146). Forward: hidden split into [hi | lo] halves and
+    one tcgen05 GEMM (two k slices against the same weight tile, bias in the epilogue).
+    Backward: the reference's f32 products (grad_hidden = g W, grad_W = g^T hidden, grad_b
+    = sum g), cast back to the parameter dtype like the reference's ``.to`` upcast."""
+
+    @staticmethod
+    def forward(ctx: Any, hidden: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:
+        rows, in_features = hidden.shape
+        out_features = weight.shape[0]
+        dev = hidden.device
+        h = hidden.contiguous()
+        w = weight.contiguous()
+        dcode = nat.float_code(w.dtype)
+        stream = nat.stream_handle(dev)
+        lib = nat.load()
+        split = torch.empty((rows, 2 * in_features), device=dev, dtype=w.dtype)
+        _launch("split_half", lib.tropnn_b200_split_half, h.data_ptr(), rows, in_features, dcode, split.data_ptr(), stream)
+        b32 = None if bias is None else bias.to(torch.float32).contiguous()
+        out = torch.empty((rows, out_features), device=dev, dtype=torch.float32)
+        _launch(
+            "linear_f32out",
+            lib.tropnn_b200_linear_f32out,
+            split.data_ptr(),
+            rows,
+            2,
+            w.data_ptr(),
+            out_features,
+            in_features,
+            dcode,
+            nat.ptr(b32),
+            out.data_ptr(),
+            stream,
+        )
+        ctx.save_for_backward(h, w)
+        ctx.bias_dtype = None if bias is None else bias.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx: Any, grad_out: Tensor) -> tuple[Tensor | None, Tensor | None, Tensor | None]:
+        h, w = ctx.saved_tensors
+        g = grad_out.to(torch.float32)
+        grad_h = g @ w.to(torch.float32) if ctx.needs_input_grad[0] else None
+        grad_w = (g.t() @ h).to(w.dtype) if ctx.needs_input_grad[1] else None
+        grad_b = None
+        if ctx.bias_dtype is not None and ctx.needs_input_grad[2]:
+            grad_b = g.sum(0).to(ctx.bias_dtype)
+        return grad_h, grad_w, grad_b
+
+
+def linear_f32out_b200(hidden: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:
+    """f32 ``hidden`` [..., in] times the half-precision ``weight`` [out, in] (+ bias) in f32."""
+    if not linear_f32out_eligible(hidden, weight):
+        raise ValueError(
+            f"linear_f32out_b200: unsupported hidden {tuple(hidden.shape)} {hidden.dtype} / weight "
+            f"{tuple(weight.shape)} {weight.dtype}"
+        )
+    lead = hidden.shape[:-1]
+    with torch.cuda.device(hidden.device):
+        out = _LinearF32OutFunction.apply(hidden.reshape(-1, hidden.shape[-1]), weight, bias)
+    return out.reshape(*lead, weight.shape[0])
