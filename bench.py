@@ -154,21 +154,45 @@ def tensor_core_route(w: Workload, rows: int) -> bool:
         return False
     kw = w.layer_kwargs
     H, K, D = kw["heads"], kw["cells"], kw["code_dim"]
-    return K in (2, 4, 8, 16, 32) and D % 8 == 0 and (D + 63) // 64 <= 6 and rows >= 128 and H * K >= 128
+    return K in (2, 4, 8, 16, 32) and D % 8 == 0 and (D + 63) // 64 <= 8 and rows >= 128 and H * K >= 128
+
+
+def tensor_core_hidden(w: Workload, rows: int) -> bool:
+    """Whether the code sum runs as the one-hot tcgen05 GEMM (the C ABI's rule)."""
+    if w.kind != "trop" or w.dtype == "float32":
+        return False
+    kw = w.layer_kwargs
+    H, K, D = kw["heads"], kw["cells"], kw["code_dim"]
+    return K in (2, 4, 8, 16, 32) and D % 64 == 0 and 64 <= D <= 256 and (H * K) % 8 == 0 and rows >= 128
 
 
 def kernel_roofline(w: Workload, kernel: str, rows: int, peaks: dict) -> tuple[str, float, str, float] | None:
     """(bound, algorithmic work per launch, unit, peak) of one kernel: FLOPs against the
-    measured bf16 tensor peak for the tensor-core score GEMM, bytes against the measured HBM
-    copy bandwidth for everything else."""
-    if kernel == "trop_route" and tensor_core_route(w, rows):
+    measured bf16 tensor peak for the tcgen05 GEMMs (route scores, one-hot code sum, the
+    output map when its FLOPs outweigh its f32 output bytes), bytes against the measured
+    HBM copy bandwidth for everything else."""
+    tc_peak, hbm_peak = peaks["bf16_tflops"], peaks["hbm_gbs"]
+    if w.kind == "trop":
         kw = w.layer_kwargs
-        flops = 2.0 * kw["heads"] * kw["cells"] * kw["code_dim"] * rows
-        return "tensor", flops, "TFLOP/s", peaks["bf16_tflops"]
+        H, K, D, out = kw["heads"], kw["cells"], kw["code_dim"], w.out_features
+        if kernel == "trop_route" and tensor_core_route(w, rows):
+            return "tensor", 2.0 * H * K * D * rows, "TFLOP/s", tc_peak
+        if kernel == "trop_hidden" and tensor_core_hidden(w, rows):
+            return "tensor", 2.0 * H * K * D * rows, "TFLOP/s", tc_peak
+        if kernel == "linear_f32out":
+            flops = 2.0 * rows * out * 2 * D  # [hi | lo] slices against one weight
+            nbytes = float(rows * out * 4 + rows * 2 * D * 2 + out * D * 2 + out * 4)
+            if flops / (tc_peak * 1e12) >= nbytes / (hbm_peak * 1e9):
+                return "tensor", flops, "TFLOP/s", tc_peak
+            return "hbm", nbytes, "GB/s", hbm_peak
+        if kernel == "split_half":
+            return "hbm", float(rows * D * 4 + rows * 2 * D * 2), "GB/s", hbm_peak
+        if kernel == "trop_code_transpose":
+            return "hbm", float(2 * H * K * D * 2), "GB/s", hbm_peak
     work = algorithmic_bytes(w, kernel, rows)
     if work is None:
         return None
-    return "hbm", work, "GB/s", peaks["hbm_gbs"]
+    return "hbm", work, "GB/s", hbm_peak
 
 
 # ---------------------------------------------------------------------------

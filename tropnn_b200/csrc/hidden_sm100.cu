@@ -16,14 +16,17 @@
 // u8 routes and written straight into TMEM (tcgen05.st), so it never touches shared
 // memory: the MMA reads A from TMEM and B from shared memory.
 //
-// CTA = 10 warps, persistent over row blocks rb = blockIdx.x + i * gridDim.x:
+// CTA = 14 warps, persistent over row blocks rb = blockIdx.x + i * gridDim.x; each CTA
+// walks the k blocks from its own starting point (rotated), so that the CTAs spread
+// their code-table reads over L2:
 //   warp 0      TMA producer of the code^T k blocks (3-8 stage ring, D x 128 B each).
 //   warp 1      allocates all 512 TMEM columns (accumulator [0, D), one-hot ring
 //               [256, 512): 8 slots of 32 columns); lane 0 issues the MMAs (M=128,
 //               N=code_dim, K=16, A from TMEM) and commits them to mbarriers.
-//   warps 2-5   build the one-hot k blocks: one thread per row, 32 packed f16/bf16 pairs
-//               per k block, stored with tcgen05.st into the thread's TMEM lane.
-//   warps 6-9   epilogue: hidden = latent + code_scale * acc for the thread's row.
+//   warps 2-9   build the one-hot k blocks: one thread per row, 32 packed f16/bf16 pairs
+//               per k block, stored with tcgen05.st into the thread's TMEM lane; two
+//               warps per lane quarter take alternate k blocks.
+//   warps 10-13 epilogue: hidden = latent + code_scale * acc for the thread's row.
 // All waits are bounded (sm100.cuh); waits by whole warps of builders and epilogue use
 // mbarrier suspend hints instead of spinning, which kept the TMA/MMA pipeline at rate.
 #include <cuda.h>
@@ -45,7 +48,7 @@ constexpr int kMaxD = 256;               // MMA N = code_dim
 constexpr int kMaxBStages = 8;
 constexpr int kMinBStages = 3;
 constexpr int kAStages = 8;              // one-hot ring slots in TMEM
-constexpr int kBuildWarps = 4;           // one per TMEM lane quarter
+constexpr int kBuildWarps = 8;           // two per TMEM lane quarter (even / odd k items)
 constexpr int kEpiWarps = 4;             // one per TMEM lane quarter
 constexpr int kThreads = 32 * (2 + kBuildWarps + kEpiWarps);
 constexpr uint32_t kTmemCols = 512;
@@ -160,6 +163,11 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Every CTA walks the code table from its own starting k block (all CTAs reading the
+  // same k block at once made its L2 lines the bottleneck); position kb of the walk is
+  // k block kb + rot (mod kblocks).
+  const int rot = static_cast<int>(int64_t(blockIdx.x) * kblocks / gridDim.x);
+  auto kblock_at = [&](int kb) { return kb + rot < kblocks ? kb + rot : kb + rot - kblocks; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < bstages; ++s) {
@@ -167,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
       mbar_init(&bs->b_empty[s], 1);
     }
     for (int s = 0; s < kAStages; ++s) {
-      mbar_init(&bs->a_full[s], kBuildWarps);
+      mbar_init(&bs->a_full[s], kBuildWarps / 2);
       mbar_init(&bs->a_empty[s], 1);
     }
     mbar_init(&bs->acc_full, 1);
@@ -202,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
             break;
           }
           mbar_expect_tx(&bs->b_full[s], uint32_t(b_stage_bytes));
-          tma_load_2d(b_smem + s * b_stage_bytes, &map_ct, &bs->b_full[s], kb * kBK, 0);
+          tma_load_2d(b_smem + s * b_stage_bytes, &map_ct, &bs->b_full[s], kblock_at(kb) * kBK, 0);
           issued[s] = uint32_t(it / bstages) + 1;
         }
       }
@@ -247,23 +255,30 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
     }
   } else if (warp < 2 + kBuildWarps) {
     // ---------------- one-hot builders ----------------
+    // Warps 2-5 build the even k items of the CTA's sequence (ait = i * kblocks + kb over
+    // its row blocks i), warps 6-9 the odd ones; each warp its TMEM lane quarter.
     const int quarter = warp & 3;
+    const int parity = (warp - 2) >> 2;
     const uint32_t lane_base = tmem_base + (uint32_t(quarter * 32) << 16) + kAColBase;
-    int ait = 0;
     bool ok = true;
-    for (int64_t rb = blockIdx.x; rb < row_blocks && ok; rb += gridDim.x) {
+    for (int ait = parity;; ait += 2) {
+      const int64_t i = ait / kblocks;
+      const int kb = static_cast<int>(ait - i * kblocks);
+      const int64_t rb = blockIdx.x + i * gridDim.x;
+      if (rb >= row_blocks || !ok) break;
       const int64_t row = rb * kBM + quarter * 32 + lane;
       const bool live = row < rows;
       const uint8_t *wrow = winner + (live ? row : 0) * H;
       const uint8_t *rrow = TRAIN ? runner + (live ? row : 0) * H : nullptr;
       const float *mrow = TRAIN ? margins + (live ? row : 0) * H : nullptr;
-      for (int kb = 0; kb < kblocks; ++kb, ++ait) {
+      const int kbe = kblock_at(kb);
+      {
         const int sa = ait % kAStages;
         // Route bytes first, so their latency overlaps the wait for the slot.
         uint32_t wc[kHeadsPerBlock], rc[kHeadsPerBlock], vw[kHeadsPerBlock], vr[kHeadsPerBlock];
 #pragma unroll
         for (int hh = 0; hh < kHeadsPerBlock; ++hh) {
-          const int h = kb * kHeadsPerBlock + hh;
+          const int h = kbe * kHeadsPerBlock + hh;
           wc[hh] = 0xFFu;
           rc[hh] = 0xFFu;
           vw[hh] = kOne;
