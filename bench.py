@@ -357,8 +357,7 @@ def _timed(steps: int, body, flush: torch.Tensor, world: int, device: torch.devi
 
 def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
     import tropnn_b200
-    from tropnn_b200 import trace
-    from tropnn_b200.distributed import allreduce_gradients
+    from tropnn_b200.distributed import PeerAllReduce, overlapped_gradient_sync
 
     rank, world, local_rank = _dist_env()
     device = torch.device("cuda", local_rank)
@@ -370,8 +369,37 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
 
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     tropnn_b200._native.load()
-
     layer = w.build().to(device).train(w.train)
+    peer = None
+    with contextlib.ExitStack() as stack:
+        if world > 1 and w.train:
+            grads = [p for p in layer.parameters() if p.requires_grad]
+            numel = sum(p.numel() for p in grads)
+            if world <= 2 and all(p.dtype == torch.float32 for p in grads) and numel <= 1 << 24:
+                # f32 gradients of a few MiB on two GPUs: the NVLink peer-memory all-reduce
+                # kernel (one-shot; NCCL's protocol is latency-bound at this size).
+                peer = PeerAllReduce(numel)
+                # The b200 Pairwise backward starts the LUT gradient's all-reduce itself, on
+                # a side stream overlapping its remaining kernels; reduce_grads() does the
+                # rest. (With NCCL the overlapped calls measured slower than one call.)
+                stack.enter_context(overlapped_gradient_sync(peer=peer))
+        try:
+            return _run_b200_body(args, w, rank, world, device, layer, peer)
+        finally:
+            if peer is not None:
+                peer.close()
+            if world > 1:
+                import torch.distributed as dist
+
+                dist.destroy_process_group()
+
+
+def _run_b200_body(
+    args: argparse.Namespace, w: Workload, rank: int, world: int, device: torch.device, layer, peer
+) -> dict | None:
+    from tropnn_b200 import trace
+    from tropnn_b200.distributed import allreduce_gradients
+
     x_host, g_host = _make_inputs(w, rank, device)
     x = x_host.to(device).requires_grad_(w.train)
     g = g_host.to(device)
@@ -379,7 +407,7 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
 
     def reduce_grads() -> None:
         if world > 1 and w.train:
-            allreduce_gradients(layer)
+            allreduce_gradients(layer, peer=peer)
 
     def eager_step() -> None:
         _step(layer, x, g, w)
@@ -389,14 +417,17 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
         eager_step()
     _barrier_sync(world, device)
 
-    # Timed region: the step captured once as a CUDA graph (no host launch gaps) and
-    # replayed; at N>1 the NCCL gradient all-reduce follows each replay.
-    graph = _capture(lambda: _step(layer, x, g, w), device)
+    # Timed region: the step, with the NCCL gradient all-reduce at N>1, captured once as a
+    # CUDA graph (no host launch gaps) and replayed.
+    def full_step() -> None:
+        _step(layer, x, g, w)
+        reduce_grads()
+
+    graph = _capture(full_step, device)
     sampler = ClockSampler(device)
 
     def graph_step() -> None:
         graph.replay()
-        reduce_grads()
 
     with sampler:
         total_ms = _max_over_ranks(_timed(args.steps, graph_step, flush, world, device), world, device)
@@ -446,10 +477,6 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
     e2e_ms = _max_over_ranks(_timed(args.steps, e2e_step, flush, world, device), world, device)
     del graph
 
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
     if rank != 0:
         return None
 
@@ -502,9 +529,9 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
             "workload": w.description,
             "rows_per_gpu": w.rows_per_gpu,
             "global_batch": rows_total,
-            "parallelism": f"dp{world} (batch-row shards, NCCL grad all-reduce)" if world > 1 else "single GPU",
+            "parallelism": (f"dp{world} (batch-row shards, {'NVLink peer-memory' if peer is not None else 'NCCL'} grad all-reduce)" if world > 1 else "single GPU"),
             "l2": f"flushed between timed steps ({L2_FLUSH_BYTES >> 20} MiB write, untimed)",
-            "timing": "step captured as one CUDA graph and replayed (all-reduce eager after it at N>1)",
+            "timing": "step (with the NCCL gradient all-reduce at N>1) captured as one CUDA graph and replayed",
         },
         "eager": {"value": round(rows_total * args.steps / (eager_ms / 1e3), 1), "unit": "rows/s",
                   "ms_per_step": round(eager_ms / args.steps, 4)},

@@ -276,6 +276,41 @@ TROPNN_B200_API int tropnn_b200_linear_f32out(const void *a, int64_t rows, int64
                               int64_t out_features, int64_t in_features, int dtype, const float *bias,
                               float *out, void *stream);
 
+/* ------------------------------------------------------------------ multi-GPU */
+
+#define TROPNN_B200_PEER_MAX_RANKS 8
+#define TROPNN_B200_PEER_MAX_SEGMENTS 8
+#define TROPNN_B200_PEER_HANDLE_BYTES 64
+
+/*
+ * Peer buffers for tropnn_b200_peer_allreduce_f32: one per rank (one process per GPU on one
+ * node). _create allocates this rank's buffer (cudaMalloc; capacity_floats a multiple of
+ * 64) and writes its CUDA IPC handle (TROPNN_B200_PEER_HANDLE_BYTES bytes) to `handle`;
+ * the ranks exchange handles, and _open maps another rank's buffer into this process.
+ * _close unmaps a peer's buffer, _destroy frees this rank's. These four are the setup of
+ * the batch-sharded data parallelism (no reference counterpart: the reference is
+ * single-device) and the only entry points that allocate.
+ */
+TROPNN_B200_API int tropnn_b200_peer_buffer_create(int64_t capacity_floats, void **local, unsigned char *handle);
+TROPNN_B200_API int tropnn_b200_peer_buffer_open(const unsigned char *handle, void **peer);
+TROPNN_B200_API int tropnn_b200_peer_buffer_close(void *peer);
+TROPNN_B200_API int tropnn_b200_peer_buffer_destroy(void *local);
+
+/*
+ * In-place sum (average when `average`) of the f32 tensors `segments[s]` (counts[s]
+ * floats each, nseg <= TROPNN_B200_PEER_MAX_SEGMENTS, total <= capacity_floats) across
+ * `world` ranks over NVLink peer memory: buffers[p] is rank p's peer buffer as mapped in
+ * this process (this rank's own at index `rank`). Every rank must make the same calls in
+ * the same order. One kernel: each rank stores its tensors into every rank's buffer over
+ * NVLink, one flag barrier, then each rank sums the copies from its own memory in rank
+ * order (bit-identical results on all ranks). A rank that does not arrive within 2 s
+ * makes the others return with the device error word set (tropnn_b200_device_error).
+ * Each peer buffer holds 2 x 8 receive areas of capacity_floats (double-buffered).
+ */
+TROPNN_B200_API int tropnn_b200_peer_allreduce_f32(void *const *buffers, int world, int rank, int64_t capacity_floats,
+                                   float *const *segments, const int64_t *counts, int nseg, int average,
+                                   void *stream);
+
 /*
  * Reads and clears the library's device error words: 1 after a tensor-core kernel gave up
  * a bounded wait (its CTA then released its resources and exited). Synchronises with the

@@ -97,3 +97,44 @@ def test_two_rank_allreduce_equals_full_batch_gradient() -> None:
         np.testing.assert_allclose(gthr, full_thr, rtol=1e-5, atol=1e-7)
         assert calls >= 2  # the LUT gradient (24 KiB) is reduced in 4 KiB slices
     np.testing.assert_array_equal(results[0][1], results[1][1])
+
+
+def _overlap_rank(rank: int, world: int, port: int, queue) -> None:
+    from tropnn_b200 import distributed as tdist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        a = torch.nn.Parameter(torch.zeros(5))
+        b = torch.nn.Parameter(torch.zeros(3))
+        a.grad = torch.full((5,), float(rank + 1))
+        b.grad = torch.full((3,), float(10 * (rank + 1)))
+        # Outside the context the in-backward hooks do nothing.
+        tdist.reduce_gradient_now(b.grad)
+        untouched = b.grad.clone()
+        with tdist.overlapped_gradient_sync():
+            tdist.reduce_gradient_now(b.grad)  # as the Pairwise backward does for thresholds
+        calls = allreduce_gradients([a, b])  # must skip b (already averaged), reduce a
+        calls_again = allreduce_gradients([a, b])  # the mark is consumed: b is reduced now
+        queue.put((rank, untouched.numpy(), a.grad.numpy(), b.grad.numpy(), calls, calls_again))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_overlapped_sync_marks_and_skips() -> None:
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_overlap_rank, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [queue.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, untouched, ga, gb, calls, calls_again in results:
+        assert np.array_equal(untouched, np.full(3, 10.0 * (rank + 1)))
+        assert np.allclose(ga, np.full(5, 1.5))  # mean of 1 and 2, reduced once
+        assert np.allclose(gb, np.full(3, 15.0))  # mean of 10 and 20 (second pass: mean of equal values)
+        assert calls == 1 and calls_again == 1

@@ -37,6 +37,7 @@ int trop_code_transpose_impl(const void *code, int pt, int64_t H, int64_t K, int
                              cudaStream_t stream);
 int read_hidden_error(int *value);
 int read_gemm_error(int *value);
+int read_peer_error(int *value);
 
 namespace {
 
@@ -661,11 +662,12 @@ int tropnn_b200_trop_code_transpose(const void *code, int param_dtype, int64_t h
 
 int tropnn_b200_device_error(int *value) {
   TB_CHECK(tropnn_b200::check_current_device());
-  int score = 0, hidden = 0, gemm = 0;
+  int score = 0, hidden = 0, gemm = 0, peer = 0;
   TB_CHECK(tropnn_b200::read_score_error(&score));
   TB_CHECK(tropnn_b200::read_hidden_error(&hidden));
   TB_CHECK(tropnn_b200::read_gemm_error(&gemm));
-  *value = score | hidden | gemm;
+  TB_CHECK(tropnn_b200::read_peer_error(&peer));
+  *value = score | hidden | gemm | peer;
   return tropnn_b200::clear_error();
 }
 

@@ -18,6 +18,7 @@ import torch
 from torch import Tensor
 
 from . import _native as nat
+from . import distributed as _dist
 from . import trace
 
 __all__ = [
@@ -198,6 +199,9 @@ class _PairwiseB200Function(torch.autograd.Function):
                 None,
                 stream,
             )
+        # Under distributed.overlapped_gradient_sync the LUT gradient's all-reduce runs on a
+        # side stream while the straight-through kernels below execute.
+        pending = _dist.begin_gradient_reduce(grad_lut) if grad_lut is not None else None
 
         grad_latent = grad_thr = None
         want_latent = ctx.needs_input_grad[0]
@@ -251,6 +255,9 @@ class _PairwiseB200Function(torch.autograd.Function):
                 )
             if want_latent:
                 grad_latent = gx.view(batch, steps, in_features)
+        _dist.end_gradient_reduce(pending, dev)
+        if grad_thr is not None:
+            _dist.reduce_gradient_now(grad_thr)
         return grad_latent, grad_thr, grad_lut, None, None, None, None, None, None, None
 
 
