@@ -112,6 +112,12 @@ WORKLOADS = {
         description="config 5: TropLinear(4096->4096, H1024, K16, D256), f16 params, eval forward, batch 65536",
         cpu_sample_rows=256,
     ),
+    "trop_cfg5_train": Workload(
+        "trop_cfg5_train", "trop", 4096, 4096, 16384, True, dtype="float16",
+        layer_kwargs=dict(heads=1024, cells=16, code_dim=256),
+        description="config 5: TropLinear(4096->4096, H1024, K16, D256), f16 params, train step (fwd + min-face bwd), batch 16384",
+        cpu_sample_rows=32,
+    ),
 }
 
 
