@@ -319,6 +319,43 @@ TROPNN_B200_API int tropnn_b200_peer_allreduce_f32(void *const *buffers, int wor
 TROPNN_B200_API int tropnn_b200_device_error(int *value);
 
 /*
+ * Tensor-core min-face backward for half-precision parameters (layers/tropical_exact.py:
+ * 204-237), four GEMMs whose left operand is the (weighted) one-hot route matrix or whose
+ * epilogue reads the routes; U8 routes, cells in {2,4,8,16,32}, code_dim in {64,...,256}
+ * (a multiple of 64), items a multiple of 8 and >= 128.
+ *
+ * trop_gm: gm[n,h] = code_scale (<g_n, code[h,r]> - <g_n, code[h,w]>) U'(m_nh),
+ *   U'(m) = -0.5 sign(m) / (1+|m|)^2, from g_split = [hi | lo] halves of grad_hidden
+ *   (tropnn_b200_split_half, [items, 2*code_dim]) against code ([heads*cells, code_dim]).
+ * trop_router_term: grad_latent = grad_hidden + sum_h gm[n,h] (W[h,w] - W[h,r]), with
+ *   router_weight_t = router_weight transposed ([code_dim, heads*cells],
+ *   tropnn_b200_trop_code_transpose); gm rounded to the parameter dtype in the product.
+ * trop_param_grad: grad[h,k,:] = out_scale sum_n (vw [w==k] + vr [r==k]) x[n,:] with x_t =
+ *   x transposed to the parameter dtype ([code_dim, items], tropnn_b200_transpose_to_half):
+ *   mode 0 (code grad, eval): vw = 1, vr = 0, out_scale = code_scale, x = grad_hidden;
+ *   mode 1 (code grad, training): vw = 1-U(m), vr = U(m) (values = margins), out_scale =
+ *   code_scale, x = grad_hidden; mode 2 (router grad): vw = gm, vr = -gm (values = gm),
+ *   out_scale = 1, x = latent, and grad_bias[h,k] = sum_n gm ([w==k] - [r==k]) when not NULL.
+ *   grad / grad_bias in the parameter dtype; x_t's rounding of grad_hidden is within the 2e-2
+ *   half-precision tolerance.
+ * transpose_to_half: out[c, r] = x[r, c] rounded to dtype; x in x_dtype (F32 or dtype).
+ * No reference counterparts as entry points: they restate the reference's backward as GEMMs.
+ */
+TROPNN_B200_API int tropnn_b200_trop_gm(const void *g_split, int64_t items, int64_t code_dim, const void *code,
+                        int param_dtype, int64_t heads, int64_t cells, const void *winner, const void *runner,
+                        const float *margins, float code_scale, float *gm, void *stream);
+TROPNN_B200_API int tropnn_b200_trop_router_term(const float *grad_hidden, int64_t items, int64_t code_dim,
+                                 const void *router_weight_t, int param_dtype, int64_t heads, int64_t cells,
+                                 const void *winner, const void *runner, const float *gm, float *grad_latent,
+                                 void *stream);
+TROPNN_B200_API int tropnn_b200_trop_param_grad(int mode, const void *x_t, int64_t items, int64_t code_dim,
+                                int param_dtype, int64_t heads, int64_t cells, const void *winner,
+                                const void *runner, const float *values, float code_scale, void *grad,
+                                void *grad_bias, void *stream);
+TROPNN_B200_API int tropnn_b200_transpose_to_half(const void *x, int x_dtype, int64_t rows, int64_t cols, int dtype,
+                                  void *out, void *stream);
+
+/*
  * Per-row part of the min-face backward (layers/tropical_exact.py:204-237):
  *   training: gm[n,h] = code_scale * U'(m) * sum_d g[n,d] (code[h,r,d] - code[h,w,d]),
  *             U'(m) = -0.5 sign(m) / (1+|m|)^2

@@ -69,11 +69,25 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, Barrier
   return sm100::mbar_wait(bar, parity, &bs->abort, &g_gemm_error);
 }
 
-template <typename PT>
+// Epilogue of the min-face backward's route-margin gradient (kernel mode GM): the GEMM
+// computes <g_n, c_{h,k}> for every cell, the epilogue keeps the winner's and the
+// runner-up's and forms gm[n,h] = code_scale (<g,c_r> - <g,c_w>) U'(m),
+// U'(m) = -0.5 sign(m) / (1+|m|)^2 (layers/tropical_exact.py:204-237).
+struct GmArgs {
+  const uint8_t *winner;
+  const uint8_t *runner;
+  const float *margins;
+  float *gm;
+  int64_t rows;
+  int heads;
+  float code_scale;
+};
+
+template <typename PT, int K>  // K = 0: f32 output map; K = cells: route-margin gradient
 __global__ void __launch_bounds__(kThreads, 1) linear_f32out_kernel(
     const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
     const __grid_constant__ CUtensorMap map_out, const float *__restrict__ bias, int out_features, int slices,
-    int b_kblocks, int stages, int tiles_total, int64_t units) {
+    int b_kblocks, int stages, int tiles_total, int64_t units, const GmArgs gmx) {
   constexpr uint32_t kIdesc =
       umma_idesc_f16(std::is_same<PT, __half>::value ? 0 : 1, kBM, kBN);
   const int a_blocks = slices * b_kblocks;
@@ -234,8 +248,50 @@ __global__ void __launch_bounds__(kThreads, 1) linear_f32out_kernel(
       for (int c = 0; c < kEpiCols; c += 32) {
         float v[32];
         tmem_ld32(taddr + uint32_t(c), v);
-        float bv[32];
         const int cc = col0 + c;
+        if constexpr (K > 0) {
+          // Route-margin gradient: 32 / K heads of this row in the chunk.
+          constexpr int kHeads = 32 / K;
+          const int64_t row = rb * kBM + quarter * 32 + lane;
+          const int h0 = cc / K;
+          uint32_t wv[kHeads], rv[kHeads];
+          float mv[kHeads];
+#pragma unroll
+          for (int hh = 0; hh < kHeads; ++hh) {
+            wv[hh] = rv[hh] = 0u;
+            mv[hh] = 0.f;
+            if (row < gmx.rows && h0 + hh < gmx.heads) {
+              const int64_t o = row * gmx.heads + h0 + hh;
+              wv[hh] = __ldg(gmx.winner + o);
+              rv[hh] = __ldg(gmx.runner + o);
+              mv[hh] = __ldg(gmx.margins + o);
+            }
+          }
+          tmem_wait_ld();
+          reg_fence(v);
+          if (c + 32 == kEpiCols) {
+            tmem_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bs->tmem_empty[b]);
+          }
+#pragma unroll
+          for (int hh = 0; hh < kHeads; ++hh) {
+            float dw = 0.f, dr = 0.f;
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+              dw = wv[hh] == uint32_t(k) ? v[hh * K + k] : dw;
+              dr = rv[hh] == uint32_t(k) ? v[hh * K + k] : dr;
+            }
+            const float m = mv[hh];
+            const float den = __fadd_rn(1.f, fabsf(m));
+            const float sgn = (m > 0.f) ? 1.f : ((m < 0.f) ? -1.f : 0.f);
+            const float gm = __fmul_rn(__fmul_rn(gmx.code_scale, __fsub_rn(dr, dw)),
+                                       __fdiv_rn(__fmul_rn(-0.5f, sgn), __fmul_rn(den, den)));
+            if (row < gmx.rows && h0 + hh < gmx.heads) gmx.gm[row * gmx.heads + h0 + hh] = gm;
+          }
+          continue;
+        }
+        float bv[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) bv[i] = 0.f;
         if (bias != nullptr) {
@@ -280,8 +336,10 @@ __global__ void __launch_bounds__(kThreads, 1) linear_f32out_kernel(
       }
     }
     // Every store must be complete before the CTA exits.
-    if (lane == 0) bulk_wait_all();
-    __syncwarp();
+    if constexpr (K == 0) {
+      if (lane == 0) bulk_wait_all();
+      __syncwarp();
+    }
   }
 
   tmem_fence_before();
@@ -327,9 +385,9 @@ int linear_stages(int a_blocks) {
   return s >= kMinStages ? s : 0;
 }
 
-template <typename PT>
+template <typename PT, int K>
 int launch_linear(const void *a, int64_t rows, int slices, const void *w, int out_features, int in_features,
-                  const float *bias, float *out, cudaStream_t stream) {
+                  const float *bias, float *out, const GmArgs &gmx, cudaStream_t stream) {
   const CUtensorMapDataType dt =
       std::is_same<PT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int b_kblocks = in_features / kBK;
@@ -339,17 +397,21 @@ int launch_linear(const void *a, int64_t rows, int slices, const void *w, int ou
   CUtensorMap map_a, map_w, map_out;
   TB_CHECK(make_map_k64(&map_a, a, dt, int64_t(slices) * in_features, rows, kBM));
   TB_CHECK(make_map_k64(&map_w, w, dt, in_features, out_features, kBoxRows));
-  TB_CHECK(make_map_f32_store32(&map_out, out, out_features, rows));
+  if constexpr (K == 0) {
+    TB_CHECK(make_map_f32_store32(&map_out, out, out_features, rows));
+  } else {
+    map_out = map_a;  // unused by the route-margin epilogue
+  }
   const int tiles_total = static_cast<int>(ceil_div(int64_t(out_features), int64_t(kBN)));
   const int64_t units = ceil_div(rows, int64_t(kBM)) * tiles_total;
   int sms = 0;
   TB_CHECK(sm_count(&sms));
-  auto kernel = linear_f32out_kernel<PT>;
+  auto kernel = linear_f32out_kernel<PT, K>;
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "linear_f32out"));
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(units, sms));
   kernel<<<grid, kThreads, smem, stream>>>(map_a, map_w, map_out, bias, out_features, slices, b_kblocks, stages,
-                                           tiles_total, units);
-  return check_launch("linear_f32out");
+                                           tiles_total, units, gmx);
+  return check_launch(K == 0 ? "linear_f32out" : "trop_gm_sm100");
 }
 
 }  // namespace
@@ -371,8 +433,36 @@ int linear_f32out_impl(const void *a, int64_t rows, int64_t slices, const void *
   TB_REQUIRE(al16(a) && al16(w) && al16(bias) && al16(out), TROPNN_B200_ERR_INVALID,
              "linear_f32out: operands must be 16-byte aligned");
   const int s = static_cast<int>(slices), n = static_cast<int>(out_features), k = static_cast<int>(in_features);
-  if (dtype == TROPNN_B200_F16) return launch_linear<__half>(a, rows, s, w, n, k, bias, out, stream);
-  return launch_linear<__nv_bfloat16>(a, rows, s, w, n, k, bias, out, stream);
+  const GmArgs none{};
+  if (dtype == TROPNN_B200_F16) return launch_linear<__half, 0>(a, rows, s, w, n, k, bias, out, none, stream);
+  return launch_linear<__nv_bfloat16, 0>(a, rows, s, w, n, k, bias, out, none, stream);
+}
+
+// gm[n,h] of the min-face backward from g split into [hi | lo] ([rows, 2*code_dim]) and
+// the code table [heads*cells, code_dim] (the B operand as stored).
+int trop_gm_sm100_impl(const void *g_split, int64_t rows, int64_t code_dim, const void *code, int dtype, int64_t heads,
+                       int64_t cells, const uint8_t *winner, const uint8_t *runner, const float *margins,
+                       float code_scale, float *gm, cudaStream_t stream) {
+  const int64_t hk = heads * cells;
+  TB_REQUIRE(linear_f32out_supported(rows, 2, hk, code_dim, dtype) &&
+                 (cells == 2 || cells == 4 || cells == 8 || cells == 16 || cells == 32),
+             TROPNN_B200_ERR_INVALID, "trop_gm_sm100: unsupported shape rows=%lld code_dim=%lld heads=%lld cells=%lld",
+             (long long)rows, (long long)code_dim, (long long)heads, (long long)cells);
+  TB_REQUIRE(g_split && code && winner && runner && margins && gm, TROPNN_B200_ERR_INVALID, "trop_gm_sm100: null pointer");
+  const GmArgs gmx{winner, runner, margins, gm, rows, static_cast<int>(heads), code_scale};
+  const int n = static_cast<int>(hk), k = static_cast<int>(code_dim);
+  auto go = [&](auto pt_tag) -> int {
+    using T = decltype(pt_tag);
+    switch (cells) {
+      case 2: return launch_linear<T, 2>(g_split, rows, 2, code, n, k, nullptr, nullptr, gmx, stream);
+      case 4: return launch_linear<T, 4>(g_split, rows, 2, code, n, k, nullptr, nullptr, gmx, stream);
+      case 8: return launch_linear<T, 8>(g_split, rows, 2, code, n, k, nullptr, nullptr, gmx, stream);
+      case 16: return launch_linear<T, 16>(g_split, rows, 2, code, n, k, nullptr, nullptr, gmx, stream);
+      default: return launch_linear<T, 32>(g_split, rows, 2, code, n, k, nullptr, nullptr, gmx, stream);
+    }
+  };
+  if (dtype == TROPNN_B200_F16) return go(__half());
+  return go(__nv_bfloat16());
 }
 
 int split_half_impl(const float *x, int64_t rows, int64_t cols, int dtype, void *out, cudaStream_t stream) {

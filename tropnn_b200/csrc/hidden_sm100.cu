@@ -57,6 +57,11 @@ constexpr size_t kSmemLimit = 227 * 1024;
 constexpr uint32_t kSleepHintNs = 1000000u;
 
 // Library-wide device error word of this kernel: nonzero after a bounded wait gave up.
+// What the one-hot left operand holds per (row, head): 1 at the winner (eval); 1-U(m) at
+// the winner and U(m) at the runner-up (training, min-face mix); +gm at the winner and -gm
+// at the runner-up (backward router term of grad_latent, gm read from `margins`).
+enum OneHotMode { kOneHotEval = 0, kOneHotMinFace = 1, kOneHotSigned = 2 };
+
 __device__ int g_hidden_error = 0;
 
 struct Barriers {
@@ -145,7 +150,7 @@ __device__ __forceinline__ void load_row32(const LT *__restrict__ p, float (&out
   }
 }
 
-template <typename PT, typename LT, int K, bool TRAIN>
+template <typename PT, typename LT, int K, int MODE>
 __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
     const __grid_constant__ CUtensorMap map_ct, const LT *__restrict__ latent, const uint8_t *__restrict__ winner,
     const uint8_t *__restrict__ runner, const float *__restrict__ margins, float code_scale, int64_t rows, int H,
@@ -269,8 +274,8 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
       const int64_t row = rb * kBM + quarter * 32 + lane;
       const bool live = row < rows;
       const uint8_t *wrow = winner + (live ? row : 0) * H;
-      const uint8_t *rrow = TRAIN ? runner + (live ? row : 0) * H : nullptr;
-      const float *mrow = TRAIN ? margins + (live ? row : 0) * H : nullptr;
+      const uint8_t *rrow = MODE != kOneHotEval ? runner + (live ? row : 0) * H : nullptr;
+      const float *mrow = MODE != kOneHotEval ? margins + (live ? row : 0) * H : nullptr;
       const int kbe = kblock_at(kb);
       {
         const int sa = ait % kAStages;
@@ -285,11 +290,16 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
           vr[hh] = 0u;
           if (live && h < H) {
             wc[hh] = __ldg(wrow + h);
-            if constexpr (TRAIN) {
+            if constexpr (MODE == kOneHotMinFace) {
               rc[hh] = __ldg(rrow + h);
               const float alpha = __fdiv_rn(0.5f, __fadd_rn(1.f, fabsf(__ldg(mrow + h))));
               vw[hh] = HalfBits<PT>::bits(__fsub_rn(1.f, alpha));
               vr[hh] = HalfBits<PT>::bits(alpha);
+            } else if constexpr (MODE == kOneHotSigned) {
+              rc[hh] = __ldg(rrow + h);
+              const float gm = __ldg(mrow + h);
+              vw[hh] = HalfBits<PT>::bits(gm);
+              vr[hh] = HalfBits<PT>::bits(-gm);
             }
           }
         }
@@ -308,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
             const uint32_t c0 = 2u * jj, c1 = c0 + 1u;
             uint32_t lo = wc[hh] == c0 ? vw[hh] : 0u;
             uint32_t hi = wc[hh] == c1 ? vw[hh] : 0u;
-            if constexpr (TRAIN) {
+            if constexpr (MODE != kOneHotEval) {
               lo |= rc[hh] == c0 ? vr[hh] : 0u;
               hi |= rc[hh] == c1 ? vr[hh] : 0u;
             }
@@ -390,7 +400,7 @@ int b_stages(int D) {
 
 template <typename PT, typename LT, int K>
 int launch_onehot(const void *latent, int64_t rows, int D, const void *code_t, int H, const uint8_t *win,
-                  const uint8_t *run, const float *m, float code_scale, bool training, float *hidden,
+                  const uint8_t *run, const float *m, float code_scale, int mode, float *hidden,
                   cudaStream_t stream) {
   const CUtensorMapDataType dt =
       std::is_same<PT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -406,7 +416,9 @@ int launch_onehot(const void *latent, int64_t rows, int D, const void *code_t, i
   int sms = 0;
   TB_CHECK(sm_count(&sms));
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(row_blocks, sms));
-  auto kernel = training ? trop_hidden_onehot_kernel<PT, LT, K, true> : trop_hidden_onehot_kernel<PT, LT, K, false>;
+  auto kernel = mode == kOneHotSigned   ? trop_hidden_onehot_kernel<PT, LT, K, kOneHotSigned>
+                : mode == kOneHotMinFace ? trop_hidden_onehot_kernel<PT, LT, K, kOneHotMinFace>
+                                         : trop_hidden_onehot_kernel<PT, LT, K, kOneHotEval>;
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_hidden_sm100"));
   kernel<<<grid, kThreads, smem, stream>>>(map_ct, static_cast<const LT *>(latent), win, run, m, code_scale, rows, H, D,
                                            kblocks, bst, row_blocks, hidden);
@@ -415,16 +427,16 @@ int launch_onehot(const void *latent, int64_t rows, int D, const void *code_t, i
 
 template <typename PT, typename LT>
 int dispatch_onehot(int K, const void *latent, int64_t rows, int D, const void *code_t, int H, const uint8_t *win,
-                    const uint8_t *run, const float *m, float code_scale, bool training, float *hidden,
+                    const uint8_t *run, const float *m, float code_scale, int mode, float *hidden,
                     cudaStream_t stream) {
   switch (K) {
-    case 2: return launch_onehot<PT, LT, 2>(latent, rows, D, code_t, H, win, run, m, code_scale, training, hidden, stream);
-    case 4: return launch_onehot<PT, LT, 4>(latent, rows, D, code_t, H, win, run, m, code_scale, training, hidden, stream);
-    case 8: return launch_onehot<PT, LT, 8>(latent, rows, D, code_t, H, win, run, m, code_scale, training, hidden, stream);
+    case 2: return launch_onehot<PT, LT, 2>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, hidden, stream);
+    case 4: return launch_onehot<PT, LT, 4>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, hidden, stream);
+    case 8: return launch_onehot<PT, LT, 8>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, hidden, stream);
     case 16:
-      return launch_onehot<PT, LT, 16>(latent, rows, D, code_t, H, win, run, m, code_scale, training, hidden, stream);
+      return launch_onehot<PT, LT, 16>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, hidden, stream);
     default:
-      return launch_onehot<PT, LT, 32>(latent, rows, D, code_t, H, win, run, m, code_scale, training, hidden, stream);
+      return launch_onehot<PT, LT, 32>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, hidden, stream);
   }
 }
 
@@ -441,25 +453,25 @@ bool hidden_sm100_supported(int64_t items, int64_t D, int64_t H, int64_t K, int 
 
 int trop_hidden_sm100_impl(const void *latent, int zt, int64_t items, int64_t D, const void *code_t, int pt,
                            int64_t H, int64_t K, const void *win, const void *run, const float *m, float code_scale,
-                           int training, float *hidden, cudaStream_t stream) {
+                           int mode, float *hidden, cudaStream_t stream) {
   TB_REQUIRE(hidden_sm100_supported(items, D, H, K, pt, zt, TROPNN_B200_U8, latent, code_t, hidden),
              TROPNN_B200_ERR_INVALID, "trop_hidden_sm100: unsupported shape, dtype or alignment");
-  TB_REQUIRE(win && (!training || (run && m)), TROPNN_B200_ERR_INVALID, "trop_hidden_sm100: null pointer");
+  TB_REQUIRE(mode >= kOneHotEval && mode <= kOneHotSigned, TROPNN_B200_ERR_INVALID, "trop_hidden_sm100: bad mode");
+  TB_REQUIRE(win && (mode == kOneHotEval || (run && m)), TROPNN_B200_ERR_INVALID, "trop_hidden_sm100: null pointer");
   const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
   const auto *w = static_cast<const uint8_t *>(win);
   const auto *r = static_cast<const uint8_t *>(run);
-  const bool train = training != 0;
   if (pt == TROPNN_B200_F16) {
     if (zt == TROPNN_B200_F32)
-      return dispatch_onehot<__half, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, train, hidden,
+      return dispatch_onehot<__half, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, hidden,
                                             stream);
-    return dispatch_onehot<__half, __half>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, train, hidden,
+    return dispatch_onehot<__half, __half>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, hidden,
                                            stream);
   }
   if (zt == TROPNN_B200_F32)
-    return dispatch_onehot<__nv_bfloat16, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, train, hidden,
+    return dispatch_onehot<__nv_bfloat16, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, hidden,
                                                  stream);
-  return dispatch_onehot<__nv_bfloat16, __nv_bfloat16>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, train,
+  return dispatch_onehot<__nv_bfloat16, __nv_bfloat16>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode,
                                                        hidden, stream);
 }
 

@@ -342,6 +342,79 @@ def _onehot_hidden_eligible(items: int, code_dim: int, heads: int, cells: int, d
     )
 
 
+def _tc_backward_eligible(items: int, code_dim: int, heads: int, cells: int, dtype: torch.dtype, idx: torch.dtype) -> bool:
+    """Shapes the tensor-core min-face backward takes (trop_gm / trop_router_term / trop_param_grad)."""
+    return (
+        dtype in (torch.float16, torch.bfloat16)
+        and idx == torch.uint8
+        and cells in (2, 4, 8, 16, 32)
+        and code_dim % 64 == 0
+        and 64 <= code_dim <= 256
+        and (heads * cells) % 8 == 0
+        and items >= 128
+        and items % 8 == 0
+    )
+
+
+def _trop_backward_tensor_cores(ctx, g, z, weight, code, winner, runner, margins, lib, stream):
+    """Min-face backward as four tcgen05 GEMMs (layers/tropical_exact.py:204-237):
+    gm from <g, c_r - c_w> (split-f32 g against the code table, route-picking epilogue),
+    grad_latent's router term as a one-hot GEMM with +-gm weights against router_weight^T,
+    and the code / router gradients as P^T X with X = g^T or z^T (one tile of 128 cells per
+    CTA, the weighted one-hot P^T assembled in TMEM)."""
+    batch, steps, code_dim, heads, cells = ctx.shape
+    items = batch * steps
+    dev = g.device
+    training = ctx.training
+    pdt = nat.float_code(weight.dtype)
+    hk = heads * cells
+    gm = None
+    if training:
+        g_split = torch.empty((items, 2 * code_dim), device=dev, dtype=weight.dtype)
+        _launch("split_half", lib.tropnn_b200_split_half, g.data_ptr(), items, code_dim, pdt, g_split.data_ptr(), stream)
+        gm = torch.empty((items, heads), device=dev, dtype=torch.float32)
+        _launch(
+            "trop_gm", lib.tropnn_b200_trop_gm, g_split.data_ptr(), items, code_dim, code.data_ptr(), pdt, heads, cells,
+            winner.data_ptr(), runner.data_ptr(), margins.data_ptr(), ctx.code_scale, gm.data_ptr(), stream,
+        )
+        w_t = torch.empty((code_dim, hk), device=dev, dtype=weight.dtype)
+        _launch("trop_code_transpose", lib.tropnn_b200_trop_code_transpose, weight.data_ptr(), pdt, heads, cells, code_dim,
+                w_t.data_ptr(), stream)
+        grad_z = torch.empty((items, code_dim), device=dev, dtype=torch.float32)
+        _launch(
+            "trop_router_term", lib.tropnn_b200_trop_router_term, g.data_ptr(), items, code_dim, w_t.data_ptr(), pdt, heads,
+            cells, winner.data_ptr(), runner.data_ptr(), gm.data_ptr(), grad_z.data_ptr(), stream,
+        )
+    else:
+        grad_z = g
+    grad_w = grad_b = grad_c = None
+    if ctx.needs_input_grad[3]:
+        g_t = torch.empty((code_dim, items), device=dev, dtype=weight.dtype)
+        _launch("transpose_to_half", lib.tropnn_b200_transpose_to_half, g.data_ptr(), nat.F32, items, code_dim, pdt,
+                g_t.data_ptr(), stream)
+        grad_c = torch.empty_like(code)
+        _launch(
+            "trop_code_grad", lib.tropnn_b200_trop_param_grad, 1 if training else 0, g_t.data_ptr(), items, code_dim, pdt,
+            heads, cells, winner.data_ptr(), nat.ptr(runner), margins.data_ptr() if training else None, ctx.code_scale,
+            grad_c.data_ptr(), None, stream,
+        )
+    if training and (ctx.needs_input_grad[1] or ctx.needs_input_grad[2]):
+        z_t = torch.empty((code_dim, items), device=dev, dtype=weight.dtype)
+        _launch("transpose_to_half", lib.tropnn_b200_transpose_to_half, z.data_ptr(), nat.float_code(z.dtype), items,
+                code_dim, pdt, z_t.data_ptr(), stream)
+        grad_w = torch.empty_like(weight)
+        grad_b = torch.empty((heads, cells), device=dev, dtype=weight.dtype)
+        _launch(
+            "trop_router_grad", lib.tropnn_b200_trop_param_grad, 2, z_t.data_ptr(), items, code_dim, pdt, heads, cells,
+            winner.data_ptr(), runner.data_ptr(), gm.data_ptr(), 1.0, grad_w.data_ptr(), grad_b.data_ptr(), stream,
+        )
+    if not ctx.needs_input_grad[1]:
+        grad_w = None
+    if not ctx.needs_input_grad[2]:
+        grad_b = None
+    return grad_z.view(batch, steps, code_dim).to(z.dtype), grad_w, grad_b, grad_c, None, None, None
+
+
 class _TropRouteB200Function(torch.autograd.Function):
     @staticmethod
     def forward(  # type: ignore[override]
@@ -458,6 +531,9 @@ class _TropRouteB200Function(torch.autograd.Function):
         lib = nat.load()
         pdt = nat.float_code(weight.dtype)
         icode = nat.index_code(winner.dtype)
+
+        if _tc_backward_eligible(items, code_dim, heads, cells, weight.dtype, winner.dtype):
+            return _trop_backward_tensor_cores(ctx, g, z, weight, code, winner, runner, margins, lib, stream)
 
         coef_w = coef_r = gm = None
         if training and items > 0:
