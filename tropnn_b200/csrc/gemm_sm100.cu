@@ -254,17 +254,23 @@ __global__ void __launch_bounds__(kThreads, 1) linear_f32out_kernel(
           constexpr int kHeads = 32 / K;
           const int64_t row = rb * kBM + quarter * 32 + lane;
           const int h0 = cc / K;
+          // Routes and the margin factor code_scale * U'(m) of each head, computed while the
+          // TMEM read is in flight (and before the 32 accumulator values are live, so that
+          // the division does not force them out of registers).
           uint32_t wv[kHeads], rv[kHeads];
-          float mv[kHeads];
+          float fv[kHeads];
 #pragma unroll
           for (int hh = 0; hh < kHeads; ++hh) {
             wv[hh] = rv[hh] = 0u;
-            mv[hh] = 0.f;
+            fv[hh] = 0.f;
             if (row < gmx.rows && h0 + hh < gmx.heads) {
               const int64_t o = row * gmx.heads + h0 + hh;
               wv[hh] = __ldg(gmx.winner + o);
               rv[hh] = __ldg(gmx.runner + o);
-              mv[hh] = __ldg(gmx.margins + o);
+              const float m = __ldg(gmx.margins + o);
+              const float den = __fadd_rn(1.f, fabsf(m));
+              const float sgn = (m > 0.f) ? 1.f : ((m < 0.f) ? -1.f : 0.f);
+              fv[hh] = __fmul_rn(gmx.code_scale, __fdiv_rn(__fmul_rn(-0.5f, sgn), __fmul_rn(den, den)));
             }
           }
           tmem_wait_ld();
@@ -276,17 +282,18 @@ __global__ void __launch_bounds__(kThreads, 1) linear_f32out_kernel(
           }
 #pragma unroll
           for (int hh = 0; hh < kHeads; ++hh) {
-            float dw = 0.f, dr = 0.f;
+            // Bitwise pick (one cell matches): written as masks, not selects, so that the
+            // compiler keeps the accumulator values in registers instead of turning the chain
+            // into an indexed load from a local-memory copy.
+            uint32_t bw = 0u, br = 0u;
 #pragma unroll
             for (int k = 0; k < K; ++k) {
-              dw = wv[hh] == uint32_t(k) ? v[hh * K + k] : dw;
-              dr = rv[hh] == uint32_t(k) ? v[hh * K + k] : dr;
+              const uint32_t x = __float_as_uint(v[hh * K + k]);
+              bw |= x & (0u - uint32_t(wv[hh] == uint32_t(k)));
+              br |= x & (0u - uint32_t(rv[hh] == uint32_t(k)));
             }
-            const float m = mv[hh];
-            const float den = __fadd_rn(1.f, fabsf(m));
-            const float sgn = (m > 0.f) ? 1.f : ((m < 0.f) ? -1.f : 0.f);
-            const float gm = __fmul_rn(__fmul_rn(gmx.code_scale, __fsub_rn(dr, dw)),
-                                       __fdiv_rn(__fmul_rn(-0.5f, sgn), __fmul_rn(den, den)));
+            const float dw = __uint_as_float(bw), dr = __uint_as_float(br);
+            const float gm = __fmul_rn(__fsub_rn(dr, dw), fv[hh]);
             if (row < gmx.rows && h0 + hh < gmx.heads) gmx.gm[row * gmx.heads + h0 + hh] = gm;
           }
           continue;

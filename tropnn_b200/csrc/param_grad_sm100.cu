@@ -226,6 +226,55 @@ __global__ void __launch_bounds__(kThreads, 1) trop_param_grad_kernel(
     const uint32_t cell = uint32_t(L % K);
     const uint32_t lane_base = tmem_base + (uint32_t(quarter * 32) << 16) + kAColBase;
     uint2 *my_stage = stage + parity * kStageEntries;
+    // Entries of a staged k block per builder thread; with few of them (cells >= 8) the
+    // raw route bytes and weights of the set's next k block are loaded into registers while
+    // the current one is built, so their latency leaves the critical path.
+    constexpr int kPer = kBK * kHeadsPerTile / 128;
+    constexpr bool kPrefetch = kPer <= 8;
+    constexpr int kPerRegs = kPrefetch ? kPer : 1;
+    uint32_t pw[kPerRegs], pr[kPerRegs];
+    float pm[kPerRegs];
+    auto fetch = [&](int a) {
+      const int i = a / kblocks;
+      const int kb = a - i * kblocks;
+      const int tile = blockIdx.x + i * gridDim.x;
+      const int h0 = tile * kHeadsPerTile;
+      const int64_t n0 = int64_t(kb) * kBK;
+#pragma unroll
+      for (int q = 0; q < kPerRegs; ++q) {
+        const int e = tid + q * 128;
+        const int rr = e / kHeadsPerTile;
+        const int h = h0 + (e - rr * kHeadsPerTile);
+        const int64_t n = n0 + rr;
+        pw[q] = pr[q] = 0xFFu;
+        pm[q] = 0.f;
+        if (tile < tiles && n < rows && h < H) {
+          const int64_t o = n * H + h;
+          pw[q] = __ldg(winner + o);
+          if constexpr (MODE != kCodeEval) {
+            pr[q] = __ldg(runner + o);
+            pm[q] = __ldg(mvals + o);
+          }
+        }
+      }
+    };
+    auto encode = [&](uint32_t w, uint32_t r, float mv) -> uint2 {
+      uint32_t vw = 0u, vr = 0u;
+      if (w != 0xFFu) {
+        if constexpr (MODE == kCodeEval) {
+          vw = half_bits<PT>(1.f);  // code_scale is applied in f32 by the epilogue
+        } else if constexpr (MODE == kCodeTrain) {
+          const float alpha = __fdiv_rn(0.5f, __fadd_rn(1.f, fabsf(mv)));
+          vw = half_bits<PT>(__fsub_rn(1.f, alpha));
+          vr = half_bits<PT>(alpha);
+        } else {
+          vw = half_bits<PT>(mv);
+          vr = half_bits<PT>(-mv);
+        }
+      }
+      return make_uint2(w | (r << 8), vw | (vr << 16));
+    };
+    if constexpr (kPrefetch) fetch(parity);
     for (int ait = parity;; ait += 2) {
       const int i = ait / kblocks;
       const int kb = ait - i * kblocks;
@@ -236,29 +285,27 @@ __global__ void __launch_bounds__(kThreads, 1) trop_param_grad_kernel(
       // Stage [64 rows x kHeadsPerTile heads] of {winner, runner, vw bits, vr bits}; the
       // previous k block of this parity has been consumed (its builders passed the named
       // barrier below after reading it).
-      for (int e = tid; e < kBK * kHeadsPerTile; e += 128) {
-        const int rr = e / kHeadsPerTile;
-        const int h = h0 + (e - rr * kHeadsPerTile);
-        const int64_t n = n0 + rr;
-        uint32_t w = 0xFFu, r = 0xFFu, vw = 0u, vr = 0u;
-        if (n < rows && h < H) {
-          const int64_t o = n * H + h;
-          w = __ldg(winner + o);
-          if constexpr (MODE == kCodeEval) {
-            vw = half_bits<PT>(1.f);  // code_scale is applied in f32 by the epilogue
-          } else if constexpr (MODE == kCodeTrain) {
-            r = __ldg(runner + o);
-            const float alpha = __fdiv_rn(0.5f, __fadd_rn(1.f, fabsf(__ldg(mvals + o))));
-            vw = half_bits<PT>(__fsub_rn(1.f, alpha));
-            vr = half_bits<PT>(alpha);
-          } else {
-            r = __ldg(runner + o);
-            const float gm = __ldg(mvals + o);
-            vw = half_bits<PT>(gm);
-            vr = half_bits<PT>(-gm);
+      if constexpr (kPrefetch) {
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) my_stage[tid + q * 128] = encode(pw[q], pr[q], pm[q]);
+        fetch(ait + 2);
+      } else {
+        for (int e = tid; e < kBK * kHeadsPerTile; e += 128) {
+          const int rr = e / kHeadsPerTile;
+          const int h = h0 + (e - rr * kHeadsPerTile);
+          const int64_t n = n0 + rr;
+          uint32_t w = 0xFFu, r = 0xFFu;
+          float mv = 0.f;
+          if (n < rows && h < H) {
+            const int64_t o = n * H + h;
+            w = __ldg(winner + o);
+            if constexpr (MODE != kCodeEval) {
+              r = __ldg(runner + o);
+              mv = __ldg(mvals + o);
+            }
           }
+          my_stage[e] = encode(w, r, mv);
         }
-        my_stage[e] = make_uint2(w | (r << 8), vw | (vr << 16));
       }
       // One thread of the set waits for the TMEM slot; the verdict passes through a
       // two-slot flag behind the named barrier, so all 128 builders of the set take the same
