@@ -28,6 +28,8 @@
 
 #include <type_traits>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -382,33 +384,87 @@ __global__ void __launch_bounds__(kThreads, 1) trop_param_grad_kernel(
   }
 }
 
-// Router-bias gradient: grad_b[h,k] = sum_n gm[n,h] ([w==k] - [r==k]); one CTA per head,
-// fixed-order reduction (deterministic).
+// Router-bias gradient: grad_b[h,k] = sum_n gm[n,h] ([w==k] - [r==k]). A cluster of
+// kBiasSlices CTAs owns 32 heads (one per lane, so every warp load reads 32 consecutive heads of
+// a row); CTA y of the cluster takes row slice y, its 16 warps take interleaved rows. Warp
+// partials are combined in warp order, then slice partials in slice order through distributed
+// shared memory, so the result is deterministic.
+constexpr int kBiasSlices = 8, kBiasWarps = 16;
+
+template <int K>
+constexpr size_t bias_smem_bytes() {
+  return sizeof(float) * (size_t(kBiasWarps) * 32 * (K + 1) + 32 * K);
+}
+
 template <typename PT, int K>
-__global__ void __launch_bounds__(256) router_bias_grad_kernel(const uint8_t *__restrict__ winner,
-                                                               const uint8_t *__restrict__ runner,
-                                                               const float *__restrict__ gm, int64_t rows, int H,
-                                                               PT *__restrict__ grad_b) {
-  __shared__ float part[256][K + 1];
-  const int h = blockIdx.x;
+__global__ void __cluster_dims__(1, kBiasSlices, 1) __launch_bounds__(kBiasWarps * 32, K >= 32 ? 1 : 2)
+    router_bias_grad_kernel(const uint8_t *__restrict__ winner, const uint8_t *__restrict__ runner,
+                            const float *__restrict__ gm, int64_t rows, int H, PT *__restrict__ grad_b) {
+  extern __shared__ float bias_smem[];
+  float *part = bias_smem;                                    // [kBiasWarps][32][K + 1]
+  float *red = bias_smem + size_t(kBiasWarps) * 32 * (K + 1);  // [32 * K]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int h = blockIdx.x * 32 + lane;
+  const int64_t per = (rows + kBiasSlices - 1) / kBiasSlices;
+  const int64_t n_begin = per * blockIdx.y, n_end = n_begin + per < rows ? n_begin + per : rows;
   float acc[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) acc[k] = 0.f;
-  for (int64_t n = threadIdx.x; n < rows; n += blockDim.x) {
-    const int64_t o = n * H + h;
-    const uint32_t w = __ldg(winner + o), r = __ldg(runner + o);
-    const float v = __ldg(gm + o);
+  if (h < H) {
+    constexpr int kUnroll = 4;
+    for (int64_t n = n_begin + warp; n < n_end; n += kUnroll * kBiasWarps) {
+      uint32_t w[kUnroll], r[kUnroll];
+      float v[kUnroll];
 #pragma unroll
-    for (int k = 0; k < K; ++k) acc[k] = __fadd_rn(acc[k], (w == uint32_t(k) ? v : 0.f) - (r == uint32_t(k) ? v : 0.f));
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t nu = n + int64_t(u) * kBiasWarps;
+        const bool ok = nu < n_end;
+        const int64_t o = (ok ? nu : n) * H + h;
+        w[u] = __ldg(winner + o);
+        r[u] = __ldg(runner + o);
+        v[u] = ok ? __ldg(gm + o) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+          acc[k] = __fadd_rn(acc[k], __fsub_rn(w[u] == uint32_t(k) ? v[u] : 0.f, r[u] == uint32_t(k) ? v[u] : 0.f));
+    }
   }
 #pragma unroll
-  for (int k = 0; k < K; ++k) part[threadIdx.x][k] = acc[k];
+  for (int k = 0; k < K; ++k) part[(warp * 32 + lane) * (K + 1) + k] = acc[k];
   __syncthreads();
-  if (threadIdx.x < K) {
-    float s = 0.f;
-    for (int t = 0; t < 256; ++t) s = __fadd_rn(s, part[t][threadIdx.x]);
-    grad_b[int64_t(h) * K + threadIdx.x] = from_f32<PT>(s);
+  for (int e = threadIdx.x; e < 32 * K; e += kBiasWarps * 32) {
+    const int hl = e / K, k = e - hl * K;
+    float sum = 0.f;
+    for (int wi = 0; wi < kBiasWarps; ++wi) sum = __fadd_rn(sum, part[(wi * 32 + hl) * (K + 1) + k]);
+    red[e] = sum;
   }
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  constexpr int kShare = 32 * K / kBiasSlices;
+  const int slice = static_cast<int>(cluster.block_rank());
+  for (int i = threadIdx.x; i < kShare; i += kBiasWarps * 32) {
+    const int e = slice * kShare + i;
+    float sum = 0.f;
+    for (int y = 0; y < kBiasSlices; ++y) sum = __fadd_rn(sum, cluster.map_shared_rank(red, y)[e]);
+    const int hl = e / K, k = e - hl * K;
+    if (blockIdx.x * 32 + hl < H) grad_b[int64_t(blockIdx.x * 32 + hl) * K + k] = from_f32<PT>(sum);
+  }
+  cluster.sync();
+}
+
+template <typename PT, int K>
+int launch_bias_grad(const uint8_t *w, const uint8_t *r, const float *gm, int64_t rows, int H, PT *grad_b,
+                     cudaStream_t stream) {
+  constexpr size_t smem = bias_smem_bytes<K>();
+  if (smem > 48 * 1024)
+    TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(router_bias_grad_kernel<PT, K>), smem,
+                                 "router_bias_grad"));
+  const dim3 grid(static_cast<unsigned>(ceil_div(int64_t(H), int64_t(32))), kBiasSlices);
+  router_bias_grad_kernel<PT, K><<<grid, kBiasWarps * 32, smem, stream>>>(w, r, gm, rows, H, grad_b);
+  return check_launch("router_bias_grad");
 }
 
 // x [rows_in, cols] (f32 or half) -> out [cols, rows_in] in PT, 32 x 32 tiles.
@@ -506,14 +562,14 @@ int trop_param_grad_sm100_impl(int mode, const void *xt, int64_t rows, int64_t D
   if (mode == 2 && grad_b != nullptr) {
     auto launch_bias = [&](auto pt_tag) -> int {
       using T = decltype(pt_tag);
+      T *gb = static_cast<T *>(grad_b);
       switch (Ki) {
-        case 2: router_bias_grad_kernel<T, 2><<<Hi, 256, 0, stream>>>(w, r, mvals, rows, Hi, static_cast<T *>(grad_b)); break;
-        case 4: router_bias_grad_kernel<T, 4><<<Hi, 256, 0, stream>>>(w, r, mvals, rows, Hi, static_cast<T *>(grad_b)); break;
-        case 8: router_bias_grad_kernel<T, 8><<<Hi, 256, 0, stream>>>(w, r, mvals, rows, Hi, static_cast<T *>(grad_b)); break;
-        case 16: router_bias_grad_kernel<T, 16><<<Hi, 256, 0, stream>>>(w, r, mvals, rows, Hi, static_cast<T *>(grad_b)); break;
-        default: router_bias_grad_kernel<T, 32><<<Hi, 256, 0, stream>>>(w, r, mvals, rows, Hi, static_cast<T *>(grad_b)); break;
+        case 2: return launch_bias_grad<T, 2>(w, r, mvals, rows, Hi, gb, stream);
+        case 4: return launch_bias_grad<T, 4>(w, r, mvals, rows, Hi, gb, stream);
+        case 8: return launch_bias_grad<T, 8>(w, r, mvals, rows, Hi, gb, stream);
+        case 16: return launch_bias_grad<T, 16>(w, r, mvals, rows, Hi, gb, stream);
+        default: return launch_bias_grad<T, 32>(w, r, mvals, rows, Hi, gb, stream);
       }
-      return check_launch("router_bias_grad");
     };
     if (pt == TROPNN_B200_F16) return launch_bias(__half());
     return launch_bias(__nv_bfloat16());
