@@ -356,6 +356,28 @@ TROPNN_B200_API int tropnn_b200_transpose_to_half(const void *x, int x_dtype, in
                                   void *out, void *stream);
 
 /*
+ * Gradients of the f32 output map out = hidden weight^T + bias (layers/tropical.py:140-146,
+ * whose F.linear runs in f32 with the half-precision weight upcast) on the tcgen05 tensor
+ * cores in tf32 with split operands (x = big + small, three products), which keeps f32
+ * accuracy and range. g = grad_out, f32 [rows, out_features]; out_features a multiple of 32;
+ * in_features a multiple of 32 in [32, 256].
+ * linear_dgrad: grad_hidden[n,i] = sum_o g[n,o] weight32[o,i]; weight32 = the weight widened
+ *   to f32 ([out_features, in_features]); grad_hidden f32 [rows, in_features].
+ * linear_wgrad: grad_weight[o,i] = sum_n g[n,o] hidden[n,i] rounded to dtype (F16/BF16), and
+ *   grad_bias[o] = sum_n g[n,o] in f32 when not NULL; hidden given as its tf32 split
+ *   (tropnn_b200_tf32_split). The row range is contracted by a 4-CTA cluster per 128 output
+ *   features and the partials summed in a fixed order (deterministic).
+ * tf32_split: x = big + small elementwise with big = tf32(x), small = tf32(x - big); count a
+ *   multiple of 4, 16-byte aligned pointers.
+ */
+TROPNN_B200_API int tropnn_b200_linear_dgrad(const float *g, int64_t rows, int64_t out_features, const float *weight32,
+                             int64_t in_features, float *grad_hidden, void *stream);
+TROPNN_B200_API int tropnn_b200_linear_wgrad(const float *g, int64_t rows, int64_t out_features, const float *hidden_big,
+                             const float *hidden_small, int64_t in_features, int dtype, void *grad_weight,
+                             float *grad_bias, void *stream);
+TROPNN_B200_API int tropnn_b200_tf32_split(const float *x, int64_t count, float *big, float *small, void *stream);
+
+/*
  * Per-row part of the min-face backward (layers/tropical_exact.py:204-237):
  *   training: gm[n,h] = code_scale * U'(m) * sum_d g[n,d] (code[h,r,d] - code[h,w,d]),
  *             U'(m) = -0.5 sign(m) / (1+|m|)^2

@@ -91,6 +91,15 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
+// 3-D tiled TMA load into this CTA's shared memory, completion counted on `bar`.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 // 2-D tiled TMA store from this CTA's shared memory (bulk-group completion); the rows and
 // columns of the box outside the tensor are not written.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
@@ -122,6 +131,45 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
   d |= uint64_t(1) << 46;          // descriptor version (sm_100)
   d |= uint64_t(2) << 61;          // SWIZZLE_128B
   return d;
+}
+
+// UMMA shared-memory descriptor of an MN-major tf32 operand: strips of 32 MN elements, each a
+// run of 128-byte K rows in the 128-byte swizzle with 32-byte atoms (the 32-byte chunk index
+// XOR (row & 3); 4-row groups 512 bytes apart, SBO), strips `strip_bytes` apart (LBO). (The
+// 16-byte-atom swizzle is K-major only for tf32: MN-major tf32 MMAs on it produce nothing.)
+__device__ __forceinline__ uint64_t umma_desc_mn_tf32(uint32_t saddr, uint32_t strip_bytes) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr >> 4) & 0x3FFFu);
+  d |= uint64_t((strip_bytes >> 4) & 0x3FFFu) << 16;  // leading byte offset: MN strip stride
+  d |= uint64_t(512 >> 4) << 32;                      // stride byte offset: 4-row K groups
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(1) << 61;                             // SWIZZLE_128B_BASE32B
+  return d;
+}
+
+// Instruction descriptor of kind::tf32: f32 accumulator, A/B tf32, each K-major (false) or
+// MN-major (true).
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(bool a_mn, bool b_mn, int m, int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
+         (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, one M x N x 8 tf32 step.
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// x rounded to tf32 (nearest, ties away; the low 13 mantissa bits zero), as an f32.
+__device__ __forceinline__ float round_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
 }
 
 // Instruction descriptor of kind::f16: f32 accumulator, A/B f16 (0) or bf16 (1), both
@@ -271,6 +319,41 @@ inline int make_map_f32_store32(CUtensorMap *map, void *ptr, int64_t inner, int6
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(TROPNN_B200_ERR_LAUNCH, "cuTensorMapEncodeTiled (store) failed (%d)", int(r));
+  return TROPNN_B200_OK;
+}
+
+// 2-D K-major tensor map over a row-major f32 [outer, inner] matrix: boxes of 32 x box_rows
+// elements (one 128-byte row each) with the 128-byte swizzle; out-of-range elements read as zero.
+inline int make_map_f32_k32(CUtensorMap *map, const void *ptr, int64_t inner, int64_t outer, int box_rows) {
+  EncodeTiledFn fn = nullptr;
+  TB_CHECK(encode_fn(&fn));
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * 4};
+  const cuuint32_t box[2] = {32u, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(TROPNN_B200_ERR_LAUNCH, "cuTensorMapEncodeTiled (f32 K) failed (%d)", int(r));
+  return TROPNN_B200_OK;
+}
+
+// 3-D MN-major view of a row-major f32 [k_rows, cols] matrix (cols a multiple of 32): element
+// (x, k, s) = m[k, 32 s + x]. A box {32, box_k, box_strips} lands as box_strips strips of
+// box_k 128-byte rows (strip stride box_k * 128 bytes) in the 128-byte swizzle with 32-byte
+// atoms, the MN-major tf32 UMMA operand layout (umma_desc_mn_tf32); out-of-range elements read
+// as zero.
+inline int make_map_f32_mn(CUtensorMap *map, const void *ptr, int64_t cols, int64_t k_rows, int box_k, int box_strips) {
+  EncodeTiledFn fn = nullptr;
+  TB_CHECK(encode_fn(&fn));
+  const cuuint64_t dims[3] = {32u, static_cast<cuuint64_t>(k_rows), static_cast<cuuint64_t>(cols / 32)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols) * 4, 128u};
+  const cuuint32_t box[3] = {32u, static_cast<cuuint32_t>(box_k), static_cast<cuuint32_t>(box_strips)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void *>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(TROPNN_B200_ERR_LAUNCH, "cuTensorMapEncodeTiled (f32 MN) failed (%d)", int(r));
   return TROPNN_B200_OK;
 }
 

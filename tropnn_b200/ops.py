@@ -749,12 +749,18 @@ def linear_f32out_eligible(hidden: Tensor, weight: Tensor) -> bool:
     )
 
 
+def linear_grad_eligible(rows: int, out_features: int, in_features: int) -> bool:
+    """Shapes the tensor-core output-map gradients take (tropnn_b200_linear_dgrad / _wgrad)."""
+    return rows >= 1 and out_features % 32 == 0 and in_features % 32 == 0 and 32 <= in_features <= 256
+
+
 class _LinearF32OutFunction(torch.autograd.Function):
     """F.linear(hidden, weight.float(), bias.float()) for f32 ``hidden`` and half-precision
     parameters (layers/tropical.py:140-146). Forward: hidden split into [hi | lo] halves and
     one tcgen05 GEMM (two k slices against the same weight tile, bias in the epilogue).
     Backward: the reference's f32 products (grad_hidden = g W, grad_W = g^T hidden, grad_b
-    = sum g), cast back to the parameter dtype like the reference's ``.to`` upcast."""
+    = sum g) as tcgen05 tf32 GEMMs with split operands (f32 accuracy and range), grad_W and
+    grad_b cast back to the parameter dtypes like the reference's ``.to`` upcast."""
 
     @staticmethod
     def forward(ctx: Any, hidden: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:
@@ -791,12 +797,41 @@ class _LinearF32OutFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx: Any, grad_out: Tensor) -> tuple[Tensor | None, Tensor | None, Tensor | None]:
         h, w = ctx.saved_tensors
-        g = grad_out.to(torch.float32)
-        grad_h = g @ w.to(torch.float32) if ctx.needs_input_grad[0] else None
-        grad_w = (g.t() @ h).to(w.dtype) if ctx.needs_input_grad[1] else None
-        grad_b = None
-        if ctx.bias_dtype is not None and ctx.needs_input_grad[2]:
-            grad_b = g.sum(0).to(ctx.bias_dtype)
+        rows, in_features = h.shape
+        out_features = w.shape[0]
+        dev = h.device
+        g = grad_out.to(torch.float32).contiguous()
+        need_b = ctx.bias_dtype is not None and ctx.needs_input_grad[2]
+        if not linear_grad_eligible(rows, out_features, in_features):
+            # Widths the tf32 gradient kernels do not tile: the reference's f32 products.
+            return (
+                g @ w.to(torch.float32) if ctx.needs_input_grad[0] else None,
+                (g.t() @ h).to(w.dtype) if ctx.needs_input_grad[1] else None,
+                g.sum(0).to(ctx.bias_dtype) if need_b else None,
+            )
+        stream = nat.stream_handle(dev)
+        lib = nat.load()
+        grad_h = grad_w = grad_b = None
+        if ctx.needs_input_grad[0]:
+            w32 = w.to(torch.float32).contiguous()
+            grad_h = torch.empty((rows, in_features), device=dev, dtype=torch.float32)
+            _launch(
+                "linear_dgrad", lib.tropnn_b200_linear_dgrad, g.data_ptr(), rows, out_features, w32.data_ptr(),
+                in_features, grad_h.data_ptr(), stream,
+            )
+        if ctx.needs_input_grad[1] or need_b:
+            h_big = torch.empty_like(h)
+            h_small = torch.empty_like(h)
+            _launch("tf32_split", lib.tropnn_b200_tf32_split, h.data_ptr(), h.numel(), h_big.data_ptr(),
+                    h_small.data_ptr(), stream)
+            gw = torch.empty_like(w)
+            gb = torch.empty((out_features,), device=dev, dtype=torch.float32) if need_b else None
+            _launch(
+                "linear_wgrad", lib.tropnn_b200_linear_wgrad, g.data_ptr(), rows, out_features, h_big.data_ptr(),
+                h_small.data_ptr(), in_features, nat.float_code(w.dtype), gw.data_ptr(), nat.ptr(gb), stream,
+            )
+            grad_w = gw if ctx.needs_input_grad[1] else None
+            grad_b = gb.to(ctx.bias_dtype) if need_b else None
         return grad_h, grad_w, grad_b
 
 
