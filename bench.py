@@ -172,33 +172,48 @@ def tensor_core_hidden(w: Workload, rows: int) -> bool:
     return K in (2, 4, 8, 16, 32) and D % 64 == 0 and 64 <= D <= 256 and (H * K) % 8 == 0 and rows >= 128
 
 
-def kernel_roofline(w: Workload, kernel: str, rows: int, peaks: dict) -> tuple[str, float, str, float] | None:
-    """(bound, algorithmic work per launch, unit, peak) of one kernel: FLOPs against the
-    measured bf16 tensor peak for the tcgen05 GEMMs (route scores, one-hot code sum, the
-    output map when its FLOPs outweigh its f32 output bytes), bytes against the measured
-    HBM copy bandwidth for everything else."""
+def kernel_roofline(w: Workload, kernel: str, rows: int, peaks: dict) -> tuple[str, float, str, float, str] | None:
+    """(bound, work per launch, unit, peak, peak label) of one kernel: executed FLOPs against
+    the measured bf16 tensor peak for the f16/bf16 tcgen05 GEMMs (route scores, one-hot code
+    sum, the output map when its FLOPs outweigh its f32 output bytes, the min-face backward
+    GEMMs), against half that peak for the tf32 output-map gradients (kind::tf32 runs at half
+    the f16 rate), bytes against the measured HBM copy bandwidth for everything else."""
     tc_peak, hbm_peak = peaks["bf16_tflops"], peaks["hbm_gbs"]
+    tc, tf32, hbm = (tc_peak, "bf16_tflops"), (tc_peak / 2, "bf16_tflops / 2 (tf32)"), (hbm_peak, "hbm_gbs")
     if w.kind == "trop":
         kw = w.layer_kwargs
         H, K, D, out = kw["heads"], kw["cells"], kw["code_dim"], w.out_features
+        hk = H * K
         if kernel == "trop_route" and tensor_core_route(w, rows):
-            return "tensor", 2.0 * H * K * D * rows, "TFLOP/s", tc_peak
+            return "tensor", 2.0 * hk * D * rows, "TFLOP/s", *tc
         if kernel == "trop_hidden" and tensor_core_hidden(w, rows):
-            return "tensor", 2.0 * H * K * D * rows, "TFLOP/s", tc_peak
+            return "tensor", 2.0 * hk * D * rows, "TFLOP/s", *tc
         if kernel == "linear_f32out":
             flops = 2.0 * rows * out * 2 * D  # [hi | lo] slices against one weight
             nbytes = float(rows * out * 4 + rows * 2 * D * 2 + out * D * 2 + out * 4)
             if flops / (tc_peak * 1e12) >= nbytes / (hbm_peak * 1e9):
-                return "tensor", flops, "TFLOP/s", tc_peak
-            return "hbm", nbytes, "GB/s", hbm_peak
+                return "tensor", flops, "TFLOP/s", *tc
+            return "hbm", nbytes, "GB/s", *hbm
+        if kernel == "trop_gm":  # [hi | lo] g against the code table, route-picking epilogue
+            return "tensor", 2.0 * rows * hk * 2 * D, "TFLOP/s", *tc
+        if kernel in ("trop_router_term", "trop_code_grad", "trop_router_grad"):
+            return "tensor", 2.0 * rows * hk * D, "TFLOP/s", *tc
+        if kernel == "linear_dgrad":  # big and small g against the weight
+            return "tensor", 2.0 * 2 * rows * out * D, "TFLOP/s", *tf32
+        if kernel == "linear_wgrad":  # big*big, small*big, big*small
+            return "tensor", 2.0 * 3 * rows * out * D, "TFLOP/s", *tf32
         if kernel == "split_half":
-            return "hbm", float(rows * D * 4 + rows * 2 * D * 2), "GB/s", hbm_peak
+            return "hbm", float(rows * D * 4 + rows * 2 * D * 2), "GB/s", *hbm
+        if kernel == "tf32_split":
+            return "hbm", float(rows * D * 12), "GB/s", *hbm
+        if kernel == "transpose_to_half":
+            return "hbm", float(rows * D * (4 + 2)), "GB/s", *hbm
         if kernel == "trop_code_transpose":
-            return "hbm", float(2 * H * K * D * 2), "GB/s", hbm_peak
+            return "hbm", float(2 * hk * D * 2), "GB/s", *hbm
     work = algorithmic_bytes(w, kernel, rows)
     if work is None:
         return None
-    return "hbm", work, "GB/s", hbm_peak
+    return "hbm", work, "GB/s", *hbm
 
 
 # ---------------------------------------------------------------------------
@@ -363,7 +378,7 @@ def _timed(steps: int, body, flush: torch.Tensor, world: int, device: torch.devi
 
 def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
     import tropnn_b200
-    from tropnn_b200.distributed import PeerAllReduce, overlapped_gradient_sync
+    from tropnn_b200.distributed import PeerAllReduce
 
     rank, world, local_rank = _dist_env()
     device = torch.device("cuda", local_rank)
@@ -381,14 +396,15 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
         if world > 1 and w.train:
             grads = [p for p in layer.parameters() if p.requires_grad]
             numel = sum(p.numel() for p in grads)
-            if world <= 2 and all(p.dtype == torch.float32 for p in grads) and numel <= 1 << 24:
-                # f32 gradients of a few MiB on two GPUs: the NVLink peer-memory all-reduce
-                # kernel (one-shot; NCCL's protocol is latency-bound at this size).
+            use_peer = {"auto": world <= PeerAllReduce.max_ranks(), "peer": world <= PeerAllReduce.max_ranks(),
+                        "nccl": False}[args.allreduce]
+            if use_peer and all(p.dtype == torch.float32 for p in grads) and numel <= 1 << 24:
+                # f32 gradients of a few MiB: the NVLink peer-memory all-reduce kernel
+                # (one-shot; NCCL's protocol is latency-bound at this size on two GPUs).
                 peer = PeerAllReduce(numel)
-                # The b200 Pairwise backward starts the LUT gradient's all-reduce itself, on
-                # a side stream overlapping its remaining kernels; reduce_grads() does the
-                # rest. (With NCCL the overlapped calls measured slower than one call.)
-                stack.enter_context(overlapped_gradient_sync(peer=peer))
+                # One call after the backward: overlapping the LUT gradient's reduction with
+                # the straight-through kernels on a side stream measured slower (two GPUs,
+                # config 2: 141.8 us per step against 118.5 us), with NCCL as well.
         try:
             return _run_b200_body(args, w, rank, world, device, layer, peer)
         finally:
@@ -497,15 +513,15 @@ def _run_b200_body(
         rl = kernel_roofline(w, name, w.rows_per_gpu, peaks)
         if rl is None:
             continue
-        bound, work, unit, peak = rl
+        bound, work, unit, peak, peak_label = rl
         mean_s = stats["mean_ms"] / 1e3
         achieved = work / mean_s / (1e12 if bound == "tensor" else 1e9)
         per_kernel_roofline[name] = {
             "kernel": name,
             "bound": bound,
             "achieved": round(achieved, 1),
-            "peak": peak,
-            "peak_source": f"{peaks_kind} {'bf16_tflops' if bound == 'tensor' else 'hbm_gbs'}",
+            "peak": round(peak, 1),
+            "peak_source": f"{peaks_kind} {peak_label}",
             "unit": unit,
             "frac": round(achieved / peak, 3),
             "traffic": traffic_table.get(name),
@@ -697,6 +713,10 @@ def main(argv: list[str] | None = None) -> int:
     parser.add_argument("--cpu-budget-s", type=float, default=10.0, help="seconds of CPU-baseline timing (rank 0, N=1)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--rows", type=int, default=0, help="override the per-GPU row count (profiling runs)")
+    parser.add_argument(
+        "--allreduce", choices=["auto", "peer", "nccl"], default="auto",
+        help="gradient all-reduce at N>1: auto/peer = the NVLink peer-memory kernel (up to 8 GPUs), nccl = NCCL",
+    )
     args = parser.parse_args(argv)
     if args.warmup < 3 and args.impl == "b200":
         parser.error("--warmup must be >= 3")

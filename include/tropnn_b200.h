@@ -105,6 +105,21 @@ TROPNN_B200_API int tropnn_b200_segment_rowsum(const float *values, int64_t rows
 /* --------------------------------------------------------- PairwiseLinear */
 
 /*
+ * LUT gradient in one kernel (the scatter of layers/pairwise.py:99-122's gather; atomics in
+ * backends/pairwise_tilelang.py:118-156):
+ *   grad_lut[t, b, :] = sum over rows n with indices[n, t] == b, in ascending n, of
+ *                       scale * grad_out[n, :]
+ * indices int64 [items, tables] (the forward's), grad_out f32 [items, out_features], grad_lut
+ * [tables, 2^comparisons, out_features] in lut_dtype, every entry written once. One CTA per
+ * (table, 64 columns) sorts the table's rows by bucket in shared memory and sums each bucket's
+ * rows in registers: deterministic, the same order as bucket_sort + segment_rowsum.
+ * comparisons <= 8 (the bucket_sort + segment_rowsum pair covers the rest).
+ */
+TROPNN_B200_API int tropnn_b200_pairwise_lut_grad(const float *grad_out, int64_t items, int64_t out_features,
+                                  const int64_t *indices, int64_t tables, int64_t comparisons, float scale,
+                                  void *grad_lut, int lut_dtype, void *stream);
+
+/*
  * Fused comparator routing + LUT gather-sum (layers/pairwise.py:99-135, base.py:76-77).
  *   u[n,t,r]   = (latent[n,a] - latent[n,b]) - thresholds[t,r],  (a,b) = anchors[t,r,:]
  *   idx[n,t]   = sum_r [u[n,t,r] > 0] << r
@@ -301,9 +316,13 @@ TROPNN_B200_API int tropnn_b200_peer_buffer_destroy(void *local);
  * floats each, nseg <= TROPNN_B200_PEER_MAX_SEGMENTS, total <= capacity_floats) across
  * `world` ranks over NVLink peer memory: buffers[p] is rank p's peer buffer as mapped in
  * this process (this rank's own at index `rank`). Every rank must make the same calls in
- * the same order. One kernel: each rank stores its tensors into every rank's buffer over
- * NVLink, one flag barrier, then each rank sums the copies from its own memory in rank
- * order (bit-identical results on all ranks). A rank that does not arrive within 2 s
+ * the same order. One kernel. Two ranks: each rank stores its tensors into every rank's
+ * buffer over NVLink, one flag barrier, then each rank sums the copies from its own memory in
+ * rank order. More ranks (two-shot): each rank stores chunk q of its tensors into rank q's
+ * buffer, flag barrier, rank q sums chunk q in rank order and stores the result into every
+ * rank's buffer, flag barrier, each rank copies the reduced chunks out (2 (W-1)/W of the
+ * data sent per rank instead of W-1 copies). Bit-identical results on all ranks; the
+ * two-shot and one-shot sums differ only in which rank adds. A rank that does not arrive within 2 s
  * makes the others return with the device error word set (tropnn_b200_device_error).
  * Each peer buffer holds 2 x 8 receive areas of capacity_floats (double-buffered).
  */

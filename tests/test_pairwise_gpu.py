@@ -225,3 +225,59 @@ def test_invalid_arguments_raise_value_and_type_errors() -> None:
         layer.anchors[0, 0, 0] = 99
     with pytest.raises(IndexError):
         layer(x)
+
+
+@pytest.mark.parametrize(
+    ("n", "out_f", "tables", "comparisons", "lut_dtype"),
+    [
+        (4096, 512, 16, 6, torch.float32),  # config 2: one group of 16 tables, two per warp
+        (517, 130, 136, 6, torch.float32),  # 9 table groups (the last of 8), ragged columns and rows
+        (300, 64, 20, 7, torch.float16),  # 128 buckets: groups of 12 tables
+        (7, 40, 3, 2, torch.bfloat16),  # fewer tables than warps; fewer rows than row slices
+        (0, 32, 8, 4, torch.float32),  # no rows: zeros
+    ],
+)
+def test_lut_grad_kernel_matches_sorted_rowsum(n, out_f, tables, comparisons, lut_dtype) -> None:
+    """tropnn_b200_pairwise_lut_grad (shared-memory partials, no sort) against the bucket_sort +
+    segment_rowsum pair and a float64 scatter: f32 sums of the same terms in another order."""
+    from tropnn_b200 import _native as nat
+    from tropnn_b200.ops import lut_grad_direct
+
+    assert lut_grad_direct(tables, comparisons)
+    lib = nat.load()
+    dev = torch.device("cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    buckets = 1 << comparisons
+    gen = torch.Generator().manual_seed(11)
+    g = torch.randn(n, out_f, generator=gen).to(dev)
+    idx = torch.randint(0, buckets, (n, tables), generator=gen).to(dev)
+    scale = 0.37
+    direct = torch.full((tables, buckets, out_f), float("nan"), device=dev, dtype=lut_dtype)
+    nat.check(
+        lib.tropnn_b200_pairwise_lut_grad(g.data_ptr(), n, out_f, idx.data_ptr(), tables, comparisons, scale,
+                                          direct.data_ptr(), nat.float_code(lut_dtype), stream),
+        "pairwise_lut_grad",
+    )
+    perm = torch.empty((tables, max(n, 1)), device=dev, dtype=torch.int32)
+    seg = torch.empty((tables, buckets + 1), device=dev, dtype=torch.int32)
+    nat.check(lib.tropnn_b200_bucket_sort(idx.data_ptr(), nat.I64, n, tables, tables, buckets, perm.data_ptr(),
+                                          seg.data_ptr(), stream), "bucket_sort")
+    sorted_sum = torch.empty_like(direct)
+    nat.check(
+        lib.tropnn_b200_segment_rowsum(g.data_ptr(), n, out_f, out_f, tables, buckets, perm.data_ptr(), seg.data_ptr(),
+                                       None, scale, None, None, None, 0.0, 1.0, sorted_sum.data_ptr(),
+                                       nat.float_code(lut_dtype), None, stream),
+        "segment_rowsum",
+    )
+    torch.cuda.synchronize()
+    exact = torch.zeros(tables, buckets, out_f, dtype=torch.float64)
+    gd, ic = g.double().cpu() * scale, idx.cpu()
+    for t in range(tables):
+        exact[t].index_add_(0, ic[:, t], gd)
+    tol = 1e-6 if lut_dtype == torch.float32 else (1e-3 if lut_dtype == torch.float16 else 8e-3)
+    assert not torch.isnan(direct.float()).any()
+    if n == 0:
+        assert float(direct.float().abs().sum()) == 0.0
+        return
+    assert rel_err(direct.double().cpu().numpy(), exact.numpy()) <= tol
+    assert rel_err(direct.double().cpu().numpy(), sorted_sum.double().cpu().numpy()) <= tol

@@ -1,8 +1,8 @@
-"""NVLink peer-memory gradient all-reduce (tropnn_b200.distributed.PeerAllReduce) on two
-GPUs: sums and averages of several f32 tensors match the exact result on every rank,
-results are bit-identical across ranks, repeated calls and CUDA-graph replays stay in
-step, and NCCL-free calls leave the device error word clear. Skipped with fewer than two
-GPUs (the round-end GPU tests run on one)."""
+"""NVLink peer-memory gradient all-reduce (tropnn_b200.distributed.PeerAllReduce) on 2, 3, 4
+and 8 GPUs (one-shot on two ranks, two-shot above): sums and averages of several f32 tensors
+match the exact result on every rank, results are bit-identical across ranks, repeated calls
+and CUDA-graph replays stay in step, and NCCL-free calls leave the device error word clear.
+Each world size is skipped with fewer GPUs (the round-end GPU tests run on one)."""
 
 from __future__ import annotations
 
@@ -13,10 +13,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs"),
-]
+pytestmark = pytest.mark.gpu
 
 
 def _free_port() -> int:
@@ -91,8 +88,10 @@ def _rank(rank: int, world: int, port: int, queue) -> None:
         dist.destroy_process_group()
 
 
-def test_two_rank_peer_allreduce() -> None:
-    world = 2
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+def test_peer_allreduce(world: int) -> None:
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     port = _free_port()
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
@@ -110,4 +109,4 @@ def test_two_rank_peer_allreduce() -> None:
         assert max(replay_errs) <= 1e-6
         assert flag == 0
         checksums.add(checksum)
-    assert len(checksums) == 1  # bit-identical results on both ranks
+    assert len(checksums) == 1  # bit-identical results on every rank

@@ -627,6 +627,10 @@ static size_t pairwise_backward_layout(void *ws, size_t bytes, int64_t items, in
   return WorkspaceCarver::align(c.used);
 }
 
+bool lut_grad_supported(int64_t tables, int64_t comparisons, int64_t out_features);
+int lut_grad_impl(const float *g, int64_t rows, int64_t out_features, const int64_t *indices, int64_t tables,
+                  int64_t comparisons, float scale, void *grad_lut, int lut_dtype, cudaStream_t stream);
+
 int pairwise_backward_impl(const float *g, int64_t items, int64_t out, float out_scale, const int64_t *idx,
                            const float *u, const int64_t *anchors, int64_t tables, int64_t comparisons, int64_t in,
                            const void *lut, int lut_dtype, int use_min, int surrogate, float *gx, void *gthr,
@@ -638,7 +642,9 @@ int pairwise_backward_impl(const float *g, int64_t items, int64_t out, float out
   const size_t need = pairwise_backward_layout(ws, ws_bytes, items, tables, comparisons, in, use_min, &L);
   TB_REQUIRE(ws != nullptr && need <= ws_bytes, TROPNN_B200_ERR_WORKSPACE,
              "pairwise_backward: workspace of %zu bytes is smaller than the %zu bytes required", ws_bytes, need);
-  if (glut != nullptr) {
+  if (glut != nullptr && lut_grad_supported(tables, comparisons, out)) {
+    TB_CHECK(lut_grad_impl(g, items, out, idx, tables, comparisons, out_scale, glut, lut_dtype, stream));
+  } else if (glut != nullptr) {
     TB_CHECK(bucket_sort_impl(idx, TROPNN_B200_I64, items, tables, tables, int64_t(1) << comparisons, L.perm, L.seg,
                               stream));
     TB_CHECK(segment_rowsum_impl(g, items, out, out, tables, int64_t(1) << comparisons, L.perm, L.seg, nullptr,

@@ -19,7 +19,8 @@
 // barrier is per CTA, and the per-CTA call counter lives on the device, so CUDA-graph
 // replays advance it too. Each wait is bounded (kWaitLimitNs): a rank that does not
 // arrive makes the others give up, set the library's error word and return.
-// Loads and stores only: no TMA, no multicast, no NVLink multicast objects.
+// More than two ranks use a two-shot variant (reduce-scatter by pushes, then all-gather by
+// pushes; below). Loads and stores only: no TMA, no multicast, no NVLink multicast objects.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -168,6 +169,127 @@ __global__ void __launch_bounds__(kThreads) peer_allreduce_kernel(const PeerArgs
   if (threadIdx.x == 0) counters(mine)[b] = call;
 }
 
+// Bounded wait of one thread until every rank's flag for CTA b reached `target` (signed
+// compare: flags are monotone counters). Returns false after kWaitLimitNs.
+__device__ bool wait_flags(const uint32_t *mine_flags, int world, uint32_t target) {
+  const uint64_t start = global_ns();
+  for (int p = 0; p < world; ++p) {
+    while (static_cast<int32_t>(load_volatile(mine_flags + p) - target) < 0) {
+      if (global_ns() - start > kWaitLimitNs) {
+        atomicExch(&g_peer_error, 1);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// Two-shot variant for more than two ranks (the one-shot push sends (W-1) copies of the
+// whole gradient per rank; this sends 2 (W-1)/W of it). CTA b's slice is cut into W chunks;
+// chunk q belongs to rank q.
+//   phase 0  push chunk q of this rank's slice into rank q's receive area (sender = this rank)
+//   barrier  flag 2 call - 1
+//   phase 1  sum chunk `rank` over the W received copies in rank order, scale, write it to
+//            the caller's tensor and push it into every other rank's receive area at the same
+//            place (sender = this rank: that chunk of that area is unused in phase 0)
+//   barrier  flag 2 call
+//   phase 2  copy the other ranks' reduced chunks from this rank's own memory to the tensor.
+// Double-buffered by call parity as the one-shot kernel; every rank's result is bit-identical.
+__global__ void __launch_bounds__(kThreads) peer_allreduce_2shot_kernel(const PeerArgs a) {
+  __shared__ int ok_s;
+  __shared__ uint32_t call_s;
+  const int b = blockIdx.x;
+  const int64_t lo = int64_t(b) * a.slice;
+  const int64_t hi = min(a.count, lo + a.slice);
+  // Chunk length: a multiple of 4 floats.
+  const int64_t chunk = ((a.slice + a.world - 1) / a.world + 3) / 4 * 4;
+  unsigned char *mine = a.buf[a.rank];
+  if (threadIdx.x == 0) call_s = counters(mine)[b] + 1;
+  __syncthreads();
+  const uint32_t call = call_s;
+  const uint32_t parity = call & 1u;
+  uint32_t *mine_flags = flags(mine) + b * kMaxRanks;
+
+  // Phase 0.
+  for (int64_t i = lo + 4 * threadIdx.x; i < hi; i += 4 * blockDim.x) {
+    float4 v;
+    const float *p4 = seg_ptr4(a, i);
+    if (p4 != nullptr) {
+      v = *reinterpret_cast<const float4 *>(p4);
+    } else {
+      v.x = *seg_ptr(a, i);
+      v.y = i + 1 < hi ? *seg_ptr(a, i + 1) : 0.f;
+      v.z = i + 2 < hi ? *seg_ptr(a, i + 2) : 0.f;
+      v.w = i + 3 < hi ? *seg_ptr(a, i + 3) : 0.f;
+    }
+    const int q = static_cast<int>((i - lo) / chunk);
+    *reinterpret_cast<float4 *>(recv(a.buf[q], a.capacity, parity, a.rank) + i) = v;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < a.world; ++p) store_volatile(flags(a.buf[p]) + b * kMaxRanks + a.rank, 2 * call - 1);
+    ok_s = wait_flags(mine_flags, a.world, 2 * call - 1) ? 1 : 0;
+    __threadfence_system();
+  }
+  __syncthreads();
+  if (!ok_s) return;
+
+  // Phase 1: this rank's chunk.
+  const int64_t c_lo = lo + a.rank * chunk;
+  const int64_t c_hi = min(hi, c_lo + chunk);
+  for (int64_t i = c_lo + 4 * threadIdx.x; i < c_hi; i += 4 * blockDim.x) {
+    float4 acc = __ldcg(reinterpret_cast<const float4 *>(recv(mine, a.capacity, parity, 0) + i));
+    for (int p = 1; p < a.world; ++p) {
+      const float4 v = __ldcg(reinterpret_cast<const float4 *>(recv(mine, a.capacity, parity, p) + i));
+      acc.x = __fadd_rn(acc.x, v.x);
+      acc.y = __fadd_rn(acc.y, v.y);
+      acc.z = __fadd_rn(acc.z, v.z);
+      acc.w = __fadd_rn(acc.w, v.w);
+    }
+    const float4 r = make_float4(__fmul_rn(acc.x, a.scale), __fmul_rn(acc.y, a.scale), __fmul_rn(acc.z, a.scale),
+                                 __fmul_rn(acc.w, a.scale));
+    for (int p = 0; p < a.world; ++p)
+      if (p != a.rank) *reinterpret_cast<float4 *>(recv(a.buf[p], a.capacity, parity, a.rank) + i) = r;
+    float *p4 = seg_ptr4(a, i);
+    if (p4 != nullptr && i + 4 <= c_hi) {
+      *reinterpret_cast<float4 *>(p4) = r;
+    } else {
+      *seg_ptr(a, i) = r.x;
+      if (i + 1 < c_hi) *seg_ptr(a, i + 1) = r.y;
+      if (i + 2 < c_hi) *seg_ptr(a, i + 2) = r.z;
+      if (i + 3 < c_hi) *seg_ptr(a, i + 3) = r.w;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < a.world; ++p) store_volatile(flags(a.buf[p]) + b * kMaxRanks + a.rank, 2 * call);
+    ok_s = wait_flags(mine_flags, a.world, 2 * call) ? 1 : 0;
+    __threadfence_system();
+  }
+  __syncthreads();
+  if (!ok_s) return;
+
+  // Phase 2: the other ranks' reduced chunks, from this rank's memory.
+  for (int64_t i = lo + 4 * threadIdx.x; i < hi; i += 4 * blockDim.x) {
+    const int q = static_cast<int>((i - lo) / chunk);
+    if (q == a.rank) continue;
+    const int64_t q_hi = min(hi, lo + (q + 1) * chunk);
+    const float4 r = __ldcg(reinterpret_cast<const float4 *>(recv(mine, a.capacity, parity, q) + i));
+    float *p4 = seg_ptr4(a, i);
+    if (p4 != nullptr && i + 4 <= q_hi) {
+      *reinterpret_cast<float4 *>(p4) = r;
+    } else {
+      *seg_ptr(a, i) = r.x;
+      if (i + 1 < q_hi) *seg_ptr(a, i + 1) = r.y;
+      if (i + 2 < q_hi) *seg_ptr(a, i + 2) = r.z;
+      if (i + 3 < q_hi) *seg_ptr(a, i + 3) = r.w;
+    }
+  }
+  if (threadIdx.x == 0) counters(mine)[b] = call;
+}
+
 }  // namespace
 
 size_t peer_buffer_bytes(int64_t capacity) { return kHeaderBytes + size_t(2) * kMaxRanks * capacity * 4; }
@@ -260,13 +382,18 @@ int tropnn_b200_peer_allreduce_f32(void *const *buffers, int world, int rank, in
     TB_REQUIRE(buffers[p] != nullptr, TROPNN_B200_ERR_INVALID, "peer_allreduce: buffer of rank %d is null", p);
     a.buf[p] = static_cast<unsigned char *>(buffers[p]);
   }
-  // Slices of >= 2048 floats (a multiple of 4), at most kMaxSlices of them.
-  int64_t slice = std::max<int64_t>(2048, ceil_div(total, int64_t(kMaxSlices)));
+  // Slices of >= 2048 floats (a multiple of 4), at most kMaxSlices of them. The slice length
+  // depends on the buffers' capacity only, so CTA b covers the same floats in every call and
+  // its call counter orders every reuse of them (the parity double-buffering relies on it).
+  int64_t slice = std::max<int64_t>(2048, ceil_div(capacity_floats, int64_t(kMaxSlices)));
   slice = ceil_div(slice, int64_t(4)) * 4;
   const int slices = static_cast<int>(ceil_div(total, slice));
   a.slice = slice;
   a.count = total;
-  peer_allreduce_kernel<<<slices, kThreads, 0, as_stream(stream)>>>(a);
+  if (world > 2)
+    peer_allreduce_2shot_kernel<<<slices, kThreads, 0, as_stream(stream)>>>(a);
+  else
+    peer_allreduce_kernel<<<slices, kThreads, 0, as_stream(stream)>>>(a);
   TB_CHECK(check_launch("peer_allreduce"));
   return clear_error();
 }

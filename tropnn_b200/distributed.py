@@ -144,8 +144,9 @@ class PeerAllReduce:
     """All-reduce of f32 gradients over NVLink peer memory for one process group on one
     node (tropnn_b200_peer_allreduce_f32): every rank allocates one peer buffer (16
     receive areas of ``capacity`` floats), the ranks exchange its CUDA IPC handle, and each
-    call is one kernel per rank that pushes its tensors into every rank's buffer and sums
-    the received copies after one flag barrier. For
+    call is one kernel per rank: on two ranks it pushes its tensors into every rank's buffer
+    and sums the received copies after one flag barrier; on more it reduce-scatters and
+    all-gathers by pushes around two flag barriers. For
     the few-MiB gradients of the benchmark layers it replaces NCCL's latency-bound
     protocol (~22 us for 2 MiB on two B200s). Collective: every rank must construct it
     and call it in the same order; call ``close`` on every rank before

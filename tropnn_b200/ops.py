@@ -87,6 +87,12 @@ def pairwise_anchor_index(anchors: Tensor, in_features: int) -> tuple[Tensor, Te
     return start, entries
 
 
+def lut_grad_direct(tables: int, comparisons: int) -> bool:
+    """Whether the LUT gradient takes the one-kernel path (tropnn_b200_pairwise_lut_grad:
+    shared-memory sort + register gather per table and 64-column block): up to 256 buckets."""
+    return tables >= 1 and 1 <= comparisons <= 8
+
+
 class _PairwiseB200Function(torch.autograd.Function):
     @staticmethod
     def forward(  # type: ignore[override]
@@ -159,7 +165,23 @@ class _PairwiseB200Function(torch.autograd.Function):
         buckets = 1 << comparisons
 
         grad_lut = None
-        if ctx.needs_input_grad[2]:
+        if ctx.needs_input_grad[2] and lut_grad_direct(tables, comparisons):
+            grad_lut = torch.empty_like(lut)
+            _launch(
+                "pairwise_lut_grad",
+                lib.tropnn_b200_pairwise_lut_grad,
+                g.data_ptr(),
+                items,
+                out_features,
+                indices.data_ptr(),
+                tables,
+                comparisons,
+                ctx.output_scale,
+                grad_lut.data_ptr(),
+                nat.float_code(grad_lut.dtype),
+                stream,
+            )
+        elif ctx.needs_input_grad[2]:
             perm = torch.empty((tables, items), device=dev, dtype=torch.int32)
             seg = torch.empty((tables, buckets + 1), device=dev, dtype=torch.int32)
             _launch(
