@@ -396,8 +396,8 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
         if world > 1 and w.train:
             grads = [p for p in layer.parameters() if p.requires_grad]
             numel = sum(p.numel() for p in grads)
-            use_peer = {"auto": world <= PeerAllReduce.max_ranks(), "peer": world <= PeerAllReduce.max_ranks(),
-                        "nccl": False}[args.allreduce]
+            # auto: the peer kernel where it was measured faster than NCCL (2 and 4 GPUs).
+            use_peer = {"auto": world <= 4, "peer": world <= PeerAllReduce.max_ranks(), "nccl": False}[args.allreduce]
             if use_peer and all(p.dtype == torch.float32 for p in grads) and numel <= 1 << 24:
                 # f32 gradients of a few MiB: the NVLink peer-memory all-reduce kernel
                 # (one-shot; NCCL's protocol is latency-bound at this size on two GPUs).
@@ -715,7 +715,8 @@ def main(argv: list[str] | None = None) -> int:
     parser.add_argument("--rows", type=int, default=0, help="override the per-GPU row count (profiling runs)")
     parser.add_argument(
         "--allreduce", choices=["auto", "peer", "nccl"], default="auto",
-        help="gradient all-reduce at N>1: auto/peer = the NVLink peer-memory kernel (up to 8 GPUs), nccl = NCCL",
+        help="gradient all-reduce at N>1: peer = the NVLink peer-memory kernel (up to 8 GPUs), nccl = NCCL, "
+        "auto = peer up to 4 GPUs, NCCL above",
     )
     args = parser.parse_args(argv)
     if args.warmup < 3 and args.impl == "b200":

@@ -113,7 +113,8 @@ TROPNN_B200_API int tropnn_b200_segment_rowsum(const float *values, int64_t rows
  * [tables, 2^comparisons, out_features] in lut_dtype, every entry written once. One CTA per
  * (table, 64 columns) sorts the table's rows by bucket in shared memory and sums each bucket's
  * rows in registers: deterministic, the same order as bucket_sort + segment_rowsum.
- * comparisons <= 8 (the bucket_sort + segment_rowsum pair covers the rest).
+ * comparisons <= 8 (the bucket_sort + segment_rowsum pair covers the rest; it is also the faster
+ * path above ~1024 columns, where this kernel's per-column-block sorts repeat).
  */
 TROPNN_B200_API int tropnn_b200_pairwise_lut_grad(const float *grad_out, int64_t items, int64_t out_features,
                                   const int64_t *indices, int64_t tables, int64_t comparisons, float scale,

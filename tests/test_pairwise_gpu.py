@@ -243,7 +243,7 @@ def test_lut_grad_kernel_matches_sorted_rowsum(n, out_f, tables, comparisons, lu
     from tropnn_b200 import _native as nat
     from tropnn_b200.ops import lut_grad_direct
 
-    assert lut_grad_direct(tables, comparisons)
+    assert lut_grad_direct(tables, comparisons, out_f)
     lib = nat.load()
     dev = torch.device("cuda")
     stream = torch.cuda.current_stream().cuda_stream

@@ -642,7 +642,9 @@ int pairwise_backward_impl(const float *g, int64_t items, int64_t out, float out
   const size_t need = pairwise_backward_layout(ws, ws_bytes, items, tables, comparisons, in, use_min, &L);
   TB_REQUIRE(ws != nullptr && need <= ws_bytes, TROPNN_B200_ERR_WORKSPACE,
              "pairwise_backward: workspace of %zu bytes is smaller than the %zu bytes required", ws_bytes, need);
-  if (glut != nullptr && lut_grad_supported(tables, comparisons, out)) {
+  // The one-kernel LUT gradient re-sorts a table's rows per 64-column block: taken up to
+  // 1024 columns, the sort + segmented-sum pair above that.
+  if (glut != nullptr && lut_grad_supported(tables, comparisons, out) && out <= 1024) {
     TB_CHECK(lut_grad_impl(g, items, out, idx, tables, comparisons, out_scale, glut, lut_dtype, stream));
   } else if (glut != nullptr) {
     TB_CHECK(bucket_sort_impl(idx, TROPNN_B200_I64, items, tables, tables, int64_t(1) << comparisons, L.perm, L.seg,
