@@ -186,9 +186,9 @@ TROPNN_B200_API size_t tropnn_b200_pairwise_backward_workspace_size(int64_t item
 /*
  * Whole PairwiseLinear backward (the autograd backward of pairwise.py:202-248):
  * grad_lut (lut dtype, may be NULL), grad_latent (f32, NULL to skip the STE part) and
- * grad_thresholds (grad_thresholds_dtype, may be NULL). Runs bucket_sort +
- * segment_rowsum for the LUT and anchor_index + ste_backward + threshold_grad for
- * the STE terms, all inside `workspace`.
+ * grad_thresholds (grad_thresholds_dtype, may be NULL). Runs pairwise_lut_grad (up to 8
+ * comparisons and 1024 columns; else bucket_sort + segment_rowsum) for the LUT and
+ * anchor_index + ste_backward + threshold_grad for the STE terms, all inside `workspace`.
  */
 TROPNN_B200_API int tropnn_b200_pairwise_backward(const float *grad_out, int64_t items, int64_t out_features,
                                   float output_scale, const int64_t *indices, const float *margins,

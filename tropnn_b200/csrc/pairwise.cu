@@ -395,9 +395,11 @@ __global__ void __launch_bounds__(256) threshold_partial_kernel(const float *__r
       if (MIN) {
         const float v = __ldg(gu + n * T + t);
         const int r = __ldg(rstar + n * T + t);
+        // Every accumulator takes v or 0 (adding 0 changes nothing): written as selects, so
+        // that the compiler keeps acc in registers instead of indexing a local-memory copy
+        // by r*.
 #pragma unroll
-        for (int c = 0; c < kMaxComparisons; ++c)
-          if (c == r) acc[c] = __fadd_rn(acc[c], v);
+        for (int c = 0; c < kMaxComparisons; ++c) acc[c] = __fadd_rn(acc[c], c == r ? v : 0.f);
       } else {
 #pragma unroll
         for (int c = 0; c < kMaxComparisons; ++c)
