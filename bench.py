@@ -378,7 +378,7 @@ def _timed(steps: int, body, flush: torch.Tensor, world: int, device: torch.devi
 
 def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
     import tropnn_b200
-    from tropnn_b200.distributed import PeerAllReduce
+    from tropnn_b200.distributed import PeerAllReduce, fused_lut_allreduce
 
     rank, world, local_rank = _dist_env()
     device = torch.device("cuda", local_rank)
@@ -391,7 +391,7 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     tropnn_b200._native.load()
     layer = w.build().to(device).train(w.train)
-    peer = None
+    peer = peer_lut = None
     with contextlib.ExitStack() as stack:
         if world > 1 and w.train:
             grads = [p for p in layer.parameters() if p.requires_grad]
@@ -402,12 +402,20 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
                 # f32 gradients of a few MiB: the NVLink peer-memory all-reduce kernel
                 # (one-shot; NCCL's protocol is latency-bound at this size on two GPUs).
                 peer = PeerAllReduce(numel)
-                # One call after the backward: overlapping the LUT gradient's reduction with
-                # the straight-through kernels on a side stream measured slower (two GPUs,
-                # config 2: 141.8 us per step against 118.5 us), with NCCL as well.
+                if w.kind == "pairwise" and args.fuse_lut_allreduce:
+                    # The LUT gradient's average runs inside the LUT-gradient kernel (a peer
+                    # set of its own); the rest goes through `peer` after the backward.
+                    kw = w.layer_kwargs
+                    cap = PeerAllReduce.lut_capacity(kw["tables"], kw["comparisons"], w.out_features)
+                    if cap > 0:
+                        peer_lut = PeerAllReduce(cap)
+                        stack.enter_context(fused_lut_allreduce(peer_lut))
         try:
             return _run_b200_body(args, w, rank, world, device, layer, peer)
         finally:
+            stack.close()
+            if peer_lut is not None:
+                peer_lut.close()
             if peer is not None:
                 peer.close()
             if world > 1:
@@ -419,6 +427,8 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
 def _run_b200_body(
     args: argparse.Namespace, w: Workload, rank: int, world: int, device: torch.device, layer, peer
 ) -> dict | None:
+    from tropnn_b200.distributed import fused_lut_peer
+
     from tropnn_b200 import trace
     from tropnn_b200.distributed import allreduce_gradients
 
@@ -551,7 +561,13 @@ def _run_b200_body(
             "workload": w.description,
             "rows_per_gpu": w.rows_per_gpu,
             "global_batch": rows_total,
-            "parallelism": (f"dp{world} (batch-row shards, {'NVLink peer-memory' if peer is not None else 'NCCL'} grad all-reduce)" if world > 1 else "single GPU"),
+            "parallelism": (
+                f"dp{world} (batch-row shards, {'NVLink peer-memory' if peer is not None else 'NCCL'} grad all-reduce"
+                + (", LUT-gradient average fused into its kernel" if fused_lut_peer() is not None else "")
+                + ")"
+                if world > 1
+                else "single GPU"
+            ),
             "l2": f"flushed between timed steps ({L2_FLUSH_BYTES >> 20} MiB write, untimed)",
             "timing": "step (with the NCCL gradient all-reduce at N>1) captured as one CUDA graph and replayed",
         },
@@ -713,6 +729,11 @@ def main(argv: list[str] | None = None) -> int:
     parser.add_argument("--cpu-budget-s", type=float, default=10.0, help="seconds of CPU-baseline timing (rank 0, N=1)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--rows", type=int, default=0, help="override the per-GPU row count (profiling runs)")
+    parser.add_argument(
+        "--fuse-lut-allreduce", type=int, choices=[0, 1], default=0,
+        help="with the peer all-reduce, average the Pairwise LUT gradient inside its kernel (1) or after the "
+        "backward (0, the default: two GPUs, config 2, 101.3 us per step against 115.8 us fused)",
+    )
     parser.add_argument(
         "--allreduce", choices=["auto", "peer", "nccl"], default="auto",
         help="gradient all-reduce at N>1: peer = the NVLink peer-memory kernel (up to 8 GPUs), nccl = NCCL, "

@@ -121,6 +121,25 @@ TROPNN_B200_API int tropnn_b200_pairwise_lut_grad(const float *grad_out, int64_t
                                   void *grad_lut, int lut_dtype, void *stream);
 
 /*
+ * tropnn_b200_pairwise_lut_grad with the data-parallel gradient all-reduce fused in (one process
+ * per GPU, the peer buffers of tropnn_b200_peer_buffer_create / _open as for
+ * tropnn_b200_peer_allreduce_f32, a set used for nothing else): every CTA pushes its block of
+ * local sums into every rank's buffer over NVLink as soon as it is computed, meets the other
+ * ranks at a per-block flag barrier and writes the rank-order sum (times 1/world when averaging),
+ * so the reduction overlaps the other blocks' work. Every rank must make the same calls.
+ * tables x ceil(out_features / 64) <= 512 blocks; capacity_floats >=
+ * tropnn_b200_pairwise_lut_grad_peer_floats(...) (-1 for unsupported shapes). world = 1 is the
+ * plain kernel.
+ */
+TROPNN_B200_API int64_t tropnn_b200_pairwise_lut_grad_peer_floats(int64_t tables, int64_t comparisons,
+                                                                  int64_t out_features);
+TROPNN_B200_API int tropnn_b200_pairwise_lut_grad_allreduce(const float *grad_out, int64_t items, int64_t out_features,
+                                            const int64_t *indices, int64_t tables, int64_t comparisons,
+                                            float scale, void *grad_lut, int lut_dtype, void *const *buffers,
+                                            int world, int rank, int64_t capacity_floats, int average,
+                                            void *stream);
+
+/*
  * Fused comparator routing + LUT gather-sum (layers/pairwise.py:99-135, base.py:76-77).
  *   u[n,t,r]   = (latent[n,a] - latent[n,b]) - thresholds[t,r],  (a,b) = anchors[t,r,:]
  *   idx[n,t]   = sum_r [u[n,t,r] > 0] << r

@@ -78,10 +78,34 @@ def _rank(rank: int, world: int, port: int, queue) -> None:
                 max(float((a.cpu().double() - e / world).abs().max() / (e / world).abs().max()) for a, e in zip(buf, expected_sum))
             )
         del graph
-        checksum = sum(float(x.double().sum()) for x in t3)
+        # The LUT gradient with the average fused into its kernel equals the plain kernel
+        # followed by the peer all-reduce (both sum the ranks' local sums in rank order).
+        lib = nat.load()
+        stream = torch.cuda.current_stream(device).cuda_stream
+        T, C, out_f, n = 16, 6, 512, 1000
+        lut_gen = torch.Generator().manual_seed(7 + rank)
+        g = torch.randn(n, out_f, generator=lut_gen).to(device)
+        idx = torch.randint(0, 1 << C, (n, T), generator=lut_gen).to(device)
+        plain = torch.empty(T, 1 << C, out_f, device=device)
+        nat.check(lib.tropnn_b200_pairwise_lut_grad(g.data_ptr(), n, out_f, idx.data_ptr(), T, C, 0.5, plain.data_ptr(),
+                                                    nat.F32, stream), "lut_grad")
+        peer.all_reduce_([plain.view(-1)], average=True)
+        lut_peer = PeerAllReduce(PeerAllReduce.lut_capacity(T, C, out_f))
+        fused_results = []
+        for _ in range(3):  # repeated calls advance the slot counters in step
+            fused = torch.full_like(plain, float("nan"))
+            buffers, w_, r_, cap = lut_peer.raw()
+            nat.check(lib.tropnn_b200_pairwise_lut_grad_allreduce(
+                g.data_ptr(), n, out_f, idx.data_ptr(), T, C, 0.5, fused.data_ptr(), nat.F32, buffers, w_, r_, cap, 1,
+                stream), "lut_grad_allreduce")
+            fused_results.append(fused)
+        torch.cuda.synchronize()
+        fused_same = all(torch.equal(f, plain) for f in fused_results)
+        lut_peer.close()
+        checksum = sum(float(x.double().sum()) for x in t3) + float(plain.double().sum())
         flag = ctypes.c_int(-1)
         nat.check(nat.load().tropnn_b200_device_error(ctypes.byref(flag)), "device_error")
-        queue.put((rank, err_sum, err_avg, same, replay_errs, checksum, flag.value))
+        queue.put((rank, err_sum, err_avg, same and fused_same, replay_errs, checksum, flag.value))
     finally:
         if peer is not None:
             peer.close()

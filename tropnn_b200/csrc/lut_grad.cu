@@ -15,10 +15,22 @@
 // per table, and nothing but the result goes back to memory (the two-kernel path it replaces
 // wrote and re-read a global row permutation and ran its sort on one CTA per table).
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace tropnn_b200 {
 
+// Fused all-reduce (world > 1): the peer buffers of one PeerAllReduce set, slot = CTA.
+struct LutPeer {
+  unsigned char *buf[TROPNN_B200_PEER_MAX_RANKS];
+  int world;
+  int rank;
+  int64_t capacity;  // floats per receive area
+  float post_scale;  // 1/world when averaging, else 1
+};
+
 namespace {
+
+__device__ int g_lut_grad_error = 0;
 
 constexpr int kWarps = 32;
 constexpr int kThreads = 32 * kWarps;
@@ -33,10 +45,10 @@ struct LutSmem {
   uint8_t key[kTileRows];          // bucket of every tile row
 };
 
-template <typename LT, int BPW, bool VEC2>
+template <typename LT, int BPW, bool VEC2, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 1)
     lut_grad_kernel(const float *__restrict__ g, int64_t rows, int out_features, const int64_t *__restrict__ idx,
-                    int tables, int buckets, float scale, LT *__restrict__ grad_lut) {
+                    int tables, int buckets, float scale, LT *__restrict__ grad_lut, const LutPeer peer) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   LutSmem &S = *reinterpret_cast<LutSmem *>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -168,6 +180,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();  // the next tile reuses the keys and the permutation
   }
 
+  if constexpr (FUSED) {
+    // All-reduce of this CTA's block across the ranks, in the same kernel: push the local sums
+    // into every rank's receive area (slot = this CTA, so its call counter orders every reuse
+    // of the area), one flag barrier per CTA, then sum the ranks' blocks in rank order from
+    // this GPU's own memory (bit-identical on every rank). CTAs push before they wait, so a
+    // rank whose CTAs are not all resident still completes.
+    __shared__ uint32_t call_s;
+    __shared__ int ok_s;
+    const int slot = blockIdx.x * gridDim.y + blockIdx.y;
+    unsigned char *mine = peer.buf[peer.rank];
+    if (threadIdx.x == 0) call_s = peer::counters(mine)[slot] + 1;
+    __syncthreads();
+    const uint32_t call = call_s, parity = call & 1u;
+    const int64_t base = int64_t(slot) * buckets * kCols + 2 * lane;
+#pragma unroll
+    for (int j = 0; j < BPW; ++j) {
+      const int b = warp + j * kWarps;
+      if (b >= buckets) continue;
+      for (int p = 0; p < peer.world; ++p)
+        *reinterpret_cast<float2 *>(peer::recv(peer.buf[p], peer.capacity, parity, peer.rank) + base + b * kCols) =
+            acc[j];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+      ok_s = peer::slot_barrier(peer.buf, peer.world, peer.rank, slot, call, &g_lut_grad_error) ? 1 : 0;
+    __syncthreads();
+    if (ok_s) {
+#pragma unroll
+      for (int j = 0; j < BPW; ++j) {
+        const int b = warp + j * kWarps;
+        if (b >= buckets) continue;
+        float2 sum = __ldcg(reinterpret_cast<const float2 *>(peer::recv(mine, peer.capacity, parity, 0) + base + b * kCols));
+        for (int p = 1; p < peer.world; ++p) {
+          const float2 v =
+              __ldcg(reinterpret_cast<const float2 *>(peer::recv(mine, peer.capacity, parity, p) + base + b * kCols));
+          sum.x = __fadd_rn(sum.x, v.x);
+          sum.y = __fadd_rn(sum.y, v.y);
+        }
+        acc[j] = make_float2(__fmul_rn(sum.x, peer.post_scale), __fmul_rn(sum.y, peer.post_scale));
+      }
+    }
+    if (threadIdx.x == 0) peer::counters(mine)[slot] = call;
+  }
+
 #pragma unroll
   for (int j = 0; j < BPW; ++j) {
     const int b = warp + j * kWarps;
@@ -180,24 +236,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <typename LT, int BPW>
 int launch_bpw(const float *g, int64_t rows, int out_features, const int64_t *idx, int tables, int buckets,
-               float scale, LT *grad_lut, cudaStream_t stream) {
+               float scale, LT *grad_lut, const LutPeer *peer, cudaStream_t stream) {
   const size_t smem = sizeof(LutSmem);
   // 8-byte loads of column pairs when every row start is 8-byte aligned.
   const bool vec2 = out_features % 2 == 0 && reinterpret_cast<uintptr_t>(g) % 8 == 0;
-  auto kernel = vec2 ? lut_grad_kernel<LT, BPW, true> : lut_grad_kernel<LT, BPW, false>;
+  auto kernel = peer != nullptr ? (vec2 ? lut_grad_kernel<LT, BPW, true, true> : lut_grad_kernel<LT, BPW, false, true>)
+                                : (vec2 ? lut_grad_kernel<LT, BPW, true, false> : lut_grad_kernel<LT, BPW, false, false>);
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "pairwise_lut_grad"));
   const dim3 grid(static_cast<unsigned>(tables), static_cast<unsigned>(ceil_div(int64_t(out_features), int64_t(kCols))));
-  kernel<<<grid, kThreads, smem, stream>>>(g, rows, out_features, idx, tables, buckets, scale, grad_lut);
+  const LutPeer none{};
+  kernel<<<grid, kThreads, smem, stream>>>(g, rows, out_features, idx, tables, buckets, scale, grad_lut,
+                                           peer != nullptr ? *peer : none);
   return check_launch("pairwise_lut_grad");
 }
 
 template <typename LT>
 int launch_lut_grad(const float *g, int64_t rows, int out_features, const int64_t *idx, int tables, int buckets,
-                    float scale, LT *grad_lut, cudaStream_t stream) {
-  if (buckets <= 32) return launch_bpw<LT, 1>(g, rows, out_features, idx, tables, buckets, scale, grad_lut, stream);
-  if (buckets <= 64) return launch_bpw<LT, 2>(g, rows, out_features, idx, tables, buckets, scale, grad_lut, stream);
-  if (buckets <= 128) return launch_bpw<LT, 4>(g, rows, out_features, idx, tables, buckets, scale, grad_lut, stream);
-  return launch_bpw<LT, 8>(g, rows, out_features, idx, tables, buckets, scale, grad_lut, stream);
+                    float scale, LT *grad_lut, const LutPeer *peer, cudaStream_t stream) {
+  if (buckets <= 32) return launch_bpw<LT, 1>(g, rows, out_features, idx, tables, buckets, scale, grad_lut, peer, stream);
+  if (buckets <= 64) return launch_bpw<LT, 2>(g, rows, out_features, idx, tables, buckets, scale, grad_lut, peer, stream);
+  if (buckets <= 128) return launch_bpw<LT, 4>(g, rows, out_features, idx, tables, buckets, scale, grad_lut, peer, stream);
+  return launch_bpw<LT, 8>(g, rows, out_features, idx, tables, buckets, scale, grad_lut, peer, stream);
 }
 
 }  // namespace
@@ -208,7 +267,8 @@ bool lut_grad_supported(int64_t tables, int64_t comparisons, int64_t out_feature
 }
 
 int lut_grad_impl(const float *g, int64_t rows, int64_t out_features, const int64_t *indices, int64_t tables,
-                  int64_t comparisons, float scale, void *grad_lut, int lut_dtype, cudaStream_t stream) {
+                  int64_t comparisons, float scale, void *grad_lut, int lut_dtype, const LutPeer *peer,
+                  cudaStream_t stream) {
   TB_REQUIRE(lut_grad_supported(tables, comparisons, out_features), TROPNN_B200_ERR_INVALID,
              "pairwise_lut_grad: unsupported shape tables=%lld comparisons=%lld out=%lld (comparisons <= 8)",
              (long long)tables, (long long)comparisons, (long long)out_features);
@@ -221,13 +281,31 @@ int lut_grad_impl(const float *g, int64_t rows, int64_t out_features, const int6
   const int o = static_cast<int>(out_features), t = static_cast<int>(tables), b = 1 << comparisons;
   switch (lut_dtype) {
     case TROPNN_B200_F32:
-      return launch_lut_grad<float>(g, rows, o, indices, t, b, scale, static_cast<float *>(grad_lut), stream);
+      return launch_lut_grad<float>(g, rows, o, indices, t, b, scale, static_cast<float *>(grad_lut), peer, stream);
     case TROPNN_B200_F16:
-      return launch_lut_grad<__half>(g, rows, o, indices, t, b, scale, static_cast<__half *>(grad_lut), stream);
+      return launch_lut_grad<__half>(g, rows, o, indices, t, b, scale, static_cast<__half *>(grad_lut), peer, stream);
     default:
-      return launch_lut_grad<__nv_bfloat16>(g, rows, o, indices, t, b, scale, static_cast<__nv_bfloat16 *>(grad_lut),
-                                            stream);
+      return launch_lut_grad<__nv_bfloat16>(g, rows, o, indices, t, b, scale,
+                                            static_cast<__nv_bfloat16 *>(grad_lut), peer, stream);
   }
+}
+
+// Receive-area floats the fused variant needs: one slot of 2^comparisons x 64 floats per CTA.
+int64_t lut_grad_peer_floats(int64_t tables, int64_t comparisons, int64_t out_features) {
+  return tables * ceil_div(out_features, int64_t(kCols)) * (int64_t(1) << comparisons) * kCols;
+}
+
+int read_lut_grad_error(int *value) {
+  int v = 0;
+  cudaError_t err = cudaMemcpyFromSymbol(&v, g_lut_grad_error, sizeof(int));
+  if (err != cudaSuccess)
+    return set_error(TROPNN_B200_ERR_LAUNCH, "reading the device error word: %s", cudaGetErrorString(err));
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_lut_grad_error, &zero, sizeof(int));
+  }
+  *value = v;
+  return TROPNN_B200_OK;
 }
 
 }  // namespace tropnn_b200
@@ -239,8 +317,44 @@ int tropnn_b200_pairwise_lut_grad(const float *grad_out, int64_t items, int64_t 
                                   void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
   TB_CHECK(tropnn_b200::lut_grad_impl(grad_out, items, out_features, indices, tables, comparisons, scale, grad_lut,
-                                      lut_dtype, tropnn_b200::as_stream(stream)));
+                                      lut_dtype, nullptr, tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
+}
+
+int64_t tropnn_b200_pairwise_lut_grad_peer_floats(int64_t tables, int64_t comparisons, int64_t out_features) {
+  if (!tropnn_b200::lut_grad_supported(tables, comparisons, out_features)) return -1;
+  return tropnn_b200::lut_grad_peer_floats(tables, comparisons, out_features);
+}
+
+int tropnn_b200_pairwise_lut_grad_allreduce(const float *grad_out, int64_t items, int64_t out_features,
+                                            const int64_t *indices, int64_t tables, int64_t comparisons, float scale,
+                                            void *grad_lut, int lut_dtype, void *const *buffers, int world, int rank,
+                                            int64_t capacity_floats, int average, void *stream) {
+  using namespace tropnn_b200;
+  TB_CHECK(check_current_device());
+  TB_REQUIRE(buffers != nullptr && world >= 1 && world <= TROPNN_B200_PEER_MAX_RANKS && rank >= 0 && rank < world,
+             TROPNN_B200_ERR_INVALID, "pairwise_lut_grad_allreduce: rank %d of world %d", rank, world);
+  TB_REQUIRE(lut_grad_supported(tables, comparisons, out_features), TROPNN_B200_ERR_INVALID,
+             "pairwise_lut_grad_allreduce: unsupported shape");
+  const int64_t slots = tables * ceil_div(out_features, int64_t(kCols));
+  TB_REQUIRE(slots <= peer::kPeerMaxSlices, TROPNN_B200_ERR_INVALID,
+             "pairwise_lut_grad_allreduce: %lld column blocks exceed the %d peer slots", (long long)slots,
+             peer::kPeerMaxSlices);
+  TB_REQUIRE(capacity_floats >= lut_grad_peer_floats(tables, comparisons, out_features), TROPNN_B200_ERR_INVALID,
+             "pairwise_lut_grad_allreduce: peer capacity %lld floats below the %lld needed", (long long)capacity_floats,
+             (long long)lut_grad_peer_floats(tables, comparisons, out_features));
+  LutPeer peer{};
+  for (int p = 0; p < world; ++p) {
+    TB_REQUIRE(buffers[p] != nullptr, TROPNN_B200_ERR_INVALID, "pairwise_lut_grad_allreduce: null buffer %d", p);
+    peer.buf[p] = static_cast<unsigned char *>(buffers[p]);
+  }
+  peer.world = world;
+  peer.rank = rank;
+  peer.capacity = capacity_floats;
+  peer.post_scale = average ? 1.f / float(world) : 1.f;
+  TB_CHECK(lut_grad_impl(grad_out, items, out_features, indices, tables, comparisons, scale, grad_lut, lut_dtype,
+                         world > 1 ? &peer : nullptr, as_stream(stream)));
+  return clear_error();
 }
 
 }  // extern "C"

@@ -630,8 +630,10 @@ static size_t pairwise_backward_layout(void *ws, size_t bytes, int64_t items, in
 }
 
 bool lut_grad_supported(int64_t tables, int64_t comparisons, int64_t out_features);
+struct LutPeer;
 int lut_grad_impl(const float *g, int64_t rows, int64_t out_features, const int64_t *indices, int64_t tables,
-                  int64_t comparisons, float scale, void *grad_lut, int lut_dtype, cudaStream_t stream);
+                  int64_t comparisons, float scale, void *grad_lut, int lut_dtype, const LutPeer *peer,
+                  cudaStream_t stream);
 
 int pairwise_backward_impl(const float *g, int64_t items, int64_t out, float out_scale, const int64_t *idx,
                            const float *u, const int64_t *anchors, int64_t tables, int64_t comparisons, int64_t in,
@@ -647,7 +649,7 @@ int pairwise_backward_impl(const float *g, int64_t items, int64_t out, float out
   // The one-kernel LUT gradient re-sorts a table's rows per 64-column block: taken up to
   // 1024 columns, the sort + segmented-sum pair above that.
   if (glut != nullptr && lut_grad_supported(tables, comparisons, out) && out <= 1024) {
-    TB_CHECK(lut_grad_impl(g, items, out, idx, tables, comparisons, out_scale, glut, lut_dtype, stream));
+    TB_CHECK(lut_grad_impl(g, items, out, idx, tables, comparisons, out_scale, glut, lut_dtype, nullptr, stream));
   } else if (glut != nullptr) {
     TB_CHECK(bucket_sort_impl(idx, TROPNN_B200_I64, items, tables, tables, int64_t(1) << comparisons, L.perm, L.seg,
                               stream));

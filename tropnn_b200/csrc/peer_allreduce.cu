@@ -1,4 +1,5 @@
-// Gradient all-reduce over NVLink peer memory (one process per GPU, one node).
+// Gradient all-reduce over NVLink peer memory (one process per GPU, one node). Buffer layout
+// and flag protocol: peer.cuh.
 //
 // The reference is single-device; the b200 layers scale by batch-row sharding and
 // average their parameter gradients across ranks after the backward. NCCL takes ~22 us
@@ -26,21 +27,21 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "peer.cuh"
 #include "tropnn_b200.h"
 
 namespace tropnn_b200 {
 
 namespace {
 
-constexpr int kMaxRanks = TROPNN_B200_PEER_MAX_RANKS;
+using namespace peer;
+
+constexpr int kMaxRanks = kPeerMaxRanks;
 constexpr int kMaxSegments = TROPNN_B200_PEER_MAX_SEGMENTS;
-constexpr int kMaxSlices = 512;      // CTAs per call
+constexpr int kMaxSlices = kPeerMaxSlices;  // CTAs per call
 constexpr int kThreads = 512;
-constexpr unsigned long long kWaitLimitNs = 2000ull * 1000ull * 1000ull;
-// Buffer layout: [flags kMaxSlices x kMaxRanks u32][counter kMaxSlices u32] (header),
-//                then 2 (parity) x kMaxRanks (sender) x capacity f32 receive areas.
-constexpr size_t kFlagWords = size_t(kMaxSlices) * kMaxRanks + kMaxSlices;
-constexpr size_t kHeaderBytes = (kFlagWords * 4 + 255) / 256 * 256;
+constexpr unsigned long long kWaitLimitNs = kPeerWaitLimitNs;
+constexpr size_t kHeaderBytes = kPeerHeaderBytes;
 
 __device__ int g_peer_error = 0;
 
@@ -57,27 +58,7 @@ struct PeerArgs {
   float scale;       // 1/world when averaging, else 1
 };
 
-__device__ __forceinline__ uint32_t *flags(unsigned char *b) { return reinterpret_cast<uint32_t *>(b); }
-__device__ __forceinline__ uint32_t *counters(unsigned char *b) {
-  return reinterpret_cast<uint32_t *>(b) + kMaxSlices * kMaxRanks;
-}
-__device__ __forceinline__ float *recv(unsigned char *b, int64_t capacity, uint32_t parity, int sender) {
-  return reinterpret_cast<float *>(b + kHeaderBytes) + (int64_t(parity) * kMaxRanks + sender) * capacity;
-}
-
-__device__ __forceinline__ void store_volatile(uint32_t *p, uint32_t v) {
-  asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t load_volatile(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
+__device__ __forceinline__ uint64_t global_ns() { return peer_ns(); }
 
 // Element i of the caller's concatenated segments.
 __device__ __forceinline__ float *seg_ptr(const PeerArgs &a, int64_t i) {

@@ -23,7 +23,14 @@ import torch
 import torch.distributed as dist
 from torch import Tensor
 
-__all__ = ["PeerAllReduce", "allreduce_gradients", "overlapped_gradient_sync", "row_range", "shard_rows"]
+__all__ = [
+    "PeerAllReduce",
+    "allreduce_gradients",
+    "fused_lut_allreduce",
+    "overlapped_gradient_sync",
+    "row_range",
+    "shard_rows",
+]
 
 DEFAULT_BUCKET_BYTES = 64 * 1024 * 1024
 
@@ -56,9 +63,38 @@ class _OverlapState:
         self.peer: PeerAllReduce | None = None
         self.lock = threading.Lock()
         self.streams: dict[torch.device, torch.cuda.Stream] = {}
+        self.lut_peer: PeerAllReduce | None = None
 
 
 _overlap = _OverlapState()
+
+
+@contextlib.contextmanager
+def fused_lut_allreduce(peer: "PeerAllReduce") -> Iterator[None]:
+    """Within this context the b200 PairwiseLinear backward computes its LUT gradient with the
+    all-reduce over ``peer``'s NVLink buffers fused into the same kernel
+    (tropnn_b200_pairwise_lut_grad_allreduce: each block is pushed to every rank as soon as it
+    is summed), averaging across ``peer``'s group, and marks it reduced so that
+    ``allreduce_gradients`` skips it. ``peer`` must be a set of its own (sized with
+    ``PeerAllReduce.lut_capacity``); layers it cannot take fall back to the regular path."""
+    with _overlap.lock:
+        prev = _overlap.lut_peer
+        _overlap.lut_peer = peer
+    try:
+        yield
+    finally:
+        with _overlap.lock:
+            _overlap.lut_peer = prev
+
+
+def fused_lut_peer() -> "PeerAllReduce | None":
+    """The peer set of an active ``fused_lut_allreduce`` context (None outside it)."""
+    return _overlap.lut_peer
+
+
+def mark_reduced(grad: Tensor) -> None:
+    """Marks ``grad`` as already averaged across the group (``allreduce_gradients`` skips it once)."""
+    setattr(grad, _REDUCED_ATTR, True)
 
 
 @contextlib.contextmanager
@@ -187,6 +223,18 @@ class PeerAllReduce:
     @staticmethod
     def max_ranks() -> int:
         return 8
+
+    @staticmethod
+    def lut_capacity(tables: int, comparisons: int, out_features: int) -> int:
+        """Floats a set needs for the fused LUT-gradient all-reduce of a PairwiseLinear layer
+        (-1 when the fused kernel does not take the shape)."""
+        from . import _native as nat
+
+        return int(nat.load().tropnn_b200_pairwise_lut_grad_peer_floats(tables, comparisons, out_features))
+
+    def raw(self) -> tuple[ctypes.Array, int, int, int]:
+        """(buffer pointer array, world, rank, capacity) for the library's fused kernels."""
+        return self._buffers, self.world, self.rank, self.capacity
 
     def accepts(self, tensors: Sequence[Tensor]) -> bool:
         """Whether one call can reduce ``tensors`` (f32, contiguous, on this GPU, fitting)."""

@@ -168,7 +168,38 @@ class _PairwiseB200Function(torch.autograd.Function):
         buckets = 1 << comparisons
 
         grad_lut = None
-        if ctx.needs_input_grad[2] and lut_grad_direct(tables, comparisons, out_features):
+        lut_peer = _dist.fused_lut_peer() if ctx.needs_input_grad[2] else None
+        if lut_peer is not None and lut_grad_direct(tables, comparisons, out_features):
+            need = lut_peer.lut_capacity(tables, comparisons, out_features)
+            if need < 0 or need > lut_peer.capacity or tables * ((out_features + 63) // 64) > 512:
+                lut_peer = None
+        else:
+            lut_peer = None
+        if lut_peer is not None:
+            # The LUT gradient and its data-parallel average in one kernel.
+            grad_lut = torch.empty_like(lut)
+            buffers, world, rank, capacity = lut_peer.raw()
+            _launch(
+                "pairwise_lut_grad",
+                lib.tropnn_b200_pairwise_lut_grad_allreduce,
+                g.data_ptr(),
+                items,
+                out_features,
+                indices.data_ptr(),
+                tables,
+                comparisons,
+                ctx.output_scale,
+                grad_lut.data_ptr(),
+                nat.float_code(grad_lut.dtype),
+                buffers,
+                world,
+                rank,
+                capacity,
+                1,
+                stream,
+            )
+            _dist.mark_reduced(grad_lut)
+        elif ctx.needs_input_grad[2] and lut_grad_direct(tables, comparisons, out_features):
             grad_lut = torch.empty_like(lut)
             _launch(
                 "pairwise_lut_grad",
@@ -226,7 +257,11 @@ class _PairwiseB200Function(torch.autograd.Function):
             )
         # Under distributed.overlapped_gradient_sync the LUT gradient's all-reduce runs on a
         # side stream while the straight-through kernels below execute.
-        pending = _dist.begin_gradient_reduce(grad_lut) if grad_lut is not None else None
+        pending = (
+            _dist.begin_gradient_reduce(grad_lut)
+            if grad_lut is not None and lut_peer is None
+            else None
+        )
 
         grad_latent = grad_thr = None
         want_latent = ctx.needs_input_grad[0]
