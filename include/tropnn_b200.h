@@ -291,13 +291,25 @@ TROPNN_B200_API int tropnn_b200_trop_code_transpose(const void *code, int param_
                                     int64_t code_dim, void *code_t, void *stream);
 
 /*
- * out[rows, 2*cols] = [hi | lo] per row of the f32 matrix x [rows, cols]: hi = x rounded
- * to dtype (F16/BF16), lo = (x - hi) rounded to dtype; hi + lo carries x to ~2^-22
- * relative (f16). cols % 4 == 0. Left operand of tropnn_b200_linear_f32out for an f32
- * input. No reference counterpart: a precision-splitting step of this backend.
+ * out[rows, 2*cols] = [hi | lo] per row of the f32 matrix x [rows, cols] times s: hi = x s
+ * rounded to dtype (F16/BF16), lo = (x s - hi) rounded to dtype; hi + lo carries x s to
+ * ~2^-22 relative (f16). s = 1 when grad_absmax is NULL, else the power-of-two gradient scale
+ * of the tensor maximum in *grad_absmax (tropnn_b200_absmax_f32). cols % 4 == 0. Left operand
+ * of tropnn_b200_linear_f32out for an f32 input. No reference counterpart: a precision-
+ * splitting step of this backend.
  */
-TROPNN_B200_API int tropnn_b200_split_half(const float *x, int64_t rows, int64_t cols, int dtype, void *out,
-                           void *stream);
+TROPNN_B200_API int tropnn_b200_split_half(const float *x, int64_t rows, int64_t cols, int dtype,
+                           const void *grad_absmax, void *out, void *stream);
+
+/*
+ * Gradient range for the half-precision backward GEMMs: *bits = max(*bits, f32 bits of
+ * max_i |x[i]|) (the caller zeroes the 4-byte word first; deterministic). The kernels that take
+ * a grad_absmax pointer scale the gradient by s = 2^e bringing that maximum into [16, 32)
+ * before rounding it to f16/bf16 and divide their f32 results by s (exact), so gradients far
+ * below f16's normal range (6.1e-5) keep their relative precision instead of underflowing; the
+ * reference computes these products in f32. x 16-byte aligned.
+ */
+TROPNN_B200_API int tropnn_b200_absmax_f32(const float *x, int64_t n, void *bits, void *stream);
 
 /*
  * out[n, o] = sum_s sum_k a[n, s*in + k] * weight[o, k] + bias[o] (f32 accumulation on the
@@ -363,9 +375,14 @@ TROPNN_B200_API int tropnn_b200_device_error(int *value);
  * epilogue reads the routes; U8 routes, cells in {2,4,8,16,32}, code_dim in {64,...,256}
  * (a multiple of 64), items a multiple of 8 and >= 128.
  *
+ * grad_absmax (every call below; NULL: unscaled) is the word of tropnn_b200_absmax_f32 over
+ * grad_hidden: g_split / x_t of grad_hidden and the gm weights are scaled by its power-of-two
+ * gradient scale before their rounding to the parameter dtype, and every result (gm included)
+ * is scaled back, so tiny gradients keep their precision with f16 parameters.
  * trop_gm: gm[n,h] = code_scale (<g_n, code[h,r]> - <g_n, code[h,w]>) U'(m_nh),
  *   U'(m) = -0.5 sign(m) / (1+|m|)^2, from g_split = [hi | lo] halves of grad_hidden
- *   (tropnn_b200_split_half, [items, 2*code_dim]) against code ([heads*cells, code_dim]).
+ *   (tropnn_b200_split_half with the same grad_absmax, [items, 2*code_dim]) against code
+ *   ([heads*cells, code_dim]).
  * trop_router_term: grad_latent = grad_hidden + sum_h gm[n,h] (W[h,w] - W[h,r]), with
  *   router_weight_t = router_weight transposed ([code_dim, heads*cells],
  *   tropnn_b200_trop_code_transpose); gm rounded to the parameter dtype in the product.
@@ -377,22 +394,24 @@ TROPNN_B200_API int tropnn_b200_device_error(int *value);
  *   out_scale = 1, x = latent, and grad_bias[h,k] = sum_n gm ([w==k] - [r==k]) when not NULL.
  *   grad / grad_bias in the parameter dtype; x_t's rounding of grad_hidden is within the 2e-2
  *   half-precision tolerance.
- * transpose_to_half: out[c, r] = x[r, c] rounded to dtype; x in x_dtype (F32 or dtype).
+ * transpose_to_half: out[c, r] = x[r, c] s rounded to dtype; x in x_dtype (F32 or dtype), s the
+ *   gradient scale of grad_absmax (1 when NULL).
  * No reference counterparts as entry points: they restate the reference's backward as GEMMs.
  */
 TROPNN_B200_API int tropnn_b200_trop_gm(const void *g_split, int64_t items, int64_t code_dim, const void *code,
                         int param_dtype, int64_t heads, int64_t cells, const void *winner, const void *runner,
-                        const float *margins, float code_scale, float *gm, void *stream);
+                        const float *margins, float code_scale, float *gm, const void *grad_absmax,
+                        void *stream);
 TROPNN_B200_API int tropnn_b200_trop_router_term(const float *grad_hidden, int64_t items, int64_t code_dim,
                                  const void *router_weight_t, int param_dtype, int64_t heads, int64_t cells,
-                                 const void *winner, const void *runner, const float *gm, float *grad_latent,
-                                 void *stream);
+                                 const void *winner, const void *runner, const float *gm,
+                                 const void *grad_absmax, float *grad_latent, void *stream);
 TROPNN_B200_API int tropnn_b200_trop_param_grad(int mode, const void *x_t, int64_t items, int64_t code_dim,
                                 int param_dtype, int64_t heads, int64_t cells, const void *winner,
                                 const void *runner, const float *values, float code_scale, void *grad,
-                                void *grad_bias, void *stream);
+                                void *grad_bias, const void *grad_absmax, void *stream);
 TROPNN_B200_API int tropnn_b200_transpose_to_half(const void *x, int x_dtype, int64_t rows, int64_t cols, int dtype,
-                                  void *out, void *stream);
+                                  const void *grad_absmax, void *out, void *stream);
 
 /*
  * Gradients of the f32 output map out = hidden weight^T + bias (layers/tropical.py:140-146,

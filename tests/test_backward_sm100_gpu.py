@@ -44,13 +44,13 @@ def _routes(z, weight, bias):
     return win.long().cpu().numpy(), run.long().cpu().numpy(), m.cpu().numpy()
 
 
-def _check(items, heads, cells, code_dim, dtype, training, seed=0):
+def _check(items, heads, cells, code_dim, dtype, training, seed=0, g_scale=1.0, check_params=True, z_dtype=None):
     gen = torch.Generator().manual_seed(seed)
-    z = torch.randn(items, code_dim, generator=gen).to(dtype).cuda()
+    z = torch.randn(items, code_dim, generator=gen).to(z_dtype or dtype).cuda()
     weight = (torch.randn(heads, cells, code_dim, generator=gen) / code_dim**0.5).to(dtype).cuda()
     bias = (0.1 * torch.randn(heads, cells, generator=gen)).to(dtype).cuda()
     code = (0.5 * torch.randn(heads, cells, code_dim, generator=gen)).to(dtype).cuda()
-    g = torch.randn(items, code_dim, generator=gen).cuda()
+    g = (torch.randn(items, code_dim, generator=gen) * g_scale).cuda()
     scale = heads**-0.5
     params = [t.clone().requires_grad_(True) for t in (weight, bias, code)]
     zl = z.clone().requires_grad_(True)
@@ -66,6 +66,8 @@ def _check(items, heads, cells, code_dim, dtype, training, seed=0):
     )
     tol = TOL[dtype]
     assert rel_err(zl.grad.float().cpu().numpy(), ref["grad_latent"]) <= tol
+    if not check_params:
+        return
     assert rel_err(params[2].grad.float().cpu().numpy(), ref["grad_code"]) <= tol
     if training:
         assert rel_err(params[0].grad.float().cpu().numpy(), ref["grad_router_weight"]) <= tol
@@ -96,6 +98,23 @@ def test_cells(cells):
 )
 def test_shapes(items, heads, cells, code_dim):
     _check(items, heads, cells, code_dim, torch.float16, True)
+
+
+@pytest.mark.parametrize("g_scale", [1e-7, 1e5])
+def test_gradient_range(g_scale):
+    """Upstream gradients far below f16's normal range (1e-7: rounded to f16 as they are, g and gm
+    would mostly flush to zero) and beyond its maximum (1e5: g itself would overflow): the
+    power-of-two gradient scale keeps grad_latent (f32 here: an f32 latent) within the tolerance
+    of O(1) gradients.
+    The parameter gradients are f16 outputs, rounded like the reference's (whose f32 values are
+    cast back to the parameter dtype), so at these scales they leave f16's range in both."""
+    _check(512, 256, 16, 128, torch.float16, True, seed=3, g_scale=g_scale, check_params=False, z_dtype=torch.float32)
+
+
+def test_small_gradients_parameter_grads():
+    """Gradients of 1e-3 (gm ~1e-5: its f16 rounding alone would keep ~1e-2 relative): every
+    gradient, the f16 parameter gradients included, within the tolerance."""
+    _check(512, 256, 16, 128, torch.float16, True, seed=4, g_scale=1e-3, z_dtype=torch.float32)
 
 
 def test_no_device_error():

@@ -79,7 +79,7 @@ def test_split_half_is_exact_to_two_terms():
     out = torch.empty(64, 256, dtype=torch.float16, device="cuda")
     nat.check(
         nat.load().tropnn_b200_split_half(
-            x.data_ptr(), 64, 128, nat.F16, out.data_ptr(), torch.cuda.current_stream().cuda_stream
+            x.data_ptr(), 64, 128, nat.F16, None, out.data_ptr(), torch.cuda.current_stream().cuda_stream
         ),
         "split_half",
     )

@@ -34,6 +34,27 @@ int ensure_dynamic_smem(const void *func, size_t bytes, const char *what);
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Power-of-two scale that brings a gradient tensor whose largest |value| has the f32 bits
+// `absmax_bits` into [16, 32): converted to f16 after it, the gradient neither underflows (f16's
+// smallest normal is 6.1e-5) nor overflows in the products formed from it, and the f32 results
+// are divided by it again exactly. 1 for a zero or non-finite maximum.
+__device__ __forceinline__ float pow2_grad_scale(uint32_t absmax_bits) {
+  const int exp_field = static_cast<int>((absmax_bits >> 23) & 0xFFu);
+  if (absmax_bits == 0u || exp_field == 0xFF) return 1.f;
+  int e = 4 - (exp_field - 127);
+  e = e < -126 ? -126 : (e > 126 ? 126 : e);
+  return __int_as_float((e + 127) << 23);
+}
+// 1/s for a power of two s from pow2_grad_scale (exact).
+__device__ __forceinline__ float pow2_inverse(float s) {
+  const int e = static_cast<int>((__float_as_uint(s) >> 23) & 0xFFu) - 127;
+  return __int_as_float((127 - e) << 23);
+}
+// The scale of pow2_grad_scale for an optional device word (NULL: 1).
+__device__ __forceinline__ float grad_scale_of(const uint32_t *absmax) {
+  return absmax != nullptr ? pow2_grad_scale(*absmax) : 1.f;
+}
+
 #define TB_REQUIRE(cond, status, ...)                  \
   do {                                                 \
     if (!(cond)) return ::tropnn_b200::set_error(status, __VA_ARGS__); \

@@ -81,6 +81,7 @@ struct GmArgs {
   int64_t rows;
   int heads;
   float code_scale;
+  const uint32_t *absmax;  // the g split was scaled by pow2_grad_scale(*absmax) (NULL: not scaled)
 };
 
 template <typename PT, int K>  // K = 0: f32 output map; K = cells: route-margin gradient
@@ -229,6 +230,8 @@ __global__ void __launch_bounds__(kThreads, 1) linear_f32out_kernel(
     const int quarter = warp & 3;
     const int group = (warp - 2) >> 2;
     uint8_t *stage = o_smem + (warp - 2) * kStageOutBytes;
+    // Route-margin gradient: undo the power-of-two scale of the g split (exact).
+    const float gm_unscale = K > 0 ? pow2_inverse(grad_scale_of(gmx.absmax)) : 1.f;
     uint32_t t = 0;
     for (int64_t u = u_begin; u < u_end; ++u, ++t) {
       const int64_t rb = u / tiles_total;
@@ -293,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_f32out_kernel(
               br |= x & (0u - uint32_t(rv[hh] == uint32_t(k)));
             }
             const float dw = __uint_as_float(bw), dr = __uint_as_float(br);
-            const float gm = __fmul_rn(__fsub_rn(dr, dw), fv[hh]);
+            const float gm = __fmul_rn(__fmul_rn(__fsub_rn(dr, dw), fv[hh]), gm_unscale);
             if (row < gmx.rows && h0 + hh < gmx.heads) gmx.gm[row * gmx.heads + h0 + hh] = gm;
           }
           continue;
@@ -358,17 +361,19 @@ __global__ void __launch_bounds__(kThreads, 1) linear_f32out_kernel(
   }
 }
 
-// [hi | lo] halves of each f32 row: hi = half(x), lo = half(x - hi).
+// [hi | lo] halves of each f32 row: hi = half(x s), lo = half(x s - hi), s = the power-of-two
+// gradient scale of *absmax (1 without it).
 template <typename PT>
 __global__ void __launch_bounds__(256) split_half_kernel(const float *__restrict__ x, int64_t rows, int cols,
-                                                          PT *__restrict__ out) {
+                                                          const uint32_t *__restrict__ absmax, PT *__restrict__ out) {
+  const float s = grad_scale_of(absmax);
   const int64_t total = rows * cols / 4;
   for (int64_t q = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; q < total; q += int64_t(gridDim.x) * blockDim.x) {
     const int64_t i = q * 4;
     const int64_t row = i / cols;
     const int col = static_cast<int>(i - row * cols);
     const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + q);
-    const float xs[4] = {v.x, v.y, v.z, v.w};
+    const float xs[4] = {__fmul_rn(v.x, s), __fmul_rn(v.y, s), __fmul_rn(v.z, s), __fmul_rn(v.w, s)};
     PT hi[4], lo[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -378,6 +383,30 @@ __global__ void __launch_bounds__(256) split_half_kernel(const float *__restrict
     PT *o = out + row * (2 * int64_t(cols)) + col;
     *reinterpret_cast<uint2 *>(o) = *reinterpret_cast<const uint2 *>(hi);
     *reinterpret_cast<uint2 *>(o + cols) = *reinterpret_cast<const uint2 *>(lo);
+  }
+}
+
+// *bits = max(*bits, f32 bits of max |x|): non-negative floats order as their bit patterns,
+// so the integer maximum is order-independent (deterministic). The caller zeroes *bits first.
+__global__ void __launch_bounds__(256) absmax_kernel(const float *__restrict__ x, int64_t n,
+                                                     uint32_t *__restrict__ bits) {
+  uint32_t m = 0u;
+  const int64_t quads = n / 4;
+  for (int64_t q = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; q < quads; q += int64_t(gridDim.x) * blockDim.x) {
+    const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + q);
+    m = max(m, max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+                   max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w)))));
+  }
+  for (int64_t i = quads * 4 + blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+    m = max(m, __float_as_uint(fabsf(__ldg(x + i))));
+  m = __reduce_max_sync(0xffffffffu, m);
+  __shared__ uint32_t wmax[8];
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t b = wmax[0];
+    for (int w = 1; w < 8; ++w) b = max(b, wmax[w]);
+    atomicMax(bits, b);
   }
 }
 
@@ -449,14 +478,14 @@ int linear_f32out_impl(const void *a, int64_t rows, int64_t slices, const void *
 // the code table [heads*cells, code_dim] (the B operand as stored).
 int trop_gm_sm100_impl(const void *g_split, int64_t rows, int64_t code_dim, const void *code, int dtype, int64_t heads,
                        int64_t cells, const uint8_t *winner, const uint8_t *runner, const float *margins,
-                       float code_scale, float *gm, cudaStream_t stream) {
+                       float code_scale, float *gm, const uint32_t *absmax, cudaStream_t stream) {
   const int64_t hk = heads * cells;
   TB_REQUIRE(linear_f32out_supported(rows, 2, hk, code_dim, dtype) &&
                  (cells == 2 || cells == 4 || cells == 8 || cells == 16 || cells == 32),
              TROPNN_B200_ERR_INVALID, "trop_gm_sm100: unsupported shape rows=%lld code_dim=%lld heads=%lld cells=%lld",
              (long long)rows, (long long)code_dim, (long long)heads, (long long)cells);
   TB_REQUIRE(g_split && code && winner && runner && margins && gm, TROPNN_B200_ERR_INVALID, "trop_gm_sm100: null pointer");
-  const GmArgs gmx{winner, runner, margins, gm, rows, static_cast<int>(heads), code_scale};
+  const GmArgs gmx{winner, runner, margins, gm, rows, static_cast<int>(heads), code_scale, absmax};
   const int n = static_cast<int>(hk), k = static_cast<int>(code_dim);
   auto go = [&](auto pt_tag) -> int {
     using T = decltype(pt_tag);
@@ -472,7 +501,8 @@ int trop_gm_sm100_impl(const void *g_split, int64_t rows, int64_t code_dim, cons
   return go(__nv_bfloat16());
 }
 
-int split_half_impl(const float *x, int64_t rows, int64_t cols, int dtype, void *out, cudaStream_t stream) {
+int split_half_impl(const float *x, int64_t rows, int64_t cols, int dtype, const uint32_t *absmax, void *out,
+                    cudaStream_t stream) {
   TB_REQUIRE(dtype == TROPNN_B200_F16 || dtype == TROPNN_B200_BF16, TROPNN_B200_ERR_DTYPE,
              "split_half: dtype %s unsupported (f16/bf16 only)", dtype_name(dtype));
   TB_REQUIRE(rows >= 0 && cols > 0 && cols % 4 == 0 && cols <= (1 << 30), TROPNN_B200_ERR_INVALID,
@@ -486,11 +516,23 @@ int split_half_impl(const float *x, int64_t rows, int64_t cols, int dtype, void 
   const int64_t quads = rows * cols / 4;
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(quads, int64_t(256)), int64_t(sms) * 8));
   if (dtype == TROPNN_B200_F16)
-    split_half_kernel<__half><<<grid, 256, 0, stream>>>(x, rows, static_cast<int>(cols), static_cast<__half *>(out));
+    split_half_kernel<__half><<<grid, 256, 0, stream>>>(x, rows, static_cast<int>(cols), absmax,
+                                                        static_cast<__half *>(out));
   else
-    split_half_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(x, rows, static_cast<int>(cols),
+    split_half_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(x, rows, static_cast<int>(cols), absmax,
                                                                static_cast<__nv_bfloat16 *>(out));
   return check_launch("split_half");
+}
+
+int absmax_impl(const float *x, int64_t n, uint32_t *bits, cudaStream_t stream) {
+  TB_REQUIRE(n >= 0 && bits != nullptr && (n == 0 || x != nullptr), TROPNN_B200_ERR_INVALID, "absmax: bad arguments");
+  TB_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0, TROPNN_B200_ERR_INVALID, "absmax: x must be 16-byte aligned");
+  if (n == 0) return TROPNN_B200_OK;
+  int sms = 0;
+  TB_CHECK(sm_count(&sms));
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(n, int64_t(1024)), int64_t(sms) * 4));
+  absmax_kernel<<<grid, 256, 0, stream>>>(x, n, bits);
+  return check_launch("absmax");
 }
 
 int read_gemm_error(int *value) {
@@ -510,9 +552,17 @@ int read_gemm_error(int *value) {
 
 extern "C" {
 
-int tropnn_b200_split_half(const float *x, int64_t rows, int64_t cols, int dtype, void *out, void *stream) {
+int tropnn_b200_split_half(const float *x, int64_t rows, int64_t cols, int dtype, const void *grad_absmax, void *out,
+                           void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
-  TB_CHECK(tropnn_b200::split_half_impl(x, rows, cols, dtype, out, tropnn_b200::as_stream(stream)));
+  TB_CHECK(tropnn_b200::split_half_impl(x, rows, cols, dtype, static_cast<const uint32_t *>(grad_absmax), out,
+                                        tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+int tropnn_b200_absmax_f32(const float *x, int64_t n, void *bits, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::absmax_impl(x, n, static_cast<uint32_t *>(bits), tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 

@@ -154,9 +154,14 @@ template <typename PT, typename LT, int K, int MODE>
 __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
     const __grid_constant__ CUtensorMap map_ct, const LT *__restrict__ latent, const uint8_t *__restrict__ winner,
     const uint8_t *__restrict__ runner, const float *__restrict__ margins, float code_scale, int64_t rows, int H,
-    int D, int kblocks, int bstages, int64_t row_blocks, float *__restrict__ hidden) {
+    int D, int kblocks, int bstages, int64_t row_blocks, const uint32_t *__restrict__ absmax,
+    float *__restrict__ hidden) {
   static_assert(K >= 2 && K <= kBK && K % 2 == 0, "cells must be even and at most 64");
   constexpr int kHeadsPerBlock = kBK / K;
+  // Signed mode (router term of grad_z): the gm weights are scaled by the power-of-two gradient
+  // scale of *absmax before their conversion to PT, the product scaled back in the epilogue.
+  const float gscale = MODE == kOneHotSigned ? grad_scale_of(absmax) : 1.f;
+  const float out_scale = __fmul_rn(code_scale, pow2_inverse(gscale));
   constexpr uint32_t kOne = HalfBits<PT>::kOne;
   const uint32_t idesc = umma_idesc_f16(HalfBits<PT>::kFormat, kBM, D);
   const int b_stage_bytes = D * 128;
@@ -297,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
               vr[hh] = HalfBits<PT>::bits(alpha);
             } else if constexpr (MODE == kOneHotSigned) {
               rc[hh] = __ldg(rrow + h);
-              const float gm = __ldg(mrow + h);
+              const float gm = __fmul_rn(__ldg(mrow + h), gscale);
               vw[hh] = HalfBits<PT>::bits(gm);
               vr[hh] = HalfBits<PT>::bits(-gm);
             }
@@ -359,9 +364,9 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
 #pragma unroll
           for (int e = 0; e < 32; e += 4)
             *reinterpret_cast<float4 *>(out + e) = make_float4(
-                __fadd_rn(lat[e], __fmul_rn(acc[e], code_scale)), __fadd_rn(lat[e + 1], __fmul_rn(acc[e + 1], code_scale)),
-                __fadd_rn(lat[e + 2], __fmul_rn(acc[e + 2], code_scale)),
-                __fadd_rn(lat[e + 3], __fmul_rn(acc[e + 3], code_scale)));
+                __fadd_rn(lat[e], __fmul_rn(acc[e], out_scale)), __fadd_rn(lat[e + 1], __fmul_rn(acc[e + 1], out_scale)),
+                __fadd_rn(lat[e + 2], __fmul_rn(acc[e + 2], out_scale)),
+                __fadd_rn(lat[e + 3], __fmul_rn(acc[e + 3], out_scale)));
         }
       }
     }
@@ -400,7 +405,7 @@ int b_stages(int D) {
 
 template <typename PT, typename LT, int K>
 int launch_onehot(const void *latent, int64_t rows, int D, const void *code_t, int H, const uint8_t *win,
-                  const uint8_t *run, const float *m, float code_scale, int mode, float *hidden,
+                  const uint8_t *run, const float *m, float code_scale, int mode, const uint32_t *absmax, float *hidden,
                   cudaStream_t stream) {
   const CUtensorMapDataType dt =
       std::is_same<PT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -421,22 +426,22 @@ int launch_onehot(const void *latent, int64_t rows, int D, const void *code_t, i
                                          : trop_hidden_onehot_kernel<PT, LT, K, kOneHotEval>;
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_hidden_sm100"));
   kernel<<<grid, kThreads, smem, stream>>>(map_ct, static_cast<const LT *>(latent), win, run, m, code_scale, rows, H, D,
-                                           kblocks, bst, row_blocks, hidden);
+                                           kblocks, bst, row_blocks, absmax, hidden);
   return check_launch("trop_hidden_sm100");
 }
 
 template <typename PT, typename LT>
 int dispatch_onehot(int K, const void *latent, int64_t rows, int D, const void *code_t, int H, const uint8_t *win,
-                    const uint8_t *run, const float *m, float code_scale, int mode, float *hidden,
+                    const uint8_t *run, const float *m, float code_scale, int mode, const uint32_t *absmax, float *hidden,
                     cudaStream_t stream) {
   switch (K) {
-    case 2: return launch_onehot<PT, LT, 2>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, hidden, stream);
-    case 4: return launch_onehot<PT, LT, 4>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, hidden, stream);
-    case 8: return launch_onehot<PT, LT, 8>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, hidden, stream);
+    case 2: return launch_onehot<PT, LT, 2>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, stream);
+    case 4: return launch_onehot<PT, LT, 4>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, stream);
+    case 8: return launch_onehot<PT, LT, 8>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, stream);
     case 16:
-      return launch_onehot<PT, LT, 16>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, hidden, stream);
+      return launch_onehot<PT, LT, 16>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, stream);
     default:
-      return launch_onehot<PT, LT, 32>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, hidden, stream);
+      return launch_onehot<PT, LT, 32>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, stream);
   }
 }
 
@@ -453,7 +458,7 @@ bool hidden_sm100_supported(int64_t items, int64_t D, int64_t H, int64_t K, int 
 
 int trop_hidden_sm100_impl(const void *latent, int zt, int64_t items, int64_t D, const void *code_t, int pt,
                            int64_t H, int64_t K, const void *win, const void *run, const float *m, float code_scale,
-                           int mode, float *hidden, cudaStream_t stream) {
+                           int mode, const uint32_t *absmax, float *hidden, cudaStream_t stream) {
   TB_REQUIRE(hidden_sm100_supported(items, D, H, K, pt, zt, TROPNN_B200_U8, latent, code_t, hidden),
              TROPNN_B200_ERR_INVALID, "trop_hidden_sm100: unsupported shape, dtype or alignment");
   TB_REQUIRE(mode >= kOneHotEval && mode <= kOneHotSigned, TROPNN_B200_ERR_INVALID, "trop_hidden_sm100: bad mode");
@@ -463,16 +468,16 @@ int trop_hidden_sm100_impl(const void *latent, int zt, int64_t items, int64_t D,
   const auto *r = static_cast<const uint8_t *>(run);
   if (pt == TROPNN_B200_F16) {
     if (zt == TROPNN_B200_F32)
-      return dispatch_onehot<__half, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, hidden,
+      return dispatch_onehot<__half, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, absmax, hidden,
                                             stream);
-    return dispatch_onehot<__half, __half>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, hidden,
+    return dispatch_onehot<__half, __half>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, absmax, hidden,
                                            stream);
   }
   if (zt == TROPNN_B200_F32)
-    return dispatch_onehot<__nv_bfloat16, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, hidden,
+    return dispatch_onehot<__nv_bfloat16, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, absmax, hidden,
                                                  stream);
   return dispatch_onehot<__nv_bfloat16, __nv_bfloat16>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode,
-                                                       hidden, stream);
+                                                       absmax, hidden, stream);
 }
 
 int trop_code_transpose_impl(const void *code, int pt, int64_t H, int64_t K, int64_t D, void *code_t,

@@ -119,12 +119,15 @@ template <typename PT, int K, int MODE>
 __global__ void __launch_bounds__(kThreads, 1) trop_param_grad_kernel(
     const __grid_constant__ CUtensorMap map_xt, const uint8_t *__restrict__ winner, const uint8_t *__restrict__ runner,
     const float *__restrict__ mvals, float code_scale, int64_t rows, int H, int D, int kblocks, int bstages, int tiles,
-    PT *__restrict__ out) {
+    const uint32_t *__restrict__ absmax, PT *__restrict__ out) {
   static_assert(K >= 2 && K <= 32 && (K & (K - 1)) == 0, "cells must be a power of two in [2, 32]");
   constexpr int kHeadsPerTile = kBM / K;
   const uint32_t idesc = umma_idesc_f16(std::is_same<PT, __half>::value ? 0 : 1, kBM, D);
   const int b_stage_bytes = D * 128;
-  const float out_scale = MODE == kRouter ? 1.f : code_scale;
+  // Gradient scale (power of two) of g_t (modes 0, 1: applied by its transpose) or of the gm
+  // weights (mode 2: applied by the builders), undone by the epilogue.
+  const float gscale = grad_scale_of(absmax);
+  const float out_scale = __fmul_rn(MODE == kRouter ? 1.f : code_scale, pow2_inverse(gscale));
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -270,8 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1) trop_param_grad_kernel(
           vw = half_bits<PT>(__fsub_rn(1.f, alpha));
           vr = half_bits<PT>(alpha);
         } else {
-          vw = half_bits<PT>(mv);
-          vr = half_bits<PT>(-mv);
+          vw = half_bits<PT>(__fmul_rn(mv, gscale));
+          vr = half_bits<PT>(-__fmul_rn(mv, gscale));
         }
       }
       return make_uint2(w | (r << 8), vw | (vr << 16));
@@ -467,16 +470,19 @@ int launch_bias_grad(const uint8_t *w, const uint8_t *r, const float *gm, int64_
   return check_launch("router_bias_grad");
 }
 
-// x [rows_in, cols] (f32 or half) -> out [cols, rows_in] in PT, 32 x 32 tiles.
+// x [rows_in, cols] (f32 or half) times the power-of-two gradient scale of *absmax (1 without it)
+// -> out [cols, rows_in] in PT, 32 x 32 tiles.
 template <typename IT, typename PT>
 __global__ void __launch_bounds__(256) transpose_to_half_kernel(const IT *__restrict__ in, PT *__restrict__ out,
-                                                                int64_t rows_in, int cols) {
+                                                                int64_t rows_in, int cols,
+                                                                const uint32_t *__restrict__ absmax) {
   __shared__ float tile[32][33];
+  const float s = grad_scale_of(absmax);
   const int64_t r0 = int64_t(blockIdx.x) * 32;
   const int c0 = blockIdx.y * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   for (int j = ty; j < 32; j += 8)
-    if (r0 + j < rows_in && c0 + tx < cols) tile[j][tx] = to_f32(in[(r0 + j) * cols + c0 + tx]);
+    if (r0 + j < rows_in && c0 + tx < cols) tile[j][tx] = __fmul_rn(to_f32(in[(r0 + j) * cols + c0 + tx]), s);
   __syncthreads();
   for (int j = ty; j < 32; j += 8)
     if (c0 + j < cols && r0 + tx < rows_in) out[int64_t(c0 + j) * rows_in + r0 + tx] = from_f32<PT>(tile[tx][j]);
@@ -491,7 +497,7 @@ int b_stages(int D) {
 
 template <typename PT, int K, int MODE>
 int launch_param_grad(const void *xt, int64_t rows, int D, int H, const uint8_t *win, const uint8_t *run,
-                      const float *mvals, float code_scale, void *out, cudaStream_t stream) {
+                      const float *mvals, float code_scale, const uint32_t *absmax, void *out, cudaStream_t stream) {
   const CUtensorMapDataType dt =
       std::is_same<PT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap map_xt;
@@ -507,19 +513,19 @@ int launch_param_grad(const void *xt, int64_t rows, int D, int H, const uint8_t 
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_param_grad"));
   const unsigned grid = static_cast<unsigned>(std::min(tiles, sms));
   kernel<<<grid, kThreads, smem, stream>>>(map_xt, win, run, mvals, code_scale, rows, H, D, kblocks, bst, tiles,
-                                           static_cast<PT *>(out));
+                                           absmax, static_cast<PT *>(out));
   return check_launch("trop_param_grad");
 }
 
 template <typename PT, int MODE>
 int dispatch_param_grad(int K, const void *xt, int64_t rows, int D, int H, const uint8_t *win, const uint8_t *run,
-                        const float *mvals, float code_scale, void *out, cudaStream_t stream) {
+                        const float *mvals, float code_scale, const uint32_t *absmax, void *out, cudaStream_t stream) {
   switch (K) {
-    case 2: return launch_param_grad<PT, 2, MODE>(xt, rows, D, H, win, run, mvals, code_scale, out, stream);
-    case 4: return launch_param_grad<PT, 4, MODE>(xt, rows, D, H, win, run, mvals, code_scale, out, stream);
-    case 8: return launch_param_grad<PT, 8, MODE>(xt, rows, D, H, win, run, mvals, code_scale, out, stream);
-    case 16: return launch_param_grad<PT, 16, MODE>(xt, rows, D, H, win, run, mvals, code_scale, out, stream);
-    default: return launch_param_grad<PT, 32, MODE>(xt, rows, D, H, win, run, mvals, code_scale, out, stream);
+    case 2: return launch_param_grad<PT, 2, MODE>(xt, rows, D, H, win, run, mvals, code_scale, absmax, out, stream);
+    case 4: return launch_param_grad<PT, 4, MODE>(xt, rows, D, H, win, run, mvals, code_scale, absmax, out, stream);
+    case 8: return launch_param_grad<PT, 8, MODE>(xt, rows, D, H, win, run, mvals, code_scale, absmax, out, stream);
+    case 16: return launch_param_grad<PT, 16, MODE>(xt, rows, D, H, win, run, mvals, code_scale, absmax, out, stream);
+    default: return launch_param_grad<PT, 32, MODE>(xt, rows, D, H, win, run, mvals, code_scale, absmax, out, stream);
   }
 }
 
@@ -535,7 +541,7 @@ bool param_grad_sm100_supported(int64_t rows, int64_t D, int64_t H, int64_t K, i
 // then grad_b (param dtype [H, K]) may be given).
 int trop_param_grad_sm100_impl(int mode, const void *xt, int64_t rows, int64_t D, int pt, int64_t H, int64_t K,
                                const void *win, const void *run, const float *mvals, float code_scale, void *out,
-                               void *grad_b, cudaStream_t stream) {
+                               void *grad_b, const uint32_t *absmax, cudaStream_t stream) {
   TB_REQUIRE(param_grad_sm100_supported(rows, D, H, K, pt), TROPNN_B200_ERR_INVALID,
              "trop_param_grad_sm100: unsupported shape rows=%lld code_dim=%lld cells=%lld dtype=%s", (long long)rows,
              (long long)D, (long long)K, dtype_name(pt));
@@ -547,16 +553,16 @@ int trop_param_grad_sm100_impl(int mode, const void *xt, int64_t rows, int64_t D
   const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
   int status;
   if (pt == TROPNN_B200_F16) {
-    status = mode == 0   ? dispatch_param_grad<__half, kCodeEval>(Ki, xt, rows, Di, Hi, w, r, mvals, code_scale, out, stream)
-             : mode == 1 ? dispatch_param_grad<__half, kCodeTrain>(Ki, xt, rows, Di, Hi, w, r, mvals, code_scale, out, stream)
-                         : dispatch_param_grad<__half, kRouter>(Ki, xt, rows, Di, Hi, w, r, mvals, code_scale, out, stream);
+    status = mode == 0   ? dispatch_param_grad<__half, kCodeEval>(Ki, xt, rows, Di, Hi, w, r, mvals, code_scale, absmax, out, stream)
+             : mode == 1 ? dispatch_param_grad<__half, kCodeTrain>(Ki, xt, rows, Di, Hi, w, r, mvals, code_scale, absmax, out, stream)
+                         : dispatch_param_grad<__half, kRouter>(Ki, xt, rows, Di, Hi, w, r, mvals, code_scale, absmax, out, stream);
   } else {
-    status = mode == 0 ? dispatch_param_grad<__nv_bfloat16, kCodeEval>(Ki, xt, rows, Di, Hi, w, r, mvals, code_scale, out,
+    status = mode == 0 ? dispatch_param_grad<__nv_bfloat16, kCodeEval>(Ki, xt, rows, Di, Hi, w, r, mvals, code_scale, absmax, out,
                                                                         stream)
              : mode == 1 ? dispatch_param_grad<__nv_bfloat16, kCodeTrain>(Ki, xt, rows, Di, Hi, w, r, mvals, code_scale,
-                                                                          out, stream)
+                                                                          absmax, out, stream)
                          : dispatch_param_grad<__nv_bfloat16, kRouter>(Ki, xt, rows, Di, Hi, w, r, mvals, code_scale,
-                                                                       out, stream);
+                                                                       absmax, out, stream);
   }
   TB_CHECK(status);
   if (mode == 2 && grad_b != nullptr) {
@@ -578,7 +584,7 @@ int trop_param_grad_sm100_impl(int mode, const void *xt, int64_t rows, int64_t D
 }
 
 int transpose_to_half_impl(const void *x, int xt_dtype, int64_t rows, int64_t cols, int pt, void *out,
-                           cudaStream_t stream) {
+                           const uint32_t *absmax, cudaStream_t stream) {
   TB_REQUIRE(pt == TROPNN_B200_F16 || pt == TROPNN_B200_BF16, TROPNN_B200_ERR_DTYPE,
              "transpose_to_half: dtype %s unsupported", dtype_name(pt));
   TB_REQUIRE(xt_dtype == TROPNN_B200_F32 || xt_dtype == pt, TROPNN_B200_ERR_DTYPE,
@@ -591,17 +597,17 @@ int transpose_to_half_impl(const void *x, int xt_dtype, int64_t rows, int64_t co
   if (pt == TROPNN_B200_F16) {
     if (xt_dtype == TROPNN_B200_F32)
       transpose_to_half_kernel<float, __half><<<grid, 256, 0, stream>>>(static_cast<const float *>(x),
-                                                                      static_cast<__half *>(out), rows, c);
+                                                                      static_cast<__half *>(out), rows, c, absmax);
     else
       transpose_to_half_kernel<__half, __half><<<grid, 256, 0, stream>>>(static_cast<const __half *>(x),
-                                                                       static_cast<__half *>(out), rows, c);
+                                                                       static_cast<__half *>(out), rows, c, absmax);
   } else {
     if (xt_dtype == TROPNN_B200_F32)
       transpose_to_half_kernel<float, __nv_bfloat16><<<grid, 256, 0, stream>>>(
-          static_cast<const float *>(x), static_cast<__nv_bfloat16 *>(out), rows, c);
+          static_cast<const float *>(x), static_cast<__nv_bfloat16 *>(out), rows, c, absmax);
     else
       transpose_to_half_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, stream>>>(
-          static_cast<const __nv_bfloat16 *>(x), static_cast<__nv_bfloat16 *>(out), rows, c);
+          static_cast<const __nv_bfloat16 *>(x), static_cast<__nv_bfloat16 *>(out), rows, c, absmax);
   }
   return check_launch("transpose_to_half");
 }

@@ -32,7 +32,7 @@ bool hidden_sm100_supported(int64_t items, int64_t D, int64_t H, int64_t K, int 
                             const void *code_t, const void *hidden);
 int trop_hidden_sm100_impl(const void *latent, int zt, int64_t items, int64_t D, const void *code_t, int pt,
                            int64_t H, int64_t K, const void *win, const void *run, const float *m, float code_scale,
-                           int mode, float *hidden, cudaStream_t stream);
+                           int mode, const uint32_t *absmax, float *hidden, cudaStream_t stream);
 int trop_code_transpose_impl(const void *code, int pt, int64_t H, int64_t K, int64_t D, void *code_t,
                              cudaStream_t stream);
 int read_hidden_error(int *value);
@@ -43,12 +43,12 @@ int read_linear_grad_error(int *value);
 int read_lut_grad_error(int *value);
 int trop_gm_sm100_impl(const void *g_split, int64_t rows, int64_t code_dim, const void *code, int dtype, int64_t heads,
                        int64_t cells, const uint8_t *winner, const uint8_t *runner, const float *margins,
-                       float code_scale, float *gm, cudaStream_t stream);
+                       float code_scale, float *gm, const uint32_t *absmax, cudaStream_t stream);
 int trop_param_grad_sm100_impl(int mode, const void *xt, int64_t rows, int64_t D, int pt, int64_t H, int64_t K,
                                const void *win, const void *run, const float *mvals, float code_scale, void *out,
-                               void *grad_b, cudaStream_t stream);
+                               void *grad_b, const uint32_t *absmax, cudaStream_t stream);
 int transpose_to_half_impl(const void *x, int xt_dtype, int64_t rows, int64_t cols, int pt, void *out,
-                           cudaStream_t stream);
+                           const uint32_t *absmax, cudaStream_t stream);
 
 namespace {
 
@@ -519,7 +519,8 @@ int trop_hidden_impl(const void *z, int zt, int64_t items, int64_t D, const void
              "trop_hidden: null pointer");
   // Half-precision codes with their transpose at hand: one-hot GEMM on the tensor cores.
   if (hidden_sm100_supported(items, D, H, K, pt, zt, it, z, code_t, hidden))
-    return trop_hidden_sm100_impl(z, zt, items, D, code_t, pt, H, K, win, run, m, code_scale, training, hidden, stream);
+    return trop_hidden_sm100_impl(z, zt, items, D, code_t, pt, H, K, win, run, m, code_scale, training, nullptr, hidden,
+                                  stream);
   const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
   const bool train = training != 0;
   const bool zp = zt != TROPNN_B200_F32;
@@ -673,40 +674,46 @@ int tropnn_b200_trop_code_transpose(const void *code, int param_dtype, int64_t h
 
 int tropnn_b200_trop_gm(const void *g_split, int64_t items, int64_t code_dim, const void *code, int param_dtype,
                         int64_t heads, int64_t cells, const void *winner, const void *runner, const float *margins,
-                        float code_scale, float *gm, void *stream) {
+                        float code_scale, float *gm, const void *grad_absmax, void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
   if (items == 0) return tropnn_b200::clear_error();
   TB_CHECK(tropnn_b200::trop_gm_sm100_impl(g_split, items, code_dim, code, param_dtype, heads, cells,
                                            static_cast<const uint8_t *>(winner), static_cast<const uint8_t *>(runner),
-                                           margins, code_scale, gm, tropnn_b200::as_stream(stream)));
+                                           margins, code_scale, gm, static_cast<const uint32_t *>(grad_absmax),
+                                           tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 
 int tropnn_b200_trop_router_term(const float *grad_hidden, int64_t items, int64_t code_dim, const void *router_weight_t,
                                  int param_dtype, int64_t heads, int64_t cells, const void *winner, const void *runner,
-                                 const float *gm, float *grad_latent, void *stream) {
+                                 const float *gm, const void *grad_absmax, float *grad_latent, void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
   if (items == 0) return tropnn_b200::clear_error();
   TB_CHECK(tropnn_b200::trop_hidden_sm100_impl(grad_hidden, TROPNN_B200_F32, items, code_dim, router_weight_t,
-                                               param_dtype, heads, cells, winner, runner, gm, 1.0f, 2, grad_latent,
+                                               param_dtype, heads, cells, winner, runner, gm, 1.0f, 2,
+                                               static_cast<const uint32_t *>(grad_absmax), grad_latent,
                                                tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 
 int tropnn_b200_trop_param_grad(int mode, const void *x_t, int64_t items, int64_t code_dim, int param_dtype,
                                 int64_t heads, int64_t cells, const void *winner, const void *runner,
-                                const float *values, float code_scale, void *grad, void *grad_bias, void *stream) {
+                                const float *values, float code_scale, void *grad, void *grad_bias,
+                                const void *grad_absmax, void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
   TB_CHECK(tropnn_b200::trop_param_grad_sm100_impl(mode, x_t, items, code_dim, param_dtype, heads, cells, winner,
                                                    runner, values, code_scale, grad, grad_bias,
+                                                   static_cast<const uint32_t *>(grad_absmax),
                                                    tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 
-int tropnn_b200_transpose_to_half(const void *x, int x_dtype, int64_t rows, int64_t cols, int dtype, void *out,
-                                  void *stream) {
+int tropnn_b200_transpose_to_half(const void *x, int x_dtype, int64_t rows, int64_t cols, int dtype,
+                                  const void *grad_absmax, void *out, void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
-  TB_CHECK(tropnn_b200::transpose_to_half_impl(x, x_dtype, rows, cols, dtype, out, tropnn_b200::as_stream(stream)));
+  TB_CHECK(tropnn_b200::transpose_to_half_impl(x, x_dtype, rows, cols, dtype, out,
+                                               static_cast<const uint32_t *>(grad_absmax),
+                                               tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 

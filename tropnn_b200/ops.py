@@ -421,21 +421,30 @@ def _trop_backward_tensor_cores(ctx, g, z, weight, code, winner, runner, margins
     gm from <g, c_r - c_w> (split-f32 g against the code table, route-picking epilogue),
     grad_latent's router term as a one-hot GEMM with +-gm weights against router_weight^T,
     and the code / router gradients as P^T X with X = g^T or z^T (one tile of 128 cells per
-    CTA, the weighted one-hot P^T assembled in TMEM)."""
+    CTA, the weighted one-hot P^T assembled in TMEM). grad_hidden and gm are scaled by a power
+    of two fitted to grad_hidden's maximum (tropnn_b200_absmax_f32) before their rounding to the
+    parameter dtype, and the results are scaled back: with f16 parameters, gradients below f16's
+    range keep the precision the reference's f32 products give them."""
     batch, steps, code_dim, heads, cells = ctx.shape
     items = batch * steps
     dev = g.device
     training = ctx.training
     pdt = nat.float_code(weight.dtype)
     hk = heads * cells
+    if g.data_ptr() % 16:
+        g = g.clone()
+    gmax = torch.zeros(1, device=dev, dtype=torch.int32)
+    _launch("absmax", lib.tropnn_b200_absmax_f32, g.data_ptr(), g.numel(), gmax.data_ptr(), stream)
     gm = None
     if training:
         g_split = torch.empty((items, 2 * code_dim), device=dev, dtype=weight.dtype)
-        _launch("split_half", lib.tropnn_b200_split_half, g.data_ptr(), items, code_dim, pdt, g_split.data_ptr(), stream)
+        _launch("split_half", lib.tropnn_b200_split_half, g.data_ptr(), items, code_dim, pdt, gmax.data_ptr(),
+                g_split.data_ptr(), stream)
         gm = torch.empty((items, heads), device=dev, dtype=torch.float32)
         _launch(
             "trop_gm", lib.tropnn_b200_trop_gm, g_split.data_ptr(), items, code_dim, code.data_ptr(), pdt, heads, cells,
-            winner.data_ptr(), runner.data_ptr(), margins.data_ptr(), ctx.code_scale, gm.data_ptr(), stream,
+            winner.data_ptr(), runner.data_ptr(), margins.data_ptr(), ctx.code_scale, gm.data_ptr(), gmax.data_ptr(),
+            stream,
         )
         w_t = torch.empty((code_dim, hk), device=dev, dtype=weight.dtype)
         _launch("trop_code_transpose", lib.tropnn_b200_trop_code_transpose, weight.data_ptr(), pdt, heads, cells, code_dim,
@@ -443,7 +452,7 @@ def _trop_backward_tensor_cores(ctx, g, z, weight, code, winner, runner, margins
         grad_z = torch.empty((items, code_dim), device=dev, dtype=torch.float32)
         _launch(
             "trop_router_term", lib.tropnn_b200_trop_router_term, g.data_ptr(), items, code_dim, w_t.data_ptr(), pdt, heads,
-            cells, winner.data_ptr(), runner.data_ptr(), gm.data_ptr(), grad_z.data_ptr(), stream,
+            cells, winner.data_ptr(), runner.data_ptr(), gm.data_ptr(), gmax.data_ptr(), grad_z.data_ptr(), stream,
         )
     else:
         grad_z = g
@@ -451,22 +460,23 @@ def _trop_backward_tensor_cores(ctx, g, z, weight, code, winner, runner, margins
     if ctx.needs_input_grad[3]:
         g_t = torch.empty((code_dim, items), device=dev, dtype=weight.dtype)
         _launch("transpose_to_half", lib.tropnn_b200_transpose_to_half, g.data_ptr(), nat.F32, items, code_dim, pdt,
-                g_t.data_ptr(), stream)
+                gmax.data_ptr(), g_t.data_ptr(), stream)
         grad_c = torch.empty_like(code)
         _launch(
             "trop_code_grad", lib.tropnn_b200_trop_param_grad, 1 if training else 0, g_t.data_ptr(), items, code_dim, pdt,
             heads, cells, winner.data_ptr(), nat.ptr(runner), margins.data_ptr() if training else None, ctx.code_scale,
-            grad_c.data_ptr(), None, stream,
+            grad_c.data_ptr(), None, gmax.data_ptr(), stream,
         )
     if training and (ctx.needs_input_grad[1] or ctx.needs_input_grad[2]):
         z_t = torch.empty((code_dim, items), device=dev, dtype=weight.dtype)
         _launch("transpose_to_half", lib.tropnn_b200_transpose_to_half, z.data_ptr(), nat.float_code(z.dtype), items,
-                code_dim, pdt, z_t.data_ptr(), stream)
+                code_dim, pdt, None, z_t.data_ptr(), stream)
         grad_w = torch.empty_like(weight)
         grad_b = torch.empty((heads, cells), device=dev, dtype=weight.dtype)
         _launch(
             "trop_router_grad", lib.tropnn_b200_trop_param_grad, 2, z_t.data_ptr(), items, code_dim, pdt, heads, cells,
-            winner.data_ptr(), runner.data_ptr(), gm.data_ptr(), 1.0, grad_w.data_ptr(), grad_b.data_ptr(), stream,
+            winner.data_ptr(), runner.data_ptr(), gm.data_ptr(), 1.0, grad_w.data_ptr(), grad_b.data_ptr(),
+            gmax.data_ptr(), stream,
         )
     if not ctx.needs_input_grad[1]:
         grad_w = None
@@ -833,7 +843,8 @@ class _LinearF32OutFunction(torch.autograd.Function):
         stream = nat.stream_handle(dev)
         lib = nat.load()
         split = torch.empty((rows, 2 * in_features), device=dev, dtype=w.dtype)
-        _launch("split_half", lib.tropnn_b200_split_half, h.data_ptr(), rows, in_features, dcode, split.data_ptr(), stream)
+        _launch("split_half", lib.tropnn_b200_split_half, h.data_ptr(), rows, in_features, dcode, None, split.data_ptr(),
+                stream)
         b32 = None if bias is None else bias.to(torch.float32).contiguous()
         out = torch.empty((rows, out_features), device=dev, dtype=torch.float32)
         _launch(
