@@ -46,6 +46,10 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr int kEpiCols = kBN * 4 / kEpiWarps;  // 128
 constexpr int kStageOutBytes = 32 * 128;       // one warp's 32 x 32 f32 store tile
+// Shared memory of the epilogue's store staging: the f32 output map (K = 0) only; the
+// route-margin gradient (K > 0) gives it to the weight ring (3 stages instead of 2 with a
+// 128 KiB left block).
+__host__ __device__ constexpr size_t out_stage_bytes(int K) { return K == 0 ? size_t(kEpiWarps) * kStageOutBytes : 0; }
 constexpr int kTmemCols = 2 * kBN;
 constexpr int kMaxABlocks = 8;                 // slices * K <= 512
 constexpr size_t kSmemLimit = 227 * 1024;
@@ -82,7 +86,46 @@ struct GmArgs {
   int heads;
   float code_scale;
   const uint32_t *absmax;  // the g split was scaled by pow2_grad_scale(*absmax) (NULL: not scaled)
+  int vec;                 // routes / margins / gm rows allow the per-thread vector accesses below
 };
+
+// code_scale * U'(m), U'(m) = -0.5 sign(m) / (1+|m|)^2 (layers/tropical_exact.py:204-237).
+__device__ __forceinline__ float margin_factor(float code_scale, float m) {
+  const float den = __fadd_rn(1.f, fabsf(m));
+  const float sgn = (m > 0.f) ? 1.f : ((m < 0.f) ? -1.f : 0.f);
+  return __fmul_rn(code_scale, __fdiv_rn(__fmul_rn(-0.5f, sgn), __fmul_rn(den, den)));
+}
+
+// The kN consecutive bytes / floats of one row starting at `o` (a multiple of kN), by vector
+// loads when `vec`, else element by element (entries at or past `valid` read as 0xFF / 0).
+template <int kN>
+__device__ __forceinline__ void load_bytes(const uint8_t *p, int64_t o, bool vec, int valid, uint8_t (&out)[kN]) {
+  if (vec && valid >= kN) {
+    if constexpr (kN == 16) {
+      *reinterpret_cast<uint4 *>(out) = __ldg(reinterpret_cast<const uint4 *>(p + o));
+    } else if constexpr (kN == 8) {
+      *reinterpret_cast<uint2 *>(out) = __ldg(reinterpret_cast<const uint2 *>(p + o));
+    } else {
+      *reinterpret_cast<uint32_t *>(out) = __ldg(reinterpret_cast<const uint32_t *>(p + o));
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kN; ++i) out[i] = i < valid ? __ldg(p + o + i) : uint8_t(0xFF);
+  }
+}
+template <int kN>
+__device__ __forceinline__ void load_floats(const float *p, int64_t o, bool vec, int valid, float (&out)[kN]) {
+#pragma unroll
+  for (int i = 0; i < kN; i += 4) {
+    if (vec && valid >= kN) {
+      const float4 q = __ldg(reinterpret_cast<const float4 *>(p + o + i));
+      out[i] = q.x, out[i + 1] = q.y, out[i + 2] = q.z, out[i + 3] = q.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) out[i + j] = i + j < valid ? __ldg(p + o + i + j) : 0.f;
+    }
+  }
+}
 
 template <typename PT, int K>  // K = 0: f32 output map; K = cells: route-margin gradient
 __global__ void __launch_bounds__(kThreads, 1) linear_f32out_kernel(
@@ -97,8 +140,8 @@ __global__ void __launch_bounds__(kThreads, 1) linear_f32out_kernel(
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *a_smem = smem;                               // a_blocks x [128 rows x 128 B]
   uint8_t *b_smem = a_smem + a_blocks * kTileBytesA;    // stages x [256 rows x 128 B]
-  uint8_t *o_smem = b_smem + stages * kTileBytesB;      // kEpiWarps x [32 rows x 128 B]
-  Barriers *bs = reinterpret_cast<Barriers *>(o_smem + kEpiWarps * kStageOutBytes);
+  uint8_t *o_smem = b_smem + stages * kTileBytesB;      // kEpiWarps x [32 rows x 128 B] (f32 output only)
+  Barriers *bs = reinterpret_cast<Barriers *>(o_smem + out_stage_bytes(K));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -239,6 +282,66 @@ __global__ void __launch_bounds__(kThreads, 1) linear_f32out_kernel(
       const int b = t & 1;
       const uint32_t use = t >> 1;
       const int col0 = tile * kBN + group * kEpiCols;
+      if constexpr (K >= 8) {
+        // Route-margin gradient, kEpiCols / K heads of this thread's row per unit: their routes
+        // and margin factors are loaded (vector loads) and computed before the accumulator is
+        // ready, so the loads overlap the MMAs; gm leaves in one vector store per 4 heads.
+        constexpr int kHpt = kEpiCols / K;
+        const int64_t row = rb * kBM + quarter * 32 + lane;
+        const int hb = col0 / K;
+        const int valid = row < gmx.rows ? max(0, min(kHpt, gmx.heads - hb)) : 0;
+        const int64_t o = row * gmx.heads + hb;
+        uint8_t wq[kHpt], rq[kHpt];
+        float fq[kHpt];
+        load_bytes<kHpt>(gmx.winner, o, gmx.vec != 0, valid, wq);
+        load_bytes<kHpt>(gmx.runner, o, gmx.vec != 0, valid, rq);
+        load_floats<kHpt>(gmx.margins, o, gmx.vec != 0, valid, fq);
+#pragma unroll
+        for (int i = 0; i < kHpt; ++i) fq[i] = __fmul_rn(margin_factor(gmx.code_scale, fq[i]), gm_unscale);
+        if (warp == 2 && lane == 0) bs->epi_go[b] = wait_bar(&bs->tmem_full[b], use & 1u, bs) ? 1 : 0;
+        named_sync(1, kEpiWarps * 32);
+        if (*reinterpret_cast<volatile int *>(&bs->epi_go[b]) == 0) break;
+        __syncwarp();
+        tmem_fence_after();
+        const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(b * kBN + group * kEpiCols);
+        float gq[kHpt];
+#pragma unroll
+        for (int c = 0; c < kEpiCols; c += 32) {
+          float v[32];
+          tmem_ld32(taddr + uint32_t(c), v);
+          tmem_wait_ld();
+          reg_fence(v);
+          if (c + 32 == kEpiCols) {
+            tmem_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bs->tmem_empty[b]);
+          }
+#pragma unroll
+          for (int hh = 0; hh < 32 / K; ++hh) {
+            const int i = c / K + hh;
+            // Bitwise pick (one cell matches): masks, not selects, so that the accumulator
+            // values stay in registers.
+            uint32_t bw = 0u, br = 0u;
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+              const uint32_t x = __float_as_uint(v[hh * K + k]);
+              bw |= x & (0u - uint32_t(wq[i] == uint32_t(k)));
+              br |= x & (0u - uint32_t(rq[i] == uint32_t(k)));
+            }
+            gq[i] = __fmul_rn(__fsub_rn(__uint_as_float(br), __uint_as_float(bw)), fq[i]);
+          }
+        }
+        if (valid == kHpt && gmx.vec != 0) {
+#pragma unroll
+          for (int i = 0; i < kHpt; i += 4)
+            *reinterpret_cast<float4 *>(gmx.gm + o + i) = make_float4(gq[i], gq[i + 1], gq[i + 2], gq[i + 3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < kHpt; ++i)
+            if (i < valid) gmx.gm[o + i] = gq[i];
+        }
+        continue;
+      }
       // One thread polls; the verdict travels through a two-slot flag (slot t&1 is
       // rewritten two units later, after every epilogue warp has read it).
       if (warp == 2 && lane == 0) bs->epi_go[b] = wait_bar(&bs->tmem_full[b], use & 1u, bs) ? 1 : 0;
@@ -410,12 +513,12 @@ __global__ void __launch_bounds__(256) absmax_kernel(const float *__restrict__ x
   }
 }
 
-size_t linear_fixed_smem(int a_blocks) {
-  return 1024 + size_t(a_blocks) * kTileBytesA + size_t(kEpiWarps) * kStageOutBytes + sizeof(Barriers);
+size_t linear_fixed_smem(int a_blocks, int K) {
+  return 1024 + size_t(a_blocks) * kTileBytesA + out_stage_bytes(K) + sizeof(Barriers);
 }
 
-int linear_stages(int a_blocks) {
-  const size_t fixed = linear_fixed_smem(a_blocks);
+int linear_stages(int a_blocks, int K) {
+  const size_t fixed = linear_fixed_smem(a_blocks, K);
   if (fixed >= kSmemLimit) return 0;
   const int s = static_cast<int>(std::min<size_t>(kMaxStages, (kSmemLimit - fixed) / kTileBytesB));
   return s >= kMinStages ? s : 0;
@@ -428,8 +531,8 @@ int launch_linear(const void *a, int64_t rows, int slices, const void *w, int ou
       std::is_same<PT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int b_kblocks = in_features / kBK;
   const int a_blocks = slices * b_kblocks;
-  const int stages = linear_stages(a_blocks);
-  const size_t smem = linear_fixed_smem(a_blocks) + size_t(stages) * kTileBytesB;
+  const int stages = linear_stages(a_blocks, K);
+  const size_t smem = linear_fixed_smem(a_blocks, K) + size_t(stages) * kTileBytesB;
   CUtensorMap map_a, map_w, map_out;
   TB_CHECK(make_map_k64(&map_a, a, dt, int64_t(slices) * in_features, rows, kBM));
   TB_CHECK(make_map_k64(&map_w, w, dt, in_features, out_features, kBoxRows));
@@ -455,7 +558,7 @@ int launch_linear(const void *a, int64_t rows, int slices, const void *w, int ou
 bool linear_f32out_supported(int64_t rows, int64_t slices, int64_t out_features, int64_t in_features, int dtype) {
   return (dtype == TROPNN_B200_F16 || dtype == TROPNN_B200_BF16) && (slices == 1 || slices == 2) && rows >= 1 &&
          rows <= (int64_t(1) << 31) - 1024 && in_features % kBK == 0 && in_features >= kBK &&
-         slices * (in_features / kBK) <= kMaxABlocks && linear_stages(static_cast<int>(slices * in_features / kBK)) > 0 &&
+         slices * (in_features / kBK) <= kMaxABlocks && linear_stages(static_cast<int>(slices * in_features / kBK), 0) > 0 &&
          out_features >= 1 && out_features % 4 == 0 && out_features <= (int64_t(1) << 30);
 }
 
@@ -485,7 +588,12 @@ int trop_gm_sm100_impl(const void *g_split, int64_t rows, int64_t code_dim, cons
              TROPNN_B200_ERR_INVALID, "trop_gm_sm100: unsupported shape rows=%lld code_dim=%lld heads=%lld cells=%lld",
              (long long)rows, (long long)code_dim, (long long)heads, (long long)cells);
   TB_REQUIRE(g_split && code && winner && runner && margins && gm, TROPNN_B200_ERR_INVALID, "trop_gm_sm100: null pointer");
-  const GmArgs gmx{winner, runner, margins, gm, rows, static_cast<int>(heads), code_scale, absmax};
+  // Per-thread vector accesses of kEpiCols / cells consecutive heads (cells >= 8): whole
+  // vectors inside each row and 16-byte aligned bases.
+  const int64_t hpt = 128 / cells;
+  auto al16 = [](const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  const int vec = (cells >= 8 && heads % hpt == 0 && al16(winner) && al16(runner) && al16(margins) && al16(gm)) ? 1 : 0;
+  const GmArgs gmx{winner, runner, margins, gm, rows, static_cast<int>(heads), code_scale, absmax, vec};
   const int n = static_cast<int>(hk), k = static_cast<int>(code_dim);
   auto go = [&](auto pt_tag) -> int {
     using T = decltype(pt_tag);
