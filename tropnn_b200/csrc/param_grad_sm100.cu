@@ -410,11 +410,15 @@ __global__ void __cluster_dims__(1, kBiasSlices, 1) __launch_bounds__(kBiasWarps
   const int h = blockIdx.x * 32 + lane;
   const int64_t per = (rows + kBiasSlices - 1) / kBiasSlices;
   const int64_t n_begin = per * blockIdx.y, n_end = n_begin + per < rows ? n_begin + per : rows;
-  float acc[K];
+  // This thread's K partial sums live in its own shared-memory row (stride K + 1: no bank
+  // conflicts): each row adds gm to the winner's cell and subtracts it from the runner-up's,
+  // two read-modify-writes instead of K selects (the same sums, bit for bit: the other cells
+  // would only add 0).
+  float *mine = part + (warp * 32 + lane) * (K + 1);
 #pragma unroll
-  for (int k = 0; k < K; ++k) acc[k] = 0.f;
+  for (int k = 0; k < K; ++k) mine[k] = 0.f;
   if (h < H) {
-    constexpr int kUnroll = 4;
+    constexpr int kUnroll = 8;
     for (int64_t n = n_begin + warp; n < n_end; n += kUnroll * kBiasWarps) {
       uint32_t w[kUnroll], r[kUnroll];
       float v[kUnroll];
@@ -423,19 +427,19 @@ __global__ void __cluster_dims__(1, kBiasSlices, 1) __launch_bounds__(kBiasWarps
         const int64_t nu = n + int64_t(u) * kBiasWarps;
         const bool ok = nu < n_end;
         const int64_t o = (ok ? nu : n) * H + h;
-        w[u] = __ldg(winner + o);
-        r[u] = __ldg(runner + o);
+        // Routes come from this library's route kernel; clamped anyway so that a corrupt one
+        // cannot address outside the thread's row.
+        w[u] = min(uint32_t(__ldg(winner + o)), uint32_t(K - 1));
+        r[u] = min(uint32_t(__ldg(runner + o)), uint32_t(K - 1));
         v[u] = ok ? __ldg(gm + o) : 0.f;
       }
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u)
-#pragma unroll
-        for (int k = 0; k < K; ++k)
-          acc[k] = __fadd_rn(acc[k], __fsub_rn(w[u] == uint32_t(k) ? v[u] : 0.f, r[u] == uint32_t(k) ? v[u] : 0.f));
+      for (int u = 0; u < kUnroll; ++u) {
+        mine[w[u]] = __fadd_rn(mine[w[u]], __fsub_rn(v[u], 0.f));
+        mine[r[u]] = __fadd_rn(mine[r[u]], __fsub_rn(0.f, v[u]));
+      }
     }
   }
-#pragma unroll
-  for (int k = 0; k < K; ++k) part[(warp * 32 + lane) * (K + 1) + k] = acc[k];
   __syncthreads();
   for (int e = threadIdx.x; e < 32 * K; e += kBiasWarps * 32) {
     const int hl = e / K, k = e - hl * K;
