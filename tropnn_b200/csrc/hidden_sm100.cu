@@ -150,11 +150,40 @@ __device__ __forceinline__ void load_row32(const LT *__restrict__ p, float (&out
   }
 }
 
+// N consecutive route bytes / margins by vector loads (N a power of two; p aligned to N
+// bytes / N floats, at most 16 bytes per load).
+template <int N>
+__device__ __forceinline__ void load_vec(const uint8_t *p, uint8_t (&o)[N]) {
+  if constexpr (N >= 16) {
+#pragma unroll
+    for (int i = 0; i < N / 16; ++i) *reinterpret_cast<uint4 *>(o + 16 * i) = __ldg(reinterpret_cast<const uint4 *>(p) + i);
+  } else if constexpr (N == 8) {
+    *reinterpret_cast<uint2 *>(o) = __ldg(reinterpret_cast<const uint2 *>(p));
+  } else if constexpr (N == 4) {
+    *reinterpret_cast<uint32_t *>(o) = __ldg(reinterpret_cast<const uint32_t *>(p));
+  } else {
+    *reinterpret_cast<uint16_t *>(o) = __ldg(reinterpret_cast<const unsigned short *>(p));
+  }
+}
+template <int N>
+__device__ __forceinline__ void load_vec(const float *p, float (&o)[N]) {
+  if constexpr (N >= 4) {
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) {
+      const float4 q = __ldg(reinterpret_cast<const float4 *>(p) + i);
+      o[4 * i] = q.x, o[4 * i + 1] = q.y, o[4 * i + 2] = q.z, o[4 * i + 3] = q.w;
+    }
+  } else {
+    const float2 q = __ldg(reinterpret_cast<const float2 *>(p));
+    o[0] = q.x, o[1] = q.y;
+  }
+}
+
 template <typename PT, typename LT, int K, int MODE>
 __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
     const __grid_constant__ CUtensorMap map_ct, const LT *__restrict__ latent, const uint8_t *__restrict__ winner,
     const uint8_t *__restrict__ runner, const float *__restrict__ margins, float code_scale, int64_t rows, int H,
-    int D, int kblocks, int bstages, int64_t row_blocks, const uint32_t *__restrict__ absmax,
+    int D, int kblocks, int bstages, int64_t row_blocks, const uint32_t *__restrict__ absmax, int vec_routes,
     float *__restrict__ hidden) {
   static_assert(K >= 2 && K <= kBK && K % 2 == 0, "cells must be even and at most 64");
   constexpr int kHeadsPerBlock = kBK / K;
@@ -271,38 +300,72 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
     const int parity = (warp - 2) >> 2;
     const uint32_t lane_base = tmem_base + (uint32_t(quarter * 32) << 16) + kAColBase;
     bool ok = true;
+    // The route bytes (and margins) of the thread's row for one k item: the next item's are
+    // fetched while this one is built, with vector loads of the item's consecutive heads.
+    struct Raw {
+      uint8_t w[kHeadsPerBlock];
+      uint8_t r[kHeadsPerBlock];
+      float m[kHeadsPerBlock];
+    };
+    auto fetch = [&](int a, Raw &raw) {
+      const int64_t ii = a / kblocks;
+      const int kb = static_cast<int>(a - ii * kblocks);
+      const int64_t rb = blockIdx.x + ii * gridDim.x;
+      if (rb >= row_blocks) return;
+      const int64_t row = rb * kBM + quarter * 32 + lane;
+      const int h0 = kblock_at(kb) * kHeadsPerBlock;
+      const int valid = row < rows ? max(0, min(kHeadsPerBlock, H - h0)) : 0;
+      const int64_t o = (row < rows ? row : 0) * H + h0;
+      if (vec_routes && valid == kHeadsPerBlock) {
+        load_vec<kHeadsPerBlock>(winner + o, raw.w);
+        if constexpr (MODE != kOneHotEval) {
+          load_vec<kHeadsPerBlock>(runner + o, raw.r);
+          load_vec<kHeadsPerBlock>(margins + o, raw.m);
+        }
+      } else {
+#pragma unroll
+        for (int hh = 0; hh < kHeadsPerBlock; ++hh) {
+          raw.w[hh] = hh < valid ? __ldg(winner + o + hh) : uint8_t(0xFF);
+          if constexpr (MODE != kOneHotEval) {
+            raw.r[hh] = hh < valid ? __ldg(runner + o + hh) : uint8_t(0xFF);
+            raw.m[hh] = hh < valid ? __ldg(margins + o + hh) : 0.f;
+          }
+        }
+      }
+    };
+    // Prefetch only while both items fit the registers (up to 8 heads per item: cells >= 8).
+    constexpr bool kPrefetch = kHeadsPerBlock <= 8;
+    Raw nxt;
+    if constexpr (kPrefetch) fetch(parity, nxt);
     for (int ait = parity;; ait += 2) {
       const int64_t i = ait / kblocks;
-      const int kb = static_cast<int>(ait - i * kblocks);
       const int64_t rb = blockIdx.x + i * gridDim.x;
       if (rb >= row_blocks || !ok) break;
-      const int64_t row = rb * kBM + quarter * 32 + lane;
-      const bool live = row < rows;
-      const uint8_t *wrow = winner + (live ? row : 0) * H;
-      const uint8_t *rrow = MODE != kOneHotEval ? runner + (live ? row : 0) * H : nullptr;
-      const float *mrow = MODE != kOneHotEval ? margins + (live ? row : 0) * H : nullptr;
-      const int kbe = kblock_at(kb);
+      Raw cur;
+      if constexpr (kPrefetch) {
+        cur = nxt;
+        fetch(ait + 2, nxt);
+      } else {
+        fetch(ait, cur);
+      }
       {
         const int sa = ait % kAStages;
-        // Route bytes first, so their latency overlaps the wait for the slot.
         uint32_t wc[kHeadsPerBlock], rc[kHeadsPerBlock], vw[kHeadsPerBlock], vr[kHeadsPerBlock];
 #pragma unroll
         for (int hh = 0; hh < kHeadsPerBlock; ++hh) {
-          const int h = kbe * kHeadsPerBlock + hh;
-          wc[hh] = 0xFFu;
+          wc[hh] = cur.w[hh];
           rc[hh] = 0xFFu;
           vw[hh] = kOne;
           vr[hh] = 0u;
-          if (live && h < H) {
-            wc[hh] = __ldg(wrow + h);
+          if (wc[hh] != 0xFFu) {
             if constexpr (MODE == kOneHotMinFace) {
-              rc[hh] = __ldg(rrow + h);
-              const float alpha = __fdiv_rn(0.5f, __fadd_rn(1.f, fabsf(__ldg(mrow + h))));
+              rc[hh] = cur.r[hh];
+              const float alpha = __fdiv_rn(0.5f, __fadd_rn(1.f, fabsf(cur.m[hh])));
               vw[hh] = HalfBits<PT>::bits(__fsub_rn(1.f, alpha));
               vr[hh] = HalfBits<PT>::bits(alpha);
             } else if constexpr (MODE == kOneHotSigned) {
-              rc[hh] = __ldg(rrow + h);
-              const float gm = __fmul_rn(__ldg(mrow + h), gscale);
+              rc[hh] = cur.r[hh];
+              const float gm = __fmul_rn(cur.m[hh], gscale);
               vw[hh] = HalfBits<PT>::bits(gm);
               vr[hh] = HalfBits<PT>::bits(-gm);
             }
@@ -421,12 +484,16 @@ int launch_onehot(const void *latent, int64_t rows, int D, const void *code_t, i
   int sms = 0;
   TB_CHECK(sm_count(&sms));
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(row_blocks, sms));
+  // Vector loads of an item's 64 / K consecutive heads: whole vectors inside each row and
+  // 16-byte aligned route / margin arrays.
+  auto al16 = [](const void *p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  const int vec_routes = (H % (kBK / K) == 0 && al16(win) && al16(run) && al16(m)) ? 1 : 0;
   auto kernel = mode == kOneHotSigned   ? trop_hidden_onehot_kernel<PT, LT, K, kOneHotSigned>
                 : mode == kOneHotMinFace ? trop_hidden_onehot_kernel<PT, LT, K, kOneHotMinFace>
                                          : trop_hidden_onehot_kernel<PT, LT, K, kOneHotEval>;
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_hidden_sm100"));
   kernel<<<grid, kThreads, smem, stream>>>(map_ct, static_cast<const LT *>(latent), win, run, m, code_scale, rows, H, D,
-                                           kblocks, bst, row_blocks, absmax, hidden);
+                                           kblocks, bst, row_blocks, absmax, vec_routes, hidden);
   return check_launch("trop_hidden_sm100");
 }
 
