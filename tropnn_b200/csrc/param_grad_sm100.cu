@@ -52,9 +52,8 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAColBase = 256;
 constexpr size_t kSmemLimit = 227 * 1024;
 constexpr uint32_t kSleepHintNs = 1000000u;
-constexpr int kMaxHeadsPerTile = kBM / 2;                     // cells >= 2
-constexpr int kStageEntries = kBK * kMaxHeadsPerTile;          // (row, head) entries per staged k block
-constexpr int kStageBytes = kStageEntries * 8;                 // {w, r, -, -, vw bits, vr bits}
+constexpr int kPRowHalves = kBK + 8;                           // 64 samples + 16 bytes of padding
+constexpr int kStageBytes = kBM * kPRowHalves * 2;             // one parity's one-hot block
 
 enum Mode { kCodeEval = 0, kCodeTrain = 1, kRouter = 2 };
 
@@ -132,8 +131,8 @@ __global__ void __launch_bounds__(kThreads, 1) trop_param_grad_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *b_smem = smem;                                       // bstages x [D rows x 128 B]
-  uint2 *stage = reinterpret_cast<uint2 *>(b_smem + bstages * b_stage_bytes);  // 2 parities x kStageEntries
-  Barriers *bs = reinterpret_cast<Barriers *>(reinterpret_cast<uint8_t *>(stage) + 2 * kStageBytes);
+  uint8_t *stage = b_smem + bstages * b_stage_bytes;  // 2 parities x [kBM][kPRowHalves] 16-bit weights
+  Barriers *bs = reinterpret_cast<Barriers *>(stage + 2 * kStageBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -227,10 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) trop_param_grad_kernel(
     const int parity = (warp - 2) >> 2;
     const int tid = (warp - 2 - 4 * parity) * 32 + lane;  // 0..127 within this parity's set
     const int L = quarter * 32 + lane;                     // TMEM lane = tile entry
-    const int hh = L / K;
-    const uint32_t cell = uint32_t(L % K);
     const uint32_t lane_base = tmem_base + (uint32_t(quarter * 32) << 16) + kAColBase;
-    uint2 *my_stage = stage + parity * kStageEntries;
     // Entries of a staged k block per builder thread; with few of them (cells >= 8) the
     // raw route bytes and weights of the set's next k block are loaded into registers while
     // the current one is built, so their latency leaves the critical path.
@@ -279,6 +275,27 @@ __global__ void __launch_bounds__(kThreads, 1) trop_param_grad_kernel(
       }
       return make_uint2(w | (r << 8), vw | (vr << 16));
     };
+    // One-hot block of the item, [128 entries][64 samples] 16-bit weights in shared memory
+    // (rows kPRowHalves apart: the padding spreads the row-per-lane 16-byte reads over the
+    // banks): the staging threads scatter each (sample, head)'s winner / runner-up weight into
+    // its entry's row, then every builder thread reads its own entry's row (the TMEM column
+    // layout: 32-bit word j = samples 2j, 2j+1) and clears it for the next item.
+    uint16_t *pm_rows = reinterpret_cast<uint16_t *>(stage) + parity * (kBM * kPRowHalves);
+    auto scatter = [&](int e, uint32_t w, uint32_t r, float mv) {
+      const uint2 v = encode(w, r, mv);
+      const int rr = e / kHeadsPerTile;
+      const int hl = e - rr * kHeadsPerTile;
+      if (w < uint32_t(K)) pm_rows[(hl * K + int(w)) * kPRowHalves + rr] = uint16_t(v.y & 0xFFFFu);
+      if constexpr (MODE != kCodeEval)
+        if (r < uint32_t(K) && r != w) pm_rows[(hl * K + int(r)) * kPRowHalves + rr] = uint16_t(v.y >> 16);
+    };
+    {
+      // This thread's row starts clear (the first named barrier below orders it before any
+      // scatter into it).
+      uint4 *my_row = reinterpret_cast<uint4 *>(pm_rows + L * kPRowHalves);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) my_row[c] = make_uint4(0u, 0u, 0u, 0u);
+    }
     if constexpr (kPrefetch) fetch(parity);
     for (int ait = parity;; ait += 2) {
       const int i = ait / kblocks;
@@ -287,12 +304,20 @@ __global__ void __launch_bounds__(kThreads, 1) trop_param_grad_kernel(
       if (tile >= tiles) break;
       const int h0 = tile * kHeadsPerTile;
       const int64_t n0 = int64_t(kb) * kBK;
-      // Stage [64 rows x kHeadsPerTile heads] of {winner, runner, vw bits, vr bits}; the
-      // previous k block of this parity has been consumed (its builders passed the named
-      // barrier below after reading it).
+      // One thread of the set waits for the TMEM slot; the verdict passes through a
+      // two-slot flag behind the named barrier, so all 128 builders of the set take the same
+      // branch (a warp leaving alone would strand the others at the next named barrier).
+      // Slot (ait/2)&1 is rewritten two items later, after every builder of the set has
+      // passed this item's later named barriers and so has read it. The barrier also orders
+      // the previous item's row clears before this item's scatter.
+      if (tid == 0)
+        verdict[parity][(ait >> 1) & 1] =
+            wait_bar_sleep(&bs->a_empty[ait % kAStages], (uint32_t(ait / kAStages) & 1u) ^ 1u, bs) ? 1 : 0;
+      named_sync(2 + parity, 128);
+      if (*reinterpret_cast<volatile int *>(&verdict[parity][(ait >> 1) & 1]) == 0) break;
       if constexpr (kPrefetch) {
 #pragma unroll
-        for (int q = 0; q < kPer; ++q) my_stage[tid + q * 128] = encode(pw[q], pr[q], pm[q]);
+        for (int q = 0; q < kPer; ++q) scatter(tid + q * 128, pw[q], pr[q], pm[q]);
         fetch(ait + 2);
       } else {
         for (int e = tid; e < kBK * kHeadsPerTile; e += 128) {
@@ -309,37 +334,24 @@ __global__ void __launch_bounds__(kThreads, 1) trop_param_grad_kernel(
               mv = __ldg(mvals + o);
             }
           }
-          my_stage[e] = encode(w, r, mv);
+          scatter(e, w, r, mv);
         }
       }
-      // One thread of the set waits for the TMEM slot; the verdict passes through a
-      // two-slot flag behind the named barrier, so all 128 builders of the set take the same
-      // branch (a warp leaving alone would strand the others at the next named barrier).
-      // Slot (ait/2)&1 is rewritten two items later, after every builder of the set has
-      // passed this item's second named barrier and so has read it.
-      if (tid == 0)
-        verdict[parity][(ait >> 1) & 1] =
-            wait_bar_sleep(&bs->a_empty[ait % kAStages], (uint32_t(ait / kAStages) & 1u) ^ 1u, bs) ? 1 : 0;
-      named_sync(2 + parity, 128);
-      if (*reinterpret_cast<volatile int *>(&verdict[parity][(ait >> 1) & 1]) == 0) break;
+      named_sync(2 + parity, 128);  // the block is complete
       tmem_fence_after();
       uint32_t reg[32];
+      uint4 *my_row = reinterpret_cast<uint4 *>(pm_rows + L * kPRowHalves);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        uint32_t lohi[2];
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const uint2 v = my_stage[(2 * j + q) * kHeadsPerTile + hh];
-          const uint32_t w = v.x & 0xFFu, r = (v.x >> 8) & 0xFFu;
-          lohi[q] = (w == cell ? (v.y & 0xFFFFu) : 0u) | (r == cell ? (v.y >> 16) : 0u);
-        }
-        reg[j] = lohi[0] | (lohi[1] << 16);
+      for (int c = 0; c < 8; ++c) {
+        const uint4 q = my_row[c];
+        reg[4 * c] = q.x, reg[4 * c + 1] = q.y, reg[4 * c + 2] = q.z, reg[4 * c + 3] = q.w;
       }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) my_row[c] = make_uint4(0u, 0u, 0u, 0u);
       tmem_st32(lane_base + uint32_t((ait % kAStages) * 32), reg);
       tmem_wait_st();
       tmem_fence_before();
-      // All 128 builders of this parity are done with the staged block before it is reused.
-      named_sync(2 + parity, 128);
+      __syncwarp();
       if (lane == 0) mbar_arrive(&bs->a_full[ait % kAStages]);
     }
   } else {
