@@ -116,7 +116,14 @@ def _overlap_rank(rank: int, world: int, port: int, queue) -> None:
             tdist.reduce_gradient_now(b.grad)  # as the Pairwise backward does for thresholds
         calls = allreduce_gradients([a, b])  # must skip b (already averaged), reduce a
         calls_again = allreduce_gradients([a, b])  # the mark is consumed: b is reduced now
-        queue.put((rank, untouched.numpy(), a.grad.numpy(), b.grad.numpy(), calls, calls_again))
+        # A gradient averaged inside its own kernel (the fused LUT-gradient path) is marked the
+        # same way and skipped once.
+        c = torch.nn.Parameter(torch.zeros(4))
+        c.grad = torch.full((4,), float(rank + 7))
+        tdist.mark_reduced(c.grad)
+        calls_marked = allreduce_gradients([c])
+        queue.put((rank, untouched.numpy(), a.grad.numpy(), b.grad.numpy(), calls, calls_again, c.grad.numpy(),
+                   calls_marked))
     finally:
         dist.destroy_process_group()
 
@@ -133,8 +140,24 @@ def test_overlapped_sync_marks_and_skips() -> None:
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for rank, untouched, ga, gb, calls, calls_again in results:
+    for rank, untouched, ga, gb, calls, calls_again, gc, calls_marked in results:
         assert np.array_equal(untouched, np.full(3, 10.0 * (rank + 1)))
         assert np.allclose(ga, np.full(5, 1.5))  # mean of 1 and 2, reduced once
         assert np.allclose(gb, np.full(3, 15.0))  # mean of 10 and 20 (second pass: mean of equal values)
         assert calls == 1 and calls_again == 1
+        assert calls_marked == 0 and np.array_equal(gc, np.full(4, float(rank + 7)))
+
+
+def test_fused_lut_context_sets_and_restores() -> None:
+    """fused_lut_allreduce publishes its peer set to the backward (fused_lut_peer) and restores
+    the previous one on exit, nested contexts included."""
+    from tropnn_b200 import distributed as tdist
+
+    assert tdist.fused_lut_peer() is None
+    outer, inner = object(), object()
+    with tdist.fused_lut_allreduce(outer):
+        assert tdist.fused_lut_peer() is outer
+        with tdist.fused_lut_allreduce(inner):
+            assert tdist.fused_lut_peer() is inner
+        assert tdist.fused_lut_peer() is outer
+    assert tdist.fused_lut_peer() is None
