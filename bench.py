@@ -569,7 +569,7 @@ def _run_b200_body(
                 else "single GPU"
             ),
             "l2": f"flushed between timed steps ({L2_FLUSH_BYTES >> 20} MiB write, untimed)",
-            "timing": "step (with the NCCL gradient all-reduce at N>1) captured as one CUDA graph and replayed",
+            "timing": "step (with the gradient all-reduce at N>1) captured as one CUDA graph and replayed",
         },
         "eager": {"value": round(rows_total * args.steps / (eager_ms / 1e3), 1), "unit": "rows/s",
                   "ms_per_step": round(eager_ms / args.steps, 4)},
