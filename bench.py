@@ -449,7 +449,7 @@ def _run_b200_body(
         eager_step()
     _barrier_sync(world, device)
 
-    # Timed region: the step, with the NCCL gradient all-reduce at N>1, captured once as a
+    # Timed region: the step, with the gradient all-reduce at N>1, captured once as a
     # CUDA graph (no host launch gaps) and replayed.
     def full_step() -> None:
         _step(layer, x, g, w)
