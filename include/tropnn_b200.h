@@ -184,14 +184,15 @@ TROPNN_B200_API int tropnn_b200_pairwise_ste_backward(const float *grad_out, int
                                       const int32_t *feat_start, const int32_t *feat_entries,
                                       float *grad_latent, float *gu, uint8_t *rstar, void *stream);
 
-/* Bytes of scratch tropnn_b200_pairwise_threshold_grad needs (row-block partial sums). */
+/* Bytes of scratch tropnn_b200_pairwise_threshold_grad needs: 0 (the stages meet in shared memory);
+ * the query and the workspace arguments stay so that callers need not change. */
 TROPNN_B200_API size_t tropnn_b200_pairwise_threshold_grad_workspace_size(int64_t items, int64_t tables,
                                                                           int64_t comparisons);
 
 /*
  * grad_thresholds[t,r] = -sum_n gu (min mode: rows whose r* == r), written in
- * grad_dtype. Two launches: per-row-block partial sums into `workspace`, then a
- * fixed-order sum of the partials (deterministic).
+ * grad_dtype. One launch of 8-CTA clusters: row-slice partial sums combined in a fixed order
+ * through distributed shared memory (deterministic). `workspace` may be NULL.
  */
 TROPNN_B200_API int tropnn_b200_pairwise_threshold_grad(const float *gu, const uint8_t *rstar, int64_t items,
                                         int64_t tables, int64_t comparisons, int use_min_margin_ste,

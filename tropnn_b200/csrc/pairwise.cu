@@ -12,6 +12,10 @@
 // Layout: latent f32 [N, in] row-major; anchors int64 [T, C, 2]; thresholds [T, C];
 // lut [T, 2^C, out] (f32/f16/bf16) row-major so a selected LUT row is one contiguous
 // `out`-wide vector; indices int64 [N, T]; margins f32 [N, T, C].
+#include <cooperative_groups.h>
+
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace tropnn_b200 {
@@ -361,75 +365,83 @@ int ste_by_width(bool use_min, const float *g, int64_t rows, int64_t out, float 
 }
 
 // ---------------------------------------------------------------------------
-// threshold gradient: fixed-order reduction over rows
+// threshold gradient: fixed-order reduction over rows, one launch
 // ---------------------------------------------------------------------------
-// Stage 1: CTA (table block of 32, row block) = 8 warps; lane <-> table (coalesced reads
-// of gu), warps stride over the block's rows, a fixed-shape combine across warps writes
-// partial[row_block][t][c]. Stage 2 sums the partials over row blocks in order. The
-// result is deterministic; rows are spread over many CTAs instead of one.
-constexpr int kThrRowsPerBlock = 64;
-constexpr int kThrMaxRowBlocks = 1024;
+// grad_thresholds[t,c] = -sum_n gu (min mode: rows whose r* == c; full mode: gu[n,t,c]). A
+// cluster of kThrSlices CTAs owns 32 tables (one per lane, so every warp load reads 32
+// consecutive (row, table) entries); CTA y of the cluster takes row slice y and its warps take
+// interleaved rows. Each thread keeps its C sums in its own shared-memory row (stride
+// kMaxComparisons + 1: no bank conflicts; min mode adds gu to cell r* only, the same sums as
+// adding 0 to the others). Warp partials are combined in warp order, slice partials in slice
+// order through distributed shared memory, so the result is deterministic, and nothing goes
+// through global memory between the two stages.
+constexpr int kThrSlices = 8, kThrWarps = 16, kThrStride = kMaxComparisons + 1;
 
-inline int64_t threshold_row_blocks(int64_t rows) {
-  return std::max<int64_t>(1, std::min<int64_t>(kThrMaxRowBlocks, ceil_div(rows, kThrRowsPerBlock)));
-}
-
-template <bool MIN>
-__global__ void __launch_bounds__(256) threshold_partial_kernel(const float *__restrict__ gu,
-                                                                const uint8_t *__restrict__ rstar, int64_t rows,
-                                                                int T, int C, float *__restrict__ partial) {
-  __shared__ float part[8][32][kMaxComparisons];
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
+template <bool MIN, typename OutT>
+__global__ void __cluster_dims__(1, kThrSlices, 1) __launch_bounds__(kThrWarps * 32, 1)
+    threshold_grad_kernel(const float *__restrict__ gu, const uint8_t *__restrict__ rstar, int64_t rows, int T,
+                          int C, OutT *__restrict__ grad) {
+  __shared__ float part[kThrWarps * 32 * kThrStride];
+  __shared__ float red[32 * kMaxComparisons];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t = blockIdx.x * 32 + lane;
-  const int64_t blocks = gridDim.y;
-  const int64_t per_block = (rows + blocks - 1) / blocks;
-  const int64_t r0 = int64_t(blockIdx.y) * per_block;
-  const int64_t r1 = min64(rows, r0 + per_block);
-  float acc[kMaxComparisons];
+  const int64_t per = (rows + kThrSlices - 1) / kThrSlices;
+  const int64_t n_begin = per * blockIdx.y, n_end = n_begin + per < rows ? n_begin + per : rows;
+  float *mine = part + (warp * 32 + lane) * kThrStride;
 #pragma unroll
-  for (int c = 0; c < kMaxComparisons; ++c) acc[c] = 0.f;
+  for (int c = 0; c < kMaxComparisons; ++c) mine[c] = 0.f;
   if (t < T) {
-#pragma unroll 4
-    for (int64_t n = r0 + warp; n < r1; n += 8) {
-      if (MIN) {
-        const float v = __ldg(gu + n * T + t);
-        const int r = __ldg(rstar + n * T + t);
-        // Every accumulator takes v or 0 (adding 0 changes nothing): written as selects, so
-        // that the compiler keeps acc in registers instead of indexing a local-memory copy
-        // by r*.
+    constexpr int kUnroll = 16;  // row loads in flight per warp
+    for (int64_t n = n_begin + warp; n < n_end; n += kUnroll * kThrWarps) {
+      if constexpr (MIN) {
+        float v[kUnroll];
+        uint32_t r[kUnroll];
 #pragma unroll
-        for (int c = 0; c < kMaxComparisons; ++c) acc[c] = __fadd_rn(acc[c], c == r ? v : 0.f);
+        for (int u = 0; u < kUnroll; ++u) {
+          const int64_t nu = n + int64_t(u) * kThrWarps;
+          const bool ok = nu < n_end;
+          const int64_t o = (ok ? nu : n) * T + t;
+          // r* comes from this library's STE kernel; clamped anyway so that a corrupt one
+          // cannot address outside the thread's row.
+          r[u] = min(uint32_t(__ldg(rstar + o)), uint32_t(C - 1));
+          v[u] = ok ? __ldg(gu + o) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) mine[r[u]] = __fadd_rn(mine[r[u]], v[u]);
       } else {
-#pragma unroll
-        for (int c = 0; c < kMaxComparisons; ++c)
-          if (c < C) acc[c] = __fadd_rn(acc[c], __ldg(gu + (n * T + t) * C + c));
+#pragma unroll 4
+        for (int u = 0; u < kUnroll; ++u) {
+          const int64_t nu = n + int64_t(u) * kThrWarps;
+          if (nu < n_end) {
+            const float *row = gu + (nu * T + t) * C;
+            for (int c = 0; c < C; ++c) mine[c] = __fadd_rn(mine[c], __ldg(row + c));
+          }
+        }
       }
     }
   }
-#pragma unroll
-  for (int c = 0; c < kMaxComparisons; ++c) part[warp][lane][c] = acc[c];
   __syncthreads();
-  for (int k = threadIdx.x; k < 32 * C; k += 256) {
-    const int l = k / C;
-    const int c = k - l * C;
-    const int tt = blockIdx.x * 32 + l;
-    if (tt < T) {
-      float s = 0.f;
-      for (int w = 0; w < 8; ++w) s = __fadd_rn(s, part[w][l][c]);
-      partial[(int64_t(blockIdx.y) * T + tt) * C + c] = s;
-    }
+  for (int e = threadIdx.x; e < 32 * C; e += kThrWarps * 32) {
+    const int l = e / C, c = e - l * C;
+    float sum = 0.f;
+    for (int w = 0; w < kThrWarps; ++w) sum = __fadd_rn(sum, part[(w * 32 + l) * kThrStride + c]);
+    red[e] = sum;
   }
-}
-
-template <typename OutT>
-__global__ void __launch_bounds__(256) threshold_combine_kernel(const float *__restrict__ partial, int blocks,
-                                                                int64_t TC, OutT *__restrict__ grad) {
-  const int64_t k = int64_t(blockIdx.x) * 256 + threadIdx.x;
-  if (k >= TC) return;
-  float s = 0.f;
-  for (int b = 0; b < blocks; ++b) s = __fadd_rn(s, __ldg(partial + int64_t(b) * TC + k));
-  grad[k] = from_f32<OutT>(-s);
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  const int share = (32 * C + kThrSlices - 1) / kThrSlices;
+  const int slice = static_cast<int>(cluster.block_rank());
+  for (int i = threadIdx.x; i < share; i += kThrWarps * 32) {
+    const int e = slice * share + i;
+    if (e >= 32 * C) break;
+    float sum = 0.f;
+    for (int y = 0; y < kThrSlices; ++y) sum = __fadd_rn(sum, cluster.map_shared_rank(red, y)[e]);
+    const int l = e / C, c = e - l * C;
+    const int tt = blockIdx.x * 32 + l;
+    if (tt < T) grad[int64_t(tt) * C + c] = from_f32<OutT>(-sum);
+  }
+  cluster.sync();  // the other CTAs' shared memory stays live until every read is done
 }
 
 // ---------------------------------------------------------------------------
@@ -564,8 +576,8 @@ int pairwise_ste_impl(const float *g, int64_t items, int64_t out, float out_scal
 }
 
 size_t threshold_grad_workspace(int64_t items, int64_t tables, int64_t comparisons) {
-  return WorkspaceCarver::align(sizeof(float) * size_t(threshold_row_blocks(items)) * size_t(tables) *
-                                size_t(comparisons));
+  (void)items, (void)tables, (void)comparisons;
+  return 0;  // one cluster launch; its stages meet in shared memory
 }
 
 int pairwise_threshold_grad_impl(const float *gu, const uint8_t *rs, int64_t items, int64_t tables,
@@ -576,32 +588,20 @@ int pairwise_threshold_grad_impl(const float *gu, const uint8_t *rs, int64_t ite
              dtype_name(grad_dtype));
   TB_REQUIRE(grad && (items == 0 || (gu && (rs || !use_min))), TROPNN_B200_ERR_INVALID,
              "pairwise_threshold_grad: null pointer");
-  const size_t need = threshold_grad_workspace(items, tables, comparisons);
-  TB_REQUIRE(ws != nullptr && ws_bytes >= need, TROPNN_B200_ERR_WORKSPACE,
-             "pairwise_threshold_grad: workspace of %zu bytes is smaller than the %zu bytes required", ws_bytes, need);
+  (void)ws, (void)ws_bytes;  // needs none (threshold_grad_workspace is 0); kept for the ABI
   const int T = static_cast<int>(tables), C = static_cast<int>(comparisons);
-  const int64_t row_blocks = threshold_row_blocks(items);
-  float *partial = static_cast<float *>(ws);
-  dim3 grid(static_cast<unsigned>(ceil_div(tables, 32)), static_cast<unsigned>(row_blocks));
-  if (use_min)
-    threshold_partial_kernel<true><<<grid, 256, 0, stream>>>(gu, rs, items, T, C, partial);
-  else
-    threshold_partial_kernel<false><<<grid, 256, 0, stream>>>(gu, rs, items, T, C, partial);
-  TB_CHECK(check_launch("pairwise_threshold_grad (partials)"));
-  const int64_t TC = tables * comparisons;
-  const unsigned cblocks = static_cast<unsigned>(ceil_div(TC, 256));
-  const int rb = static_cast<int>(row_blocks);
+  const dim3 grid(static_cast<unsigned>(ceil_div(tables, int64_t(32))), kThrSlices);
+  auto go = [&](auto *out) {
+    using OutT = std::remove_pointer_t<decltype(out)>;
+    if (use_min)
+      threshold_grad_kernel<true, OutT><<<grid, kThrWarps * 32, 0, stream>>>(gu, rs, items, T, C, out);
+    else
+      threshold_grad_kernel<false, OutT><<<grid, kThrWarps * 32, 0, stream>>>(gu, rs, items, T, C, out);
+  };
   switch (grad_dtype) {
-    case TROPNN_B200_F32:
-      threshold_combine_kernel<float><<<cblocks, 256, 0, stream>>>(partial, rb, TC, static_cast<float *>(grad));
-      break;
-    case TROPNN_B200_F16:
-      threshold_combine_kernel<__half><<<cblocks, 256, 0, stream>>>(partial, rb, TC, static_cast<__half *>(grad));
-      break;
-    default:
-      threshold_combine_kernel<__nv_bfloat16><<<cblocks, 256, 0, stream>>>(partial, rb, TC,
-                                                                           static_cast<__nv_bfloat16 *>(grad));
-      break;
+    case TROPNN_B200_F32: go(static_cast<float *>(grad)); break;
+    case TROPNN_B200_F16: go(static_cast<__half *>(grad)); break;
+    default: go(static_cast<__nv_bfloat16 *>(grad)); break;
   }
   return check_launch("pairwise_threshold_grad");
 }
