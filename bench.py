@@ -18,12 +18,14 @@ timed region, the copies of neighbouring steps overlapping the compute on two co
 streams (a prefetching input pipeline; every step's copies and L2 flush are inside the
 timed span); ``e2e_serial`` is the same with each step's copies and compute in sequence.
 ``roofline`` is the dominant kernel's algorithmic bytes per launch over
-its mean CUDA-event duration in the timed region. ``cpu_baseline`` times the numpy
-oracle of the reference's torch path on the host cores (rank 0, N=1 only).
+its mean CUDA-event duration in the timed region. ``cpu_baseline`` times the reference's
+CPU path (below) on the host cores (rank 0, N=1 only).
 
-``--impl reference`` runs the CPU arm: the oracle port of the reference's torch CPU
-path, on all host threads, on a bounded row sample per step; under torchrun only rank 0
-runs it.
+``--impl reference`` runs the CPU arm: the oracle port of the reference's CPU path, on all
+host threads, on a bounded row sample per step; under torchrun only rank 0 runs it. Both
+CPU legs time the reference's faster CPU path on the workload (``--cpu-impl auto``): the
+numpy oracle of its torch path, or for config 1 eval the C++ restatement of its Zig CPU
+inference kernels (``oracle/native_cpu.cpp``, ``backend="zig"``); ``--cpu-impl`` picks one.
 """
 
 from __future__ import annotations
@@ -72,6 +74,10 @@ class Workload:
     layer_kwargs: dict = field(default_factory=dict)
     description: str = ""
     cpu_sample_rows: int = 0  # rows per CPU-baseline step (0 = the full per-GPU batch)
+    # The reference's faster CPU path on this workload: "torch" (its default backend) or "zig"
+    # (its CPU inference kernels, eval only). Config 1 eval, 8 rows: Zig ~2x the torch path;
+    # config 5 eval: the torch path's BLAS scores beat the Zig per-cell dot products.
+    cpu_impl: str = "torch"
 
     @property
     def cpu_rows(self) -> int:
@@ -97,6 +103,7 @@ WORKLOADS = {
         "trop_cfg1", "trop", 256, 512, 8, False,
         layer_kwargs=dict(heads=32, cells=4, code_dim=32),
         description="BASELINE config 1: TropLinear(256->512, H32, K4, D32), fp32, eval forward, batch 8",
+        cpu_impl="zig",
     ),
     "trop_cfg3_layer1": Workload(
         "trop_cfg3_layer1", "trop", 784, 128, 512, True,
@@ -675,20 +682,46 @@ def _run_b200_body(
 # ---------------------------------------------------------------------------
 
 
-def _oracle_params(w: Workload) -> tuple[dict[str, np.ndarray], object]:
-    """Seeded parameters as numpy; half tensors are upcast once (exactly, as the reference's
-    ``.to(compute_dtype)`` does on every call) so the timed steps do not repeat it."""
+def _oracle_params(w: Workload, impl: str = "torch") -> tuple[dict[str, np.ndarray], object]:
+    """Seeded parameters as numpy. For the torch path half tensors are upcast once (exactly, as
+    the reference's ``.to(compute_dtype)`` does on every call) so the timed steps do not repeat
+    it; the Zig path reads f16 parameters as they are (its f16 kernels widen per element)."""
     layer = w.build()
     params = {}
     for k, v in layer.state_dict().items():
         a = v.detach().numpy()
-        params[k] = a.astype(np.float32) if a.dtype == np.float16 else a
+        params[k] = a.astype(np.float32) if a.dtype == np.float16 and impl == "torch" else a
     return params, layer
 
 
-def _oracle_step(w: Workload, params: dict, layer, x: np.ndarray, g: np.ndarray) -> None:
+def cpu_impl_for(w: Workload, requested: str) -> str:
+    """The CPU path a leg times: with "auto" the reference's faster path on the workload
+    (``Workload.cpu_impl``); "zig" (the C++ restatement of the Zig inference kernels) exists for
+    eval workloads only."""
+    if requested == "zig" and w.train:
+        raise SystemExit(f"--cpu-impl zig: {w.name} is a training workload; the Zig kernels are inference only")
+    if requested == "auto":
+        return "torch" if w.train else w.cpu_impl
+    return requested
+
+
+_CPU_IMPL_TEXT = {
+    "torch": "numpy oracle of the reference torch CPU path",
+    "zig": "C++ restatement of the reference's Zig CPU inference kernels, backend='zig'",
+}
+
+
+def _oracle_step(w: Workload, params: dict, layer, x: np.ndarray, g: np.ndarray, impl: str = "torch") -> None:
     import oracle
 
+    if impl == "zig":
+        from oracle import native
+
+        if w.kind == "pairwise":
+            native.pairwise_eval(x, params, output_scale=layer.output_scale, threads=1)
+        else:
+            native.trop_linear_eval(x, params, code_scale=layer.code_scale, threads=1)
+        return
     if w.kind == "pairwise":
         fwd = oracle.pairwise_forward(x, params["anchors"], params["thresholds"], params["lut"], output_scale=layer.output_scale)
         if w.train:
@@ -705,18 +738,23 @@ def _oracle_step(w: Workload, params: dict, layer, x: np.ndarray, g: np.ndarray)
 _POOL_STATE: dict = {}
 
 
-def _pool_init(workload: str, sample_rows: int, workers: int) -> None:
-    """Spawned CPU worker: one BLAS thread, its own seeded parameters and row chunk."""
+def _pool_init(workload: str, sample_rows: int, workers: int, impl: str = "torch") -> None:
+    """Spawned CPU worker: one BLAS thread (one native thread), its own seeded parameters and
+    row chunk."""
     from threadpoolctl import threadpool_limits
 
     torch.set_num_threads(1)
     _POOL_STATE["limits"] = threadpool_limits(limits=1)
     w = WORKLOADS[workload]
-    params, layer = _oracle_params(w)
+    if impl == "zig":
+        from oracle import native
+
+        native.load()
+    params, layer = _oracle_params(w, impl)
     gen = np.random.default_rng(7)
     x = gen.standard_normal((sample_rows, w.in_features), dtype=np.float32)
     g = gen.standard_normal((sample_rows, w.out_features), dtype=np.float32)
-    _POOL_STATE.update(w=w, params=params, layer=layer, x=x, g=g,
+    _POOL_STATE.update(w=w, params=params, layer=layer, x=x, g=g, impl=impl,
                        chunks=[c for c in np.array_split(np.arange(sample_rows), workers) if c.size])
 
 
@@ -725,19 +763,23 @@ def _pool_task(i: int) -> int:
     chunks = s["chunks"]
     if i < len(chunks):
         c = chunks[i]
-        _oracle_step(s["w"], s["params"], s["layer"], s["x"][c], s["g"][c])
+        _oracle_step(s["w"], s["params"], s["layer"], s["x"][c], s["g"][c], s["impl"])
     return i
 
 
 def time_cpu(w: Workload, sample_rows: int, workers: int, *, reps: int | None = None, budget_s: float = 10.0,
-             warmup: int = 1) -> dict:
+             warmup: int = 1, impl: str = "torch") -> dict:
     """rows/s of the oracle on ``sample_rows`` rows per step, the rows split over ``workers``
     spawn-started processes (one core each). Wall time of ``reps`` steps (or of as many
     steps as fit in ``budget_s``) after ``warmup`` steps."""
     import multiprocessing
 
     ctx = multiprocessing.get_context("spawn")
-    with ctx.Pool(workers, initializer=_pool_init, initargs=(w.name, sample_rows, workers)) as pool:
+    if impl == "zig":
+        from oracle import native
+
+        native.build()  # before the workers start: they only load it
+    with ctx.Pool(workers, initializer=_pool_init, initargs=(w.name, sample_rows, workers, impl)) as pool:
         for _ in range(max(1, warmup)):
             pool.map(_pool_task, range(workers), chunksize=1)
         done = 0
@@ -749,16 +791,16 @@ def time_cpu(w: Workload, sample_rows: int, workers: int, *, reps: int | None = 
     return {"rows_per_s": sample_rows * done / dt, "seconds": dt, "steps": done}
 
 
-def cpu_baseline(w: Workload, budget_s: float) -> dict:
+def cpu_baseline(w: Workload, budget_s: float, impl: str = "torch") -> dict:
     workers = os.cpu_count() or 1
     sample = w.cpu_rows
-    res = time_cpu(w, sample, workers, budget_s=budget_s, warmup=2)
+    res = time_cpu(w, sample, workers, budget_s=budget_s, warmup=2, impl=impl)
     return {
         "value": round(res["rows_per_s"], 1),
         "unit": "rows/s",
         "cores": workers,
         "kind": "port",
-        "sample": f"{res['steps']} steps x {sample} rows of {w.name} (numpy oracle of the reference torch CPU path), "
+        "sample": f"{res['steps']} steps x {sample} rows of {w.name} ({_CPU_IMPL_TEXT[impl]}), "
         f"{res['seconds']:.1f} s over {workers} single-threaded processes",
     }
 
@@ -769,7 +811,8 @@ def run_reference(args: argparse.Namespace, w: Workload) -> dict | None:
         return None
     threads = os.cpu_count() or 1
     sample = w.cpu_rows
-    res = time_cpu(w, sample, threads, reps=args.steps, warmup=args.warmup)
+    impl = cpu_impl_for(w, args.cpu_impl)
+    res = time_cpu(w, sample, threads, reps=args.steps, warmup=args.warmup, impl=impl)
     value = res["rows_per_s"]
     return {
         "metric": "TropLinear/PairwiseLinear rows/s fwd+bwd, 1-8 B200; % of HBM/TC roofline",
@@ -791,7 +834,7 @@ def run_reference(args: argparse.Namespace, w: Workload) -> dict | None:
             "unit": "rows/s",
             "cores": threads,
             "kind": "port",
-            "sample": f"{args.steps} steps x {sample} rows (numpy oracle of the reference torch CPU path, "
+            "sample": f"{args.steps} steps x {sample} rows ({_CPU_IMPL_TEXT[impl]}, "
             f"{threads} single-threaded processes)",
         },
         "e2e": {"value": round(value, 1), "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -807,6 +850,12 @@ def main(argv: list[str] | None = None) -> int:
     parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
     parser.add_argument("--cpu-budget-s", type=float, default=10.0, help="seconds of CPU-baseline timing (rank 0, N=1)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument(
+        "--cpu-impl", choices=["auto", "torch", "zig"], default="auto",
+        help="CPU path of the cpu_baseline leg and the reference arm: torch = numpy oracle of the reference "
+        "torch path; zig = C++ restatement of its Zig inference kernels (eval workloads only); auto = the "
+        "reference's faster CPU path on the workload (zig for config 1, torch otherwise)",
+    )
     parser.add_argument("--rows", type=int, default=0, help="override the per-GPU row count (profiling runs)")
     parser.add_argument(
         "--fuse-lut-allreduce", type=int, choices=[0, 1], default=0,
@@ -835,7 +884,7 @@ def main(argv: list[str] | None = None) -> int:
     else:
         line = run_b200(args, w)
         if line is not None and world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(w, args.cpu_budget_s)
+            line["cpu_baseline"] = cpu_baseline(w, args.cpu_budget_s, cpu_impl_for(w, args.cpu_impl))
     if line is not None:
         print(json.dumps(line), flush=True)
     return 0
