@@ -65,7 +65,7 @@ L2_FLUSH_BYTES = 256 * 1024 * 1024
 @dataclass
 class Workload:
     name: str
-    kind: str  # "pairwise" | "trop"
+    kind: str  # "pairwise" | "trop" | "trop_clf" | "pair_clf" (the two-layer classifiers)
     in_features: int
     out_features: int
     rows_per_gpu: int
@@ -78,14 +78,25 @@ class Workload:
     # (its CPU inference kernels, eval only). Config 1 eval, 8 rows: Zig ~2x the torch path;
     # config 5 eval: the torch path's BLAS scores beat the Zig per-cell dot products.
     cpu_impl: str = "torch"
+    hidden: int = 0  # classifiers: width of the hidden layer
 
     @property
     def cpu_rows(self) -> int:
         return self.cpu_sample_rows or self.rows_per_gpu
 
+    @property
+    def classifier(self) -> bool:
+        return self.kind in ("trop_clf", "pair_clf")
+
     def build(self):
         import tropnn_b200
 
+        if self.classifier:
+            # examples/emnist.py:121-175: routed layers in_features -> hidden -> out_features,
+            # seeds seed + index, no activation between them.
+            cls = tropnn_b200.TropLinear if self.kind == "trop_clf" else tropnn_b200.PairwiseLinear
+            dims = [self.in_features, self.hidden, self.out_features]
+            return _Classifier([cls(a, b, seed=i, **self.layer_kwargs) for i, (a, b) in enumerate(zip(dims[:-1], dims[1:]))])
         cls = tropnn_b200.PairwiseLinear if self.kind == "pairwise" else tropnn_b200.TropLinear
         layer = cls(self.in_features, self.out_features, seed=0, **self.layer_kwargs)
         if self.dtype == "float16":
@@ -93,11 +104,44 @@ class Workload:
         return layer
 
 
+class _Classifier(torch.nn.Module):
+    """The reference example's routed classifier (examples/emnist.py:121-175): 2-D input lifted
+    to one step, the routed layers applied in order, the step axis dropped again."""
+
+    def __init__(self, layers: list) -> None:
+        super().__init__()
+        self.layers = torch.nn.ModuleList(layers)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.ndim == 2:
+            x = x.unsqueeze(1)
+        for layer in self.layers:
+            x = layer(x)
+        return x.squeeze(1)
+
+
 WORKLOADS = {
     "pairwise_cfg2": Workload(
         "pairwise_cfg2", "pairwise", 256, 512, 4096, True,
         layer_kwargs=dict(tables=16, comparisons=6, surrogate="fast_sigmoid_odd", use_min_margin_ste=True),
         description="BASELINE config 2: PairwiseLinear(256->512, tables=16, comparisons=6), fp32, fwd + STE bwd, batch 4096",
+    ),
+    "pairwise_cfg2_b8": Workload(
+        "pairwise_cfg2_b8", "pairwise", 256, 512, 8, True,
+        layer_kwargs=dict(tables=16, comparisons=6, surrogate="fast_sigmoid_odd", use_min_margin_ste=True),
+        description="BASELINE config 2 at batch 8: PairwiseLinear(256->512, tables=16, comparisons=6), fp32, fwd + STE bwd",
+    ),
+    "trop_cfg3_clf": Workload(
+        "trop_cfg3_clf", "trop_clf", 784, 10, 512, True, hidden=128,
+        layer_kwargs=dict(heads=256, cells=16, code_dim=64),
+        description="BASELINE config 3: TropLinear classifier 784->128->10 (H256, K16, D64), fp32, one train step "
+        "(fwd, cross-entropy, min-face bwd, Adam lr 1e-3), batch 512, x ~ U[0,1], labels ~ U{0..9}",
+    ),
+    "pair_cfg4_clf": Workload(
+        "pair_cfg4_clf", "pair_clf", 784, 10, 512, True, hidden=128,
+        layer_kwargs=dict(tables=136, comparisons=6),
+        description="BASELINE config 4: PairwiseLinear classifier 784->128->10 (T136, C6), fp32, one train step "
+        "(fwd, cross-entropy, STE/LUT-grad bwd, Adam lr 1e-3), batch 512, x ~ U[0,1], labels ~ U{0..9}",
     ),
     "trop_cfg1": Workload(
         "trop_cfg1", "trop", 256, 512, 8, False,
@@ -122,6 +166,12 @@ WORKLOADS = {
         description="config 5: TropLinear(4096->4096, H1024, K16, D256), f16 params, eval forward, batch 65536",
         cpu_sample_rows=256,
     ),
+    "pairwise_cfg5_eval": Workload(
+        "pairwise_cfg5_eval", "pairwise", 4096, 4096, 65536, False, dtype="float16",
+        layer_kwargs=dict(tables=1024, comparisons=8),
+        description="config 5: PairwiseLinear(4096->4096, T1024, C8), f16 params, eval forward, batch 65536",
+        cpu_sample_rows=32,
+    ),
     "trop_cfg5_train": Workload(
         "trop_cfg5_train", "trop", 4096, 4096, 16384, True, dtype="float16",
         layer_kwargs=dict(heads=1024, cells=16, code_dim=256),
@@ -134,6 +184,8 @@ WORKLOADS = {
 def algorithmic_bytes(w: Workload, kernel: str, rows: int) -> float | None:
     """Algorithmic bytes one launch of ``kernel`` moves for ``rows`` rows (per-row formulas of
     the hot-path measurement plan; parameter bytes counted once per gathered row)."""
+    if w.classifier:
+        return None  # two layers of different shapes share the kernel names
     kw = w.layer_kwargs
     elt = 2 if w.dtype == "float16" else 4
     if w.kind == "pairwise":
@@ -338,14 +390,31 @@ def _barrier_sync(world: int, device: torch.device) -> None:
 
 
 def _make_inputs(w: Workload, rank: int, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    """x and the upstream gradient, or for the classifiers x ~ U[0,1] and labels ~ U{0..C-1}."""
     gen = torch.Generator().manual_seed(1 + rank)
+    if w.classifier:
+        x = torch.rand(w.rows_per_gpu, w.in_features, generator=gen)
+        labels = torch.randint(0, w.out_features, (w.rows_per_gpu,), generator=gen)
+        return x, labels
     x = torch.randn(w.rows_per_gpu, w.in_features, generator=gen)
     g = torch.randn(w.rows_per_gpu, 1, w.out_features, generator=gen)
     return x, g
 
 
+def _input_grad(w: Workload) -> bool:
+    """Whether the step wants d(loss)/dx (the layer workloads' upstream-gradient steps)."""
+    return w.train and not w.classifier
+
+
 def _step(layer, x: torch.Tensor, g: torch.Tensor | None, w: Workload) -> torch.Tensor:
-    """One forward (+ backward) of the layer through its public module API."""
+    """One forward (+ backward) of the layer through its public module API. Classifiers: the
+    logits' cross-entropy against the labels ``g``, backward, the loss returned (the optimizer
+    step follows the gradient all-reduce: ``_optimizer_step``)."""
+    if w.classifier:
+        layer.optimizer.zero_grad(set_to_none=True)
+        loss = torch.nn.functional.cross_entropy(layer(x), g)
+        loss.backward()
+        return loss
     if w.train:
         for p in layer.parameters():
             p.grad = None
@@ -354,6 +423,33 @@ def _step(layer, x: torch.Tensor, g: torch.Tensor | None, w: Workload) -> torch.
         return y
     with torch.no_grad():
         return layer(x)
+
+
+def _optimizer_step(layer) -> None:
+    opt = getattr(layer, "optimizer", None)
+    if opt is not None:
+        opt.step()
+
+
+def _results(w: Workload, y: torch.Tensor, xd: torch.Tensor) -> list[torch.Tensor]:
+    """Device tensors a step hands back to the host: the loss (classifiers), or the output and,
+    when training, the input gradient."""
+    if w.classifier:
+        return [y.detach().reshape(1)]
+    out = [y.detach().float()]
+    if w.train:
+        out.append(xd.grad)
+    return out
+
+
+def _result_buffers(w: Workload, x_host: torch.Tensor) -> list[torch.Tensor]:
+    """Pinned host buffers matching ``_results``."""
+    if w.classifier:
+        return [torch.empty(1, dtype=torch.float32).pin_memory()]
+    bufs = [torch.empty((w.rows_per_gpu, 1, w.out_features), dtype=torch.float32).pin_memory()]
+    if w.train:
+        bufs.append(torch.empty_like(x_host).pin_memory())
+    return bufs
 
 
 def _capture(fn, device: torch.device, during_capture=contextlib.nullcontext) -> torch.cuda.CUDAGraph:
@@ -386,14 +482,14 @@ def _timed(steps: int, body, flush: torch.Tensor, world: int, device: torch.devi
     return sum(s.elapsed_time(e) for s, e in zip(starts, ends))
 
 
-def _pipelined_e2e(steps, layer, w, x_pin, g_pin, y_pin, gx_pin, reduce_grads, flush, world, device) -> float:
+def _pipelined_e2e(steps, layer, w, x_pin, g_pin, out_pins, reduce_grads, flush, world, device) -> float:
     """``steps`` e2e steps as a prefetching pipeline; returns the device time (ms) of the whole
     span, from before the first input copy to after the last result copy.
 
     Step i: the copy-in stream uploads the pinned inputs into device buffer i % 2 (once step
     i-2 has finished with it); the compute stream flushes L2 and runs the step through the
-    module API; the copy-out stream copies the output and the input gradient into pinned
-    buffer i % 2. Events order the three streams, and ``record_stream`` keeps the step's
+    module API; the copy-out stream copies the step's results (``_results``) into pinned
+    buffer set i % 2. Events order the three streams, and ``record_stream`` keeps the step's
     output tensors alive until their copy has run."""
     if steps == 0:
         return 0.0
@@ -401,8 +497,7 @@ def _pipelined_e2e(steps, layer, w, x_pin, g_pin, y_pin, gx_pin, reduce_grads, f
     cin, cout = torch.cuda.Stream(device), torch.cuda.Stream(device)
     xd = [torch.empty(x_pin.shape, dtype=x_pin.dtype, device=device) for _ in range(2)]
     gd = [torch.empty(g_pin.shape, dtype=g_pin.dtype, device=device) for _ in range(2)] if w.train else [None, None]
-    y_host = [y_pin, torch.empty_like(y_pin).pin_memory()]
-    gx_host = [gx_pin, torch.empty_like(gx_pin).pin_memory()]
+    out_host = [out_pins, [torch.empty_like(b).pin_memory() for b in out_pins]]
     in_ready = [torch.cuda.Event() for _ in range(steps)]
     done = [torch.cuda.Event() for _ in range(steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -425,19 +520,15 @@ def _pipelined_e2e(steps, layer, w, x_pin, g_pin, y_pin, gx_pin, reduce_grads, f
             upload(i + 1)
         comp.wait_event(in_ready[i])
         flush.fill_(float(i))
-        xi = xd[i % 2].detach().requires_grad_(w.train)
+        xi = xd[i % 2].detach().requires_grad_(_input_grad(w))
         y = _step(layer, xi, gd[i % 2], w)
         reduce_grads()
         done[i].record(comp)
         with torch.cuda.stream(cout):
             cout.wait_event(done[i])
-            yf = y.detach().float()
-            y_host[i % 2].copy_(yf, non_blocking=True)
-            yf.record_stream(cout)
-            if w.train:
-                y.record_stream(cout)
-                xi.grad.record_stream(cout)
-                gx_host[i % 2].copy_(xi.grad, non_blocking=True)
+            for buf, r in zip(out_host[i % 2], _results(w, y, xi)):
+                r.record_stream(cout)
+                buf.copy_(r, non_blocking=True)
     comp.wait_stream(cout)
     comp.wait_stream(cin)
     end.record(comp)
@@ -460,6 +551,10 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     tropnn_b200._native.load()
     layer = w.build().to(device).train(w.train)
+    if w.classifier:
+        # Adam as the reference example trains (examples/emnist.py:310, AdamW with weight_decay 0),
+        # capturable so that the whole step goes into one CUDA graph.
+        layer.optimizer = torch.optim.Adam(layer.parameters(), lr=1e-3, capturable=True)
     peer = peer_lut = None
     with contextlib.ExitStack() as stack:
         if world > 1 and w.train:
@@ -502,13 +597,16 @@ def _run_b200_body(
     from tropnn_b200.distributed import allreduce_gradients
 
     x_host, g_host = _make_inputs(w, rank, device)
-    x = x_host.to(device).requires_grad_(w.train)
+    x = x_host.to(device).requires_grad_(_input_grad(w))
     g = g_host.to(device)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
 
     def reduce_grads() -> None:
+        """After the backward: the gradient all-reduce at N>1, then the optimizer step
+        (classifiers)."""
         if world > 1 and w.train:
             allreduce_gradients(layer, peer=peer)
+        _optimizer_step(layer)
 
     def eager_step() -> None:
         _step(layer, x, g, w)
@@ -559,19 +657,17 @@ def _run_b200_body(
     # (+ input gradient) copied back inside the timed region.
     x_pin = x_host.pin_memory()
     g_pin = g_host.pin_memory()
-    y_pin = torch.empty((w.rows_per_gpu, 1, w.out_features), dtype=torch.float32).pin_memory()
-    gx_pin = torch.empty_like(x_host).pin_memory()
-    h2d = x_pin.numel() * 4 + (g_pin.numel() * 4 if w.train else 0)
-    d2h = y_pin.numel() * 4 + (gx_pin.numel() * 4 if w.train else 0)
+    out_pins = _result_buffers(w, x_host)
+    h2d = x_pin.numel() * x_pin.element_size() + (g_pin.numel() * g_pin.element_size() if w.train else 0)
+    d2h = sum(b.numel() * b.element_size() for b in out_pins)
 
     def e2e_step() -> None:
-        xd = x_pin.to(device, non_blocking=True).requires_grad_(w.train)
+        xd = x_pin.to(device, non_blocking=True).requires_grad_(_input_grad(w))
         gd = g_pin.to(device, non_blocking=True) if w.train else None
         y = _step(layer, xd, gd, w)
         reduce_grads()
-        y_pin.copy_(y.detach().float(), non_blocking=True)
-        if w.train:
-            gx_pin.copy_(xd.grad, non_blocking=True)
+        for buf, r in zip(out_pins, _results(w, y, xd)):
+            buf.copy_(r, non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
@@ -580,7 +676,7 @@ def _run_b200_body(
     # The same steps as a prefetching pipeline: step i+1's inputs go up on one copy stream
     # and step i-1's results come back on another while step i computes.
     def e2e_pipelined(steps: int) -> float:
-        return _pipelined_e2e(steps, layer, w, x_pin, g_pin, y_pin, gx_pin, reduce_grads, flush, world, device)
+        return _pipelined_e2e(steps, layer, w, x_pin, g_pin, out_pins, reduce_grads, flush, world, device)
 
     e2e_pipelined(args.warmup)
     e2e_ms = _max_over_ranks(e2e_pipelined(args.steps), world, device)
@@ -657,8 +753,10 @@ def _run_b200_body(
             "d2h_bytes_per_step": d2h,
             "ms_per_step": round(e2e_ms / args.steps, 4),
             "path": (
-                "eager module API, pinned host inputs in, output + input gradient out; copies of "
-                "neighbouring steps overlap the compute on two copy streams; L2 flush per step inside the span"
+                ("eager module API, pinned x and labels in, loss out" if w.classifier
+                 else "eager module API, pinned host inputs in, output + input gradient out")
+                + "; copies of neighbouring steps overlap the compute on two copy streams; L2 flush per step "
+                "inside the span"
             ),
         },
         "e2e_serial": {
@@ -694,6 +792,70 @@ def _oracle_params(w: Workload, impl: str = "torch") -> tuple[dict[str, np.ndarr
     return params, layer
 
 
+def _classifier_state(w: Workload) -> dict:
+    """CPU state of a classifier step: per layer its f32 parameters (numpy), the module (for its
+    settings and parameter names) and Adam moments."""
+    model = w.build()
+    layers = []
+    for mod in model.layers:
+        params = {k: (v.detach().numpy().astype(np.float32) if v.is_floating_point() else v.detach().numpy())
+                  for k, v in mod.state_dict().items()}
+        names = [k for k, _ in mod.named_parameters()]
+        adam = {k: (np.zeros_like(params[k]), np.zeros_like(params[k])) for k in names}
+        layers.append({"module": mod, "params": params, "names": names, "adam": adam})
+    return {"layers": layers, "t": 0}
+
+
+def _adam_update(p: np.ndarray, g: np.ndarray, m: np.ndarray, v: np.ndarray, t: int, lr: float = 1e-3,
+                 b1: float = 0.9, b2: float = 0.999, eps: float = 1e-8) -> None:
+    """torch.optim.Adam's update (weight_decay 0), in place, float32."""
+    f = np.float32
+    m *= f(b1)
+    m += f(1 - b1) * g
+    v *= f(b2)
+    v += f(1 - b2) * g * g
+    denom = np.sqrt(v) / f(math.sqrt(1 - b2 ** t)) + f(eps)
+    p -= f(lr / (1 - b1 ** t)) * m / denom
+
+
+def _oracle_classifier_step(w: Workload, state: dict, x: np.ndarray, labels: np.ndarray) -> None:
+    """One classifier train step in numpy (the reference's torch path): each layer's forward,
+    cross-entropy on the logits, each layer's backward in reverse, Adam on every parameter."""
+    import oracle
+
+    acts, fwds = [x], []
+    for lay in state["layers"]:
+        mod, params = lay["module"], lay["params"]
+        if w.kind == "trop_clf":
+            f = oracle.trop_linear_forward(acts[-1], params, code_scale=mod.code_scale, training=True)
+            acts.append(f["y"])
+        else:
+            f = oracle.pairwise_forward(acts[-1], params["anchors"], params["thresholds"], params["lut"],
+                                        output_scale=mod.output_scale)
+            acts.append(f["out"])
+        fwds.append(f)
+    logits = acts[-1].astype(np.float32)
+    e = np.exp(logits - logits.max(axis=1, keepdims=True))
+    grad = (e / e.sum(axis=1, keepdims=True)).astype(np.float32)
+    grad[np.arange(len(labels)), labels] -= np.float32(1.0)
+    grad /= np.float32(len(labels))
+    state["t"] += 1
+    for i in reversed(range(len(state["layers"]))):
+        lay = state["layers"][i]
+        mod, params = lay["module"], lay["params"]
+        if w.kind == "trop_clf":
+            grads = oracle.trop_linear_backward(grad, acts[i], params, fwds[i], code_scale=mod.code_scale, training=True)
+        else:
+            grads = oracle.pairwise_backward(
+                grad, fwds[i]["indices"], fwds[i]["margins"], params["anchors"], params["lut"], in_features=mod.in_features,
+                output_scale=mod.output_scale, use_min_margin_ste=mod.use_min_margin_ste, surrogate=mod.surrogate,
+            )
+        grad = grads["x"]
+        for name in lay["names"]:
+            m, v = lay["adam"][name]
+            _adam_update(params[name], grads[name], m, v, state["t"])
+
+
 def cpu_impl_for(w: Workload, requested: str) -> str:
     """The CPU path a leg times: with "auto" the reference's faster path on the workload
     (``Workload.cpu_impl``); "zig" (the C++ restatement of the Zig inference kernels) exists for
@@ -714,6 +876,9 @@ _CPU_IMPL_TEXT = {
 def _oracle_step(w: Workload, params: dict, layer, x: np.ndarray, g: np.ndarray, impl: str = "torch") -> None:
     import oracle
 
+    if w.classifier:
+        _oracle_classifier_step(w, params, x, g)
+        return
     if impl == "zig":
         from oracle import native
 
@@ -750,10 +915,15 @@ def _pool_init(workload: str, sample_rows: int, workers: int, impl: str = "torch
         from oracle import native
 
         native.load()
-    params, layer = _oracle_params(w, impl)
     gen = np.random.default_rng(7)
-    x = gen.standard_normal((sample_rows, w.in_features), dtype=np.float32)
-    g = gen.standard_normal((sample_rows, w.out_features), dtype=np.float32)
+    if w.classifier:
+        params, layer = _classifier_state(w), None
+        x = gen.random((sample_rows, w.in_features), dtype=np.float32)
+        g = gen.integers(0, w.out_features, sample_rows)
+    else:
+        params, layer = _oracle_params(w, impl)
+        x = gen.standard_normal((sample_rows, w.in_features), dtype=np.float32)
+        g = gen.standard_normal((sample_rows, w.out_features), dtype=np.float32)
     _POOL_STATE.update(w=w, params=params, layer=layer, x=x, g=g, impl=impl,
                        chunks=[c for c in np.array_split(np.arange(sample_rows), workers) if c.size])
 
