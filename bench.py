@@ -856,15 +856,31 @@ def _oracle_classifier_step(w: Workload, state: dict, x: np.ndarray, labels: np.
             _adam_update(params[name], grads[name], m, v, state["t"])
 
 
+def _zig_port_usable() -> str | None:
+    """None when the C++ Zig restatement builds and loads on this host, else why not."""
+    try:
+        from oracle import native
+
+        native.build()
+        native.load()
+    except (OSError, RuntimeError, subprocess.CalledProcessError) as exc:
+        return str(exc).splitlines()[0]
+    return None
+
+
 def cpu_impl_for(w: Workload, requested: str) -> str:
     """The CPU path a leg times: with "auto" the reference's faster path on the workload
     (``Workload.cpu_impl``); "zig" (the C++ restatement of the Zig inference kernels) exists for
     eval workloads only."""
     if requested == "zig" and w.train:
         raise SystemExit(f"--cpu-impl zig: {w.name} is a training workload; the Zig kernels are inference only")
-    if requested == "auto":
-        return "torch" if w.train else w.cpu_impl
-    return requested
+    impl = ("torch" if w.train else w.cpu_impl) if requested == "auto" else requested
+    if impl == "zig" and requested == "auto":
+        why = _zig_port_usable()
+        if why is not None:
+            print(f"warning: the Zig-kernel port is unusable here ({why}); timing the torch port", file=sys.stderr)
+            return "torch"
+    return impl
 
 
 _CPU_IMPL_TEXT = {
