@@ -4,6 +4,7 @@ cross-entropy gradient against torch's own on CPU, and the CPU oracle step end t
 from __future__ import annotations
 
 import numpy as np
+import pytest
 import torch
 
 import bench
@@ -45,3 +46,41 @@ def test_classifier_oracle_step_runs_and_moves_parameters() -> None:
     grad = e / e.sum(axis=1, keepdims=True)
     grad[np.arange(6), labels.numpy()] -= 1.0
     assert np.allclose(grad / 6, logits.grad.numpy(), atol=1e-7)
+
+
+def test_reference_arm_line_keeps_the_contract(monkeypatch) -> None:
+    """bench.py --impl reference on config 1: one JSON object with the base keys, impl, a
+    cpu_baseline describing the run (here the C++ Zig-kernel port) and an e2e with no copies;
+    ranks other than 0 print nothing."""
+    import argparse
+
+    args = argparse.Namespace(steps=1, warmup=1, cpu_impl="auto")
+    w = bench.WORKLOADS["trop_cfg1"]
+    monkeypatch.setenv("RANK", "1")
+    monkeypatch.setenv("WORLD_SIZE", "2")
+    assert bench.run_reference(args, w) is None
+    monkeypatch.setenv("RANK", "0")
+    monkeypatch.setenv("WORLD_SIZE", "1")
+    line = bench.run_reference(args, w)
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+                "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["impl"] == "reference" and line["value"] > 0 and line["steps"] == 1
+    assert line["cpu_baseline"]["kind"] == "port" and "Zig" in line["cpu_baseline"]["sample"]
+    assert line["e2e"] == {"value": line["value"], "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_cpu_path_choice_and_e2e_buffers(monkeypatch) -> None:
+    W = bench.WORKLOADS
+    monkeypatch.setattr(torch.Tensor, "pin_memory", lambda self: self)  # no driver here: shapes only
+    assert bench.cpu_impl_for(W["pairwise_cfg2"], "auto") == "torch"  # training: the torch path only
+    assert bench.cpu_impl_for(W["trop_cfg5_eval"], "auto") == "torch"  # BLAS scores beat the Zig dots there
+    assert bench.cpu_impl_for(W["trop_cfg1"], "auto") == "zig"
+    with pytest.raises(SystemExit):
+        bench.cpu_impl_for(W["pairwise_cfg2"], "zig")
+    x = torch.empty(W["pairwise_cfg2"].rows_per_gpu, 256)
+    bufs = bench._result_buffers(W["pairwise_cfg2"], x)
+    assert [tuple(b.shape) for b in bufs] == [(4096, 1, 512), (4096, 256)]
+    assert [tuple(b.shape) for b in bench._result_buffers(W["trop_cfg3_clf"], torch.empty(512, 784))] == [(1,)]
+    assert bench._input_grad(W["pairwise_cfg2"]) and not bench._input_grad(W["trop_cfg3_clf"])
+    assert not bench._input_grad(W["trop_cfg1"])
