@@ -37,6 +37,7 @@ __all__ = [
     "surrogate_gradient",
     "top2_indices",
     "trop_linear_backward",
+    "trop_linear_exact_eval",
     "trop_linear_forward",
     "trop_route_backward",
     "trop_route_hidden",
@@ -229,6 +230,29 @@ def trop_linear_forward(
     )
     y = (route["hidden"] @ _f32(params["output_proj.weight"]).T + _f32(params["output_proj.bias"])).astype(F32)
     return {"y": y, "z": z, **route}
+
+
+def trop_linear_exact_eval(x: np.ndarray, params: dict[str, np.ndarray], *, code_scale: float) -> dict[str, np.ndarray]:
+    """TropLinear eval with ``exact_fused="eval"`` (layers/tropical_exact.py:257-358, selected at
+    layers/tropical.py:92 in eval under no_grad): the reassociated form with effective weights,
+    every product in float32 (parameters upcast to the compute dtype, x not rounded to them):
+    router_eff = W P [H,K,in], value_eff = c Wout^T [H,K,out], base = Wout P [out,in];
+    scores = x router_eff^T + b, top-2; y = x base^T + b_out + code_scale * sum_h value_eff[h, w]."""
+    w = _f32(params["router_weight"])
+    heads, cells, dim = w.shape
+    proj = _f32(params["proj.weight"])
+    w_out = _f32(params["output_proj.weight"])
+    router_eff = (w.reshape(heads * cells, dim) @ proj).astype(F32)
+    value_eff = (_f32(params["code"]).reshape(heads * cells, dim) @ w_out.T).astype(F32).reshape(heads, cells, -1)
+    base = (w_out @ proj).astype(F32)
+    x32 = _f32(x)
+    n = x32.shape[0]
+    scores = ((x32 @ router_eff.T).reshape(n, heads, cells) + _f32(params["router_bias"])[None]).astype(F32)
+    winner, runner, margins = top2_indices(scores)
+    out = (x32 @ base.T + _f32(params["output_proj.bias"])).astype(F32)
+    value_sum = value_eff[np.arange(heads)[None, :], winner].sum(axis=1, dtype=F32)
+    y = (out + value_sum * F32(code_scale)).astype(F32)
+    return {"y": y, "winner": winner, "runner": runner, "margins": margins, "scores": scores}
 
 
 def trop_linear_backward(

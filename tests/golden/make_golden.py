@@ -3,10 +3,14 @@
 Run in a checkout where the reference package is importable (default: a read-only
 source tree at $TROPNN_REFERENCE, imported as ``tropnn`` through a temporary symlink):
 
-    TROPNN_REFERENCE=/path/to/tropnn python tests/golden/make_golden.py
+    TROPNN_REFERENCE=/path/to/tropnn python tests/golden/make_golden.py [--only NAME ...]
 
-Each case records, from the reference's default torch path on CPU (``backend="torch"``,
-``exact_fused="off"``): the seeded state_dict, the seeded inputs, the forward outputs,
+(``--only`` rewrites just the named fixtures; every case still draws its inputs, in order,
+from the one seeded generator, so each fixture's inputs do not depend on the selection.)
+
+Each case records, from the reference's torch path on CPU (``backend="torch"``,
+``exact_fused="off"``, or ``"eval"`` where a case's kwargs ask for the reassociated eval path of
+layers/tropical_exact.py:297-358): the seeded state_dict, the seeded inputs, the forward outputs,
 the route debug cache (``_last_indices`` / ``_last_margins``) and, for training cases,
 every gradient of ``(y * grad_out).sum()`` (an upstream gradient ``grad_out``). The
 fixtures are the parity anchor of the numpy oracle and of the CUDA kernels; nothing at
@@ -101,7 +105,7 @@ def _bias_separate(layer, values: torch.Tensor) -> None:
         layer.router_bias.copy_(values.expand_as(layer.router_bias))
 
 
-def main() -> None:
+def main(only: set[str] | None = None) -> None:
     tropnn = _import_reference()
     TropLinear, PairwiseLinear = tropnn.TropLinear, tropnn.PairwiseLinear
     gen = torch.Generator().manual_seed(1)
@@ -121,7 +125,8 @@ def main() -> None:
         meta = dict(kind="trop", in_features=in_f, out_features=out_f, heads=heads, cells=cells, code_dim=code_dim,
                     seed=seed, train=train, half=half, code_scale=layer.code_scale, kwargs=kw,
                     router_bias=None if bias is None else [float(v) for v in bias])
-        _save(name, rec, meta)
+        if only is None or name in only:
+            _save(name, rec, meta)
         manifest[name] = meta
 
     def pair(name, in_f, out_f, *, tables, comparisons, batch, steps=None, train, seed=0, half=False, uniform=False, **kw):
@@ -135,7 +140,8 @@ def main() -> None:
         rec = _run_case(layer, x, train=train, grad_out=g)
         meta = dict(kind="pairwise", in_features=in_f, out_features=out_f, tables=tables, comparisons=comparisons,
                     seed=seed, train=train, half=half, output_scale=layer.output_scale, kwargs=kw)
-        _save(name, rec, meta)
+        if only is None or name in only:
+            _save(name, rec, meta)
         manifest[name] = meta
 
     # config 1: TropLinear(256->512, H32, K4, D32) eval forward, batch 8, seed 0.
@@ -166,6 +172,13 @@ def main() -> None:
          bias=torch.linspace(-4.0, 3.0, steps=8), cache_route_debug=False)
     trop("small_trop_eval_3d", 6, 4, heads=3, cells=4, code_dim=5, batch=5, steps=2, train=False, seed=1)
     trop("small_trop_cells300_train", 16, 8, heads=3, cells=300, code_dim=8, batch=6, train=True, seed=3)
+    # exact_fused="eval": the reassociated eval path (layers/tropical_exact.py:297-358; run under
+    # no_grad, as its dispatch at layers/tropical.py:92 requires).
+    trop("cfg1_trop_exact_eval_b8", 256, 512, heads=32, cells=4, code_dim=32, batch=8, train=False, exact_fused="eval")
+    trop("small_trop_exact_eval_3d", 6, 4, heads=3, cells=4, code_dim=5, batch=5, steps=2, train=False, seed=4,
+         exact_fused="eval")
+    trop("cfg5s_trop_half_exact_eval_b32", 256, 256, heads=64, cells=16, code_dim=64, batch=32, train=False, half=True,
+         exact_fused="eval")
 
     # Full-size seeded init of config 5's TropLinear: sha256 of every state_dict tensor.
     big = TropLinear(4096, 4096, heads=1024, cells=16, code_dim=256, seed=0).half()
@@ -176,4 +189,9 @@ def main() -> None:
 
 
 if __name__ == "__main__":
-    main()
+    import argparse
+
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--only", nargs="*", default=None, help="fixture names to (re)write; default all")
+    args = parser.parse_args()
+    main(set(args.only) if args.only is not None else None)

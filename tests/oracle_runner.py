@@ -18,7 +18,10 @@ def run_oracle(arrays: dict[str, np.ndarray], meta: dict, state: dict[str, np.nd
     train = meta["train"]
     out: dict[str, np.ndarray] = {}
     if meta["kind"] == "trop":
-        fwd = oracle.trop_linear_forward(x, state, code_scale=meta["code_scale"], training=train)
+        if meta["kwargs"].get("exact_fused") == "eval" and not train:
+            fwd = oracle.trop_linear_exact_eval(x, state, code_scale=meta["code_scale"])
+        else:
+            fwd = oracle.trop_linear_forward(x, state, code_scale=meta["code_scale"], training=train)
         out["y"] = fwd["y"].reshape(b, s, -1)
         out["last_indices"] = fwd["winner"].reshape(b, s, -1)
         out["last_margins"] = fwd["margins"].reshape(b, s, -1)

@@ -17,8 +17,15 @@ pytestmark = pytest.mark.gpu
 FP32_TOL = 1e-5
 
 
-def _gate_from_state(x: np.ndarray, st: dict) -> tuple[np.ndarray, np.ndarray]:
-    ref = oracle.trop_linear_forward(x, st, code_scale=1.0, training=False)
+def _exact_eval(meta: dict) -> bool:
+    return meta["kwargs"].get("exact_fused") == "eval" and not meta["train"]
+
+
+def _gate_from_state(x: np.ndarray, st: dict, exact: bool = False) -> tuple[np.ndarray, np.ndarray]:
+    if exact:
+        ref = oracle.trop_linear_exact_eval(x, st, code_scale=1.0)
+    else:
+        ref = oracle.trop_linear_forward(x, st, code_scale=1.0, training=False)
     return route_gate(ref["scores"])
 
 
@@ -28,10 +35,11 @@ def test_trop_matches_reference_golden(name: str) -> None:
     layer = build_layer(arrays, meta)
     st = state_arrays(layer)
     got = run_b200(layer, arrays, meta)
-    tol = tolerance(meta)
+    # The exact eval path computes in f32 whatever the parameter dtype (so does the reference's).
+    tol = FP32_TOL if _exact_eval(meta) else tolerance(meta)
     assert rel_err(got["y"], arrays["y"]) <= tol
     x = arrays["x"].reshape(-1, arrays["x"].shape[-1]).astype(np.float32)
-    win, _ = _gate_from_state(x, st)
+    win, _ = _gate_from_state(x, st, exact=_exact_eval(meta))
     if "last_indices" in arrays:
         assert np.array_equal(got["last_indices"].reshape(win.shape)[win], arrays["last_indices"].reshape(win.shape)[win])
         assert rel_err(got["last_margins"], arrays["last_margins"]) <= max(tol, 1e-5)
@@ -214,3 +222,66 @@ def test_invalid_arguments_raise() -> None:
         tropnn_b200.trop_route_hidden_b200(z, layer.router_weight, layer.router_bias[:2], layer.code, code_scale=1.0)
     with pytest.raises(ValueError):
         tropnn_b200.trop_route_hidden_b200(z[..., :4], layer.router_weight, layer.router_bias, layer.code, code_scale=1.0)
+
+
+@pytest.mark.parametrize(
+    ("in_f", "out_f", "heads", "cells", "code_dim", "n", "half"),
+    [
+        (256, 512, 32, 4, 32, 4096, False),  # config 1's layer at a wide batch
+        (784, 128, 256, 16, 64, 512, False),  # config 3 layer 1
+        (256, 256, 64, 16, 64, 300, True),  # f16 parameters: the exact path still computes in f32
+        (1536, 40, 8, 3, 24, 65, False),  # the widest input the exact path routes on; 3 cells
+    ],
+)
+def test_exact_eval_path_matches_oracle(in_f, out_f, heads, cells, code_dim, n, half) -> None:
+    """exact_fused="eval" in eval under no_grad (layers/tropical.py:92): the reassociated path of
+    layers/tropical_exact.py:297-358 against its oracle restatement. Winners bit-exact where the
+    top-2 margin clears the parity gate; outputs of the rows whose every head clears it within
+    1e-5 relative."""
+    layer = tropnn_b200.TropLinear(in_f, out_f, heads=heads, cells=cells, code_dim=code_dim, seed=5,
+                                   exact_fused="eval")
+    if half:
+        layer = layer.half()
+    layer = layer.cuda().eval()
+    gen = torch.Generator().manual_seed(9)
+    x = torch.randn(n, in_f, generator=gen)
+    with torch.no_grad():
+        y = layer(x.cuda())
+    assert getattr(layer, "_b200_exact_eval_cache", None) is not None  # the exact path ran
+    st = state_arrays(layer)
+    ref = oracle.trop_linear_exact_eval(x.numpy(), st, code_scale=layer.code_scale)
+    win, _ = route_gate(ref["scores"])
+    got_w = layer._last_indices.cpu().numpy().reshape(n, heads)
+    assert np.array_equal(got_w[win], ref["winner"][win])
+    assert rel_err(layer._last_margins.cpu().numpy().reshape(n, heads), ref["margins"]) <= 1e-5
+    rows = win.all(axis=1) & (got_w == ref["winner"]).all(axis=1)
+    assert rows.mean() > 0.5
+    assert rel_err(y.float().cpu().numpy().reshape(n, -1)[rows], ref["y"][rows]) <= FP32_TOL
+
+
+def test_exact_eval_dispatch_and_cache() -> None:
+    """The exact path runs only in eval under no_grad and for inputs of at most 1536 features;
+    its effective weights are rebuilt when a parameter changes in place."""
+    layer = tropnn_b200.TropLinear(64, 48, heads=8, cells=4, code_dim=16, seed=2, exact_fused="eval").cuda()
+    x = torch.randn(33, 64, device="cuda")
+    layer.train()
+    with torch.no_grad():
+        layer(x)
+    assert getattr(layer, "_b200_exact_eval_cache", None) is None  # training: the default path
+    layer.eval()
+    layer(x)
+    assert getattr(layer, "_b200_exact_eval_cache", None) is None  # grad enabled: the default path
+    with torch.no_grad():
+        y0 = layer(x)
+        key0 = layer._b200_exact_eval_cache[0]
+        layer.code.mul_(2.0)
+        y1 = layer(x)
+    assert layer._b200_exact_eval_cache[0] != key0
+    st = state_arrays(layer)
+    ref = oracle.trop_linear_exact_eval(x.cpu().numpy(), st, code_scale=layer.code_scale)
+    assert rel_err(y1.cpu().numpy().reshape(33, -1), ref["y"]) <= FP32_TOL
+    assert not torch.equal(y0, y1)
+    wide = tropnn_b200.TropLinear(2048, 16, heads=4, cells=4, code_dim=16, seed=3, exact_fused="eval").cuda().eval()
+    with torch.no_grad():
+        wide(torch.randn(5, 2048, device="cuda"))
+    assert getattr(wide, "_b200_exact_eval_cache", None) is None  # wider than the route kernel's row stage

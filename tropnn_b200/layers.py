@@ -25,10 +25,12 @@ import torch.nn as nn
 from torch import Tensor
 
 from .ops import (
+    EXACT_EVAL_MAX_IN,
     linear_f32out_b200,
     linear_f32out_eligible,
     pairwise_anchor_index,
     pairwise_b200,
+    trop_exact_eval_b200,
     trop_route_hidden_packed,
 )
 
@@ -91,6 +93,66 @@ def _require_f32_compute(compute_dtype: torch.dtype, layer_name: str) -> None:
 # ---------------------------------------------------------------------------
 
 
+def _exact_eval_params(layer: nn.Module, device: torch.device) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """Effective weights of the exact eval path in f32 (layers/tropical_exact.py:257-291):
+    router_eff = W P [H,K,in], router_bias, value_eff = c Wout^T [H,K,out], base = Wout P
+    [out,in], cached per parameter version like the reference's _exact_eval_cache."""
+    bias = layer.output_proj.bias
+    key = (
+        device,
+        layer.proj.weight._version,
+        layer.output_proj.weight._version,
+        -1 if bias is None else bias._version,
+        layer.router_weight._version,
+        layer.router_bias._version,
+        layer.code._version,
+        layer.proj.weight.data_ptr(),
+        layer.router_weight.data_ptr(),
+        layer.code.data_ptr(),
+    )
+    cached = getattr(layer, "_b200_exact_eval_cache", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    f32 = torch.float32
+    proj = layer.proj.weight.to(device=device, dtype=f32)
+    w_out = layer.output_proj.weight.to(device=device, dtype=f32)
+    heads, cells, dim = layer.router_weight.shape
+    router_eff = torch.matmul(layer.router_weight.to(device=device, dtype=f32).reshape(heads * cells, dim), proj)
+    value_eff = torch.matmul(layer.code.to(device=device, dtype=f32).reshape(heads * cells, dim), w_out.t())
+    base = torch.matmul(w_out, proj)
+    params = (
+        router_eff.view(heads, cells, -1).contiguous(),
+        layer.router_bias.to(device=device, dtype=f32).contiguous(),
+        value_eff.view(heads, cells, -1).contiguous(),
+        base.contiguous(),
+    )
+    layer._b200_exact_eval_cache = (key, params)
+    return params
+
+
+def _trop_exact_eval_b200(layer: nn.Module, x: Tensor) -> Tensor:
+    """TropLinear forward with ``exact_fused="eval"`` in eval under no_grad
+    (layers/tropical_exact.py:297-358): x in the compute dtype (not rounded to the parameters),
+    scores against W P on the route kernel, y = x (Wout P)^T + b_out (cuBLAS, as the reference's
+    matmul) plus code_scale * sum_h (c Wout^T)[h, winner] on the code-sum kernel."""
+    input_dtype = x.dtype
+    compute_dtype = _compute_dtype(x)
+    _require_f32_compute(compute_dtype, "TropLinear")
+    batch, steps, in_features = x.shape
+    x_flat = x.to(compute_dtype).reshape(batch * steps, in_features).contiguous()
+    router_eff, router_bias, value_eff, base = _exact_eval_params(layer, x.device)
+    base_out = torch.matmul(x_flat, base.t())
+    bias = layer.output_proj.bias
+    if bias is not None:
+        base_out = base_out + bias.to(device=x.device, dtype=compute_dtype)
+    y, winner, margins = trop_exact_eval_b200(
+        x_flat, router_eff, router_bias, value_eff, base_out, code_scale=layer.code_scale,
+        keep_margins=getattr(layer, "cache_route_debug", True),
+    )
+    _store_debug(layer, winner.view(batch, steps, -1), margins.view(batch, steps, -1) if margins.numel() else margins)
+    return y.view(batch, steps, -1).to(dtype=input_dtype)
+
+
 def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
     """Full TropLinear forward on sm_100a for any module with the TropLinear attributes.
 
@@ -102,6 +164,15 @@ def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
     if x.ndim == 2:
         x = x.unsqueeze(1)
     _require_cuda_input(x, "TropLinear")
+    if (
+        getattr(layer, "exact_fused", "off") == "eval"
+        and not layer.training
+        and not torch.is_grad_enabled()
+        and layer.in_features <= EXACT_EVAL_MAX_IN
+    ):
+        # layers/tropical.py:92: the reassociated eval path (wider inputs keep the default
+        # path, the same function up to rounding).
+        return _trop_exact_eval_b200(layer, x)
     input_dtype = x.dtype
     compute_dtype = _compute_dtype(x)
     _require_f32_compute(compute_dtype, "TropLinear")
@@ -272,8 +343,9 @@ class TropLinear(RoutedLinearBase):
         self.code_dim = code_dim
         self.code_scale = 1.0 / math.sqrt(heads) if use_output_scaling else 1.0
         self.cpu_param_dtype = cpu_param_dtype
-        # The fused b200 route serves every exact_fused mode: the scores are never
-        # materialised, so the option only keeps its reference meaning for state.
+        # "eval" selects the reassociated eval path (effective weights, trop_forward_b200);
+        # "train" and "off" run the fused b200 route, whose training backward already is the
+        # exact min-face one (scores never materialised).
         self.exact_fused = exact_fused
         self.score_route_max_bytes = score_route_max_bytes
         self.cache_route_debug = cache_route_debug

@@ -805,6 +805,61 @@ def trop_route_hidden_packed(
         )
 
 
+# in_features the exact eval path routes on: the fp32 route kernel stages a row of x per lane in
+# shared memory (32 rows x (in + 4) floats within 200 KiB).
+EXACT_EVAL_MAX_IN = 1536
+
+
+def trop_exact_eval_b200(
+    x: Tensor,
+    router_eff: Tensor,
+    router_bias: Tensor,
+    value_eff: Tensor,
+    base_out: Tensor,
+    *,
+    code_scale: float,
+    keep_margins: bool = True,
+) -> tuple[Tensor, Tensor, Tensor]:
+    """TropLinear's ``exact_fused="eval"`` forward (layers/tropical_exact.py:297-358) on sm_100a,
+    given its effective weights: the route kernel scores x [N, in] against router_eff
+    [H, K, in] (+ router_bias, fp32 FMA) and keeps the top-2; the code-sum kernel adds
+    code_scale * sum_h value_eff[h, winner] [H, K, out] onto base_out = x base^T + b [N, out].
+    Returns (y [N, out] f32, winner [N, H] in the packed route dtype, margins [N, H] f32, or
+    empty without ``keep_margins``). Inference only: no autograd."""
+    for name, t in (("x", x), ("router_eff", router_eff), ("router_bias", router_bias), ("value_eff", value_eff),
+                    ("base_out", base_out)):
+        _require_cuda(t, name)
+        _require_f32(t, name)
+        if t.device != x.device:
+            raise ValueError(f"{name} is on {t.device} but x is on {x.device}")
+    items, in_features = x.shape
+    heads, cells, _ = router_eff.shape
+    out_features = value_eff.shape[2]
+    if router_eff.shape[2] != in_features or router_bias.shape != (heads, cells) or value_eff.shape[:2] != (heads, cells):
+        raise ValueError("trop_exact_eval_b200: effective weight shapes do not match")
+    if base_out.shape != (items, out_features):
+        raise ValueError(f"base_out must have shape {(items, out_features)}, got {tuple(base_out.shape)}")
+    if in_features > EXACT_EVAL_MAX_IN:
+        raise ValueError(f"trop_exact_eval_b200 routes on at most {EXACT_EVAL_MAX_IN} input features, got {in_features}")
+    dev = x.device
+    idx_dtype = packed_route_index_dtype(cells)
+    winner = torch.empty((items, heads), device=dev, dtype=idx_dtype)
+    margins = torch.empty((items, heads) if keep_margins else (0,), device=dev, dtype=torch.float32)
+    y = torch.empty((items, out_features), device=dev, dtype=torch.float32)
+    xs, w, b, v, base = (t.contiguous() for t in (x, router_eff, router_bias, value_eff, base_out))
+    lib = nat.load()
+    icode = nat.index_code(idx_dtype)
+    with torch.cuda.device(dev):
+        stream = nat.stream_handle(dev)
+        _launch("trop_route", lib.tropnn_b200_trop_route, xs.data_ptr(), nat.F32, items, in_features, w.data_ptr(),
+                b.data_ptr(), nat.F32, nat.F32, heads, cells, None, winner.data_ptr(), None, icode,
+                margins.data_ptr() if margins.numel() else None, stream)
+        _launch("trop_hidden", lib.tropnn_b200_trop_hidden, base.data_ptr(), nat.F32, items, out_features, v.data_ptr(),
+                None, nat.F32, heads, cells, winner.data_ptr(), None, icode, None, float(code_scale), 0, y.data_ptr(),
+                stream)
+    return y, winner, margins
+
+
 def linear_f32out_eligible(hidden: Tensor, weight: Tensor) -> bool:
     """Shapes the tensor-core f32-input linear map takes (tropnn_b200_linear_f32out)."""
     out_features, in_features = weight.shape
