@@ -7,6 +7,7 @@ import hashlib
 import json
 from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
 
@@ -105,3 +106,27 @@ def test_missing_library_fails_loudly(tmp_path: Path) -> None:
 
     with pytest.raises(nat.B200Unavailable, match="not found"):
         nat.load(tmp_path / "missing.so")
+
+
+def test_exact_eval_effective_weights_and_cache() -> None:
+    """The exact eval path's effective weights (layers/tropical_exact.py:257-291) against numpy,
+    built once per parameter version and rebuilt after an in-place update (host logic; the
+    kernels that consume them are checked in tests/test_tropical_gpu.py)."""
+    from tropnn_b200.layers import _exact_eval_params
+
+    layer = tropnn_b200.TropLinear(12, 7, heads=3, cells=4, code_dim=5, seed=1, exact_fused="eval")
+    cpu = torch.device("cpu")
+    router_eff, bias, value_eff, base = _exact_eval_params(layer, cpu)
+    w = layer.router_weight.detach().numpy().reshape(12, 5)
+    p = layer.proj.weight.detach().numpy()
+    w_out = layer.output_proj.weight.detach().numpy()
+    assert np.allclose(router_eff.numpy().reshape(12, 12), w @ p, atol=1e-6)
+    assert np.allclose(value_eff.numpy().reshape(12, 7), layer.code.detach().numpy().reshape(12, 5) @ w_out.T, atol=1e-6)
+    assert np.allclose(base.numpy(), w_out @ p, atol=1e-6)
+    assert torch.equal(bias, layer.router_bias.detach())
+    assert _exact_eval_params(layer, cpu)[0] is router_eff  # cached
+    with torch.no_grad():
+        layer.proj.weight.mul_(0.5)
+    again = _exact_eval_params(layer, cpu)
+    assert again[0] is not router_eff
+    assert np.allclose(again[3].numpy(), w_out @ (0.5 * p), atol=1e-6)
