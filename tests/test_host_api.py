@@ -117,9 +117,9 @@ def test_exact_eval_effective_weights_and_cache() -> None:
     layer = tropnn_b200.TropLinear(12, 7, heads=3, cells=4, code_dim=5, seed=1, exact_fused="eval")
     cpu = torch.device("cpu")
     router_eff, bias, value_eff, base = _exact_eval_params(layer, cpu)
-    w = layer.router_weight.detach().numpy().reshape(12, 5)
-    p = layer.proj.weight.detach().numpy()
-    w_out = layer.output_proj.weight.detach().numpy()
+    w = layer.router_weight.detach().numpy().reshape(12, 5).copy()
+    p = layer.proj.weight.detach().numpy().copy()  # copies: the parameter changes in place below
+    w_out = layer.output_proj.weight.detach().numpy().copy()
     assert np.allclose(router_eff.numpy().reshape(12, 12), w @ p, atol=1e-6)
     assert np.allclose(value_eff.numpy().reshape(12, 7), layer.code.detach().numpy().reshape(12, 5) @ w_out.T, atol=1e-6)
     assert np.allclose(base.numpy(), w_out @ p, atol=1e-6)

@@ -114,18 +114,19 @@ def _exact_eval_params(layer: nn.Module, device: torch.device) -> tuple[Tensor, 
     if cached is not None and cached[0] == key:
         return cached[1]
     f32 = torch.float32
-    proj = layer.proj.weight.to(device=device, dtype=f32)
-    w_out = layer.output_proj.weight.to(device=device, dtype=f32)
     heads, cells, dim = layer.router_weight.shape
-    router_eff = torch.matmul(layer.router_weight.to(device=device, dtype=f32).reshape(heads * cells, dim), proj)
-    value_eff = torch.matmul(layer.code.to(device=device, dtype=f32).reshape(heads * cells, dim), w_out.t())
-    base = torch.matmul(w_out, proj)
-    params = (
-        router_eff.view(heads, cells, -1).contiguous(),
-        layer.router_bias.to(device=device, dtype=f32).contiguous(),
-        value_eff.view(heads, cells, -1).contiguous(),
-        base.contiguous(),
-    )
+    with torch.no_grad():  # inference weights: the cache holds no autograd history
+        proj = layer.proj.weight.to(device=device, dtype=f32)
+        w_out = layer.output_proj.weight.to(device=device, dtype=f32)
+        router_eff = torch.matmul(layer.router_weight.to(device=device, dtype=f32).reshape(heads * cells, dim), proj)
+        value_eff = torch.matmul(layer.code.to(device=device, dtype=f32).reshape(heads * cells, dim), w_out.t())
+        base = torch.matmul(w_out, proj)
+        params = (
+            router_eff.view(heads, cells, -1).contiguous(),
+            layer.router_bias.to(device=device, dtype=f32).contiguous(),
+            value_eff.view(heads, cells, -1).contiguous(),
+            base.contiguous(),
+        )
     layer._b200_exact_eval_cache = (key, params)
     return params
 
