@@ -1,31 +1,37 @@
 """Throughput of tropnn's routed-layer hot path on B200 (backend="b200").
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--secondary NAME]
+                    [--impl b200|reference]
 
 Metric: rows/s of TropLinear / PairwiseLinear forward + backward. The
-default workload is BASELINE config 2: PairwiseLinear(256->512, tables=16,
-comparisons=6, fast_sigmoid_odd, min-margin STE), fp32, forward + STE backward with an
-upstream gradient ~ N(0,1), 4096 rows per GPU (weak scaling; at N>1 each step ends
-with the NCCL all-reduce of the parameter gradients). Other workloads are selectable
-with --workload. Data are seeded synthetic tensors of the configured shapes.
+default workload is BASELINE config 5, the configuration the metric is quoted on: the
+TropLinear(4096->4096, heads=1024, cells=16, code_dim=256) train step with f16 parameters
+(forward, min-face backward of an upstream gradient ~ N(0,1), every parameter gradient)
+on a global batch of 16384 rows, split evenly over the N GPUs (strong scaling; at N>1 each
+step ends with the all-reduce of the parameter gradients). The config 5
+PairwiseLinear(4096->4096, tables=1024, comparisons=8) train step follows as a second keyed
+result (``secondary``). Other workloads are selectable with --workload. Data are seeded
+synthetic tensors of the configured shapes.
 
 One step = (untimed L2 flush) -> [timed: zero grads, forward, backward, grad
 all-reduce]. W warm-up steps, then exactly K timed steps bracketed by barrier +
 synchronize, each timed with CUDA events on the launching stream; the max over ranks
 is reported. ``e2e`` repeats the step through the same public API with the inputs
 copied from pinned host memory and the output + input gradient copied back inside the
-timed region, the copies of neighbouring steps overlapping the compute on two copy
-streams (a prefetching input pipeline; every step's copies and L2 flush are inside the
-timed span); ``e2e_serial`` is the same with each step's copies and compute in sequence.
-``roofline`` is the dominant kernel's algorithmic bytes per launch over
-its mean CUDA-event duration in the timed region. ``cpu_baseline`` times the reference's
-CPU path (below) on the host cores (rank 0, N=1 only).
+timed region, in two forms: a prefetching pipeline (the copies of neighbouring steps
+overlap the compute on two copy streams; every step's copies and L2 flush are inside the
+timed span) and each step in sequence; ``e2e`` is the faster, ``e2e_modes`` has both.
+``roofline`` is the dominant kernel's algorithmic work per launch over its mean
+CUDA-event duration in the timed region. ``cpu_baseline`` times the reference's CPU path
+(below) on the host cores (rank 0, N=1 only).
 
-``--impl reference`` runs the CPU arm: the oracle port of the reference's CPU path, on all
-host threads, on a bounded row sample per step; under torchrun only rank 0 runs it. Both
-CPU legs time the reference's faster CPU path on the workload (``--cpu-impl auto``): the
-numpy oracle of its torch path, or for config 1 eval the C++ restatement of its Zig CPU
-inference kernels (``oracle/native_cpu.cpp``, ``backend="zig"``); ``--cpu-impl`` picks one.
+``--impl reference`` runs the CPU arm on rank 0 (the other ranks exit without work): the
+reference package's own torch CPU path (its default ``backend="torch"``), imported unmodified
+from where the reference arm installs it (``baseline/_ref``), on every host core through
+torch's threads, on a bounded row sample per step. Without that install it times the numpy
+port of the same path (``oracle/``) on all cores as single-threaded processes, and for config
+1 eval the C++ restatement of the reference's Zig CPU inference kernels (its faster CPU path
+there); ``--cpu-impl`` picks one.
 """
 
 from __future__ import annotations
@@ -50,6 +56,7 @@ if str(REPO) not in sys.path:
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
+METRIC = "TropLinear/PairwiseLinear rows/s fwd+bwd, 1-8 B200; % of HBM/TC roofline"
 PEAKS_PATH = REPO / "MEASURED_PEAKS.json"
 TRAFFIC_PATH = REPO / "profiles" / "traffic.json"
 FALLBACK_HBM_GBS = 6650.0
@@ -79,10 +86,31 @@ class Workload:
     # config 5 eval: the torch path's BLAS scores beat the Zig per-cell dot products.
     cpu_impl: str = "torch"
     hidden: int = 0  # classifiers: width of the hidden layer
+    # "weak": rows_per_gpu rows on every rank; "strong": rows_per_gpu is the global batch,
+    # split evenly over the ranks (config 5 is quoted on a fixed global batch).
+    scaling: str = "weak"
+
+    def rows_on_rank(self, world: int) -> int:
+        if self.scaling == "strong":
+            if self.rows_per_gpu % world:
+                raise SystemExit(f"{self.name}: global batch {self.rows_per_gpu} does not split over {world} ranks")
+            return self.rows_per_gpu // world
+        return self.rows_per_gpu
+
+    def global_rows(self, world: int) -> int:
+        return self.rows_per_gpu if self.scaling == "strong" else self.rows_per_gpu * world
+
+    # rows per step when the reference package's own torch path is timed (one process on every
+    # host core); 0 = the numpy-port sample size.
+    ref_sample_rows: int = 0
 
     @property
     def cpu_rows(self) -> int:
         return self.cpu_sample_rows or self.rows_per_gpu
+
+    @property
+    def ref_rows(self) -> int:
+        return self.ref_sample_rows or self.cpu_rows
 
     @property
     def classifier(self) -> bool:
@@ -159,24 +187,32 @@ WORKLOADS = {
         layer_kwargs=dict(tables=1024, comparisons=8),
         description="config 5: PairwiseLinear(4096->4096, T1024, C8), f16 params, train step, batch 16384",
         cpu_sample_rows=64,
+        scaling="strong",
+        ref_sample_rows=2,
     ),
     "trop_cfg5_eval": Workload(
         "trop_cfg5_eval", "trop", 4096, 4096, 65536, False, dtype="float16",
         layer_kwargs=dict(heads=1024, cells=16, code_dim=256),
         description="config 5: TropLinear(4096->4096, H1024, K16, D256), f16 params, eval forward, batch 65536",
         cpu_sample_rows=256,
+        scaling="strong",
+        ref_sample_rows=64,
     ),
     "pairwise_cfg5_eval": Workload(
         "pairwise_cfg5_eval", "pairwise", 4096, 4096, 65536, False, dtype="float16",
         layer_kwargs=dict(tables=1024, comparisons=8),
         description="config 5: PairwiseLinear(4096->4096, T1024, C8), f16 params, eval forward, batch 65536",
         cpu_sample_rows=32,
+        scaling="strong",
+        ref_sample_rows=4,
     ),
     "trop_cfg5_train": Workload(
         "trop_cfg5_train", "trop", 4096, 4096, 16384, True, dtype="float16",
         layer_kwargs=dict(heads=1024, cells=16, code_dim=256),
         description="config 5: TropLinear(4096->4096, H1024, K16, D256), f16 params, train step (fwd + min-face bwd), batch 16384",
         cpu_sample_rows=32,
+        scaling="strong",
+        ref_sample_rows=16,
     ),
 }
 
@@ -536,21 +572,38 @@ def _pipelined_e2e(steps, layer, w, x_pin, g_pin, out_pins, reduce_grads, flush,
     return start.elapsed_time(end)
 
 
-def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
-    import tropnn_b200
-    from tropnn_b200.distributed import PeerAllReduce, fused_lut_allreduce
-
-    rank, world, local_rank = _dist_env()
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
+def _init_dist(device: torch.device, world: int) -> None:
     if world > 1:
         import datetime
 
         import torch.distributed as dist
 
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+
+
+def _end_dist(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
+    """One workload on this rank's GPU (process group already set up at N>1); rank 0 gets the
+    JSON line's fields, the other ranks None."""
+    import dataclasses
+
+    import tropnn_b200
+    from tropnn_b200.distributed import PeerAllReduce, fused_lut_allreduce
+
+    rank, world, local_rank = _dist_env()
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
     tropnn_b200._native.load()
-    layer = w.build().to(device).train(w.train)
+    # This rank's share of the step: the whole per-GPU batch (weak scaling) or an even slice
+    # of the global batch (strong scaling).
+    w_rank = dataclasses.replace(w, rows_per_gpu=w.rows_on_rank(world), scaling="weak")
+    layer = w_rank.build().to(device).train(w.train)
     if w.classifier:
         # Adam as the reference example trains (examples/emnist.py:310, AdamW with weight_decay 0),
         # capturable so that the whole step goes into one CUDA graph.
@@ -575,28 +628,27 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
                         peer_lut = PeerAllReduce(cap)
                         stack.enter_context(fused_lut_allreduce(peer_lut))
         try:
-            return _run_b200_body(args, w, rank, world, device, layer, peer)
+            return _run_b200_body(args, w, w_rank, rank, world, device, layer, peer)
         finally:
             stack.close()
             if peer_lut is not None:
                 peer_lut.close()
             if peer is not None:
                 peer.close()
-            if world > 1:
-                import torch.distributed as dist
-
-                dist.destroy_process_group()
+            del layer
+            torch.cuda.synchronize(device)
+            torch.cuda.empty_cache()
 
 
 def _run_b200_body(
-    args: argparse.Namespace, w: Workload, rank: int, world: int, device: torch.device, layer, peer
+    args: argparse.Namespace, w: Workload, w_rank: Workload, rank: int, world: int, device: torch.device, layer, peer
 ) -> dict | None:
     from tropnn_b200.distributed import fused_lut_peer
 
     from tropnn_b200 import trace
     from tropnn_b200.distributed import allreduce_gradients
 
-    x_host, g_host = _make_inputs(w, rank, device)
+    x_host, g_host = _make_inputs(w_rank, rank, device)
     x = x_host.to(device).requires_grad_(_input_grad(w))
     g = g_host.to(device)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
@@ -657,7 +709,7 @@ def _run_b200_body(
     # (+ input gradient) copied back inside the timed region.
     x_pin = x_host.pin_memory()
     g_pin = g_host.pin_memory()
-    out_pins = _result_buffers(w, x_host)
+    out_pins = _result_buffers(w_rank, x_host)
     h2d = x_pin.numel() * x_pin.element_size() + (g_pin.numel() * g_pin.element_size() if w.train else 0)
     d2h = sum(b.numel() * b.element_size() for b in out_pins)
 
@@ -685,20 +737,25 @@ def _run_b200_body(
     if rank != 0:
         return None
 
-    rows_total = w.rows_per_gpu * world
+    rows_total = w.global_rows(world)
     value = rows_total * args.steps / (total_ms / 1e3)
-    e2e_value = rows_total * args.steps / (e2e_ms / 1e3)
+    # e2e: the faster of the two end-to-end modes (the pipeline wins when the host copies
+    # dominate, the serial form when host launch work does).
+    e2e_modes = {"pipelined": e2e_ms, "serial": e2e_serial_ms}
+    e2e_mode = min(e2e_modes, key=e2e_modes.get)
+    e2e_value = rows_total * args.steps / (e2e_modes[e2e_mode] / 1e3)
 
     peaks, peaks_kind = _peaks()
     traffic_table = json.loads(TRAFFIC_PATH.read_text()).get(w.name, {}) if TRAFFIC_PATH.exists() else {}
     per_kernel_roofline = {}
     for name, stats in kernels.items():
-        rl = kernel_roofline(w, name, w.rows_per_gpu, peaks)
+        rl = kernel_roofline(w, name, w_rank.rows_per_gpu, peaks)
         if rl is None:
             continue
         bound, work, unit, peak, peak_label = rl
         mean_s = stats["mean_ms"] / 1e3
         achieved = work / mean_s / (1e12 if bound == "tensor" else 1e9)
+        traffic = traffic_table.get(name)
         per_kernel_roofline[name] = {
             "kernel": name,
             "bound": bound,
@@ -707,10 +764,14 @@ def _run_b200_body(
             "peak_source": f"{peaks_kind} {peak_label}",
             "unit": unit,
             "frac": round(achieved / peak, 3),
-            "traffic": traffic_table.get(name),
+            "traffic": traffic.get("bytes") if isinstance(traffic, dict) else traffic,
             ("algorithmic_flops_per_launch" if bound == "tensor" else "algorithmic_bytes_per_launch"): work,
             "mean_launch_us": round(mean_s * 1e6, 2),
         }
+        if isinstance(traffic, dict):
+            # ncu figures of one capture of the same kernel (profiles/): L2 throughput and the
+            # DRAM bytes behind a logical-bytes fraction above 1 (L2-resident tables).
+            per_kernel_roofline[name]["ncu"] = {k: v for k, v in traffic.items() if k != "bytes"}
     roofline = None
     if per_kernel_roofline:
         top = max(per_kernel_roofline, key=lambda k: kernels[k]["total_ms"])
@@ -718,7 +779,7 @@ def _run_b200_body(
     step_kernel_ms = sum(v["total_ms"] for v in kernels.values()) / args.steps
 
     return {
-        "metric": "TropLinear/PairwiseLinear rows/s fwd+bwd, 1-8 B200; % of HBM/TC roofline",
+        "metric": METRIC,
         "value": round(value, 1),
         "unit": "rows/s",
         "n_gpus": world,
@@ -726,13 +787,13 @@ def _run_b200_body(
         "warmup": args.warmup,
         "ms_per_step": round(total_ms / args.steps, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": w.scaling,
         "vs_baseline": None,
         "dtype": "f32" if w.dtype == "float32" else "f16 params / f32 accumulate",
         "data": "synthetic (seeded N(0,1) inputs and upstream grads; seeded default init)",
         "config": {
             "workload": w.description,
-            "rows_per_gpu": w.rows_per_gpu,
+            "rows_per_gpu": w_rank.rows_per_gpu,
             "global_batch": rows_total,
             "parallelism": (
                 f"dp{world} (batch-row shards, {'NVLink peer-memory' if peer is not None else 'NCCL'} grad all-reduce"
@@ -751,20 +812,19 @@ def _run_b200_body(
             "unit": "rows/s",
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "ms_per_step": round(e2e_ms / args.steps, 4),
+            "ms_per_step": round(e2e_modes[e2e_mode] / args.steps, 4),
+            "mode": e2e_mode,
             "path": (
                 ("eager module API, pinned x and labels in, loss out" if w.classifier
                  else "eager module API, pinned host inputs in, output + input gradient out")
-                + "; copies of neighbouring steps overlap the compute on two copy streams; L2 flush per step "
-                "inside the span"
+                + ("; copies of neighbouring steps overlap the compute on two copy streams; L2 flush per step "
+                   "inside the span" if e2e_mode == "pipelined"
+                   else "; each step's copies and compute in sequence (untimed L2 flush between steps)")
+                + "; the faster of the pipelined and serial modes (both below)"
             ),
         },
-        "e2e_serial": {
-            "value": round(rows_total * args.steps / (e2e_serial_ms / 1e3), 1),
-            "unit": "rows/s",
-            "ms_per_step": round(e2e_serial_ms / args.steps, 4),
-            "path": "as e2e, each step's copies and compute in sequence (untimed L2 flush between steps)",
-        },
+        "e2e_modes": {k: {"value": round(rows_total * args.steps / (v / 1e3), 1), "unit": "rows/s",
+                          "ms_per_step": round(v / args.steps, 4)} for k, v in e2e_modes.items()},
         "gpu_launches": launches_per_step * args.steps,
         "kernels": {k: {"launches_per_step": v["launches"] // args.steps, "mean_us": round(v["mean_ms"] * 1e3, 2)}
                     for k, v in kernels.items()},
@@ -868,25 +928,102 @@ def _zig_port_usable() -> str | None:
     return None
 
 
+def reference_package_root() -> Path | None:
+    """Directory holding the reference package ``tropnn`` as installed for the reference arm
+    (``pip install --no-deps --target baseline/_ref <reference source>``), or the directory named
+    by ``TROPNN_REFERENCE``; None when neither has it."""
+    for root in (os.environ.get("TROPNN_REFERENCE"), str(REPO / "baseline" / "_ref")):
+        if root and (Path(root) / "tropnn" / "__init__.py").is_file():
+            return Path(root)
+    return None
+
+
 def cpu_impl_for(w: Workload, requested: str) -> str:
-    """The CPU path a leg times: with "auto" the reference's faster path on the workload
-    (``Workload.cpu_impl``); "zig" (the C++ restatement of the Zig inference kernels) exists for
-    eval workloads only."""
+    """The CPU path a leg times. "auto": the reference's faster CPU path on the workload: its own
+    torch path imported from the installed reference package ("reference") when present, else
+    the numpy port of it ("torch"), and for config 1 eval the C++ restatement of its Zig CPU
+    inference kernels ("zig", eval workloads only)."""
     if requested == "zig" and w.train:
         raise SystemExit(f"--cpu-impl zig: {w.name} is a training workload; the Zig kernels are inference only")
-    impl = ("torch" if w.train else w.cpu_impl) if requested == "auto" else requested
-    if impl == "zig" and requested == "auto":
+    if requested == "reference" and reference_package_root() is None:
+        raise SystemExit("--cpu-impl reference: the reference package is not installed under baseline/_ref")
+    if requested != "auto":
+        return requested
+    if not w.train and w.cpu_impl == "zig":
         why = _zig_port_usable()
-        if why is not None:
-            print(f"warning: the Zig-kernel port is unusable here ({why}); timing the torch port", file=sys.stderr)
-            return "torch"
-    return impl
+        if why is None:
+            return "zig"
+        print(f"warning: the Zig-kernel port is unusable here ({why}); timing the torch path", file=sys.stderr)
+    return "reference" if reference_package_root() is not None else "torch"
 
 
 _CPU_IMPL_TEXT = {
+    "reference": "the reference package's own torch CPU path (backend='torch'), unmodified",
     "torch": "numpy oracle of the reference torch CPU path",
     "zig": "C++ restatement of the reference's Zig CPU inference kernels, backend='zig'",
 }
+
+
+def _reference_module(w: Workload):
+    """The workload's layer (or classifier) built from the reference package's own classes with
+    their default torch backend, same seeds and dtype as the b200 arm."""
+    root = reference_package_root()
+    if str(root) not in sys.path:
+        sys.path.append(str(root))
+    import tropnn
+
+    if w.classifier:
+        cls = tropnn.TropLinear if w.kind == "trop_clf" else tropnn.PairwiseLinear
+        dims = [w.in_features, w.hidden, w.out_features]
+        model = _Classifier([cls(a, b, seed=i, **w.layer_kwargs) for i, (a, b) in enumerate(zip(dims[:-1], dims[1:]))])
+        model.optimizer = torch.optim.Adam(model.parameters(), lr=1e-3)
+        return model.train()
+    cls = tropnn.PairwiseLinear if w.kind == "pairwise" else tropnn.TropLinear
+    layer = cls(w.in_features, w.out_features, seed=0, **w.layer_kwargs)
+    if w.dtype == "float16":
+        layer = layer.half()
+    return layer.train(w.train)
+
+
+def time_reference_torch(w: Workload, sample_rows: int, *, reps: int | None = None, budget_s: float = 10.0,
+                         warmup: int = 1) -> dict:
+    """rows/s of the reference package's own torch path on ``sample_rows`` rows per step, in this
+    process with torch's intra-op threads on every host core: eval = no_grad forward; train =
+    zero grads, forward, backward of the upstream gradient; classifiers = forward, cross-entropy,
+    backward, Adam step."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    module = _reference_module(w)
+    gen = torch.Generator().manual_seed(7)
+    if w.classifier:
+        x = torch.rand(sample_rows, w.in_features, generator=gen)
+        g = torch.randint(0, w.out_features, (sample_rows,), generator=gen)
+    else:
+        x = torch.randn(sample_rows, w.in_features, generator=gen)
+        g = torch.randn(sample_rows, 1, w.out_features, generator=gen)
+
+    def step() -> None:
+        if w.classifier:
+            module.optimizer.zero_grad(set_to_none=True)
+            torch.nn.functional.cross_entropy(module(x), g).backward()
+            module.optimizer.step()
+        elif w.train:
+            for p in module.parameters():
+                p.grad = None
+            xi = x.detach().requires_grad_(True)
+            module(xi).backward(g)
+        else:
+            with torch.no_grad():
+                module(x)
+
+    for _ in range(max(1, warmup)):
+        step()
+    done = 0
+    t0 = time.perf_counter()
+    while (reps is not None and done < reps) or (reps is None and (done == 0 or time.perf_counter() - t0 < budget_s)):
+        step()
+        done += 1
+    dt = time.perf_counter() - t0
+    return {"rows_per_s": sample_rows * done / dt, "seconds": dt, "steps": done, "threads": torch.get_num_threads()}
 
 
 def _oracle_step(w: Workload, params: dict, layer, x: np.ndarray, g: np.ndarray, impl: str = "torch") -> None:
@@ -978,6 +1115,17 @@ def time_cpu(w: Workload, sample_rows: int, workers: int, *, reps: int | None = 
 
 
 def cpu_baseline(w: Workload, budget_s: float, impl: str = "torch") -> dict:
+    if impl == "reference":
+        sample = w.ref_rows
+        res = time_reference_torch(w, sample, budget_s=budget_s, warmup=1)
+        return {
+            "value": round(res["rows_per_s"], 1),
+            "unit": "rows/s",
+            "cores": res["threads"],
+            "kind": "reference",
+            "sample": f"{res['steps']} steps x {sample} rows of {w.name} ({_CPU_IMPL_TEXT[impl]}), "
+            f"{res['seconds']:.1f} s, {res['threads']} torch threads",
+        }
     workers = os.cpu_count() or 1
     sample = w.cpu_rows
     res = time_cpu(w, sample, workers, budget_s=budget_s, warmup=2, impl=impl)
@@ -995,13 +1143,21 @@ def run_reference(args: argparse.Namespace, w: Workload) -> dict | None:
     rank, world, _ = _dist_env()
     if rank != 0:
         return None
-    threads = os.cpu_count() or 1
-    sample = w.cpu_rows
     impl = cpu_impl_for(w, args.cpu_impl)
-    res = time_cpu(w, sample, threads, reps=args.steps, warmup=args.warmup, impl=impl)
+    if impl == "reference":
+        sample = w.ref_rows
+        res = time_reference_torch(w, sample, reps=args.steps, warmup=args.warmup)
+        cores, kind = res["threads"], "reference"
+        how = f"{res['threads']} torch threads in one process"
+    else:
+        cores = os.cpu_count() or 1
+        sample = w.cpu_rows
+        res = time_cpu(w, sample, cores, reps=args.steps, warmup=args.warmup, impl=impl)
+        kind = "port"
+        how = f"{cores} single-threaded processes"
     value = res["rows_per_s"]
     return {
-        "metric": "TropLinear/PairwiseLinear rows/s fwd+bwd, 1-8 B200; % of HBM/TC roofline",
+        "metric": METRIC,
         "impl": "reference",
         "value": round(value, 1),
         "unit": "rows/s",
@@ -1010,7 +1166,7 @@ def run_reference(args: argparse.Namespace, w: Workload) -> dict | None:
         "warmup": args.warmup,
         "ms_per_step": round(res["seconds"] / args.steps * 1e3, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": w.scaling,
         "vs_baseline": None,
         "dtype": "f32" if w.dtype == "float32" else "f16 params / f32 accumulate",
         "data": "synthetic (seeded N(0,1) inputs and upstream grads; seeded default init)",
@@ -1018,10 +1174,9 @@ def run_reference(args: argparse.Namespace, w: Workload) -> dict | None:
         "cpu_baseline": {
             "value": round(value, 1),
             "unit": "rows/s",
-            "cores": threads,
-            "kind": "port",
-            "sample": f"{args.steps} steps x {sample} rows ({_CPU_IMPL_TEXT[impl]}, "
-            f"{threads} single-threaded processes)",
+            "cores": cores,
+            "kind": kind,
+            "sample": f"{args.steps} steps x {sample} rows ({_CPU_IMPL_TEXT[impl]}, {how})",
         },
         "e2e": {"value": round(value, 1), "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -1032,17 +1187,23 @@ def main(argv: list[str] | None = None) -> int:
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=50)
     parser.add_argument("--warmup", type=int, default=10)
-    parser.add_argument("--workload", choices=sorted(WORKLOADS), default="pairwise_cfg2")
+    parser.add_argument("--workload", choices=sorted(WORKLOADS), default="trop_cfg5_train")
+    parser.add_argument(
+        "--secondary", choices=["none", *sorted(WORKLOADS)], default="pairwise_cfg5_train",
+        help="a second workload timed after the first (same GPUs, same K/W), reported under 'secondary' "
+        "(default: the config 5 PairwiseLinear train step beside the config 5 TropLinear one)",
+    )
     parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
     parser.add_argument("--cpu-budget-s", type=float, default=10.0, help="seconds of CPU-baseline timing (rank 0, N=1)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument(
-        "--cpu-impl", choices=["auto", "torch", "zig"], default="auto",
-        help="CPU path of the cpu_baseline leg and the reference arm: torch = numpy oracle of the reference "
-        "torch path; zig = C++ restatement of its Zig inference kernels (eval workloads only); auto = the "
-        "reference's faster CPU path on the workload (zig for config 1, torch otherwise)",
+        "--cpu-impl", choices=["auto", "reference", "torch", "zig"], default="auto",
+        help="CPU path of the cpu_baseline leg and the reference arm: reference = the reference package's own "
+        "torch path (installed under baseline/_ref); torch = numpy port of that path; zig = C++ restatement of "
+        "its Zig inference kernels (eval workloads only); auto = the reference's faster CPU path on the workload",
     )
-    parser.add_argument("--rows", type=int, default=0, help="override the per-GPU row count (profiling runs)")
+    parser.add_argument("--rows", type=int, default=0, help="override the row count (per GPU, or global for "
+                        "strong-scaling workloads; profiling runs)")
     parser.add_argument(
         "--fuse-lut-allreduce", type=int, choices=[0, 1], default=0,
         help="with the peer all-reduce, average the Pairwise LUT gradient inside its kernel (1) or after the "
@@ -1056,19 +1217,36 @@ def main(argv: list[str] | None = None) -> int:
     args = parser.parse_args(argv)
     if args.warmup < 3 and args.impl == "b200":
         parser.error("--warmup must be >= 3")
-    w = WORKLOADS[args.workload]
-    if args.rows > 0:
-        import dataclasses
+    import dataclasses
 
-        w = dataclasses.replace(w, rows_per_gpu=args.rows, description=f"{w.description} [rows overridden: {args.rows}]")
-    _, world, _ = _dist_env()
+    def workload(name: str) -> Workload:
+        w = WORKLOADS[name]
+        if args.rows > 0:
+            w = dataclasses.replace(w, rows_per_gpu=args.rows, description=f"{w.description} [rows overridden: {args.rows}]")
+        return w
+
+    w = workload(args.workload)
+    _, world, local_rank = _dist_env()
     if world != args.gpus:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}; reporting WORLD_SIZE", file=sys.stderr)
 
     if args.impl == "reference":
         line = run_reference(args, w)
     else:
-        line = run_b200(args, w)
+        device = torch.device("cuda", local_rank)
+        torch.cuda.set_device(device)
+        _init_dist(device, world)
+        try:
+            line = run_b200(args, w)
+            if args.secondary != "none" and args.secondary != args.workload:
+                second = run_b200(args, workload(args.secondary))
+                if line is not None and second is not None:
+                    line["secondary"] = {k: second[k] for k in (
+                        "value", "unit", "ms_per_step", "scaling", "dtype", "config", "e2e", "e2e_modes",
+                        "gpu_launches", "kernels", "roofline", "kernel_rooflines", "clocks")}
+                    line["gpu_launches_secondary"] = second["gpu_launches"]
+        finally:
+            _end_dist(world)
         if line is not None and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w, args.cpu_budget_s, cpu_impl_for(w, args.cpu_impl))
     if line is not None:

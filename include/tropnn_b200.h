@@ -233,9 +233,14 @@ TROPNN_B200_API int tropnn_b200_pairwise_backward(const float *grad_out, int64_t
  * larger are rejected with TROPNN_B200_ERR_INVALID. The buffer is shared by every call on
  * a GPU: calls that can overlap on that GPU (different streams, threads or processes
  * sharing the context) race on it and must be serialised by the caller. The first call
- * on each device looks up the buffer's device address (cudaGetSymbolAddress) and caches
- * it; make that first call before any stream capture. Each GPU on which it has run keeps
- * the 8 MiB until the process exits. Arguments and results as tropnn_b200_pairwise_backward.
+ * on each device (and again after that device's context was destroyed and recreated)
+ * looks up the buffer's device address (cudaGetSymbolAddress) and caches it with the
+ * context's id; make that first call before any stream capture. The 8 MiB are reserved on
+ * a GPU when the library's module loads there (on first use of its kernels with lazy
+ * module loading, the default; at context creation on every device with
+ * CUDA_MODULE_LOADING=EAGER), whether or not this entry point is called, and are held
+ * until the process exits. Invalid sizes are rejected with TROPNN_B200_ERR_INVALID before
+ * the size check. Arguments and results as tropnn_b200_pairwise_backward.
  */
 TROPNN_B200_API int tropnn_b200_pairwise_backward_noalloc(const float *grad_out, int64_t items, int64_t out_features,
                                           float output_scale, const int64_t *indices, const float *margins,

@@ -335,20 +335,22 @@ def pairwise_backward(
     use_min_margin_ste: bool,
     surrogate: str = "fast_sigmoid_odd",
     ste: bool = True,
+    lut_grad: bool = True,
 ) -> dict[str, np.ndarray | None]:
     """Autograd of PairwiseLinear's torch path (layers/pairwise.py:137-200, 243-248).
 
     grad_lut[t, idx] += g (the STE term's forward factor is 0, so it adds nothing);
     with ``ste``: min mode r* = argmin |u| (first on ties), nb = idx ^ 2^r*,
     gu = <g, lut[t,nb] - lut[t,idx]> S(u_r*), grad_x[a] += gu, grad_x[b] -= gu,
-    grad_theta[t,r*] -= gu; full mode does every r.
+    grad_theta[t,r*] -= gu; full mode does every r. ``lut_grad=False`` skips the LUT
+    gradient (``"lut"`` is None), so that large layers can be checked row chunk by row chunk.
     """
     g = (_f32(grad_out) * F32(output_scale)).astype(F32) if output_scale != 1.0 else _f32(grad_out)
     lut32 = _f32(lut)
     tables, table_size, out_features = lut32.shape
     n = g.shape[0]
-    grad_lut = np.zeros_like(lut32)
-    for t in range(tables):
+    grad_lut = np.zeros_like(lut32) if lut_grad else None
+    for t in range(tables if lut_grad else 0):
         # index_select backward: the rows of g summed per selected LUT row (a stable
         # sort groups each bucket's rows in ascending row order, then one reduceat).
         idx_t = indices[:, t]

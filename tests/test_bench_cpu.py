@@ -73,8 +73,10 @@ def test_reference_arm_line_keeps_the_contract(monkeypatch) -> None:
 def test_cpu_path_choice_and_e2e_buffers(monkeypatch) -> None:
     W = bench.WORKLOADS
     monkeypatch.setattr(torch.Tensor, "pin_memory", lambda self: self)  # no driver here: shapes only
-    assert bench.cpu_impl_for(W["pairwise_cfg2"], "auto") == "torch"  # training: the torch path only
-    assert bench.cpu_impl_for(W["trop_cfg5_eval"], "auto") == "torch"  # BLAS scores beat the Zig dots there
+    # Training and config 5: the reference's torch path, itself when installed, else its port.
+    torch_path = "reference" if bench.reference_package_root() is not None else "torch"
+    assert bench.cpu_impl_for(W["pairwise_cfg2"], "auto") == torch_path
+    assert bench.cpu_impl_for(W["trop_cfg5_eval"], "auto") == torch_path  # BLAS scores beat the Zig dots there
     assert bench.cpu_impl_for(W["trop_cfg1"], "auto") == "zig"
     with pytest.raises(SystemExit):
         bench.cpu_impl_for(W["pairwise_cfg2"], "zig")
@@ -84,3 +86,28 @@ def test_cpu_path_choice_and_e2e_buffers(monkeypatch) -> None:
     assert [tuple(b.shape) for b in bench._result_buffers(W["trop_cfg3_clf"], torch.empty(512, 784))] == [(1,)]
     assert bench._input_grad(W["pairwise_cfg2"]) and not bench._input_grad(W["trop_cfg3_clf"])
     assert not bench._input_grad(W["trop_cfg1"])
+
+
+def test_workload_scaling_splits_the_global_batch() -> None:
+    W = bench.WORKLOADS
+    assert W["trop_cfg5_train"].scaling == "strong"
+    assert [W["trop_cfg5_train"].rows_on_rank(n) for n in (1, 2, 4, 8)] == [16384, 8192, 4096, 2048]
+    assert W["trop_cfg5_train"].global_rows(8) == 16384
+    assert W["pairwise_cfg2"].rows_on_rank(4) == 4096 and W["pairwise_cfg2"].global_rows(4) == 4 * 4096
+
+
+def test_reference_arm_times_the_reference_package_itself(monkeypatch) -> None:
+    """With the reference installed, --impl reference times its own torch path (kind
+    "reference"), here on a tiny config 2 sample."""
+    import argparse
+    import dataclasses
+
+    if bench.reference_package_root() is None:
+        pytest.skip("the reference package is not installed under baseline/_ref")
+    monkeypatch.setenv("RANK", "0")
+    monkeypatch.setenv("WORLD_SIZE", "1")
+    w = dataclasses.replace(bench.WORKLOADS["pairwise_cfg2"], ref_sample_rows=16)
+    line = bench.run_reference(argparse.Namespace(steps=2, warmup=1, cpu_impl="auto"), w)
+    assert line["impl"] == "reference" and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "reference" and "torch threads" in line["cpu_baseline"]["sample"]
+    assert line["config"]["rows_per_step_sample"] == 16

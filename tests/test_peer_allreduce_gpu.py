@@ -2,7 +2,7 @@
 and 8 GPUs (one-shot on two ranks, two-shot above): sums and averages of several f32 tensors
 match the exact result on every rank, results are bit-identical across ranks, repeated calls
 and CUDA-graph replays stay in step, and NCCL-free calls leave the device error word clear.
-Each world size is skipped with fewer GPUs (the round-end GPU tests run on one)."""
+Each world size is skipped on a machine with fewer GPUs."""
 
 from __future__ import annotations
 

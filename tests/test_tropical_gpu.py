@@ -80,8 +80,19 @@ def _check_against_oracle(layer: tropnn_b200.TropLinear, x: np.ndarray, g: np.nd
     win, _ = route_gate(fwd["scores"])
     assert np.array_equal(got["winner"][win], fwd["winner"][win])
     assert rel_err(got["margins"], fwd["margins"]) <= max(tol, 1e-5)
-    if not np.array_equal(got["winner"], fwd["winner"]):
-        pytest.skip("a near-tie route flipped; value comparison needs identical routes")
+    agree = (got["winner"] == fwd["winner"]).all(axis=1)
+    if not agree.all():
+        # A route outside the parity gate (a near tie) flipped. Rows are independent, so the
+        # values are compared on the rows whose routes all agree, by running both sides again
+        # on those rows alone; flips must stay rare.
+        assert int((~agree).sum()) <= max(1, x.shape[0] // 100), f"{int((~agree).sum())} rows with flipped routes"
+        keep = np.nonzero(agree)[0]
+        x, g = x[keep], g[keep]
+        for p in layer.parameters():
+            p.grad = None
+        fwd = oracle.trop_linear_forward(x, st, code_scale=layer.code_scale, training=train, param_dtype=pdt)
+        got = _run(layer, x, g, train=train)
+        assert np.array_equal(got["winner"], fwd["winner"])
     assert rel_err(got["y"], fwd["y"]) <= tol
     ref = oracle.trop_linear_backward(g, x, st, fwd, code_scale=layer.code_scale, training=train, param_dtype=pdt)
     assert rel_err(got["grad.x"], ref["x"]) <= tol

@@ -46,17 +46,18 @@ def _outputs(layer: tropnn_b200.PairwiseLinear, rows: int):
 def _backward(layer, rows, g, idx, u, *, noalloc: bool):
     lib = nat.load()
     gx, gthr, glut = _outputs(layer, rows)
+    use_min = int(layer.use_min_margin_ste)
     common = (
         g.data_ptr(), rows, layer.out_features, layer.output_scale, idx.data_ptr(), u.data_ptr(),
         layer.anchors.data_ptr(), layer.tables, layer.comparisons, layer.in_features, layer.lut.data_ptr(), nat.F32,
-        1, nat.SURROGATES["fast_sigmoid_odd"], gx.data_ptr(), gthr.data_ptr(), nat.F32, glut.data_ptr(),
+        use_min, nat.SURROGATES["fast_sigmoid_odd"], gx.data_ptr(), gthr.data_ptr(), nat.F32, glut.data_ptr(),
     )
     stream = torch.cuda.current_stream().cuda_stream
     if noalloc:
         status = lib.tropnn_b200_pairwise_backward_noalloc(*common, stream)
     else:
         ws_bytes = lib.tropnn_b200_pairwise_backward_workspace_size(rows, layer.tables, layer.comparisons,
-                                                                     layer.in_features, 1)
+                                                                     layer.in_features, use_min)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
         status = lib.tropnn_b200_pairwise_backward(*common, ws.data_ptr(), ws_bytes, stream)
     nat.check(status, "pairwise backward")
@@ -64,10 +65,22 @@ def _backward(layer, rows, g, idx, u, *, noalloc: bool):
     return gx.cpu().numpy(), gthr.cpu().numpy(), glut.detach().cpu().numpy()
 
 
-def test_noalloc_backward_matches_workspace_backward_twice() -> None:
-    # Config 2's layer: PairwiseLinear(256 -> 512, T16, C6), 4096 rows (well inside 8 MiB).
-    layer = tropnn_b200.PairwiseLinear(256, 512, tables=16, comparisons=6, seed=0).cuda()
-    rows = 4096
+@pytest.mark.parametrize(
+    ("in_f", "out_f", "tables", "comparisons", "use_min", "rows"),
+    [
+        # Config 2's layer, 4096 rows: the one-kernel LUT gradient and the min-margin STE.
+        (256, 512, 16, 6, True, 4096),
+        # More than 1024 columns and the full STE: the bucket_sort + segment_rowsum LUT
+        # gradient, whose row permutation and bucket segments live in the fixed buffer, and
+        # the per-comparison STE gradients (rows x tables x comparisons floats).
+        (96, 1100, 12, 5, False, 2048),
+    ],
+)
+def test_noalloc_backward_matches_workspace_backward_twice(in_f, out_f, tables, comparisons, use_min, rows) -> None:
+    layer = tropnn_b200.PairwiseLinear(in_f, out_f, tables=tables, comparisons=comparisons, seed=0,
+                                       use_min_margin_ste=use_min).cuda()
+    need = nat.load().tropnn_b200_pairwise_backward_workspace_size(rows, tables, comparisons, in_f, int(use_min))
+    assert 0 < need <= (8 << 20)
     for call, seed in enumerate((11, 12)):  # two calls in a row, different inputs
         g, idx, u = _forward(layer, seed, rows)
         want = _backward(layer, rows, g, idx, u, noalloc=False)
@@ -87,4 +100,14 @@ def test_noalloc_backward_rejects_problems_beyond_its_buffer() -> None:
         None, None, nat.F32, None, torch.cuda.current_stream().cuda_stream,
     )
     with pytest.raises(ValueError, match="fixed 8388608-byte buffer"):
+        nat.check(status, "pairwise_backward_noalloc")
+
+
+def test_noalloc_backward_rejects_bad_sizes() -> None:
+    lib = nat.load()
+    status = lib.tropnn_b200_pairwise_backward_noalloc(
+        None, 16, 16, 1.0, None, None, None, 0, 4, 32, None, nat.F32, 1, 0,
+        None, None, nat.F32, None, torch.cuda.current_stream().cuda_stream,
+    )
+    with pytest.raises(ValueError, match="bad sizes"):
         nat.check(status, "pairwise_backward_noalloc")

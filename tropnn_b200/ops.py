@@ -59,6 +59,14 @@ def _require_f32(t: Tensor, what: str) -> None:
         raise TypeError(f"backend='b200' computes in float32; {what} has dtype {t.dtype}")
 
 
+def _check_target(target: str) -> None:
+    """The ``target`` keyword of the reference's TileLang wrappers (tilelang_route.py:688,
+    pairwise_tilelang.py:545): a compile target. The b200 kernels are prebuilt for sm_100a,
+    so any CUDA target selects them and anything else is refused."""
+    if not isinstance(target, str) or not target.split()[0:1] == ["cuda"]:
+        raise ValueError(f"backend='b200' runs prebuilt sm_100a kernels; target must be a CUDA target, got {target!r}")
+
+
 # ---------------------------------------------------------------------------
 # PairwiseLinear
 # ---------------------------------------------------------------------------
@@ -350,6 +358,7 @@ def pairwise_b200(
     *,
     use_min_margin_ste: bool,
     surrogate: str = "fast_sigmoid_odd",
+    target: str = "cuda",
     output_scale: float = 1.0,
     ste: bool = True,
     anchor_index: tuple[Tensor, Tensor] | None = None,
@@ -357,11 +366,14 @@ def pairwise_b200(
     """PairwiseLinear route + LUT sum with the STE backward, on sm_100a.
 
     Returns ``(out [B,S,out] f32, indices [B,S,T] int64, margins [B,S,T,C] f32)`` like
-    ``pairwise_tilelang``. ``output_scale`` is folded into the kernels (the
-    ``output * output_scale`` of layers/base.py:76-77); ``ste=False`` drops the
-    straight-through terms so ``latent``/``thresholds`` get no gradient, which is what the
-    torch path does outside training (layers/pairwise.py:245).
+    ``pairwise_tilelang``. ``target`` is the TileLang compile target of the reference's
+    signature: only CUDA targets are accepted (the kernels are prebuilt for sm_100a).
+    ``output_scale`` is folded into the kernels (the ``output * output_scale`` of
+    layers/base.py:76-77); ``ste=False`` drops the straight-through terms so
+    ``latent``/``thresholds`` get no gradient, which is what the torch path does outside
+    training (layers/pairwise.py:245).
     """
+    _check_target(target)
     if surrogate not in nat.SURROGATES:
         raise ValueError(f"Pairwise b200 backend does not support surrogate={surrogate!r}")
     _check_pairwise_args(latent, anchors, thresholds, lut)
@@ -748,6 +760,8 @@ def trop_route_hidden_b200(
     *,
     code_scale: float,
     training: bool = False,
+    target: str = "cuda",
+    score_route_max_bytes: int | None = None,
 ) -> tuple[Tensor, Tensor, Tensor]:
     """TropLinear route + selected-code sum with the min-face backward, on sm_100a.
 
@@ -758,7 +772,13 @@ def trop_route_hidden_b200(
     accumulation. Returns ``(hidden [B,S,D] f32, winner [B,S,H] int64, margins [B,S,H]
     f32)`` like ``trop_route_hidden_tilelang``. In eval mode (``training=False``) the output
     does not depend on the margins, so router gradients are ``None`` as in the torch path.
+    ``target`` (a CUDA compile target) and ``score_route_max_bytes`` (the reference's cap on
+    materialised score chunks, tilelang_route.py:689) are accepted for signature parity; the
+    fused kernels materialise no scores, so the cap only has to be valid.
     """
+    _check_target(target)
+    if score_route_max_bytes is not None and score_route_max_bytes < 0:
+        raise ValueError(f"score_route_max_bytes must be >= 0 when set, got {score_route_max_bytes}")
     hidden, winner, margins = trop_route_hidden_packed(
         latent, router_weight, router_bias, code, code_scale=code_scale, training=training, keep_margins=True
     )
