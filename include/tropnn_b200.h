@@ -273,6 +273,21 @@ TROPNN_B200_API int tropnn_b200_trop_route(const void *latent, int latent_dtype,
                            float *margins, void *stream);
 
 /*
+ * Input projection z = P(x) (layers/tropical.py:96-99, `proj(x.to(P.dtype))`) for half-precision
+ * projection weights: z[n, :] = half(sum_i half(x[n, i]) * P[:, i]) with f32 accumulation,
+ * z [items, code_dim] in param_dtype. x f32 [items, in_features] (in_features a multiple of 8),
+ * P [code_dim, in_features] in param_dtype (F16/BF16), code_dim in {64, 128, 192, 256}. One
+ * tcgen05 GEMM that rounds x to the parameter dtype on chip (no separate cast pass over x).
+ * With few row blocks the contraction is split across SMs into slices whose f32 partials go
+ * to `workspace` (tropnn_b200_trop_proj_workspace_size bytes; 0 when unsplit) and are summed
+ * in slice order (deterministic).
+ */
+TROPNN_B200_API size_t tropnn_b200_trop_proj_workspace_size(int64_t items, int64_t in_features, int64_t code_dim);
+TROPNN_B200_API int tropnn_b200_trop_proj(const float *x, int64_t items, int64_t in_features,
+                                          const void *proj_weight, int param_dtype, int64_t code_dim, void *z,
+                                          void *workspace, size_t workspace_bytes, void *stream);
+
+/*
  * hidden[n,:] = latent[n,:] + code_scale * sum_h chat[n,h,:] with chat = code[h,w] (eval)
  * or code[h,w] + U(m) (code[h,r] - code[h,w]), U(m) = 0.5/(1+|m|) (training)
  * (layers/tropical.py:131-138, routing.py:13-15). code in param_dtype; latent in

@@ -12,8 +12,7 @@
   map, and in training every gradient: projection, router weight and bias, code, output map).
   Rows are drawn from a seeded pool and kept where every head's route is pinned by the parity
   gate (winner, and in training the runner as well), so that the row-summed parameter
-  gradients are comparable; the count is rounded down to a multiple of 8 (the tensor-core
-  backward's row granularity).
+  gradients are comparable (a multiple of 8 rows: the tensor-core backward's granularity).
 
 Tolerance: 2e-2 relative (f16 parameters), the parity rule for half-precision layers.
 """
@@ -26,6 +25,7 @@ import torch
 
 import oracle
 import tropnn_b200
+import tropnn_b200.ops
 from oracle.tropnn_oracle import _round_to
 from tests.golden_cases import rel_err, route_gate, state_arrays
 
@@ -126,29 +126,55 @@ def trop_cfg5():
     return layer, state_arrays(layer)
 
 
-def _pinned_rows(st: dict, pool: np.ndarray, rows: int, train: bool) -> np.ndarray:
-    """The first ``rows`` rows of ``pool`` (a multiple of 8) whose routes the parity gate pins."""
-    z = _round_to(_round_to(pool, "float16") @ st["proj.weight"].astype(np.float32).T, "float16")
-    win, run = route_gate(oracle.trop_scores(z, st["router_weight"], st["router_bias"]))
+def _pinned_rows(st: dict, z_pool: np.ndarray, rows: int, train: bool, rel: float = 3e-4) -> np.ndarray:
+    """Indices of the first ``rows`` rows (a multiple of 8) whose routes clear the margin gate
+    at ``rel`` (three times the parity gate, so that the few-unit f32 differences of another
+    contraction split cannot undo it), judged on the scores of ``z_pool``."""
+    win, run = route_gate(oracle.trop_scores(z_pool, st["router_weight"], st["router_bias"]), rel=rel)
     keep = np.nonzero((run if train else win).all(axis=1))[0]
     assert keep.size >= rows, f"only {keep.size} pinned rows in the pool"
-    return pool[keep[:rows]]
+    return keep[:rows]
 
 
 @pytest.mark.parametrize("train", [True, False])
 def test_trop_config5_layer_matches_oracle(trop_cfg5, train: bool) -> None:
+    """The projection is checked on its own (z within one f16 unit of the oracle's rounded z
+    plus the f32 accumulation error: two summation orders can round a sum on a boundary
+    differently), and the route, code
+    sum, output map and every gradient are checked on the GPU's z, so that a one-unit z
+    difference cannot move a score across the margin gate."""
     layer, st = trop_cfg5
     rows = 512
     gen = torch.Generator().manual_seed(31 if train else 32)
-    x = _pinned_rows(st, torch.randn(2048, 4096, generator=gen).numpy(), rows, train)
+    pool = torch.randn(2048, 4096, generator=gen).numpy()
     g = torch.randn(rows, 4096, generator=gen).numpy()
     layer = layer.cuda().train(train)
+    z_oracle = _round_to(_round_to(pool, "float16") @ st["proj.weight"].astype(np.float32).T, "float16")
+    with torch.no_grad():
+        z_pool = tropnn_b200.ops.trop_project_b200(torch.from_numpy(pool).cuda(), layer.proj.weight).float().cpu().numpy()
+    # One f16 unit, plus the f32 accumulation error of the 4096-long contraction (~1e-5 of
+    # the largest |z|: it dominates where a sum cancels to near zero).
+    ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(z_oracle), 2.0**-14))) - 10)
+    bound = ulp + 3e-5 * float(np.abs(z_oracle).max())
+    assert np.all(np.abs(z_pool - z_oracle) <= bound), "projection beyond one f16 unit of the oracle"
+    keep = _pinned_rows(st, z_pool, rows, train)
+    x = pool[keep]
+    # z of exactly these rows as the layer computes it (the projection splits its contraction
+    # by row count, so a different batch can round a few sums differently).
+    with torch.no_grad():
+        z = tropnn_b200.ops.trop_project_b200(torch.from_numpy(x).cuda(), layer.proj.weight).float().cpu().numpy()
+    win, run = route_gate(oracle.trop_scores(z, st["router_weight"], st["router_bias"]))
+    assert (run if train else win).all(), "a selected row lost its margin"
     layer.zero_grad(set_to_none=True)
     xt = torch.from_numpy(x).cuda().requires_grad_(True)
     y = layer(xt)
     y.backward(torch.from_numpy(g).cuda().view_as(y))
     torch.cuda.synchronize()
-    fwd = oracle.trop_linear_forward(x, st, code_scale=layer.code_scale, training=train, param_dtype="float16")
+    # The oracle's forward from the GPU's z (tropical.py:131-146 after :96-99).
+    route = oracle.trop_route_hidden(z, st["router_weight"], st["router_bias"], st["code"], code_scale=layer.code_scale,
+                                     training=train)
+    fwd = {**route, "z": z,
+           "y": route["hidden"] @ st["output_proj.weight"].astype(np.float32).T + st["output_proj.bias"].astype(np.float32)}
     assert np.array_equal(layer._last_indices.cpu().numpy().reshape(rows, -1), fwd["winner"])
     assert rel_err(layer._last_margins.cpu().numpy().reshape(rows, -1), fwd["margins"]) <= HALF_TOL
     assert rel_err(y.detach().float().cpu().numpy().reshape(rows, -1), fwd["y"]) <= HALF_TOL

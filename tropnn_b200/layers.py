@@ -30,7 +30,9 @@ from .ops import (
     linear_f32out_eligible,
     pairwise_anchor_index,
     pairwise_b200,
+    proj_eligible,
     trop_exact_eval_b200,
+    trop_project_b200,
     trop_route_hidden_packed,
 )
 
@@ -157,10 +159,11 @@ def _trop_exact_eval_b200(layer: nn.Module, x: Tensor) -> Tensor:
 def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
     """Full TropLinear forward on sm_100a for any module with the TropLinear attributes.
 
-    The projection (tropical.py:96-99) is a dense cuBLAS GEMM through torch; the route
-    scores, top-2, code sum and their backward are the b200 kernels
-    (ops.trop_route_hidden_packed); the output map (tropical.py:140-146) is the b200
-    tensor-core linear map for half-precision weights (ops.linear_f32out_b200), else torch.
+    The projection (tropical.py:96-99) runs on the b200 tensor-core projection kernel for
+    half-precision weights (ops.trop_project_b200), else torch; the route scores, top-2, code
+    sum and their backward are the b200 kernels (ops.trop_route_hidden_packed); the output map
+    (tropical.py:140-146) is the b200 tensor-core linear map for half-precision weights
+    (ops.linear_f32out_b200), else torch.
     """
     if x.ndim == 2:
         x = x.unsqueeze(1)
@@ -177,7 +180,11 @@ def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
     input_dtype = x.dtype
     compute_dtype = _compute_dtype(x)
     _require_f32_compute(compute_dtype, "TropLinear")
-    z = layer.proj(x.to(dtype=layer.proj.weight.dtype))
+    if proj_eligible(x, layer.proj.weight):
+        # Half-precision projection weight: the tensor-core projection kernel rounds x on chip.
+        z = trop_project_b200(x, layer.proj.weight)
+    else:
+        z = layer.proj(x.to(dtype=layer.proj.weight.dtype))
     # The reference upcasts z to the compute dtype (tropical.py:99); with half-precision
     # parameters the b200 op takes z in that dtype instead (the upcast is exact and happens
     # in-kernel), which lets the route scores run on the tensor cores.

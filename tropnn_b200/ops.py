@@ -992,3 +992,89 @@ def linear_f32out_b200(hidden: Tensor, weight: Tensor, bias: Tensor | None) -> T
     with torch.cuda.device(hidden.device):
         out = _LinearF32OutFunction.apply(hidden.reshape(-1, hidden.shape[-1]), weight, bias)
     return out.reshape(*lead, weight.shape[0])
+
+
+# ---------------------------------------------------------------------------
+# TropLinear input projection
+# ---------------------------------------------------------------------------
+
+
+def proj_eligible(x: Tensor, weight: Tensor) -> bool:
+    """Shapes the tensor-core projection takes (tropnn_b200_trop_proj): f32 input, f16/bf16
+    weight [code_dim, in] with code_dim in {64, 128, 192, 256} and in a multiple of 8."""
+    code_dim, in_features = weight.shape
+    return (
+        x.is_cuda
+        and x.dtype == torch.float32
+        and weight.dtype in (torch.float16, torch.bfloat16)
+        and code_dim in (64, 128, 192, 256)
+        and in_features % 8 == 0
+        and x.shape[-1] == in_features
+    )
+
+
+def _launch_proj(x: Tensor, weight: Tensor) -> Tensor:
+    rows, in_features = x.shape
+    code_dim = weight.shape[0]
+    dev = x.device
+    lib = nat.load()
+    z = torch.empty((rows, code_dim), device=dev, dtype=weight.dtype)
+    ws_bytes = int(lib.tropnn_b200_trop_proj_workspace_size(rows, in_features, code_dim))
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8) if ws_bytes else None
+    _launch(
+        "trop_proj", lib.tropnn_b200_trop_proj, x.data_ptr(), rows, in_features, weight.data_ptr(),
+        nat.float_code(weight.dtype), code_dim, z.data_ptr(), nat.ptr(ws), ws_bytes, nat.stream_handle(dev),
+    )
+    return z
+
+
+class _TropProjFunction(torch.autograd.Function):
+    """z = proj(x.to(P.dtype)) (layers/tropical.py:96-99) for a half-precision P: forward on
+    the tcgen05 projection kernel (x rounded on chip, f32 accumulation, z rounded to P's dtype).
+    Backward of the reference's half-precision F.linear: grad_x = grad_z P on the tcgen05
+    linear map (f32 result; the reference rounds it to P's dtype and back, a difference below
+    that dtype's rounding), grad_P = grad_z^T half(x)."""
+
+    @staticmethod
+    def forward(ctx: Any, x: Tensor, weight: Tensor) -> Tensor:
+        xc = x.contiguous()
+        w = weight.contiguous()
+        z = _launch_proj(xc, w)
+        ctx.save_for_backward(xc, w)
+        return z
+
+    @staticmethod
+    def backward(ctx: Any, grad_z: Tensor) -> tuple[Tensor | None, Tensor | None]:
+        x, w = ctx.saved_tensors
+        rows, in_features = x.shape
+        code_dim = w.shape[0]
+        dev = x.device
+        g = grad_z.to(w.dtype).contiguous()
+        lib = nat.load()
+        stream = nat.stream_handle(dev)
+        grad_x = grad_w = None
+        if ctx.needs_input_grad[0]:
+            pdt = nat.float_code(w.dtype)
+            w_t = torch.empty((in_features, code_dim), device=dev, dtype=w.dtype)
+            _launch("trop_code_transpose", lib.tropnn_b200_trop_code_transpose, w.data_ptr(), pdt, code_dim, 1,
+                    in_features, w_t.data_ptr(), stream)
+            grad_x = torch.empty((rows, in_features), device=dev, dtype=torch.float32)
+            _launch("linear_f32out", lib.tropnn_b200_linear_f32out, g.data_ptr(), rows, 1, w_t.data_ptr(),
+                    in_features, code_dim, pdt, None, grad_x.data_ptr(), stream)
+        if ctx.needs_input_grad[1]:
+            grad_w = g.t().matmul(x.to(w.dtype))
+        return grad_x, grad_w
+
+
+def trop_project_b200(x: Tensor, weight: Tensor) -> Tensor:
+    """``proj(x.to(weight.dtype))`` for f32 ``x`` [..., in] and a half-precision ``weight``
+    [code_dim, in], on the tensor-core projection kernel; returns z [..., code_dim] in the
+    weight's dtype."""
+    if not proj_eligible(x, weight):
+        raise ValueError(
+            f"trop_project_b200: unsupported x {tuple(x.shape)} {x.dtype} / weight {tuple(weight.shape)} {weight.dtype}"
+        )
+    lead = x.shape[:-1]
+    with torch.cuda.device(x.device):
+        z = _TropProjFunction.apply(x.reshape(-1, x.shape[-1]), weight)
+    return z.reshape(*lead, weight.shape[0])
