@@ -288,6 +288,29 @@ TROPNN_B200_API int tropnn_b200_trop_proj(const float *x, int64_t items, int64_t
                                           void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * f32 matrix product on the tensor cores, for TropLinear's f32 parameters (the projection
+ * tropical.py:96-99 and output map :140-146 with their backward products, and the exact eval
+ * path's effective weights and base output, tropical_exact.py:257-358, all f32 GEMMs in the
+ * reference): c[i, j] = sum_{l<k} a[i*lda + l] * b[j*ldb + l] (+ bias[j]) for i < m, j < n,
+ * written to c[i*ldc + j]. lda and ldb multiples of 4, a and b 16-byte aligned; bias may be
+ * NULL. Each operand is split into two tf32 parts and three tcgen05 kind::tf32 products are
+ * summed (3xTF32: f32 range, ~2^-22 relative per product). With few 128 x 128 output tiles the
+ * contraction is split across SMs; the slices' f32 partials go to `workspace`
+ * (tropnn_b200_gemm_tf32x3_workspace_size bytes; 0 when unsplit) and are summed in slice order.
+ */
+TROPNN_B200_API size_t tropnn_b200_gemm_tf32x3_workspace_size(int64_t m, int64_t n, int64_t k);
+TROPNN_B200_API int tropnn_b200_gemm_tf32x3(const float *a, int64_t lda, const float *b, int64_t ldb, int64_t m,
+                                            int64_t n, int64_t k, const float *bias, float *c, int64_t ldc,
+                                            void *workspace, size_t workspace_bytes, void *stream);
+/* out[j*ldo + i] = x[i*ldx + j] for i < rows, j < cols; out[j*ldo + i] = 0 for rows <= i < ldo.
+ * A layout step of the f32 products above (no reference counterpart). */
+TROPNN_B200_API int tropnn_b200_transpose_f32(const float *x, int64_t rows, int64_t cols, int64_t ldx, float *out,
+                                              int64_t ldo, void *stream);
+/* out[j] = sum_i x[i*ldx + j] in row order (the output-map bias gradient of the f32 path). */
+TROPNN_B200_API int tropnn_b200_colsum_f32(const float *x, int64_t rows, int64_t cols, int64_t ldx, float *out,
+                                           void *stream);
+
+/*
  * hidden[n,:] = latent[n,:] + code_scale * sum_h chat[n,h,:] with chat = code[h,w] (eval)
  * or code[h,w] + U(m) (code[h,r] - code[h,w]), U(m) = 0.5/(1+|m|) (training)
  * (layers/tropical.py:131-138, routing.py:13-15). code in param_dtype; latent in

@@ -93,8 +93,10 @@ def route_gate(scores: np.ndarray, rel: float = 1e-4) -> tuple[np.ndarray, np.nd
     winner where s1 - s2 > rel * max(|s1|, |s2|), runner additionally where s2 - s3 > ..."""
     top = -np.sort(-scores, axis=-1)
     s1, s2 = top[..., 0], top[..., 1]
-    s3 = top[..., 2] if scores.shape[-1] > 2 else np.full_like(s2, -np.inf)
     win = (s1 - s2) > rel * np.maximum(np.maximum(np.abs(s1), np.abs(s2)), 1e-30)
+    if scores.shape[-1] == 2:
+        return win, win  # with two cells the winner fixes the runner-up
+    s3 = top[..., 2]
     run = win & ((s2 - s3) > rel * np.maximum(np.maximum(np.abs(s2), np.abs(s3)), 1e-30))
     return win, run
 

@@ -27,7 +27,8 @@ import oracle
 import tropnn_b200
 import tropnn_b200.ops
 from oracle.tropnn_oracle import _round_to
-from tests.golden_cases import rel_err, route_gate, state_arrays
+from tests.golden_cases import rel_err, state_arrays
+from tests.trop_check import check_trop_layer, pinned_batch
 
 pytestmark = pytest.mark.gpu
 HALF_TOL = 2e-2
@@ -126,69 +127,23 @@ def trop_cfg5():
     return layer, state_arrays(layer)
 
 
-def _pinned_rows(st: dict, z_pool: np.ndarray, rows: int, train: bool, rel: float = 3e-4) -> np.ndarray:
-    """Indices of the first ``rows`` rows (a multiple of 8) whose routes clear the margin gate
-    at ``rel`` (three times the parity gate, so that the few-unit f32 differences of another
-    contraction split cannot undo it), judged on the scores of ``z_pool``."""
-    win, run = route_gate(oracle.trop_scores(z_pool, st["router_weight"], st["router_bias"]), rel=rel)
-    keep = np.nonzero((run if train else win).all(axis=1))[0]
-    assert keep.size >= rows, f"only {keep.size} pinned rows in the pool"
-    return keep[:rows]
-
-
 @pytest.mark.parametrize("train", [True, False])
 def test_trop_config5_layer_matches_oracle(trop_cfg5, train: bool) -> None:
-    """The projection is checked on its own (z within one f16 unit of the oracle's rounded z
-    plus the f32 accumulation error: two summation orders can round a sum on a boundary
-    differently), and the route, code
-    sum, output map and every gradient are checked on the GPU's z, so that a one-unit z
-    difference cannot move a score across the margin gate."""
+    """The projection against the oracle's rounded z (one f16 unit plus the f32 accumulation
+    error: two summation orders may round a sum on a boundary differently), then the whole
+    layer, forward and backward, on 512 pinned rows with the oracle routing on the layer's z
+    (tests/trop_check.py)."""
     layer, st = trop_cfg5
-    rows = 512
     gen = torch.Generator().manual_seed(31 if train else 32)
-    pool = torch.randn(2048, 4096, generator=gen).numpy()
-    g = torch.randn(rows, 4096, generator=gen).numpy()
-    layer = layer.cuda().train(train)
+    pool = torch.randn(3072, 4096, generator=gen).numpy()
+    g = torch.randn(512, 4096, generator=gen).numpy()
+    layer = layer.cuda()
     z_oracle = _round_to(_round_to(pool, "float16") @ st["proj.weight"].astype(np.float32).T, "float16")
     with torch.no_grad():
         z_pool = tropnn_b200.ops.trop_project_b200(torch.from_numpy(pool).cuda(), layer.proj.weight).float().cpu().numpy()
-    # One f16 unit, plus the f32 accumulation error of the 4096-long contraction (~1e-5 of
-    # the largest |z|: it dominates where a sum cancels to near zero).
     ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(z_oracle), 2.0**-14))) - 10)
     bound = ulp + 3e-5 * float(np.abs(z_oracle).max())
     assert np.all(np.abs(z_pool - z_oracle) <= bound), "projection beyond one f16 unit of the oracle"
-    keep = _pinned_rows(st, z_pool, rows, train)
-    x = pool[keep]
-    # z of exactly these rows as the layer computes it (the projection splits its contraction
-    # by row count, so a different batch can round a few sums differently).
-    with torch.no_grad():
-        z = tropnn_b200.ops.trop_project_b200(torch.from_numpy(x).cuda(), layer.proj.weight).float().cpu().numpy()
-    win, run = route_gate(oracle.trop_scores(z, st["router_weight"], st["router_bias"]))
-    assert (run if train else win).all(), "a selected row lost its margin"
-    layer.zero_grad(set_to_none=True)
-    xt = torch.from_numpy(x).cuda().requires_grad_(True)
-    y = layer(xt)
-    y.backward(torch.from_numpy(g).cuda().view_as(y))
-    torch.cuda.synchronize()
-    # The oracle's forward from the GPU's z (tropical.py:131-146 after :96-99).
-    route = oracle.trop_route_hidden(z, st["router_weight"], st["router_bias"], st["code"], code_scale=layer.code_scale,
-                                     training=train)
-    fwd = {**route, "z": z,
-           "y": route["hidden"] @ st["output_proj.weight"].astype(np.float32).T + st["output_proj.bias"].astype(np.float32)}
-    assert np.array_equal(layer._last_indices.cpu().numpy().reshape(rows, -1), fwd["winner"])
-    assert rel_err(layer._last_margins.cpu().numpy().reshape(rows, -1), fwd["margins"]) <= HALF_TOL
-    assert rel_err(y.detach().float().cpu().numpy().reshape(rows, -1), fwd["y"]) <= HALF_TOL
-    ref = oracle.trop_linear_backward(g, x, st, fwd, code_scale=layer.code_scale, training=train,
-                                      param_dtype="float16")
-    assert rel_err(xt.grad.cpu().numpy(), ref["x"]) <= HALF_TOL
-    for key in ("proj.weight", "code", "output_proj.weight", "output_proj.bias"):
-        p = dict(layer.named_parameters())[key]
-        assert p.grad is not None and p.grad.dtype == torch.float16, key
-        assert rel_err(p.grad.float().cpu().numpy(), ref[key]) <= HALF_TOL, key
-    if train:
-        for key in ("router_weight", "router_bias"):
-            p = dict(layer.named_parameters())[key]
-            assert rel_err(p.grad.float().cpu().numpy(), ref[key]) <= HALF_TOL, key
-    else:
-        assert layer.router_weight.grad is None and layer.router_bias.grad is None
+    x = pinned_batch(layer, pool, 512, train=train)
+    check_trop_layer(layer, x, g, train=train, tol=HALF_TOL)
     layer.cpu()

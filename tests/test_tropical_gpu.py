@@ -1,6 +1,7 @@
 """TropLinear backend="b200" on the GPU against the reference's golden vectors and the numpy
 oracle. Route indices are compared where the top-2 margin exceeds 1e-4 relative (the
-parity gate); values within 1e-5 relative in fp32, 2e-2 with f16/bf16 parameters."""
+parity gate); values within 1e-5 relative in fp32, 2e-2 with f16/bf16 parameters, on
+batches whose routes the gate pins (tests/trop_check.py)."""
 
 from __future__ import annotations
 
@@ -12,6 +13,7 @@ import oracle
 import tropnn_b200
 from tests.golden_cases import build_layer, case_names, load_case, rel_err, route_gate, state_arrays, tolerance
 from tests.gpu_runner import run_b200
+from tests.trop_check import check_trop_layer, check_trop_routes, pinned_batch
 
 pytestmark = pytest.mark.gpu
 FP32_TOL = 1e-5
@@ -73,43 +75,20 @@ def _run(layer: tropnn_b200.TropLinear, x: np.ndarray, g: np.ndarray, *, train: 
 
 
 def _check_against_oracle(layer: tropnn_b200.TropLinear, x: np.ndarray, g: np.ndarray, *, train: bool, tol: float) -> None:
-    st = state_arrays(layer)
-    pdt = str(layer.proj.weight.dtype).replace("torch.", "")
-    fwd = oracle.trop_linear_forward(x, st, code_scale=layer.code_scale, training=train, param_dtype=pdt)
-    got = _run(layer, x, g, train=train)
-    win, _ = route_gate(fwd["scores"])
-    assert np.array_equal(got["winner"][win], fwd["winner"][win])
-    assert rel_err(got["margins"], fwd["margins"]) <= max(tol, 1e-5)
-    agree = (got["winner"] == fwd["winner"]).all(axis=1)
-    if not agree.all():
-        # A route outside the parity gate (a near tie) flipped. Rows are independent, so the
-        # values are compared on the rows whose routes all agree, by running both sides again
-        # on those rows alone; flips must stay rare.
-        assert int((~agree).sum()) <= max(1, x.shape[0] // 100), f"{int((~agree).sum())} rows with flipped routes"
-        keep = np.nonzero(agree)[0]
-        x, g = x[keep], g[keep]
-        for p in layer.parameters():
-            p.grad = None
-        fwd = oracle.trop_linear_forward(x, st, code_scale=layer.code_scale, training=train, param_dtype=pdt)
-        got = _run(layer, x, g, train=train)
-        assert np.array_equal(got["winner"], fwd["winner"])
-    assert rel_err(got["y"], fwd["y"]) <= tol
-    ref = oracle.trop_linear_backward(g, x, st, fwd, code_scale=layer.code_scale, training=train, param_dtype=pdt)
-    assert rel_err(got["grad.x"], ref["x"]) <= tol
-    for key in ("proj.weight", "code", "output_proj.weight", "output_proj.bias"):
-        assert rel_err(got[f"grad.{key}"], ref[key]) <= tol, key
-    if train:
-        for key in ("router_weight", "router_bias"):
-            assert rel_err(got[f"grad.{key}"], ref[key]) <= tol, key
-    else:
-        assert got["grad.router_weight"] is None and got["grad.router_bias"] is None
+    """Routes of the whole pool ``x`` under the gate, then routes, values and every gradient on
+    a batch of half the pool (rounded to a multiple of 8) whose routes the gate pins."""
+    check_trop_routes(layer, x, train=train)
+    rows = max(1, x.shape[0] // 2 // 8 * 8) if x.shape[0] >= 16 else max(1, x.shape[0] // 2)
+    xb = pinned_batch(layer, x, rows, train=train)
+    check_trop_layer(layer, xb, g[:rows], train=train, tol=tol)
 
 
 @pytest.mark.parametrize("train", [True, False])
 def test_config3_layer1_batch512(train: bool) -> None:
-    """Config 3 layer 1: TropLinear(784->128, H256, K16, D64), U[0,1] inputs, batch 512."""
+    """Config 3 layer 1: TropLinear(784->128, H256, K16, D64), U[0,1] inputs, batch 512 (from a
+    pool of 1024 rows)."""
     layer = tropnn_b200.TropLinear(784, 128, heads=256, cells=16, code_dim=64, seed=0)
-    x, g = _inputs(512, 784, 128, uniform=True)
+    x, g = _inputs(1024, 784, 128, uniform=True)
     _check_against_oracle(layer, x, g, train=train, tol=FP32_TOL)
 
 
@@ -125,7 +104,7 @@ def test_config3_layer1_batch512(train: bool) -> None:
 )
 def test_shapes_and_edges(in_f: int, out_f: int, heads: int, cells: int, code_dim: int, n: int) -> None:
     layer = tropnn_b200.TropLinear(in_f, out_f, heads=heads, cells=cells, code_dim=code_dim, seed=4)
-    x, g = _inputs(n, in_f, out_f, seed=2)
+    x, g = _inputs(2 * n, in_f, out_f, seed=2)
     _check_against_oracle(layer, x, g, train=True, tol=FP32_TOL)
 
 
@@ -136,7 +115,7 @@ def test_half_precision_parameters(dtype: torch.dtype) -> None:
     with torch.no_grad():
         layer.router_bias.copy_(torch.linspace(-2.0, 2.0, 16).expand_as(layer.router_bias))
     layer = layer.to(dtype)
-    x, g = _inputs(256, 256, 256, seed=3)
+    x, g = _inputs(512, 256, 256, seed=3)
     _check_against_oracle(layer, x, g, train=True, tol=2e-2)
     assert layer.code.grad.dtype == dtype and layer.router_weight.grad.dtype == dtype
 

@@ -86,6 +86,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tropnn_b200_trop_code_transpose": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p]),
     "tropnn_b200_trop_proj_workspace_size": (_sz, [_i64, _i64, _i64]),
     "tropnn_b200_trop_proj": (_i32, [_p, _i64, _i64, _p, _i32, _i64, _p, _p, _sz, _p]),
+    "tropnn_b200_gemm_tf32x3_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "tropnn_b200_gemm_tf32x3": (_i32, [_p, _i64, _p, _i64, _i64, _i64, _i64, _p, _p, _i64, _p, _sz, _p]),
+    "tropnn_b200_transpose_f32": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _p]),
+    "tropnn_b200_colsum_f32": (_i32, [_p, _i64, _i64, _i64, _p, _p]),
     "tropnn_b200_split_half": (_i32, [_p, _i64, _i64, _i32, _p, _p, _p]),
     "tropnn_b200_absmax_f32": (_i32, [_p, _i64, _p, _p]),
     "tropnn_b200_linear_f32out": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _i32, _p, _p, _p]),

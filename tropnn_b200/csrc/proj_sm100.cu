@@ -134,6 +134,32 @@ __device__ __forceinline__ void store_chunk(const float (&v)[64], uint8_t *stage
   }
 }
 
+// Sum over `splits` slice partials at base[s * slice_stride + offset] in slice order, with up
+// to 4 slices' loads in flight at once.
+__device__ __forceinline__ float4 sum_slices(const float4 *base, int splits, size_t slice_stride, size_t offset) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s0 = 0; s0 < splits; s0 += 4) {
+    float4 q[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (s0 + i < splits) q[i] = __ldcg(base + size_t(s0 + i) * slice_stride + offset);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (s0 + i < splits) {
+        if (s0 + i == 0) {
+          acc = q[i];
+        } else {
+          acc.x = __fadd_rn(acc.x, q[i].x);
+          acc.y = __fadd_rn(acc.y, q[i].y);
+          acc.z = __fadd_rn(acc.z, q[i].z);
+          acc.w = __fadd_rn(acc.w, q[i].w);
+        }
+      }
+    }
+  }
+  return acc;
+}
+
 template <typename PT>
 __global__ void __launch_bounds__(kThreads, 1) trop_proj_kernel(const __grid_constant__ CUtensorMap map_x,
                                                                 const __grid_constant__ CUtensorMap map_p,
@@ -354,23 +380,27 @@ __global__ void __launch_bounds__(kThreads, 1) trop_proj_kernel(const __grid_con
       __threadfence();
       const float4 *base = partial + size_t(rb) * g.splits * (g.D / 4) * kBM + r;
       for (int ch = group; ch < chunks; ch += 2) {
-        float v[64];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float4 acc = __ldcg(base + size_t(ch * 16 + j) * kBM);
-          for (int sl = 1; sl < g.splits; ++sl) {
-            const float4 q = __ldcg(base + (size_t(sl) * (g.D / 4) + ch * 16 + j) * kBM);
-            acc.x = __fadd_rn(acc.x, q.x);
-            acc.y = __fadd_rn(acc.y, q.y);
-            acc.z = __fadd_rn(acc.z, q.z);
-            acc.w = __fadd_rn(acc.w, q.w);
-          }
-          v[4 * j] = acc.x;
-          v[4 * j + 1] = acc.y;
-          v[4 * j + 2] = acc.z;
-          v[4 * j + 3] = acc.w;
+        if (lane == 0) bulk_wait_read_all();  // the previous store has read the staging tile
+        __syncwarp();
+        uint8_t *my_row = stage + lane * 128;
+#pragma unroll 1
+        for (int m = 0; m < 8; ++m) {
+          // 8 columns: two float4 of every slice, summed in slice order, rounded to PT.
+          const float4 lo = sum_slices(base, g.splits, size_t(g.D / 4) * kBM, size_t(ch * 16 + 2 * m) * kBM);
+          const float4 hi = sum_slices(base, g.splits, size_t(g.D / 4) * kBM, size_t(ch * 16 + 2 * m + 1) * kBM);
+          uint4 q;
+          q.x = pack2<PT>(lo.x, lo.y);
+          q.y = pack2<PT>(lo.z, lo.w);
+          q.z = pack2<PT>(hi.x, hi.y);
+          q.w = pack2<PT>(hi.z, hi.w);
+          *reinterpret_cast<uint4 *>(my_row + ((m ^ (lane & 7)) << 4)) = q;
         }
-        store_chunk<PT>(v, stage, lane, &map_z, ch * 64, row0);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&map_z, stage, ch * 64, row0);
+          bulk_commit();
+        }
       }
     }
     if (lane == 0) bulk_wait_all();

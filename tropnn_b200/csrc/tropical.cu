@@ -42,6 +42,7 @@ int read_param_grad_error(int *value);
 int read_linear_grad_error(int *value);
 int read_lut_grad_error(int *value);
 int read_proj_error(int *value);
+int read_gemm_tf32_error(int *value);
 int trop_gm_sm100_impl(const void *g_split, int64_t rows, int64_t code_dim, const void *code, int dtype, int64_t heads,
                        int64_t cells, const uint8_t *winner, const uint8_t *runner, const float *margins,
                        float code_scale, float *gm, const uint32_t *absmax, cudaStream_t stream);
@@ -720,7 +721,7 @@ int tropnn_b200_transpose_to_half(const void *x, int x_dtype, int64_t rows, int6
 
 int tropnn_b200_device_error(int *value) {
   TB_CHECK(tropnn_b200::check_current_device());
-  int score = 0, hidden = 0, gemm = 0, peer = 0, pgrad = 0, lgrad = 0, lutg = 0, proj = 0;
+  int score = 0, hidden = 0, gemm = 0, peer = 0, pgrad = 0, lgrad = 0, lutg = 0, proj = 0, gtf32 = 0;
   TB_CHECK(tropnn_b200::read_score_error(&score));
   TB_CHECK(tropnn_b200::read_hidden_error(&hidden));
   TB_CHECK(tropnn_b200::read_gemm_error(&gemm));
@@ -729,7 +730,8 @@ int tropnn_b200_device_error(int *value) {
   TB_CHECK(tropnn_b200::read_linear_grad_error(&lgrad));
   TB_CHECK(tropnn_b200::read_lut_grad_error(&lutg));
   TB_CHECK(tropnn_b200::read_proj_error(&proj));
-  *value = score | hidden | gemm | peer | pgrad | lgrad | lutg | proj;
+  TB_CHECK(tropnn_b200::read_gemm_tf32_error(&gtf32));
+  *value = score | hidden | gemm | peer | pgrad | lgrad | lutg | proj | gtf32;
   return tropnn_b200::clear_error();
 }
 

@@ -26,6 +26,10 @@ from torch import Tensor
 
 from .ops import (
     EXACT_EVAL_MAX_IN,
+    gemm_f32,
+    gemm_f32_eligible,
+    linear_f32_b200,
+    linear_f32_eligible,
     linear_f32out_b200,
     linear_f32out_eligible,
     pairwise_anchor_index,
@@ -34,6 +38,7 @@ from .ops import (
     trop_exact_eval_b200,
     trop_project_b200,
     trop_route_hidden_packed,
+    transpose_f32,
 )
 
 __all__ = [
@@ -118,11 +123,20 @@ def _exact_eval_params(layer: nn.Module, device: torch.device) -> tuple[Tensor, 
     f32 = torch.float32
     heads, cells, dim = layer.router_weight.shape
     with torch.no_grad():  # inference weights: the cache holds no autograd history
-        proj = layer.proj.weight.to(device=device, dtype=f32)
-        w_out = layer.output_proj.weight.to(device=device, dtype=f32)
-        router_eff = torch.matmul(layer.router_weight.to(device=device, dtype=f32).reshape(heads * cells, dim), proj)
-        value_eff = torch.matmul(layer.code.to(device=device, dtype=f32).reshape(heads * cells, dim), w_out.t())
-        base = torch.matmul(w_out, proj)
+        proj = layer.proj.weight.to(device=device, dtype=f32).contiguous()
+        w_out = layer.output_proj.weight.to(device=device, dtype=f32).contiguous()
+        weight = layer.router_weight.to(device=device, dtype=f32).reshape(heads * cells, dim).contiguous()
+        code = layer.code.to(device=device, dtype=f32).reshape(heads * cells, dim).contiguous()
+        if gemm_f32_eligible(proj, w_out, weight, code):
+            # f32 products on the tensor cores (3xTF32): W P and Wout P against P^T.
+            proj_t = transpose_f32(proj)
+            router_eff = gemm_f32(weight, proj_t, k=dim)
+            value_eff = gemm_f32(code, w_out)
+            base = gemm_f32(w_out, proj_t, k=dim)
+        else:
+            router_eff = torch.matmul(weight, proj)
+            value_eff = torch.matmul(code, w_out.t())
+            base = torch.matmul(w_out, proj)
         params = (
             router_eff.view(heads, cells, -1).contiguous(),
             layer.router_bias.to(device=device, dtype=f32).contiguous(),
@@ -136,18 +150,23 @@ def _exact_eval_params(layer: nn.Module, device: torch.device) -> tuple[Tensor, 
 def _trop_exact_eval_b200(layer: nn.Module, x: Tensor) -> Tensor:
     """TropLinear forward with ``exact_fused="eval"`` in eval under no_grad
     (layers/tropical_exact.py:297-358): x in the compute dtype (not rounded to the parameters),
-    scores against W P on the route kernel, y = x (Wout P)^T + b_out (cuBLAS, as the reference's
-    matmul) plus code_scale * sum_h (c Wout^T)[h, winner] on the code-sum kernel."""
+    scores against W P on the route kernel, y = x (Wout P)^T + b_out (the reference's f32 matmul,
+    here the 3xTF32 tensor-core product) plus code_scale * sum_h (c Wout^T)[h, winner] on the
+    code-sum kernel."""
     input_dtype = x.dtype
     compute_dtype = _compute_dtype(x)
     _require_f32_compute(compute_dtype, "TropLinear")
     batch, steps, in_features = x.shape
     x_flat = x.to(compute_dtype).reshape(batch * steps, in_features).contiguous()
     router_eff, router_bias, value_eff, base = _exact_eval_params(layer, x.device)
-    base_out = torch.matmul(x_flat, base.t())
     bias = layer.output_proj.bias
-    if bias is not None:
-        base_out = base_out + bias.to(device=x.device, dtype=compute_dtype)
+    if gemm_f32_eligible(x_flat, base):
+        # x (Wout P)^T + b_out on the f32 tensor-core product (3xTF32).
+        base_out = gemm_f32(x_flat, base, None if bias is None else bias.to(device=x.device, dtype=compute_dtype))
+    else:
+        base_out = torch.matmul(x_flat, base.t())
+        if bias is not None:
+            base_out = base_out + bias.to(device=x.device, dtype=compute_dtype)
     y, winner, margins = trop_exact_eval_b200(
         x_flat, router_eff, router_bias, value_eff, base_out, code_scale=layer.code_scale,
         keep_margins=getattr(layer, "cache_route_debug", True),
@@ -160,10 +179,12 @@ def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
     """Full TropLinear forward on sm_100a for any module with the TropLinear attributes.
 
     The projection (tropical.py:96-99) runs on the b200 tensor-core projection kernel for
-    half-precision weights (ops.trop_project_b200), else torch; the route scores, top-2, code
-    sum and their backward are the b200 kernels (ops.trop_route_hidden_packed); the output map
-    (tropical.py:140-146) is the b200 tensor-core linear map for half-precision weights
-    (ops.linear_f32out_b200), else torch.
+    half-precision weights (ops.trop_project_b200) and on the 3xTF32 tensor-core product for
+    f32 weights (ops.linear_f32_b200); the route scores, top-2, code sum and their backward are
+    the b200 kernels (ops.trop_route_hidden_packed); the output map (tropical.py:140-146) is the
+    b200 tensor-core linear map for half-precision weights (ops.linear_f32out_b200) or the
+    3xTF32 product for f32 weights. Widths the kernels do not tile (inputs not a multiple of 4
+    floats wide) use torch.
     """
     if x.ndim == 2:
         x = x.unsqueeze(1)
@@ -183,6 +204,9 @@ def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
     if proj_eligible(x, layer.proj.weight):
         # Half-precision projection weight: the tensor-core projection kernel rounds x on chip.
         z = trop_project_b200(x, layer.proj.weight)
+    elif linear_f32_eligible(x.to(torch.float32), layer.proj.weight):
+        # f32 projection weight: the reference's f32 GEMM as 3xTF32 on the tensor cores.
+        z = linear_f32_b200(x.to(torch.float32), layer.proj.weight, None)
     else:
         z = layer.proj(x.to(dtype=layer.proj.weight.dtype))
     # The reference upcasts z to the compute dtype (tropical.py:99); with half-precision
@@ -203,6 +227,9 @@ def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
         # Half-precision output weight: the f32 product on the tensor cores (split f32
         # hidden, bias fused), the reference's f32 math in the backward.
         output = linear_f32out_b200(hidden, layer.output_proj.weight, bias)
+    elif linear_f32_eligible(hidden, layer.output_proj.weight) and (bias is None or bias.dtype == torch.float32):
+        # f32 output weight: the reference's f32 F.linear as 3xTF32 on the tensor cores.
+        output = linear_f32_b200(hidden, layer.output_proj.weight, bias)
     else:
         weight = layer.output_proj.weight.to(dtype=compute_dtype)
         output = torch.matmul(hidden, weight.t())

@@ -1078,3 +1078,115 @@ def trop_project_b200(x: Tensor, weight: Tensor) -> Tensor:
     with torch.cuda.device(x.device):
         z = _TropProjFunction.apply(x.reshape(-1, x.shape[-1]), weight)
     return z.reshape(*lead, weight.shape[0])
+
+
+# ---------------------------------------------------------------------------
+# f32 linear maps on the tensor cores (3xTF32)
+# ---------------------------------------------------------------------------
+
+
+def _ceil4(n: int) -> int:
+    return (n + 3) // 4 * 4
+
+
+def gemm_f32_eligible(*mats: Tensor) -> bool:
+    """f32 CUDA matrices whose rows the tensor-core f32 product can read with TMA: contiguous,
+    16-byte aligned, a row length that is a multiple of 4 floats."""
+    return all(
+        t.is_cuda and t.dtype == torch.float32 and t.dim() == 2 and t.is_contiguous() and t.shape[1] % 4 == 0
+        and t.data_ptr() % 16 == 0
+        for t in mats
+    )
+
+
+def gemm_f32(a: Tensor, b: Tensor, bias: Tensor | None = None, *, k: int | None = None, n: int | None = None) -> Tensor:
+    """C = A B^T (+ bias) for f32 A [m, >=k] and B [>=n, >=k] (row strides = their widths),
+    on the 3xTF32 tensor-core kernel (tropnn_b200_gemm_tf32x3); returns C [m, n] f32."""
+    m = a.shape[0]
+    k = a.shape[1] if k is None else k
+    n = b.shape[0] if n is None else n
+    dev = a.device
+    c = torch.empty((m, n), device=dev, dtype=torch.float32)
+    bias_c = None if bias is None else bias.to(torch.float32).contiguous()
+    lib = nat.load()
+    ws_bytes = int(lib.tropnn_b200_gemm_tf32x3_workspace_size(m, n, k))
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8) if ws_bytes else None
+    _launch("gemm_tf32x3", lib.tropnn_b200_gemm_tf32x3, a.data_ptr(), a.shape[1], b.data_ptr(), b.shape[1], m,
+            n, k, nat.ptr(bias_c), c.data_ptr(), n, nat.ptr(ws), ws_bytes, nat.stream_handle(dev))
+    return c
+
+
+def transpose_f32(x: Tensor, pad_to: int = 4) -> Tensor:
+    """x^T for an f32 [rows, cols] matrix, as [cols, ldo] with ldo = rows rounded up to
+    ``pad_to`` and the padding columns zero (tropnn_b200_transpose_f32)."""
+    rows, cols = x.shape
+    ldo = (rows + pad_to - 1) // pad_to * pad_to
+    out = torch.empty((cols, ldo), device=x.device, dtype=torch.float32)
+    _launch("transpose_f32", nat.load().tropnn_b200_transpose_f32, x.data_ptr(), rows, cols, x.shape[1],
+            out.data_ptr(), ldo, nat.stream_handle(x.device))
+    return out
+
+
+def _padded_cols(x: Tensor) -> Tensor:
+    """x [rows, n] with its rows padded with zeros to a multiple of 4 floats (TMA row stride)."""
+    n = x.shape[1]
+    if n % 4 == 0:
+        return x.contiguous()
+    return torch.nn.functional.pad(x, (0, _ceil4(n) - n)).contiguous()
+
+
+class _LinearF32Function(torch.autograd.Function):
+    """F.linear(x, weight, bias) in f32 (the reference's f32 projection and output map,
+    layers/tropical.py:96-99, :140-146) on the 3xTF32 tensor-core product, forward and
+    backward: y = x W^T + b, grad_x = g W, grad_W = g^T x, grad_b = sum_n g."""
+
+    @staticmethod
+    def forward(ctx: Any, x: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:
+        xc = x.contiguous()
+        w = weight.contiguous()
+        y = gemm_f32(xc, w, bias)
+        ctx.save_for_backward(xc, w)
+        ctx.has_bias = bias is not None
+        return y
+
+    @staticmethod
+    def backward(ctx: Any, grad_y: Tensor) -> tuple[Tensor | None, Tensor | None, Tensor | None]:
+        x, w = ctx.saved_tensors
+        rows, in_features = x.shape
+        out_features = w.shape[0]
+        g = grad_y.to(torch.float32).contiguous()
+        grad_x = grad_w = grad_b = None
+        if ctx.needs_input_grad[0]:
+            # grad_x = g W: B = W^T [in, out] (row stride padded to 4 floats).
+            grad_x = gemm_f32(_padded_cols(g), transpose_f32(w), k=out_features, n=in_features)
+        if ctx.needs_input_grad[1]:
+            # grad_W = g^T x: A = g^T [out, rows], B = x^T [in, rows].
+            grad_w = gemm_f32(transpose_f32(g), transpose_f32(x), k=rows, n=in_features)
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            grad_b = torch.empty(out_features, device=g.device, dtype=torch.float32)
+            _launch("colsum_f32", nat.load().tropnn_b200_colsum_f32, g.data_ptr(), rows, out_features, out_features,
+                    grad_b.data_ptr(), nat.stream_handle(g.device))
+        return grad_x, grad_w, grad_b
+
+
+def linear_f32_eligible(x: Tensor, weight: Tensor) -> bool:
+    """Shapes the f32 tensor-core linear map takes: f32 CUDA input and weight with an input
+    width that is a multiple of 4."""
+    return (
+        x.is_cuda
+        and x.dtype == torch.float32
+        and weight.dtype == torch.float32
+        and weight.dim() == 2
+        and x.shape[-1] == weight.shape[1]
+        and weight.shape[1] % 4 == 0
+    )
+
+
+def linear_f32_b200(x: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:
+    """``F.linear(x, weight, bias)`` in f32 on the tensor cores (3xTF32), with its backward."""
+    if not linear_f32_eligible(x, weight):
+        raise ValueError(f"linear_f32_b200: unsupported x {tuple(x.shape)} {x.dtype} / weight {tuple(weight.shape)}")
+    lead = x.shape[:-1]
+    with torch.cuda.device(x.device):
+        y = _LinearF32Function.apply(x.reshape(-1, x.shape[-1]), weight, bias)
+    return y.reshape(*lead, weight.shape[0])
