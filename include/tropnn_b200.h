@@ -320,12 +320,18 @@ TROPNN_B200_API int tropnn_b200_colsum_f32(const float *x, int64_t rows, int64_t
  * {2,4,8,16,32}, code_dim in {64,128,192,256}, heads*cells % 8 == 0 and >= 128 items,
  * the sum runs as a one-hot GEMM on the tensor cores (tcgen05); in training the two
  * mixing weights are then rounded to the parameter dtype. Otherwise a per-row gather.
+ * With fewer 128-row blocks than the SMs can take, the tensor-core path splits the
+ * (head, cell) contraction into slices when `workspace` holds
+ * tropnn_b200_trop_hidden_workspace_size() bytes (their f32 partials, summed in slice order);
+ * with a NULL or smaller workspace it runs unsplit. Same for tropnn_b200_trop_router_term.
  */
+TROPNN_B200_API size_t tropnn_b200_trop_hidden_workspace_size(int64_t items, int64_t code_dim, int64_t heads,
+                                                              int64_t cells);
 TROPNN_B200_API int tropnn_b200_trop_hidden(const void *latent, int latent_dtype, int64_t items, int64_t code_dim,
                             const void *code, const void *code_t, int param_dtype, int64_t heads, int64_t cells,
                             const void *winner, const void *runner, int index_dtype,
                             const float *margins, float code_scale, int training,
-                            float *hidden, void *stream);
+                            float *hidden, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
  * code_t[d, h*cells + k] = code[h, k, d]: the K-major right operand of the tensor-core
@@ -449,7 +455,8 @@ TROPNN_B200_API int tropnn_b200_trop_gm(const void *g_split, int64_t items, int6
 TROPNN_B200_API int tropnn_b200_trop_router_term(const float *grad_hidden, int64_t items, int64_t code_dim,
                                  const void *router_weight_t, int param_dtype, int64_t heads, int64_t cells,
                                  const void *winner, const void *runner, const float *gm,
-                                 const void *grad_absmax, float *grad_latent, void *stream);
+                                 const void *grad_absmax, float *grad_latent, void *workspace,
+                                 size_t workspace_bytes, void *stream);
 TROPNN_B200_API int tropnn_b200_trop_param_grad(int mode, const void *x_t, int64_t items, int64_t code_dim,
                                 int param_dtype, int64_t heads, int64_t cells, const void *winner,
                                 const void *runner, const float *values, float code_scale, void *grad,
@@ -464,7 +471,10 @@ TROPNN_B200_API int tropnn_b200_transpose_to_half(const void *x, int x_dtype, in
  * accuracy and range. g = grad_out, f32 [rows, out_features]; out_features a multiple of 32;
  * in_features a multiple of 32 in [32, 256].
  * linear_dgrad: grad_hidden[n,i] = sum_o g[n,o] weight32[o,i]; weight32 = the weight widened
- *   to f32 ([out_features, in_features]); grad_hidden f32 [rows, in_features].
+ *   to f32 ([out_features, in_features]); grad_hidden f32 [rows, in_features]. With few
+ *   128-row blocks the out_features contraction is split across SMs when `workspace` holds
+ *   tropnn_b200_linear_dgrad_workspace_size() bytes (slice partials summed in slice order);
+ *   NULL runs it unsplit.
  * linear_wgrad: grad_weight[o,i] = sum_n g[n,o] hidden[n,i] rounded to dtype (F16/BF16), and
  *   grad_bias[o] = sum_n g[n,o] in f32 when not NULL; hidden given as its tf32 split
  *   (tropnn_b200_tf32_split). The row range is contracted by a 4-CTA cluster per 128 output
@@ -472,8 +482,11 @@ TROPNN_B200_API int tropnn_b200_transpose_to_half(const void *x, int x_dtype, in
  * tf32_split: x = big + small elementwise with big = tf32(x), small = tf32(x - big); count a
  *   multiple of 4, 16-byte aligned pointers.
  */
+TROPNN_B200_API size_t tropnn_b200_linear_dgrad_workspace_size(int64_t rows, int64_t out_features,
+                                                               int64_t in_features);
 TROPNN_B200_API int tropnn_b200_linear_dgrad(const float *g, int64_t rows, int64_t out_features, const float *weight32,
-                             int64_t in_features, float *grad_hidden, void *stream);
+                             int64_t in_features, float *grad_hidden, void *workspace, size_t workspace_bytes,
+                             void *stream);
 TROPNN_B200_API int tropnn_b200_linear_wgrad(const float *g, int64_t rows, int64_t out_features, const float *hidden_big,
                              const float *hidden_small, int64_t in_features, int dtype, void *grad_weight,
                              float *grad_bias, void *stream);

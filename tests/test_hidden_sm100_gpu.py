@@ -46,11 +46,13 @@ def _hidden(latent, code, winner, runner, margins, code_scale, training, use_tc)
             "trop_code_transpose",
         )
     hidden = torch.empty((items, code_dim), device=latent.device, dtype=torch.float32)
+    ws_bytes = int(lib.tropnn_b200_trop_hidden_workspace_size(items, code_dim, heads, cells)) if use_tc else 0
+    ws = torch.empty(ws_bytes, device=latent.device, dtype=torch.uint8) if ws_bytes else None
     nat.check(
         lib.tropnn_b200_trop_hidden(
             latent.data_ptr(), nat.float_code(latent.dtype), items, code_dim, code.data_ptr(), nat.ptr(code_t),
             nat.float_code(code.dtype), heads, cells, winner.data_ptr(), runner.data_ptr(), nat.U8,
-            margins.data_ptr(), float(code_scale), int(training), hidden.data_ptr(), stream,
+            margins.data_ptr(), float(code_scale), int(training), hidden.data_ptr(), nat.ptr(ws), ws_bytes, stream,
         ),
         "trop_hidden",
     )
@@ -108,6 +110,7 @@ def test_cells(cells):
         (1000, 200, 8, 192),  # many row blocks, N=192
         (129, 20, 2, 64),  # one live row in the last block, 40 entries (one partial k block)
         (20000, 64, 16, 128),  # ~1 row block per CTA and more: the persistent loop
+        (300, 1024, 16, 128),  # 3 row blocks: the contraction split into 16 slices, ragged rows
     ],
 )
 def test_ragged_shapes(items, heads, cells, code_dim):

@@ -42,9 +42,12 @@ def _dgrad(g, w):
     in_features = w.shape[1]
     w32 = w.float().contiguous()
     out = torch.full((rows, in_features), float("nan"), device="cuda")
+    lib = nat.load()
+    ws_bytes = int(lib.tropnn_b200_linear_dgrad_workspace_size(rows, out_features, in_features))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda") if ws_bytes else None
     nat.check(
-        nat.load().tropnn_b200_linear_dgrad(g.data_ptr(), rows, out_features, w32.data_ptr(), in_features,
-                                            out.data_ptr(), _stream()),
+        lib.tropnn_b200_linear_dgrad(g.data_ptr(), rows, out_features, w32.data_ptr(), in_features, out.data_ptr(),
+                                     nat.ptr(ws), ws_bytes, _stream()),
         "linear_dgrad",
     )
     return out

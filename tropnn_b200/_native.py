@@ -17,7 +17,7 @@ from pathlib import Path
 import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtropnn_b200.so"
-ABI_VERSION = 12
+ABI_VERSION = 13
 
 # tropnn_b200_dtype
 F32, F16, BF16, U8, I16, I64 = 0, 1, 2, 3, 4, 5
@@ -79,9 +79,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _i64, _i64, _f32, _p, _p, _p, _i64, _i64, _i64, _p, _i32, _i32, _i32, _p, _p, _i32, _p, _p],
     ),
     "tropnn_b200_trop_route": (_i32, [_p, _i32, _i64, _i64, _p, _p, _i32, _i32, _i64, _i64, _p, _p, _p, _i32, _p, _p]),
+    "tropnn_b200_trop_hidden_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
     "tropnn_b200_trop_hidden": (
         _i32,
-        [_p, _i32, _i64, _i64, _p, _p, _i32, _i64, _i64, _p, _p, _i32, _p, _f32, _i32, _p, _p],
+        [_p, _i32, _i64, _i64, _p, _p, _i32, _i64, _i64, _p, _p, _i32, _p, _f32, _i32, _p, _p, _sz, _p],
     ),
     "tropnn_b200_trop_code_transpose": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p]),
     "tropnn_b200_trop_proj_workspace_size": (_sz, [_i64, _i64, _i64]),
@@ -100,10 +101,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tropnn_b200_peer_allreduce_f32": (_i32, [_p, _i32, _i32, _i64, _p, _p, _i32, _i32, _p]),
     "tropnn_b200_device_error": (_i32, [ctypes.POINTER(ctypes.c_int)]),
     "tropnn_b200_trop_gm": (_i32, [_p, _i64, _i64, _p, _i32, _i64, _i64, _p, _p, _p, _f32, _p, _p, _p]),
-    "tropnn_b200_trop_router_term": (_i32, [_p, _i64, _i64, _p, _i32, _i64, _i64, _p, _p, _p, _p, _p, _p]),
+    "tropnn_b200_trop_router_term": (_i32, [_p, _i64, _i64, _p, _i32, _i64, _i64, _p, _p, _p, _p, _p, _p, _sz, _p]),
     "tropnn_b200_trop_param_grad": (_i32, [_i32, _p, _i64, _i64, _i32, _i64, _i64, _p, _p, _p, _f32, _p, _p, _p, _p]),
     "tropnn_b200_transpose_to_half": (_i32, [_p, _i32, _i64, _i64, _i32, _p, _p, _p]),
-    "tropnn_b200_linear_dgrad": (_i32, [_p, _i64, _i64, _p, _i64, _p, _p]),
+    "tropnn_b200_linear_dgrad_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "tropnn_b200_linear_dgrad": (_i32, [_p, _i64, _i64, _p, _i64, _p, _p, _sz, _p]),
     "tropnn_b200_linear_wgrad": (_i32, [_p, _i64, _i64, _p, _p, _i64, _i32, _p, _p, _p]),
     "tropnn_b200_tf32_split": (_i32, [_p, _i64, _p, _p, _p]),
     "tropnn_b200_trop_backward_rows": (

@@ -34,6 +34,14 @@ int ensure_dynamic_smem(const void *func, size_t bytes, const char *what);
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Epilogues of slice_reduce_impl (slice_reduce.cu): the sum of a split contraction's slice
+// partials (float4 partial[tile * splits + slice][tile_cols / 4][128 rows]) rounded to a half
+// dtype, plus an f32 bias, or added to a latent row times a scale.
+enum SliceReduceMode { kReduceHalf = 0, kReduceF32 = 1, kReduceHidden = 2 };
+int slice_reduce_impl(int mode, const void *partial, int splits, int n_tiles, int tile_cols, int64_t rows,
+                      int64_t cols, void *out, int out_dtype, int64_t ldo, const float *bias, const void *latent,
+                      int latent_dtype, float scale, cudaStream_t stream);
+
 // Power-of-two scale that brings a gradient tensor whose largest |value| has the f32 bits
 // `absmax_bits` into [16, 32): converted to f16 after it, the gradient neither underflows (f16's
 // smallest normal is 6.1e-5) nor overflows in the products formed from it, and the f32 results

@@ -13,8 +13,8 @@
 // Work unit = (128-row block of C, 128-column block of C, k slice); persistent grid, one CTA
 // per SM, contiguous unit ranges. With fewer output tiles than ~3/4 of the SMs (the small
 // products of configs 1 and 3) the contraction is cut into up to 16 slices: each slice's f32
-// partial goes to the caller's workspace (row index fastest) and the tile's last slice to
-// arrive (a per-tile counter) sums them in slice order, deterministically. CTA = 10 warps:
+// partial goes to the caller's workspace (row index fastest) and slice_reduce, launched next,
+// sums them in slice order (deterministic) and adds the bias. CTA = 10 warps:
 //   warp 0      TMA producer: per 32-wide k block the 128 x 32 f32 tiles of A and B
 //               (128-byte swizzle) into a 3-stage ring.
 //   warp 1      allocates 512 TMEM columns (two units in flight, each a big and a cross
@@ -109,36 +109,10 @@ __device__ __forceinline__ float4 split_big(float4 x, float4 *small) {
   return hi;
 }
 
-// Sum over `splits` slice partials at base[s * slice_stride + offset] in slice order, with up
-// to 8 slices' loads in flight at once.
-__device__ __forceinline__ float4 sum_slices(const float4 *base, int splits, size_t slice_stride, size_t offset) {
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s0 = 0; s0 < splits; s0 += 8) {
-    float4 q[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (s0 + i < splits) q[i] = __ldcg(base + size_t(s0 + i) * slice_stride + offset);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (s0 + i < splits) {
-        if (s0 + i == 0) {
-          acc = q[i];
-        } else {
-          acc.x = __fadd_rn(acc.x, q[i].x);
-          acc.y = __fadd_rn(acc.y, q[i].y);
-          acc.z = __fadd_rn(acc.z, q[i].z);
-          acc.w = __fadd_rn(acc.w, q[i].w);
-        }
-      }
-    }
-  }
-  return acc;
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                        const __grid_constant__ CUtensorMap map_c, const GemmGeom g, const float *__restrict__ bias,
-                       float *__restrict__ c_ptr, float4 *__restrict__ partial, int *__restrict__ counters) {
+                       float *__restrict__ c_ptr, float4 *__restrict__ partial) {
   const uint32_t idesc = umma_idesc_tf32(false, false, kBM, kBN);
 
   extern __shared__ uint8_t smem_raw[];
@@ -350,31 +324,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bs->tmem_empty[b]);
-      if (g.splits == 1) continue;
-
-      // The output tile's last slice to arrive sums the slices in slice order.
-      __threadfence();
-      named_sync(1, kEpiWarps * 32);
-      if (ew == 0 && lane == 0) {
-        const int last = atomicAdd(counters + w.tile, 1) == g.splits - 1;
-        if (last) counters[w.tile] = 0;  // ready for the next launch (stream order)
-        bs->epi_go[b] = last ? 2 : 1;
-      }
-      named_sync(1, kEpiWarps * 32);
-      if (*reinterpret_cast<volatile int *>(&bs->epi_go[b]) != 2) continue;
-      __threadfence();
-      const float4 *base = partial + size_t(w.tile) * g.splits * (kBN / 4) * kBM + r;
-      for (int c = 0; c < kBN; c += 32) {
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 q = sum_slices(base, g.splits, size_t(kBN / 4) * kBM, size_t(c / 4 + j) * kBM);
-          v[4 * j] = q.x, v[4 * j + 1] = q.y, v[4 * j + 2] = q.z, v[4 * j + 3] = q.w;
-        }
-        const int64_t col = int64_t(w.nt) * kBN + c;
-        add_bias(v, col);
-        store32(v, w.mt, col);
-      }
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
@@ -475,8 +424,7 @@ GemmGeom gemm_geometry(int64_t m, int64_t n, int64_t k) {
 
 size_t gemm_workspace_bytes(const GemmGeom &g) {
   if (g.splits == 1) return 0;
-  return WorkspaceCarver::align(size_t(g.units) * kBM * kBN * sizeof(float)) +
-         WorkspaceCarver::align(size_t(g.units / g.splits) * sizeof(int));
+  return WorkspaceCarver::align(size_t(g.units) * kBM * kBN * sizeof(float));
 }
 
 }  // namespace
@@ -504,16 +452,12 @@ int gemm_tf32x3_impl(const float *a, int64_t lda, const float *b, int64_t ldb, i
   g.ldc = ldc;
   g.tma_store = (ldc % 4 == 0 && al16(c)) ? 1 : 0;
   float4 *partial = nullptr;
-  int *counters = nullptr;
   if (g.splits > 1) {
     WorkspaceCarver wc(ws, ws_bytes);
     partial = wc.take<float4>(size_t(g.units) * kBM * (kBN / 4));
-    counters = wc.take<int>(size_t(g.units / g.splits));
-    TB_REQUIRE(partial != nullptr && counters != nullptr, TROPNN_B200_ERR_WORKSPACE,
+    TB_REQUIRE(partial != nullptr, TROPNN_B200_ERR_WORKSPACE,
                "gemm_tf32x3: workspace of %zu bytes is smaller than the %zu bytes required", ws_bytes,
                gemm_workspace_bytes(g));
-    if (cudaMemsetAsync(counters, 0, size_t(g.units / g.splits) * sizeof(int), stream) != cudaSuccess)
-      return check_launch("gemm_tf32x3 (counter reset)");
   }
   CUtensorMap map_a, map_b, map_c;
   TB_CHECK(make_map_f32_ld(&map_a, a, k, m, lda, kBK, kBM, true));
@@ -529,8 +473,12 @@ int gemm_tf32x3_impl(const float *a, int64_t lda, const float *b, int64_t ldb, i
   int sms = 0;
   TB_CHECK(sm_count(&sms));
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(g.units, sms));
-  gemm_tf32x3_kernel<<<grid, kThreads, smem, stream>>>(map_a, map_b, map_c, g, bias, c, partial, counters);
-  return check_launch("gemm_tf32x3");
+  gemm_tf32x3_kernel<<<grid, kThreads, smem, stream>>>(map_a, map_b, map_c, g, bias, c, partial);
+  TB_CHECK(check_launch("gemm_tf32x3"));
+  if (g.splits == 1) return TROPNN_B200_OK;
+  // The slices summed in slice order, plus the bias.
+  return slice_reduce_impl(kReduceF32, partial, g.splits, g.n_tiles, kBN, m, n, c, TROPNN_B200_F32, ldc, bias,
+                           nullptr, TROPNN_B200_F32, 1.f, stream);
 }
 
 int transpose_f32_impl(const float *x, int64_t rows, int64_t cols, int64_t ldx, float *out, int64_t ldo,

@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
     const __grid_constant__ CUtensorMap map_ct, const LT *__restrict__ latent, const uint8_t *__restrict__ winner,
     const uint8_t *__restrict__ runner, const float *__restrict__ margins, float code_scale, int64_t rows, int H,
     int D, int kblocks, int bstages, int64_t row_blocks, const uint32_t *__restrict__ absmax, int vec_routes,
-    float *__restrict__ hidden) {
+    float *__restrict__ hidden, int splits, float4 *__restrict__ partial) {
   static_assert(K >= 2 && K <= kBK && K % 2 == 0, "cells must be even and at most 64");
   constexpr int kHeadsPerBlock = kBK / K;
   // Signed mode (router term of grad_z): the gm weights are scaled by the power-of-two gradient
@@ -210,8 +210,15 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
   // Every CTA walks the code table from its own starting k block (all CTAs reading the
   // same k block at once made its L2 lines the bottleneck); position kb of the walk is
   // k block kb + rot (mod kblocks).
-  const int rot = static_cast<int>(int64_t(blockIdx.x) * kblocks / gridDim.x);
-  auto kblock_at = [&](int kb) { return kb + rot < kblocks ? kb + rot : kb + rot - kblocks; };
+  // With the contraction split into `splits` slices of kps k blocks, unit u = (row block
+  // u / splits, slice u % splits) walks its slice from a rotated start the same way.
+  const int kps = kblocks / splits;
+  const int64_t units = row_blocks * splits;
+  const int rot = static_cast<int>(int64_t(blockIdx.x) * kps / gridDim.x);
+  auto kblock_at = [&](int64_t u, int kb) {
+    const int ks = static_cast<int>(u % splits);
+    return ks * kps + (kb + rot < kps ? kb + rot : kb + rot - kps);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < bstages; ++s) {
@@ -245,8 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
       for (int s = 0; s < kMaxBStages; ++s) issued[s] = 0;
       bool ok = true;
       int it = 0;
-      for (int64_t rb = blockIdx.x; rb < row_blocks && ok; rb += gridDim.x) {
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+      for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        for (int kb = 0; kb < kps; ++kb, ++it) {
           const int s = it % bstages;
           const uint32_t phase = uint32_t(it / bstages) & 1u;
           if (!wait_bar(&bs->b_empty[s], phase ^ 1u, bs)) {
@@ -254,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
             break;
           }
           mbar_expect_tx(&bs->b_full[s], uint32_t(b_stage_bytes));
-          tma_load_2d(b_smem + s * b_stage_bytes, &map_ct, &bs->b_full[s], kblock_at(kb) * kBK, 0);
+          tma_load_2d(b_smem + s * b_stage_bytes, &map_ct, &bs->b_full[s], kblock_at(u, kb) * kBK, 0);
           issued[s] = uint32_t(it / bstages) + 1;
         }
       }
@@ -267,13 +274,13 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
       bool ok = true;
       int bit = 0, ait = 0;
       uint32_t i = 0;
-      for (int64_t rb = blockIdx.x; rb < row_blocks && ok; rb += gridDim.x, ++i) {
+      for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x, ++i) {
         if (!wait_bar(&bs->acc_empty, (i & 1u) ^ 1u, bs)) {
           ok = false;
           break;
         }
         tmem_fence_after();
-        for (int kb = 0; kb < kblocks; ++kb, ++bit, ++ait) {
+        for (int kb = 0; kb < kps; ++kb, ++bit, ++ait) {
           const int sa = ait % kAStages, sb = bit % bstages;
           if (!wait_bar(&bs->a_full[sa], uint32_t(ait / kAStages) & 1u, bs) ||
               !wait_bar(&bs->b_full[sb], uint32_t(bit / bstages) & 1u, bs)) {
@@ -299,8 +306,8 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
     }
   } else if (warp < 2 + kBuildWarps) {
     // ---------------- one-hot builders ----------------
-    // Warps 2-5 build the even k items of the CTA's sequence (ait = i * kblocks + kb over
-    // its row blocks i), warps 6-9 the odd ones; each warp its TMEM lane quarter.
+    // Warps 2-5 build the even k items of the CTA's sequence (ait = i * kps + kb over its
+    // units i), warps 6-9 the odd ones; each warp its TMEM lane quarter.
     const int quarter = warp & 3;
     const int parity = (warp - 2) >> 2;
     const uint32_t lane_base = tmem_base + (uint32_t(quarter * 32) << 16) + kAColBase;
@@ -314,12 +321,12 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
       float m[kHeadsPerBlock];
     };
     auto fetch = [&](int a, Raw &raw) {
-      const int64_t ii = a / kblocks;
-      const int kb = static_cast<int>(a - ii * kblocks);
-      const int64_t rb = blockIdx.x + ii * gridDim.x;
-      if (rb >= row_blocks) return;
-      const int64_t row = rb * kBM + quarter * 32 + lane;
-      const int h0 = kblock_at(kb) * kHeadsPerBlock;
+      const int64_t ii = a / kps;
+      const int kb = static_cast<int>(a - ii * kps);
+      const int64_t u = blockIdx.x + ii * gridDim.x;
+      if (u >= units) return;
+      const int64_t row = (u / splits) * kBM + quarter * 32 + lane;
+      const int h0 = kblock_at(u, kb) * kHeadsPerBlock;
       const int valid = row < rows ? max(0, min(kHeadsPerBlock, H - h0)) : 0;
       const int64_t o = (row < rows ? row : 0) * H + h0;
       if (vec_routes && valid == kHeadsPerBlock) {
@@ -344,9 +351,9 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
     Raw nxt;
     if constexpr (kPrefetch) fetch(parity, nxt);
     for (int ait = parity;; ait += 2) {
-      const int64_t i = ait / kblocks;
-      const int64_t rb = blockIdx.x + i * gridDim.x;
-      if (rb >= row_blocks || !ok) break;
+      const int64_t i = ait / kps;
+      const int64_t u = blockIdx.x + i * gridDim.x;
+      if (u >= units || !ok) break;
       Raw cur;
       if constexpr (kPrefetch) {
         cur = nxt;
@@ -414,24 +421,34 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
     const int quarter = warp & 3;
     const uint32_t lane_base = tmem_base + (uint32_t(quarter * 32) << 16);
     uint32_t i = 0;
-    for (int64_t rb = blockIdx.x; rb < row_blocks; rb += gridDim.x, ++i) {
-      const int64_t row = rb * kBM + quarter * 32 + lane;
+    for (int64_t u = blockIdx.x; u < units; u += gridDim.x, ++i) {
+      const int64_t row = (u / splits) * kBM + quarter * 32 + lane;
       if (!warp_wait_sleep(&bs->acc_full, i & 1u, bs, lane)) break;
       tmem_fence_after();
       for (int c = 0; c < D; c += 32) {
         float acc[32];
         tmem_ld32(lane_base + uint32_t(c), acc);
         float lat[32];
-        if (row < rows) load_row32<LT>(latent + row * D + c, lat);
+        if (splits == 1 && row < rows) load_row32<LT>(latent + row * D + c, lat);
         tmem_wait_ld();
         reg_fence(acc);
         if (c + 32 >= D) {
-          // The accumulator is in registers: the next row block may start.
+          // The accumulator is in registers: the next unit may start.
           tmem_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bs->acc_empty);
         }
-        if (row < rows) {
+        if (splits > 1) {
+          // Slice partial for slice_reduce: [unit][column / 4][row], row index fastest, with the
+          // signed mode's power-of-two gradient scale undone (exact; slice_reduce applies
+          // code_scale and adds the latent).
+          const float unscale = pow2_inverse(gscale);
+          float4 *p = partial + (size_t(u) * (D / 4) + c / 4) * kBM + quarter * 32 + lane;
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            p[size_t(e) * kBM] = make_float4(__fmul_rn(acc[4 * e], unscale), __fmul_rn(acc[4 * e + 1], unscale),
+                                             __fmul_rn(acc[4 * e + 2], unscale), __fmul_rn(acc[4 * e + 3], unscale));
+        } else if (row < rows) {
           float *out = hidden + row * D + c;
 #pragma unroll
           for (int e = 0; e < 32; e += 4)
@@ -475,10 +492,33 @@ int b_stages(int D) {
   return s >= kMinBStages ? s : 0;
 }
 
+constexpr int kTargetUnits = 148;  // B200 SMs
+constexpr int kMaxSplits = 16;
+constexpr int kMinKBlocksPerSplit = 8;
+
+// Slices of the (head, cell) contraction: 1 with enough row blocks for the SMs, else the
+// largest divisor of the k-block count up to the SMs' share of the row blocks (>= 8 k blocks
+// a slice).
+int onehot_splits(int64_t rows, int64_t hk) {
+  const int64_t row_blocks = ceil_div(rows, int64_t(kBM));
+  const int kblocks = static_cast<int>(ceil_div(hk, int64_t(kBK)));
+  if (row_blocks * 4 >= int64_t(kTargetUnits) * 3) return 1;
+  const int want = static_cast<int>(std::min<int64_t>(kMaxSplits, ceil_div(kTargetUnits, row_blocks)));
+  for (int s = want; s > 1; --s)
+    if (kblocks % s == 0 && kblocks / s >= kMinKBlocksPerSplit) return s;
+  return 1;
+}
+
+size_t onehot_workspace(int64_t rows, int64_t D, int64_t hk) {
+  const int splits = onehot_splits(rows, hk);
+  if (splits == 1) return 0;
+  return WorkspaceCarver::align(size_t(ceil_div(rows, int64_t(kBM))) * splits * size_t(D) * kBM * sizeof(float));
+}
+
 template <typename PT, typename LT, int K>
 int launch_onehot(const void *latent, int64_t rows, int D, const void *code_t, int H, const uint8_t *win,
                   const uint8_t *run, const float *m, float code_scale, int mode, const uint32_t *absmax, float *hidden,
-                  cudaStream_t stream) {
+                  void *ws, size_t ws_bytes, cudaStream_t stream) {
   const CUtensorMapDataType dt =
       std::is_same<PT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int64_t hk = int64_t(H) * K;
@@ -490,9 +530,17 @@ int launch_onehot(const void *latent, int64_t rows, int D, const void *code_t, i
   // CTA allocates all 512 TMEM columns.
   const size_t smem = std::max<size_t>(1024 + size_t(bst) * D * 128 + kRowBufBytes + sizeof(Barriers), 120 * 1024);
   const int64_t row_blocks = ceil_div(rows, int64_t(kBM));
+  // Few row blocks: split the contraction when the caller gave room for the slice partials.
+  int splits = onehot_splits(rows, hk);
+  float4 *partial = nullptr;
+  if (splits > 1) {
+    WorkspaceCarver wc(ws, ws_bytes);
+    partial = wc.take<float4>(size_t(row_blocks) * splits * size_t(D / 4) * kBM);
+    if (partial == nullptr) splits = 1;
+  }
   int sms = 0;
   TB_CHECK(sm_count(&sms));
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(row_blocks, sms));
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(row_blocks * splits, sms));
   // Vector loads of an item's 64 / K consecutive heads: whole vectors inside each row and
   // 16-byte aligned route / margin arrays.
   auto al16 = [](const void *p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
@@ -502,22 +550,28 @@ int launch_onehot(const void *latent, int64_t rows, int D, const void *code_t, i
                                          : trop_hidden_onehot_kernel<PT, LT, K, kOneHotEval>;
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_hidden_sm100"));
   kernel<<<grid, kThreads, smem, stream>>>(map_ct, static_cast<const LT *>(latent), win, run, m, code_scale, rows, H, D,
-                                           kblocks, bst, row_blocks, absmax, vec_routes, hidden);
-  return check_launch("trop_hidden_sm100");
+                                           kblocks, bst, row_blocks, absmax, vec_routes, hidden, splits, partial);
+  TB_CHECK(check_launch("trop_hidden_sm100"));
+  if (splits == 1) return TROPNN_B200_OK;
+  // hidden = latent + code_scale * (slices summed in slice order).
+  return slice_reduce_impl(kReduceHidden, partial, splits, 1, D, rows, D, hidden, TROPNN_B200_F32, D, nullptr, latent,
+                           std::is_same<LT, float>::value ? TROPNN_B200_F32
+                           : std::is_same<LT, __half>::value ? TROPNN_B200_F16 : TROPNN_B200_BF16,
+                           code_scale, stream);
 }
 
 template <typename PT, typename LT>
 int dispatch_onehot(int K, const void *latent, int64_t rows, int D, const void *code_t, int H, const uint8_t *win,
                     const uint8_t *run, const float *m, float code_scale, int mode, const uint32_t *absmax, float *hidden,
-                    cudaStream_t stream) {
+                    void *ws, size_t wsb, cudaStream_t stream) {
   switch (K) {
-    case 2: return launch_onehot<PT, LT, 2>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, stream);
-    case 4: return launch_onehot<PT, LT, 4>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, stream);
-    case 8: return launch_onehot<PT, LT, 8>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, stream);
+    case 2: return launch_onehot<PT, LT, 2>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, ws, wsb, stream);
+    case 4: return launch_onehot<PT, LT, 4>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, ws, wsb, stream);
+    case 8: return launch_onehot<PT, LT, 8>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, ws, wsb, stream);
     case 16:
-      return launch_onehot<PT, LT, 16>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, stream);
+      return launch_onehot<PT, LT, 16>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, ws, wsb, stream);
     default:
-      return launch_onehot<PT, LT, 32>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, stream);
+      return launch_onehot<PT, LT, 32>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, ws, wsb, stream);
   }
 }
 
@@ -532,9 +586,14 @@ bool hidden_sm100_supported(int64_t items, int64_t D, int64_t H, int64_t K, int 
          items >= kBM && b_stages(static_cast<int>(D)) > 0 && al16(latent) && al16(code_t) && al16(hidden);
 }
 
+size_t trop_hidden_sm100_workspace(int64_t items, int64_t D, int64_t H, int64_t K) {
+  if (items < 0 || D < 1 || H < 1 || K < 1) return 0;
+  return onehot_workspace(items, D, H * K);
+}
+
 int trop_hidden_sm100_impl(const void *latent, int zt, int64_t items, int64_t D, const void *code_t, int pt,
                            int64_t H, int64_t K, const void *win, const void *run, const float *m, float code_scale,
-                           int mode, const uint32_t *absmax, float *hidden, cudaStream_t stream) {
+                           int mode, const uint32_t *absmax, float *hidden, void *ws, size_t wsb, cudaStream_t stream) {
   TB_REQUIRE(hidden_sm100_supported(items, D, H, K, pt, zt, TROPNN_B200_U8, latent, code_t, hidden),
              TROPNN_B200_ERR_INVALID, "trop_hidden_sm100: unsupported shape, dtype or alignment");
   TB_REQUIRE(mode >= kOneHotEval && mode <= kOneHotSigned, TROPNN_B200_ERR_INVALID, "trop_hidden_sm100: bad mode");
@@ -545,15 +604,15 @@ int trop_hidden_sm100_impl(const void *latent, int zt, int64_t items, int64_t D,
   if (pt == TROPNN_B200_F16) {
     if (zt == TROPNN_B200_F32)
       return dispatch_onehot<__half, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, absmax, hidden,
-                                            stream);
+                                            ws, wsb, stream);
     return dispatch_onehot<__half, __half>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, absmax, hidden,
-                                           stream);
+                                           ws, wsb, stream);
   }
   if (zt == TROPNN_B200_F32)
     return dispatch_onehot<__nv_bfloat16, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, absmax, hidden,
-                                                 stream);
+                                                 ws, wsb, stream);
   return dispatch_onehot<__nv_bfloat16, __nv_bfloat16>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode,
-                                                       absmax, hidden, stream);
+                                                       absmax, hidden, ws, wsb, stream);
 }
 
 int trop_code_transpose_impl(const void *code, int pt, int64_t H, int64_t K, int64_t D, void *code_t,

@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     linear_grad_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                        const __grid_constant__ CUtensorMap map_b2, const __grid_constant__ CUtensorMap map_out, int n,
                        int kblocks, int stages, int m_extent, void *__restrict__ grad_w, int pt,
-                       float *__restrict__ grad_b) {
+                       float *__restrict__ grad_b, int dgrad_splits, float4 *__restrict__ dgrad_partial) {
   constexpr int KS = stage_k(KIND);
   constexpr uint32_t kABytes = a_tile_bytes(KIND);
   const uint32_t b_bytes = uint32_t(n) * KS * 4;
@@ -126,6 +126,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if constexpr (KIND == kWgrad) {
     kb_begin = static_cast<int>(int64_t(kblocks) * blockIdx.y / kSlices);
     kb_end = static_cast<int>(int64_t(kblocks) * (blockIdx.y + 1) / kSlices);
+  } else {
+    // DGRAD with few row blocks: CTA (x, y) contracts slice y of dgrad_splits (blockIdx.y).
+    kb_begin = static_cast<int>(int64_t(kblocks) * blockIdx.y / dgrad_splits);
+    kb_end = static_cast<int>(int64_t(kblocks) * (blockIdx.y + 1) / dgrad_splits);
   }
 
   if (threadIdx.x == 0) {
@@ -288,7 +292,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (KIND == kDgrad) {
       // 32 x 32 f32 tiles: registers -> this warp's 4 KB swizzled shared tile -> TMA store.
       uint8_t *stage = ring + (warp - 2) * 4096;
-      if (go) {
+      if (go && dgrad_partial != nullptr) {
+        // Slice partial for slice_reduce: [row block * splits + slice][column / 4][row].
+        float4 *p = dgrad_partial + (size_t(blockIdx.x) * dgrad_splits + blockIdx.y) * size_t(n / 4) * kBM + row;
+        for (int c = 0; c < n; c += 32) {
+          float v[32];
+          if (kb_end > kb_begin) {
+            load_sum(taddr + uint32_t(c), v);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            p[size_t(c / 4 + j) * kBM] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+      } else if (go) {
         for (int c = 0; c < n; c += 32) {
           float v[32];
           load_sum(taddr + uint32_t(c), v);
@@ -425,8 +444,23 @@ bool linear_grad_supported(int64_t rows, int64_t out_features, int64_t in_featur
          grad_stages(kDgrad, static_cast<int>(in_features)) > 0 && grad_stages(kWgrad, static_cast<int>(in_features)) > 0;
 }
 
+// DGRAD's contraction (out_features) in slices when the row blocks leave most SMs idle.
+constexpr int kDgradTargetCtas = 148;
+int dgrad_splits(int64_t rows, int64_t out_features) {
+  const int64_t row_blocks = ceil_div(rows, int64_t(kBM));
+  const int64_t kblocks = ceil_div(out_features, int64_t(stage_k(kDgrad)));
+  if (row_blocks * 4 >= int64_t(kDgradTargetCtas) * 3) return 1;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({16, ceil_div(kDgradTargetCtas, row_blocks), kblocks / 8})));
+}
+
+size_t dgrad_workspace(int64_t rows, int64_t out_features, int64_t in_features) {
+  const int s = dgrad_splits(rows, out_features);
+  if (s == 1) return 0;
+  return WorkspaceCarver::align(size_t(ceil_div(rows, int64_t(kBM))) * s * size_t(in_features) * kBM * sizeof(float));
+}
+
 int linear_dgrad_impl(const float *g, int64_t rows, int64_t out_features, const float *weight32, int64_t in_features,
-                      float *grad_hidden, cudaStream_t stream) {
+                      float *grad_hidden, void *ws, size_t ws_bytes, cudaStream_t stream) {
   TB_REQUIRE(linear_grad_supported(rows, out_features, in_features), TROPNN_B200_ERR_INVALID,
              "linear_dgrad: unsupported shape rows=%lld out=%lld in=%lld", (long long)rows, (long long)out_features,
              (long long)in_features);
@@ -443,10 +477,22 @@ int linear_dgrad_impl(const float *g, int64_t rows, int64_t out_features, const 
   auto kernel = linear_grad_kernel<kDgrad>;
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "linear_dgrad"));
   const int kblocks = static_cast<int>(ceil_div(out_features, int64_t(stage_k(kDgrad))));
-  const unsigned grid = static_cast<unsigned>(ceil_div(rows, int64_t(kBM)));
+  const int64_t row_blocks = ceil_div(rows, int64_t(kBM));
+  // Few row blocks: split the contraction when the caller gave room for the slice partials.
+  int splits = dgrad_splits(rows, out_features);
+  float4 *partial = nullptr;
+  if (splits > 1) {
+    WorkspaceCarver wc(ws, ws_bytes);
+    partial = wc.take<float4>(size_t(row_blocks) * splits * size_t(n / 4) * kBM);
+    if (partial == nullptr) splits = 1;
+  }
+  const dim3 grid(static_cast<unsigned>(row_blocks), static_cast<unsigned>(splits));
   kernel<<<grid, kThreads, smem, stream>>>(map_a, map_b, map_b, map_out, n, kblocks, stages, static_cast<int>(rows),
-                                           nullptr, 0, nullptr);
-  return check_launch("linear_dgrad");
+                                           nullptr, 0, nullptr, splits, partial);
+  TB_CHECK(check_launch("linear_dgrad"));
+  if (splits == 1) return TROPNN_B200_OK;
+  return slice_reduce_impl(kReduceF32, partial, splits, 1, n, rows, in_features, grad_hidden, TROPNN_B200_F32,
+                           in_features, nullptr, nullptr, TROPNN_B200_F32, 1.f, stream);
 }
 
 int linear_wgrad_impl(const float *g, int64_t rows, int64_t out_features, const float *hidden_big,
@@ -483,7 +529,8 @@ int linear_wgrad_impl(const float *g, int64_t rows, int64_t out_features, const 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, map_a, map_b, map_b2, map_a, n, kblocks, stages,
-                                             static_cast<int>(out_features), grad_weight, dtype, grad_bias);
+                                             static_cast<int>(out_features), grad_weight, dtype, grad_bias, 1,
+                                             static_cast<float4 *>(nullptr));
   if (err != cudaSuccess)
     return set_error(TROPNN_B200_ERR_LAUNCH, "linear_wgrad launch failed: %s", cudaGetErrorString(err));
   return check_launch("linear_wgrad");
@@ -522,12 +569,18 @@ int read_linear_grad_error(int *value) {
 
 extern "C" {
 
+size_t tropnn_b200_linear_dgrad_workspace_size(int64_t rows, int64_t out_features, int64_t in_features) {
+  if (rows < 1 || out_features < 1 || in_features < 1) return 0;
+  return tropnn_b200::dgrad_workspace(rows, out_features, in_features);
+}
+
 int tropnn_b200_linear_dgrad(const float *g, int64_t rows, int64_t out_features, const float *weight32,
-                             int64_t in_features, float *grad_hidden, void *stream) {
+                             int64_t in_features, float *grad_hidden, void *workspace, size_t workspace_bytes,
+                             void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
   if (rows == 0) return tropnn_b200::clear_error();
-  TB_CHECK(tropnn_b200::linear_dgrad_impl(g, rows, out_features, weight32, in_features, grad_hidden,
-                                          tropnn_b200::as_stream(stream)));
+  TB_CHECK(tropnn_b200::linear_dgrad_impl(g, rows, out_features, weight32, in_features, grad_hidden, workspace,
+                                          workspace_bytes, tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 

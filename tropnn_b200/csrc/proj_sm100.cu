@@ -12,9 +12,9 @@
 // unit covers all of `in` (one slice); with few (small batches, or one GPU's shard of a
 // strong-scaled batch) the contraction is cut into up to 16 slices so that every SM has a
 // unit: each slice's f32 partial goes to the caller's workspace in a TMEM-native layout
-// (row index fastest: coalesced stores), and the CTA that completes a row block's last
-// slice (a per-row-block arrival counter) sums the slices in slice order, so results are
-// deterministic. Persistent grid, one CTA per SM, contiguous unit ranges. CTA = 14 warps:
+// (row index fastest: coalesced stores), and slice_reduce (launched next, stream-ordered)
+// sums the slices in slice order and rounds them, so results are deterministic.
+// Persistent grid, one CTA per SM, contiguous unit ranges. CTA = 14 warps:
 //   warp 0      TMA producer: per k block two 128 x 32 f32 boxes of x (128-byte swizzle)
 //               and the code_dim x 64 tile of P, into a 3-4 stage ring.
 //   warp 1      allocates 2 x code_dim TMEM columns (double-buffered f32 accumulator);
@@ -24,7 +24,7 @@
 //               128-byte-swizzle layout the MMA reads as its A operand.
 //   warps 6-13  epilogue: 64-column chunks of the accumulator, rounded to the parameter
 //               dtype, staged in shared memory and written with TMA stores (or written as
-//               f32 slice partials, and reduced by the row block's last slice).
+//               f32 slice partials for slice_reduce).
 // Every wait is bounded (sm100.cuh): a wait that gives up sets the library's device error
 // word, the other roles leave, copies and MMAs in flight are drained and TMEM is freed.
 // Every TMA load is a plain per-CTA load of this GPU's own memory.
@@ -71,7 +71,6 @@ struct Barriers {
   uint32_t tmem_base;
   int abort;
   int epi_go[2];
-  int last[2];
 };
 
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, Barriers *bs) {
@@ -134,38 +133,11 @@ __device__ __forceinline__ void store_chunk(const float (&v)[64], uint8_t *stage
   }
 }
 
-// Sum over `splits` slice partials at base[s * slice_stride + offset] in slice order, with up
-// to 4 slices' loads in flight at once.
-__device__ __forceinline__ float4 sum_slices(const float4 *base, int splits, size_t slice_stride, size_t offset) {
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s0 = 0; s0 < splits; s0 += 4) {
-    float4 q[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (s0 + i < splits) q[i] = __ldcg(base + size_t(s0 + i) * slice_stride + offset);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (s0 + i < splits) {
-        if (s0 + i == 0) {
-          acc = q[i];
-        } else {
-          acc.x = __fadd_rn(acc.x, q[i].x);
-          acc.y = __fadd_rn(acc.y, q[i].y);
-          acc.z = __fadd_rn(acc.z, q[i].z);
-          acc.w = __fadd_rn(acc.w, q[i].w);
-        }
-      }
-    }
-  }
-  return acc;
-}
-
 template <typename PT>
 __global__ void __launch_bounds__(kThreads, 1) trop_proj_kernel(const __grid_constant__ CUtensorMap map_x,
                                                                 const __grid_constant__ CUtensorMap map_p,
                                                                 const __grid_constant__ CUtensorMap map_z,
-                                                                const ProjGeom g, float4 *__restrict__ partial,
-                                                                int *__restrict__ counters) {
+                                                                const ProjGeom g, float4 *__restrict__ partial) {
   constexpr int kFmt = std::is_same<PT, __half>::value ? 0 : 1;
   const uint32_t idesc = umma_idesc_f16(kFmt, kBM, g.D);
   const int stage_bytes = kXBytes + g.D * 128;
@@ -364,44 +336,6 @@ __global__ void __launch_bounds__(kThreads, 1) trop_proj_kernel(const __grid_con
       tmem_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bs->tmem_empty[b]);
-      if (g.splits == 1) continue;
-
-      // The row block's last slice to arrive sums the slices in slice order.
-      __threadfence();
-      epilogue_sync();
-      if (ew == 0 && lane == 0) {
-        const int old = atomicAdd(counters + rb, 1);
-        const int last = old == g.splits - 1;
-        if (last) counters[rb] = 0;  // ready for the next launch (stream order)
-        bs->last[b] = last;
-      }
-      epilogue_sync();
-      if (*reinterpret_cast<volatile int *>(&bs->last[b]) == 0) continue;
-      __threadfence();
-      const float4 *base = partial + size_t(rb) * g.splits * (g.D / 4) * kBM + r;
-      for (int ch = group; ch < chunks; ch += 2) {
-        if (lane == 0) bulk_wait_read_all();  // the previous store has read the staging tile
-        __syncwarp();
-        uint8_t *my_row = stage + lane * 128;
-#pragma unroll 1
-        for (int m = 0; m < 8; ++m) {
-          // 8 columns: two float4 of every slice, summed in slice order, rounded to PT.
-          const float4 lo = sum_slices(base, g.splits, size_t(g.D / 4) * kBM, size_t(ch * 16 + 2 * m) * kBM);
-          const float4 hi = sum_slices(base, g.splits, size_t(g.D / 4) * kBM, size_t(ch * 16 + 2 * m + 1) * kBM);
-          uint4 q;
-          q.x = pack2<PT>(lo.x, lo.y);
-          q.y = pack2<PT>(lo.z, lo.w);
-          q.z = pack2<PT>(hi.x, hi.y);
-          q.w = pack2<PT>(hi.z, hi.w);
-          *reinterpret_cast<uint4 *>(my_row + ((m ^ (lane & 7)) << 4)) = q;
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&map_z, stage, ch * 64, row0);
-          bulk_commit();
-        }
-      }
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
@@ -451,9 +385,7 @@ ProjGeom proj_geometry(int64_t rows, int64_t in, int64_t D) {
 
 size_t proj_workspace_bytes(const ProjGeom &g) {
   if (g.splits == 1) return 0;
-  const int64_t row_blocks = g.units / g.splits;
-  return WorkspaceCarver::align(size_t(g.units) * size_t(g.D) * kBM * sizeof(float)) +
-         WorkspaceCarver::align(size_t(row_blocks) * sizeof(int));
+  return WorkspaceCarver::align(size_t(g.units) * size_t(g.D) * kBM * sizeof(float));
 }
 
 template <typename PT>
@@ -466,17 +398,12 @@ int launch_proj(const float *x, const void *P, void *z, const ProjGeom &g, int64
   TB_CHECK(make_map_k64(&map_p, P, dt, in, g.D, kPBoxRows));
   TB_CHECK(make_map_k64(&map_z, z, dt, g.D, g.rows, 32));
   float4 *partial = nullptr;
-  int *counters = nullptr;
   if (g.splits > 1) {
     WorkspaceCarver c(ws, ws_bytes);
     partial = c.take<float4>(size_t(g.units) * size_t(g.D / 4) * kBM);
-    counters = c.take<int>(size_t(g.units / g.splits));
-    TB_REQUIRE(partial != nullptr && counters != nullptr, TROPNN_B200_ERR_WORKSPACE,
+    TB_REQUIRE(partial != nullptr, TROPNN_B200_ERR_WORKSPACE,
                "trop_proj: workspace of %zu bytes is smaller than the %zu bytes required", ws_bytes,
                proj_workspace_bytes(g));
-    // Arrival counters start at zero (each launch's last slice resets its row block's).
-    if (cudaMemsetAsync(counters, 0, size_t(g.units / g.splits) * sizeof(int), stream) != cudaSuccess)
-      return check_launch("trop_proj (counter reset)");
   }
   const size_t smem = proj_smem_bytes(g.D, g.stages);
   auto kernel = trop_proj_kernel<PT>;
@@ -484,8 +411,13 @@ int launch_proj(const float *x, const void *P, void *z, const ProjGeom &g, int64
   int sms = 0;
   TB_CHECK(sm_count(&sms));
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(g.units, sms));
-  kernel<<<grid, kThreads, smem, stream>>>(map_x, map_p, map_z, g, partial, counters);
-  return check_launch("trop_proj");
+  kernel<<<grid, kThreads, smem, stream>>>(map_x, map_p, map_z, g, partial);
+  TB_CHECK(check_launch("trop_proj"));
+  if (g.splits == 1) return TROPNN_B200_OK;
+  // The slices summed in slice order and rounded to the parameter dtype.
+  return slice_reduce_impl(kReduceHalf, partial, g.splits, 1, g.D, g.rows, g.D, z,
+                           std::is_same<PT, __half>::value ? TROPNN_B200_F16 : TROPNN_B200_BF16, g.D, nullptr, nullptr,
+                           TROPNN_B200_F32, 1.f, stream);
 }
 
 }  // namespace

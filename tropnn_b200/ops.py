@@ -428,6 +428,14 @@ def _tc_backward_eligible(items: int, code_dim: int, heads: int, cells: int, dty
     )
 
 
+def _hidden_workspace(lib: Any, items: int, code_dim: int, heads: int, cells: int, dev: torch.device) -> Tensor | None:
+    """Room for the slice partials of the tensor-core code sum / router term when a batch has
+    too few 128-row blocks for the SMs (tropnn_b200_trop_hidden_workspace_size; None when it
+    runs unsplit)."""
+    nbytes = int(lib.tropnn_b200_trop_hidden_workspace_size(items, code_dim, heads, cells))
+    return torch.empty(nbytes, device=dev, dtype=torch.uint8) if nbytes else None
+
+
 def _trop_backward_tensor_cores(ctx, g, z, weight, code, winner, runner, margins, lib, stream):
     """Min-face backward as four tcgen05 GEMMs (layers/tropical_exact.py:204-237):
     gm from <g, c_r - c_w> (split-f32 g against the code table, route-picking epilogue),
@@ -462,9 +470,11 @@ def _trop_backward_tensor_cores(ctx, g, z, weight, code, winner, runner, margins
         _launch("trop_code_transpose", lib.tropnn_b200_trop_code_transpose, weight.data_ptr(), pdt, heads, cells, code_dim,
                 w_t.data_ptr(), stream)
         grad_z = torch.empty((items, code_dim), device=dev, dtype=torch.float32)
+        ws = _hidden_workspace(lib, items, code_dim, heads, cells, dev)
         _launch(
             "trop_router_term", lib.tropnn_b200_trop_router_term, g.data_ptr(), items, code_dim, w_t.data_ptr(), pdt, heads,
-            cells, winner.data_ptr(), runner.data_ptr(), gm.data_ptr(), gmax.data_ptr(), grad_z.data_ptr(), stream,
+            cells, winner.data_ptr(), runner.data_ptr(), gm.data_ptr(), gmax.data_ptr(), grad_z.data_ptr(),
+            nat.ptr(ws), 0 if ws is None else ws.numel(), stream,
         )
     else:
         grad_z = g
@@ -570,6 +580,7 @@ class _TropRouteB200Function(torch.autograd.Function):
                 code_t.data_ptr(),
                 stream,
             )
+        hidden_ws = _hidden_workspace(lib, items, code_dim, heads, cells, dev) if code_t is not None else None
         _launch(
             "trop_hidden",
             lib.tropnn_b200_trop_hidden,
@@ -589,6 +600,8 @@ class _TropRouteB200Function(torch.autograd.Function):
             float(code_scale),
             int(bool(training)),
             hidden.data_ptr(),
+            nat.ptr(hidden_ws),
+            0 if hidden_ws is None else hidden_ws.numel(),
             stream,
         )
         ctx.save_for_backward(z, weight, code_c, winner, runner, margins)
@@ -876,7 +889,7 @@ def trop_exact_eval_b200(
                 margins.data_ptr() if margins.numel() else None, stream)
         _launch("trop_hidden", lib.tropnn_b200_trop_hidden, base.data_ptr(), nat.F32, items, out_features, v.data_ptr(),
                 None, nat.F32, heads, cells, winner.data_ptr(), None, icode, None, float(code_scale), 0, y.data_ptr(),
-                stream)
+                None, 0, stream)
     return y, winner, margins
 
 
@@ -961,9 +974,11 @@ class _LinearF32OutFunction(torch.autograd.Function):
         if ctx.needs_input_grad[0]:
             w32 = w.to(torch.float32).contiguous()
             grad_h = torch.empty((rows, in_features), device=dev, dtype=torch.float32)
+            ws_bytes = int(lib.tropnn_b200_linear_dgrad_workspace_size(rows, out_features, in_features))
+            ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8) if ws_bytes else None
             _launch(
                 "linear_dgrad", lib.tropnn_b200_linear_dgrad, g.data_ptr(), rows, out_features, w32.data_ptr(),
-                in_features, grad_h.data_ptr(), stream,
+                in_features, grad_h.data_ptr(), nat.ptr(ws), ws_bytes, stream,
             )
         if ctx.needs_input_grad[1] or need_b:
             h_big = torch.empty_like(h)
