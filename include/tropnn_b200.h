@@ -265,12 +265,20 @@ TROPNN_B200_API int tropnn_b200_pairwise_backward_noalloc(const float *grad_out,
  * [heads, cells] in bias_dtype (F32 or param_dtype). winner_i64 (int64 [items, heads])
  * may be NULL; winner in index_dtype (U8/I16/I64, the packing of routing.py:18-31);
  * runner (index_dtype) and margins (f32 [items, heads]) may be NULL when not needed.
+ * F32 latent, parameters and bias with U8 routes, cells in {2,4,8,16,32}, code_dim a
+ * multiple of 4 up to 128 and a `workspace` of tropnn_b200_trop_route_workspace_size() bytes:
+ * the scores run on the tensor cores as well, in kind::tf32 with every operand split into two
+ * tf32 parts (3xTF32, ~2^-22 relative per product; the split operands go to the workspace).
+ * With a NULL or smaller workspace those shapes take the fp32 FMA path.
  */
+TROPNN_B200_API size_t tropnn_b200_trop_route_workspace_size(int64_t items, int64_t code_dim, int64_t heads,
+                                                             int64_t cells, int latent_dtype, int param_dtype);
 TROPNN_B200_API int tropnn_b200_trop_route(const void *latent, int latent_dtype, int64_t items, int64_t code_dim,
                            const void *router_weight, const void *router_bias, int bias_dtype, int param_dtype,
                            int64_t heads, int64_t cells,
                            int64_t *winner_i64, void *winner, void *runner, int index_dtype,
-                           float *margins, void *stream);
+                           float *margins, void *workspace,
+                           size_t workspace_bytes, void *stream);
 
 /*
  * Input projection z = P(x) (layers/tropical.py:96-99, `proj(x.to(P.dtype))`) for half-precision

@@ -36,7 +36,7 @@ def _routes(z, weight, bias):
         lib.tropnn_b200_trop_route(
             z.data_ptr(), nat.float_code(z.dtype), items, code_dim, weight.data_ptr(), bias.float().data_ptr(), nat.F32,
             nat.float_code(weight.dtype), heads, cells, None, win.data_ptr(), run.data_ptr(), nat.U8, m.data_ptr(),
-            torch.cuda.current_stream().cuda_stream,
+            None, 0, torch.cuda.current_stream().cuda_stream,
         ),
         "trop_route",
     )

@@ -59,6 +59,7 @@ constexpr int kEpiCols = kBN * 4 / kEpiWarps;  // accumulator columns per epilog
 constexpr int kTmemCols = 2 * kBN;             // double-buffered accumulator: all 512 columns
 constexpr int kMaxKBlocks = 8;                 // code_dim <= 512
 constexpr size_t kSmemLimit = 227 * 1024;
+constexpr uint32_t kSleepHintNs = 1000000u;  // mbarrier suspend-time hint of whole-warp waits
 
 // Library-wide device error word: nonzero after a bounded wait gave up.
 __device__ int g_score_error = 0;
@@ -149,12 +150,16 @@ __device__ __forceinline__ void store_run(float *dst, const float (&v)[N]) {
   }
 }
 
-template <typename PT, int K>
+// BIAS_MMA: the bias enters the accumulator through one more K=16 MMA per unit: a constant
+// "ones" block (columns 0 and 1 of every row = 1) against the tile's rows of bias_ext
+// [H*K, 64] (column 0 = half(b), column 1 = half(b - half(b)), the rest 0), so the epilogue
+// adds nothing; otherwise the epilogue adds the f32 bias.
+template <typename PT, int K, bool BIAS_MMA>
 __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
-    const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_w, const float *__restrict__ bias,
-    int64_t rows, int H, int kblocks, int stages, int tiles_total, int64_t units, int flags, bool vec_stores,
-    int64_t *__restrict__ winner_i64, uint8_t *__restrict__ winner, uint8_t *__restrict__ runner,
-    float *__restrict__ margins) {
+    const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_w,
+    const __grid_constant__ CUtensorMap map_bias, const float *__restrict__ bias, int64_t rows, int H, int kblocks,
+    int stages, int tiles_total, int64_t units, int flags, bool vec_stores, int64_t *__restrict__ winner_i64,
+    uint8_t *__restrict__ winner, uint8_t *__restrict__ runner, float *__restrict__ margins) {
   static_assert(32 % K == 0 && K >= 2, "cells must divide 32");
   static_assert(kEpiCols % 32 == 0, "an epilogue warp reads whole 32-column chunks");
   constexpr int kHeadsPerGroup = kEpiCols / K;  // heads in one epilogue warp's columns
@@ -171,7 +176,8 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
   // 1024-byte alignment for the 128-byte swizzle atoms.
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *a_smem = smem;                                // kblocks x [128 rows x 128 B]
-  uint8_t *b_smem = a_smem + kblocks * kTileBytesA;      // stages x [256 rows x 128 B]
+  uint8_t *ones_smem = a_smem + kblocks * kTileBytesA;   // BIAS_MMA: the constant ones block
+  uint8_t *b_smem = ones_smem + (BIAS_MMA ? kTileBytesA : 0);  // stages x [256 rows x 128 B]
   Barriers *bs = reinterpret_cast<Barriers *>(b_smem + stages * kTileBytesB);
 
   const int warp = threadIdx.x >> 5;
@@ -199,16 +205,32 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
     __syncwarp();
     tmem_alloc(&bs->tmem_base, kTmemCols);
   }
+  if constexpr (BIAS_MMA) {
+    if (warp >= 2 && warp < 6) {
+      // Row r of the ones block (K-major, 128-byte swizzle): elements 0 and 1 are 1, the
+      // rest 0 (element 0 sits in 16-byte chunk 0, stored at chunk 0 ^ (r & 7)).
+      const int r = (warp - 2) * 32 + lane;
+      constexpr uint32_t kOne = std::is_same<PT, __half>::value ? 0x3C00u : 0x3F80u;
+      uint8_t *row = ones_smem + r * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<uint4 *>(row + ((j ^ (r & 7)) << 4)) =
+            j == 0 ? make_uint4(kOne | (kOne << 16), 0u, 0u, 0u) : make_uint4(0u, 0u, 0u, 0u);
+      fence_proxy_async_smem();
+    }
+  }
   tmem_fence_before();
   __syncthreads();
   tmem_fence_after();
   const uint32_t tmem_base = bs->tmem_base;
+  const int ksteps = kblocks + (BIAS_MMA ? 1 : 0);  // ring stages per unit
 
   if (warp == 0) {
     if (lane == 0 && u_begin < u_end) {
       // ---------------- TMA producer ----------------
       prefetch_map(&map_z);
       prefetch_map(&map_w);
+      if constexpr (BIAS_MMA) prefetch_map(&map_bias);
       uint32_t issued[kMaxStages];
       for (int s = 0; s < kMaxStages; ++s) issued[s] = 0;
       bool ok = true;
@@ -229,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
           ++a_loads;
           cur_rb = rb;
         }
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        for (int kb = 0; kb < ksteps; ++kb, ++it) {
           const int s = it % stages;
           const uint32_t phase = uint32_t(it / stages) & 1u;
           if (!mbar_wait(&bs->empty[s], phase ^ 1u, bs)) {
@@ -237,9 +259,11 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
             break;
           }
           mbar_expect_tx(&bs->full[s], kTileBytesB);
+          // The weight k blocks, then (BIAS_MMA) the tile's rows of bias_ext.
+          const CUtensorMap *map = kb < kblocks ? &map_w : &map_bias;
+          const int x = kb < kblocks ? kb * kBK : 0;
           for (int q = 0; q < kBN / kBoxRows; ++q)
-            tma_load_2d(b_smem + s * kTileBytesB + q * kBoxRows * 128, &map_w, &bs->full[s], kb * kBK,
-                        tile * kBN + q * kBoxRows);
+            tma_load_2d(b_smem + s * kTileBytesB + q * kBoxRows * 128, map, &bs->full[s], x, tile * kBN + q * kBoxRows);
           issued[s] = uint32_t(it / stages) + 1;
         }
       }
@@ -277,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
         }
         tmem_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(b * kBN);
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        for (int kb = 0; kb < ksteps; ++kb, ++it) {
           const int s = it % stages;
           const uint32_t phase = uint32_t(it / stages) & 1u;
           if (!mbar_wait(&bs->full[s], phase, bs)) {
@@ -285,12 +309,17 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
             break;
           }
           tmem_fence_after();
-          const uint32_t a_base = smem_addr(a_smem + kb * kTileBytesA);
           const uint32_t b_base = smem_addr(b_smem + s * kTileBytesB);
+          if (kb < kblocks) {
+            const uint32_t a_base = smem_addr(a_smem + kb * kTileBytesA);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_f16(d_tmem, umma_desc_sw128(a_base + kk * 32), umma_desc_sw128(b_base + kk * 32), kIdesc,
-                     (kb | kk) != 0 ? 1u : 0u);
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma_f16(d_tmem, umma_desc_sw128(a_base + kk * 32), umma_desc_sw128(b_base + kk * 32), kIdesc,
+                       (kb | kk) != 0 ? 1u : 0u);
+          } else {
+            // Bias: ones (columns 0, 1) x bias_ext (columns 0, 1), one K=16 step.
+            umma_f16(d_tmem, umma_desc_sw128(smem_addr(ones_smem)), umma_desc_sw128(b_base), kIdesc, 1u);
+          }
           umma_commit(&bs->empty[s]);
         }
         if (!ok) break;
@@ -315,16 +344,15 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
       const int h0 = tile * kHeadsPerTile + group * kHeadsPerGroup;
       const int64_t c0 = int64_t(tile) * kBN + group * kEpiCols;
       const int64_t row = rb * kBM + r;
-      // One epilogue thread polls the accumulator barrier and the others wait on a
-      // hardware named barrier (all epilogue warps polling slowed the TMA/MMA pipeline).
-      // The verdict passes through a two-slot flag: slot t&1 is rewritten two units later,
-      // after every epilogue warp has passed the next named barrier and so has read it.
-      // All epilogue warps thus take the same branch, and the .sync.aligned TMEM loads
-      // below run converged.
-      if (warp == 2 && lane == 0) bs->epi_go[b] = mbar_wait(&bs->tmem_full[b], use & 1u, bs) ? 1 : 0;
-      epilogue_sync();
-      if (*reinterpret_cast<volatile int *>(&bs->epi_go[b]) == 0) break;
+      // Lane 0 of every epilogue warp waits for the accumulator with the mbarrier suspend
+      // hint (sleeping between polls, so that 16 waiting warps take no issue slots from the
+      // TMA and MMA threads) and the warp follows its verdict, converged, so the .sync.aligned
+      // TMEM loads below run converged; warps start as soon as the accumulator is ready.
+      int go = 1;
+      if (lane == 0) go = mbar_wait_sleep(&bs->tmem_full[b], use & 1u, &bs->abort, &g_score_error, kSleepHintNs) ? 1 : 0;
       __syncwarp();
+      go = __shfl_sync(0xffffffffu, go, 0);
+      if (!go) break;
       tmem_fence_after();
       uint8_t wv[kStoreHeads], rv[kStoreHeads];
       float mv[kStoreHeads];
@@ -333,7 +361,12 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
       for (int c = 0; c < kEpiCols; c += 32) {
         float v[32], bv[32];
         tmem_ld32(taddr + uint32_t(c), v);
-        load_bias32(bias, c0 + c, hk, bv);  // in flight together with the TMEM read
+        if constexpr (BIAS_MMA) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) bv[i] = 0.f;
+        } else {
+          load_bias32(bias, c0 + c, hk, bv);  // in flight together with the TMEM read
+        }
         tmem_wait_ld();
         reg_fence(v);
         if (c + 32 == kEpiCols) {
@@ -359,9 +392,10 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
 #pragma unroll
           for (int p = 0; p < K / 2; ++p) {
             const int k = 2 * p;
-            const float x = packed_key<kIdxMask>(__fadd_rn(v[hh * K + k], bv[hh * K + k]), uint32_t(K - 1 - k));
-            const float y =
-                packed_key<kIdxMask>(__fadd_rn(v[hh * K + k + 1], bv[hh * K + k + 1]), uint32_t(K - 2 - k));
+            const float sx = BIAS_MMA ? v[hh * K + k] : __fadd_rn(v[hh * K + k], bv[hh * K + k]);
+            const float sy = BIAS_MMA ? v[hh * K + k + 1] : __fadd_rn(v[hh * K + k + 1], bv[hh * K + k + 1]);
+            const float x = packed_key<kIdxMask>(sx, uint32_t(K - 1 - k));
+            const float y = packed_key<kIdxMask>(sy, uint32_t(K - 2 - k));
             hi[p] = fmaxf(x, y);
             lo[p] = fminf(x, y);
           }
@@ -420,32 +454,61 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
 
 // --------------------------------------------------------------------------- host side
 
-size_t score_smem_bytes(int kblocks, int stages) {
-  return 1024 + size_t(kblocks) * kTileBytesA + size_t(stages) * kTileBytesB + sizeof(Barriers);
+size_t score_smem_bytes(int kblocks, int stages, bool bias_mma) {
+  return 1024 + size_t(kblocks + (bias_mma ? 1 : 0)) * kTileBytesA + size_t(stages) * kTileBytesB + sizeof(Barriers);
 }
 
-// Weight-ring depth: the shared memory left after the resident z block, up to kMaxStages;
-// 0 when fewer than kMinStages fit.
-int score_stages(int kblocks) {
-  const size_t fixed = score_smem_bytes(kblocks, 0);
+// Weight-ring depth: the shared memory left after the resident z block (and the ones block),
+// up to kMaxStages; 0 when fewer than kMinStages fit.
+int score_stages(int kblocks, bool bias_mma) {
+  const size_t fixed = score_smem_bytes(kblocks, 0, bias_mma);
   if (fixed >= kSmemLimit) return 0;
   const int stages = static_cast<int>(std::min<size_t>(kMaxStages, (kSmemLimit - fixed) / kTileBytesB));
   return stages >= kMinStages ? stages : 0;
 }
 
+// bias_ext[r, 0] = half(b[r]), bias_ext[r, 1] = half(b[r] - half(b[r])), the other 62 columns 0:
+// the right operand of the bias MMA step (b = hi + lo to ~2^-22 relative for f16, exactly for a
+// bias that is a half-precision parameter upcast).
+template <typename PT>
+__global__ void bias_ext_kernel(const float *__restrict__ bias, int64_t hk, PT *__restrict__ out) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= hk * 64) return;
+  const int64_t r = i >> 6;
+  const int c = static_cast<int>(i & 63);
+  float v = 0.f;
+  if (c < 2) {
+    const float b = __ldg(bias + r);
+    const float hi = to_f32<PT>(from_f32<PT>(b));
+    v = c == 0 ? hi : __fsub_rn(b, hi);
+  }
+  out[i] = from_f32<PT>(v);
+}
+
 template <typename PT, int K>
 int launch_score(const void *z, int64_t rows, int D, const void *W, const void *bias, int H, int64_t *w64,
-                 uint8_t *win, uint8_t *run, float *m, cudaStream_t stream) {
+                 uint8_t *win, uint8_t *run, float *m, void *bias_ext, cudaStream_t stream) {
   const CUtensorMapDataType dt =
       std::is_same<PT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int kblocks = (D + kBK - 1) / kBK;
-  const int stages = score_stages(kblocks);
+  const int64_t hk = int64_t(H) * K;
+  // The bias MMA needs room for bias_ext and a ring of at least kMinStages beside the ones block.
+  const bool bias_mma = bias_ext != nullptr && score_stages(kblocks, true) > 0;
+  const int stages = score_stages(kblocks, bias_mma);
   TB_REQUIRE(stages > 0, TROPNN_B200_ERR_INVALID, "trop_score_sm100: code_dim=%d does not fit shared memory", D);
-  const size_t smem = score_smem_bytes(kblocks, stages);
-  CUtensorMap map_z, map_w;
+  const size_t smem = score_smem_bytes(kblocks, stages, bias_mma);
+  CUtensorMap map_z, map_w, map_bias;
   TB_CHECK(make_map_k64(&map_z, z, dt, D, rows, kBM));
-  TB_CHECK(make_map_k64(&map_w, W, dt, D, int64_t(H) * K, kBoxRows));
-  const int tiles_total = static_cast<int>(ceil_div(int64_t(H) * K, kBN));
+  TB_CHECK(make_map_k64(&map_w, W, dt, D, hk, kBoxRows));
+  if (bias_mma) {
+    const unsigned blocks = static_cast<unsigned>(ceil_div(hk * 64, int64_t(256)));
+    bias_ext_kernel<PT><<<blocks, 256, 0, stream>>>(static_cast<const float *>(bias), hk, static_cast<PT *>(bias_ext));
+    TB_CHECK(check_launch("trop_score_sm100 (bias_ext)"));
+    TB_CHECK(make_map_k64(&map_bias, bias_ext, dt, 64, hk, kBoxRows));
+  } else {
+    map_bias = map_w;  // unused
+  }
+  const int tiles_total = static_cast<int>(ceil_div(hk, kBN));
   const int64_t units = ceil_div(rows, int64_t(kBM)) * tiles_total;
   int sms = 0;
   TB_CHECK(sm_count(&sms));
@@ -454,26 +517,339 @@ int launch_score(const void *z, int64_t rows, int D, const void *W, const void *
   constexpr int kRun = score_store_heads(K);
   auto al16 = [](const void *p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   const bool vec_stores = (H % kRun == 0) && al16(win) && al16(run) && al16(m);
-  auto kernel = trop_score_top2_kernel<PT, K>;
+  auto kernel = bias_mma ? trop_score_top2_kernel<PT, K, true> : trop_score_top2_kernel<PT, K, false>;
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_score_sm100"));
   // Persistent grid: one CTA per SM (shared memory and TMEM admit no second), units
   // split evenly.
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(units, sms));
-  kernel<<<grid, kThreads, smem, stream>>>(map_z, map_w, static_cast<const float *>(bias), rows, H, kblocks, stages,
-                                           tiles_total, units, flags, vec_stores, w64, win, run, m);
+  kernel<<<grid, kThreads, smem, stream>>>(map_z, map_w, map_bias, static_cast<const float *>(bias), rows, H, kblocks,
+                                           stages, tiles_total, units, flags, vec_stores, w64, win, run, m);
   return check_launch("trop_score_sm100");
 }
 
 template <typename PT>
 int dispatch_cells(int K, const void *z, int64_t rows, int D, const void *W, const void *bias, int H, int64_t *w64,
-                   uint8_t *win, uint8_t *run, float *m, cudaStream_t stream) {
+                   uint8_t *win, uint8_t *run, float *m, void *bias_ext, cudaStream_t stream) {
   switch (K) {
-    case 2: return launch_score<PT, 2>(z, rows, D, W, bias, H, w64, win, run, m, stream);
-    case 4: return launch_score<PT, 4>(z, rows, D, W, bias, H, w64, win, run, m, stream);
-    case 8: return launch_score<PT, 8>(z, rows, D, W, bias, H, w64, win, run, m, stream);
-    case 16: return launch_score<PT, 16>(z, rows, D, W, bias, H, w64, win, run, m, stream);
-    default: return launch_score<PT, 32>(z, rows, D, W, bias, H, w64, win, run, m, stream);
+    case 2: return launch_score<PT, 2>(z, rows, D, W, bias, H, w64, win, run, m, bias_ext, stream);
+    case 4: return launch_score<PT, 4>(z, rows, D, W, bias, H, w64, win, run, m, bias_ext, stream);
+    case 8: return launch_score<PT, 8>(z, rows, D, W, bias, H, w64, win, run, m, bias_ext, stream);
+    case 16: return launch_score<PT, 16>(z, rows, D, W, bias, H, w64, win, run, m, bias_ext, stream);
+    default: return launch_score<PT, 32>(z, rows, D, W, bias, H, w64, win, run, m, bias_ext, stream);
   }
+}
+
+// ---------------------------------------------------------------------------------------
+// f32 parameters: the same route on kind::tf32 with split operands (3xTF32).
+//
+// The reference's f32 scores (backend.py:45-46) have no f32 MMA to run on; with x = big +
+// small (big = tf32(x), small = tf32(x - big)) the products big*big' + big*small' +
+// small*big' keep about 2^-22 relative accuracy per product (3xTF32), far inside the 1e-4
+// relative margin gate that decides which routes are pinned. big*big' accumulates in one TMEM
+// accumulator and the cross terms in another (the accumulator's per-addition truncation then
+// stays at the level of the dominant sum), added in the epilogue before the top-2. z and the
+// router weights arrive split (tf32_split into the caller's workspace): the z block (big and
+// small, K-major f32, code_dim <= 128) is resident, the weight tiles stream through a ring of
+// 32 KB stages (big and small 128 x 32 f32 each). Unit = 128 rows x 128 score columns; two
+// units in flight use all 512 TMEM columns. Roles as the f16 kernel: warp 0 TMA, warp 1
+// TMEM + MMA (3 MMAs per 8-wide k step), warps 2-17 epilogue (32 columns each: one
+// tcgen05.ld of each accumulator, bias, top-2 per head).
+constexpr int kBNt = 128;                  // score columns per tf32 unit
+constexpr int kBKt = 32;                   // f32 per 128-byte swizzled row
+constexpr int kTileT = kBM * 128;          // one 128 x 32 f32 tile (16 KB)
+constexpr int kStageBytesT = 2 * kTileT;   // big + small weight tile
+constexpr int kMaxKBlocksT = 4;            // code_dim <= 128
+constexpr int kEpiColsT = kBNt * 4 / kEpiWarps;
+
+static_assert(kEpiColsT == 32, "the tf32 epilogue reads one 32-column chunk per warp");
+
+template <int K>
+__global__ void __launch_bounds__(kThreads, 1) trop_score_tf32_kernel(
+    const __grid_constant__ CUtensorMap map_zb, const __grid_constant__ CUtensorMap map_zs,
+    const __grid_constant__ CUtensorMap map_wb, const __grid_constant__ CUtensorMap map_ws,
+    const float *__restrict__ bias, int64_t rows, int H, int kblocks, int stages, int tiles_total, int64_t units,
+    int flags, bool vec_stores, int64_t *__restrict__ winner_i64, uint8_t *__restrict__ winner,
+    uint8_t *__restrict__ runner, float *__restrict__ margins) {
+  static_assert(32 % K == 0 && K >= 2, "cells must divide 32");
+  constexpr int kHeadsPerChunk = 32 / K;
+  constexpr int kHeadsPerTile = kBNt / K;
+  constexpr int kIdxBits = K <= 2 ? 1 : K <= 4 ? 2 : K <= 8 ? 3 : K <= 16 ? 4 : 5;
+  constexpr uint32_t kIdxMask = (1u << kIdxBits) - 1u;
+  constexpr uint32_t kIdesc = umma_idesc_tf32(false, false, kBM, kBNt);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *a_smem = smem;                                // kblocks x [z big | z small] (32 KB each)
+  uint8_t *b_smem = a_smem + kblocks * 2 * kTileT;       // stages x [w big | w small]
+  Barriers *bs = reinterpret_cast<Barriers *>(b_smem + stages * kStageBytesT);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t u_begin = units * blockIdx.x / gridDim.x;
+  const int64_t u_end = units * (blockIdx.x + 1) / gridDim.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&bs->full[s], 1);
+      mbar_init(&bs->empty[s], 1);
+    }
+    mbar_init(&bs->a_full, 1);
+    mbar_init(&bs->a_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bs->tmem_full[b], 1);
+      mbar_init(&bs->tmem_empty[b], kEpiWarps);
+    }
+    mbar_init(&bs->mma_done, 1);
+    bs->abort = 0;
+    mbar_init_fence();
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(&bs->tmem_base, kTmemCols);
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem_base = bs->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0 && u_begin < u_end) {
+      // ---------------- TMA producer ----------------
+      prefetch_map(&map_zb);
+      prefetch_map(&map_zs);
+      prefetch_map(&map_wb);
+      prefetch_map(&map_ws);
+      uint32_t issued[kMaxStages];
+      for (int s = 0; s < kMaxStages; ++s) issued[s] = 0;
+      bool ok = true;
+      int it = 0, a_loads = 0;
+      int64_t cur_rb = -1;
+      for (int64_t u = u_begin; u < u_end && ok; ++u) {
+        const int64_t rb = u / tiles_total;
+        const int tile = static_cast<int>(u - rb * tiles_total);
+        if (rb != cur_rb) {
+          if (a_loads > 0 && !mbar_wait(&bs->a_empty, uint32_t(a_loads - 1) & 1u, bs)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bs->a_full, uint32_t(kblocks) * 2 * kTileT);
+          for (int kb = 0; kb < kblocks; ++kb) {
+            tma_load_2d(a_smem + kb * 2 * kTileT, &map_zb, &bs->a_full, kb * kBKt, static_cast<int>(rb * kBM));
+            tma_load_2d(a_smem + kb * 2 * kTileT + kTileT, &map_zs, &bs->a_full, kb * kBKt, static_cast<int>(rb * kBM));
+          }
+          ++a_loads;
+          cur_rb = rb;
+        }
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % stages;
+          if (!mbar_wait(&bs->empty[s], (uint32_t(it / stages) & 1u) ^ 1u, bs)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bs->full[s], kStageBytesT);
+          tma_load_2d(b_smem + s * kStageBytesT, &map_wb, &bs->full[s], kb * kBKt, tile * kBNt);
+          tma_load_2d(b_smem + s * kStageBytesT + kTileT, &map_ws, &bs->full[s], kb * kBKt, tile * kBNt);
+          issued[s] = uint32_t(it / stages) + 1;
+        }
+      }
+      if (a_loads > 0) mbar_drain(&bs->a_full, uint32_t(a_loads - 1) & 1u);
+      for (int s = 0; s < stages; ++s)
+        if (issued[s] > 0) mbar_drain(&bs->full[s], (issued[s] - 1) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && u_begin < u_end) {
+      // ---------------- MMA issuer ----------------
+      bool ok = true;
+      int it = 0, a_uses = 0;
+      int64_t cur_rb = -1;
+      uint32_t t = 0;
+      for (int64_t u = u_begin; u < u_end && ok; ++u, ++t) {
+        const int64_t rb = u / tiles_total;
+        if (rb != cur_rb) {
+          if (a_uses > 0) umma_commit(&bs->a_empty);
+          if (!mbar_wait(&bs->a_full, uint32_t(a_uses) & 1u, bs)) {
+            ok = false;
+            break;
+          }
+          tmem_fence_after();
+          ++a_uses;
+          cur_rb = rb;
+        }
+        const int b = t & 1;
+        if (!mbar_wait(&bs->tmem_empty[b], ((t >> 1) & 1u) ^ 1u, bs)) {
+          ok = false;
+          break;
+        }
+        tmem_fence_after();
+        const uint32_t d_big = tmem_base + uint32_t(b * 2 * kBNt);
+        const uint32_t d_cross = d_big + kBNt;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % stages;
+          if (!mbar_wait(&bs->full[s], uint32_t(it / stages) & 1u, bs)) {
+            ok = false;
+            break;
+          }
+          tmem_fence_after();
+          const uint32_t za = smem_addr(a_smem + kb * 2 * kTileT), zs = za + kTileT;
+          const uint32_t wa = smem_addr(b_smem + s * kStageBytesT), ws = wa + kTileT;
+#pragma unroll
+          for (int kk = 0; kk < kBKt / 8; ++kk) {
+            const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+            const uint64_t dz = umma_desc_sw128(za + kk * 32), dw = umma_desc_sw128(wa + kk * 32);
+            umma_tf32(d_big, dz, dw, kIdesc, acc);
+            umma_tf32(d_cross, dz, umma_desc_sw128(ws + kk * 32), kIdesc, acc);
+            umma_tf32(d_cross, umma_desc_sw128(zs + kk * 32), dw, kIdesc, 1u);
+          }
+          umma_commit(&bs->empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&bs->tmem_full[b]);
+      }
+      umma_commit(&bs->mma_done);
+      mbar_drain(&bs->mma_done, 0);
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int quarter = warp & 3;
+    const int group = (warp - 2) >> 2;  // which 32 columns of the unit
+    const int r = quarter * 32 + lane;
+    const int64_t hk = int64_t(H) * K;
+    uint32_t t = 0;
+    for (int64_t u = u_begin; u < u_end; ++u, ++t) {
+      const int64_t rb = u / tiles_total;
+      const int tile = static_cast<int>(u - rb * tiles_total);
+      const int b = t & 1;
+      const int64_t row = rb * kBM + r;
+      const int64_t c0 = int64_t(tile) * kBNt + group * kEpiColsT;
+      int go = 1;
+      if (lane == 0) go = mbar_wait_sleep(&bs->tmem_full[b], (t >> 1) & 1u, &bs->abort, &g_score_error, kSleepHintNs) ? 1 : 0;
+      __syncwarp();
+      go = __shfl_sync(0xffffffffu, go, 0);
+      if (!go) break;
+      tmem_fence_after();
+      const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(b * 2 * kBNt + group * kEpiColsT);
+      float v[32];
+      {
+        float x[32];
+        tmem_ld32(taddr, v);
+        tmem_ld32(taddr + kBNt, x);
+        tmem_wait_ld();
+        reg_fence(v);
+        reg_fence(x);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], x[j]);  // big products + cross terms
+      }
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bs->tmem_empty[b]);
+      {
+        float bv[32];
+        load_bias32(bias, c0, hk, bv);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], bv[j]);
+      }
+      uint8_t wv[kHeadsPerChunk], rv[kHeadsPerChunk];
+      float mv[kHeadsPerChunk];
+#pragma unroll
+      for (int hh = 0; hh < kHeadsPerChunk; ++hh) {
+        // Top-2 on index-packed keys, as the f16 kernel (the cell index K-1-k in the lowest
+        // kIdxBits mantissa bits).
+        float hi[K / 2], lo[K / 2];
+#pragma unroll
+        for (int p = 0; p < K / 2; ++p) {
+          const int k = 2 * p;
+          const float a = packed_key<kIdxMask>(v[hh * K + k], uint32_t(K - 1 - k));
+          const float c = packed_key<kIdxMask>(v[hh * K + k + 1], uint32_t(K - 2 - k));
+          hi[p] = fmaxf(a, c);
+          lo[p] = fminf(a, c);
+        }
+#pragma unroll
+        for (int w = 1; w < K / 2; w *= 2) {
+#pragma unroll
+          for (int p = 0; p + w < K / 2; p += 2 * w) {
+            const float a1 = hi[p], b1 = hi[p + w];
+            lo[p] = fmax3(fminf(a1, b1), lo[p], lo[p + w]);
+            hi[p] = fmaxf(a1, b1);
+          }
+        }
+        const float k1 = hi[0], k2 = lo[0];
+        wv[hh] = static_cast<uint8_t>(K - 1 - (__float_as_uint(k1) & kIdxMask));
+        rv[hh] = static_cast<uint8_t>(K - 1 - (__float_as_uint(k2) & kIdxMask));
+        mv[hh] = __fsub_rn(k1, k2);
+      }
+      if (row < rows) {
+        const int hs = tile * kHeadsPerTile + group * kHeadsPerChunk;
+        const int64_t o = row * H + hs;
+        if (vec_stores && hs + kHeadsPerChunk <= H) {
+          store_run<kHeadsPerChunk>(winner + o, wv);
+          if (flags & kWriteRunner) store_run<kHeadsPerChunk>(runner + o, rv);
+          if (flags & kWriteMargins) store_run<kHeadsPerChunk>(margins + o, mv);
+        } else {
+#pragma unroll
+          for (int hh = 0; hh < kHeadsPerChunk; ++hh) {
+            if (hs + hh < H) {
+              winner[o + hh] = wv[hh];
+              if (flags & kWriteRunner) runner[o + hh] = rv[hh];
+              if (flags & kWriteMargins) margins[o + hh] = mv[hh];
+            }
+          }
+        }
+        if (winner_i64 != nullptr) {
+#pragma unroll
+          for (int hh = 0; hh < kHeadsPerChunk; ++hh)
+            if (hs + hh < H) winner_i64[o + hh] = wv[hh];
+        }
+      }
+    }
+  }
+
+  tmem_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+size_t score_tf32_smem_bytes(int kblocks, int stages) {
+  return 1024 + size_t(kblocks) * 2 * kTileT + size_t(stages) * kStageBytesT + sizeof(Barriers);
+}
+
+int score_tf32_stages(int kblocks) {
+  const size_t fixed = score_tf32_smem_bytes(kblocks, 0);
+  if (fixed >= kSmemLimit) return 0;
+  const int stages = static_cast<int>(std::min<size_t>(kMaxStages, (kSmemLimit - fixed) / kStageBytesT));
+  return stages >= kMinStages ? stages : 0;
+}
+
+template <int K>
+int launch_score_tf32(const float *zb, const float *zs, int64_t rows, int D, const float *wb, const float *wsm,
+                      const float *bias, int H, int64_t *w64, uint8_t *win, uint8_t *run, float *m,
+                      cudaStream_t stream) {
+  const int kblocks = static_cast<int>(ceil_div(D, kBKt));
+  const int stages = score_tf32_stages(kblocks);
+  TB_REQUIRE(stages > 0, TROPNN_B200_ERR_INVALID, "trop_score_tf32: code_dim=%d does not fit shared memory", D);
+  CUtensorMap map_zb, map_zs, map_wb, map_ws;
+  TB_CHECK(make_map_f32_k32(&map_zb, zb, D, rows, kBM));
+  TB_CHECK(make_map_f32_k32(&map_zs, zs, D, rows, kBM));
+  TB_CHECK(make_map_f32_k32(&map_wb, wb, D, int64_t(H) * K, kBNt));
+  TB_CHECK(make_map_f32_k32(&map_ws, wsm, D, int64_t(H) * K, kBNt));
+  const int tiles_total = static_cast<int>(ceil_div(int64_t(H) * K, kBNt));
+  const int64_t units = ceil_div(rows, int64_t(kBM)) * tiles_total;
+  int sms = 0;
+  TB_CHECK(sm_count(&sms));
+  const int flags = (run != nullptr ? kWriteRunner : 0) | (m != nullptr ? kWriteMargins : 0);
+  constexpr int kRun = 32 / K;
+  auto al16 = [](const void *p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  const bool vec_stores = (H % kRun == 0) && al16(win) && al16(run) && al16(m);
+  const size_t smem = score_tf32_smem_bytes(kblocks, stages);
+  auto kernel = trop_score_tf32_kernel<K>;
+  TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_score_tf32"));
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(units, sms));
+  kernel<<<grid, kThreads, smem, stream>>>(map_zb, map_zs, map_wb, map_ws, bias, rows, H, kblocks, stages, tiles_total,
+                                           units, flags, vec_stores, w64, win, run, m);
+  return check_launch("trop_score_tf32");
 }
 
 }  // namespace
@@ -484,12 +860,17 @@ bool score_sm100_supported(int64_t D, int64_t K, int pt, int bias_dtype, const v
   const int64_t kblocks = (D + kBK - 1) / kBK;
   auto al16 = [](const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   return (pt == TROPNN_B200_F16 || pt == TROPNN_B200_BF16) && bias_dtype == TROPNN_B200_F32 && cells_ok &&
-         D % 8 == 0 && kblocks <= kMaxKBlocks && score_stages(static_cast<int>(kblocks)) > 0 && al16(z) &&
+         D % 8 == 0 && kblocks <= kMaxKBlocks && score_stages(static_cast<int>(kblocks), false) > 0 && al16(z) &&
          al16(W) && al16(bias);
 }
 
+size_t score_sm100_workspace(int64_t H, int64_t K, int pt) {
+  return (pt == TROPNN_B200_F16 || pt == TROPNN_B200_BF16) ? WorkspaceCarver::align(size_t(H) * K * 64 * 2) : 0;
+}
+
 int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W, const void *bias, int pt, int64_t H,
-                          int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, cudaStream_t stream) {
+                          int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, void *ws, size_t ws_bytes,
+                          cudaStream_t stream) {
   TB_REQUIRE(score_sm100_supported(D, K, pt, TROPNN_B200_F32, z, W, bias), TROPNN_B200_ERR_INVALID,
              "trop_score_sm100: unsupported shape or alignment code_dim=%lld cells=%lld dtype=%s", (long long)D,
              (long long)K, dtype_name(pt));
@@ -500,8 +881,54 @@ int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W
              "trop_score_sm100: %lld rows x %lld score columns exceed the 32-bit tile coordinates",
              (long long)items, (long long)(H * K));
   const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
-  if (pt == TROPNN_B200_F16) return dispatch_cells<__half>(Ki, z, items, Di, W, bias, Hi, w64, win, run, m, stream);
-  return dispatch_cells<__nv_bfloat16>(Ki, z, items, Di, W, bias, Hi, w64, win, run, m, stream);
+  // With room for bias_ext the bias enters the MMA; without, the epilogue adds it.
+  void *bias_ext = (ws != nullptr && ws_bytes >= score_sm100_workspace(H, K, pt)) ? ws : nullptr;
+  if (pt == TROPNN_B200_F16)
+    return dispatch_cells<__half>(Ki, z, items, Di, W, bias, Hi, w64, win, run, m, bias_ext, stream);
+  return dispatch_cells<__nv_bfloat16>(Ki, z, items, Di, W, bias, Hi, w64, win, run, m, bias_ext, stream);
+}
+
+
+int tf32_split_impl(const float *x, int64_t count, float *big, float *small, cudaStream_t stream);
+
+bool score_tf32_supported(int64_t D, int64_t K, int pt, int bias_dtype, const void *z, const void *W,
+                          const void *bias) {
+  const bool cells_ok = K == 2 || K == 4 || K == 8 || K == 16 || K == 32;
+  auto al16 = [](const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  return pt == TROPNN_B200_F32 && bias_dtype == TROPNN_B200_F32 && cells_ok && D % 4 == 0 && D >= 4 &&
+         D <= kMaxKBlocksT * kBKt && score_tf32_stages(static_cast<int>(ceil_div(D, kBKt))) > 0 && al16(z) && al16(W) &&
+         al16(bias);
+}
+
+size_t score_tf32_workspace(int64_t items, int64_t D, int64_t H, int64_t K) {
+  return 2 * WorkspaceCarver::align(size_t(items) * D * sizeof(float)) +
+         2 * WorkspaceCarver::align(size_t(H) * K * D * sizeof(float));
+}
+
+int trop_score_tf32_impl(const float *z, int64_t items, int64_t D, const float *W, const float *bias, int64_t H,
+                         int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, void *ws, size_t ws_bytes,
+                         cudaStream_t stream) {
+  TB_REQUIRE(score_tf32_supported(D, K, TROPNN_B200_F32, TROPNN_B200_F32, z, W, bias), TROPNN_B200_ERR_INVALID,
+             "trop_score_tf32: unsupported shape or alignment code_dim=%lld cells=%lld", (long long)D, (long long)K);
+  if (items == 0) return TROPNN_B200_OK;
+  TB_REQUIRE(items <= (int64_t(1) << 31) - 1024 && H * K <= (int64_t(1) << 31) - 1024, TROPNN_B200_ERR_INVALID,
+             "trop_score_tf32: sizes exceed the 32-bit tile coordinates");
+  WorkspaceCarver c(ws, ws_bytes);
+  float *zb = c.take<float>(size_t(items) * D), *zs = c.take<float>(size_t(items) * D);
+  float *wb = c.take<float>(size_t(H) * K * D), *wsm = c.take<float>(size_t(H) * K * D);
+  TB_REQUIRE(zb && zs && wb && wsm, TROPNN_B200_ERR_WORKSPACE,
+             "trop_score_tf32: workspace of %zu bytes is smaller than the %zu bytes required", ws_bytes,
+             score_tf32_workspace(items, D, H, K));
+  TB_CHECK(tf32_split_impl(z, items * D, zb, zs, stream));
+  TB_CHECK(tf32_split_impl(W, H * K * D, wb, wsm, stream));
+  const int Di = static_cast<int>(D), Hi = static_cast<int>(H);
+  switch (K) {
+    case 2: return launch_score_tf32<2>(zb, zs, items, Di, wb, wsm, bias, Hi, w64, win, run, m, stream);
+    case 4: return launch_score_tf32<4>(zb, zs, items, Di, wb, wsm, bias, Hi, w64, win, run, m, stream);
+    case 8: return launch_score_tf32<8>(zb, zs, items, Di, wb, wsm, bias, Hi, w64, win, run, m, stream);
+    case 16: return launch_score_tf32<16>(zb, zs, items, Di, wb, wsm, bias, Hi, w64, win, run, m, stream);
+    default: return launch_score_tf32<32>(zb, zs, items, Di, wb, wsm, bias, Hi, w64, win, run, m, stream);
+  }
 }
 
 int read_score_error(int *value) {

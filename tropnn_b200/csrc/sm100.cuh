@@ -74,6 +74,31 @@ __device__ inline bool mbar_wait(uint64_t *bar, uint32_t parity, int *abort, int
   }
 }
 
+// Bounded wait as mbar_wait, polling with the mbarrier suspend-time hint `hint_ns`: the thread
+// sleeps between polls until the phase completes (or the hint expires), so that whole warps
+// can wait without taking issue slots from the TMA and MMA threads.
+__device__ inline bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, int *abort, int *error_word, uint32_t hint_ns) {
+  const uint64_t start = global_ns();
+  volatile int *ab = abort;
+  for (;;) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    if (ok) return true;
+    if (*ab) return false;
+    if (global_ns() - start > kWaitLimitNs) {
+      *ab = 1;
+      atomicExch(error_word, 1);
+      return false;
+    }
+  }
+}
+
 // Drain-only wait used on exit paths: bounded, raises nothing.
 __device__ inline void mbar_drain(uint64_t *bar, uint32_t parity) {
   const uint64_t start = global_ns();

@@ -26,8 +26,16 @@ int segment_rowsum_impl(const float *values, int64_t rows, int64_t width, int64_
 bool score_sm100_supported(int64_t D, int64_t K, int pt, int bias_dtype, const void *z, const void *W,
                            const void *bias);
 int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W, const void *bias, int pt, int64_t H,
-                          int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, cudaStream_t stream);
+                          int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, void *ws, size_t ws_bytes,
+                          cudaStream_t stream);
+size_t score_sm100_workspace(int64_t H, int64_t K, int pt);
 int read_score_error(int *value);
+bool score_tf32_supported(int64_t D, int64_t K, int pt, int bias_dtype, const void *z, const void *W,
+                          const void *bias);
+size_t score_tf32_workspace(int64_t items, int64_t D, int64_t H, int64_t K);
+int trop_score_tf32_impl(const float *z, int64_t items, int64_t D, const float *W, const float *bias, int64_t H,
+                         int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, void *ws, size_t ws_bytes,
+                         cudaStream_t stream);
 bool hidden_sm100_supported(int64_t items, int64_t D, int64_t H, int64_t K, int pt, int zt, int it, const void *latent,
                             const void *code_t, const void *hidden);
 int trop_hidden_sm100_impl(const void *latent, int zt, int64_t items, int64_t D, const void *code_t, int pt,
@@ -456,8 +464,23 @@ int check_latent_dtype(int zt, int pt, const char *what) {
   return TROPNN_B200_OK;
 }
 
+// The route's f32 tensor-core path (3xTF32) applies to f32 latent, parameters and bias with u8
+// routes and the tile shapes of trop_score_tf32; it needs a workspace for the split operands.
+bool route_tf32_applies(int zt, int pt, int bt, int it, int64_t D, int64_t H, int64_t K, const void *z, const void *W,
+                        const void *b) {
+  return zt == TROPNN_B200_F32 && it == TROPNN_B200_U8 && H * K >= 32 && score_tf32_supported(D, K, pt, bt, z, W, b);
+}
+
+size_t trop_route_workspace(int64_t items, int64_t D, int64_t H, int64_t K, int zt, int pt) {
+  if (items < 0 || D < 1 || H < 1 || K < 1) return 0;
+  if (zt == TROPNN_B200_F32 && pt == TROPNN_B200_F32) return score_tf32_workspace(items, D, H, K);
+  if (zt == pt) return score_sm100_workspace(H, K, pt);  // the half-precision path's bias operand
+  return 0;
+}
+
 int trop_route_impl(const void *z, int zt, int64_t items, int64_t D, const void *W, const void *b, int bt, int pt,
-                    int64_t H, int64_t K, int64_t *w64, void *win, void *run, int it, float *m, cudaStream_t stream) {
+                    int64_t H, int64_t K, int64_t *w64, void *win, void *run, int it, float *m, void *ws,
+                    size_t ws_bytes, cudaStream_t stream) {
   TB_CHECK(validate_trop(items, D, H, K));
   TB_REQUIRE(is_float_dtype(pt), TROPNN_B200_ERR_DTYPE, "trop_route: param dtype %s unsupported", dtype_name(pt));
   TB_CHECK(check_index_dtype(K, it));
@@ -471,7 +494,13 @@ int trop_route_impl(const void *z, int zt, int64_t items, int64_t D, const void 
   const bool zp = zt != TROPNN_B200_F32;
   if (zp && it == TROPNN_B200_U8 && items >= 128 && H * K >= 128 && score_sm100_supported(D, K, pt, bt, z, W, b))
     return trop_score_sm100_impl(z, items, D, W, b, pt, H, K, w64, static_cast<uint8_t *>(win),
-                                 static_cast<uint8_t *>(run), m, stream);
+                                 static_cast<uint8_t *>(run), m, ws, ws_bytes, stream);
+  // f32 latent and parameters with room for the split operands: 3xTF32 on the tensor cores.
+  if (ws != nullptr && route_tf32_applies(zt, pt, bt, it, D, H, K, z, W, b) &&
+      ws_bytes >= score_tf32_workspace(items, D, H, K))
+    return trop_score_tf32_impl(static_cast<const float *>(z), items, D, static_cast<const float *>(W),
+                                static_cast<const float *>(b), H, K, w64, static_cast<uint8_t *>(win),
+                                static_cast<uint8_t *>(run), m, ws, ws_bytes, stream);
   int status = TROPNN_B200_OK;
   const bool bias_f32 = bt == TROPNN_B200_F32;
   TB_DISPATCH_PT(pt, TB_DISPATCH_IT(it, status = route_by_rows<PT, IT>(z, zp, items, static_cast<int>(D), W, b,
@@ -644,15 +673,19 @@ int trop_backward_impl(const float *g, const float *z, int64_t items, int64_t D,
 
 extern "C" {
 
+size_t tropnn_b200_trop_route_workspace_size(int64_t items, int64_t code_dim, int64_t heads, int64_t cells,
+                                             int latent_dtype, int param_dtype) {
+  return tropnn_b200::trop_route_workspace(items, code_dim, heads, cells, latent_dtype, param_dtype);
+}
+
 int tropnn_b200_trop_route(const void *latent, int latent_dtype, int64_t items, int64_t code_dim,
                            const void *router_weight, const void *router_bias, int bias_dtype, int param_dtype,
                            int64_t heads, int64_t cells, int64_t *winner_i64, void *winner, void *runner,
-                           int index_dtype, float *margins, void *stream) {
+                           int index_dtype, float *margins, void *workspace, size_t workspace_bytes, void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
   TB_CHECK(tropnn_b200::trop_route_impl(latent, latent_dtype, items, code_dim, router_weight, router_bias, bias_dtype,
-                                        param_dtype,
-                                        heads, cells, winner_i64, winner, runner, index_dtype, margins,
-                                        tropnn_b200::as_stream(stream)));
+                                        param_dtype, heads, cells, winner_i64, winner, runner, index_dtype, margins,
+                                        workspace, workspace_bytes, tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 

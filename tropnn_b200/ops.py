@@ -543,6 +543,9 @@ class _TropRouteB200Function(torch.autograd.Function):
         zcode = nat.float_code(z.dtype)
         # The tensor-core route reads the bias in f32 (exact upcast of the parameter).
         bias_in = bias if bias.dtype == torch.float32 else bias.float()
+        # f32 latent and parameters: room for the split operands of the 3xTF32 tensor-core route.
+        route_ws_bytes = int(lib.tropnn_b200_trop_route_workspace_size(items, code_dim, heads, cells, zcode, pdt))
+        route_ws = torch.empty(route_ws_bytes, device=dev, dtype=torch.uint8) if route_ws_bytes else None
         _launch(
             "trop_route",
             lib.tropnn_b200_trop_route,
@@ -561,6 +564,8 @@ class _TropRouteB200Function(torch.autograd.Function):
             nat.ptr(runner),
             icode,
             margins.data_ptr() if margins.numel() else None,
+            nat.ptr(route_ws),
+            route_ws_bytes,
             stream,
         )
         # Half-precision codes: the selected-code sum runs as a one-hot tensor-core GEMM
@@ -886,7 +891,7 @@ def trop_exact_eval_b200(
         stream = nat.stream_handle(dev)
         _launch("trop_route", lib.tropnn_b200_trop_route, xs.data_ptr(), nat.F32, items, in_features, w.data_ptr(),
                 b.data_ptr(), nat.F32, nat.F32, heads, cells, None, winner.data_ptr(), None, icode,
-                margins.data_ptr() if margins.numel() else None, stream)
+                margins.data_ptr() if margins.numel() else None, None, 0, stream)
         _launch("trop_hidden", lib.tropnn_b200_trop_hidden, base.data_ptr(), nat.F32, items, out_features, v.data_ptr(),
                 None, nat.F32, heads, cells, winner.data_ptr(), None, icode, None, float(code_scale), 0, y.data_ptr(),
                 None, 0, stream)
