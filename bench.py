@@ -217,26 +217,43 @@ WORKLOADS = {
 }
 
 
+# A table at most this large stays in the 126 MB L2 across a launch: its gathered rows are L2
+# hits, and only its first read reaches HBM.
+L2_RESIDENT_BYTES = 64 << 20
+
+
+def lut_l2_resident(w: Workload) -> bool:
+    """Whether a Pairwise workload's LUT fits the L2 share that keeps its gathers off HBM."""
+    kw = w.layer_kwargs
+    elt = 2 if w.dtype == "float16" else 4
+    return w.kind == "pairwise" and kw["tables"] * (1 << kw["comparisons"]) * w.out_features * elt <= L2_RESIDENT_BYTES
+
+
 def algorithmic_bytes(w: Workload, kernel: str, rows: int) -> float | None:
     """Algorithmic bytes one launch of ``kernel`` moves for ``rows`` rows (per-row formulas of
-    the hot-path measurement plan; parameter bytes counted once per gathered row)."""
+    the hot-path measurement plan; parameter bytes counted once per gathered row). An
+    L2-resident Pairwise LUT (config 2) is counted once per launch instead: its per-row gathers
+    never reach HBM, so counting them would put the HBM fraction above 1."""
     if w.classifier:
         return None  # two layers of different shapes share the kernel names
     kw = w.layer_kwargs
     elt = 2 if w.dtype == "float16" else 4
     if w.kind == "pairwise":
         T, C, out, inn = kw["tables"], kw["comparisons"], w.out_features, w.in_features
+        lut_bytes = T * (1 << C) * out * elt
+        resident = lut_l2_resident(w)
+        gathered = 0 if resident else 1
         per_row = {
-            "pairwise_forward": T * out * elt + inn * 4 + out * 4 + T * 8 + T * C * 4,
-            "pairwise_ste_backward": out * 4 + 2 * T * out * elt + inn * 4 + T * 8 + T * C * 4 + T * 4 + T,
+            "pairwise_forward": gathered * T * out * elt + inn * 4 + out * 4 + T * 8 + T * C * 4,
+            "pairwise_ste_backward": out * 4 + gathered * 2 * T * out * elt + inn * 4 + T * 8 + T * C * 4 + T * 4 + T,
             "pairwise_lut_grad": T * out * 4 + T * 4,
             "bucket_sort": T * 8 + T * 4,
             "pairwise_threshold_grad": T * 4 + T,
         }.get(kernel)
         if per_row is None:
             return None
-        fixed = T * (1 << C) * out * elt if kernel == "pairwise_lut_grad" else 0
-        return float(per_row * rows + fixed)
+        once = kernel == "pairwise_lut_grad" or (resident and kernel in ("pairwise_forward", "pairwise_ste_backward"))
+        return float(per_row * rows + (lut_bytes if once else 0))
     H, K, D = kw["heads"], kw["cells"], kw["code_dim"]
     per_row = {
         "trop_route": D * 4 + H * (8 + 1 + 1 + 4),
@@ -253,11 +270,14 @@ def algorithmic_bytes(w: Workload, kernel: str, rows: int) -> float | None:
 
 
 def tensor_core_route(w: Workload, rows: int) -> bool:
-    """Whether trop_route runs on the tcgen05 tensor cores for this workload (the C ABI's rule)."""
-    if w.kind != "trop" or w.dtype == "float32":
+    """Whether trop_route runs on the tcgen05 tensor cores for this workload (the C ABI's rule:
+    kind::f16 for half parameters, 3xTF32 for f32 parameters with code_dim <= 128)."""
+    if w.kind != "trop":
         return False
     kw = w.layer_kwargs
     H, K, D = kw["heads"], kw["cells"], kw["code_dim"]
+    if w.dtype == "float32":
+        return K in (2, 4, 8, 16, 32) and D % 4 == 0 and D <= 128 and H * K >= 32
     return K in (2, 4, 8, 16, 32) and D % 8 == 0 and (D + 63) // 64 <= 8 and rows >= 128 and H * K >= 128
 
 
@@ -283,7 +303,19 @@ def kernel_roofline(w: Workload, kernel: str, rows: int, peaks: dict) -> tuple[s
         H, K, D, out = kw["heads"], kw["cells"], kw["code_dim"], w.out_features
         hk = H * K
         if kernel == "trop_route" and tensor_core_route(w, rows):
+            # f32 parameters run kind::tf32 (half the f16 rate) with three products per step.
+            if w.dtype == "float32":
+                return "tensor", 3 * 2.0 * hk * D * rows, "TFLOP/s", *tf32
             return "tensor", 2.0 * hk * D * rows, "TFLOP/s", *tc
+        if kernel == "trop_proj":
+            # z = half(x) P^T: 2 in D FLOP a row; x read once in f32 (in * 4 bytes a row): the
+            # slower of the two bounds.
+            inn = w.in_features
+            flops = 2.0 * rows * inn * D
+            nbytes = float(rows * inn * 4 + rows * D * 2 + D * inn * 2)
+            if flops / (tc_peak * 1e12) >= nbytes / (hbm_peak * 1e9):
+                return "tensor", flops, "TFLOP/s", *tc
+            return "hbm", nbytes, "GB/s", *hbm
         if kernel == "trop_hidden" and tensor_core_hidden(w, rows):
             return "tensor", 2.0 * hk * D * rows, "TFLOP/s", *tc
         if kernel == "linear_f32out":
@@ -454,6 +486,7 @@ def _step(layer, x: torch.Tensor, g: torch.Tensor | None, w: Workload) -> torch.
     if w.train:
         for p in layer.parameters():
             p.grad = None
+        x.grad = None  # the input's gradient is the step's output, not an accumulator
         y = layer(x)
         y.backward(g)
         return y
@@ -768,6 +801,10 @@ def _run_b200_body(
             ("algorithmic_flops_per_launch" if bound == "tensor" else "algorithmic_bytes_per_launch"): work,
             "mean_launch_us": round(mean_s * 1e6, 2),
         }
+        if w.kind == "pairwise" and name in ("pairwise_forward", "pairwise_ste_backward"):
+            per_kernel_roofline[name]["lut"] = (
+                "L2-resident: counted once per launch" if lut_l2_resident(w) else "gathered rows counted per row (logical)"
+            )
         if isinstance(traffic, dict):
             # ncu figures of one capture of the same kernel (profiles/): L2 throughput and the
             # DRAM bytes behind a logical-bytes fraction above 1 (L2-resident tables).
