@@ -271,13 +271,13 @@ def algorithmic_bytes(w: Workload, kernel: str, rows: int) -> float | None:
 
 def tensor_core_route(w: Workload, rows: int) -> bool:
     """Whether trop_route runs on the tcgen05 tensor cores for this workload (the C ABI's rule:
-    kind::f16 for half parameters, 3xTF32 for f32 parameters with code_dim <= 128)."""
+    kind::f16 for half parameters, 3xTF32 for f32 parameters with code_dim <= 128 from 64 rows on)."""
     if w.kind != "trop":
         return False
     kw = w.layer_kwargs
     H, K, D = kw["heads"], kw["cells"], kw["code_dim"]
     if w.dtype == "float32":
-        return K in (2, 4, 8, 16, 32) and D % 4 == 0 and D <= 128 and H * K >= 32
+        return K in (2, 4, 8, 16, 32) and D % 4 == 0 and D <= 128 and H * K >= 32 and rows >= 64
     return K in (2, 4, 8, 16, 32) and D % 8 == 0 and (D + 63) // 64 <= 8 and rows >= 128 and H * K >= 128
 
 

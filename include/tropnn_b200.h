@@ -269,7 +269,8 @@ TROPNN_B200_API int tropnn_b200_pairwise_backward_noalloc(const float *grad_out,
  * multiple of 4 up to 128 and a `workspace` of tropnn_b200_trop_route_workspace_size() bytes:
  * the scores run on the tensor cores as well, in kind::tf32 with every operand split into two
  * tf32 parts (3xTF32, ~2^-22 relative per product; the split operands go to the workspace).
- * With a NULL or smaller workspace those shapes take the fp32 FMA path.
+ * With a NULL or smaller workspace, or fewer than 64 items, those shapes take the fp32 FMA
+ * path.
  */
 TROPNN_B200_API size_t tropnn_b200_trop_route_workspace_size(int64_t items, int64_t code_dim, int64_t heads,
                                                              int64_t cells, int latent_dtype, int param_dtype);
@@ -305,6 +306,8 @@ TROPNN_B200_API int tropnn_b200_trop_proj(const float *x, int64_t items, int64_t
  * summed (3xTF32: f32 range, ~2^-22 relative per product). With few 128 x 128 output tiles the
  * contraction is split across SMs; the slices' f32 partials go to `workspace`
  * (tropnn_b200_gemm_tf32x3_workspace_size bytes; 0 when unsplit) and are summed in slice order.
+ * Products of at most 32 rows (m <= 32) run as f32 FMA instead (one warp per column of c, no
+ * workspace): below one 128-row MMA tile the tensor-core pipeline costs more than the math.
  */
 TROPNN_B200_API size_t tropnn_b200_gemm_tf32x3_workspace_size(int64_t m, int64_t n, int64_t k);
 TROPNN_B200_API int tropnn_b200_gemm_tf32x3(const float *a, int64_t lda, const float *b, int64_t ldb, int64_t m,

@@ -24,7 +24,10 @@ FP32_TOL = 1e-5
         (512, 64, 784, False),  # config 3 layer 1 projection
         (512, 128, 64, True),  # config 3 layer 1 output map
         (512, 10, 64, True),  # config 3 layer 2 output map (n % 4 != 0: plain stores)
-        (8, 512, 32, True),  # config 1 output map
+        (8, 512, 32, True),  # config 1 output map (at most 32 rows: the f32 FMA kernel)
+        (32, 300, 1000, False),  # the largest row count of the f32 FMA kernel, long contraction
+        (1, 7, 8, True),  # one row
+        (33, 64, 256, True),  # the fewest rows of the tensor-core kernel
         (300, 200, 100, True),  # ragged everywhere
         (4096, 4096, 256, False),  # many tiles
     ],

@@ -118,7 +118,8 @@ def test_no_device_error_after_tensor_core_runs() -> None:
     ("items", "heads", "cells", "code_dim"),
     [
         (512, 256, 16, 64),  # config 3's router
-        (8, 32, 4, 32),  # config 1's router
+        (8, 32, 4, 32),  # config 1's router (below 64 rows: the fp32 FMA kernel either way)
+        (64, 32, 4, 32),  # the fewest rows the tf32 path takes
         (300, 12, 16, 64),  # ragged rows, a half-filled score tile
         (1000, 40, 8, 128),  # largest code_dim of the tf32 path (4 k blocks)
         (129, 9, 32, 36),  # code_dim not a multiple of 32 (zero-filled k block)

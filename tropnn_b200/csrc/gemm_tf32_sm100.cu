@@ -374,6 +374,41 @@ __global__ void colsum_f32_kernel(const float *__restrict__ x, int64_t rows, int
   }
 }
 
+// Products with at most kSmallRows rows of C (config 1's 8-row batch): an M=128 MMA tile
+// would be mostly padding and the TMA / TMEM pipeline set-up its whole cost, so they run as
+// f32 FMA: one warp per column of C, lanes over k (coalesced rows of A and B), up to 8 rows
+// of C per pass, partial sums added across the warp by a fixed butterfly (deterministic).
+constexpr int kSmallRows = 32;
+constexpr int kSmallWarps = 8;
+
+__global__ void __launch_bounds__(kSmallWarps * 32) gemm_f32_rows_kernel(
+    const float *__restrict__ a, int64_t lda, const float *__restrict__ b, int64_t ldb, int m, int64_t n, int64_t k,
+    const float *__restrict__ bias, float *__restrict__ c, int64_t ldc) {
+  const int lane = threadIdx.x & 31;
+  const int64_t col = int64_t(blockIdx.x) * kSmallWarps + (threadIdx.x >> 5);
+  if (col >= n) return;
+  const float *brow = b + col * ldb;
+  const float bcol = bias != nullptr ? __ldg(bias + col) : 0.f;
+  for (int r0 = 0; r0 < m; r0 += 8) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int64_t kk = lane; kk < k; kk += 32) {
+      const float bv = __ldg(brow + kk);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (r0 + i < m) acc[i] = fmaf(__ldg(a + int64_t(r0 + i) * lda + kk), bv, acc[i]);
+    }
+    float mine = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float v = warp_sum(acc[i]);
+      if (lane == i) mine = v;
+    }
+    if (lane < 8 && r0 + lane < m) c[int64_t(r0 + lane) * ldc + col] = __fadd_rn(mine, bcol);
+  }
+}
+
 // --------------------------------------------------------------------------- host side
 
 size_t gemm_smem_bytes(int stages) {
@@ -430,7 +465,7 @@ size_t gemm_workspace_bytes(const GemmGeom &g) {
 }  // namespace
 
 size_t gemm_tf32x3_workspace(int64_t m, int64_t n, int64_t k) {
-  if (m < 0 || n < 1 || k < 1) return 0;
+  if (m <= kSmallRows || n < 1 || k < 1) return 0;
   return gemm_workspace_bytes(gemm_geometry(m, n, k));
 }
 
@@ -448,6 +483,13 @@ int gemm_tf32x3_impl(const float *a, int64_t lda, const float *b, int64_t ldb, i
   TB_REQUIRE(a && b && c, TROPNN_B200_ERR_INVALID, "gemm_tf32x3: null pointer");
   auto al16 = [](const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   TB_REQUIRE(al16(a) && al16(b), TROPNN_B200_ERR_INVALID, "gemm_tf32x3: A and B must be 16-byte aligned");
+  if (m <= kSmallRows) {
+    TB_REQUIRE(ceil_div(n, int64_t(kSmallWarps)) < (int64_t(1) << 31), TROPNN_B200_ERR_INVALID,
+               "gemm_tf32x3: n=%lld exceeds the grid", (long long)n);
+    gemm_f32_rows_kernel<<<static_cast<unsigned>(ceil_div(n, int64_t(kSmallWarps))), kSmallWarps * 32, 0, stream>>>(
+        a, lda, b, ldb, static_cast<int>(m), n, k, bias, c, ldc);
+    return check_launch("gemm_tf32x3");
+  }
   GemmGeom g = gemm_geometry(m, n, k);
   g.ldc = ldc;
   g.tma_store = (ldc % 4 == 0 && al16(c)) ? 1 : 0;

@@ -54,10 +54,6 @@ constexpr int kThreads = 32 * (2 + kBuildWarps + kEpiWarps);
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAColBase = 256;      // one-hot ring after the (<= 256-column) accumulator
 constexpr size_t kSmemLimit = 227 * 1024;
-// Each builder thread's one-hot row for one k item: 64 16-bit weights (the item's 32 TMEM
-// columns) + 16 bytes of padding, so the row-per-lane 16-byte accesses spread over the banks.
-constexpr int kRowBufHalves = kBK + 8;
-constexpr size_t kRowBufBytes = size_t(kBuildWarps) * 32 * kRowBufHalves * 2;
 constexpr uint32_t kSleepHintNs = 1000000u;
 
 // Library-wide device error word of this kernel: nonzero after a bounded wait gave up.
@@ -202,8 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *b_smem = smem;  // bstages x [D rows x 128 B], K-major, 128-byte swizzle
-  uint16_t *row_bufs = reinterpret_cast<uint16_t *>(b_smem + bstages * b_stage_bytes);  // builders' rows
-  Barriers *bs = reinterpret_cast<Barriers *>(reinterpret_cast<uint8_t *>(row_bufs) + kRowBufBytes);
+  Barriers *bs = reinterpret_cast<Barriers *>(b_smem + bstages * b_stage_bytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -311,7 +306,6 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
     const int quarter = warp & 3;
     const int parity = (warp - 2) >> 2;
     const uint32_t lane_base = tmem_base + (uint32_t(quarter * 32) << 16) + kAColBase;
-    uint16_t *my_buf = row_bufs + ((warp - 2) * 32 + lane) * kRowBufHalves;
     bool ok = true;
     // The route bytes (and margins) of the thread's row for one k item: the next item's are
     // fetched while this one is built, with vector loads of the item's consecutive heads.
@@ -390,24 +384,24 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
         }
         tmem_fence_after();
         // Column j of the k block holds entries 2j (low half) and 2j+1 (high half), entry
-        // hh * K + k being head hh's cell k: the routed cells' weights go into this thread's
-        // cleared row buffer, which is then read back as the 32 column words.
-        uint4 *row4 = reinterpret_cast<uint4 *>(my_buf);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) row4[c] = make_uint4(0u, 0u, 0u, 0u);
-        __syncwarp();  // orders the 16-byte clears before the 2-byte weight stores (and back)
-#pragma unroll
-        for (int hh = 0; hh < kHeadsPerBlock; ++hh) {
-          if (wc[hh] < uint32_t(K)) my_buf[hh * K + int(wc[hh])] = uint16_t(vw[hh]);
-          if constexpr (MODE != kOneHotEval)
-            if (rc[hh] < uint32_t(K) && rc[hh] != wc[hh]) my_buf[hh * K + int(rc[hh])] = uint16_t(vr[hh]);
-        }
-        __syncwarp();
+        // hh * K + k being head hh's cell k. Head hh's routed cells land in words
+        // hh * K/2 + (cell >> 1), in the half given by cell & 1: each word is a compare and a
+        // select against the (at most two) routed word indices, all in registers.
         uint32_t reg[32];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 q = row4[c];
-          reg[4 * c] = q.x, reg[4 * c + 1] = q.y, reg[4 * c + 2] = q.z, reg[4 * c + 3] = q.w;
+        for (int hh = 0; hh < kHeadsPerBlock; ++hh) {
+          const uint32_t qa = wc[hh] >> 1;
+          const uint32_t a = vw[hh] << ((wc[hh] & 1u) << 4);
+#pragma unroll
+          for (int p = 0; p < K / 2; ++p) {
+            uint32_t v = qa == uint32_t(p) ? a : 0u;
+            if constexpr (MODE != kOneHotEval) {
+              const uint32_t qb = rc[hh] != wc[hh] ? rc[hh] >> 1 : 0xFFu;
+              const uint32_t b = vr[hh] << ((rc[hh] & 1u) << 4);
+              v |= qb == uint32_t(p) ? b : 0u;
+            }
+            reg[hh * (K / 2) + p] = v;
+          }
         }
         tmem_st32(lane_base + uint32_t(sa * 32), reg);
         tmem_wait_st();
@@ -487,7 +481,7 @@ __global__ void __launch_bounds__(256) transpose_kernel(const PT *__restrict__ i
 
 int b_stages(int D) {
   const size_t stage = size_t(D) * 128;
-  const size_t room = kSmemLimit - 1024 - kRowBufBytes - sizeof(Barriers);
+  const size_t room = kSmemLimit - 1024 - sizeof(Barriers);
   const int s = static_cast<int>(std::min<size_t>(kMaxBStages, room / stage));
   return s >= kMinBStages ? s : 0;
 }
@@ -528,7 +522,7 @@ int launch_onehot(const void *latent, int64_t rows, int D, const void *code_t, i
   const int bst = b_stages(D);
   // At least half of the SM's shared memory, so that no second CTA shares the SM: each
   // CTA allocates all 512 TMEM columns.
-  const size_t smem = std::max<size_t>(1024 + size_t(bst) * D * 128 + kRowBufBytes + sizeof(Barriers), 120 * 1024);
+  const size_t smem = std::max<size_t>(1024 + size_t(bst) * D * 128 + sizeof(Barriers), 120 * 1024);
   const int64_t row_blocks = ceil_div(rows, int64_t(kBM));
   // Few row blocks: split the contraction when the caller gave room for the slice partials.
   int splits = onehot_splits(rows, hk);

@@ -466,9 +466,14 @@ int check_latent_dtype(int zt, int pt, const char *what) {
 
 // The route's f32 tensor-core path (3xTF32) applies to f32 latent, parameters and bias with u8
 // routes and the tile shapes of trop_score_tf32; it needs a workspace for the split operands.
-bool route_tf32_applies(int zt, int pt, int bt, int it, int64_t D, int64_t H, int64_t K, const void *z, const void *W,
-                        const void *b) {
-  return zt == TROPNN_B200_F32 && it == TROPNN_B200_U8 && H * K >= 32 && score_tf32_supported(D, K, pt, bt, z, W, b);
+// f32 scores on the tensor cores (3xTF32) from 64 rows on; fewer rows leave an M=128 MMA tile
+// mostly empty, and the fp32 FMA kernel answers sooner.
+constexpr int64_t kRouteTf32MinItems = 64;
+
+bool route_tf32_applies(int64_t items, int zt, int pt, int bt, int it, int64_t D, int64_t H, int64_t K, const void *z,
+                        const void *W, const void *b) {
+  return items >= kRouteTf32MinItems && zt == TROPNN_B200_F32 && it == TROPNN_B200_U8 && H * K >= 32 &&
+         score_tf32_supported(D, K, pt, bt, z, W, b);
 }
 
 size_t trop_route_workspace(int64_t items, int64_t D, int64_t H, int64_t K, int zt, int pt) {
@@ -496,7 +501,7 @@ int trop_route_impl(const void *z, int zt, int64_t items, int64_t D, const void 
     return trop_score_sm100_impl(z, items, D, W, b, pt, H, K, w64, static_cast<uint8_t *>(win),
                                  static_cast<uint8_t *>(run), m, ws, ws_bytes, stream);
   // f32 latent and parameters with room for the split operands: 3xTF32 on the tensor cores.
-  if (ws != nullptr && route_tf32_applies(zt, pt, bt, it, D, H, K, z, W, b) &&
+  if (ws != nullptr && route_tf32_applies(items, zt, pt, bt, it, D, H, K, z, W, b) &&
       ws_bytes >= score_tf32_workspace(items, D, H, K))
     return trop_score_tf32_impl(static_cast<const float *>(z), items, D, static_cast<const float *>(W),
                                 static_cast<const float *>(b), H, K, w64, static_cast<uint8_t *>(win),
