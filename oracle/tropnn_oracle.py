@@ -27,6 +27,7 @@ import numpy as np
 F32 = np.float32
 
 __all__ = [
+    "fan_generated_values",
     "fast_sigmoid_odd_surrogate",
     "izhikevich_surrogate",
     "minface_mix",
@@ -36,6 +37,8 @@ __all__ = [
     "pairwise_indices",
     "surrogate_gradient",
     "top2_indices",
+    "trop_fan_backward",
+    "trop_fan_forward",
     "trop_linear_backward",
     "trop_linear_exact_eval",
     "trop_linear_forward",
@@ -291,6 +294,107 @@ def trop_linear_backward(
         "output_proj.weight": (gy.T @ fwd["hidden"]).astype(F32),
         "output_proj.bias": gy.sum(axis=0, dtype=F32),
     }
+
+
+# ---------------------------------------------------------------------------
+# TropFanLinear
+# ---------------------------------------------------------------------------
+
+
+def fan_generated_values(params: dict[str, np.ndarray], *, fan_value_mode: str) -> np.ndarray:
+    """TropFanLinear.generated_values (layers/fan.py:159-171) in float32: "site" mode is
+    F.normalize(sites, dim=-1, eps=1e-12) * value_scale[..., None]; "basis" mode is
+    einsum("hkr,rd->hkd", value_coeff, value_basis)."""
+    if fan_value_mode == "site":
+        sites = _f32(params["sites"])
+        norm = np.sqrt(np.square(sites).sum(axis=-1, keepdims=True, dtype=F32)).astype(F32)
+        unit = (sites / np.maximum(norm, F32(1e-12))).astype(F32)
+        return (unit * _f32(params["value_scale"])[..., None]).astype(F32)
+    return np.einsum("hkr,rd->hkd", _f32(params["value_coeff"]), _f32(params["value_basis"]), dtype=F32).astype(F32)
+
+
+def trop_fan_forward(
+    x: np.ndarray,
+    params: dict[str, np.ndarray],
+    *,
+    code_scale: float,
+    training: bool,
+    fan_value_mode: str,
+    param_dtype: str | None = None,
+) -> dict[str, np.ndarray]:
+    """TropFanLinear.forward (layers/fan.py:96-99, :201-222, :276-330 via base.py:64-84): the
+    projection as TropLinear's, scores against the sites with the lifting as bias, the top-2,
+    the (min-face mixed in training) generated values of the routed cells summed onto the
+    latent, and the output map."""
+    pdt = _param_dtype(params, param_dtype)
+    x32 = _round_to(x, pdt)
+    z = _round_to(x32 @ _f32(params["proj.weight"]).T, pdt)
+    values = fan_generated_values(params, fan_value_mode=fan_value_mode)
+    route = trop_route_hidden(z, params["sites"], params["lifting"], values, code_scale=code_scale, training=training)
+    y = (route["hidden"] @ _f32(params["output_proj.weight"]).T + _f32(params["output_proj.bias"])).astype(F32)
+    return {"y": y, "z": z, "values": values, **route}
+
+
+def trop_fan_backward(
+    grad_y: np.ndarray,
+    x: np.ndarray,
+    params: dict[str, np.ndarray],
+    fwd: dict[str, np.ndarray],
+    *,
+    code_scale: float,
+    training: bool,
+    fan_value_mode: str,
+    param_dtype: str | None = None,
+) -> dict[str, np.ndarray | None]:
+    """Autograd of trop_fan_forward: TropLinear's backward with the sites as router weights
+    and the value table as code, then the value gradient carried into the value parameters
+    (site mode: the normalisation's Jacobian (g - u (u.g)) / max(|s|, eps) and value_scale's
+    sum(g . u); basis mode: the two einsum factors)."""
+    gy = _f32(grad_y)
+    w_out = _f32(params["output_proj.weight"])
+    grad_hidden = gy @ w_out
+    route = trop_route_backward(
+        grad_hidden,
+        fwd["z"],
+        params["sites"],
+        fwd["values"],
+        fwd["winner"],
+        fwd["runner"],
+        fwd["margins"],
+        code_scale=code_scale,
+        training=training,
+    )
+    gz = route["grad_latent"]
+    gv = route["grad_code"]
+    x32 = _round_to(x, _param_dtype(params, param_dtype))
+    out: dict[str, np.ndarray | None] = {
+        "x": (gz @ _f32(params["proj.weight"])).astype(F32),
+        "proj.weight": (gz.T @ x32).astype(F32),
+        "lifting": route["grad_router_bias"],
+        "output_proj.weight": (gy.T @ fwd["hidden"]).astype(F32),
+        "output_proj.bias": gy.sum(axis=0, dtype=F32),
+    }
+    grad_sites = route["grad_router_weight"]
+    if fan_value_mode == "site":
+        sites = _f32(params["sites"])
+        norm = np.sqrt(np.square(sites).sum(axis=-1, keepdims=True, dtype=F32)).astype(F32)
+        denom = np.maximum(norm, F32(1e-12))
+        unit = (sites / denom).astype(F32)
+        scale = _f32(params["value_scale"])[..., None]
+        out["value_scale"] = (gv * unit).sum(axis=-1, dtype=F32)
+        g_unit = (gv * scale).astype(F32)
+        radial = (g_unit * unit).sum(axis=-1, keepdims=True, dtype=F32)
+        from_values = np.where(norm > F32(1e-12), (g_unit - unit * radial) / denom, g_unit / denom).astype(F32)
+    else:
+        coeff = _f32(params["value_coeff"])
+        basis = _f32(params["value_basis"])
+        out["value_coeff"] = np.einsum("hkd,rd->hkr", gv, basis, dtype=F32).astype(F32)
+        out["value_basis"] = np.einsum("hkr,hkd->rd", coeff, gv, dtype=F32).astype(F32)
+        from_values = None
+    if from_values is not None:
+        grad_sites = from_values if grad_sites is None else (grad_sites + from_values).astype(F32)
+    out["sites"] = grad_sites
+    return out
 
 
 # ---------------------------------------------------------------------------

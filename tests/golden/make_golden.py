@@ -8,7 +8,8 @@ source tree at $TROPNN_REFERENCE, imported as ``tropnn`` through a temporary sym
 (``--only`` rewrites just the named fixtures; every case still draws its inputs, in order,
 from the one seeded generator, so each fixture's inputs do not depend on the selection.)
 
-Each case records, from the reference's torch path on CPU (``backend="torch"``,
+Each case records, from the reference's torch path on CPU (``backend="torch"``; TropLinear,
+TropFanLinear and PairwiseLinear;
 ``exact_fused="off"``, or ``"eval"`` where a case's kwargs ask for the reassociated eval path of
 layers/tropical_exact.py:297-358): the seeded state_dict, the seeded inputs, the forward outputs,
 the route debug cache (``_last_indices`` / ``_last_margins``) and, for training cases,
@@ -107,7 +108,7 @@ def _bias_separate(layer, values: torch.Tensor) -> None:
 
 def main(only: set[str] | None = None) -> None:
     tropnn = _import_reference()
-    TropLinear, PairwiseLinear = tropnn.TropLinear, tropnn.PairwiseLinear
+    TropLinear, PairwiseLinear, TropFanLinear = tropnn.TropLinear, tropnn.PairwiseLinear, tropnn.TropFanLinear
     gen = torch.Generator().manual_seed(1)
     manifest = {}
 
@@ -140,6 +141,25 @@ def main(only: set[str] | None = None) -> None:
         rec = _run_case(layer, x, train=train, grad_out=g)
         meta = dict(kind="pairwise", in_features=in_f, out_features=out_f, tables=tables, comparisons=comparisons,
                     seed=seed, train=train, half=half, output_scale=layer.output_scale, kwargs=kw)
+        if only is None or name in only:
+            _save(name, rec, meta)
+        manifest[name] = meta
+
+    def fan(name, in_f, out_f, *, heads, cells, code_dim, batch, steps=None, train, seed=0, half=False, lifting=None, **kw):
+        layer = TropFanLinear(in_f, out_f, heads=heads, cells=cells, code_dim=code_dim, seed=seed, **kw)
+        if lifting is not None:
+            with torch.no_grad():
+                layer.lifting.copy_(lifting.expand_as(layer.lifting))
+        if half:
+            layer = layer.half()
+        shape = (batch, in_f) if steps is None else (batch, steps, in_f)
+        x = torch.randn(shape, generator=gen)
+        y_shape = (batch, 1 if steps is None else steps, out_f)
+        g = torch.randn(y_shape, generator=gen) if train else None
+        rec = _run_case(layer, x, train=train, grad_out=g)
+        meta = dict(kind="fan", in_features=in_f, out_features=out_f, heads=heads, cells=cells, code_dim=code_dim,
+                    seed=seed, train=train, half=half, code_scale=layer.code_scale, kwargs=kw,
+                    fan_value_mode=layer.fan_value_mode, lifting=None if lifting is None else [float(v) for v in lifting])
         if only is None or name in only:
             _save(name, rec, meta)
         manifest[name] = meta
@@ -179,6 +199,16 @@ def main(only: set[str] | None = None) -> None:
          exact_fused="eval")
     trop("cfg5s_trop_half_exact_eval_b32", 256, 256, heads=64, cells=16, code_dim=64, batch=32, train=False, half=True,
          exact_fused="eval")
+
+    # TropFanLinear (layers/fan.py:21-330): site and basis value modes, train and eval, f32 and f16.
+    fan("small_fan_site_train", 6, 4, heads=3, cells=4, code_dim=5, batch=5, steps=2, train=True, seed=2,
+        lifting=torch.tensor([-3.0, -1.0, 1.0, 3.0]))
+    fan("small_fan_basis_train", 6, 4, heads=3, cells=4, code_dim=5, batch=5, steps=2, train=True, seed=3,
+        lifting=torch.tensor([-3.0, -1.0, 1.0, 3.0]), fan_value_mode="basis", fan_basis_rank=3)
+    fan("cfg1s_fan_site_eval_b8", 256, 512, heads=32, cells=4, code_dim=32, batch=8, train=False)
+    fan("mid_fan_basis_train_b16", 256, 128, heads=64, cells=16, code_dim=64, batch=16, train=True, seed=1,
+        fan_value_mode="basis", fan_basis_rank=16)
+    fan("mid_fan_site_half_train_b32", 256, 256, heads=64, cells=16, code_dim=64, batch=32, train=True, half=True)
 
     # Full-size seeded init of config 5's TropLinear: sha256 of every state_dict tensor.
     big = TropLinear(4096, 4096, heads=1024, cells=16, code_dim=256, seed=0).half()

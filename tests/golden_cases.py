@@ -52,6 +52,19 @@ def build_layer(arrays: dict[str, np.ndarray], meta: dict) -> torch.nn.Module:
         if meta.get("router_bias") is not None:
             with torch.no_grad():
                 layer.router_bias.copy_(torch.tensor(meta["router_bias"]).expand_as(layer.router_bias))
+    elif meta["kind"] == "fan":
+        layer = tropnn_b200.TropFanLinear(
+            meta["in_features"],
+            meta["out_features"],
+            heads=meta["heads"],
+            cells=meta["cells"],
+            code_dim=meta["code_dim"],
+            seed=meta["seed"],
+            **kw,
+        )
+        if meta.get("lifting") is not None:
+            with torch.no_grad():
+                layer.lifting.copy_(torch.tensor(meta["lifting"]).expand_as(layer.lifting))
     else:
         layer = tropnn_b200.PairwiseLinear(
             meta["in_features"],

@@ -33,6 +33,21 @@ def run_oracle(arrays: dict[str, np.ndarray], meta: dict, state: dict[str, np.nd
             for key in ("proj.weight", "router_weight", "router_bias", "code", "output_proj.weight", "output_proj.bias"):
                 out[f"grad.{key}"] = grads[key]
         return out
+    if meta["kind"] == "fan":
+        mode = meta["fan_value_mode"]
+        fwd = oracle.trop_fan_forward(x, state, code_scale=meta["code_scale"], training=train, fan_value_mode=mode)
+        out["y"] = fwd["y"].reshape(b, s, -1)
+        out["last_indices"] = fwd["winner"].reshape(b, s, -1)
+        out["last_margins"] = fwd["margins"].reshape(b, s, -1)
+        out["_scores"] = fwd["scores"]
+        if train:
+            gy = arrays["grad_out"].reshape(b * s, -1).astype(np.float32)
+            grads = oracle.trop_fan_backward(gy, x, state, fwd, code_scale=meta["code_scale"], training=True, fan_value_mode=mode)
+            out["grad.x"] = grads["x"].reshape(arrays["x"].shape)
+            for key in grads:
+                if key != "x":
+                    out[f"grad.{key}"] = grads[key]
+        return out
     kw = meta["kwargs"]
     fwd = oracle.pairwise_forward(x, state["anchors"], state["thresholds"], state["lut"], output_scale=meta["output_scale"])
     out["y"] = fwd["out"].reshape(b, s, -1)

@@ -20,7 +20,7 @@ def test_oracle_matches_reference_golden(name: str) -> None:
     tol = tolerance(meta)
     assert rel_err(got["y"], arrays["y"]) <= tol
     if "last_indices" in arrays:
-        if meta["kind"] == "trop":
+        if meta["kind"] in ("trop", "fan"):
             win, _ = route_gate(got["_scores"])
             ref = arrays["last_indices"].reshape(win.shape)
             assert np.array_equal(got["last_indices"].reshape(win.shape)[win], ref[win])

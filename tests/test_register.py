@@ -1,5 +1,5 @@
 """``tropnn_b200.register`` on the reference package's own classes (host side, no GPU): a
-reference ``TropLinear`` / ``PairwiseLinear`` built with ``backend="b200"`` has the reference's
+reference ``TropLinear`` / ``TropFanLinear`` / ``PairwiseLinear`` built with ``backend="b200"`` has the reference's
 parameters (bit-identical to this package's layers for the same seed), rejects CPU input
 instead of falling back, and every other backend keeps its reference behaviour."""
 
@@ -25,6 +25,19 @@ def test_registered_trop_matches_own_layer() -> None:
     own = tropnn_b200.TropLinear(48, 40, heads=8, cells=4, code_dim=16, seed=3)
     assert isinstance(ref, tropnn.TropLinear) and ref.backend == "b200"
     _same_state(ref, own)
+    with pytest.raises(ValueError, match="CUDA"):
+        ref(torch.randn(2, 48))
+
+
+@pytest.mark.parametrize("mode", ["site", "basis"])
+def test_registered_fan_matches_own_layer(mode: str) -> None:
+    tropnn = import_reference()
+    ref = tropnn.TropFanLinear(48, 40, heads=8, cells=4, code_dim=16, seed=4, backend="b200", fan_value_mode=mode,
+                               fan_basis_rank=5)
+    own = tropnn_b200.TropFanLinear(48, 40, heads=8, cells=4, code_dim=16, seed=4, fan_value_mode=mode, fan_basis_rank=5)
+    assert ref.backend == "b200"
+    _same_state(ref, own)
+    torch.testing.assert_close(ref.generated_values(), own.generated_values(), rtol=0, atol=0)
     with pytest.raises(ValueError, match="CUDA"):
         ref(torch.randn(2, 48))
 

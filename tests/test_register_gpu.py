@@ -1,4 +1,4 @@
-"""The reference package's own TropLinear / PairwiseLinear, switched to backend="b200" by
+"""The reference package's own TropLinear / TropFanLinear / PairwiseLinear, switched to backend="b200" by
 ``tropnn_b200.register``, on the GPU against every golden case the reference recorded: same
 outputs, route debug cache and gradients as the reference's torch path within the parity
 tolerances, and bit-identical to this package's own layers (one code path)."""
@@ -25,6 +25,12 @@ def _reference_layer(tropnn, meta: dict) -> torch.nn.Module:
         if meta.get("router_bias") is not None:
             with torch.no_grad():
                 layer.router_bias.copy_(torch.tensor(meta["router_bias"]).expand_as(layer.router_bias))
+    elif meta["kind"] == "fan":
+        layer = tropnn.TropFanLinear(meta["in_features"], meta["out_features"], heads=meta["heads"], cells=meta["cells"],
+                                     code_dim=meta["code_dim"], seed=meta["seed"], backend="b200", **kw)
+        if meta.get("lifting") is not None:
+            with torch.no_grad():
+                layer.lifting.copy_(torch.tensor(meta["lifting"]).expand_as(layer.lifting))
     else:
         layer = tropnn.PairwiseLinear(meta["in_features"], meta["out_features"], tables=meta["tables"],
                                       comparisons=meta["comparisons"], seed=meta["seed"], backend="b200", **kw)

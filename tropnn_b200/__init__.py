@@ -1,8 +1,9 @@
-"""tropnn_b200: backend="b200" for tropnn's TropLinear and PairwiseLinear on NVIDIA B200.
+"""tropnn_b200: backend="b200" for tropnn's TropLinear, TropFanLinear and PairwiseLinear on
+NVIDIA B200.
 
 Public surface:
-  * ``TropLinear``, ``PairwiseLinear``, ``RoutedLinearBase`` — drop-in layers with the
-    reference's constructor arguments, parameters and ``state_dict``.
+  * ``TropLinear``, ``TropFanLinear``, ``PairwiseLinear``, ``RoutedLinearBase`` — drop-in
+    layers with the reference's constructor arguments, parameters and ``state_dict``.
   * ``trop_route_hidden_b200``, ``pairwise_b200`` — the operator-level entry points
     (mirroring ``trop_route_hidden_tilelang`` / ``pairwise_tilelang``).
   * ``register(tropnn)`` — lets the reference package's own classes accept
@@ -15,7 +16,15 @@ from __future__ import annotations
 
 from typing import Any
 
-from .layers import PairwiseLinear, RoutedLinearBase, TropLinear, pairwise_forward_b200, trop_forward_b200
+from .layers import (
+    PairwiseLinear,
+    RoutedLinearBase,
+    TropFanLinear,
+    TropLinear,
+    fan_forward_b200,
+    pairwise_forward_b200,
+    trop_forward_b200,
+)
 from .ops import (
     packed_route_index_dtype,
     pairwise_anchor_index,
@@ -27,6 +36,7 @@ from .ops import (
 __all__ = [
     "PairwiseLinear",
     "RoutedLinearBase",
+    "TropFanLinear",
     "TropLinear",
     "packed_route_index_dtype",
     "pairwise_anchor_index",
@@ -38,7 +48,8 @@ __all__ = [
 
 
 def register(tropnn: Any) -> None:
-    """Adds backend="b200" to the reference package's TropLinear and PairwiseLinear.
+    """Adds backend="b200" to the reference package's TropLinear, TropFanLinear and
+    PairwiseLinear.
 
     After ``register(tropnn)``, ``tropnn.TropLinear(..., backend="b200")`` builds the
     reference module itself (same init, same parameters; the constructor runs with the
@@ -65,6 +76,17 @@ def register(tropnn: Any) -> None:
 
     _wrap_init(trop_cls)
     _wrap_init(pair_cls)
+    fan_cls = getattr(tropnn, "TropFanLinear", None)
+    if fan_cls is not None:
+        _wrap_init(fan_cls)
+        fan_forward = fan_cls.forward
+
+        def _fan_forward(self: Any, x: Any) -> Any:
+            if self.backend == "b200":
+                return fan_forward_b200(self, x)
+            return fan_forward(self, x)
+
+        fan_cls.forward = _fan_forward
 
     trop_forward = trop_cls.forward
 

@@ -22,6 +22,7 @@ from typing import Literal
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 from torch import Tensor
 
 from .ops import (
@@ -44,7 +45,10 @@ from .ops import (
 __all__ = [
     "PairwiseLinear",
     "RoutedLinearBase",
+    "TropFanLinear",
     "TropLinear",
+    "fan_forward_b200",
+    "fan_generated_values",
     "pairwise_route_output_b200",
     "trop_forward_b200",
 ]
@@ -198,9 +202,18 @@ def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
         # layers/tropical.py:92: the reassociated eval path (wider inputs keep the default
         # path, the same function up to rounding).
         return _trop_exact_eval_b200(layer, x)
+    return _routed_code_forward_b200(layer, x, layer.router_weight, layer.router_bias, layer.code, "TropLinear")
+
+
+def _routed_code_forward_b200(
+    layer: nn.Module, x: Tensor, router_weight: Tensor, router_bias: Tensor, code: Tensor, layer_name: str
+) -> Tensor:
+    """Projection, tropical routing with the selected-code sum, output map: the part TropLinear
+    (layers/tropical.py:89-99, :131-146) and TropFanLinear (layers/fan.py:96-99, :201-222, :276-330)
+    share; TropFanLinear's router is its sites and lifting and its code its generated values."""
     input_dtype = x.dtype
     compute_dtype = _compute_dtype(x)
-    _require_f32_compute(compute_dtype, "TropLinear")
+    _require_f32_compute(compute_dtype, layer_name)
     if proj_eligible(x, layer.proj.weight):
         # Half-precision projection weight: the tensor-core projection kernel rounds x on chip.
         z = trop_project_b200(x, layer.proj.weight)
@@ -212,12 +225,12 @@ def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
     # The reference upcasts z to the compute dtype (tropical.py:99); with half-precision
     # parameters the b200 op takes z in that dtype instead (the upcast is exact and happens
     # in-kernel), which lets the route scores run on the tensor cores.
-    latent = z if z.dtype in (torch.float16, torch.bfloat16) and z.dtype == layer.router_weight.dtype else z.to(compute_dtype)
+    latent = z if z.dtype in (torch.float16, torch.bfloat16) and z.dtype == router_weight.dtype else z.to(compute_dtype)
     hidden, winner, margins = trop_route_hidden_packed(
         latent,
-        layer.router_weight,
-        layer.router_bias,
-        layer.code,
+        router_weight,
+        router_bias,
+        code,
         code_scale=layer.code_scale,
         training=layer.training,
         keep_margins=getattr(layer, "cache_route_debug", True),
@@ -237,6 +250,39 @@ def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
             output = output + bias.to(dtype=compute_dtype)
     _store_debug(layer, winner, margins)
     return output.to(dtype=input_dtype)
+
+
+def fan_generated_values(layer: nn.Module, compute_dtype: torch.dtype) -> Tensor:
+    """TropFanLinear's value table [heads, cells, code_dim] (layers/fan.py:159-171), in the
+    compute dtype from the parameters: "site" mode scales each unit-normalised site by its
+    value_scale, "basis" mode is value_coeff times value_basis. A parameter-sized step
+    (independent of the batch), kept differentiable so that autograd carries the code-sum
+    kernel's value gradient back into sites / value_scale / value_coeff / value_basis."""
+    if layer.fan_value_mode == "site":
+        unit = F.normalize(layer.sites.to(compute_dtype), dim=-1, eps=1e-12)
+        return unit * layer.value_scale.to(compute_dtype).unsqueeze(-1)
+    return torch.einsum("hkr,rd->hkd", layer.value_coeff.to(compute_dtype), layer.value_basis.to(compute_dtype))
+
+
+def fan_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
+    """TropFanLinear forward on sm_100a for any module with the TropFanLinear attributes
+    (layers/fan.py:276-330): the TropLinear path with the sites and lifting as the router and
+    the generated values as the code table (scores, top-2, min-face mix and selected-value sum
+    on the b200 kernels, as are the projection and the output map)."""
+    if x.ndim == 2:
+        x = x.unsqueeze(1)
+    _require_cuda_input(x, "TropFanLinear")
+    if layer.fan_recovery_mode != "untied":
+        raise RuntimeError(
+            "TropFanLinear fan_recovery_mode='tied' is only supported by the scaling benchmark tied recovery wrapper"
+        )
+    compute_dtype = _compute_dtype(x)
+    values = fan_generated_values(layer, compute_dtype)
+    # The route kernels take the code table in the router's dtype: half-precision layers round
+    # the f32 values to it (2^-11 relative for f16, inside the half-precision tolerance).
+    return _routed_code_forward_b200(
+        layer, x, layer.sites, layer.lifting, values.to(layer.sites.dtype), "TropFanLinear"
+    )
 
 
 def _anchor_index(layer: nn.Module, anchors: Tensor) -> tuple[Tensor, Tensor]:
@@ -410,6 +456,99 @@ class TropLinear(RoutedLinearBase):
 
     def forward(self, x: Tensor) -> Tensor:
         return trop_forward_b200(self, x)
+
+
+FAN_VALUE_MODES = ("site", "basis")
+FAN_RECOVERY_MODES = ("untied", "tied")
+
+
+class TropFanLinear(RoutedLinearBase):
+    """Tropical normal-fan layer (layers/fan.py:21-330) on sm_100a: routing sites with a
+    lifting define the tropical polynomial, and the values the winning cells contribute are
+    generated from the sites (``fan_value_mode="site"``: unit site times value_scale) or from
+    a shared rank-``fan_basis_rank`` basis (``"basis"``: value_coeff times value_basis) instead
+    of a free code table."""
+
+    def __init__(
+        self,
+        in_features: int,
+        out_features: int,
+        *,
+        heads: int = 32,
+        cells: int = 4,
+        code_dim: int = 32,
+        backend: Backend = "b200",
+        seed: int = 0,
+        value_init_std: float = 0.02,
+        fan_value_mode: Literal["site", "basis"] = "site",
+        fan_basis_rank: int = 16,
+        fan_recovery_mode: Literal["untied", "tied"] = "untied",
+        use_output_scaling: bool = True,
+        cpu_param_dtype: Literal["f32", "f16"] = "f32",
+    ) -> None:
+        if heads < 1:
+            raise ValueError(f"heads must be >= 1, got {heads}")
+        if cells < 2:
+            raise ValueError(f"cells must be >= 2, got {cells}")
+        if code_dim < 1:
+            raise ValueError(f"code_dim must be >= 1, got {code_dim}")
+        if fan_value_mode not in FAN_VALUE_MODES:
+            raise ValueError(f"fan_value_mode must be one of {FAN_VALUE_MODES}, got {fan_value_mode!r}")
+        if fan_recovery_mode not in FAN_RECOVERY_MODES:
+            raise ValueError(f"fan_recovery_mode must be one of {FAN_RECOVERY_MODES}, got {fan_recovery_mode!r}")
+        if fan_basis_rank < 1:
+            raise ValueError(f"fan_basis_rank must be >= 1, got {fan_basis_rank}")
+        if cpu_param_dtype not in {"f32", "f16"}:
+            raise ValueError(f"cpu_param_dtype must be 'f32' or 'f16', got {cpu_param_dtype!r}")
+        super().__init__(in_features, out_features, backend=backend, output_scale=1.0)
+        self.heads = heads
+        self.cells = cells
+        self.code_dim = code_dim
+        self.code_scale = 1.0 / math.sqrt(heads) if use_output_scaling else 1.0
+        self.fan_value_mode = fan_value_mode
+        self.fan_basis_rank = fan_basis_rank
+        self.fan_recovery_mode = fan_recovery_mode
+        self.cpu_param_dtype = cpu_param_dtype
+
+        # Seeded initialisation in the reference's RNG order (layers/fan.py:87-103).
+        torch.manual_seed(seed)
+        self.proj = nn.Linear(in_features, code_dim, bias=False)
+        nn.init.normal_(self.proj.weight, mean=0.0, std=1.0 / math.sqrt(max(1, in_features)))
+        site_std = 1.0 / math.sqrt(max(1, code_dim))
+        self.sites = nn.Parameter(torch.randn(heads, cells, code_dim) * site_std)
+        self.lifting = nn.Parameter(torch.zeros(heads, cells))
+        if fan_value_mode == "site":
+            self.value_scale = nn.Parameter(torch.randn(heads, cells) * value_init_std)
+            self.value_coeff = None
+            self.value_basis = None
+        else:
+            self.value_scale = None
+            self.value_coeff = nn.Parameter(
+                torch.randn(heads, cells, fan_basis_rank) * value_init_std / math.sqrt(fan_basis_rank)
+            )
+            self.value_basis = nn.Parameter(torch.randn(fan_basis_rank, code_dim) / math.sqrt(max(1, code_dim)))
+        self.output_proj = nn.Linear(code_dim, out_features)
+        nn.init.kaiming_uniform_(self.output_proj.weight, a=math.sqrt(5))
+        if self.output_proj.bias is not None:
+            fan_in = self.output_proj.weight.shape[1]
+            bound = 1 / math.sqrt(fan_in) if fan_in > 0 else 0
+            nn.init.uniform_(self.output_proj.bias, -bound, bound)
+
+    def extra_repr(self) -> str:
+        return (
+            f"in_features={self.in_features}, out_features={self.out_features}, heads={self.heads}, "
+            f"cells={self.cells}, code_dim={self.code_dim}, fan_value_mode={self.fan_value_mode!r}, "
+            f"fan_basis_rank={self.fan_basis_rank}, fan_recovery_mode={self.fan_recovery_mode!r}, backend={self.backend!r}, "
+            f"cpu_param_dtype={self.cpu_param_dtype!r}"
+        )
+
+    def generated_values(self, *, input_device: torch.device | None = None, compute_dtype: torch.dtype | None = None) -> Tensor:
+        """The value table [heads, cells, code_dim] (layers/fan.py:159-171)."""
+        values = fan_generated_values(self, self.sites.dtype if compute_dtype is None else compute_dtype)
+        return values if input_device is None else values.to(input_device)
+
+    def forward(self, x: Tensor) -> Tensor:
+        return fan_forward_b200(self, x)
 
 
 class PairwiseLinear(RoutedLinearBase):
