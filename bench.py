@@ -316,6 +316,10 @@ def kernel_roofline(w: Workload, kernel: str, rows: int, peaks: dict) -> tuple[s
             if flops / (tc_peak * 1e12) >= nbytes / (hbm_peak * 1e9):
                 return "tensor", flops, "TFLOP/s", *tc
             return "hbm", nbytes, "GB/s", *hbm
+        if kernel == "trop_proj_wgrad":
+            # grad_P = g^T half(x): x read once in f32, g^T [D, rows] and grad_P once in half.
+            inn = w.in_features
+            return "hbm", float(rows * inn * 4 + D * rows * 2 + D * inn * 2), "GB/s", *hbm
         if kernel == "trop_hidden" and tensor_core_hidden(w, rows):
             return "tensor", 2.0 * hk * D * rows, "TFLOP/s", *tc
         if kernel == "linear_f32out":

@@ -292,6 +292,22 @@ TROPNN_B200_API int tropnn_b200_trop_route(const void *latent, int latent_dtype,
  * in slice order (deterministic).
  */
 TROPNN_B200_API size_t tropnn_b200_trop_proj_workspace_size(int64_t items, int64_t in_features, int64_t code_dim);
+/*
+ * Weight gradient of that projection (the reference's half-precision F.linear backward):
+ * grad_weight[d, i] = sum_n grad_z[n, d] * half(x[n, i]) for f32 x [items, in_features] and
+ * grad_z_t = grad_z transposed to [code_dim, items] in param_dtype (tropnn_b200_transpose_to_half);
+ * grad_weight [code_dim, in_features] in param_dtype. f32 accumulation on the tensor cores, x
+ * rounded on chip (read once, no cast pass), one rounding of the result; the sample range is cut
+ * into slices whose f32 partials go to `workspace` (tropnn_b200_trop_proj_wgrad_workspace_size
+ * bytes) and are summed in slice order (deterministic). items and in_features multiples of 8,
+ * code_dim in {64, 128, 192, 256}.
+ */
+TROPNN_B200_API size_t tropnn_b200_trop_proj_wgrad_workspace_size(int64_t items, int64_t in_features,
+                                                                  int64_t code_dim);
+TROPNN_B200_API int tropnn_b200_trop_proj_wgrad(const float *x, int64_t items, int64_t in_features,
+                                                const void *grad_z_t, int param_dtype, int64_t code_dim,
+                                                void *grad_weight, void *workspace, size_t workspace_bytes,
+                                                void *stream);
 TROPNN_B200_API int tropnn_b200_trop_proj(const float *x, int64_t items, int64_t in_features,
                                           const void *proj_weight, int param_dtype, int64_t code_dim, void *z,
                                           void *workspace, size_t workspace_bytes, void *stream);

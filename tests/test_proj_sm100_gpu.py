@@ -3,7 +3,8 @@ against an f64 reference of the same rounding steps: at most one unit in the las
 parameter dtype anywhere (the f32 accumulation order differs from the reference's, which can only
 move a sum across a rounding boundary), on the unsplit and the split-contraction paths, ragged
 row and input widths, every supported code_dim, f16 and bf16; split runs are deterministic.
-The projection's backward (grad_x on the tensor-core linear map, grad_P) against f64 products."""
+The projection's backward (grad_x on the tensor-core linear map, grad_P on the tensor-core
+weight-gradient kernel) against f64 products."""
 
 from __future__ import annotations
 
@@ -88,3 +89,47 @@ def test_projection_rejects_unsupported_shapes() -> None:
                                        torch.cuda.current_stream().cuda_stream)
     with pytest.raises(ValueError, match="in_features"):
         nat.check(status, "trop_proj")
+
+
+def _wgrad(x: torch.Tensor, g: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """grad_P = g^T half(x) through the C ABI (g transposed first, as the layer does)."""
+    lib = nat.load()
+    rows, in_f = x.shape
+    dim = g.shape[1]
+    pdt = nat.float_code(dtype)
+    stream = nat.stream_handle(x.device)
+    g_t = torch.empty((dim, rows), device=x.device, dtype=dtype)
+    nat.check(lib.tropnn_b200_transpose_to_half(g.data_ptr(), pdt, rows, dim, pdt, None, g_t.data_ptr(), stream),
+              "transpose_to_half")
+    out = torch.empty((dim, in_f), device=x.device, dtype=dtype)
+    ws_bytes = int(lib.tropnn_b200_trop_proj_wgrad_workspace_size(rows, in_f, dim))
+    ws = torch.empty(max(ws_bytes, 1), device=x.device, dtype=torch.uint8)
+    nat.check(lib.tropnn_b200_trop_proj_wgrad(x.data_ptr(), rows, in_f, g_t.data_ptr(), pdt, dim, out.data_ptr(),
+                                              ws.data_ptr(), ws_bytes, stream), "trop_proj_wgrad")
+    return out
+
+
+@pytest.mark.parametrize(
+    ("rows", "in_f", "dim", "dtype"),
+    [
+        (16384, 4096, 256, torch.float16),  # config 5's train step: 4 sample slices per feature tile
+        (2048, 4096, 256, torch.float16),  # one GPU's shard at 8 GPUs
+        (200, 200, 64, torch.bfloat16),  # ragged samples (zero-filled k block) and features
+        (8, 512, 128, torch.float16),  # one k block: unsplit, direct stores
+        (1000, 784, 192, torch.bfloat16),
+    ],
+)
+def test_projection_weight_gradient(rows: int, in_f: int, dim: int, dtype: torch.dtype) -> None:
+    """grad_P against f64 sums of the rounded operands: one rounding unit plus the f32
+    accumulation error; deterministic."""
+    gen = torch.Generator().manual_seed(rows + dim)
+    x = torch.randn(rows, in_f, generator=gen)
+    g = torch.randn(rows, dim, generator=gen).to(dtype)
+    xd, gd = x.cuda(), g.cuda()
+    got = _wgrad(xd, gd, dtype)
+    torch.cuda.synchronize()
+    ref = g.double().t() @ x.to(dtype).double()
+    err = (got.cpu().double() - ref).abs()
+    bound = _ulp(ref, dtype).double() + 3e-5 * float(ref.abs().max())
+    assert bool((err <= bound).all()), float((err / bound).max())
+    assert torch.equal(got, _wgrad(xd, gd, dtype))

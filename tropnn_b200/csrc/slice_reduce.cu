@@ -9,6 +9,8 @@
 //   kReduceHalf    out[row, col] = half(sum)                 (the projection's z)
 //   kReduceF32     out[row, col] = sum + bias[col]           (the f32 product)
 //   kReduceHidden  out[row, col] = latent[row, col] + scale * sum   (code sum / router term)
+//   kReduceHalfT   out[col, row] = half(sum)                 (the projection's weight gradient,
+//                                                             computed transposed)
 // A block takes 32 rows x one tile's columns: the slices' loads are coalesced over the rows
 // (all of a thread's slices in flight at once), the sums are transposed through shared memory
 // and written coalesced over the columns.
@@ -61,6 +63,14 @@ __global__ void __launch_bounds__(kThreads) slice_reduce_kernel(const float4 *__
   __syncthreads();
   const int64_t row0 = rb * 128 + sub * 32;
   const int64_t col0 = int64_t(nt) * tile_cols;
+  if constexpr (MODE == kReduceHalfT) {
+    // Transposed: a warp writes 32 consecutive rows of one output row (column of the tile).
+    for (int e = threadIdx.x; e < kRows * tile_cols; e += kThreads) {
+      const int cc = e / kRows, rr = e - cc * kRows;
+      const int64_t row = row0 + rr, col = col0 + cc;
+      if (row < rows && col < cols) out[col * ldo + row] = from_f32<OT>(tile[rr][cc]);
+    }
+  } else {
   for (int e = threadIdx.x; e < kRows * tile_cols; e += kThreads) {
     const int rr = e / tile_cols, cc = e - rr * tile_cols;
     const int64_t row = row0 + rr, col = col0 + cc;
@@ -73,6 +83,7 @@ __global__ void __launch_bounds__(kThreads) slice_reduce_kernel(const float4 *__
     } else {
       out[row * ldo + col] = __fadd_rn(to_f32<LT>(latent[row * cols + col]), __fmul_rn(sum, scale));
     }
+  }
   }
 }
 
@@ -104,6 +115,12 @@ int slice_reduce_impl(int mode, const void *partial, int splits, int n_tiles, in
                                                          nullptr, nullptr, 1.f, stream);
       return launch_reduce<kReduceHalf, __nv_bfloat16, float>(partial, splits, n_tiles, tile_cols, rows, cols, out,
                                                               ldo, nullptr, nullptr, 1.f, stream);
+    case kReduceHalfT:
+      if (out_dtype == TROPNN_B200_F16)
+        return launch_reduce<kReduceHalfT, __half, float>(partial, splits, n_tiles, tile_cols, rows, cols, out, ldo,
+                                                          nullptr, nullptr, 1.f, stream);
+      return launch_reduce<kReduceHalfT, __nv_bfloat16, float>(partial, splits, n_tiles, tile_cols, rows, cols, out,
+                                                               ldo, nullptr, nullptr, 1.f, stream);
     case kReduceF32:
       return launch_reduce<kReduceF32, float, float>(partial, splits, n_tiles, tile_cols, rows, cols, out, ldo, bias,
                                                      nullptr, 1.f, stream);

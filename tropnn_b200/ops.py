@@ -1053,7 +1053,8 @@ class _TropProjFunction(torch.autograd.Function):
     the tcgen05 projection kernel (x rounded on chip, f32 accumulation, z rounded to P's dtype).
     Backward of the reference's half-precision F.linear: grad_x = grad_z P on the tcgen05
     linear map (f32 result; the reference rounds it to P's dtype and back, a difference below
-    that dtype's rounding), grad_P = grad_z^T half(x)."""
+    that dtype's rounding), grad_P = grad_z^T half(x) on the tcgen05 weight-gradient kernel
+    (x rounded on chip; cuBLAS only for batches that are not a multiple of 8 rows)."""
 
     @staticmethod
     def forward(ctx: Any, x: Tensor, weight: Tensor) -> Tensor:
@@ -1082,7 +1083,20 @@ class _TropProjFunction(torch.autograd.Function):
             _launch("linear_f32out", lib.tropnn_b200_linear_f32out, g.data_ptr(), rows, 1, w_t.data_ptr(),
                     in_features, code_dim, pdt, None, grad_x.data_ptr(), stream)
         if ctx.needs_input_grad[1]:
-            grad_w = g.t().matmul(x.to(w.dtype))
+            if rows % 8 == 0:
+                # grad_P = g^T half(x) on the tensor cores, x rounded on chip (no cast pass).
+                pdt = nat.float_code(w.dtype)
+                g_t = torch.empty((code_dim, rows), device=dev, dtype=w.dtype)
+                _launch("transpose_to_half", lib.tropnn_b200_transpose_to_half, g.data_ptr(), pdt, rows, code_dim, pdt,
+                        None, g_t.data_ptr(), stream)
+                grad_w = torch.empty_like(w)
+                ws_bytes = int(lib.tropnn_b200_trop_proj_wgrad_workspace_size(rows, in_features, code_dim))
+                ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8) if ws_bytes else None
+                _launch("trop_proj_wgrad", lib.tropnn_b200_trop_proj_wgrad, x.data_ptr(), rows, in_features,
+                        g_t.data_ptr(), pdt, code_dim, grad_w.data_ptr(), nat.ptr(ws), ws_bytes, stream)
+            else:
+                # Batches whose transposed gradient rows are not 16-byte multiples: the library GEMM.
+                grad_w = g.t().matmul(x.to(w.dtype))
         return grad_x, grad_w
 
 
