@@ -145,3 +145,30 @@ def test_no_device_error_after_tensor_core_runs():
     flag = ctypes.c_int(-1)
     nat.check(nat.load().tropnn_b200_device_error(ctypes.byref(flag)), "device_error")
     assert flag.value == 0
+
+
+@pytest.mark.parametrize(("heads", "cells", "dim"), [(1024, 16, 256), (10, 3, 40), (9, 3, 40), (5, 3, 7)])
+def test_code_transpose_exact(heads: int, cells: int, dim: int) -> None:
+    """code [H, K, D] -> code^T [D, H*K], bit for bit (the paired-word kernel for even sizes, the
+    element kernel otherwise)."""
+    lib = nat.load()
+    code = torch.randn(heads, cells, dim, device="cuda").half()
+    out = torch.empty((dim, heads * cells), device="cuda", dtype=torch.float16)
+    nat.check(lib.tropnn_b200_trop_code_transpose(code.data_ptr(), nat.F16, heads, cells, dim, out.data_ptr(),
+                                                  nat.stream_handle(code.device)), "trop_code_transpose")
+    torch.cuda.synchronize()
+    assert torch.equal(out, code.reshape(heads * cells, dim).t())
+
+
+@pytest.mark.parametrize(("rows", "cols", "src"), [(16384, 256, torch.float32), (16384, 256, torch.float16),
+                                                   (301, 64, torch.float32), (2, 5, torch.bfloat16)])
+def test_transpose_to_half_exact(rows: int, cols: int, src: torch.dtype) -> None:
+    """x [rows, cols] -> half(x)^T [cols, rows] (no gradient scale), bit for bit."""
+    lib = nat.load()
+    dst = torch.bfloat16 if src == torch.bfloat16 else torch.float16
+    x = torch.randn(rows, cols, device="cuda").to(src)
+    out = torch.empty((cols, rows), device="cuda", dtype=dst)
+    nat.check(lib.tropnn_b200_transpose_to_half(x.data_ptr(), nat.float_code(src), rows, cols, nat.float_code(dst), None,
+                                                out.data_ptr(), nat.stream_handle(x.device)), "transpose_to_half")
+    torch.cuda.synchronize()
+    assert torch.equal(out, x.to(dst).t())

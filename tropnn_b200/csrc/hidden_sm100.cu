@@ -479,6 +479,39 @@ __global__ void __launch_bounds__(256) transpose_kernel(const PT *__restrict__ i
     if (c0 + j < cols_in && r0 + tx < rows_in) out[int64_t(c0 + j) * rows_in + r0 + tx] = tile[tx][j];
 }
 
+// The same transpose for even sizes, 64 x 64 tiles moved as 32-bit pairs: a thread reads two
+// consecutive input rows' pair (r, c..c+1), (r+1, c..c+1), regroups them into the pairs
+// (c, r..r+1) and (c+1, r..r+1) with byte permutes, and the two 32 x 33-word shared tiles give
+// 128-byte coalesced reads and writes without bank conflicts.
+__global__ void __launch_bounds__(256) transpose_pairs_kernel(const uint32_t *__restrict__ in, uint32_t *__restrict__ out,
+                                                              int64_t rows_in, int cols_in) {
+  __shared__ uint32_t lo_t[32][33], hi_t[32][33];
+  const int64_t r0 = int64_t(blockIdx.x) * 64;  // input rows (output columns)
+  const int c0 = blockIdx.y * 64;              // input columns (output rows)
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t in_words = cols_in / 2, out_words = rows_in / 2;
+  for (int rr = ty; rr < 32; rr += 8) {
+    const int64_t r = r0 + 2 * rr;
+    const int c = c0 + 2 * tx;
+    uint32_t a = 0u, b = 0u;
+    if (c < cols_in) {
+      if (r < rows_in) a = in[r * in_words + c / 2];
+      if (r + 1 < rows_in) b = in[(r + 1) * in_words + c / 2];
+    }
+    lo_t[rr][tx] = __byte_perm(a, b, 0x5410);  // (a.lo, b.lo): column c, rows r, r + 1
+    hi_t[rr][tx] = __byte_perm(a, b, 0x7632);  // (a.hi, b.hi): column c + 1
+  }
+  __syncthreads();
+  for (int cc = ty; cc < 32; cc += 8) {
+    const int c = c0 + 2 * cc;
+    const int64_t r = r0 + 2 * tx;
+    if (r < rows_in) {
+      if (c < cols_in) out[int64_t(c) * out_words + r / 2] = lo_t[tx][cc];
+      if (c + 1 < cols_in) out[int64_t(c + 1) * out_words + r / 2] = hi_t[tx][cc];
+    }
+  }
+}
+
 int b_stages(int D) {
   const size_t stage = size_t(D) * 128;
   const size_t room = kSmemLimit - 1024 - sizeof(Barriers);
@@ -618,6 +651,15 @@ int trop_code_transpose_impl(const void *code, int pt, int64_t H, int64_t K, int
              (long long)D);
   TB_REQUIRE(code && code_t, TROPNN_B200_ERR_INVALID, "trop_code_transpose: null pointer");
   const int64_t rows_in = H * K;
+  const bool pairs = rows_in % 2 == 0 && D % 2 == 0 && reinterpret_cast<uintptr_t>(code) % 4 == 0 &&
+                     reinterpret_cast<uintptr_t>(code_t) % 4 == 0;
+  if (pairs) {
+    const dim3 grid2(static_cast<unsigned>(ceil_div(rows_in, int64_t(64))), static_cast<unsigned>(ceil_div(D, int64_t(64))));
+    TB_REQUIRE(grid2.y < 65536, TROPNN_B200_ERR_INVALID, "trop_code_transpose: code_dim too large");
+    transpose_pairs_kernel<<<grid2, 256, 0, stream>>>(static_cast<const uint32_t *>(code),
+                                                      static_cast<uint32_t *>(code_t), rows_in, static_cast<int>(D));
+    return check_launch("trop_code_transpose");
+  }
   const dim3 grid(static_cast<unsigned>(ceil_div(rows_in, int64_t(32))), static_cast<unsigned>(ceil_div(D, int64_t(32))));
   if (pt == TROPNN_B200_F16)
     transpose_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half *>(code), static_cast<__half *>(code_t),

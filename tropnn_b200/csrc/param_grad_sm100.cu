@@ -504,6 +504,29 @@ __global__ void __launch_bounds__(256) transpose_to_half_kernel(const IT *__rest
     if (c0 + j < cols && r0 + tx < rows_in) out[int64_t(c0 + j) * rows_in + r0 + tx] = from_f32<PT>(tile[tx][j]);
 }
 
+// The same for an even row count: 64 input rows per tile, and each thread writes two
+// consecutive rows of one output row as one 4-byte store (128-byte coalesced warp stores).
+template <typename IT, typename PT>
+__global__ void __launch_bounds__(256) transpose_to_half_pairs_kernel(const IT *__restrict__ in, PT *__restrict__ out,
+                                                                      int64_t rows_in, int cols,
+                                                                      const uint32_t *__restrict__ absmax) {
+  __shared__ float tile[64][33];
+  const float s = grad_scale_of(absmax);
+  const int64_t r0 = int64_t(blockIdx.x) * 64;
+  const int c0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int j = ty; j < 64; j += 8)
+    if (r0 + j < rows_in && c0 + tx < cols) tile[j][tx] = __fmul_rn(to_f32(in[(r0 + j) * cols + c0 + tx]), s);
+  __syncthreads();
+  for (int j = ty; j < 32; j += 8) {
+    const int64_t r = r0 + 2 * tx;
+    if (c0 + j < cols && r < rows_in) {
+      *reinterpret_cast<uint32_t *>(out + int64_t(c0 + j) * rows_in + r) =
+          half_bits<PT>(tile[2 * tx][j]) | (half_bits<PT>(tile[2 * tx + 1][j]) << 16);
+    }
+  }
+}
+
 int b_stages(int D) {
   const size_t stage = size_t(D) * 128;
   const size_t room = kSmemLimit - 1024 - 2 * size_t(kStageBytes) - sizeof(Barriers);
@@ -608,8 +631,29 @@ int transpose_to_half_impl(const void *x, int xt_dtype, int64_t rows, int64_t co
   TB_REQUIRE(rows >= 0 && cols > 0 && cols <= (1 << 20), TROPNN_B200_ERR_INVALID, "transpose_to_half: bad shape");
   if (rows == 0) return TROPNN_B200_OK;
   TB_REQUIRE(x && out, TROPNN_B200_ERR_INVALID, "transpose_to_half: null pointer");
-  const dim3 grid(static_cast<unsigned>(ceil_div(rows, int64_t(32))), static_cast<unsigned>(ceil_div(cols, int64_t(32))));
   const int c = static_cast<int>(cols);
+  if (rows % 2 == 0 && reinterpret_cast<uintptr_t>(out) % 4 == 0) {
+    // 64-row tiles, pairs of output elements per 4-byte store.
+    const dim3 grid2(static_cast<unsigned>(ceil_div(rows, int64_t(64))), static_cast<unsigned>(ceil_div(cols, int64_t(32))));
+    TB_REQUIRE(grid2.y < 65536, TROPNN_B200_ERR_INVALID, "transpose_to_half: too many columns");
+    if (pt == TROPNN_B200_F16) {
+      if (xt_dtype == TROPNN_B200_F32)
+        transpose_to_half_pairs_kernel<float, __half><<<grid2, 256, 0, stream>>>(
+            static_cast<const float *>(x), static_cast<__half *>(out), rows, c, absmax);
+      else
+        transpose_to_half_pairs_kernel<__half, __half><<<grid2, 256, 0, stream>>>(
+            static_cast<const __half *>(x), static_cast<__half *>(out), rows, c, absmax);
+    } else {
+      if (xt_dtype == TROPNN_B200_F32)
+        transpose_to_half_pairs_kernel<float, __nv_bfloat16><<<grid2, 256, 0, stream>>>(
+            static_cast<const float *>(x), static_cast<__nv_bfloat16 *>(out), rows, c, absmax);
+      else
+        transpose_to_half_pairs_kernel<__nv_bfloat16, __nv_bfloat16><<<grid2, 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16 *>(x), static_cast<__nv_bfloat16 *>(out), rows, c, absmax);
+    }
+    return check_launch("transpose_to_half");
+  }
+  const dim3 grid(static_cast<unsigned>(ceil_div(rows, int64_t(32))), static_cast<unsigned>(ceil_div(cols, int64_t(32))));
   if (pt == TROPNN_B200_F16) {
     if (xt_dtype == TROPNN_B200_F32)
       transpose_to_half_kernel<float, __half><<<grid, 256, 0, stream>>>(static_cast<const float *>(x),
