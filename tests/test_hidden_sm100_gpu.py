@@ -31,7 +31,7 @@ def _routes(items: int, heads: int, cells: int, gen: torch.Generator) -> tuple[t
     return winner.to(torch.uint8), runner.to(torch.uint8), margins
 
 
-def _hidden(latent, code, winner, runner, margins, code_scale, training, use_tc):
+def _hidden(latent, code, winner, runner, margins, code_scale, training, use_tc, workspace=True):
     lib = nat.load()
     items, code_dim = latent.shape
     heads, cells, _ = code.shape
@@ -46,7 +46,7 @@ def _hidden(latent, code, winner, runner, margins, code_scale, training, use_tc)
             "trop_code_transpose",
         )
     hidden = torch.empty((items, code_dim), device=latent.device, dtype=torch.float32)
-    ws_bytes = int(lib.tropnn_b200_trop_hidden_workspace_size(items, code_dim, heads, cells)) if use_tc else 0
+    ws_bytes = int(lib.tropnn_b200_trop_hidden_workspace_size(items, code_dim, heads, cells)) if use_tc and workspace else 0
     ws = torch.empty(ws_bytes, device=latent.device, dtype=torch.uint8) if ws_bytes else None
     nat.check(
         lib.tropnn_b200_trop_hidden(
@@ -116,6 +116,27 @@ def test_cells(cells):
 def test_ragged_shapes(items, heads, cells, code_dim):
     _check(items, heads, cells, code_dim, torch.float16, training=False)
     _check(items, heads, cells, code_dim, torch.bfloat16, training=True)
+
+
+@pytest.mark.parametrize("training", [False, True])
+def test_split_contraction_and_no_workspace(training):
+    """5 row blocks of 256 k blocks: the contraction cut into slices summed in slice order by
+    slice_reduce; without a workspace each row block takes one CTA over all its k blocks. Both
+    agree with the gather kernel and with each other up to f32 summation order."""
+    gen = torch.Generator().manual_seed(9)
+    items, heads, cells, code_dim = 640, 1024, 16, 256
+    latent = torch.randn(items, code_dim, generator=gen).half().cuda()
+    code = (torch.randn(heads, cells, code_dim, generator=gen) * 0.5).half().cuda()
+    winner, runner, margins = (t.cuda() for t in _routes(items, heads, cells, gen))
+    scale = heads**-0.5
+    split = _hidden(latent, code, winner, runner, margins, scale, training, use_tc=True)
+    whole = _hidden(latent, code, winner, runner, margins, scale, training, use_tc=True, workspace=False)
+    simt = _hidden(latent, code, winner, runner, margins, scale, training, use_tc=False)
+    tol = TRAIN_TOL[torch.float16] if training else 1e-5
+    assert rel_err(split, simt) <= tol and rel_err(whole, simt) <= tol
+    assert rel_err(split, whole) <= 1e-5
+    again = _hidden(latent, code, winner, runner, margins, scale, training, use_tc=True)
+    assert np.array_equal(split, again)  # deterministic
 
 
 def test_f32_latent():
