@@ -351,6 +351,10 @@ TROPNN_B200_API int tropnn_b200_colsum_f32(const float *x, int64_t rows, int64_t
  * (head, cell) contraction into slices when `workspace` holds
  * tropnn_b200_trop_hidden_workspace_size() bytes (their f32 partials, summed in slice order);
  * with a NULL or smaller workspace it runs unsplit. Same for tropnn_b200_trop_router_term.
+ * hidden_split (may be NULL; F16/BF16 codes, code_dim % 4 == 0, 16-byte aligned): also
+ * written as [items, 2*code_dim] in param_dtype, the [hi | lo] split of each hidden row
+ * (tropnn_b200_split_half with a NULL scale) that tropnn_b200_linear_f32out takes for the
+ * output map; the tensor-core path forms it in the same epilogue as hidden.
  */
 TROPNN_B200_API size_t tropnn_b200_trop_hidden_workspace_size(int64_t items, int64_t code_dim, int64_t heads,
                                                               int64_t cells);
@@ -358,7 +362,8 @@ TROPNN_B200_API int tropnn_b200_trop_hidden(const void *latent, int latent_dtype
                             const void *code, const void *code_t, int param_dtype, int64_t heads, int64_t cells,
                             const void *winner, const void *runner, int index_dtype,
                             const float *margins, float code_scale, int training,
-                            float *hidden, void *workspace, size_t workspace_bytes, void *stream);
+                            float *hidden, void *hidden_split, void *workspace, size_t workspace_bytes,
+                            void *stream);
 
 /*
  * code_t[d, h*cells + k] = code[h, k, d]: the K-major right operand of the tensor-core

@@ -31,7 +31,7 @@ def _routes(items: int, heads: int, cells: int, gen: torch.Generator) -> tuple[t
     return winner.to(torch.uint8), runner.to(torch.uint8), margins
 
 
-def _hidden(latent, code, winner, runner, margins, code_scale, training, use_tc, workspace=True):
+def _hidden(latent, code, winner, runner, margins, code_scale, training, use_tc, workspace=True, split=None):
     lib = nat.load()
     items, code_dim = latent.shape
     heads, cells, _ = code.shape
@@ -52,7 +52,8 @@ def _hidden(latent, code, winner, runner, margins, code_scale, training, use_tc,
         lib.tropnn_b200_trop_hidden(
             latent.data_ptr(), nat.float_code(latent.dtype), items, code_dim, code.data_ptr(), nat.ptr(code_t),
             nat.float_code(code.dtype), heads, cells, winner.data_ptr(), runner.data_ptr(), nat.U8,
-            margins.data_ptr(), float(code_scale), int(training), hidden.data_ptr(), nat.ptr(ws), ws_bytes, stream,
+            margins.data_ptr(), float(code_scale), int(training), hidden.data_ptr(), nat.ptr(split), nat.ptr(ws),
+            ws_bytes, stream,
         ),
         "trop_hidden",
     )
@@ -193,3 +194,38 @@ def test_transpose_to_half_exact(rows: int, cols: int, src: torch.dtype) -> None
                                                 out.data_ptr(), nat.stream_handle(x.device)), "transpose_to_half")
     torch.cuda.synchronize()
     assert torch.equal(out, x.to(dst).t())
+
+
+def _split_half(hidden: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    lib = nat.load()
+    rows, cols = hidden.shape
+    out = torch.empty((rows, 2 * cols), device=hidden.device, dtype=dtype)
+    nat.check(lib.tropnn_b200_split_half(hidden.data_ptr(), rows, cols, nat.float_code(dtype), None, out.data_ptr(),
+                                         nat.stream_handle(hidden.device)), "split_half")
+    return out
+
+
+@pytest.mark.parametrize(
+    ("items", "heads", "cells", "code_dim", "dtype", "training", "use_tc", "workspace"),
+    [
+        (640, 1024, 16, 256, torch.float16, True, True, True),  # split contraction: slice_reduce writes it
+        (640, 1024, 16, 256, torch.bfloat16, False, True, False),  # one CTA per row block: the kernel epilogue
+        (20000, 64, 16, 128, torch.float16, False, True, True),  # persistent loop, unsplit
+        (300, 12, 16, 64, torch.bfloat16, True, True, True),  # ragged rows
+        (300, 12, 16, 64, torch.float16, True, False, False),  # gather path: split_half after it
+    ],
+)
+def test_hidden_split_operand(items, heads, cells, code_dim, dtype, training, use_tc, workspace):
+    """The [hi | lo] split written beside hidden equals split_half(hidden) bit for bit, and the
+    hidden written with it equals the hidden written without it."""
+    gen = torch.Generator().manual_seed(21)
+    latent = torch.randn(items, code_dim, generator=gen).to(dtype).cuda()
+    code = (torch.randn(heads, cells, code_dim, generator=gen) * 0.5).to(dtype).cuda()
+    winner, runner, margins = (t.cuda() for t in _routes(items, heads, cells, gen))
+    split = torch.full((items, 2 * code_dim), float("nan"), device="cuda", dtype=dtype)
+    with_split = _hidden(latent, code, winner, runner, margins, 0.03, training, use_tc, workspace, split=split)
+    plain = _hidden(latent, code, winner, runner, margins, 0.03, training, use_tc, workspace)
+    assert np.array_equal(with_split, plain)
+    expect = _split_half(torch.from_numpy(with_split).cuda(), dtype)
+    torch.cuda.synchronize()
+    assert torch.equal(split.view(torch.int16), expect.view(torch.int16))

@@ -17,7 +17,7 @@ from pathlib import Path
 import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtropnn_b200.so"
-ABI_VERSION = 15
+ABI_VERSION = 16
 
 # tropnn_b200_dtype
 F32, F16, BF16, U8, I16, I64 = 0, 1, 2, 3, 4, 5
@@ -85,7 +85,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tropnn_b200_trop_hidden_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
     "tropnn_b200_trop_hidden": (
         _i32,
-        [_p, _i32, _i64, _i64, _p, _p, _i32, _i64, _i64, _p, _p, _i32, _p, _f32, _i32, _p, _p, _sz, _p],
+        [_p, _i32, _i64, _i64, _p, _p, _i32, _i64, _i64, _p, _p, _i32, _p, _f32, _i32, _p, _p, _p, _sz, _p],
     ),
     "tropnn_b200_trop_code_transpose": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p]),
     "tropnn_b200_trop_proj_workspace_size": (_sz, [_i64, _i64, _i64]),

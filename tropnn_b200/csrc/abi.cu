@@ -106,7 +106,7 @@ extern "C" {
 
 const char *tropnn_b200_last_error(void) { return tropnn_b200::g_last_error.c_str(); }
 
-int tropnn_b200_abi_version(void) { return 15; }
+int tropnn_b200_abi_version(void) { return 16; }
 
 int tropnn_b200_check_device(int device) {
   int major = 0;

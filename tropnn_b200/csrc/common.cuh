@@ -37,11 +37,13 @@ inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s
 // Epilogues of slice_reduce_impl (slice_reduce.cu): the sum of a split contraction's slice
 // partials (float4 partial[tile * splits + slice][tile_cols / 4][128 rows]) rounded to a half
 // dtype (or rounded and written transposed), plus an f32 bias, or added to a latent row times a
-// scale.
+// scale (kReduceHidden also writes the [hi | lo] half-precision split of each hidden row to
+// `split` [rows, 2 * cols] when it is given).
 enum SliceReduceMode { kReduceHalf = 0, kReduceF32 = 1, kReduceHidden = 2, kReduceHalfT = 3 };
 int slice_reduce_impl(int mode, const void *partial, int splits, int n_tiles, int tile_cols, int64_t rows,
                       int64_t cols, void *out, int out_dtype, int64_t ldo, const float *bias, const void *latent,
-                      int latent_dtype, float scale, cudaStream_t stream);
+                      int latent_dtype, float scale, cudaStream_t stream, void *split = nullptr,
+                      int split_dtype = 0);
 
 // Power-of-two scale that brings a gradient tensor whose largest |value| has the f32 bits
 // `absmax_bits` into [16, 32): converted to f16 after it, the gradient neither underflows (f16's

@@ -127,6 +127,15 @@ struct HalfBits<__nv_bfloat16> {
   __device__ static uint32_t bits(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
 };
 
+// The f32 value of half-precision bits.
+template <typename PT>
+__device__ __forceinline__ float half_value(uint32_t bits) {
+  if constexpr (std::is_same<PT, __half>::value)
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits)));
+  else
+    return __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(bits)));
+}
+
 // 32 latent values of one row as f32.
 template <typename LT>
 __device__ __forceinline__ void load_row32(const LT *__restrict__ p, float (&out)[32]) {
@@ -184,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
     const __grid_constant__ CUtensorMap map_ct, const LT *__restrict__ latent, const uint8_t *__restrict__ winner,
     const uint8_t *__restrict__ runner, const float *__restrict__ margins, float code_scale, int64_t rows, int H,
     int D, int kblocks, int bstages, int64_t row_blocks, const uint32_t *__restrict__ absmax, int vec_routes,
-    float *__restrict__ hidden, int splits, float4 *__restrict__ partial) {
+    float *__restrict__ hidden, PT *__restrict__ hidden_split, int splits, float4 *__restrict__ partial) {
   static_assert(K >= 2 && K <= kBK && K % 2 == 0, "cells must be even and at most 64");
   constexpr int kHeadsPerBlock = kBK / K;
   // Signed mode (router term of grad_z): the gm weights are scaled by the power-of-two gradient
@@ -443,13 +452,30 @@ __global__ void __launch_bounds__(kThreads, 1) trop_hidden_onehot_kernel(
             p[size_t(e) * kBM] = make_float4(__fmul_rn(acc[4 * e], unscale), __fmul_rn(acc[4 * e + 1], unscale),
                                              __fmul_rn(acc[4 * e + 2], unscale), __fmul_rn(acc[4 * e + 3], unscale));
         } else if (row < rows) {
+          float h[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) h[e] = __fadd_rn(lat[e], __fmul_rn(acc[e], out_scale));
           float *out = hidden + row * D + c;
 #pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            *reinterpret_cast<float4 *>(out + e) = make_float4(
-                __fadd_rn(lat[e], __fmul_rn(acc[e], out_scale)), __fadd_rn(lat[e + 1], __fmul_rn(acc[e + 1], out_scale)),
-                __fadd_rn(lat[e + 2], __fmul_rn(acc[e + 2], out_scale)),
-                __fadd_rn(lat[e + 3], __fmul_rn(acc[e + 3], out_scale)));
+          for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4 *>(out + e) = make_float4(h[e], h[e + 1], h[e + 2], h[e + 3]);
+          if (hidden_split != nullptr) {
+            // The output map's operand [hi | lo] of the row (hi = half(h), lo = half(h - hi)),
+            // written here instead of by a separate split pass over hidden.
+            PT *hi_row = hidden_split + row * (2 * int64_t(D)) + c;
+#pragma unroll
+            for (int e = 0; e < 32; e += 8) {
+              uint32_t hb[4], lb[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const uint32_t h0 = HalfBits<PT>::bits(h[e + 2 * k]), h1 = HalfBits<PT>::bits(h[e + 2 * k + 1]);
+                hb[k] = h0 | (h1 << 16);
+                lb[k] = HalfBits<PT>::bits(__fsub_rn(h[e + 2 * k], half_value<PT>(h0))) |
+                        (HalfBits<PT>::bits(__fsub_rn(h[e + 2 * k + 1], half_value<PT>(h1))) << 16);
+              }
+              *reinterpret_cast<uint4 *>(hi_row + e) = make_uint4(hb[0], hb[1], hb[2], hb[3]);
+              *reinterpret_cast<uint4 *>(hi_row + D + e) = make_uint4(lb[0], lb[1], lb[2], lb[3]);
+            }
+          }
         }
       }
     }
@@ -545,7 +571,7 @@ size_t onehot_workspace(int64_t rows, int64_t D, int64_t hk) {
 template <typename PT, typename LT, int K>
 int launch_onehot(const void *latent, int64_t rows, int D, const void *code_t, int H, const uint8_t *win,
                   const uint8_t *run, const float *m, float code_scale, int mode, const uint32_t *absmax, float *hidden,
-                  void *ws, size_t ws_bytes, cudaStream_t stream) {
+                  void *hidden_split, void *ws, size_t ws_bytes, cudaStream_t stream) {
   const CUtensorMapDataType dt =
       std::is_same<PT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int64_t hk = int64_t(H) * K;
@@ -577,28 +603,35 @@ int launch_onehot(const void *latent, int64_t rows, int D, const void *code_t, i
                                          : trop_hidden_onehot_kernel<PT, LT, K, kOneHotEval>;
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_hidden_sm100"));
   kernel<<<grid, kThreads, smem, stream>>>(map_ct, static_cast<const LT *>(latent), win, run, m, code_scale, rows, H, D,
-                                           kblocks, bst, row_blocks, absmax, vec_routes, hidden, splits, partial);
+                                           kblocks, bst, row_blocks, absmax, vec_routes, hidden,
+                                           static_cast<PT *>(hidden_split), splits, partial);
   TB_CHECK(check_launch("trop_hidden_sm100"));
   if (splits == 1) return TROPNN_B200_OK;
-  // hidden = latent + code_scale * (slices summed in slice order).
+  // hidden = latent + code_scale * (slices summed in slice order), and its [hi | lo] split.
   return slice_reduce_impl(kReduceHidden, partial, splits, 1, D, rows, D, hidden, TROPNN_B200_F32, D, nullptr, latent,
                            std::is_same<LT, float>::value ? TROPNN_B200_F32
                            : std::is_same<LT, __half>::value ? TROPNN_B200_F16 : TROPNN_B200_BF16,
-                           code_scale, stream);
+                           code_scale, stream, hidden_split,
+                           std::is_same<PT, __half>::value ? TROPNN_B200_F16 : TROPNN_B200_BF16);
 }
 
 template <typename PT, typename LT>
 int dispatch_onehot(int K, const void *latent, int64_t rows, int D, const void *code_t, int H, const uint8_t *win,
                     const uint8_t *run, const float *m, float code_scale, int mode, const uint32_t *absmax, float *hidden,
-                    void *ws, size_t wsb, cudaStream_t stream) {
+                    void *hs, void *ws, size_t wsb, cudaStream_t stream) {
   switch (K) {
-    case 2: return launch_onehot<PT, LT, 2>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, ws, wsb, stream);
-    case 4: return launch_onehot<PT, LT, 4>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, ws, wsb, stream);
-    case 8: return launch_onehot<PT, LT, 8>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, ws, wsb, stream);
+    case 2: return launch_onehot<PT, LT, 2>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, hs,
+                                        ws, wsb, stream);
+    case 4: return launch_onehot<PT, LT, 4>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, hs,
+                                        ws, wsb, stream);
+    case 8: return launch_onehot<PT, LT, 8>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, hs,
+                                        ws, wsb, stream);
     case 16:
-      return launch_onehot<PT, LT, 16>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, ws, wsb, stream);
+      return launch_onehot<PT, LT, 16>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, hs,
+                                        ws, wsb, stream);
     default:
-      return launch_onehot<PT, LT, 32>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, ws, wsb, stream);
+      return launch_onehot<PT, LT, 32>(latent, rows, D, code_t, H, win, run, m, code_scale, mode, absmax, hidden, hs,
+                                        ws, wsb, stream);
   }
 }
 
@@ -620,7 +653,10 @@ size_t trop_hidden_sm100_workspace(int64_t items, int64_t D, int64_t H, int64_t 
 
 int trop_hidden_sm100_impl(const void *latent, int zt, int64_t items, int64_t D, const void *code_t, int pt,
                            int64_t H, int64_t K, const void *win, const void *run, const float *m, float code_scale,
-                           int mode, const uint32_t *absmax, float *hidden, void *ws, size_t wsb, cudaStream_t stream) {
+                           int mode, const uint32_t *absmax, float *hidden, void *hidden_split, void *ws, size_t wsb,
+                           cudaStream_t stream) {
+  TB_REQUIRE(hidden_split == nullptr || reinterpret_cast<uintptr_t>(hidden_split) % 16 == 0, TROPNN_B200_ERR_INVALID,
+             "trop_hidden_sm100: hidden_split must be 16-byte aligned");
   TB_REQUIRE(hidden_sm100_supported(items, D, H, K, pt, zt, TROPNN_B200_U8, latent, code_t, hidden),
              TROPNN_B200_ERR_INVALID, "trop_hidden_sm100: unsupported shape, dtype or alignment");
   TB_REQUIRE(mode >= kOneHotEval && mode <= kOneHotSigned, TROPNN_B200_ERR_INVALID, "trop_hidden_sm100: bad mode");
@@ -631,15 +667,15 @@ int trop_hidden_sm100_impl(const void *latent, int zt, int64_t items, int64_t D,
   if (pt == TROPNN_B200_F16) {
     if (zt == TROPNN_B200_F32)
       return dispatch_onehot<__half, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, absmax, hidden,
-                                            ws, wsb, stream);
+                                            hidden_split, ws, wsb, stream);
     return dispatch_onehot<__half, __half>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, absmax, hidden,
-                                           ws, wsb, stream);
+                                           hidden_split, ws, wsb, stream);
   }
   if (zt == TROPNN_B200_F32)
-    return dispatch_onehot<__nv_bfloat16, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, absmax, hidden,
-                                                 ws, wsb, stream);
+    return dispatch_onehot<__nv_bfloat16, float>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode, absmax,
+                                                 hidden, hidden_split, ws, wsb, stream);
   return dispatch_onehot<__nv_bfloat16, __nv_bfloat16>(Ki, latent, items, Di, code_t, Hi, w, r, m, code_scale, mode,
-                                                       absmax, hidden, ws, wsb, stream);
+                                                       absmax, hidden, hidden_split, ws, wsb, stream);
 }
 
 int trop_code_transpose_impl(const void *code, int pt, int64_t H, int64_t K, int64_t D, void *code_t,

@@ -8,7 +8,9 @@
 // order (deterministic) and applies the product's epilogue:
 //   kReduceHalf    out[row, col] = half(sum)                 (the projection's z)
 //   kReduceF32     out[row, col] = sum + bias[col]           (the f32 product)
-//   kReduceHidden  out[row, col] = latent[row, col] + scale * sum   (code sum / router term)
+//   kReduceHidden  out[row, col] = latent[row, col] + scale * sum   (code sum / router term),
+//                  and optionally split[row] = [hi | lo] with hi = half(out), lo = half(out - hi)
+//                  (the operand of the output map's f32-input product)
 //   kReduceHalfT   out[col, row] = half(sum)                 (the projection's weight gradient,
 //                                                             computed transposed)
 // A block takes 32 rows x one tile's columns: the slices' loads are coalesced over the rows
@@ -30,7 +32,8 @@ __global__ void __launch_bounds__(kThreads) slice_reduce_kernel(const float4 *__
                                                                int n_tiles, int tile_cols, int64_t rows, int64_t cols,
                                                                OT *__restrict__ out, int64_t ldo,
                                                                const float *__restrict__ bias,
-                                                               const LT *__restrict__ latent, float scale) {
+                                                               const LT *__restrict__ latent, float scale,
+                                                               void *__restrict__ split, int split_f16) {
   __shared__ float tile[kRows][kMaxTileCols + 1];
   const int64_t rb = blockIdx.y;                   // 128-row block
   const int sub = blockIdx.x % 4;                  // which 32 rows of it
@@ -81,7 +84,20 @@ __global__ void __launch_bounds__(kThreads) slice_reduce_kernel(const float4 *__
     } else if constexpr (MODE == kReduceF32) {
       out[row * ldo + col] = bias != nullptr ? __fadd_rn(sum, __ldg(bias + col)) : sum;
     } else {
-      out[row * ldo + col] = __fadd_rn(to_f32<LT>(latent[row * cols + col]), __fmul_rn(sum, scale));
+      const float h = __fadd_rn(to_f32<LT>(latent[row * cols + col]), __fmul_rn(sum, scale));
+      out[row * ldo + col] = h;
+      if (split != nullptr) {
+        const int64_t o = row * 2 * cols + col;
+        if (split_f16) {
+          const __half hi = from_f32<__half>(h);
+          static_cast<__half *>(split)[o] = hi;
+          static_cast<__half *>(split)[o + cols] = from_f32<__half>(__fsub_rn(h, to_f32(hi)));
+        } else {
+          const __nv_bfloat16 hi = from_f32<__nv_bfloat16>(h);
+          static_cast<__nv_bfloat16 *>(split)[o] = hi;
+          static_cast<__nv_bfloat16 *>(split)[o + cols] = from_f32<__nv_bfloat16>(__fsub_rn(h, to_f32(hi)));
+        }
+      }
     }
   }
   }
@@ -89,13 +105,14 @@ __global__ void __launch_bounds__(kThreads) slice_reduce_kernel(const float4 *__
 
 template <int MODE, typename OT, typename LT>
 int launch_reduce(const void *partial, int splits, int n_tiles, int tile_cols, int64_t rows, int64_t cols, void *out,
-                  int64_t ldo, const float *bias, const void *latent, float scale, cudaStream_t stream) {
+                  int64_t ldo, const float *bias, const void *latent, float scale, cudaStream_t stream,
+                  void *split = nullptr, int split_f16 = 0) {
   const int64_t row_blocks = ceil_div(rows, int64_t(128));
   TB_REQUIRE(row_blocks < 65536, TROPNN_B200_ERR_INVALID, "slice_reduce: %lld rows exceed the grid", (long long)rows);
   const dim3 grid(static_cast<unsigned>(4 * n_tiles), static_cast<unsigned>(row_blocks));
   slice_reduce_kernel<MODE, OT, LT><<<grid, kThreads, 0, stream>>>(
       static_cast<const float4 *>(partial), splits, n_tiles, tile_cols, rows, cols, static_cast<OT *>(out), ldo, bias,
-      static_cast<const LT *>(latent), scale);
+      static_cast<const LT *>(latent), scale, split, split_f16);
   return check_launch("slice_reduce");
 }
 
@@ -103,7 +120,7 @@ int launch_reduce(const void *partial, int splits, int n_tiles, int tile_cols, i
 
 int slice_reduce_impl(int mode, const void *partial, int splits, int n_tiles, int tile_cols, int64_t rows,
                       int64_t cols, void *out, int out_dtype, int64_t ldo, const float *bias, const void *latent,
-                      int latent_dtype, float scale, cudaStream_t stream) {
+                      int latent_dtype, float scale, cudaStream_t stream, void *split, int split_dtype) {
   TB_REQUIRE(splits >= 1 && splits <= kMaxSplits && tile_cols % 4 == 0 && tile_cols >= 4 &&
                  tile_cols <= kMaxTileCols && n_tiles >= 1,
              TROPNN_B200_ERR_INVALID, "slice_reduce: bad geometry splits=%d tile_cols=%d", splits, tile_cols);
@@ -124,15 +141,19 @@ int slice_reduce_impl(int mode, const void *partial, int splits, int n_tiles, in
     case kReduceF32:
       return launch_reduce<kReduceF32, float, float>(partial, splits, n_tiles, tile_cols, rows, cols, out, ldo, bias,
                                                      nullptr, 1.f, stream);
-    default:
+    default: {
+      TB_REQUIRE(split == nullptr || split_dtype == TROPNN_B200_F16 || split_dtype == TROPNN_B200_BF16,
+                 TROPNN_B200_ERR_DTYPE, "slice_reduce: split dtype %s unsupported", dtype_name(split_dtype));
+      const int f16 = split_dtype == TROPNN_B200_F16 ? 1 : 0;
       if (latent_dtype == TROPNN_B200_F32)
         return launch_reduce<kReduceHidden, float, float>(partial, splits, n_tiles, tile_cols, rows, cols, out, ldo,
-                                                          nullptr, latent, scale, stream);
+                                                          nullptr, latent, scale, stream, split, f16);
       if (latent_dtype == TROPNN_B200_F16)
         return launch_reduce<kReduceHidden, float, __half>(partial, splits, n_tiles, tile_cols, rows, cols, out, ldo,
-                                                           nullptr, latent, scale, stream);
+                                                           nullptr, latent, scale, stream, split, f16);
       return launch_reduce<kReduceHidden, float, __nv_bfloat16>(partial, splits, n_tiles, tile_cols, rows, cols, out,
-                                                                ldo, nullptr, latent, scale, stream);
+                                                                ldo, nullptr, latent, scale, stream, split, f16);
+    }
   }
 }
 

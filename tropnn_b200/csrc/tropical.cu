@@ -40,7 +40,10 @@ bool hidden_sm100_supported(int64_t items, int64_t D, int64_t H, int64_t K, int 
                             const void *code_t, const void *hidden);
 int trop_hidden_sm100_impl(const void *latent, int zt, int64_t items, int64_t D, const void *code_t, int pt,
                            int64_t H, int64_t K, const void *win, const void *run, const float *m, float code_scale,
-                           int mode, const uint32_t *absmax, float *hidden, void *ws, size_t wsb, cudaStream_t stream);
+                           int mode, const uint32_t *absmax, float *hidden, void *hidden_split, void *ws, size_t wsb,
+                           cudaStream_t stream);
+int split_half_impl(const float *x, int64_t rows, int64_t cols, int dtype, const uint32_t *absmax, void *out,
+                    cudaStream_t stream);
 size_t trop_hidden_sm100_workspace(int64_t items, int64_t D, int64_t H, int64_t K);
 int trop_code_transpose_impl(const void *code, int pt, int64_t H, int64_t K, int64_t D, void *code_t,
                              cudaStream_t stream);
@@ -546,8 +549,10 @@ int hidden_by_width(const void *z, int64_t items, int D, const void *code, int H
 
 int trop_hidden_impl(const void *z, int zt, int64_t items, int64_t D, const void *code, const void *code_t, int pt,
                      int64_t H, int64_t K, const void *win, const void *run, int it, const float *m, float code_scale,
-                     int training, float *hidden, void *ws, size_t wsb, cudaStream_t stream) {
+                     int training, float *hidden, void *hidden_split, void *ws, size_t wsb, cudaStream_t stream) {
   TB_CHECK(validate_trop(items, D, H, K));
+  TB_REQUIRE(hidden_split == nullptr || pt == TROPNN_B200_F16 || pt == TROPNN_B200_BF16, TROPNN_B200_ERR_DTYPE,
+             "trop_hidden: hidden_split needs f16/bf16 codes, got %s", dtype_name(pt));
   TB_REQUIRE(is_float_dtype(pt), TROPNN_B200_ERR_DTYPE, "trop_hidden: param dtype %s unsupported", dtype_name(pt));
   TB_CHECK(check_index_dtype(K, it));
   TB_CHECK(check_latent_dtype(zt, pt, "trop_hidden"));
@@ -557,7 +562,7 @@ int trop_hidden_impl(const void *z, int zt, int64_t items, int64_t D, const void
   // Half-precision codes with their transpose at hand: one-hot GEMM on the tensor cores.
   if (hidden_sm100_supported(items, D, H, K, pt, zt, it, z, code_t, hidden))
     return trop_hidden_sm100_impl(z, zt, items, D, code_t, pt, H, K, win, run, m, code_scale, training, nullptr, hidden,
-                                  ws, wsb, stream);
+                                  hidden_split, ws, wsb, stream);
   const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
   const bool train = training != 0;
   const bool zp = zt != TROPNN_B200_F32;
@@ -573,7 +578,8 @@ int trop_hidden_impl(const void *z, int zt, int64_t items, int64_t D, const void
     status = hidden_by_width<PT, IT, false>(z, items, Di, code, Hi, Ki, win, run, m, code_scale, train, hidden,
                                             stream);
   }))
-  return status;
+  if (status != TROPNN_B200_OK || hidden_split == nullptr) return status;
+  return split_half_impl(hidden, items, D, pt, nullptr, hidden_split, stream);
 }
 
 template <typename PT, typename IT, int VEC, int NJ>
@@ -701,11 +707,11 @@ size_t tropnn_b200_trop_hidden_workspace_size(int64_t items, int64_t code_dim, i
 int tropnn_b200_trop_hidden(const void *latent, int latent_dtype, int64_t items, int64_t code_dim, const void *code,
                             const void *code_t, int param_dtype, int64_t heads, int64_t cells, const void *winner,
                             const void *runner, int index_dtype, const float *margins, float code_scale, int training,
-                            float *hidden, void *workspace, size_t workspace_bytes, void *stream) {
+                            float *hidden, void *hidden_split, void *workspace, size_t workspace_bytes, void *stream) {
   TB_CHECK(tropnn_b200::check_current_device());
   TB_CHECK(tropnn_b200::trop_hidden_impl(latent, latent_dtype, items, code_dim, code, code_t, param_dtype, heads, cells,
-                                         winner, runner, index_dtype, margins, code_scale, training, hidden, workspace,
-                                         workspace_bytes, tropnn_b200::as_stream(stream)));
+                                         winner, runner, index_dtype, margins, code_scale, training, hidden,
+                                         hidden_split, workspace, workspace_bytes, tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 
@@ -737,8 +743,8 @@ int tropnn_b200_trop_router_term(const float *grad_hidden, int64_t items, int64_
   if (items == 0) return tropnn_b200::clear_error();
   TB_CHECK(tropnn_b200::trop_hidden_sm100_impl(grad_hidden, TROPNN_B200_F32, items, code_dim, router_weight_t,
                                                param_dtype, heads, cells, winner, runner, gm, 1.0f, 2,
-                                               static_cast<const uint32_t *>(grad_absmax), grad_latent, workspace,
-                                               workspace_bytes, tropnn_b200::as_stream(stream)));
+                                               static_cast<const uint32_t *>(grad_absmax), grad_latent, nullptr,
+                                               workspace, workspace_bytes, tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 

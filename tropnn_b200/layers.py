@@ -33,12 +33,13 @@ from .ops import (
     linear_f32_eligible,
     linear_f32out_b200,
     linear_f32out_eligible,
+    linear_f32out_shape_ok,
     pairwise_anchor_index,
     pairwise_b200,
     proj_eligible,
     trop_exact_eval_b200,
     trop_project_b200,
-    trop_route_hidden_packed,
+    trop_route_hidden_split,
     transpose_f32,
 )
 
@@ -185,7 +186,7 @@ def trop_forward_b200(layer: nn.Module, x: Tensor) -> Tensor:
     The projection (tropical.py:96-99) runs on the b200 tensor-core projection kernel for
     half-precision weights (ops.trop_project_b200) and on the 3xTF32 tensor-core product for
     f32 weights (ops.linear_f32_b200); the route scores, top-2, code sum and their backward are
-    the b200 kernels (ops.trop_route_hidden_packed); the output map (tropical.py:140-146) is the
+    the b200 kernels (ops.trop_route_hidden_split); the output map (tropical.py:140-146) is the
     b200 tensor-core linear map for half-precision weights (ops.linear_f32out_b200) or the
     3xTF32 product for f32 weights. Widths the kernels do not tile (inputs not a multiple of 4
     floats wide) use torch.
@@ -226,7 +227,17 @@ def _routed_code_forward_b200(
     # parameters the b200 op takes z in that dtype instead (the upcast is exact and happens
     # in-kernel), which lets the route scores run on the tensor cores.
     latent = z if z.dtype in (torch.float16, torch.bfloat16) and z.dtype == router_weight.dtype else z.to(compute_dtype)
-    hidden, winner, margins = trop_route_hidden_packed(
+    out_weight = layer.output_proj.weight
+    # Half-precision output weight of the code dtype: the code sum's epilogue also writes the
+    # [hi | lo] split of hidden that the output map's tensor-core product reads.
+    fuse_split = (
+        out_weight.dtype == code.dtype
+        and out_weight.dtype in (torch.float16, torch.bfloat16)
+        and out_weight.is_cuda
+        and linear_f32out_shape_ok(out_weight.shape[0], out_weight.shape[1])
+        and out_weight.shape[1] == code.shape[-1]
+    )
+    hidden, winner, margins, hidden_split = trop_route_hidden_split(
         latent,
         router_weight,
         router_bias,
@@ -234,12 +245,13 @@ def _routed_code_forward_b200(
         code_scale=layer.code_scale,
         training=layer.training,
         keep_margins=getattr(layer, "cache_route_debug", True),
+        split_dtype=out_weight.dtype if fuse_split else None,
     )
     bias = layer.output_proj.bias
-    if linear_f32out_eligible(hidden, layer.output_proj.weight):
+    if linear_f32out_eligible(hidden, out_weight):
         # Half-precision output weight: the f32 product on the tensor cores (split f32
         # hidden, bias fused), the reference's f32 math in the backward.
-        output = linear_f32out_b200(hidden, layer.output_proj.weight, bias)
+        output = linear_f32out_b200(hidden, out_weight, bias, hidden_split=hidden_split)
     elif linear_f32_eligible(hidden, layer.output_proj.weight) and (bias is None or bias.dtype == torch.float32):
         # f32 output weight: the reference's f32 F.linear as 3xTF32 on the tensor cores.
         output = linear_f32_b200(hidden, layer.output_proj.weight, bias)

@@ -504,7 +504,7 @@ def _trop_backward_tensor_cores(ctx, g, z, weight, code, winner, runner, margins
         grad_w = None
     if not ctx.needs_input_grad[2]:
         grad_b = None
-    return grad_z.view(batch, steps, code_dim).to(z.dtype), grad_w, grad_b, grad_c, None, None, None
+    return grad_z.view(batch, steps, code_dim).to(z.dtype), grad_w, grad_b, grad_c, None, None, None, None
 
 
 class _TropRouteB200Function(torch.autograd.Function):
@@ -518,7 +518,8 @@ class _TropRouteB200Function(torch.autograd.Function):
         code_scale: float,
         training: bool,
         keep_margins: bool,
-    ) -> tuple[Tensor, Tensor, Tensor]:
+        split_dtype: torch.dtype | None,
+    ) -> tuple[Tensor, Tensor, Tensor, Tensor]:
         batch, steps, code_dim = latent.shape
         heads, cells, _ = router_weight.shape
         items = batch * steps
@@ -537,6 +538,10 @@ class _TropRouteB200Function(torch.autograd.Function):
         runner = torch.empty((items, heads), device=dev, dtype=idx_dtype) if training else None
         margins = torch.empty((items, heads) if (training or keep_margins) else (0,), device=dev, dtype=torch.float32)
         hidden = torch.empty((items, code_dim), device=dev, dtype=torch.float32)
+        # The output map's [hi | lo] operand, written by the code sum's epilogue (no separate
+        # split pass over hidden).
+        split = torch.empty((items, 2 * code_dim) if split_dtype is not None else (0,), device=dev,
+                            dtype=split_dtype if split_dtype is not None else code_c.dtype)
         stream = nat.stream_handle(dev)
         lib = nat.load()
         icode = nat.index_code(idx_dtype)
@@ -605,6 +610,7 @@ class _TropRouteB200Function(torch.autograd.Function):
             float(code_scale),
             int(bool(training)),
             hidden.data_ptr(),
+            split.data_ptr() if split.numel() else None,
             nat.ptr(hidden_ws),
             0 if hidden_ws is None else hidden_ws.numel(),
             stream,
@@ -615,12 +621,14 @@ class _TropRouteB200Function(torch.autograd.Function):
         ctx.shape = (batch, steps, code_dim, heads, cells)
         winner_out = winner.view(batch, steps, heads)
         margins_out = margins.view(batch, steps, heads) if margins.dim() == 2 else margins
-        ctx.mark_non_differentiable(winner_out, margins_out)
-        return hidden.view(batch, steps, code_dim), winner_out, margins_out
+        ctx.mark_non_differentiable(winner_out, margins_out, split)
+        return hidden.view(batch, steps, code_dim), winner_out, margins_out, split
 
     @staticmethod
-    def backward(ctx: Any, grad_hidden: Tensor, grad_winner: Tensor | None, grad_margins: Tensor | None) -> tuple[Any, ...]:
-        del grad_winner, grad_margins
+    def backward(
+        ctx: Any, grad_hidden: Tensor, grad_winner: Tensor | None, grad_margins: Tensor | None, grad_split: Tensor | None
+    ) -> tuple[Any, ...]:
+        del grad_winner, grad_margins, grad_split
         z, weight, code, winner, runner, margins = ctx.saved_tensors
         batch, steps, code_dim, heads, cells = ctx.shape
         items = batch * steps
@@ -767,7 +775,7 @@ class _TropRouteB200Function(torch.autograd.Function):
             grad_b = None
         # A half-precision latent gets its gradient rounded once to its dtype, as the
         # reference's `.to(compute_dtype)` backward does.
-        return grad_z.view(batch, steps, code_dim).to(z.dtype), grad_w, grad_b, grad_c, None, None, None
+        return grad_z.view(batch, steps, code_dim).to(z.dtype), grad_w, grad_b, grad_c, None, None, None, None
 
 
 def trop_route_hidden_b200(
@@ -817,6 +825,28 @@ def trop_route_hidden_packed(
     cells <= 256, layers/routing.py:18-23) instead of int64, and the margins computed in
     eval only when ``keep_margins`` (otherwise an empty tensor). The layers use it so the
     int64 debug-cache copy of the routes is made only when someone reads it."""
+    hidden, winner, margins, _ = trop_route_hidden_split(
+        latent, router_weight, router_bias, code, code_scale=code_scale, training=training, keep_margins=keep_margins
+    )
+    return hidden, winner, margins
+
+
+def trop_route_hidden_split(
+    latent: Tensor,
+    router_weight: Tensor,
+    router_bias: Tensor,
+    code: Tensor,
+    *,
+    code_scale: float,
+    training: bool = False,
+    keep_margins: bool = True,
+    split_dtype: torch.dtype | None = None,
+) -> tuple[Tensor, Tensor, Tensor, Tensor | None]:
+    """``trop_route_hidden_packed`` that also returns hidden's [hi | lo] split in
+    ``split_dtype`` ([items, 2 * code_dim], hi = half(hidden), lo = half(hidden - hi)): the left
+    operand of the output map's f32-input product (``linear_f32out_b200(..., hidden_split=)``),
+    formed by the code sum's epilogue. ``split_dtype`` must be the code dtype (f16/bf16); None
+    returns no split."""
     for name, t in (("latent", latent), ("router_weight", router_weight), ("router_bias", router_bias), ("code", code)):
         _require_cuda(t, name)
         if t.device != latent.device:
@@ -837,10 +867,14 @@ def trop_route_hidden_packed(
         )
     if not math.isfinite(float(code_scale)):
         raise ValueError(f"code_scale must be finite, got {code_scale}")
+    if split_dtype is not None and (split_dtype != code.dtype or split_dtype not in (torch.float16, torch.bfloat16)
+                                    or latent.shape[-1] % 4 != 0):
+        raise ValueError(f"split_dtype {split_dtype} needs f16/bf16 codes of that dtype and code_dim % 4 == 0")
     with torch.cuda.device(latent.device):
-        return _TropRouteB200Function.apply(
-            latent, router_weight, router_bias, code, float(code_scale), bool(training), bool(keep_margins)
+        hidden, winner, margins, split = _TropRouteB200Function.apply(
+            latent, router_weight, router_bias, code, float(code_scale), bool(training), bool(keep_margins), split_dtype
         )
+    return hidden, winner, margins, (split if split_dtype is not None else None)
 
 
 # in_features the exact eval path routes on: the fp32 route kernel stages a row of x per lane in
@@ -894,8 +928,13 @@ def trop_exact_eval_b200(
                 margins.data_ptr() if margins.numel() else None, None, 0, stream)
         _launch("trop_hidden", lib.tropnn_b200_trop_hidden, base.data_ptr(), nat.F32, items, out_features, v.data_ptr(),
                 None, nat.F32, heads, cells, winner.data_ptr(), None, icode, None, float(code_scale), 0, y.data_ptr(),
-                None, 0, stream)
+                None, None, 0, stream)
     return y, winner, margins
+
+
+def linear_f32out_shape_ok(out_features: int, in_features: int) -> bool:
+    """Weight shapes [out, in] the tensor-core f32-input linear map tiles."""
+    return in_features % 64 == 0 and 64 <= in_features <= 256 and out_features % 4 == 0
 
 
 def linear_f32out_eligible(hidden: Tensor, weight: Tensor) -> bool:
@@ -905,9 +944,7 @@ def linear_f32out_eligible(hidden: Tensor, weight: Tensor) -> bool:
         hidden.is_cuda
         and hidden.dtype == torch.float32
         and weight.dtype in (torch.float16, torch.bfloat16)
-        and in_features % 64 == 0
-        and 64 <= in_features <= 256
-        and out_features % 4 == 0
+        and linear_f32out_shape_ok(out_features, in_features)
         and hidden.shape[-1] == in_features
     )
 
@@ -926,7 +963,7 @@ class _LinearF32OutFunction(torch.autograd.Function):
     grad_b cast back to the parameter dtypes like the reference's ``.to`` upcast."""
 
     @staticmethod
-    def forward(ctx: Any, hidden: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:
+    def forward(ctx: Any, hidden: Tensor, weight: Tensor, bias: Tensor | None, hidden_split: Tensor | None) -> Tensor:
         rows, in_features = hidden.shape
         out_features = weight.shape[0]
         dev = hidden.device
@@ -935,9 +972,12 @@ class _LinearF32OutFunction(torch.autograd.Function):
         dcode = nat.float_code(w.dtype)
         stream = nat.stream_handle(dev)
         lib = nat.load()
-        split = torch.empty((rows, 2 * in_features), device=dev, dtype=w.dtype)
-        _launch("split_half", lib.tropnn_b200_split_half, h.data_ptr(), rows, in_features, dcode, None, split.data_ptr(),
-                stream)
+        if hidden_split is not None:
+            split = hidden_split  # formed by the producer of hidden (the code sum's epilogue)
+        else:
+            split = torch.empty((rows, 2 * in_features), device=dev, dtype=w.dtype)
+            _launch("split_half", lib.tropnn_b200_split_half, h.data_ptr(), rows, in_features, dcode, None,
+                    split.data_ptr(), stream)
         b32 = None if bias is None else bias.to(torch.float32).contiguous()
         out = torch.empty((rows, out_features), device=dev, dtype=torch.float32)
         _launch(
@@ -959,7 +999,7 @@ class _LinearF32OutFunction(torch.autograd.Function):
         return out
 
     @staticmethod
-    def backward(ctx: Any, grad_out: Tensor) -> tuple[Tensor | None, Tensor | None, Tensor | None]:
+    def backward(ctx: Any, grad_out: Tensor) -> tuple[Tensor | None, Tensor | None, Tensor | None, None]:
         h, w = ctx.saved_tensors
         rows, in_features = h.shape
         out_features = w.shape[0]
@@ -972,6 +1012,7 @@ class _LinearF32OutFunction(torch.autograd.Function):
                 g @ w.to(torch.float32) if ctx.needs_input_grad[0] else None,
                 (g.t() @ h).to(w.dtype) if ctx.needs_input_grad[1] else None,
                 g.sum(0).to(ctx.bias_dtype) if need_b else None,
+                None,
             )
         stream = nat.stream_handle(dev)
         lib = nat.load()
@@ -998,19 +1039,34 @@ class _LinearF32OutFunction(torch.autograd.Function):
             )
             grad_w = gw if ctx.needs_input_grad[1] else None
             grad_b = gb.to(ctx.bias_dtype) if need_b else None
-        return grad_h, grad_w, grad_b
+        return grad_h, grad_w, grad_b, None
 
 
-def linear_f32out_b200(hidden: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:
-    """f32 ``hidden`` [..., in] times the half-precision ``weight`` [out, in] (+ bias) in f32."""
+def linear_f32out_b200(
+    hidden: Tensor, weight: Tensor, bias: Tensor | None, hidden_split: Tensor | None = None
+) -> Tensor:
+    """f32 ``hidden`` [..., in] times the half-precision ``weight`` [out, in] (+ bias) in f32.
+    ``hidden_split`` (optional): hidden's [hi | lo] split [rows, 2 * in] in the weight dtype,
+    as ``trop_route_hidden_split`` returns it; without it the split is formed here."""
     if not linear_f32out_eligible(hidden, weight):
         raise ValueError(
             f"linear_f32out_b200: unsupported hidden {tuple(hidden.shape)} {hidden.dtype} / weight "
             f"{tuple(weight.shape)} {weight.dtype}"
         )
+    rows = hidden.numel() // max(hidden.shape[-1], 1)
+    if hidden_split is not None and (
+        hidden_split.dtype != weight.dtype
+        or tuple(hidden_split.shape) != (rows, 2 * hidden.shape[-1])
+        or not hidden_split.is_contiguous()
+        or hidden_split.device != hidden.device
+    ):
+        raise ValueError(
+            f"linear_f32out_b200: hidden_split {tuple(hidden_split.shape)} {hidden_split.dtype} does not match "
+            f"hidden {tuple(hidden.shape)} and weight {weight.dtype}"
+        )
     lead = hidden.shape[:-1]
     with torch.cuda.device(hidden.device):
-        out = _LinearF32OutFunction.apply(hidden.reshape(-1, hidden.shape[-1]), weight, bias)
+        out = _LinearF32OutFunction.apply(hidden.reshape(-1, hidden.shape[-1]), weight, bias, hidden_split)
     return out.reshape(*lead, weight.shape[0])
 
 
