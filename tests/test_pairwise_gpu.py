@@ -281,3 +281,60 @@ def test_lut_grad_kernel_matches_sorted_rowsum(n, out_f, tables, comparisons, lu
         return
     assert rel_err(direct.double().cpu().numpy(), exact.numpy()) <= tol
     assert rel_err(direct.double().cpu().numpy(), sorted_sum.double().cpu().numpy()) <= tol
+
+
+@pytest.mark.parametrize(
+    ("rows", "in_f", "out_f", "tables", "comparisons", "lut_dtype"),
+    [
+        (37, 64, 512, 16, 4, torch.float32),  # small LUT: the per-row-block kernel
+        (258, 512, 4096, 64, 8, torch.float16),  # 128 MiB LUT: the staged gather, ragged last unit
+        (70, 256, 2560, 64, 8, torch.float16),  # partial column chunk (2560 of 4096)
+        (33, 256, 1536, 32, 8, torch.float32),  # f32 LUT, one partial 2048-column chunk
+        (19, 128, 2048, 16, 10, torch.bfloat16),  # 1024-entry tables
+        (20, 64, 8448, 8, 8, torch.float16),  # three column chunks, the last 256 columns wide
+    ],
+)
+def test_forward_sum_is_table_ordered_f32(rows, in_f, out_f, tables, comparisons, lut_dtype) -> None:
+    """y = out_scale * (((0 + L[0, i0]) + L[1, i1]) + ...) in f32, bit for bit, for the
+    per-row-block kernel and for the staged gather of LUTs larger than L2; indices and margins
+    against the oracle's routing."""
+    gen = torch.Generator().manual_seed(7)
+    x = torch.randn(rows, in_f, generator=gen).cuda()
+    anchors = torch.randint(0, in_f, (tables, comparisons, 2), generator=gen).cuda()
+    thr = (torch.randn(tables, comparisons, generator=gen) * 0.1).cuda()
+    lut = torch.randn(tables, 1 << comparisons, out_f, generator=gen).to(lut_dtype).cuda()
+    scale = 0.37
+    with torch.no_grad():
+        y, idx, margins = tropnn_b200.ops.pairwise_b200(x.view(rows, 1, in_f), anchors, thr, lut, use_min_margin_ste=True,
+                                                  output_scale=scale)
+        idx = idx.view(rows, tables)
+        acc = torch.zeros(rows, out_f, device="cuda")
+        for t in range(tables):
+            acc = acc + lut[t, idx[:, t]].float()
+        expect = acc * scale
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(rows, out_f), expect)
+    ref_idx, ref_u = oracle.pairwise_indices(x.cpu().numpy(), anchors.cpu().numpy(), thr.cpu().numpy())
+    assert np.array_equal(idx.cpu().numpy(), ref_idx)
+    assert np.array_equal(margins.view(rows, tables, comparisons).cpu().numpy(), ref_u)
+
+
+@pytest.mark.parametrize(
+    ("in_f", "out_f", "tables", "comparisons", "n", "dtype", "surrogate"),
+    [
+        (512, 2048, 32, 8, 203, torch.float32, "fast_sigmoid_odd"),  # 64 MiB f32 LUT, ragged last unit
+        (256, 4096, 40, 8, 77, torch.float16, "izhikevich"),  # 80 MiB f16 LUT, full 8 KB rows
+        (128, 3072, 48, 8, 9, torch.bfloat16, "fast_sigmoid_odd"),  # 6 KB rows, one partial unit
+    ],
+)
+def test_staged_paths_match_oracle(in_f, out_f, tables, comparisons, n, dtype, surrogate) -> None:
+    """LUTs larger than 32 MiB take the staged forward and the staged min-margin STE backward
+    (the kernels of config 5): forward bit-exact routes and margins, output and every gradient
+    against the oracle (1e-5 for f32 parameters, 2e-2 for half precision)."""
+    layer = tropnn_b200.PairwiseLinear(in_f, out_f, tables=tables, comparisons=comparisons, seed=8, surrogate=surrogate)
+    if dtype != torch.float32:
+        layer = layer.to(dtype)
+    with torch.no_grad():
+        layer.thresholds.normal_(0.0, 0.3)
+    x, g = _inputs(n, in_f, out_f, seed=9)
+    _compare(_run(layer, x, g), _oracle_case(layer, x, g), tol=FP32_TOL if dtype == torch.float32 else 2e-2)

@@ -17,6 +17,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace tropnn_b200 {
 
@@ -141,6 +142,287 @@ int launch_forward(const float *x, int64_t rows, int64_t in, const int64_t *anch
   return check_launch("pairwise_forward");
 }
 
+// Forward for LUTs larger than L2 (config 5: 1024 tables x 256 entries x 4096 f16 columns =
+// 2 GiB): pairwise_forward_staged_kernel. A selected LUT row is only reused from L2 while the
+// rows that select it pass its table at about the same time, so the CTAs must walk the tables
+// in step: a CTA takes a unit of kStageRows rows x one 8 KB column chunk of the LUT rows, and
+// the units run in waves of one unit per SM (one launch per wave), whose CTAs start together,
+// do the same work per table and so read the LUT from DRAM about once per wave.
+//
+// A CTA first computes its rows' routes (their latent rows staged in the still idle stage
+// ring, a thread per table: anchors and thresholds read once for all the rows), keeps them in
+// shared memory and, in the first column chunk, writes them out with the margins. Then one
+// producer thread streams, table after table, the unit's selected row slices (kStageRows bulk
+// copies of 8 KB, one per producer lane) into a ring of shared-memory slots of kSlotRows row
+// slices, each slot with its own full and empty barrier, about 200 KB in flight per SM
+// whatever the registers, and 16 consumer warps add 16 bytes of every row slice per thread
+// into f32 accumulators (kStageRows x 16 bytes of columns each), in the order of the copies. Per output element
+// the tables are summed in table order from 0, as in pairwise_forward_kernel: both kernels
+// give identical y, indices and margins. Every wait is bounded (an expired wait raises the
+// CTA's abort flag and g_pairwise_error); the producer lets its copies in flight land before
+// the CTA exits.
+__device__ int g_pairwise_error = 0;
+
+// 16 bytes of LUT values in shared memory as VEC f32.
+template <typename LutT, int VEC>
+__device__ __forceinline__ void smem_vec16(const uint8_t *p, float (&v)[VEC]) {
+  const uint4 q = *reinterpret_cast<const uint4 *>(p);
+  if constexpr (std::is_same<LutT, float>::value) {
+    v[0] = __uint_as_float(q.x);
+    v[1] = __uint_as_float(q.y);
+    v[2] = __uint_as_float(q.z);
+    v[3] = __uint_as_float(q.w);
+  } else {
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f;
+      if constexpr (std::is_same<LutT, __half>::value)
+        f = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+      else
+        f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+}
+
+constexpr int kStageRows = 8;
+constexpr int kStageConsumers = 512;                    // 16 warps, 16 bytes of a row slice per thread
+constexpr int kStageSliceBytes = kStageConsumers * 16;  // 8 KB of each selected LUT row per unit
+constexpr int kSlotRows = 8;                                  // row slices per ring slot
+constexpr int kSlotsPerTable = kStageRows / kSlotRows;
+constexpr int kSlotBytes = kSlotRows * kStageSliceBytes;
+constexpr int kSlotMax = 32;
+constexpr int kStageSmemLimit = 227 * 1024;  // dynamic shared memory of one CTA
+
+struct StageBarriers {
+  uint64_t full[kSlotMax];
+  uint64_t empty[kSlotMax];
+  int abort;
+};
+
+template <typename LutT, typename ThrT>
+__global__ void __launch_bounds__(kStageConsumers + 32, 1) pairwise_forward_staged_kernel(
+    const float *__restrict__ x, int64_t rows, int64_t in, const int64_t *__restrict__ anchors,
+    const ThrT *__restrict__ thr, int T, int C, const LutT *__restrict__ lut, int64_t out, float out_scale,
+    float *__restrict__ y, int64_t *__restrict__ idx_out, float *__restrict__ u_out, int64_t unit0, int64_t groups,
+    int slots) {
+  constexpr int VEC = 16 / sizeof(LutT);
+  constexpr int64_t kSliceCols = kStageSliceBytes / sizeof(LutT);
+  extern __shared__ __align__(128) uint8_t stage_smem[];
+  uint8_t *ring = stage_smem;  // [slots][kSlotRows][kStageSliceBytes]
+  auto *bars = reinterpret_cast<StageBarriers *>(stage_smem + size_t(slots) * kSlotBytes);
+  auto *widx = reinterpret_cast<uint16_t *>(bars + 1);  // [kStageRows][T]
+
+  const int64_t unit = unit0 + blockIdx.x;
+  const int64_t chunk = unit / groups;  // the units of one column chunk are consecutive
+  const int64_t row0 = (unit - chunk * groups) * kStageRows;
+  const int rows_here = static_cast<int>(min64(kStageRows, rows - row0));
+  const int64_t col0 = chunk * kSliceCols;
+  const int64_t slice_cols = min64(kSliceCols, out - col0);
+  const uint32_t slice_bytes = static_cast<uint32_t>(slice_cols * sizeof(LutT));
+  const int64_t table_size = int64_t(1) << C;
+  const bool write_routes = chunk == 0;
+
+  // Routes: as many latent rows as the ring holds at a time, a thread per table.
+  float *xs = reinterpret_cast<float *>(ring);
+  const int ring_rows = static_cast<int>(min64(rows_here, int64_t(slots) * kSlotBytes / (in * 4)));
+  for (int r0 = 0; r0 < rows_here; r0 += ring_rows) {
+    const int rn = min(ring_rows, rows_here - r0);
+    const float *xb = x + (row0 + r0) * in;
+    const int64_t n = rn * in;
+    if ((in & 3) == 0 && (reinterpret_cast<uintptr_t>(xb) & 15) == 0) {
+      // Four 16-byte loads in flight per thread per pass.
+      const float4 *src = reinterpret_cast<const float4 *>(xb);
+      float4 *dst = reinterpret_cast<float4 *>(xs);
+      const int64_t n4 = n / 4, step = blockDim.x;
+      for (int64_t i = threadIdx.x; i < n4; i += 4 * step) {
+        float4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (i + k * step < n4) v[k] = __ldg(src + i + k * step);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (i + k * step < n4) dst[i + k * step] = v[k];
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < n; i += blockDim.x) xs[i] = __ldg(xb + i);
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+      int a[kMaxComparisons], b[kMaxComparisons];
+      float th[kMaxComparisons];
+#pragma unroll
+      for (int c = 0; c < kMaxComparisons; ++c) {
+        if (c < C) {
+          const int64_t e = (int64_t(t) * C + c) * 2;
+          a[c] = static_cast<int>(clamp_feature(__ldg(anchors + e), in));
+          b[c] = static_cast<int>(clamp_feature(__ldg(anchors + e + 1), in));
+          th[c] = ldg_f32(thr + int64_t(t) * C + c);
+        }
+      }
+      for (int r = 0; r < rn; ++r) {
+        const float *xr = xs + int64_t(r) * in;
+        const int64_t nt = (row0 + r0 + r) * T + t;
+        int bits = 0;
+#pragma unroll
+        for (int c = 0; c < kMaxComparisons; ++c) {
+          if (c < C) {
+            const float u = __fsub_rn(__fsub_rn(xr[a[c]], xr[b[c]]), th[c]);
+            if (write_routes) u_out[nt * C + c] = u;
+            bits |= (u > 0.f ? 1 : 0) << c;
+          }
+        }
+        widx[(r0 + r) * T + t] = static_cast<uint16_t>(bits);
+        if (write_routes) idx_out[nt] = bits;
+      }
+    }
+    __syncthreads();
+  }
+  // The ring's generic reads above come before the bulk copies that write it.
+  sm100::fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < slots; ++s) {
+      sm100::mbar_init(&bars->full[s], 1);
+      sm100::mbar_init(&bars->empty[s], kStageConsumers / 32);
+    }
+    bars->abort = 0;
+    sm100::mbar_init_fence();
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp == kStageConsumers / 32) {
+    // Producer warp, one table per pass: lane j < kSlotsPerTable claims the table's slot j
+    // (waits for it to be free, posts its byte count), then lane r copies row r.
+    int64_t issued = 0;  // slots issued
+    bool ok = true;
+    for (int t = 0; t < T; ++t) {
+      const int64_t q = int64_t(t) * kSlotsPerTable + lane;
+      bool lane_ok = true;
+      if (lane < kSlotsPerTable) {
+        const int slot = static_cast<int>(q % slots);
+        if (q >= slots)
+          lane_ok = sm100::mbar_wait(&bars->empty[slot], static_cast<uint32_t>(((q / slots) - 1) & 1), &bars->abort,
+                                     &g_pairwise_error);
+        const int rows_in = max(0, min(kSlotRows, rows_here - lane * kSlotRows));
+        if (lane_ok) sm100::mbar_expect_tx(&bars->full[slot], slice_bytes * rows_in);
+      }
+      if (!__all_sync(0xffffffffu, lane_ok)) {
+        ok = false;
+        break;
+      }
+      if (lane < rows_here) {
+        const int slot = static_cast<int>((int64_t(t) * kSlotsPerTable + lane / kSlotRows) % slots);
+        sm100::bulk_load_1d(ring + size_t(slot) * kSlotBytes + (lane % kSlotRows) * kStageSliceBytes,
+                            lut + (int64_t(t) * table_size + widx[lane * T + t]) * out + col0, slice_bytes,
+                            &bars->full[slot]);
+      }
+      issued += kSlotsPerTable;
+      __syncwarp();
+    }
+    if (!ok && lane == 0) {
+      // Aborted: the copies already issued land before the CTA's shared memory is released.
+      for (int64_t u = issued > slots ? issued - slots : 0; u < issued; ++u)
+        sm100::mbar_drain(&bars->full[u % slots], static_cast<uint32_t>((u / slots) & 1));
+    }
+    return;
+  }
+
+  // Consumers: thread i owns columns [i * VEC, i * VEC + VEC) of the slice for every row.
+  const int64_t c = int64_t(threadIdx.x) * VEC;
+  float acc[kStageRows][VEC];
+#pragma unroll
+  for (int r = 0; r < kStageRows; ++r)
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[r][e] = 0.f;
+  int slot = 0;
+  uint32_t phase = 0;
+  bool ok = true;
+  for (int t = 0; t < T && ok; ++t) {
+#pragma unroll
+    for (int j = 0; j < kSlotsPerTable; ++j) {
+      if (ok) {
+        if (!sm100::mbar_wait(&bars->full[slot], phase, &bars->abort, &g_pairwise_error)) {
+          ok = false;
+        } else {
+          const uint8_t *src = ring + size_t(slot) * kSlotBytes + threadIdx.x * 16;
+#pragma unroll
+          for (int rr = 0; rr < kSlotRows; ++rr) {
+            const int r = j * kSlotRows + rr;
+            if (r < rows_here) {
+              float v[VEC];
+              smem_vec16<LutT, VEC>(src + rr * kStageSliceBytes, v);
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) acc[r][e] = __fadd_rn(acc[r][e], v[e]);
+            }
+          }
+          __syncwarp();
+          if (lane == 0) sm100::mbar_arrive(&bars->empty[slot]);
+          if (++slot == slots) {
+            slot = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  }
+  if (c >= slice_cols) return;
+#pragma unroll
+  for (int r = 0; r < kStageRows; ++r) {
+    if (r < rows_here) {
+      float *yrow = y + (row0 + r) * out + col0 + c;
+#pragma unroll
+      for (int e = 0; e < VEC; e += 4)
+        *reinterpret_cast<float4 *>(yrow + e) =
+            make_float4(__fmul_rn(acc[r][e], out_scale), __fmul_rn(acc[r][e + 1], out_scale),
+                        __fmul_rn(acc[r][e + 2], out_scale), __fmul_rn(acc[r][e + 3], out_scale));
+    }
+  }
+}
+
+// LUT bytes above which the forward runs staged in waves: a LUT within a quarter of L2 stays
+// resident there under any schedule, and pairwise_forward_kernel fills the GPU with smaller CTAs.
+constexpr int64_t kStagedLutBytes = int64_t(32) << 20;
+
+size_t staged_smem(int slots, int T) {
+  return size_t(slots) * kSlotBytes + sizeof(StageBarriers) + sizeof(uint16_t) * kStageRows * T;
+}
+
+// Ring slots that fit next to the unit's routes (0 when fewer than two tables' rows fit).
+int staged_slots(int T) {
+  for (int s = kSlotMax; s >= 2 * kSlotsPerTable; --s)
+    if (staged_smem(s, T) <= size_t(kStageSmemLimit)) return s;
+  return 0;
+}
+
+template <typename LutT, typename ThrT>
+int launch_forward_staged(const float *x, int64_t rows, int64_t in, const int64_t *anchors, const void *thr, int T,
+                          int C, const void *lut, int64_t out, float out_scale, float *y, int64_t *idx, float *u,
+                          cudaStream_t stream) {
+  int dev = 0, sms = 0;
+  TB_REQUIRE(cudaGetDevice(&dev) == cudaSuccess &&
+                 cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0,
+             TROPNN_B200_ERR_LAUNCH, "pairwise_forward: device query failed");
+  constexpr int64_t kSliceCols = kStageSliceBytes / sizeof(LutT);
+  const int slots = staged_slots(T);
+  const size_t smem = staged_smem(slots, T);
+  const int64_t groups = ceil_div(rows, int64_t(kStageRows));
+  const int64_t units = groups * ceil_div(out, kSliceCols);
+  auto kernel = pairwise_forward_staged_kernel<LutT, ThrT>;
+  TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "pairwise_forward_staged"));
+  for (int64_t unit0 = 0; unit0 < units; unit0 += sms) {
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(sms, units - unit0));
+    kernel<<<grid, kStageConsumers + 32, smem, stream>>>(x, rows, in, anchors, static_cast<const ThrT *>(thr), T, C,
+                                                         static_cast<const LutT *>(lut), out, out_scale, y, idx, u,
+                                                         unit0, groups, slots);
+    TB_CHECK(check_launch("pairwise_forward_staged"));
+  }
+  return TROPNN_B200_OK;
+}
+
 template <typename LutT, typename ThrT>
 int forward_by_width(const float *x, int64_t rows, int64_t in, const int64_t *anchors, const void *thr, int T, int C,
                      const void *lut, int64_t out, float out_scale, float *y, int64_t *idx, float *u,
@@ -149,6 +431,12 @@ int forward_by_width(const float *x, int64_t rows, int64_t in, const int64_t *an
   const bool vec_ok = (out % kVec == 0) && (reinterpret_cast<uintptr_t>(lut) % 16 == 0) &&
                       (reinterpret_cast<uintptr_t>(y) % 16 == 0);
   if (vec_ok) {
+    // LUTs far larger than L2 with wide rows: the staged kernel in waves.
+    const int64_t lut_bytes = int64_t(T) * (int64_t(1) << C) * out * int64_t(sizeof(LutT));
+    if (lut_bytes > kStagedLutBytes && out * int64_t(sizeof(LutT)) >= kStageSliceBytes / 2 && staged_slots(T) > 0 &&
+        in * 4 <= int64_t(staged_slots(T)) * kSlotBytes)
+      return launch_forward_staged<LutT, ThrT>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u,
+                                               stream);
     // Column tile of 512 outputs (f32) or 1024 (16-bit) when the rows alone fill the GPU,
     // narrower tiles otherwise.
     if (out > 32 * kVec * 2 || ceil_div(rows, kFwdRows) >= 4 * 148)
@@ -349,6 +637,253 @@ int launch_ste(bool use_min, const float *g, int64_t rows, int64_t out, float ou
   return check_launch("pairwise_ste_backward");
 }
 
+// Min-margin STE backward for LUTs larger than L2 (config 5): pairwise_ste_staged_kernel, staged
+// like pairwise_forward_staged_kernel. A unit is kSteRows rows (all `out` columns in one 8 KB
+// LUT row slice); units run in waves of one per SM, so that the rows of a wave gather the same
+// tables at about the same time and the LUT comes from DRAM about once per wave. Per table, the
+// producer warp copies the current bucket's and the min-margin neighbour's row slices of every
+// row (2 x kSteRows bulk copies, one per lane) into one slot of a three-table ring. Consumer
+// thread i keeps g[row, i*VEC .. i*VEC+VEC) * out_scale of the unit's rows in registers and
+// forms its partial of dot = g . (lut[nb] - lut[cur]) per row; a warp reduces its rows'
+// partials with a transposed butterfly, and every kSteBatch tables the 16 warps' sums are added
+// in warp order, times the surrogate slope at u*, into gu. grad_x is then gathered per input
+// feature through the inverse anchor map, as in pairwise_ste_kernel. Four rows per unit keep a
+// table's slot at 64 KB (three tables in flight, like the forward) and g in 32 registers.
+// Every wait is bounded; after an expired wait the consumers keep taking the same named
+// barriers (skipping the work), so none is left waiting.
+constexpr int kSteRows = 4;
+constexpr int kSteSlotBytes = kSteRows * 2 * kStageSliceBytes;  // [rows][cur, nb][slice]
+constexpr int kSteSlotMax = 8;
+constexpr int kSteBatch = 16;
+constexpr int kSteWarps = kStageConsumers / 32;
+
+struct SteBarriers {
+  uint64_t full[kSteSlotMax];
+  uint64_t empty[kSteSlotMax];
+  int abort;
+};
+
+size_t ste_staged_smem(int slots, int T) {
+  return size_t(slots) * kSteSlotBytes + sizeof(SteBarriers) + sizeof(float) * kSteBatch * kSteWarps * kSteRows +
+         sizeof(uint16_t) * kSteRows * T;
+}
+
+// Ring slots (one table each) that fit next to the routes and the batch sums, at least two.
+int ste_staged_slots(int T) {
+  for (int s = kSteSlotMax; s >= 2; --s)
+    if (ste_staged_smem(s, T) <= size_t(kStageSmemLimit)) return s;
+  return 0;
+}
+
+// Sum over the warp of p[r] for each of 4 rows; lane l ends with row ((l >> 4) & 1) * 2 +
+// ((l >> 3) & 1) (a fixed order: deterministic).
+__device__ __forceinline__ float warp_sum_rows4(const float (&p)[4], int lane) {
+  const bool hi16 = lane & 16, hi8 = lane & 8;
+  float q[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float send = hi16 ? p[k] : p[k + 2];
+    const float keep = hi16 ? p[k + 2] : p[k];
+    q[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+  float x = (hi8 ? q[1] : q[0]) + __shfl_xor_sync(0xffffffffu, hi8 ? q[0] : q[1], 8);
+  x += __shfl_xor_sync(0xffffffffu, x, 4);
+  x += __shfl_xor_sync(0xffffffffu, x, 2);
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  return x;
+}
+
+template <typename LutT>
+__global__ void __launch_bounds__(kStageConsumers + 32, 1) pairwise_ste_staged_kernel(
+    const float *__restrict__ g, int64_t rows, int64_t out, float out_scale, const int64_t *__restrict__ idx,
+    const float *__restrict__ u, int T, int C, int64_t in, const LutT *__restrict__ lut, int surrogate,
+    const int32_t *__restrict__ feat_start, const int32_t *__restrict__ feat_entries, float *__restrict__ grad_x,
+    float *__restrict__ gu_out, uint8_t *__restrict__ rstar_out, int64_t unit0, int slots) {
+  constexpr int VEC = 16 / sizeof(LutT);
+  extern __shared__ __align__(128) uint8_t ste_stage_smem[];
+  uint8_t *ring = ste_stage_smem;  // [slots][kSteRows][2][kStageSliceBytes]
+  auto *bars = reinterpret_cast<SteBarriers *>(ste_stage_smem + size_t(slots) * kSteSlotBytes);
+  auto *red = reinterpret_cast<float *>(bars + 1);                                 // [kSteBatch][kSteWarps][kSteRows]
+  auto *info = reinterpret_cast<uint16_t *>(red + kSteBatch * kSteWarps * kSteRows);  // cur | r* << 12
+
+  const int64_t row0 = (unit0 + blockIdx.x) * kSteRows;
+  const int rows_here = static_cast<int>(min64(kSteRows, rows - row0));
+  const uint32_t slice_bytes = static_cast<uint32_t>(out * sizeof(LutT));
+  const int64_t table_size = int64_t(1) << C;
+
+  // r* = argmin_c |u| (first on ties) and the current bucket of every (row, table).
+  for (int i = threadIdx.x; i < rows_here * T; i += blockDim.x) {
+    const int r = i / T;
+    const int t = i - r * T;
+    const int64_t nt = (row0 + r) * T + t;
+    const float *urow = u + nt * C;
+    int rmin = 0;
+    float best = fabsf(__ldg(urow));
+    for (int c = 1; c < C; ++c) {
+      const float v = fabsf(__ldg(urow + c));
+      if (v < best) {
+        best = v;
+        rmin = c;
+      }
+    }
+    info[i] = static_cast<uint16_t>(__ldg(idx + nt) | (rmin << 12));
+    rstar_out[nt] = static_cast<uint8_t>(rmin);
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < slots; ++s) {
+      sm100::mbar_init(&bars->full[s], 1);
+      sm100::mbar_init(&bars->empty[s], kSteWarps);
+    }
+    bars->abort = 0;
+    sm100::mbar_init_fence();
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp == kSteWarps) {
+    // Producer warp, one table per pass: lane 0 claims the table's slot, then lane l < 2 kSteRows
+    // copies row l % kSteRows's current (l < kSteRows) or neighbour row slice.
+    bool ok = true;
+    int t = 0;
+    for (; t < T; ++t) {
+      const int slot = t % slots;
+      bool lane_ok = true;
+      if (lane == 0) {
+        if (t >= slots)
+          lane_ok = sm100::mbar_wait(&bars->empty[slot], static_cast<uint32_t>(((t / slots) - 1) & 1), &bars->abort,
+                                     &g_pairwise_error);
+        if (lane_ok) sm100::mbar_expect_tx(&bars->full[slot], 2 * slice_bytes * rows_here);
+      }
+      if (!__all_sync(0xffffffffu, lane_ok)) {
+        ok = false;
+        break;
+      }
+      const int r = lane % kSteRows;
+      if (lane < 2 * kSteRows && r < rows_here) {
+        const int which = lane / kSteRows;  // 0: current bucket, 1: min-margin neighbour
+        const int v = info[r * T + t];
+        const int cur = v & 0xfff;
+        const int entry = which ? (cur ^ (1 << (v >> 12))) : cur;
+        sm100::bulk_load_1d(ring + size_t(slot) * kSteSlotBytes + (r * 2 + which) * kStageSliceBytes,
+                            lut + (int64_t(t) * table_size + entry) * out, slice_bytes, &bars->full[slot]);
+      }
+      __syncwarp();
+    }
+    if (!ok && lane == 0) {
+      for (int q = t > slots ? t - slots : 0; q < t; ++q)
+        sm100::mbar_drain(&bars->full[q % slots], static_cast<uint32_t>((q / slots) & 1));
+    }
+    return;
+  }
+
+  // Consumers.
+  const int64_t c = int64_t(threadIdx.x) * VEC;
+  const bool has_cols = c < out;
+  float gv[kSteRows][VEC];
+#pragma unroll
+  for (int r = 0; r < kSteRows; ++r) {
+    if (r < rows_here && has_cols) {
+      VecLoad<float, VEC>::load(g + (row0 + r) * out + c, gv[r]);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) gv[r][e] = __fmul_rn(gv[r][e], out_scale);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) gv[r][e] = 0.f;
+    }
+  }
+  const int my_row = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
+  bool ok = true;
+  for (int t = 0; t < T; ++t) {
+    const int slot = t % slots;
+    float part[kSteRows];
+#pragma unroll
+    for (int r = 0; r < kSteRows; ++r) part[r] = 0.f;
+    if (ok) {
+      ok = __all_sync(0xffffffffu, sm100::mbar_wait(&bars->full[slot], static_cast<uint32_t>((t / slots) & 1),
+                                                    &bars->abort, &g_pairwise_error));
+      if (ok) {
+        const uint8_t *src = ring + size_t(slot) * kSteSlotBytes + threadIdx.x * 16;
+#pragma unroll
+        for (int r = 0; r < kSteRows; ++r) {
+          // Columns past `out` and rows past the unit's were not copied: never read them.
+          if (has_cols && r < rows_here) {
+            float vc[VEC], vn[VEC];
+            smem_vec16<LutT, VEC>(src + (r * 2) * kStageSliceBytes, vc);
+            smem_vec16<LutT, VEC>(src + (r * 2 + 1) * kStageSliceBytes, vn);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) part[r] = fmaf(gv[r][e], __fsub_rn(vn[e], vc[e]), part[r]);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&bars->empty[slot]);
+      }
+    }
+    const int tb = t % kSteBatch;
+    const float sum = warp_sum_rows4(part, lane);
+    if ((lane & 7) == 0) red[(tb * kSteWarps + warp) * kSteRows + my_row] = sum;
+    if (tb == kSteBatch - 1 || t == T - 1) {
+      // The batch's dots: the warps' sums in warp order, times the surrogate slope at u*.
+      sm100::named_sync(1, kStageConsumers);
+      const int t0 = t - tb;
+      for (int k = threadIdx.x; k < (tb + 1) * kSteRows; k += kStageConsumers) {
+        const int b = k / kSteRows, r = k - b * kSteRows;
+        if (r < rows_here) {
+          float dot = 0.f;
+          for (int w = 0; w < kSteWarps; ++w) dot = __fadd_rn(dot, red[(b * kSteWarps + w) * kSteRows + r]);
+          const int64_t nt = (row0 + r) * T + t0 + b;
+          const float ustar = __ldg(u + nt * C + (info[r * T + t0 + b] >> 12));
+          gu_out[nt] = __fmul_rn(dot, surrogate_grad(ustar, surrogate));
+        }
+      }
+      sm100::named_sync(1, kStageConsumers);
+    }
+  }
+
+  // grad_x[n, i] = sum over the (table, comparison) entries that read feature i (sign by side)
+  // of gu where the comparison is the row's r*, in entry order.
+  for (int64_t k = threadIdx.x; k < int64_t(rows_here) * in; k += kStageConsumers) {
+    const int r = static_cast<int>(k / in);
+    const int64_t i = k - int64_t(r) * in;
+    const int64_t n = row0 + r;
+    const int lo = __ldg(feat_start + i);
+    const int hi = __ldg(feat_start + i + 1);
+    float acc = 0.f;
+    for (int j = lo; j < hi; ++j) {
+      const int e = __ldg(feat_entries + j);
+      const int tc = e >> 1;
+      const int t = tc / C;
+      const int cc = tc - t * C;
+      const float v = (info[r * T + t] >> 12) == cc ? gu_out[n * T + t] : 0.f;
+      acc = (e & 1) ? __fsub_rn(acc, v) : __fadd_rn(acc, v);
+    }
+    grad_x[n * in + i] = acc;
+  }
+}
+
+template <typename LutT>
+int launch_ste_staged(const float *g, int64_t rows, int64_t out, float out_scale, const int64_t *idx, const float *u,
+                      int T, int C, int64_t in, const void *lut, int surrogate, const int32_t *fs, const int32_t *fe,
+                      float *gx, float *gu, uint8_t *rs, cudaStream_t stream) {
+  int dev = 0, sms = 0;
+  TB_REQUIRE(cudaGetDevice(&dev) == cudaSuccess &&
+                 cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0,
+             TROPNN_B200_ERR_LAUNCH, "pairwise_ste_backward: device query failed");
+  const int slots = ste_staged_slots(T);
+  const size_t smem = ste_staged_smem(slots, T);
+  auto kernel = pairwise_ste_staged_kernel<LutT>;
+  TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "pairwise_ste_staged"));
+  const int64_t units = ceil_div(rows, int64_t(kSteRows));
+  for (int64_t unit0 = 0; unit0 < units; unit0 += sms) {
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(sms, units - unit0));
+    kernel<<<grid, kStageConsumers + 32, smem, stream>>>(g, rows, out, out_scale, idx, u, T, C, in,
+                                                         static_cast<const LutT *>(lut), surrogate, fs, fe, gx, gu,
+                                                         rs, unit0, slots);
+    TB_CHECK(check_launch("pairwise_ste_staged"));
+  }
+  return TROPNN_B200_OK;
+}
+
 template <typename LutT>
 int ste_by_width(bool use_min, const float *g, int64_t rows, int64_t out, float out_scale, const int64_t *idx,
                  const float *u, int T, int C, int64_t in, const void *lut, int surrogate, const int32_t *fs,
@@ -357,6 +892,13 @@ int ste_by_width(bool use_min, const float *g, int64_t rows, int64_t out, float 
   // 16-byte LUT loads need kVec | out; g is f32 so with kVec = 8 two float4 loads.
   const bool vec_ok = (out % kVec == 0) && (reinterpret_cast<uintptr_t>(lut) % 16 == 0) &&
                       (reinterpret_cast<uintptr_t>(g) % 16 == 0);
+  // Min-margin STE over a LUT far larger than L2 whose rows fit one 8 KB slice: staged in waves.
+  const int64_t lut_bytes = int64_t(T) * (int64_t(1) << C) * out * int64_t(sizeof(LutT));
+  const int64_t row_bytes = out * int64_t(sizeof(LutT));
+  if (use_min && vec_ok && lut_bytes > kStagedLutBytes && row_bytes <= kStageSliceBytes &&
+      row_bytes >= kStageSliceBytes / 2 && ste_staged_slots(T) > 0 && C <= 12)
+    return launch_ste_staged<LutT>(g, rows, out, out_scale, idx, u, T, C, in, lut, surrogate, fs, fe, gx, gu, rs,
+                                   stream);
   if (vec_ok)
     return launch_ste<LutT, kVec>(use_min, g, rows, out, out_scale, idx, u, T, C, in, lut, surrogate, fs, fe, gx, gu,
                                   rs, stream);
@@ -537,6 +1079,19 @@ int pairwise_forward_impl(const float *latent, int64_t items, int64_t in, const 
       return forward_by_thr<__nv_bfloat16>(thr_dtype, latent, items, in, anchors, thr, T, C, lut, out, out_scale, y,
                                            idx, u, stream);
   }
+}
+
+int read_pairwise_error(int *value) {
+  int v = 0;
+  cudaError_t err = cudaMemcpyFromSymbol(&v, g_pairwise_error, sizeof(int));
+  if (err != cudaSuccess)
+    return set_error(TROPNN_B200_ERR_LAUNCH, "reading the device error word: %s", cudaGetErrorString(err));
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_pairwise_error, &zero, sizeof(int));
+  }
+  *value = v;
+  return TROPNN_B200_OK;
 }
 
 int pairwise_anchor_index_impl(const int64_t *anchors, int64_t tables, int64_t comparisons, int64_t in,

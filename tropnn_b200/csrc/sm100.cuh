@@ -107,6 +107,15 @@ __device__ inline void mbar_drain(uint64_t *bar, uint32_t parity) {
   }
 }
 
+// 1-D bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global
+// memory into this CTA's shared memory, completion counted on `bar` (no cluster delivery).
+__device__ __forceinline__ void bulk_load_1d(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
 // 2-D tiled TMA load into this CTA's shared memory, completion counted on `bar`.
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
   asm volatile(

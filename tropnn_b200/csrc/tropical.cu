@@ -30,6 +30,7 @@ int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W
                           cudaStream_t stream);
 size_t score_sm100_workspace(int64_t H, int64_t K, int pt);
 int read_score_error(int *value);
+int read_pairwise_error(int *value);
 bool score_tf32_supported(int64_t D, int64_t K, int pt, int bias_dtype, const void *z, const void *W,
                           const void *bias);
 size_t score_tf32_workspace(int64_t items, int64_t D, int64_t H, int64_t K);
@@ -771,7 +772,7 @@ int tropnn_b200_transpose_to_half(const void *x, int x_dtype, int64_t rows, int6
 
 int tropnn_b200_device_error(int *value) {
   TB_CHECK(tropnn_b200::check_current_device());
-  int score = 0, hidden = 0, gemm = 0, peer = 0, pgrad = 0, lgrad = 0, lutg = 0, proj = 0, gtf32 = 0;
+  int score = 0, hidden = 0, gemm = 0, peer = 0, pgrad = 0, lgrad = 0, lutg = 0, proj = 0, gtf32 = 0, pair = 0;
   TB_CHECK(tropnn_b200::read_score_error(&score));
   TB_CHECK(tropnn_b200::read_hidden_error(&hidden));
   TB_CHECK(tropnn_b200::read_gemm_error(&gemm));
@@ -781,7 +782,8 @@ int tropnn_b200_device_error(int *value) {
   TB_CHECK(tropnn_b200::read_lut_grad_error(&lutg));
   TB_CHECK(tropnn_b200::read_proj_error(&proj));
   TB_CHECK(tropnn_b200::read_gemm_tf32_error(&gtf32));
-  *value = score | hidden | gemm | peer | pgrad | lgrad | lutg | proj | gtf32;
+  TB_CHECK(tropnn_b200::read_pairwise_error(&pair));
+  *value = score | hidden | gemm | peer | pgrad | lgrad | lutg | proj | gtf32 | pair;
   return tropnn_b200::clear_error();
 }
 
