@@ -680,10 +680,9 @@ def run_b200(args: argparse.Namespace, w: Workload) -> dict | None:
 def _run_b200_body(
     args: argparse.Namespace, w: Workload, w_rank: Workload, rank: int, world: int, device: torch.device, layer, peer
 ) -> dict | None:
-    from tropnn_b200.distributed import fused_lut_peer
-
+    from tropnn_b200 import _native as nat
     from tropnn_b200 import trace
-    from tropnn_b200.distributed import allreduce_gradients
+    from tropnn_b200.distributed import allreduce_gradients, fused_lut_peer
 
     x_host, g_host = _make_inputs(w_rank, rank, device)
     x = x_host.to(device).requires_grad_(_input_grad(w))
@@ -725,13 +724,18 @@ def _run_b200_body(
 
     @contextlib.contextmanager
     def tracing():
+        lib = nat.load()
+        before = lib.tropnn_b200_kernel_launches()
         with trace.launch_trace() as t:
             holder["trace"] = t
             yield
+        # The library's own count of the kernels the captured step launches (an entry point
+        # can launch several: split-contraction reductions, the staged kernels' waves).
+        holder["kernels"] = lib.tropnn_b200_kernel_launches() - before
 
     traced = _capture(lambda: _step(layer, x, g, w), device, during_capture=tracing)
     tr = holder["trace"]
-    launches_per_step = len(tr.records)
+    launches_per_step = holder["kernels"]
     for i in range(args.steps):
         flush.fill_(float(i))
         traced.replay()

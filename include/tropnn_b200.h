@@ -70,6 +70,10 @@ TROPNN_B200_API const char *tropnn_b200_last_error(void);
 TROPNN_B200_API int tropnn_b200_abi_version(void);
 /* TROPNN_B200_OK when `device` is an sm_100 GPU, else TROPNN_B200_ERR_DEVICE. */
 TROPNN_B200_API int tropnn_b200_check_device(int device);
+/* Kernels this library has launched in this process so far (all devices and threads); a
+ * launch recorded into a CUDA graph counts once, when it is recorded. No reference
+ * counterpart: instrumentation. */
+TROPNN_B200_API unsigned long long tropnn_b200_kernel_launches(void);
 
 /* ------------------------------------------------------- shared machinery */
 

@@ -17,7 +17,7 @@ from pathlib import Path
 import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtropnn_b200.so"
-ABI_VERSION = 16
+ABI_VERSION = 17
 
 # tropnn_b200_dtype
 F32, F16, BF16, U8, I16, I64 = 0, 1, 2, 3, 4, 5
@@ -46,6 +46,7 @@ _sz = ctypes.c_size_t
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tropnn_b200_last_error": (ctypes.c_char_p, []),
     "tropnn_b200_abi_version": (_i32, []),
+    "tropnn_b200_kernel_launches": (ctypes.c_ulonglong, []),
     "tropnn_b200_check_device": (_i32, [_i32]),
     "tropnn_b200_bucket_sort": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "tropnn_b200_segment_rowsum": (

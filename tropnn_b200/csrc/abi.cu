@@ -1,4 +1,5 @@
 // Status plumbing and device checks shared by every entry point.
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -11,6 +12,9 @@ thread_local std::string g_last_error;
 // Compute-capability major per device ordinal, 0 = not queried yet. A benign race
 // at worst queries twice.
 int g_cc_major[64] = {0};
+// Kernels launched by this library in this process (every launch is followed by one
+// check_launch).
+std::atomic<unsigned long long> g_kernel_launches{0};
 }  // namespace
 
 int set_error(int status, const char *fmt, ...) {
@@ -63,6 +67,7 @@ int check_launch(const char *what) {
   if (err != cudaSuccess) {
     return set_error(TROPNN_B200_ERR_LAUNCH, "%s: CUDA error: %s", what, cudaGetErrorString(err));
   }
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
   return TROPNN_B200_OK;
 }
 
@@ -106,7 +111,11 @@ extern "C" {
 
 const char *tropnn_b200_last_error(void) { return tropnn_b200::g_last_error.c_str(); }
 
-int tropnn_b200_abi_version(void) { return 16; }
+int tropnn_b200_abi_version(void) { return 17; }
+
+unsigned long long tropnn_b200_kernel_launches(void) {
+  return tropnn_b200::g_kernel_launches.load(std::memory_order_relaxed);
+}
 
 int tropnn_b200_check_device(int device) {
   int major = 0;
