@@ -320,18 +320,21 @@ def test_forward_sum_is_table_ordered_f32(rows, in_f, out_f, tables, comparisons
 
 
 @pytest.mark.parametrize(
-    ("in_f", "out_f", "tables", "comparisons", "n", "dtype", "surrogate"),
+    ("in_f", "out_f", "tables", "comparisons", "n", "dtype", "surrogate", "use_min"),
     [
-        (512, 2048, 32, 8, 203, torch.float32, "fast_sigmoid_odd"),  # 64 MiB f32 LUT, ragged last unit
-        (256, 4096, 40, 8, 77, torch.float16, "izhikevich"),  # 80 MiB f16 LUT, full 8 KB rows
-        (128, 3072, 48, 8, 9, torch.bfloat16, "fast_sigmoid_odd"),  # 6 KB rows, one partial unit
+        (512, 2048, 32, 8, 203, torch.float32, "fast_sigmoid_odd", True),  # 64 MiB f32 LUT, ragged last unit
+        (256, 4096, 40, 8, 77, torch.float16, "izhikevich", True),  # 80 MiB f16 LUT, full 8 KB rows
+        (128, 3072, 48, 8, 9, torch.bfloat16, "fast_sigmoid_odd", True),  # 6 KB rows, one partial unit
+        (64, 2048, 2, 12, 5, torch.float32, "fast_sigmoid_odd", True),  # 12 comparisons (4096-entry tables)
+        (128, 2048, 40, 8, 37, torch.float32, "izhikevich", False),  # full STE: the per-row STE kernel
     ],
 )
-def test_staged_paths_match_oracle(in_f, out_f, tables, comparisons, n, dtype, surrogate) -> None:
+def test_staged_paths_match_oracle(in_f, out_f, tables, comparisons, n, dtype, surrogate, use_min) -> None:
     """LUTs larger than 32 MiB take the staged forward and the staged min-margin STE backward
     (the kernels of config 5): forward bit-exact routes and margins, output and every gradient
     against the oracle (1e-5 for f32 parameters, 2e-2 for half precision)."""
-    layer = tropnn_b200.PairwiseLinear(in_f, out_f, tables=tables, comparisons=comparisons, seed=8, surrogate=surrogate)
+    layer = tropnn_b200.PairwiseLinear(in_f, out_f, tables=tables, comparisons=comparisons, seed=8, surrogate=surrogate,
+                                       use_min_margin_ste=use_min)
     if dtype != torch.float32:
         layer = layer.to(dtype)
     with torch.no_grad():
