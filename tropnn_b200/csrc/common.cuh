@@ -96,6 +96,30 @@ inline const char *dtype_name(int dt) {
 }
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Slice count for a contraction of `kblocks` k blocks per output tile over `tiles` tiles on
+// `sms` SMs running one unit (tile, slice) at a time each: the s in [1, max_splits], with at
+// least min_kb k blocks a slice, that minimises the critical path, ceil(tiles * s / sms) rounds
+// of ceil(kblocks / s) k blocks at kb_us each, plus s slice partials of slice_us each for the
+// ordered reduction that follows a split (none for s = 1). Ties go to fewer slices. A count
+// just above a multiple of the SMs costs a whole extra round, which the old rule (enough
+// slices to reach the SM count) often paid.
+inline int balanced_splits(int64_t tiles, int64_t kblocks, int64_t sms, int max_splits, int min_kb, double kb_us,
+                           double slice_us) {
+  int best = 1;
+  double best_cost = double(ceil_div(tiles, sms)) * double(kblocks) * kb_us;
+  for (int s = 2; s <= max_splits; ++s) {
+    const int64_t kbps = ceil_div(kblocks, s);
+    if (kbps < min_kb) break;
+    if (ceil_div(kblocks, kbps) != s) continue;  // forms fewer slices: a smaller s covers it
+    const double cost = double(ceil_div(tiles * s, sms)) * double(kbps) * kb_us + double(s) * slice_us;
+    if (cost < best_cost) {
+      best = s;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 
 // 256-byte aligned carving of a caller-provided workspace.

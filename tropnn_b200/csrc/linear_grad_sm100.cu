@@ -446,15 +446,18 @@ bool linear_grad_supported(int64_t rows, int64_t out_features, int64_t in_featur
 
 // DGRAD's contraction (out_features) in slices when the row blocks leave most SMs idle.
 constexpr int kDgradTargetCtas = 148;
-int dgrad_splits(int64_t rows, int64_t out_features) {
+int dgrad_splits(int64_t rows, int64_t out_features, int64_t in_features) {
+  // CTA (row block, slice): slices of at least 8 k blocks (~0.53 us each: big and small g
+  // against the 32-deep f32 weight slab), filling the SMs in whole rounds; each slice adds a
+  // [rows, in] f32 partial to the ordered reduction (~5 TB/s).
   const int64_t row_blocks = ceil_div(rows, int64_t(kBM));
   const int64_t kblocks = ceil_div(out_features, int64_t(stage_k(kDgrad)));
-  if (row_blocks * 4 >= int64_t(kDgradTargetCtas) * 3) return 1;
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({16, ceil_div(kDgradTargetCtas, row_blocks), kblocks / 8})));
+  return balanced_splits(row_blocks, kblocks, kDgradTargetCtas, 16, 8, 0.53,
+                         double(rows) * double(in_features) * 4.0 / 5e6);
 }
 
 size_t dgrad_workspace(int64_t rows, int64_t out_features, int64_t in_features) {
-  const int s = dgrad_splits(rows, out_features);
+  const int s = dgrad_splits(rows, out_features, in_features);
   if (s == 1) return 0;
   return WorkspaceCarver::align(size_t(ceil_div(rows, int64_t(kBM))) * s * size_t(in_features) * kBM * sizeof(float));
 }
@@ -479,7 +482,7 @@ int linear_dgrad_impl(const float *g, int64_t rows, int64_t out_features, const 
   const int kblocks = static_cast<int>(ceil_div(out_features, int64_t(stage_k(kDgrad))));
   const int64_t row_blocks = ceil_div(rows, int64_t(kBM));
   // Few row blocks: split the contraction when the caller gave room for the slice partials.
-  int splits = dgrad_splits(rows, out_features);
+  int splits = dgrad_splits(rows, out_features, in_features);
   float4 *partial = nullptr;
   if (splits > 1) {
     WorkspaceCarver wc(ws, ws_bytes);

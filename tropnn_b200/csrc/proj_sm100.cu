@@ -625,12 +625,11 @@ ProjGeom proj_geometry(int64_t rows, int64_t in, int64_t D) {
   g.D = static_cast<int>(D);
   g.kblocks = static_cast<int>(ceil_div(in, kBK));
   const int64_t row_blocks = ceil_div(rows, int64_t(kBM));
-  int splits = 1;
-  if (row_blocks * 4 < int64_t(kTargetUnits) * 3) {
-    // Fewer row blocks than ~3/4 of the SMs: cut the contraction (>= 4 k blocks a slice).
-    splits = static_cast<int>(std::min<int64_t>(kMaxSplits, ceil_div(kTargetUnits, row_blocks)));
-    splits = std::max(1, std::min(splits, g.kblocks / kMinKBlocksPerSplit));
-  }
+  // Few row blocks: cut the contraction so that the units fill the SMs in whole rounds. A k
+  // block streams 32 KB of x per CTA (~0.75 us at the HBM rate per SM); each slice adds a
+  // [rows, D] f32 partial to the ordered reduction (~5 TB/s).
+  const int splits = balanced_splits(row_blocks, g.kblocks, kTargetUnits, kMaxSplits, kMinKBlocksPerSplit, 0.75,
+                                     double(rows) * double(D) * 4.0 / 5e6);
   g.kb_per_split = static_cast<int>(ceil_div(g.kblocks, splits));
   g.splits = static_cast<int>(ceil_div(g.kblocks, g.kb_per_split));
   g.stages = proj_stages(D);
