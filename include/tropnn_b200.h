@@ -545,6 +545,24 @@ TROPNN_B200_API int tropnn_b200_trop_backward_rows(const float *grad_hidden, int
                                    float *grad_latent, float *coef_w, float *coef_r, float *gm,
                                    void *stream);
 
+/*
+ * Parameter gradients of an f32 TropLinear from its rows, without sorting (the batch sums of
+ * tropical_exact.py:204-237):
+ *   grad_code[h,k,:]   = sum_n coef_w[n,h] [w=k] g[n,:] + coef_r[n,h] [r=k] g[n,:]
+ *   grad_router[h,k,:] = sum_n gm[n,h] ([w=k] - [r=k]) z[n,:],  grad_bias[h,k] likewise
+ * with coef_w / coef_r / gm from tropnn_b200_trop_backward_rows (coef_w NULL: the constant
+ * coef_const; coef_r / runner NULL: no runner-up term, as in eval). F32 parameters, U8
+ * routes, 2-32 cells; any output NULL is skipped (the router weight and bias go together).
+ * Deterministic (eight row groups summed in group order). tropnn_b200_trop_backward takes this
+ * path itself for such layers. No reference counterpart beyond the batch sums it computes.
+ */
+TROPNN_B200_API int tropnn_b200_trop_param_grad_rows(const float *grad_hidden, const float *latent, int64_t items,
+                                     int64_t code_dim, int param_dtype, int64_t heads, int64_t cells,
+                                     const void *winner, const void *runner, int index_dtype,
+                                     const float *coef_w, const float *coef_r, float coef_const,
+                                     const float *gm, void *grad_code, void *grad_router_weight,
+                                     void *grad_router_bias, void *stream);
+
 /* Bytes of scratch tropnn_b200_trop_backward needs. */
 TROPNN_B200_API size_t tropnn_b200_trop_backward_workspace_size(int64_t items, int64_t heads, int64_t cells, int training);
 

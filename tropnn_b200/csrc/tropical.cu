@@ -653,6 +653,171 @@ size_t trop_backward_workspace(int64_t items, int64_t H, int64_t K, int training
   return trop_backward_layout(nullptr, 0, items, H, K, training, &L);
 }
 
+namespace {
+
+// Parameter gradients of an f32 TropLinear straight from the rows (no bucket sort): CTA =
+// (head h, 32-column chunk), 8 warps = 8 row groups of 32 columns; group q takes rows q, q+8,
+// ... in order and accumulates in its own shared-memory copy (a warp's lanes update one cell
+// row: no bank conflicts)
+//   grad_code[h, k, c]   += coef_w[n, h] [w = k] g[n, c] + coef_r[n, h] [r = k] g[n, c]
+//   grad_router[h, k, c] += gm[n, h] ([w = k] - [r = k]) z[n, c]
+//   grad_bias[h, k]      += gm[n, h] ([w = k] - [r = k])
+// (tropical_exact.py:204-237 summed over the batch); the eight copies are then added in group
+// order (deterministic). Rows go in chunks of kPgrChunk: the chunk's routes, coefficients and
+// g / z column slices are first staged in shared memory with every load in flight at once,
+// so the accumulation loop reads shared memory only.
+constexpr int kPgrGroups = 8;
+constexpr int kPgrCols = 32;
+constexpr int kPgrMaxCells = 32;
+constexpr int kPgrChunk = 128;
+
+__host__ __device__ inline int pgr_acc_floats(int K, bool code, bool router) {
+  return (code ? kPgrGroups * K * kPgrCols : 0) + (router ? kPgrGroups * K * (kPgrCols + 1) : 0);
+}
+
+__global__ void __launch_bounds__(kPgrGroups * kPgrCols) trop_param_grad_rows_kernel(
+    const float *__restrict__ g, const float *__restrict__ z, int64_t items, int D, int H, int K,
+    const uint8_t *__restrict__ win, const uint8_t *__restrict__ run, const float *__restrict__ coef_w,
+    const float *__restrict__ coef_r, float coef_const, const float *__restrict__ gm, float *__restrict__ gc,
+    float *__restrict__ gW, float *__restrict__ gb) {
+  extern __shared__ float pgr_smem[];
+  const int h = blockIdx.x;
+  const int chunk = blockIdx.y;
+  const int q = threadIdx.x >> 5;
+  const int cl = threadIdx.x & 31;
+  const int col0 = chunk * kPgrCols;
+  const bool want_code = gc != nullptr, want_router = gW != nullptr;
+  const bool has_run = run != nullptr, has_cr = has_run && coef_r != nullptr;
+  float *accC = pgr_smem;                                              // [groups][K][32]
+  float *accW = accC + (want_code ? kPgrGroups * K * kPgrCols : 0);    // [groups][K][32]
+  float *accB = accW + (want_router ? kPgrGroups * K * kPgrCols : 0);  // [groups][K]
+  const int total = pgr_acc_floats(K, want_code, want_router);
+  float *s_cw = pgr_smem + total;  // staged per row of the chunk
+  float *s_cr = s_cw + kPgrChunk;
+  float *s_gm = s_cr + kPgrChunk;
+  int *s_route = reinterpret_cast<int *>(s_gm + kPgrChunk);  // w | r << 8 (-1: skip the row)
+  float *s_g = reinterpret_cast<float *>(s_route + kPgrChunk);  // [chunk rows][32]
+  float *s_z = s_g + kPgrChunk * kPgrCols;                       // [chunk rows][32]
+  for (int i = threadIdx.x; i < total; i += blockDim.x) pgr_smem[i] = 0.f;
+  float *myC = accC + q * K * kPgrCols + cl;
+  float *myW = accW + q * K * kPgrCols + cl;
+  float *myB = accB + q * K;
+  const bool bias_lane = want_router && cl == 0 && chunk == 0;
+  for (int64_t n0 = 0; n0 < items; n0 += kPgrChunk) {
+    const int nrows = static_cast<int>(min64(kPgrChunk, items - n0));
+    __syncthreads();  // the previous chunk is done with the staging arrays (and the zeroing above)
+    for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
+      const int64_t nh = (n0 + i) * H + h;
+      const int w = __ldg(win + nh);
+      const int r = has_run ? __ldg(run + nh) : 0;
+      // Not a route of this layer: nothing to add for the row.
+      s_route[i] = (w < K && r < K) ? (w | (r << 8)) : -1;
+      s_cw[i] = coef_w != nullptr ? __ldg(coef_w + nh) : coef_const;
+      s_cr[i] = has_cr ? __ldg(coef_r + nh) : 0.f;
+      s_gm[i] = gm != nullptr ? __ldg(gm + nh) : 0.f;
+    }
+    // The chunk's column slices: consecutive threads read consecutive columns of a row, eight
+    // loads of each slice in flight per thread before the stores.
+    constexpr int kU = 8;
+    const int n_el = nrows * kPgrCols;
+    for (int base = threadIdx.x; base < n_el; base += kU * kPgrGroups * kPgrCols) {
+      float vg[kU], vz[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int i = base + u * kPgrGroups * kPgrCols;
+        const int64_t n = n0 + (i >> 5);
+        const int c = col0 + (i & 31);
+        const bool live = i < n_el && c < D;
+        vg[u] = (want_code && live) ? __ldg(g + n * D + c) : 0.f;
+        vz[u] = (want_router && live) ? __ldg(z + n * D + c) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int i = base + u * kPgrGroups * kPgrCols;
+        if (i < n_el) {
+          if (want_code) s_g[i] = vg[u];
+          if (want_router) s_z[i] = vz[u];
+        }
+      }
+    }
+    __syncthreads();
+    for (int j = q; j < nrows; j += kPgrGroups) {
+      const int route = s_route[j];
+      if (route < 0) continue;
+      const int w = route & 0xff, r = route >> 8;
+      if (want_code) {
+        const float gv = s_g[j * kPgrCols + cl];
+        myC[w * kPgrCols] = fmaf(s_cw[j], gv, myC[w * kPgrCols]);
+        if (has_cr) myC[r * kPgrCols] = fmaf(s_cr[j], gv, myC[r * kPgrCols]);
+      }
+      if (want_router) {
+        const float zv = s_z[j * kPgrCols + cl];
+        const float m = s_gm[j];
+        myW[w * kPgrCols] = fmaf(m, zv, myW[w * kPgrCols]);
+        myW[r * kPgrCols] = fmaf(-m, zv, myW[r * kPgrCols]);
+        if (bias_lane) {
+          myB[w] = __fadd_rn(myB[w], m);
+          myB[r] = __fsub_rn(myB[r], m);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < K * kPgrCols; i += blockDim.x) {
+    const int k = i / kPgrCols, c = i - k * kPgrCols;
+    const int oc = col0 + c;
+    if (oc >= D) continue;
+    const int64_t o = (int64_t(h) * K + k) * D + oc;
+    if (want_code) {
+      float s = accC[k * kPgrCols + c];
+      for (int p = 1; p < kPgrGroups; ++p) s = __fadd_rn(s, accC[(p * K + k) * kPgrCols + c]);
+      gc[o] = s;
+    }
+    if (want_router) {
+      float s = accW[k * kPgrCols + c];
+      for (int p = 1; p < kPgrGroups; ++p) s = __fadd_rn(s, accW[(p * K + k) * kPgrCols + c]);
+      gW[o] = s;
+    }
+  }
+  if (want_router && chunk == 0 && threadIdx.x < K) {
+    float s = accB[threadIdx.x];
+    for (int p = 1; p < kPgrGroups; ++p) s = __fadd_rn(s, accB[p * K + threadIdx.x]);
+    gb[int64_t(h) * K + threadIdx.x] = s;
+  }
+}
+
+}  // namespace
+
+bool trop_param_grad_rows_supported(int pt, int it, int64_t K, int64_t H, int64_t D) {
+  return pt == TROPNN_B200_F32 && it == TROPNN_B200_U8 && K >= 2 && K <= kPgrMaxCells && H >= 1 && H < 65536 * 1024 &&
+         D >= 1 && D <= (1 << 20);
+}
+
+int trop_param_grad_rows_impl(const float *g, const float *z, int64_t items, int64_t D, int64_t H, int64_t K,
+                              const void *win, const void *run, const float *coef_w, const float *coef_r,
+                              float coef_const, const float *gm, float *gc, float *gW, float *gb,
+                              cudaStream_t stream) {
+  TB_REQUIRE(trop_param_grad_rows_supported(TROPNN_B200_F32, TROPNN_B200_U8, K, H, D), TROPNN_B200_ERR_INVALID,
+             "trop_param_grad_rows: unsupported shape heads=%lld cells=%lld code_dim=%lld", (long long)H, (long long)K,
+             (long long)D);
+  TB_REQUIRE((gW == nullptr) == (gb == nullptr), TROPNN_B200_ERR_INVALID,
+             "trop_param_grad_rows: grad_router_weight and grad_router_bias go together");
+  TB_REQUIRE(win != nullptr && (gc == nullptr || g != nullptr) &&
+                 (gW == nullptr || (z != nullptr && run != nullptr && gm != nullptr)) &&
+                 (coef_r == nullptr || run != nullptr),
+             TROPNN_B200_ERR_INVALID, "trop_param_grad_rows: null pointer");
+  if (gc == nullptr && gW == nullptr) return TROPNN_B200_OK;
+  const size_t smem = sizeof(float) * (pgr_acc_floats(static_cast<int>(K), gc != nullptr, gW != nullptr) +
+                                       4 * kPgrChunk + 2 * kPgrChunk * kPgrCols);
+  TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(trop_param_grad_rows_kernel), smem,
+                               "trop_param_grad_rows"));
+  const dim3 grid(static_cast<unsigned>(H), static_cast<unsigned>(ceil_div(D, int64_t(kPgrCols))));
+  trop_param_grad_rows_kernel<<<grid, kPgrGroups * kPgrCols, smem, stream>>>(
+      g, z, items, static_cast<int>(D), static_cast<int>(H), static_cast<int>(K), static_cast<const uint8_t *>(win),
+      static_cast<const uint8_t *>(run), coef_w, coef_r, coef_const, gm, gc, gW, gb);
+  return check_launch("trop_param_grad_rows");
+}
+
 int trop_backward_impl(const float *g, const float *z, int64_t items, int64_t D, const void *W, const void *code,
                        int pt, int64_t H, int64_t K, const void *win, const void *run, int it, const float *m,
                        float code_scale, int training, float *gz, void *gW, void *gb, void *gc, void *ws,
@@ -666,6 +831,14 @@ int trop_backward_impl(const float *g, const float *z, int64_t items, int64_t D,
   TB_CHECK(trop_backward_rows_impl(g, items, D, W, code, pt, H, K, win, run, it, m, code_scale, training, gz,
                                    L.coef_w, L.coef_r, L.gm, stream));
   if (items == 0) return TROPNN_B200_OK;
+  if (trop_param_grad_rows_supported(pt, it, K, H, D)) {
+    TB_REQUIRE(!(training && (gW != nullptr || gb != nullptr)) || (gW != nullptr && gb != nullptr && z != nullptr),
+               TROPNN_B200_ERR_INVALID, "trop_backward: grad_router_weight, grad_router_bias and latent go together");
+    return trop_param_grad_rows_impl(g, z, items, D, H, K, win, training ? run : nullptr, L.coef_w,
+                                     training ? L.coef_r : nullptr, 1.f, L.gm, static_cast<float *>(gc),
+                                     training ? static_cast<float *>(gW) : nullptr,
+                                     training ? static_cast<float *>(gb) : nullptr, stream);
+  }
   TB_CHECK(bucket_sort_impl(win, it, items, H, H, K, L.perm_w, L.seg_w, stream));
   if (training) TB_CHECK(bucket_sort_impl(run, it, items, H, H, K, L.perm_r, L.seg_r, stream));
   if (gc != nullptr) {
@@ -796,6 +969,23 @@ int tropnn_b200_trop_backward_rows(const float *grad_hidden, int64_t items, int6
   TB_CHECK(tropnn_b200::trop_backward_rows_impl(grad_hidden, items, code_dim, router_weight, code, param_dtype, heads,
                                                 cells, winner, runner, index_dtype, margins, code_scale, training,
                                                 grad_latent, coef_w, coef_r, gm, tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+int tropnn_b200_trop_param_grad_rows(const float *grad_hidden, const float *latent, int64_t items, int64_t code_dim,
+                                     int param_dtype, int64_t heads, int64_t cells, const void *winner,
+                                     const void *runner, int index_dtype, const float *coef_w, const float *coef_r,
+                                     float coef_const, const float *gm, void *grad_code, void *grad_router_weight,
+                                     void *grad_router_bias, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::validate_trop(items, code_dim, heads, cells));
+  TB_REQUIRE(tropnn_b200::trop_param_grad_rows_supported(param_dtype, index_dtype, cells, heads, code_dim),
+             TROPNN_B200_ERR_INVALID, "trop_param_grad_rows: needs F32 parameters, U8 routes and 2-32 cells");
+  if (items == 0) return tropnn_b200::clear_error();
+  TB_CHECK(tropnn_b200::trop_param_grad_rows_impl(
+      grad_hidden, latent, items, code_dim, heads, cells, winner, runner, coef_w, coef_r, coef_const, gm,
+      static_cast<float *>(grad_code), static_cast<float *>(grad_router_weight), static_cast<float *>(grad_router_bias),
+      tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 

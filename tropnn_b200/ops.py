@@ -436,6 +436,11 @@ def _hidden_workspace(lib: Any, items: int, code_dim: int, heads: int, cells: in
     return torch.empty(nbytes, device=dev, dtype=torch.uint8) if nbytes else None
 
 
+def _param_grad_rows_eligible(param_dtype: torch.dtype, index_dtype: torch.dtype, cells: int) -> bool:
+    """Layers whose code / router gradients tropnn_b200_trop_param_grad_rows sums directly."""
+    return param_dtype == torch.float32 and index_dtype == torch.uint8 and 2 <= cells <= 32
+
+
 def _trop_backward_tensor_cores(ctx, g, z, weight, code, winner, runner, margins, lib, stream):
     """Min-face backward as four tcgen05 GEMMs (layers/tropical_exact.py:204-237):
     gm from <g, c_r - c_w> (split-f32 g against the code table, route-picking epilogue),
@@ -679,7 +684,20 @@ class _TropRouteB200Function(torch.autograd.Function):
         want_code = ctx.needs_input_grad[3]
         want_router = training and (ctx.needs_input_grad[1] or ctx.needs_input_grad[2])
         grad_w = grad_b = grad_c = None
-        if (want_code or want_router) and items > 0:
+        if (want_code or want_router) and items > 0 and _param_grad_rows_eligible(weight.dtype, winner.dtype, cells):
+            # f32 parameters, u8 routes, up to 32 cells: the batch sums straight from the rows.
+            grad_c = torch.empty_like(code) if want_code else None
+            if want_router:
+                grad_w = torch.empty_like(weight)
+                grad_b = torch.empty((heads, cells), device=dev, dtype=weight.dtype)
+            z32 = z if z.dtype == torch.float32 else z.float()
+            _launch(
+                "trop_param_grad_rows", lib.tropnn_b200_trop_param_grad_rows, g.data_ptr(), z32.data_ptr(), items,
+                code_dim, pdt, heads, cells, winner.data_ptr(), nat.ptr(runner) if training else None, icode,
+                nat.ptr(coef_w), nat.ptr(coef_r) if training else None, ctx.code_scale, nat.ptr(gm),
+                nat.ptr(grad_c), nat.ptr(grad_w), nat.ptr(grad_b), stream,
+            )
+        elif (want_code or want_router) and items > 0:
             perm_w = torch.empty((heads, items), device=dev, dtype=torch.int32)
             seg_w = torch.empty((heads, cells + 1), device=dev, dtype=torch.int32)
             _launch(
