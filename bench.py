@@ -787,7 +787,13 @@ def _run_b200_body(
     e2e_value = rows_total * args.steps / (e2e_modes[e2e_mode] / 1e3)
 
     peaks, peaks_kind = _peaks()
-    traffic_table = json.loads(TRAFFIC_PATH.read_text()).get(w.name, {}) if TRAFFIC_PATH.exists() else {}
+    # The captures in profiles/traffic.json are of one GPU running the workload's full batch: at
+    # other per-GPU row counts (N > 1, --rows) the launch moves other bytes, so none is attached.
+    traffic_table = (
+        json.loads(TRAFFIC_PATH.read_text()).get(w.name, {})
+        if TRAFFIC_PATH.exists() and world == 1 and not args.rows
+        else {}
+    )
     per_kernel_roofline = {}
     for name, stats in kernels.items():
         rl = kernel_roofline(w, name, w_rank.rows_per_gpu, peaks)
