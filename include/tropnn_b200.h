@@ -106,6 +106,22 @@ TROPNN_B200_API int tropnn_b200_segment_rowsum(const float *values, int64_t rows
                                const int32_t *perm1, const int32_t *seg1, const float *coef1, float coef_sign1,
                                float scale, void *out, int out_dtype, void *bucket_sum, void *stream);
 
+/*
+ * tropnn_b200_segment_rowsum over half-precision values, one list, no coefficients:
+ * out[g*buckets + b, :] = scale / s * sum_{j in seg} values[perm[g*rows + j] * ld, :width], with
+ * values = x * s rounded to value_dtype (F16/BF16) and s the power-of-two gradient scale of
+ * *grad_absmax (tropnn_b200_split_half with the same word; NULL: s = 1). width and ld multiples
+ * of 8, values 16-byte aligned. Half the bytes per gathered row of the f32 form: the LUT
+ * gradient of half-precision PairwiseLinear layers (rounded to that dtype in any case). The
+ * rounding of x to value_dtype adds at most one half-precision unit of relative error per
+ * summand. Deterministic.
+ */
+TROPNN_B200_API int tropnn_b200_segment_rowsum_half(const void *values, int value_dtype, int64_t rows,
+                                                    int64_t width, int64_t ld, int64_t groups, int64_t buckets,
+                                                    const int32_t *perm, const int32_t *seg, float scale,
+                                                    const void *grad_absmax, void *out, int out_dtype,
+                                                    void *stream);
+
 /* --------------------------------------------------------- PairwiseLinear */
 
 /*

@@ -17,7 +17,7 @@ from pathlib import Path
 import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtropnn_b200.so"
-ABI_VERSION = 18
+ABI_VERSION = 19
 
 # tropnn_b200_dtype
 F32, F16, BF16, U8, I16, I64 = 0, 1, 2, 3, 4, 5
@@ -52,6 +52,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tropnn_b200_segment_rowsum": (
         _i32,
         [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _f32, _p, _p, _p, _f32, _f32, _p, _i32, _p, _p],
+    ),
+    "tropnn_b200_segment_rowsum_half": (
+        _i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _p, _p, _f32, _p, _p, _i32, _p]
     ),
     "tropnn_b200_pairwise_lut_grad": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _f32, _p, _i32, _p]),
     "tropnn_b200_pairwise_lut_grad_peer_floats": (_i64, [_i64, _i64, _i64]),

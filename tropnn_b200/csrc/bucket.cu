@@ -8,6 +8,8 @@
 // warp per bucket sums its rows and writes the table entry exactly once. No zeroing,
 // no atomics, and the summation order is fixed (ascending row inside a bucket), so
 // the result is bit-reproducible run to run.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace tropnn_b200 {
@@ -185,8 +187,8 @@ struct SegList {
   float sign;
 };
 
-template <int VEC, int NV>
-__device__ __forceinline__ void accumulate_list(const SegList &L, const float *__restrict__ values, int64_t rows,
+template <typename VT, int VEC, int NV>
+__device__ __forceinline__ void accumulate_list(const SegList &L, const VT *__restrict__ values, int64_t rows,
                                                 int64_t ld, int64_t groups, int buckets, int64_t g, int b,
                                                 int64_t col0, int64_t width, float (&acc)[NV][VEC],
                                                 float &coef_total) {
@@ -214,7 +216,7 @@ __device__ __forceinline__ void accumulate_list(const SegList &L, const float *_
       if (col < width) {
         float v[4][VEC];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) VecLoad<float, VEC>::load(values + n[u] * ld + col, v[u]);
+        for (int u = 0; u < 4; ++u) VecLoad<VT, VEC>::load(values + n[u] * ld + col, v[u]);
 #pragma unroll
         for (int u = 0; u < 4; ++u)
 #pragma unroll
@@ -226,13 +228,13 @@ __device__ __forceinline__ void accumulate_list(const SegList &L, const float *_
     const int64_t n = __ldg(permp + j);
     const float c = L.coef ? __fmul_rn(L.sign, __ldg(L.coef + n * groups + g)) : L.sign;
     coef_total += c;
-    const float *vrow = values + n * ld;
+    const VT *vrow = values + n * ld;
 #pragma unroll
     for (int s = 0; s < NV; ++s) {
       const int64_t col = col0 + int64_t(s) * 32 * VEC + int64_t(lane) * VEC;
       if (col < width) {
         float v[VEC];
-        VecLoad<float, VEC>::load(vrow + col, v);
+        VecLoad<VT, VEC>::load(vrow + col, v);
 #pragma unroll
         for (int e = 0; e < VEC; ++e) acc[s][e] = fmaf(c, v[e], acc[s][e]);
       }
@@ -240,10 +242,13 @@ __device__ __forceinline__ void accumulate_list(const SegList &L, const float *_
   }
 }
 
-template <typename OutT, int VEC, int NV>
+template <typename OutT, int VEC, int NV, typename VT = float>
 __global__ void __launch_bounds__(kSegWarps * 32) segment_rowsum_kernel(
-    const float *__restrict__ values, int64_t rows, int64_t width, int64_t ld, int64_t groups, int buckets,
-    SegList l0, SegList l1, bool has_l1, float scale, OutT *__restrict__ out, OutT *__restrict__ bucket_sum) {
+    const VT *__restrict__ values, int64_t rows, int64_t width, int64_t ld, int64_t groups, int buckets,
+    SegList l0, SegList l1, bool has_l1, float scale, OutT *__restrict__ out, OutT *__restrict__ bucket_sum,
+    const uint32_t *__restrict__ absmax = nullptr) {
+  // Half-precision values carry the power-of-two gradient scale of *absmax; undone here (exact).
+  if (absmax != nullptr) scale = __fmul_rn(scale, pow2_inverse(grad_scale_of(absmax)));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int quads = (buckets + kSegWarps - 1) / kSegWarps;
@@ -258,8 +263,9 @@ __global__ void __launch_bounds__(kSegWarps * 32) segment_rowsum_kernel(
 #pragma unroll
     for (int e = 0; e < VEC; ++e) acc[s][e] = 0.f;
   float coef_total = 0.f;
-  accumulate_list<VEC, NV>(l0, values, rows, ld, groups, buckets, g, b, col0, width, acc, coef_total);
-  if (has_l1) accumulate_list<VEC, NV>(l1, values, rows, ld, groups, buckets, g, b, col0, width, acc, coef_total);
+  accumulate_list<VT, VEC, NV>(l0, values, rows, ld, groups, buckets, g, b, col0, width, acc, coef_total);
+  if (has_l1)
+    accumulate_list<VT, VEC, NV>(l1, values, rows, ld, groups, buckets, g, b, col0, width, acc, coef_total);
 
   OutT *orow = out + (g * buckets + b) * width;
 #pragma unroll
@@ -358,6 +364,60 @@ int bucket_sort_impl(const void *keys, int key_dtype, int64_t rows, int64_t grou
   return check_launch("bucket_sort");
 }
 
+// segment_rowsum over half-precision values (one list, no coefficients): out[g, b, :] = scale /
+// s * sum over the bucket's rows of values[n, :], where the values are x * s rounded to the
+// parameter dtype and s is the power-of-two gradient scale of *absmax (tropnn_b200_split_half with
+// the same word). Half the bytes of the f32 rows per gathered row; used for the LUT gradient of
+// half-precision Pairwise layers, whose result is rounded to that dtype anyway.
+int segment_rowsum_half_impl(const void *values, int value_dtype, int64_t rows, int64_t width, int64_t ld,
+                             int64_t groups, int64_t buckets, const int32_t *perm, const int32_t *seg, float scale,
+                             const uint32_t *absmax, void *out, int out_dtype, cudaStream_t stream) {
+  TB_REQUIRE(value_dtype == TROPNN_B200_F16 || value_dtype == TROPNN_B200_BF16, TROPNN_B200_ERR_DTYPE,
+             "segment_rowsum_half: value dtype %s unsupported", dtype_name(value_dtype));
+  TB_REQUIRE(is_float_dtype(out_dtype), TROPNN_B200_ERR_DTYPE, "segment_rowsum_half: out dtype %s unsupported",
+             dtype_name(out_dtype));
+  TB_REQUIRE(rows >= 0 && width >= 0 && groups >= 0 && buckets >= 1 && ld >= width && width % 8 == 0 && ld % 8 == 0,
+             TROPNN_B200_ERR_INVALID,
+             "segment_rowsum_half: bad sizes rows=%lld width=%lld ld=%lld (width and ld multiples of 8)",
+             (long long)rows, (long long)width, (long long)ld);
+  if (groups == 0 || width == 0) return TROPNN_B200_OK;
+  TB_REQUIRE(out != nullptr && seg != nullptr && (rows == 0 || (values != nullptr && perm != nullptr)),
+             TROPNN_B200_ERR_INVALID, "segment_rowsum_half: null pointer");
+  TB_REQUIRE(reinterpret_cast<uintptr_t>(values) % 16 == 0, TROPNN_B200_ERR_INVALID,
+             "segment_rowsum_half: values must be 16-byte aligned");
+  const SegList l0{perm, seg, nullptr, 1.f};
+  const SegList none{nullptr, nullptr, nullptr, 0.f};
+  constexpr int kVec = 8, kNv = 4;
+  const int64_t quads = ceil_div(buckets, kSegWarps);
+  const int64_t col_tiles = ceil_div(width, int64_t(32 * kVec * kNv));
+  TB_REQUIRE(groups * quads < (int64_t(1) << 31) && col_tiles < 65536, TROPNN_B200_ERR_INVALID,
+             "segment_rowsum_half: grid too large");
+  const dim3 grid(static_cast<unsigned>(groups * quads), static_cast<unsigned>(col_tiles));
+  auto go = [&](auto *vt, auto *ot) {
+    using VT = std::remove_pointer_t<decltype(vt)>;
+    using OT = std::remove_pointer_t<decltype(ot)>;
+    segment_rowsum_kernel<OT, kVec, kNv, VT><<<grid, kSegWarps * 32, 0, stream>>>(
+        static_cast<const VT *>(values), rows, width, ld, groups, static_cast<int>(buckets), l0, none, false, scale,
+        static_cast<OT *>(out), nullptr, absmax);
+  };
+  const bool f16 = value_dtype == TROPNN_B200_F16;
+  switch (out_dtype) {
+    case TROPNN_B200_F32:
+      f16 ? go(static_cast<__half *>(nullptr), static_cast<float *>(nullptr))
+          : go(static_cast<__nv_bfloat16 *>(nullptr), static_cast<float *>(nullptr));
+      break;
+    case TROPNN_B200_F16:
+      f16 ? go(static_cast<__half *>(nullptr), static_cast<__half *>(nullptr))
+          : go(static_cast<__nv_bfloat16 *>(nullptr), static_cast<__half *>(nullptr));
+      break;
+    default:
+      f16 ? go(static_cast<__half *>(nullptr), static_cast<__nv_bfloat16 *>(nullptr))
+          : go(static_cast<__nv_bfloat16 *>(nullptr), static_cast<__nv_bfloat16 *>(nullptr));
+      break;
+  }
+  return check_launch("segment_rowsum_half");
+}
+
 int segment_rowsum_impl(const float *values, int64_t rows, int64_t width, int64_t ld, int64_t groups,
                         int64_t buckets, const int32_t *perm0, const int32_t *seg0, const float *coef0,
                         float coef_sign0, const int32_t *perm1, const int32_t *seg1, const float *coef1,
@@ -413,6 +473,16 @@ int tropnn_b200_segment_rowsum(const float *values, int64_t rows, int64_t width,
   TB_CHECK(tropnn_b200::segment_rowsum_impl(values, rows, width, ld, groups, buckets, perm0, seg0, coef0,
                                             coef_sign0, perm1, seg1, coef1, coef_sign1, scale, out, out_dtype,
                                             bucket_sum, tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+int tropnn_b200_segment_rowsum_half(const void *values, int value_dtype, int64_t rows, int64_t width, int64_t ld,
+                                    int64_t groups, int64_t buckets, const int32_t *perm, const int32_t *seg,
+                                    float scale, const void *grad_absmax, void *out, int out_dtype, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::segment_rowsum_half_impl(values, value_dtype, rows, width, ld, groups, buckets, perm, seg,
+                                                 scale, static_cast<const uint32_t *>(grad_absmax), out, out_dtype,
+                                                 tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 

@@ -240,29 +240,45 @@ class _PairwiseB200Function(torch.autograd.Function):
                 stream,
             )
             grad_lut = torch.empty_like(lut)
-            _launch(
-                "pairwise_lut_grad",
-                lib.tropnn_b200_segment_rowsum,
-                g.data_ptr(),
-                items,
-                out_features,
-                out_features,
-                tables,
-                buckets,
-                perm.data_ptr(),
-                seg.data_ptr(),
-                None,
-                ctx.output_scale,
-                None,
-                None,
-                None,
-                0.0,
-                1.0,
-                grad_lut.data_ptr(),
-                nat.float_code(grad_lut.dtype),
-                None,
-                stream,
-            )
+            if lut.dtype in (torch.float16, torch.bfloat16) and out_features % 8 == 0 and g.data_ptr() % 16 == 0:
+                # Half-precision LUT: the bucket sums gather g rounded to the LUT dtype (after a
+                # power-of-two scale fitted to g's maximum, undone in the sums' epilogue), half
+                # the bytes of every gathered row; the sums are rounded to that dtype anyway.
+                pdt = nat.float_code(lut.dtype)
+                gmax = torch.zeros(1, device=dev, dtype=torch.int32)
+                _launch("absmax", lib.tropnn_b200_absmax_f32, g.data_ptr(), g.numel(), gmax.data_ptr(), stream)
+                g_half = torch.empty((items, 2 * out_features), device=dev, dtype=lut.dtype)
+                _launch("split_half", lib.tropnn_b200_split_half, g.data_ptr(), items, out_features, pdt,
+                        gmax.data_ptr(), g_half.data_ptr(), stream)
+                _launch(
+                    "pairwise_lut_grad", lib.tropnn_b200_segment_rowsum_half, g_half.data_ptr(), pdt, items,
+                    out_features, 2 * out_features, tables, buckets, perm.data_ptr(), seg.data_ptr(),
+                    ctx.output_scale, gmax.data_ptr(), grad_lut.data_ptr(), nat.float_code(grad_lut.dtype), stream,
+                )
+            else:
+                _launch(
+                    "pairwise_lut_grad",
+                    lib.tropnn_b200_segment_rowsum,
+                    g.data_ptr(),
+                    items,
+                    out_features,
+                    out_features,
+                    tables,
+                    buckets,
+                    perm.data_ptr(),
+                    seg.data_ptr(),
+                    None,
+                    ctx.output_scale,
+                    None,
+                    None,
+                    None,
+                    0.0,
+                    1.0,
+                    grad_lut.data_ptr(),
+                    nat.float_code(grad_lut.dtype),
+                    None,
+                    stream,
+                )
         # Under distributed.overlapped_gradient_sync the LUT gradient's all-reduce runs on a
         # side stream while the straight-through kernels below execute.
         pending = (
