@@ -341,3 +341,46 @@ def test_staged_paths_match_oracle(in_f, out_f, tables, comparisons, n, dtype, s
         layer.thresholds.normal_(0.0, 0.3)
     x, g = _inputs(n, in_f, out_f, seed=9)
     _compare(_run(layer, x, g), _oracle_case(layer, x, g), tol=FP32_TOL if dtype == torch.float32 else 2e-2)
+
+
+@pytest.mark.parametrize(
+    ("rows", "width", "groups", "buckets", "vdtype", "gscale", "tol"),
+    [
+        (517, 2048, 6, 256, torch.float16, 1.0, 2e-3),
+        (300, 1536, 4, 64, torch.bfloat16, 1.0, 1e-2),
+        (257, 4096, 3, 256, torch.float16, 1e-7, 2e-3),  # far below f16's normal range: the scale keeps it
+    ],
+)
+def test_segment_rowsum_half_matches_f32_sums(rows, width, groups, buckets, vdtype, gscale, tol) -> None:
+    """tropnn_b200_segment_rowsum_half over g rounded by split_half (power-of-two scale from the
+    gradient maximum) against tropnn_b200_segment_rowsum over the f32 g: within one rounding of
+    the value dtype per summand."""
+    from tropnn_b200 import _native as nat
+
+    lib = nat.load()
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(rows)
+    g = (torch.randn(rows, width, generator=gen) * gscale).to(dev)
+    keys = torch.randint(0, buckets, (rows, groups), generator=gen).to(dev)
+    stream = nat.stream_handle(dev)
+    perm = torch.empty((groups, rows), device=dev, dtype=torch.int32)
+    seg = torch.empty((groups, buckets + 1), device=dev, dtype=torch.int32)
+    nat.check(lib.tropnn_b200_bucket_sort(keys.data_ptr(), nat.I64, rows, groups, groups, buckets, perm.data_ptr(),
+                                          seg.data_ptr(), stream), "bucket_sort")
+    ref = torch.empty((groups, buckets, width), device=dev)
+    nat.check(lib.tropnn_b200_segment_rowsum(g.data_ptr(), rows, width, width, groups, buckets, perm.data_ptr(),
+                                             seg.data_ptr(), None, 0.5, None, None, None, 0.0, 1.0, ref.data_ptr(),
+                                             nat.F32, None, stream), "segment_rowsum")
+    gmax = torch.zeros(1, device=dev, dtype=torch.int32)
+    nat.check(lib.tropnn_b200_absmax_f32(g.data_ptr(), g.numel(), gmax.data_ptr(), stream), "absmax")
+    split = torch.empty((rows, 2 * width), device=dev, dtype=vdtype)
+    nat.check(lib.tropnn_b200_split_half(g.data_ptr(), rows, width, nat.float_code(vdtype), gmax.data_ptr(),
+                                         split.data_ptr(), stream), "split_half")
+    got = torch.full((groups, buckets, width), float("nan"), device=dev)
+    nat.check(lib.tropnn_b200_segment_rowsum_half(split.data_ptr(), nat.float_code(vdtype), rows, width, 2 * width,
+                                                  groups, buckets, perm.data_ptr(), seg.data_ptr(), 0.5,
+                                                  gmax.data_ptr(), got.data_ptr(), nat.F32, stream),
+              "segment_rowsum_half")
+    torch.cuda.synchronize()
+    assert torch.isfinite(got).all()
+    assert rel_err(got.cpu().numpy(), ref.cpu().numpy()) <= tol
