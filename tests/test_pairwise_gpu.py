@@ -384,3 +384,22 @@ def test_segment_rowsum_half_matches_f32_sums(rows, width, groups, buckets, vdty
     torch.cuda.synchronize()
     assert torch.isfinite(got).all()
     assert rel_err(got.cpu().numpy(), ref.cpu().numpy()) <= tol
+
+
+def test_small_batch_kernels_are_bit_identical_to_the_per_row_kernels() -> None:
+    """Up to 64 rows the forward runs a CTA per row (threads over the columns) and up to 256
+    rows the min-margin STE does (tables split over its warps); both keep the per-row kernels'
+    summation orders, so the first rows' output and grad_x of a 300-row batch (per-row kernels)
+    and of those rows alone (row-CTA kernels) are equal bit for bit, and both match the
+    oracle."""
+    layer = tropnn_b200.PairwiseLinear(256, 512, tables=16, comparisons=6, seed=2)
+    with torch.no_grad():
+        layer.thresholds.normal_(0.0, 0.2)
+    x, g = _inputs(300, 256, 512, seed=12)
+    big = _run(layer, x, g)
+    layer.zero_grad(set_to_none=True)
+    small = _run(layer, x[:8], g[:8])
+    assert np.array_equal(small["out"], big["out"][:8])
+    assert np.array_equal(small["indices"], big["indices"][:8])
+    assert np.array_equal(small["grad.x"], big["grad.x"][:8])
+    _compare(small, _oracle_case(layer, x[:8], g[:8]))

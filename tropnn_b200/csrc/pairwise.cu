@@ -423,6 +423,68 @@ int launch_forward_staged(const float *x, int64_t rows, int64_t in, const int64_
   return TROPNN_B200_OK;
 }
 
+// Forward for a few rows (latency-bound batches): a CTA per row, its threads over the columns,
+// eight tables' LUT loads in flight per thread. Each output element is still summed in table
+// order from 0, so y, indices and margins are bit-identical to pairwise_forward_kernel's.
+constexpr int kFwdRowThreads = 128;
+constexpr int64_t kFwdRowCtaRows = 64;
+
+template <typename LutT, typename ThrT, int VEC>
+__global__ void __launch_bounds__(kFwdRowThreads) pairwise_forward_rowcta_kernel(
+    const float *__restrict__ x, int64_t rows, int64_t in, const int64_t *__restrict__ anchors,
+    const ThrT *__restrict__ thr, int T, int C, const LutT *__restrict__ lut, int64_t out, float out_scale,
+    float *__restrict__ y, int64_t *__restrict__ idx_out, float *__restrict__ u_out) {
+  extern __shared__ int row_idx[];  // [T]
+  const int64_t n = blockIdx.x;
+  const int64_t table_size = int64_t(1) << C;
+  const float *xrow = x + n * in;
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    int bits = 0;
+#pragma unroll
+    for (int c = 0; c < kMaxComparisons; ++c) {
+      if (c < C) {
+        const int64_t e = (int64_t(t) * C + c) * 2;
+        const int64_t a = clamp_feature(__ldg(anchors + e), in);
+        const int64_t b = clamp_feature(__ldg(anchors + e + 1), in);
+        const float uv = __fsub_rn(__fsub_rn(__ldg(xrow + a), __ldg(xrow + b)), ldg_f32(thr + int64_t(t) * C + c));
+        u_out[(n * T + t) * C + c] = uv;
+        bits |= (uv > 0.f ? 1 : 0) << c;
+      }
+    }
+    row_idx[t] = bits;
+    idx_out[n * T + t] = bits;
+  }
+  __syncthreads();
+  for (int64_t col = int64_t(threadIdx.x) * VEC; col < out; col += int64_t(blockDim.x) * VEC) {
+    float acc[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
+#pragma unroll 8
+    for (int t = 0; t < T; ++t) {
+      float v[VEC];
+      VecLoad<LutT, VEC>::load(lut + (int64_t(t) * table_size + row_idx[t]) * out + col, v);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[e] = __fadd_rn(acc[e], v[e]);
+    }
+    float *yrow = y + n * out + col;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) yrow[e] = __fmul_rn(acc[e], out_scale);
+  }
+}
+
+template <typename LutT, typename ThrT, int VEC>
+int launch_forward_rowcta(const float *x, int64_t rows, int64_t in, const int64_t *anchors, const void *thr, int T,
+                          int C, const void *lut, int64_t out, float out_scale, float *y, int64_t *idx, float *u,
+                          cudaStream_t stream) {
+  const size_t smem = sizeof(int) * T;
+  auto kernel = pairwise_forward_rowcta_kernel<LutT, ThrT, VEC>;
+  TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "pairwise_forward_rowcta"));
+  kernel<<<static_cast<unsigned>(rows), kFwdRowThreads, smem, stream>>>(
+      x, rows, in, anchors, static_cast<const ThrT *>(thr), T, C, static_cast<const LutT *>(lut), out, out_scale, y,
+      idx, u);
+  return check_launch("pairwise_forward");
+}
+
 template <typename LutT, typename ThrT>
 int forward_by_width(const float *x, int64_t rows, int64_t in, const int64_t *anchors, const void *thr, int T, int C,
                      const void *lut, int64_t out, float out_scale, float *y, int64_t *idx, float *u,
@@ -437,6 +499,10 @@ int forward_by_width(const float *x, int64_t rows, int64_t in, const int64_t *an
         in * 4 <= int64_t(staged_slots(T)) * kSlotBytes)
       return launch_forward_staged<LutT, ThrT>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u,
                                                stream);
+    // A few rows: a CTA per row.
+    if (rows <= kFwdRowCtaRows)
+      return launch_forward_rowcta<LutT, ThrT, kVec>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u,
+                                                     stream);
     // Column tile of 512 outputs (f32) or 1024 (16-bit) when the rows alone fill the GPU,
     // narrower tiles otherwise.
     if (out > 32 * kVec * 2 || ceil_div(rows, kFwdRows) >= 4 * 148)
@@ -445,6 +511,9 @@ int forward_by_width(const float *x, int64_t rows, int64_t in, const int64_t *an
     return launch_forward<LutT, ThrT, kVec, 1>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u,
                                                stream);
   }
+  if (rows <= kFwdRowCtaRows)
+    return launch_forward_rowcta<LutT, ThrT, 1>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u,
+                                                stream);
   if (out > 64)
     return launch_forward<LutT, ThrT, 1, 4>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u, stream);
   return launch_forward<LutT, ThrT, 1, 1>(x, rows, in, anchors, thr, T, C, lut, out, out_scale, y, idx, u, stream);
@@ -617,10 +686,101 @@ __global__ void __launch_bounds__(kSteMaxWarps * 32) pairwise_ste_kernel(
   }
 }
 
+// Min-margin STE backward for a few rows (latency-bound batches: the per-row kernel above gives
+// each row one warp, which walks all its tables in series): a CTA per row, its warps taking the
+// tables in parallel. Every table's dot is formed exactly as above (lane l sums columns l*VEC +
+// k*32*VEC in order, then the warp butterfly), and grad_latent is the same per-feature gather,
+// so gu, r* and grad_latent are bit-identical to pairwise_ste_kernel's.
+constexpr int kSteRowWarps = 8;
+
+template <typename LutT, int VEC>
+__global__ void __launch_bounds__(kSteRowWarps * 32) pairwise_ste_rowcta_kernel(
+    const float *__restrict__ g, int64_t rows, int64_t out, float out_scale, const int64_t *__restrict__ idx,
+    const float *__restrict__ u, int T, int C, int64_t in, const LutT *__restrict__ lut, int surrogate,
+    const int32_t *__restrict__ feat_start, const int32_t *__restrict__ feat_entries, float *__restrict__ grad_x,
+    float *__restrict__ gu_out, uint8_t *__restrict__ rstar_out) {
+  extern __shared__ float row_smem[];
+  float *gu_s = row_smem;                                        // [T]
+  uint8_t *rs_s = reinterpret_cast<uint8_t *>(gu_s + T);         // [T]
+  uint16_t *cur_s = reinterpret_cast<uint16_t *>(rs_s + ((T + 1) & ~1));  // [T]
+  const int64_t n = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t table_size = int64_t(1) << C;
+  // r* = argmin |u| (first on ties), the current bucket and u at r* per table.
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    const float *urow = u + (n * T + t) * C;
+    int rmin = 0;
+    float ustar = __ldg(urow);
+    float best = fabsf(ustar);
+    for (int c = 1; c < C; ++c) {
+      const float v = __ldg(urow + c);
+      if (fabsf(v) < best) {
+        best = fabsf(v);
+        rmin = c;
+        ustar = v;
+      }
+    }
+    rs_s[t] = static_cast<uint8_t>(rmin);
+    cur_s[t] = static_cast<uint16_t>(__ldg(idx + n * T + t));
+    gu_s[t] = ustar;
+  }
+  __syncthreads();
+  const float *grow = g + n * out;
+  for (int t = warp; t < T; t += kSteRowWarps) {
+    const int cur = cur_s[t];
+    const LutT *lcur = lut + (int64_t(t) * table_size + cur) * out;
+    const LutT *lnb = lut + (int64_t(t) * table_size + (cur ^ (1 << rs_s[t]))) * out;
+    float dot = 0.f;
+    for (int64_t col = int64_t(lane) * VEC; col < out; col += 32 * VEC) {
+      float gv[VEC], vc[VEC], vn[VEC];
+      VecLoad<float, VEC>::load(grow + col, gv);
+      VecLoad<LutT, VEC>::load(lcur + col, vc);
+      VecLoad<LutT, VEC>::load(lnb + col, vn);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) dot = fmaf(__fmul_rn(gv[e], out_scale), __fsub_rn(vn[e], vc[e]), dot);
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) {
+      const float gu = __fmul_rn(dot, surrogate_grad(gu_s[t], surrogate));
+      gu_s[t] = gu;
+      gu_out[n * T + t] = gu;
+      rstar_out[n * T + t] = rs_s[t];
+    }
+  }
+  __syncthreads();
+  float *gxrow = grad_x + n * in;
+  for (int64_t i = threadIdx.x; i < in; i += blockDim.x) {
+    const int lo = __ldg(feat_start + i);
+    const int hi = __ldg(feat_start + i + 1);
+    float acc = 0.f;
+    for (int j = lo; j < hi; ++j) {
+      const int e = __ldg(feat_entries + j);
+      const int tc = e >> 1;
+      const int t = tc / C;
+      const int c = tc - t * C;
+      const float v = (rs_s[t] == c) ? gu_s[t] : 0.f;
+      acc = (e & 1) ? __fsub_rn(acc, v) : __fadd_rn(acc, v);
+    }
+    gxrow[i] = acc;
+  }
+}
+
+// Rows below which the min-margin STE takes a CTA per row: fewer rows than about two waves of the
+// per-row kernel's 4-warp CTAs.
+constexpr int64_t kSteRowCtaRows = 256;
+
 template <typename LutT, int VEC>
 int launch_ste(bool use_min, const float *g, int64_t rows, int64_t out, float out_scale, const int64_t *idx,
                const float *u, int T, int C, int64_t in, const void *lut, int surrogate, const int32_t *fs,
                const int32_t *fe, float *gx, float *gu, uint8_t *rs, cudaStream_t stream) {
+  if (use_min && rows <= kSteRowCtaRows && rows > 0) {
+    const size_t row_smem = sizeof(float) * T + size_t((T + 1) & ~1) + sizeof(uint16_t) * T;
+    auto kernel = pairwise_ste_rowcta_kernel<LutT, VEC>;
+    TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), row_smem, "pairwise_ste_rowcta"));
+    kernel<<<static_cast<unsigned>(rows), kSteRowWarps * 32, row_smem, stream>>>(
+        g, rows, out, out_scale, idx, u, T, C, in, static_cast<const LutT *>(lut), surrogate, fs, fe, gx, gu, rs);
+    return check_launch("pairwise_ste_backward");
+  }
   // gu (f32, one per table or per comparison) + r* (u8) + current bucket (u16) per row.
   const size_t per_warp = sizeof(float) * (use_min ? T : T * C) + 3 * size_t(T);
   int warps = kSteMaxWarps;
