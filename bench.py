@@ -338,6 +338,8 @@ def kernel_roofline(w: Workload, kernel: str, rows: int, peaks: dict) -> tuple[s
             return "tensor", 2.0 * 3 * rows * out * D, "TFLOP/s", *tf32
         if kernel == "split_half":
             return "hbm", float(rows * D * 4 + rows * 2 * D * 2), "GB/s", *hbm
+        if kernel == "split_transpose_half":  # f32 g in, [hi | lo] and hi^T out
+            return "hbm", float(rows * D * (4 + 4 + 2)), "GB/s", *hbm
         if kernel == "tf32_split":
             return "hbm", float(rows * D * 12), "GB/s", *hbm
         if kernel == "transpose_to_half":

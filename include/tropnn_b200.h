@@ -404,6 +404,18 @@ TROPNN_B200_API int tropnn_b200_split_half(const float *x, int64_t rows, int64_t
                            const void *grad_absmax, void *out, void *stream);
 
 /*
+ * tropnn_b200_split_half and its transpose in one pass over x: out_split [rows, 2*cols] as
+ * tropnn_b200_split_half writes it, and out_t [cols, rows] = its hi half transposed, equal
+ * to tropnn_b200_transpose_to_half of x with the same grad_absmax. rows even, cols % 4 == 0;
+ * x 16-byte, out_split 8-byte, out_t 4-byte aligned. The half-precision backward uses it on
+ * grad_hidden, whose split feeds tropnn_b200_trop_gm and whose transpose feeds the code
+ * gradient. No reference counterpart: a precision-splitting step of this backend.
+ */
+TROPNN_B200_API int tropnn_b200_split_transpose_half(const float *x, int64_t rows, int64_t cols, int dtype,
+                                                     const void *grad_absmax, void *out_split, void *out_t,
+                                                     void *stream);
+
+/*
  * Gradient range for the half-precision backward GEMMs: *bits = max(*bits, f32 bits of
  * max_i |x[i]|) (the caller zeroes the 4-byte word first; deterministic). The kernels that take
  * a grad_absmax pointer scale the gradient by s = 2^e bringing that maximum into [16, 32)

@@ -196,6 +196,64 @@ def test_transpose_to_half_exact(rows: int, cols: int, src: torch.dtype) -> None
     assert torch.equal(out, x.to(dst).t())
 
 
+@pytest.mark.parametrize(("rows", "cols", "dtype"), [(302, 6, torch.float16), (3, 7, torch.float16),
+                                                     (130, 66, torch.bfloat16)])
+def test_transpose_to_half_half_input_shapes(rows: int, cols: int, dtype: torch.dtype) -> None:
+    """Half in, half out, no scale (the paired 4-byte transpose, or 2-byte moves for odd shapes):
+    a plain transpose, bit for bit."""
+    lib = nat.load()
+    x = torch.randn(rows, cols, device="cuda").to(dtype)
+    out = torch.full((cols, rows), float("nan"), device="cuda", dtype=dtype)
+    nat.check(lib.tropnn_b200_transpose_to_half(x.data_ptr(), nat.float_code(dtype), rows, cols, nat.float_code(dtype),
+                                                None, out.data_ptr(), nat.stream_handle(x.device)), "transpose_to_half")
+    torch.cuda.synchronize()
+    assert torch.equal(out, x.t())
+
+
+@pytest.mark.parametrize(
+    ("rows", "cols", "dtype", "scale"),
+    [(16384, 256, torch.float16, 1e-6), (2048, 256, torch.float16, None), (302, 68, torch.bfloat16, 1e3),
+     (2, 4, torch.float16, None), (130, 132, torch.float16, 1e-3)],
+)
+def test_split_transpose_half_matches_the_two_passes(rows: int, cols: int, dtype: torch.dtype, scale) -> None:
+    """tropnn_b200_split_transpose_half writes split_half's [hi | lo] and transpose_to_half's hi^T
+    bit for bit, with and without a gradient scale (tiles of 64 rows x 64 columns: ragged edges in
+    both directions)."""
+    lib = nat.load()
+    stream = nat.stream_handle(torch.device("cuda"))
+    code = nat.float_code(dtype)
+    gen = torch.Generator().manual_seed(rows + cols)
+    x = (torch.randn(rows, cols, generator=gen) * (1.0 if scale is None else scale)).cuda()
+    gmax = None
+    if scale is not None:
+        gmax = torch.zeros(1, device="cuda", dtype=torch.int32)
+        nat.check(lib.tropnn_b200_absmax_f32(x.data_ptr(), x.numel(), gmax.data_ptr(), stream), "absmax")
+    want_split = torch.empty((rows, 2 * cols), device="cuda", dtype=dtype)
+    want_t = torch.empty((cols, rows), device="cuda", dtype=dtype)
+    nat.check(lib.tropnn_b200_split_half(x.data_ptr(), rows, cols, code, nat.ptr(gmax), want_split.data_ptr(), stream),
+              "split_half")
+    nat.check(lib.tropnn_b200_transpose_to_half(x.data_ptr(), nat.F32, rows, cols, code, nat.ptr(gmax),
+                                                want_t.data_ptr(), stream), "transpose_to_half")
+    got_split = torch.full((rows, 2 * cols), float("nan"), device="cuda", dtype=dtype)
+    got_t = torch.full((cols, rows), float("nan"), device="cuda", dtype=dtype)
+    nat.check(lib.tropnn_b200_split_transpose_half(x.data_ptr(), rows, cols, code, nat.ptr(gmax), got_split.data_ptr(),
+                                                   got_t.data_ptr(), stream), "split_transpose_half")
+    torch.cuda.synchronize()
+    assert torch.equal(got_split.view(torch.int16), want_split.view(torch.int16))
+    assert torch.equal(got_t.view(torch.int16), want_t.view(torch.int16))
+
+
+def test_split_transpose_half_rejects_odd_rows() -> None:
+    lib = nat.load()
+    x = torch.randn(3, 4, device="cuda")
+    split = torch.empty((3, 8), device="cuda", dtype=torch.float16)
+    xt = torch.empty((4, 3), device="cuda", dtype=torch.float16)
+    status = lib.tropnn_b200_split_transpose_half(x.data_ptr(), 3, 4, nat.F16, None, split.data_ptr(), xt.data_ptr(),
+                                                  nat.stream_handle(x.device))
+    with pytest.raises(ValueError, match="must be even"):
+        nat.check(status, "split_transpose_half")
+
+
 def _split_half(hidden: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     lib = nat.load()
     rows, cols = hidden.shape

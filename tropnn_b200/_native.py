@@ -17,7 +17,7 @@ from pathlib import Path
 import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtropnn_b200.so"
-ABI_VERSION = 19
+ABI_VERSION = 20
 
 # tropnn_b200_dtype
 F32, F16, BF16, U8, I16, I64 = 0, 1, 2, 3, 4, 5
@@ -101,6 +101,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tropnn_b200_transpose_f32": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _p]),
     "tropnn_b200_colsum_f32": (_i32, [_p, _i64, _i64, _i64, _p, _p]),
     "tropnn_b200_split_half": (_i32, [_p, _i64, _i64, _i32, _p, _p, _p]),
+    "tropnn_b200_split_transpose_half": (_i32, [_p, _i64, _i64, _i32, _p, _p, _p, _p]),
     "tropnn_b200_absmax_f32": (_i32, [_p, _i64, _p, _p]),
     "tropnn_b200_linear_f32out": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _i32, _p, _p, _p]),
     "tropnn_b200_peer_buffer_create": (_i32, [_i64, ctypes.POINTER(_p), _p]),

@@ -111,7 +111,7 @@ extern "C" {
 
 const char *tropnn_b200_last_error(void) { return tropnn_b200::g_last_error.c_str(); }
 
-int tropnn_b200_abi_version(void) { return 19; }
+int tropnn_b200_abi_version(void) { return 20; }
 
 unsigned long long tropnn_b200_kernel_launches(void) {
   return tropnn_b200::g_kernel_launches.load(std::memory_order_relaxed);

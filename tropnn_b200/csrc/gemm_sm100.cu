@@ -489,6 +489,70 @@ __global__ void __launch_bounds__(256) split_half_kernel(const float *__restrict
   }
 }
 
+template <typename PT>
+__device__ __forceinline__ uint32_t pack_pair(PT a, PT b) {
+  return uint32_t(*reinterpret_cast<const unsigned short *>(&a)) |
+         (uint32_t(*reinterpret_cast<const unsigned short *>(&b)) << 16);
+}
+
+// split_half and its transpose in one pass over x: out_split [rows, 2 cols] = [hi | lo] of
+// x s (split_half_kernel's arithmetic) and out_t [cols, rows] = hi^T (what transpose_to_half
+// writes for the same x and scale). 64 x 64 tiles of 256 threads; each warp takes pairs of
+// rows, so the shared tile holds (row 2p, row 2p + 1) pairs per 4-byte word and every
+// transposed store is a 128-byte warp store. Even rows and cols (the host checks).
+template <typename PT>
+__global__ void __launch_bounds__(256) split_transpose_half_kernel(const float *__restrict__ x, int64_t rows,
+                                                                   int cols, const uint32_t *__restrict__ absmax,
+                                                                   PT *__restrict__ out_split,
+                                                                   PT *__restrict__ out_t) {
+  __shared__ uint32_t pair_t[64][33];  // [tile column][row pair]
+  const float s = grad_scale_of(absmax);
+  const int64_t r0 = int64_t(blockIdx.x) * 64;
+  const int c0 = blockIdx.y * 64;
+  const int tx = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int c = c0 + 2 * tx;
+  const bool col_ok = c < cols;
+  float2 v[4][2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = r0 + 2 * (w + 8 * i);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      v[i][h] = make_float2(0.f, 0.f);
+      if (col_ok && r + h < rows) v[i][h] = __ldg(reinterpret_cast<const float2 *>(x + (r + h) * cols + c));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int p = w + 8 * i;
+    const int64_t r = r0 + 2 * p;
+    PT hi[2][2];  // [row of the pair][column of the pair]
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float xs0 = __fmul_rn(v[i][h].x, s), xs1 = __fmul_rn(v[i][h].y, s);
+      hi[h][0] = from_f32<PT>(xs0);
+      hi[h][1] = from_f32<PT>(xs1);
+      const PT lo0 = from_f32<PT>(__fsub_rn(xs0, to_f32(hi[h][0])));
+      const PT lo1 = from_f32<PT>(__fsub_rn(xs1, to_f32(hi[h][1])));
+      if (col_ok && r + h < rows) {
+        PT *o = out_split + (r + h) * (2 * int64_t(cols)) + c;
+        *reinterpret_cast<uint32_t *>(o) = pack_pair(hi[h][0], hi[h][1]);
+        *reinterpret_cast<uint32_t *>(o + cols) = pack_pair(lo0, lo1);
+      }
+    }
+    pair_t[2 * tx][p] = pack_pair(hi[0][0], hi[1][0]);
+    pair_t[2 * tx + 1][p] = pack_pair(hi[0][1], hi[1][1]);
+  }
+  __syncthreads();
+  const int64_t rr = r0 + 2 * tx;  // first of this thread's pair of output columns
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int cc = w + 8 * i;
+    if (c0 + cc < cols && rr < rows)
+      *reinterpret_cast<uint32_t *>(out_t + int64_t(c0 + cc) * rows + rr) = pair_t[cc][tx];
+  }
+}
+
 // *bits = max(*bits, f32 bits of max |x|): non-negative floats order as their bit patterns,
 // so the integer maximum is order-independent (deterministic). The caller zeroes *bits first.
 __global__ void __launch_bounds__(256) absmax_kernel(const float *__restrict__ x, int64_t n,
@@ -632,6 +696,31 @@ int split_half_impl(const float *x, int64_t rows, int64_t cols, int dtype, const
   return check_launch("split_half");
 }
 
+int split_transpose_half_impl(const float *x, int64_t rows, int64_t cols, int dtype, const uint32_t *absmax,
+                              void *out_split, void *out_t, cudaStream_t stream) {
+  TB_REQUIRE(dtype == TROPNN_B200_F16 || dtype == TROPNN_B200_BF16, TROPNN_B200_ERR_DTYPE,
+             "split_transpose_half: dtype %s unsupported (f16/bf16 only)", dtype_name(dtype));
+  TB_REQUIRE(rows >= 0 && rows % 2 == 0 && cols > 0 && cols % 4 == 0 && cols <= (1 << 20), TROPNN_B200_ERR_INVALID,
+             "split_transpose_half: rows=%lld must be even and cols=%lld a positive multiple of 4", (long long)rows,
+             (long long)cols);
+  if (rows == 0) return TROPNN_B200_OK;
+  TB_REQUIRE(x && out_split && out_t, TROPNN_B200_ERR_INVALID, "split_transpose_half: null pointer");
+  TB_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(out_split) % 8 == 0 &&
+                 reinterpret_cast<uintptr_t>(out_t) % 4 == 0,
+             TROPNN_B200_ERR_INVALID, "split_transpose_half: misaligned operands");
+  const dim3 grid(static_cast<unsigned>(ceil_div(rows, int64_t(64))), static_cast<unsigned>(ceil_div(cols, int64_t(64))));
+  TB_REQUIRE(grid.x < (1u << 31) && grid.y < 65536, TROPNN_B200_ERR_INVALID, "split_transpose_half: too large");
+  if (dtype == TROPNN_B200_F16)
+    split_transpose_half_kernel<__half><<<grid, 256, 0, stream>>>(x, rows, static_cast<int>(cols), absmax,
+                                                                  static_cast<__half *>(out_split),
+                                                                  static_cast<__half *>(out_t));
+  else
+    split_transpose_half_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(x, rows, static_cast<int>(cols), absmax,
+                                                                         static_cast<__nv_bfloat16 *>(out_split),
+                                                                         static_cast<__nv_bfloat16 *>(out_t));
+  return check_launch("split_transpose_half");
+}
+
 int absmax_impl(const float *x, int64_t n, uint32_t *bits, cudaStream_t stream) {
   TB_REQUIRE(n >= 0 && bits != nullptr && (n == 0 || x != nullptr), TROPNN_B200_ERR_INVALID, "absmax: bad arguments");
   TB_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0, TROPNN_B200_ERR_INVALID, "absmax: x must be 16-byte aligned");
@@ -665,6 +754,14 @@ int tropnn_b200_split_half(const float *x, int64_t rows, int64_t cols, int dtype
   TB_CHECK(tropnn_b200::check_current_device());
   TB_CHECK(tropnn_b200::split_half_impl(x, rows, cols, dtype, static_cast<const uint32_t *>(grad_absmax), out,
                                         tropnn_b200::as_stream(stream)));
+  return tropnn_b200::clear_error();
+}
+
+int tropnn_b200_split_transpose_half(const float *x, int64_t rows, int64_t cols, int dtype, const void *grad_absmax,
+                                     void *out_split, void *out_t, void *stream) {
+  TB_CHECK(tropnn_b200::check_current_device());
+  TB_CHECK(tropnn_b200::split_transpose_half_impl(x, rows, cols, dtype, static_cast<const uint32_t *>(grad_absmax),
+                                                  out_split, out_t, tropnn_b200::as_stream(stream)));
   return tropnn_b200::clear_error();
 }
 

@@ -622,6 +622,9 @@ int trop_param_grad_sm100_impl(int mode, const void *xt, int64_t rows, int64_t D
   return TROPNN_B200_OK;
 }
 
+int trop_code_transpose_impl(const void *code, int pt, int64_t H, int64_t K, int64_t D, void *code_t,
+                             cudaStream_t stream);
+
 int transpose_to_half_impl(const void *x, int xt_dtype, int64_t rows, int64_t cols, int pt, void *out,
                            const uint32_t *absmax, cudaStream_t stream) {
   TB_REQUIRE(pt == TROPNN_B200_F16 || pt == TROPNN_B200_BF16, TROPNN_B200_ERR_DTYPE,
@@ -631,6 +634,9 @@ int transpose_to_half_impl(const void *x, int xt_dtype, int64_t rows, int64_t co
   TB_REQUIRE(rows >= 0 && cols > 0 && cols <= (1 << 20), TROPNN_B200_ERR_INVALID, "transpose_to_half: bad shape");
   if (rows == 0) return TROPNN_B200_OK;
   TB_REQUIRE(x && out, TROPNN_B200_ERR_INVALID, "transpose_to_half: null pointer");
+  // Half in, half out, no scale: a plain transpose of 2-byte values, which the parameter
+  // transpose does with 4-byte moves on both sides (the kernels below load 2 bytes a thread).
+  if (xt_dtype == pt && absmax == nullptr) return trop_code_transpose_impl(x, pt, rows, 1, cols, out, stream);
   const int c = static_cast<int>(cols);
   if (rows % 2 == 0 && reinterpret_cast<uintptr_t>(out) % 4 == 0) {
     // 64-row tiles, pairs of output elements per 4-byte store.

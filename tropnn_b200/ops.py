@@ -477,10 +477,17 @@ def _trop_backward_tensor_cores(ctx, g, z, weight, code, winner, runner, margins
     gmax = torch.zeros(1, device=dev, dtype=torch.int32)
     _launch("absmax", lib.tropnn_b200_absmax_f32, g.data_ptr(), g.numel(), gmax.data_ptr(), stream)
     gm = None
+    g_t = None  # grad_hidden^T in the parameter dtype, the code gradient's operand
     if training:
         g_split = torch.empty((items, 2 * code_dim), device=dev, dtype=weight.dtype)
-        _launch("split_half", lib.tropnn_b200_split_half, g.data_ptr(), items, code_dim, pdt, gmax.data_ptr(),
-                g_split.data_ptr(), stream)
+        if ctx.needs_input_grad[3] and items % 2 == 0:
+            # The [hi | lo] split and the code gradient's transposed operand in one pass over g.
+            g_t = torch.empty((code_dim, items), device=dev, dtype=weight.dtype)
+            _launch("split_transpose_half", lib.tropnn_b200_split_transpose_half, g.data_ptr(), items, code_dim, pdt,
+                    gmax.data_ptr(), g_split.data_ptr(), g_t.data_ptr(), stream)
+        else:
+            _launch("split_half", lib.tropnn_b200_split_half, g.data_ptr(), items, code_dim, pdt, gmax.data_ptr(),
+                    g_split.data_ptr(), stream)
         gm = torch.empty((items, heads), device=dev, dtype=torch.float32)
         _launch(
             "trop_gm", lib.tropnn_b200_trop_gm, g_split.data_ptr(), items, code_dim, code.data_ptr(), pdt, heads, cells,
@@ -501,9 +508,10 @@ def _trop_backward_tensor_cores(ctx, g, z, weight, code, winner, runner, margins
         grad_z = g
     grad_w = grad_b = grad_c = None
     if ctx.needs_input_grad[3]:
-        g_t = torch.empty((code_dim, items), device=dev, dtype=weight.dtype)
-        _launch("transpose_to_half", lib.tropnn_b200_transpose_to_half, g.data_ptr(), nat.F32, items, code_dim, pdt,
-                gmax.data_ptr(), g_t.data_ptr(), stream)
+        if g_t is None:
+            g_t = torch.empty((code_dim, items), device=dev, dtype=weight.dtype)
+            _launch("transpose_to_half", lib.tropnn_b200_transpose_to_half, g.data_ptr(), nat.F32, items, code_dim,
+                    pdt, gmax.data_ptr(), g_t.data_ptr(), stream)
         grad_c = torch.empty_like(code)
         _launch(
             "trop_code_grad", lib.tropnn_b200_trop_param_grad, 1 if training else 0, g_t.data_ptr(), items, code_dim, pdt,
