@@ -64,8 +64,8 @@ def _check(items: int, heads: int, cells: int, code_dim: int, dtype: torch.dtype
     win_gate, run_gate = route_gate(scores)
     assert win_gate.mean() > 0.99
     ref_w, ref_r, ref_m = oracle.top2_indices(scores)
-    # Half latent, f32 bias: tensor-core path, the bias added in the epilogue (no workspace) or
-    # entering the accumulator through one more MMA step (with the workspace for bias_ext).
+    # Half latent, f32 bias: tensor-core path, the bias added in the epilogue; a workspace (which
+    # this path does not use) changes nothing.
     for workspace in (False, True):
         tc = _route(z, weight, bias.float(), workspace=workspace)
         assert np.array_equal(tc[0], tc[1].astype(np.int64))
@@ -143,6 +143,6 @@ def test_f32_tensor_core_route(items: int, heads: int, cells: int, code_dim: int
 def test_f32_route_workspace_query() -> None:
     lib = nat.load()
     assert lib.tropnn_b200_trop_route_workspace_size(512, 64, 256, 16, nat.F32, nat.F32) >= 2 * 4 * (512 + 4096) * 64
-    # Half precision: bias_ext [H*K, 64] for the bias MMA step.
-    assert lib.tropnn_b200_trop_route_workspace_size(512, 64, 256, 16, nat.F16, nat.F16) == 4096 * 64 * 2
+    # Half precision: the tensor-core route needs no scratch.
+    assert lib.tropnn_b200_trop_route_workspace_size(512, 64, 256, 16, nat.F16, nat.F16) == 0
     assert lib.tropnn_b200_trop_route_workspace_size(512, 64, 256, 16, nat.F32, nat.F16) == 0

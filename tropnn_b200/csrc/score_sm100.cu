@@ -150,14 +150,14 @@ __device__ __forceinline__ void store_run(float *dst, const float (&v)[N]) {
   }
 }
 
-// BIAS_MMA: the bias enters the accumulator through one more K=16 MMA per unit: a constant
-// "ones" block (columns 0 and 1 of every row = 1) against the tile's rows of bias_ext
-// [H*K, 64] (column 0 = half(b), column 1 = half(b - half(b)), the rest 0), so the epilogue
-// adds nothing; otherwise the epilogue adds the f32 bias.
-template <typename PT, int K, bool BIAS_MMA>
+// The epilogue adds the f32 bias to each score (its 32 values per chunk loaded while the
+// TMEM read is in flight). Folding the bias into the MMA as one more k step against a
+// "ones" block measured 7 % slower at 65536 rows and no faster at 16384: that step streams
+// one more 32 KB ring stage per unit beside the four weight k blocks.
+template <typename PT, int K>
 __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
     const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_w,
-    const __grid_constant__ CUtensorMap map_bias, const float *__restrict__ bias, int64_t rows, int H, int kblocks,
+    const float *__restrict__ bias, int64_t rows, int H, int kblocks,
     int stages, int tiles_total, int64_t units, int flags, bool vec_stores, int64_t *__restrict__ winner_i64,
     uint8_t *__restrict__ winner, uint8_t *__restrict__ runner, float *__restrict__ margins) {
   static_assert(32 % K == 0 && K >= 2, "cells must divide 32");
@@ -175,9 +175,8 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms.
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *a_smem = smem;                                // kblocks x [128 rows x 128 B]
-  uint8_t *ones_smem = a_smem + kblocks * kTileBytesA;   // BIAS_MMA: the constant ones block
-  uint8_t *b_smem = ones_smem + (BIAS_MMA ? kTileBytesA : 0);  // stages x [256 rows x 128 B]
+  uint8_t *a_smem = smem;                               // kblocks x [128 rows x 128 B]
+  uint8_t *b_smem = a_smem + kblocks * kTileBytesA;     // stages x [256 rows x 128 B]
   Barriers *bs = reinterpret_cast<Barriers *>(b_smem + stages * kTileBytesB);
 
   const int warp = threadIdx.x >> 5;
@@ -205,32 +204,17 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
     __syncwarp();
     tmem_alloc(&bs->tmem_base, kTmemCols);
   }
-  if constexpr (BIAS_MMA) {
-    if (warp >= 2 && warp < 6) {
-      // Row r of the ones block (K-major, 128-byte swizzle): elements 0 and 1 are 1, the
-      // rest 0 (element 0 sits in 16-byte chunk 0, stored at chunk 0 ^ (r & 7)).
-      const int r = (warp - 2) * 32 + lane;
-      constexpr uint32_t kOne = std::is_same<PT, __half>::value ? 0x3C00u : 0x3F80u;
-      uint8_t *row = ones_smem + r * 128;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        *reinterpret_cast<uint4 *>(row + ((j ^ (r & 7)) << 4)) =
-            j == 0 ? make_uint4(kOne | (kOne << 16), 0u, 0u, 0u) : make_uint4(0u, 0u, 0u, 0u);
-      fence_proxy_async_smem();
-    }
-  }
   tmem_fence_before();
   __syncthreads();
   tmem_fence_after();
   const uint32_t tmem_base = bs->tmem_base;
-  const int ksteps = kblocks + (BIAS_MMA ? 1 : 0);  // ring stages per unit
+  const int ksteps = kblocks;  // ring stages per unit
 
   if (warp == 0) {
     if (lane == 0 && u_begin < u_end) {
       // ---------------- TMA producer ----------------
       prefetch_map(&map_z);
       prefetch_map(&map_w);
-      if constexpr (BIAS_MMA) prefetch_map(&map_bias);
       uint32_t issued[kMaxStages];
       for (int s = 0; s < kMaxStages; ++s) issued[s] = 0;
       bool ok = true;
@@ -259,11 +243,9 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
             break;
           }
           mbar_expect_tx(&bs->full[s], kTileBytesB);
-          // The weight k blocks, then (BIAS_MMA) the tile's rows of bias_ext.
-          const CUtensorMap *map = kb < kblocks ? &map_w : &map_bias;
-          const int x = kb < kblocks ? kb * kBK : 0;
           for (int q = 0; q < kBN / kBoxRows; ++q)
-            tma_load_2d(b_smem + s * kTileBytesB + q * kBoxRows * 128, map, &bs->full[s], x, tile * kBN + q * kBoxRows);
+            tma_load_2d(b_smem + s * kTileBytesB + q * kBoxRows * 128, &map_w, &bs->full[s], kb * kBK,
+                        tile * kBN + q * kBoxRows);
           issued[s] = uint32_t(it / stages) + 1;
         }
       }
@@ -310,16 +292,11 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
           }
           tmem_fence_after();
           const uint32_t b_base = smem_addr(b_smem + s * kTileBytesB);
-          if (kb < kblocks) {
-            const uint32_t a_base = smem_addr(a_smem + kb * kTileBytesA);
+          const uint32_t a_base = smem_addr(a_smem + kb * kTileBytesA);
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              umma_f16(d_tmem, umma_desc_sw128(a_base + kk * 32), umma_desc_sw128(b_base + kk * 32), kIdesc,
-                       (kb | kk) != 0 ? 1u : 0u);
-          } else {
-            // Bias: ones (columns 0, 1) x bias_ext (columns 0, 1), one K=16 step.
-            umma_f16(d_tmem, umma_desc_sw128(smem_addr(ones_smem)), umma_desc_sw128(b_base), kIdesc, 1u);
-          }
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16(d_tmem, umma_desc_sw128(a_base + kk * 32), umma_desc_sw128(b_base + kk * 32), kIdesc,
+                     (kb | kk) != 0 ? 1u : 0u);
           umma_commit(&bs->empty[s]);
         }
         if (!ok) break;
@@ -361,12 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
       for (int c = 0; c < kEpiCols; c += 32) {
         float v[32], bv[32];
         tmem_ld32(taddr + uint32_t(c), v);
-        if constexpr (BIAS_MMA) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) bv[i] = 0.f;
-        } else {
-          load_bias32(bias, c0 + c, hk, bv);  // in flight together with the TMEM read
-        }
+        load_bias32(bias, c0 + c, hk, bv);  // in flight together with the TMEM read
         tmem_wait_ld();
         reg_fence(v);
         if (c + 32 == kEpiCols) {
@@ -392,8 +364,8 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
 #pragma unroll
           for (int p = 0; p < K / 2; ++p) {
             const int k = 2 * p;
-            const float sx = BIAS_MMA ? v[hh * K + k] : __fadd_rn(v[hh * K + k], bv[hh * K + k]);
-            const float sy = BIAS_MMA ? v[hh * K + k + 1] : __fadd_rn(v[hh * K + k + 1], bv[hh * K + k + 1]);
+            const float sx = __fadd_rn(v[hh * K + k], bv[hh * K + k]);
+            const float sy = __fadd_rn(v[hh * K + k + 1], bv[hh * K + k + 1]);
             const float x = packed_key<kIdxMask>(sx, uint32_t(K - 1 - k));
             const float y = packed_key<kIdxMask>(sy, uint32_t(K - 2 - k));
             hi[p] = fmaxf(x, y);
@@ -454,60 +426,32 @@ __global__ void __launch_bounds__(kThreads, 1) trop_score_top2_kernel(
 
 // --------------------------------------------------------------------------- host side
 
-size_t score_smem_bytes(int kblocks, int stages, bool bias_mma) {
-  return 1024 + size_t(kblocks + (bias_mma ? 1 : 0)) * kTileBytesA + size_t(stages) * kTileBytesB + sizeof(Barriers);
+size_t score_smem_bytes(int kblocks, int stages) {
+  return 1024 + size_t(kblocks) * kTileBytesA + size_t(stages) * kTileBytesB + sizeof(Barriers);
 }
 
-// Weight-ring depth: the shared memory left after the resident z block (and the ones block),
-// up to kMaxStages; 0 when fewer than kMinStages fit.
-int score_stages(int kblocks, bool bias_mma) {
-  const size_t fixed = score_smem_bytes(kblocks, 0, bias_mma);
+// Weight-ring depth: the shared memory left after the resident z block, up to kMaxStages; 0
+// when fewer than kMinStages fit.
+int score_stages(int kblocks) {
+  const size_t fixed = score_smem_bytes(kblocks, 0);
   if (fixed >= kSmemLimit) return 0;
   const int stages = static_cast<int>(std::min<size_t>(kMaxStages, (kSmemLimit - fixed) / kTileBytesB));
   return stages >= kMinStages ? stages : 0;
 }
 
-// bias_ext[r, 0] = half(b[r]), bias_ext[r, 1] = half(b[r] - half(b[r])), the other 62 columns 0:
-// the right operand of the bias MMA step (b = hi + lo to ~2^-22 relative for f16, exactly for a
-// bias that is a half-precision parameter upcast).
-template <typename PT>
-__global__ void bias_ext_kernel(const float *__restrict__ bias, int64_t hk, PT *__restrict__ out) {
-  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= hk * 64) return;
-  const int64_t r = i >> 6;
-  const int c = static_cast<int>(i & 63);
-  float v = 0.f;
-  if (c < 2) {
-    const float b = __ldg(bias + r);
-    const float hi = to_f32<PT>(from_f32<PT>(b));
-    v = c == 0 ? hi : __fsub_rn(b, hi);
-  }
-  out[i] = from_f32<PT>(v);
-}
-
 template <typename PT, int K>
 int launch_score(const void *z, int64_t rows, int D, const void *W, const void *bias, int H, int64_t *w64,
-                 uint8_t *win, uint8_t *run, float *m, void *bias_ext, cudaStream_t stream) {
+                 uint8_t *win, uint8_t *run, float *m, cudaStream_t stream) {
   const CUtensorMapDataType dt =
       std::is_same<PT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int kblocks = (D + kBK - 1) / kBK;
   const int64_t hk = int64_t(H) * K;
-  // The bias MMA needs room for bias_ext and a ring of at least kMinStages beside the ones block.
-  const bool bias_mma = bias_ext != nullptr && score_stages(kblocks, true) > 0;
-  const int stages = score_stages(kblocks, bias_mma);
+  const int stages = score_stages(kblocks);
   TB_REQUIRE(stages > 0, TROPNN_B200_ERR_INVALID, "trop_score_sm100: code_dim=%d does not fit shared memory", D);
-  const size_t smem = score_smem_bytes(kblocks, stages, bias_mma);
-  CUtensorMap map_z, map_w, map_bias;
+  const size_t smem = score_smem_bytes(kblocks, stages);
+  CUtensorMap map_z, map_w;
   TB_CHECK(make_map_k64(&map_z, z, dt, D, rows, kBM));
   TB_CHECK(make_map_k64(&map_w, W, dt, D, hk, kBoxRows));
-  if (bias_mma) {
-    const unsigned blocks = static_cast<unsigned>(ceil_div(hk * 64, int64_t(256)));
-    bias_ext_kernel<PT><<<blocks, 256, 0, stream>>>(static_cast<const float *>(bias), hk, static_cast<PT *>(bias_ext));
-    TB_CHECK(check_launch("trop_score_sm100 (bias_ext)"));
-    TB_CHECK(make_map_k64(&map_bias, bias_ext, dt, 64, hk, kBoxRows));
-  } else {
-    map_bias = map_w;  // unused
-  }
   const int tiles_total = static_cast<int>(ceil_div(hk, kBN));
   const int64_t units = ceil_div(rows, int64_t(kBM)) * tiles_total;
   int sms = 0;
@@ -517,25 +461,25 @@ int launch_score(const void *z, int64_t rows, int D, const void *W, const void *
   constexpr int kRun = score_store_heads(K);
   auto al16 = [](const void *p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   const bool vec_stores = (H % kRun == 0) && al16(win) && al16(run) && al16(m);
-  auto kernel = bias_mma ? trop_score_top2_kernel<PT, K, true> : trop_score_top2_kernel<PT, K, false>;
+  auto kernel = trop_score_top2_kernel<PT, K>;
   TB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), smem, "trop_score_sm100"));
   // Persistent grid: one CTA per SM (shared memory and TMEM admit no second), units
   // split evenly.
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(units, sms));
-  kernel<<<grid, kThreads, smem, stream>>>(map_z, map_w, map_bias, static_cast<const float *>(bias), rows, H, kblocks,
-                                           stages, tiles_total, units, flags, vec_stores, w64, win, run, m);
+  kernel<<<grid, kThreads, smem, stream>>>(map_z, map_w, static_cast<const float *>(bias), rows, H, kblocks, stages,
+                                           tiles_total, units, flags, vec_stores, w64, win, run, m);
   return check_launch("trop_score_sm100");
 }
 
 template <typename PT>
 int dispatch_cells(int K, const void *z, int64_t rows, int D, const void *W, const void *bias, int H, int64_t *w64,
-                   uint8_t *win, uint8_t *run, float *m, void *bias_ext, cudaStream_t stream) {
+                   uint8_t *win, uint8_t *run, float *m, cudaStream_t stream) {
   switch (K) {
-    case 2: return launch_score<PT, 2>(z, rows, D, W, bias, H, w64, win, run, m, bias_ext, stream);
-    case 4: return launch_score<PT, 4>(z, rows, D, W, bias, H, w64, win, run, m, bias_ext, stream);
-    case 8: return launch_score<PT, 8>(z, rows, D, W, bias, H, w64, win, run, m, bias_ext, stream);
-    case 16: return launch_score<PT, 16>(z, rows, D, W, bias, H, w64, win, run, m, bias_ext, stream);
-    default: return launch_score<PT, 32>(z, rows, D, W, bias, H, w64, win, run, m, bias_ext, stream);
+    case 2: return launch_score<PT, 2>(z, rows, D, W, bias, H, w64, win, run, m, stream);
+    case 4: return launch_score<PT, 4>(z, rows, D, W, bias, H, w64, win, run, m, stream);
+    case 8: return launch_score<PT, 8>(z, rows, D, W, bias, H, w64, win, run, m, stream);
+    case 16: return launch_score<PT, 16>(z, rows, D, W, bias, H, w64, win, run, m, stream);
+    default: return launch_score<PT, 32>(z, rows, D, W, bias, H, w64, win, run, m, stream);
   }
 }
 
@@ -860,17 +804,12 @@ bool score_sm100_supported(int64_t D, int64_t K, int pt, int bias_dtype, const v
   const int64_t kblocks = (D + kBK - 1) / kBK;
   auto al16 = [](const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   return (pt == TROPNN_B200_F16 || pt == TROPNN_B200_BF16) && bias_dtype == TROPNN_B200_F32 && cells_ok &&
-         D % 8 == 0 && kblocks <= kMaxKBlocks && score_stages(static_cast<int>(kblocks), false) > 0 && al16(z) &&
+         D % 8 == 0 && kblocks <= kMaxKBlocks && score_stages(static_cast<int>(kblocks)) > 0 && al16(z) &&
          al16(W) && al16(bias);
 }
 
-size_t score_sm100_workspace(int64_t H, int64_t K, int pt) {
-  return (pt == TROPNN_B200_F16 || pt == TROPNN_B200_BF16) ? WorkspaceCarver::align(size_t(H) * K * 64 * 2) : 0;
-}
-
 int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W, const void *bias, int pt, int64_t H,
-                          int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, void *ws, size_t ws_bytes,
-                          cudaStream_t stream) {
+                          int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, cudaStream_t stream) {
   TB_REQUIRE(score_sm100_supported(D, K, pt, TROPNN_B200_F32, z, W, bias), TROPNN_B200_ERR_INVALID,
              "trop_score_sm100: unsupported shape or alignment code_dim=%lld cells=%lld dtype=%s", (long long)D,
              (long long)K, dtype_name(pt));
@@ -881,11 +820,8 @@ int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W
              "trop_score_sm100: %lld rows x %lld score columns exceed the 32-bit tile coordinates",
              (long long)items, (long long)(H * K));
   const int Di = static_cast<int>(D), Hi = static_cast<int>(H), Ki = static_cast<int>(K);
-  // With room for bias_ext the bias enters the MMA; without, the epilogue adds it.
-  void *bias_ext = (ws != nullptr && ws_bytes >= score_sm100_workspace(H, K, pt)) ? ws : nullptr;
-  if (pt == TROPNN_B200_F16)
-    return dispatch_cells<__half>(Ki, z, items, Di, W, bias, Hi, w64, win, run, m, bias_ext, stream);
-  return dispatch_cells<__nv_bfloat16>(Ki, z, items, Di, W, bias, Hi, w64, win, run, m, bias_ext, stream);
+  if (pt == TROPNN_B200_F16) return dispatch_cells<__half>(Ki, z, items, Di, W, bias, Hi, w64, win, run, m, stream);
+  return dispatch_cells<__nv_bfloat16>(Ki, z, items, Di, W, bias, Hi, w64, win, run, m, stream);
 }
 
 

@@ -26,9 +26,7 @@ int segment_rowsum_impl(const float *values, int64_t rows, int64_t width, int64_
 bool score_sm100_supported(int64_t D, int64_t K, int pt, int bias_dtype, const void *z, const void *W,
                            const void *bias);
 int trop_score_sm100_impl(const void *z, int64_t items, int64_t D, const void *W, const void *bias, int pt, int64_t H,
-                          int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, void *ws, size_t ws_bytes,
-                          cudaStream_t stream);
-size_t score_sm100_workspace(int64_t H, int64_t K, int pt);
+                          int64_t K, int64_t *w64, uint8_t *win, uint8_t *run, float *m, cudaStream_t stream);
 int read_score_error(int *value);
 int read_pairwise_error(int *value);
 bool score_tf32_supported(int64_t D, int64_t K, int pt, int bias_dtype, const void *z, const void *W,
@@ -483,7 +481,6 @@ bool route_tf32_applies(int64_t items, int zt, int pt, int bt, int it, int64_t D
 size_t trop_route_workspace(int64_t items, int64_t D, int64_t H, int64_t K, int zt, int pt) {
   if (items < 0 || D < 1 || H < 1 || K < 1) return 0;
   if (zt == TROPNN_B200_F32 && pt == TROPNN_B200_F32) return score_tf32_workspace(items, D, H, K);
-  if (zt == pt) return score_sm100_workspace(H, K, pt);  // the half-precision path's bias operand
   return 0;
 }
 
@@ -503,7 +500,7 @@ int trop_route_impl(const void *z, int zt, int64_t items, int64_t D, const void 
   const bool zp = zt != TROPNN_B200_F32;
   if (zp && it == TROPNN_B200_U8 && items >= 128 && H * K >= 128 && score_sm100_supported(D, K, pt, bt, z, W, b))
     return trop_score_sm100_impl(z, items, D, W, b, pt, H, K, w64, static_cast<uint8_t *>(win),
-                                 static_cast<uint8_t *>(run), m, ws, ws_bytes, stream);
+                                 static_cast<uint8_t *>(run), m, stream);
   // f32 latent and parameters with room for the split operands: 3xTF32 on the tensor cores.
   if (ws != nullptr && route_tf32_applies(items, zt, pt, bt, it, D, H, K, z, W, b) &&
       ws_bytes >= score_tf32_workspace(items, D, H, K))
