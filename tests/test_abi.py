@@ -58,3 +58,7 @@ def test_workspace_queries_are_host_only(lib: ctypes.CDLL) -> None:
     size_t = lib.tropnn_b200_trop_backward_workspace_size(512, 256, 16, 1)
     assert size_t >= 512 * 256 * 4 * 5
     assert lib.tropnn_b200_trop_backward_workspace_size(512, 256, 16, 0) < size_t
+    # The half-precision route (tcgen05 scores, bias in the epilogue) takes no scratch; the f32 one
+    # keeps its split operands in the workspace.
+    assert lib.tropnn_b200_trop_route_workspace_size(512, 64, 256, 16, nat.F16, nat.F16) == 0
+    assert lib.tropnn_b200_trop_route_workspace_size(512, 64, 256, 16, nat.F32, nat.F32) > 0
