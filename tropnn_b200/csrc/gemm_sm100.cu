@@ -708,8 +708,10 @@ int split_transpose_half_impl(const float *x, int64_t rows, int64_t cols, int dt
   TB_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(out_split) % 8 == 0 &&
                  reinterpret_cast<uintptr_t>(out_t) % 4 == 0,
              TROPNN_B200_ERR_INVALID, "split_transpose_half: misaligned operands");
-  const dim3 grid(static_cast<unsigned>(ceil_div(rows, int64_t(64))), static_cast<unsigned>(ceil_div(cols, int64_t(64))));
-  TB_REQUIRE(grid.x < (1u << 31) && grid.y < 65536, TROPNN_B200_ERR_INVALID, "split_transpose_half: too large");
+  const int64_t row_tiles = ceil_div(rows, int64_t(64)), col_tiles = ceil_div(cols, int64_t(64));
+  TB_REQUIRE(row_tiles < (int64_t(1) << 31) && col_tiles < 65536, TROPNN_B200_ERR_INVALID,
+             "split_transpose_half: rows=%lld too large", (long long)rows);
+  const dim3 grid(static_cast<unsigned>(row_tiles), static_cast<unsigned>(col_tiles));
   if (dtype == TROPNN_B200_F16)
     split_transpose_half_kernel<__half><<<grid, 256, 0, stream>>>(x, rows, static_cast<int>(cols), absmax,
                                                                   static_cast<__half *>(out_split),
